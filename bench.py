@@ -1,0 +1,291 @@
+#!/usr/bin/env python
+"""Headline benchmark: dense-1B SFT training tokens/s on N B200 GPUs.
+
+Config: 16 layers, d_model 2048, 32 query / 8 KV heads,
+head_dim 64, SwiGLU d_ff 8192, RMSNorm, RoPE theta 500000, vocab 128256, tied
+embeddings; seq 4096, 8 sequences per GPU (weak scaling), first 25% of each
+sequence prompt-masked; bf16; synthetic uniform token ids; random init.
+
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+
+For N > 1 launch one rank per GPU with torch.distributed.run (127.0.0.1).
+Two timed phases over the same Trainer.train_step (the public training API):
+  * value: device time (CUDA events, barrier + synchronize on both sides,
+    max over ranks) with the batch already resident on the device;
+  * e2e:   wall time per step including the pinned-host -> device copy of the
+    batch and the device -> host read of the loss, max over ranks.
+Rank 0 prints ONE JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+METRIC = "train tokens/s (FSDP/TP/EP) + GRPO tokens/s at 1/2/4/8 B200 vs ref NCCL build"
+MODEL_NAME = "dense-1B (16L d2048 32q/8kv hd64 ff8192 V128256 tied, RoPE 5e5)"
+BASELINE_VALUE = None  # BASELINE.json "published" is empty for this config
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--batch-per-gpu", type=int, default=8)
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as fh:
+            for line in fh:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append((float(parts[1]), float(parts[2]), float(parts[3]), float(parts[4]), parts[5:9]))
+                except ValueError:
+                    continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [r for r in rows if r[3] >= 50] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[4]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(loaded), "reasons": reasons}
+
+
+# --------------------------------------------------------------------------- helpers
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(x: float) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+    return x
+
+
+def barrier():
+    import torch
+    import torch.distributed as dist
+
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.barrier(device_ids=[torch.cuda.current_device()])
+
+
+def time_device(step, k: int) -> float:
+    """ms per step: CUDA events on the launching stream, barrier+sync both sides, max over ranks."""
+    import torch
+
+    barrier()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(k):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    barrier()
+    return max_over_ranks(a.elapsed_time(b) / k)
+
+
+def time_wall(step, k: int) -> float:
+    import torch
+
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(k):
+        step()
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    barrier()
+    return max_over_ranks((t1 - t0) * 1e3 / k)
+
+
+def emit(rank: int, payload: dict) -> None:
+    if rank == 0:
+        print(json.dumps(payload), flush=True)
+
+
+# --------------------------------------------------------------------------- our framework
+def run_ours(args, world, rank, local):
+    import torch
+
+    from rl_project_b200.core.config import ExperimentManifest
+    from rl_project_b200.core.lifecycle import RunContext
+    from rl_project_b200.data.synthetic import SyntheticSFTSource
+    from rl_project_b200.data.tokenizers import ByteTokenizer
+    from rl_project_b200.models.policy import NativePolicy
+    from rl_project_b200.models.transformer.model import TransformerLM
+    from rl_project_b200.ops._ext import launch_count, native
+    from rl_project_b200.parallel.strategies import build_strategy
+    from rl_project_b200.training.common.trainer import Trainer
+    from rl_project_b200.training.sft import SFTAlgorithm, SFTConfig
+
+    native()  # the sm_100a library must be loaded
+    strategy_name = "fsdp" if world > 1 else "single"
+    manifest = ExperimentManifest.from_dict({
+        "name": "bench-dense1b-sft", "algorithm": "sft", "model_preset": "bl_dense_1b",
+        "model": {"block_size": args.seq},
+        "trainer": {"batch_size": args.batch_per_gpu, "max_steps": 10**9, "eval_every": 0, "log_every": 0,
+                    "seed": 1234, "precision": {"dtype": "bfloat16"},
+                    "optimizer": {"learning_rate": 3e-4, "grad_clip": 1.0, "weight_decay": 0.1},
+                    "schedule": {"name": "constant", "warmup_steps": 0},
+                    "checkpoint": {"save_every": 0, "auto_resume": False}},
+        "distributed": {"strategy": strategy_name, "timeout_s": 300},
+        "output_dir": os.path.join(tempfile.gettempdir(), f"rlb_bench_{rank}"),
+    })
+    strategy = build_strategy(manifest.distributed)
+    strategy.setup()
+    torch.cuda.set_device(local)
+    ctx = RunContext.create(manifest, metrics_backend="none", distributed=world > 1)
+    spec = manifest.model
+    torch.manual_seed(1234)
+    with torch.device(ctx.device):
+        model = TransformerLM(spec)
+    policy = NativePolicy(model, ByteTokenizer())
+    host_src = SyntheticSFTSource(spec.vocab_size, args.seq, args.batch_per_gpu, prompt_fraction=0.25, seed=1234,
+                                  rank=rank, pin=True)
+
+    class Resident:
+        """The same batches, already on the device (device-timed phase)."""
+
+        def __init__(self, src):
+            self.batches = [b.to(ctx.device) for b in src._pool]
+            self.i = 0
+
+        def next_batch(self):
+            b = self.batches[self.i % len(self.batches)]
+            self.i += 1
+            return b
+
+    alg = SFTAlgorithm(policy, Resident(host_src), SFTConfig(batch_size=args.batch_per_gpu, max_length=args.seq + 1))
+    trainer = Trainer(ctx, alg, strategy=strategy)
+    n_params = sum(p.numel() for p in model.parameters())
+
+    for _ in range(args.warmup):
+        trainer.train_step()
+    clocks = ClockSampler(local)
+    clocks.start()
+    l0 = launch_count()
+    ms = time_device(trainer.train_step, args.steps)
+    launches = (launch_count() - l0) // args.steps
+    clk = clocks.stop()
+    tokens_step = args.seq * args.batch_per_gpu * world
+    value = tokens_step / (ms / 1e3)
+
+    e2e = None
+    if not args.no_e2e:
+        alg.dataset = host_src  # pinned host batches -> device every step, loss read back every step
+        for _ in range(max(1, args.warmup // 2)):
+            trainer.train_step()
+        k = args.e2e_steps or args.steps
+        ms_e2e = time_wall(trainer.train_step, k)
+        h2d = host_src.bytes_per_batch()
+        e2e = {"value": tokens_step / (ms_e2e / 1e3), "unit": "tokens/s", "ms_per_step": ms_e2e,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 * (2 + 1), "api": "Trainer.train_step"}
+
+    last = trainer.history[-1]
+    flops_tok = 6 * n_params + 12 * spec.n_layer * spec.n_embd * args.seq // 2  # causal attention
+    peak = _peak_tflops()
+    payload = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": (value / BASELINE_VALUE) if BASELINE_VALUE else None, "dtype": "bf16",
+        "data": "synthetic (uniform token ids, seeded per rank; random-init weights)",
+        "config": {"model": MODEL_NAME, "global_batch": args.batch_per_gpu * world, "seq_len": args.seq,
+                   "parallelism": (f"fsdp{world}" if world > 1 else "single"), "prompt_mask": 0.25,
+                   "params": n_params, "optimizer": "AdamW fp32 master, clip 1.0",
+                   "l2": "inputs larger than L2 (activations >> 126 MB per step)",
+                   "model_tflops_per_gpu": flops_tok * args.seq * args.batch_per_gpu / (ms / 1e3) / 1e12,
+                   "mfu_vs_measured_bf16": (flops_tok * args.seq * args.batch_per_gpu / (ms / 1e3) / 1e12 / peak)
+                   if peak else None,
+                   "final_loss": last.loss},
+        "clocks": clk, "e2e": e2e, "gpu_launches": int(launches), "impl": "ours",
+    }
+    emit(rank, payload)
+    strategy.teardown()
+
+
+def _peak_tflops():
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as fh:
+            return float(json.load(fh)["bf16_tflops_sustained"])
+    except Exception:
+        return None
+
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        if rank == 0:
+            print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    if args.impl == "reference":
+        from baseline.harness import run_reference
+
+        payload = run_reference(args, world, rank, local, time_device=time_device, time_wall=time_wall,
+                                clock_sampler=ClockSampler, metric=METRIC, model_name=MODEL_NAME)
+        emit(rank, payload)
+        return
+    run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

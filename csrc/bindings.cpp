@@ -1,0 +1,303 @@
+// Torch bindings for the sm_100a kernels (module rl_project_b200._C).
+// Every kernel file is plain CUDA with a C-style launcher; this file owns the
+// tensor checks, the current-stream lookup and the error translation.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+
+#include "launchers.h"
+
+namespace {
+
+inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+inline int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && cached[dev]) return cached[dev];
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
+#define CHECK_OK(expr, what)                                                                 \
+  do {                                                                                       \
+    cudaError_t _e = (expr);                                                                 \
+    TORCH_CHECK(_e == cudaSuccess, "rl_project_b200 kernel ", what, " failed: ",            \
+                cudaGetErrorString(_e));                                                     \
+  } while (0)
+
+inline void check_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+inline void check_bf16(const at::Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+}
+inline void check_contig(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+inline long long* lptr(const at::Tensor& t) { return reinterpret_cast<long long*>(t.data_ptr<int64_t>()); }
+inline const void* opt_ptr(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr() : nullptr; }
+
+// ---------------------------------------------------------------- RMSNorm
+std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& delta, const at::Tensor& w,
+                                    double eps) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_contig(x, "x");
+  const c10::cuda::CUDAGuard g(x.device());
+  const int dim = (int)x.size(-1);
+  const long long rows = x.numel() / dim;
+  auto y = at::empty_like(x);
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  at::Tensor h;
+  if (delta.has_value()) {
+    check_bf16(*delta, "delta");
+    check_contig(*delta, "delta");
+    h = at::empty_like(x);
+  }
+  CHECK_OK(rlb_rmsnorm_fwd(x.data_ptr(), opt_ptr(delta), w.data_ptr(), h.defined() ? h.data_ptr() : nullptr,
+                           y.data_ptr(), rstd.data_ptr<float>(), rows, dim, (float)eps, sm_count(), cur_stream()),
+           "rmsnorm_fwd");
+  if (h.defined()) return {y, rstd, h};
+  return {y, rstd};
+}
+
+std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& h, const at::Tensor& w, const at::Tensor& rstd,
+                                    const at::Tensor& dy, const c10::optional<at::Tensor>& dres) {
+  check_bf16(h, "h");
+  check_bf16(dy, "dy");
+  check_contig(h, "h");
+  check_contig(dy, "dy");
+  const c10::cuda::CUDAGuard g(h.device());
+  const int dim = (int)h.size(-1);
+  const long long rows = h.numel() / dim;
+  auto dx = at::empty_like(h);
+  const int grid = rlb_rmsnorm_bwd_grid(rows, sm_count());
+  auto part = at::empty({grid, dim}, h.options().dtype(at::kFloat));
+  auto dw = at::empty_like(w);
+  CHECK_OK(rlb_rmsnorm_bwd(h.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), dy.data_ptr(), opt_ptr(dres),
+                           dx.data_ptr(), part.data_ptr<float>(), dw.data_ptr(), w.scalar_type() == at::kFloat, rows,
+                           dim, sm_count(), cur_stream()),
+           "rmsnorm_bwd");
+  return {dx, dw};
+}
+
+// ---------------------------------------------------------------- RoPE
+std::vector<at::Tensor> rope_qkv_fwd(const at::Tensor& qkv, const at::Tensor& cos_t, const at::Tensor& sin_t,
+                                     const c10::optional<at::Tensor>& positions, int64_t B, int64_t T, int64_t Hq,
+                                     int64_t Hkv, int64_t D, int64_t pos_offset, bool heads_major) {
+  check_bf16(qkv, "qkv");
+  TORCH_CHECK(qkv.stride(-1) == 1, "qkv inner stride must be 1");
+  const c10::cuda::CUDAGuard g(qkv.device());
+  auto opts = qkv.options();
+  at::Tensor q, k, v;
+  if (heads_major) {
+    q = at::empty({B, Hq, T, D}, opts);
+    k = at::empty({B, Hkv, T, D}, opts);
+    v = at::empty({B, Hkv, T, D}, opts);
+  } else {
+    q = at::empty({B, T, Hq, D}, opts);
+    k = at::empty({B, T, Hkv, D}, opts);
+    v = at::empty({B, T, Hkv, D}, opts);
+  }
+  const long long row_stride = qkv.stride(-2);
+  CHECK_OK(rlb_rope_qkv_fwd(qkv.data_ptr(), row_stride, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                            cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
+                            positions.has_value() ? positions->data_ptr<int>() : nullptr, (int)B, (int)T, (int)Hq,
+                            (int)Hkv, (int)D, (int)pos_offset, heads_major ? 1 : 0, sm_count(), cur_stream()),
+           "rope_qkv_fwd");
+  return {q, k, v};
+}
+
+at::Tensor rope_qkv_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tensor& dv, const at::Tensor& cos_t,
+                        const at::Tensor& sin_t, const c10::optional<at::Tensor>& positions, int64_t B, int64_t T,
+                        int64_t Hq, int64_t Hkv, int64_t D, int64_t pos_offset, bool heads_major) {
+  check_bf16(dq, "dq");
+  check_contig(dq, "dq");
+  check_contig(dk, "dk");
+  check_contig(dv, "dv");
+  const c10::cuda::CUDAGuard g(dq.device());
+  auto dqkv = at::empty({B, T, (Hq + 2 * Hkv) * D}, dq.options());
+  CHECK_OK(rlb_rope_qkv_bwd(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dqkv.data_ptr(), (Hq + 2 * Hkv) * D,
+                            cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
+                            positions.has_value() ? positions->data_ptr<int>() : nullptr, (int)B, (int)T, (int)Hq,
+                            (int)Hkv, (int)D, (int)pos_offset, heads_major ? 1 : 0, sm_count(), cur_stream()),
+           "rope_qkv_bwd");
+  return dqkv;
+}
+
+void rope_inplace(at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t,
+                  const c10::optional<at::Tensor>& positions, int64_t pos_offset, bool inverse) {
+  // x viewed as [B, T, H, D] with arbitrary outer strides, inner stride 1
+  check_bf16(x, "x");
+  TORCH_CHECK(x.dim() == 4 && x.stride(3) == 1, "rope_inplace expects [B,T,H,D] with unit inner stride");
+  const c10::cuda::CUDAGuard g(x.device());
+  CHECK_OK(rlb_rope_inplace(x.data_ptr(), (int)x.size(0), (int)x.size(1), (int)x.size(2), (int)x.size(3),
+                            x.stride(0), x.stride(1), x.stride(2), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
+                            positions.has_value() ? positions->data_ptr<int>() : nullptr, (int)pos_offset,
+                            inverse ? 1 : 0, sm_count(), cur_stream()),
+           "rope_inplace");
+}
+
+// ---------------------------------------------------------------- SwiGLU / GELU
+at::Tensor swiglu_fwd(const at::Tensor& h13) {
+  check_bf16(h13, "h13");
+  check_contig(h13, "h13");
+  const c10::cuda::CUDAGuard g(h13.device());
+  const int F = (int)(h13.size(-1) / 2);
+  auto sizes = h13.sizes().vec();
+  sizes.back() = F;
+  auto out = at::empty(sizes, h13.options());
+  CHECK_OK(rlb_swiglu_fwd(h13.data_ptr(), out.data_ptr(), h13.numel() / (2 * F), F, sm_count(), cur_stream()),
+           "swiglu_fwd");
+  return out;
+}
+
+at::Tensor swiglu_bwd(const at::Tensor& h13, const at::Tensor& da) {
+  check_bf16(h13, "h13");
+  check_contig(da, "da");
+  const c10::cuda::CUDAGuard g(h13.device());
+  const int F = (int)(h13.size(-1) / 2);
+  auto dh = at::empty_like(h13);
+  CHECK_OK(rlb_swiglu_bwd(h13.data_ptr(), da.data_ptr(), dh.data_ptr(), h13.numel() / (2 * F), F, sm_count(),
+                          cur_stream()),
+           "swiglu_bwd");
+  return dh;
+}
+
+at::Tensor gelu(const at::Tensor& x, const c10::optional<at::Tensor>& dy) {
+  check_bf16(x, "x");
+  check_contig(x, "x");
+  const c10::cuda::CUDAGuard g(x.device());
+  auto out = at::empty_like(x);
+  CHECK_OK(rlb_gelu(x.data_ptr(), opt_ptr(dy), out.data_ptr(), x.numel(), sm_count(), cur_stream()), "gelu");
+  return out;
+}
+
+// ---------------------------------------------------------------- log-softmax gather
+std::vector<at::Tensor> logprob_fwd(const at::Tensor& logits, const c10::optional<at::Tensor>& targets,
+                                    bool with_entropy, const c10::optional<at::Tensor>& status) {
+  check_bf16(logits, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be [N, V] with unit inner stride");
+  const c10::cuda::CUDAGuard g(logits.device());
+  const long long rows = logits.size(0);
+  const int V = (int)logits.size(1);
+  auto fopt = logits.options().dtype(at::kFloat);
+  auto lse = at::empty({rows}, fopt);
+  auto lp = at::empty({rows}, fopt);
+  at::Tensor ent = with_entropy ? at::empty({rows}, fopt) : at::Tensor();
+  const long long* tg = nullptr;
+  if (targets.has_value()) {
+    TORCH_CHECK(targets->scalar_type() == at::kLong && targets->is_contiguous(), "targets must be contiguous int64");
+    tg = lptr(*targets);
+  }
+  CHECK_OK(rlb_logprob_fwd(logits.data_ptr(), logits.stride(0), rows, V, tg, lse.data_ptr<float>(),
+                           lp.data_ptr<float>(), with_entropy ? ent.data_ptr<float>() : nullptr,
+                           status.has_value() ? status->data_ptr<int>() : nullptr, cur_stream()),
+           "logprob_fwd");
+  if (with_entropy) return {lse, lp, ent};
+  return {lse, lp};
+}
+
+void logprob_bwd_(at::Tensor& logits, const c10::optional<at::Tensor>& targets, const at::Tensor& lse,
+                  const c10::optional<at::Tensor>& g_lp, const c10::optional<at::Tensor>& ent,
+                  const c10::optional<at::Tensor>& g_ent, double scale) {
+  check_bf16(logits, "logits");
+  const c10::cuda::CUDAGuard g(logits.device());
+  CHECK_OK(rlb_logprob_bwd(logits.data_ptr(), logits.stride(0), logits.size(0), (int)logits.size(1),
+                           targets.has_value() ? lptr(*targets) : nullptr, lse.data_ptr<float>(),
+                           g_lp.has_value() ? g_lp->data_ptr<float>() : nullptr,
+                           ent.has_value() ? ent->data_ptr<float>() : nullptr,
+                           g_ent.has_value() ? g_ent->data_ptr<float>() : nullptr, (float)scale, cur_stream()),
+           "logprob_bwd");
+}
+
+// ---------------------------------------------------------------- AdamW
+void grad_norm(const at::Tensor& tensors, const at::Tensor& chunks, int64_t nchunks, at::Tensor& partial,
+               double max_norm, double inv_scale, at::Tensor& norm_coef) {
+  const c10::cuda::CUDAGuard g(partial.device());
+  CHECK_OK(rlb_grad_norm(tensors.data_ptr(), chunks.data_ptr(), (int)nchunks, partial.data_ptr<float>(),
+                         (int)partial.numel(), (float)max_norm, (float)inv_scale, norm_coef.data_ptr<float>(),
+                         cur_stream()),
+           "grad_norm");
+}
+
+void adam_step(const at::Tensor& tensors, const at::Tensor& chunks, int64_t nchunks,
+               const c10::optional<at::Tensor>& coef, double lr, double b1, double b2, double eps, int64_t step,
+               bool decoupled) {
+  const c10::cuda::CUDAGuard g(tensors.device());
+  const int grid = std::min<int64_t>(nchunks, (int64_t)sm_count() * 8);
+  CHECK_OK(rlb_adam_step(tensors.data_ptr(), chunks.data_ptr(), (int)nchunks,
+                         coef.has_value() ? coef->data_ptr<float>() + 1 : nullptr, (float)lr, (float)b1, (float)b2,
+                         (float)eps, (int)step, decoupled ? 1 : 0, grid < 1 ? 1 : grid, cur_stream()),
+           "adam_step");
+}
+
+// ---------------------------------------------------------------- embedding
+at::Tensor embed_fwd(const at::Tensor& idx, const at::Tensor& W, const c10::optional<at::Tensor>& status) {
+  check_bf16(W, "W");
+  TORCH_CHECK(idx.scalar_type() == at::kLong && idx.is_contiguous(), "idx must be contiguous int64");
+  const c10::cuda::CUDAGuard g(W.device());
+  auto sizes = idx.sizes().vec();
+  sizes.push_back(W.size(1));
+  auto out = at::empty(sizes, W.options());
+  CHECK_OK(rlb_embed_fwd(lptr(idx), W.data_ptr(), out.data_ptr(), idx.numel(), (int)W.size(1),
+                         W.size(0), status.has_value() ? status->data_ptr<int>() : nullptr, sm_count(), cur_stream()),
+           "embed_fwd");
+  return out;
+}
+
+at::Tensor embed_bwd(const at::Tensor& idx, const at::Tensor& dy, int64_t vocab) {
+  check_bf16(dy, "dy");
+  const c10::cuda::CUDAGuard g(dy.device());
+  auto flat = idx.reshape({-1});
+  auto sorted = at::sort(flat);
+  auto ids = std::get<0>(sorted).contiguous();
+  auto perm = std::get<1>(sorted).contiguous();
+  const int dim = (int)dy.size(-1);
+  auto dW = at::zeros({vocab, dim}, dy.options());
+  CHECK_OK(rlb_embed_bwd(lptr(ids), lptr(perm), dy.contiguous().data_ptr(),
+                         dW.data_ptr(), flat.numel(), dim, vocab, sm_count(), cur_stream()),
+           "embed_bwd");
+  return dW;
+}
+
+// ---------------------------------------------------------------- NF4
+at::Tensor nf4_dequant(const at::Tensor& packed, const at::Tensor& absmax, const at::Tensor& table, int64_t n,
+                       int64_t block, bool bf16) {
+  check_cuda(packed, "packed");
+  const c10::cuda::CUDAGuard g(packed.device());
+  auto out = at::empty({n}, packed.options().dtype(bf16 ? at::kBFloat16 : at::kFloat));
+  CHECK_OK(rlb_nf4_dequant(packed.data_ptr(), absmax.data_ptr<float>(), table.data_ptr<float>(), n, (int)block,
+                           out.data_ptr(), bf16 ? 1 : 0, sm_count(), cur_stream()),
+           "nf4_dequant");
+  return out;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "rl_project_b200 sm_100a kernels";
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rope_qkv_fwd", &rope_qkv_fwd);
+  m.def("rope_qkv_bwd", &rope_qkv_bwd);
+  m.def("rope_inplace", &rope_inplace);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("gelu", &gelu);
+  m.def("logprob_fwd", &logprob_fwd);
+  m.def("logprob_bwd_", &logprob_bwd_);
+  m.def("grad_norm", &grad_norm);
+  m.def("adam_step", &adam_step);
+  m.def("adam_chunk_size", &rlb_adam_chunk_size);
+  m.def("adam_tensor_desc_bytes", &rlb_adam_tensor_desc_bytes);
+  m.def("embed_fwd", &embed_fwd);
+  m.def("embed_bwd", &embed_bwd);
+  m.def("nf4_dequant", &nf4_dequant);
+}

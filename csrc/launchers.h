@@ -1,0 +1,46 @@
+// C-style launchers exported by the kernel translation units.
+#pragma once
+#include <cuda_runtime.h>
+
+cudaError_t rlb_rmsnorm_fwd(const void* x, const void* delta, const void* w, void* h_out, void* y, float* rstd,
+                            long long rows, int dim, float eps, int sms, cudaStream_t s);
+int rlb_rmsnorm_bwd_grid(long long rows, int sms);
+cudaError_t rlb_rmsnorm_bwd(const void* h, const void* w, const float* rstd, const void* dy, const void* dres,
+                            void* dx, float* dw_part, void* dw_out, int dw_is_f32, long long rows, int dim, int sms,
+                            cudaStream_t s);
+
+cudaError_t rlb_rope_qkv_fwd(const void* qkv, long long row_stride, void* q, void* k, void* v, const float* cos_t,
+                             const float* sin_t, const int* positions, int B, int T, int Hq, int Hkv, int D,
+                             int pos_offset, int heads_major, int sms, cudaStream_t s);
+cudaError_t rlb_rope_qkv_bwd(const void* dq, const void* dk, const void* dv, void* dqkv, long long row_stride,
+                             const float* cos_t, const float* sin_t, const int* positions, int B, int T, int Hq,
+                             int Hkv, int D, int pos_offset, int heads_major, int sms, cudaStream_t s);
+cudaError_t rlb_rope_inplace(void* x, int B, int T, int H, int D, long long sb, long long st, long long sh,
+                             const float* cos_t, const float* sin_t, const int* positions, int pos_offset,
+                             int inverse, int sms, cudaStream_t s);
+
+cudaError_t rlb_swiglu_fwd(const void* h13, void* out, long long rows, int F, int sms, cudaStream_t s);
+cudaError_t rlb_swiglu_bwd(const void* h13, const void* da, void* dh13, long long rows, int F, int sms,
+                           cudaStream_t s);
+cudaError_t rlb_gelu(const void* x, const void* dy, void* out, long long n, int sms, cudaStream_t s);
+
+cudaError_t rlb_logprob_fwd(const void* logits, long long ld, long long rows, int V, const long long* tgt,
+                            float* lse, float* lp, float* ent, int* status, cudaStream_t s);
+cudaError_t rlb_logprob_bwd(void* logits, long long ld, long long rows, int V, const long long* tgt,
+                            const float* lse, const float* g_lp, const float* ent, const float* g_ent, float scale,
+                            cudaStream_t s);
+
+int rlb_adam_chunk_size();
+int rlb_adam_tensor_desc_bytes();
+cudaError_t rlb_grad_norm(const void* tensors, const void* chunks, int nchunks, float* partial, int grid,
+                          float max_norm, float inv_scale, float* norm_coef, cudaStream_t s);
+cudaError_t rlb_adam_step(const void* tensors, const void* chunks, int nchunks, const float* coef, float lr, float b1,
+                          float b2, float eps, int step, int decoupled, int grid, cudaStream_t s);
+
+cudaError_t rlb_embed_fwd(const long long* idx, const void* W, void* out, long long n, int dim, long long vocab,
+                          int* status, int sms, cudaStream_t s);
+cudaError_t rlb_embed_bwd(const long long* sorted_ids, const long long* perm, const void* dy, void* dW, long long n,
+                          int dim, long long vocab, int sms, cudaStream_t s);
+
+cudaError_t rlb_nf4_dequant(const void* packed, const float* absmax, const float* table, long long n, int block,
+                            void* out, int out_bf16, int sms, cudaStream_t s);

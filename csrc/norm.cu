@@ -1,0 +1,197 @@
+// RMSNorm forward / backward, optionally fused with the residual add that
+// precedes it in a pre-norm block:
+//   h = x (+ delta);  y = h * rsqrt(mean(h^2) + eps) * w
+// One warp owns one row; each lane holds NV 16-byte vectors of the row in
+// registers, so the row is read from HBM exactly once per pass.
+// Semantics follow src/forgeline/models/transformer/norm.py:9-17 (fp32 statistics).
+#include "common.cuh"
+
+namespace rlb {
+
+template <int NV>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ delta,
+    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ h_out,
+    __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out, long long rows, int dim, float eps) {
+  const int lane = threadIdx.x & 31;
+  const long long warps_total = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows;
+       row += warps_total) {
+    const __nv_bfloat16* xr = x + row * dim;
+    float v[NV][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (lane + 32 * j) * 8;
+      if (c < dim) {
+        unpack8(ldg8(xr + c), v[j]);
+        if (delta != nullptr) {
+          float d[8];
+          unpack8(ldg8(delta + row * dim + c), d);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) v[j][k] += d[k];
+          // the residual stream is kept in bf16: round before the statistics so
+          // that forward and backward see the same h
+          bf16x8 hv = pack8(v[j]);
+          stg8(h_out + row * dim + c, hv);
+          unpack8(hv, v[j]);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss += v[j][k] * v[j][k];
+      }
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)dim + eps);
+    if (lane == 0 && rstd_out != nullptr) rstd_out[row] = r;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (lane + 32 * j) * 8;
+      if (c < dim) {
+        float wf[8], o[8];
+        unpack8(ldg8(w + c), wf);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = v[j][k] * r * wf[k];
+        stg8(y + row * dim + c, pack8(o));
+      }
+    }
+  }
+}
+
+// dx = r * (dxh - xh * mean(dxh * xh)),  dxh = dy * w,  xh = h * r
+// dx additionally gets `dres` (gradient arriving on the residual stream).
+// Per-block partial sums of dw = sum_rows dy * xh go to dw_part[blockIdx.x].
+template <int NV>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
+    const __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ w,
+    const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dy,
+    const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
+    float* __restrict__ dw_part, long long rows, int dim) {
+  extern __shared__ float smem[];  // [8 warps][dim]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float acc[NV][8];
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[j][k] = 0.f;
+  float wf[NV][8];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = (lane + 32 * j) * 8;
+    if (c < dim) unpack8(ldg8(w + c), wf[j]);
+  }
+  const long long warps_total = (long long)gridDim.x * 8;
+  for (long long row = (long long)blockIdx.x * 8 + warp; row < rows; row += warps_total) {
+    const float r = rstd[row];
+    float xh[NV][8], g[NV][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (lane + 32 * j) * 8;
+      if (c < dim) {
+        unpack8(ldg8(h + row * dim + c), xh[j]);
+        unpack8(ldg8(dy + row * dim + c), g[j]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          xh[j][k] *= r;
+          acc[j][k] += g[j][k] * xh[j][k];
+          g[j][k] *= wf[j][k];
+          dot += g[j][k] * xh[j][k];
+        }
+      }
+    }
+    dot = warp_sum(dot) / (float)dim;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (lane + 32 * j) * 8;
+      if (c < dim) {
+        float o[8];
+        float rr[8];
+        if (dres != nullptr) unpack8(ldg8(dres + row * dim + c), rr);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          o[k] = r * (g[j][k] - xh[j][k] * dot);
+          if (dres != nullptr) o[k] += rr[k];
+        }
+        stg8(dx + row * dim + c, pack8(o));
+      }
+    }
+  }
+  // reduce the 8 warps' dw partials through shared memory
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = (lane + 32 * j) * 8;
+    if (c < dim)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) smem[warp * dim + c + k] = acc[j][k];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < dim; c += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) s += smem[q * dim + c];
+    dw_part[(long long)blockIdx.x * dim + c] = s;
+  }
+}
+
+// Column sums of a [parts, dim] fp32 matrix -> dw (bf16 or fp32).
+__global__ void colsum_kernel(const float* __restrict__ part, int parts, int dim, float* __restrict__ out_f32,
+                              __nv_bfloat16* __restrict__ out_bf16) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= dim) return;
+  float s = 0.f;
+  for (int p = 0; p < parts; ++p) s += part[(long long)p * dim + c];
+  if (out_f32) out_f32[c] = s;
+  if (out_bf16) out_bf16[c] = __float2bfloat16(s);
+}
+
+static int pick_grid(long long rows, int sms) {
+  long long want = (rows + 7) / 8;
+  long long cap = (long long)sms * 8;
+  return (int)(want < cap ? want : cap);
+}
+
+#define RLB_NV_DISPATCH(dim, KERNEL_CALL)           \
+  do {                                              \
+    if ((dim) <= 256) { constexpr int NV = 1; KERNEL_CALL; }        \
+    else if ((dim) <= 512) { constexpr int NV = 2; KERNEL_CALL; }   \
+    else if ((dim) <= 1024) { constexpr int NV = 4; KERNEL_CALL; }  \
+    else if ((dim) <= 2048) { constexpr int NV = 8; KERNEL_CALL; }  \
+    else if ((dim) <= 4096) { constexpr int NV = 16; KERNEL_CALL; } \
+    else { return cudaErrorInvalidValue; }          \
+  } while (0)
+
+}  // namespace rlb
+
+using namespace rlb;
+
+// Launchers (return cudaError_t so bindings can raise).
+cudaError_t rlb_rmsnorm_fwd(const void* x, const void* delta, const void* w, void* h_out, void* y, float* rstd,
+                            long long rows, int dim, float eps, int sms, cudaStream_t s) {
+  if (dim % 8 != 0) return cudaErrorInvalidValue;
+  const int grid = pick_grid(rows, sms);
+  RLB_NV_DISPATCH(dim, (rmsnorm_fwd_kernel<NV><<<grid, 256, 0, s>>>(
+                           (const __nv_bfloat16*)x, (const __nv_bfloat16*)delta, (const __nv_bfloat16*)w,
+                           (__nv_bfloat16*)h_out, (__nv_bfloat16*)y, rstd, rows, dim, eps)));
+  return cudaGetLastError();
+}
+
+// dw_part must hold grid*dim floats where grid = rlb_rmsnorm_bwd_grid(rows, sms).
+int rlb_rmsnorm_bwd_grid(long long rows, int sms) { return pick_grid(rows, sms) < 1 ? 1 : pick_grid(rows, sms); }
+
+cudaError_t rlb_rmsnorm_bwd(const void* h, const void* w, const float* rstd, const void* dy, const void* dres,
+                            void* dx, float* dw_part, void* dw_out, int dw_is_f32, long long rows, int dim, int sms,
+                            cudaStream_t s) {
+  if (dim % 8 != 0) return cudaErrorInvalidValue;
+  const int grid = rlb_rmsnorm_bwd_grid(rows, sms);
+  const size_t smem = (size_t)8 * dim * sizeof(float);
+  RLB_NV_DISPATCH(dim, ({
+                    auto k = rmsnorm_bwd_kernel<NV>;
+                    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                    k<<<grid, 256, smem, s>>>((const __nv_bfloat16*)h, (const __nv_bfloat16*)w, rstd,
+                                              (const __nv_bfloat16*)dy, (const __nv_bfloat16*)dres,
+                                              (__nv_bfloat16*)dx, dw_part, rows, dim);
+                  }));
+  colsum_kernel<<<ceil_div(dim, 256), 256, 0, s>>>(dw_part, grid, dim, dw_is_f32 ? (float*)dw_out : nullptr,
+                                                   dw_is_f32 ? nullptr : (__nv_bfloat16*)dw_out);
+  return cudaGetLastError();
+}

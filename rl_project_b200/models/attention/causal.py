@@ -1,0 +1,83 @@
+"""Grouped-query causal self-attention with KV cache, sliding window and logit cap.
+
+Behaviour and parameter names follow ``src/forgeline/models/attention/causal.py:18-134``
+(``q_proj``/``k_proj``/``v_proj``/``c_proj``; window on every layer or on odd
+layers only; tanh soft-cap; ``(k, v)`` cache ``[B, Hkv, T, D]``).  The three
+projections run as ONE GEMM over the concatenated weight and RoPE is fused
+with the head split (csrc/rope.cu).
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+import torch.nn as nn
+
+from rl_project_b200.core.config import ModelSpec
+from rl_project_b200.ops.attention import attention_reference, causal_attention
+from rl_project_b200.ops.linear import linear
+from rl_project_b200.ops.rope import RopeTable, rope_split_qkv
+
+KVCache = Tuple[torch.Tensor, torch.Tensor]
+
+
+def layer_window(spec: ModelSpec, layer_id: int) -> int:
+    if spec.alternating_layers:
+        return spec.sliding_window if layer_id % 2 == 1 else 0
+    return spec.sliding_window if spec.sliding_window > 0 else 0
+
+
+class CausalSelfAttention(nn.Module):
+    def __init__(self, spec: ModelSpec, layer_id: int = 0):
+        super().__init__()
+        self.n_head = spec.n_head
+        self.n_kv_head = spec.n_kv_head
+        self.n_embd = spec.n_embd
+        self.head_dim = spec.n_embd // spec.n_head
+        self.n_rep = spec.n_head // spec.n_kv_head
+        self.dropout_rate = spec.dropout
+        self.use_rope = spec.use_rope
+        self.attn_logit_cap = spec.attn_logit_cap
+        self.window_size = layer_window(spec, layer_id)
+        self.q_proj = nn.Linear(spec.n_embd, spec.n_head * self.head_dim, bias=spec.bias)
+        self.k_proj = nn.Linear(spec.n_embd, spec.n_kv_head * self.head_dim, bias=spec.bias)
+        self.v_proj = nn.Linear(spec.n_embd, spec.n_kv_head * self.head_dim, bias=spec.bias)
+        self.c_proj = nn.Linear(spec.n_embd, spec.n_embd, bias=spec.bias)
+        self.resid_dropout = nn.Dropout(spec.dropout)
+        self.rope = RopeTable(self.head_dim, spec.rope_theta, spec.rope_scaling_type, spec.rope_scaling_factor,
+                              spec.block_size)
+
+    def _qkv(self, x: torch.Tensor) -> torch.Tensor:
+        mods = (self.q_proj, self.k_proj, self.v_proj)
+        if all(type(m) is nn.Linear for m in mods):
+            w = torch.cat([m.weight for m in mods], 0)
+            b = torch.cat([m.bias for m in mods], 0) if self.q_proj.bias is not None else None
+            return linear(x, w, b)
+        return torch.cat([m(x) for m in mods], dim=-1)
+
+    def _out(self, y: torch.Tensor) -> torch.Tensor:
+        if type(self.c_proj) is nn.Linear:
+            y = linear(y, self.c_proj.weight, self.c_proj.bias)
+        else:
+            y = self.c_proj(y)
+        return self.resid_dropout(y)
+
+    def forward(self, x: torch.Tensor, past_kv: Optional[KVCache] = None, positions: Optional[torch.Tensor] = None):
+        B, T, C = x.shape
+        qkv = self._qkv(x)
+        offset = past_kv[0].shape[2] if past_kv is not None else 0
+        q, k, v = rope_split_qkv(qkv, self.rope, self.n_head, self.n_kv_head, self.head_dim, offset=offset,
+                                 positions=positions, rotate=self.use_rope)
+        if past_kv is not None:
+            k = torch.cat([past_kv[0], k], dim=2)
+            v = torch.cat([past_kv[1], v], dim=2)
+        present = (k, v)
+        drop = self.dropout_rate if self.training else 0.0
+        if past_kv is None:
+            y = causal_attention(q, k, v, window=self.window_size, softcap=self.attn_logit_cap, dropout_p=drop)
+        else:
+            y = attention_reference(q, k, v, window=self.window_size, softcap=self.attn_logit_cap,
+                                    q_offset=k.shape[2] - T)
+        y = y.transpose(1, 2).reshape(B, T, C)
+        return self._out(y), present

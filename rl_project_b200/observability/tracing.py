@@ -1,0 +1,106 @@
+"""Timing: host spans (``Tracer``), CUDA-event device timers and NVTX ranges.
+
+``Tracer`` keeps the reference's span API (``src/forgeline/observability/tracing.py:11-57``).
+``CudaTimer`` measures on the device with CUDA events; ``max_over_ranks``
+reduces a per-rank device time to the slowest rank, which is how every
+multi-GPU number in this framework is reported.
+"""
+
+from __future__ import annotations
+
+import time
+from contextlib import contextmanager
+from dataclasses import dataclass, field
+from typing import Dict, Iterator, List, Optional
+
+import torch
+
+
+@dataclass
+class Span:
+    name: str
+    start: float
+    end: Optional[float] = None
+    attributes: Dict[str, object] = field(default_factory=dict)
+
+    @property
+    def duration_ms(self) -> float:
+        stop = self.end if self.end is not None else time.time()
+        return (stop - self.start) * 1e3
+
+
+class Tracer:
+    def __init__(self) -> None:
+        self.spans: List[Span] = []
+
+    @contextmanager
+    def span(self, name: str, **attributes: object) -> Iterator[Span]:
+        s = Span(name, time.time(), attributes=dict(attributes))
+        try:
+            yield s
+        finally:
+            s.end = time.time()
+            self.spans.append(s)
+
+    def durations(self, name: str) -> List[float]:
+        return [s.duration_ms for s in self.spans if s.name == name and s.end is not None]
+
+    def summary(self) -> Dict[str, Dict[str, float]]:
+        agg: Dict[str, Dict[str, float]] = {}
+        for s in self.spans:
+            row = agg.setdefault(s.name, {"count": 0.0, "total_ms": 0.0, "max_ms": 0.0})
+            d = s.duration_ms
+            row["count"] += 1
+            row["total_ms"] += d
+            row["max_ms"] = max(row["max_ms"], d)
+        for row in agg.values():
+            row["mean_ms"] = row["total_ms"] / max(1.0, row["count"])
+        return agg
+
+
+_TRACER = Tracer()
+
+
+def global_tracer() -> Tracer:
+    return _TRACER
+
+
+@contextmanager
+def nvtx_range(name: str) -> Iterator[None]:
+    if torch.cuda.is_available():
+        torch.cuda.nvtx.range_push(name)
+        try:
+            yield
+        finally:
+            torch.cuda.nvtx.range_pop()
+    else:
+        yield
+
+
+class CudaTimer:
+    """Device time between ``start()`` and ``stop()`` on the current stream (ms)."""
+
+    def __init__(self) -> None:
+        self._a = torch.cuda.Event(enable_timing=True)
+        self._b = torch.cuda.Event(enable_timing=True)
+
+    def start(self) -> None:
+        self._a.record()
+
+    def stop(self) -> float:
+        self._b.record()
+        self._b.synchronize()
+        return float(self._a.elapsed_time(self._b))
+
+
+def max_over_ranks(value: float, device: Optional[torch.device] = None) -> float:
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return float(value)
+    dev = device or (torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu"))
+    if dist.get_backend() == "gloo":
+        dev = torch.device("cpu")
+    t = torch.tensor([float(value)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())

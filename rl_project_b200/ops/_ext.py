@@ -1,0 +1,96 @@
+"""Loader for the in-tree sm_100a extension ``rl_project_b200._C``.
+
+On a CUDA tensor every op in this package runs its native kernel; if the
+extension is missing there, ``native()`` raises instead of silently falling
+back to an eager PyTorch path.  CPU tensors use the plain-PyTorch reference
+implementation of the same op (the numerics oracle and the CPU training path).
+"""
+
+from __future__ import annotations
+
+import os
+from typing import Any, Optional
+
+import torch
+
+_C: Optional[Any] = None
+_err: Optional[BaseException] = None
+
+try:  # pragma: no cover - depends on the build
+    from rl_project_b200 import _C as _C  # type: ignore[no-redef]
+except BaseException as exc:  # noqa: BLE001
+    _C = None
+    _err = exc
+
+
+# kernels launched by each binding (launch accounting for benchmarks)
+_LAUNCHES = {"rmsnorm_bwd": 2, "grad_norm": 2, "adam_chunk_size": 0, "adam_tensor_desc_bytes": 0}
+
+
+class _Counted:
+    """Forwards to the extension module and counts the kernels each call launches."""
+
+    def __init__(self, mod: Any):
+        self._mod = mod
+        self._fns: dict = {}
+        self.launches = 0
+
+    def __getattr__(self, name: str):
+        fns = self.__dict__["_fns"]
+        if name not in fns:
+            fn = getattr(self.__dict__["_mod"], name)
+            if not callable(fn):
+                return fn
+            n = _LAUNCHES.get(name, 1)
+
+            def call(*a, __fn=fn, __n=n, **k):
+                self.launches += __n
+                return __fn(*a, **k)
+
+            fns[name] = call
+        return fns[name]
+
+
+_counted = _Counted(_C) if _C is not None else None
+
+
+def available() -> bool:
+    return _C is not None
+
+
+def native() -> Any:
+    if _counted is None:
+        raise RuntimeError(
+            "rl_project_b200._C (the sm_100a kernel library) is not built or failed to load: "
+            f"{_err!r}. Build it with `python setup.py build_ext --inplace`."
+        )
+    return _counted
+
+
+def launch_count() -> int:
+    """Native kernels launched so far in this process (through the bindings)."""
+    return _counted.launches if _counted is not None else 0
+
+
+def count_launches(n: int) -> None:
+    """Record launches made outside the counted bindings (e.g. extensions built separately)."""
+    if _counted is not None:
+        _counted.launches += n
+
+
+def on_gpu(t: torch.Tensor) -> bool:
+    return t.is_cuda
+
+
+_SMS: dict = {}
+
+
+def sm_count(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SMS:
+        _SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SMS[idx]
+
+
+def debug_checks() -> bool:
+    return os.environ.get("RLB_DEBUG_BOUNDS", "0") == "1"

@@ -1,0 +1,179 @@
+"""Fused multi-tensor AdamW with fp32 master weights (kernel: csrc/adamw.cu).
+
+``FusedAdamW`` keeps bf16 parameters for compute and an fp32 master copy,
+``exp_avg`` and ``exp_avg_sq`` in three flat fp32 buffers (one allocation
+each).  One ``step`` is three launches regardless of the parameter count:
+squared-norm partials, the norm/clip finish, and the update itself; the clip
+coefficient never leaves the device.  Semantics match torch.optim.AdamW /
+Adam as configured by ``src/forgeline/training/common/optim.py:11-30``.
+"""
+
+from __future__ import annotations
+
+import struct
+from typing import Dict, Iterable, List, Optional
+
+import torch
+
+from rl_project_b200.ops._ext import native
+
+_DESC = struct.Struct("<QQQQQqfi")  # must equal sizeof(AdamTensor) in csrc/adamw.cu
+
+
+class FusedAdamW(torch.optim.Optimizer):
+    def __init__(self, params: Iterable, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
+                 weight_decay: float = 0.0, decoupled: bool = True):
+        defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
+        super().__init__(params, defaults)
+        self.decoupled = decoupled
+        self._flat: Dict[str, torch.Tensor] = {}
+        self._desc_key = None
+        self._desc = None
+        self._chunks = None
+        self._nchunks = 0
+        self._partial = None
+        self.norm_coef: Optional[torch.Tensor] = None
+        self._step = 0
+        self._init_state()
+
+    # ------------------------------------------------------------------ state
+    def _params(self) -> List[torch.nn.Parameter]:
+        return [p for g in self.param_groups for p in g["params"]]
+
+    def _init_state(self) -> None:
+        ps = self._params()
+        if not ps:
+            raise ValueError("no parameters")
+        dev = ps[0].device
+        if dev.type != "cuda":
+            raise ValueError("FusedAdamW runs on CUDA parameters; use torch.optim.AdamW on CPU")
+        total = sum(p.numel() for p in ps)
+        for name in ("master", "exp_avg", "exp_avg_sq"):
+            self._flat[name] = torch.zeros(total, dtype=torch.float32, device=dev)
+        off = 0
+        for p in ps:
+            n = p.numel()
+            st = self.state[p]
+            st["master"] = self._flat["master"][off:off + n].view_as(p)
+            st["master"].copy_(p.detach().float())
+            st["exp_avg"] = self._flat["exp_avg"][off:off + n].view_as(p)
+            st["exp_avg_sq"] = self._flat["exp_avg_sq"][off:off + n].view_as(p)
+            st["step"] = torch.zeros((), dtype=torch.float32)
+            off += n
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        self._partial = torch.empty(sms * 4, dtype=torch.float32, device=dev)
+        self.norm_coef = torch.zeros(2, dtype=torch.float32, device=dev)
+
+    def _build_desc(self) -> None:
+        C = native()
+        chunk = C.adam_chunk_size()
+        assert C.adam_tensor_desc_bytes() == _DESC.size
+        ps, wds, raw, chunks = [], [], bytearray(), []
+        for g in self.param_groups:
+            for p in g["params"]:
+                if p.grad is None:
+                    continue
+                ps.append(p)
+                wds.append(float(g["weight_decay"]))
+        key = tuple((p.data_ptr(), p.grad.data_ptr(), p.grad.dtype) for p in ps)
+        if key == self._desc_key:
+            return
+        for i, (p, wd) in enumerate(zip(ps, wds)):
+            st = self.state[p]
+            g = p.grad
+            if not g.is_contiguous():
+                raise RuntimeError("FusedAdamW needs contiguous gradients")
+            p16 = p.data_ptr() if p.dtype == torch.bfloat16 else 0
+            if p.dtype not in (torch.bfloat16, torch.float32):
+                raise RuntimeError(f"unsupported parameter dtype {p.dtype}")
+            if p.dtype == torch.float32:
+                # fp32 parameters: the parameter itself is the master copy
+                st["master"] = p.data
+            raw += _DESC.pack(st["master"].data_ptr(), p16, g.data_ptr(), st["exp_avg"].data_ptr(),
+                              st["exp_avg_sq"].data_ptr(), p.numel(), wd, 1 if g.dtype == torch.bfloat16 else 0)
+            for c in range((p.numel() + chunk - 1) // chunk):
+                chunks.extend((i, c))
+        dev = ps[0].device
+        self._desc = torch.frombuffer(bytes(raw), dtype=torch.uint8).to(dev)
+        self._chunks = torch.tensor(chunks, dtype=torch.int32).to(dev)
+        self._nchunks = len(chunks) // 2
+        self._desc_key = key
+
+    # ------------------------------------------------------------------ step
+    @torch.no_grad()
+    def clip_grad_norm(self, max_norm: float, inv_scale: float = 1.0) -> torch.Tensor:
+        """Compute the global grad norm on device and arm the clip coefficient for ``step``.
+
+        Returns a 0-d device tensor with the (unscaled) norm; nothing is synchronised.
+        """
+        self._build_desc()
+        native().grad_norm(self._desc, self._chunks, self._nchunks, self._partial, float(max_norm),
+                           float(inv_scale), self.norm_coef)
+        self._armed = True
+        return self.norm_coef[0]
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = closure() if closure is not None else None
+        self._build_desc()
+        if self._nchunks == 0:
+            return loss
+        if not getattr(self, "_armed", False):
+            self.norm_coef.fill_(1.0)
+        self._armed = False
+        self._step += 1
+        g0 = self.param_groups[0]
+        lrs = {float(g["lr"]) for g in self.param_groups}
+        if len(lrs) != 1:
+            raise RuntimeError("FusedAdamW expects one learning rate for all groups")
+        b1, b2 = g0["betas"]
+        for g in self.param_groups:
+            for p in g["params"]:
+                if p.grad is not None:
+                    self.state[p]["step"] += 1
+        native().adam_step(self._desc, self._chunks, self._nchunks, self.norm_coef, float(g0["lr"]), float(b1),
+                           float(b2), float(g0["eps"]), self._step, self.decoupled)
+        return loss
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        super().zero_grad(set_to_none=set_to_none)
+
+    # ------------------------------------------------------------------ (de)serialisation
+    def state_dict(self):
+        sd = super().state_dict()
+        # detach views from the flat buffers so a checkpoint stores each tensor once
+        for st in sd["state"].values():
+            for k, v in list(st.items()):
+                if isinstance(v, torch.Tensor):
+                    st[k] = v.detach().clone()
+        sd["fused_step"] = self._step
+        return sd
+
+    def load_state_dict(self, state_dict) -> None:
+        ps = self._params()
+        saved = state_dict.get("state", {})
+        for i, p in enumerate(ps):
+            src = saved.get(i, {})
+            st = self.state[p]
+            for k in ("exp_avg", "exp_avg_sq", "master"):
+                if k in src:
+                    st[k].copy_(src[k].to(st[k].device, torch.float32))
+                elif k == "master":
+                    st[k].copy_(p.detach().float())
+            if "step" in src:
+                st["step"] = torch.as_tensor(src["step"], dtype=torch.float32).clone()
+        for g, sg in zip(self.param_groups, state_dict.get("param_groups", [])):
+            for k, v in sg.items():
+                if k != "params":
+                    g[k] = v
+        self._step = int(state_dict.get("fused_step", max((int(s.get("step", 0)) for s in saved.values()),
+                                                          default=0)))
+        # re-derive the bf16 compute weights from the restored masters
+        with torch.no_grad():
+            for p in ps:
+                if p.dtype != torch.float32:
+                    p.copy_(self.state[p]["master"].to(p.dtype))
+        self._desc_key = None
+
+    def master_params(self) -> Dict[torch.nn.Parameter, torch.Tensor]:
+        return {p: self.state[p]["master"] for p in self._params()}

@@ -1,0 +1,174 @@
+"""Distributed strategies behind one interface (``DistributedStrategy`` protocol,
+``src/forgeline/distributed/strategies.py:17-218`` names):
+single, ddp, fsdp, zero2, deepspeed, tensor_parallel, pipeline_parallel,
+expert_parallel, hybrid (3-D mesh).
+
+Each strategy validates on CPU; ``setup`` only creates a process group when
+launched (or when a 1-process group is explicitly allowed).
+"""
+
+from __future__ import annotations
+
+from typing import Any, Optional
+
+import torch
+import torch.nn as nn
+
+from rl_project_b200.core.config import DistributedConfig
+from rl_project_b200.core.errors import DistributedConfigError, OptionalDependencyError
+from rl_project_b200.parallel import runtime as rt
+
+
+class SingleProcessStrategy:
+    name = "single"
+
+    def __init__(self, cfg: Optional[DistributedConfig] = None):
+        self.cfg = cfg or DistributedConfig()
+
+    def setup(self) -> None:
+        pass
+
+    def wrap_model(self, model: nn.Module) -> nn.Module:
+        return model
+
+    def unwrap_model(self, model: nn.Module) -> nn.Module:
+        return model
+
+    def is_main_process(self) -> bool:
+        return True
+
+    def world_size(self) -> int:
+        return 1
+
+    def rank(self) -> int:
+        return 0
+
+    def barrier(self) -> None:
+        pass
+
+    def teardown(self) -> None:
+        pass
+
+
+class _ProcessGroupStrategy(SingleProcessStrategy):
+    def __init__(self, cfg: DistributedConfig, allow_single_process: bool = True):
+        super().__init__(cfg)
+        self.allow_single_process = allow_single_process
+        self.info: Optional[rt.DistributedInfo] = None
+
+    def setup(self) -> None:
+        env = rt.read_launcher_env()
+        if not env.launched and not self.allow_single_process:
+            raise DistributedConfigError(f"{self.name} strategy requires a torchrun launch (RANK/WORLD_SIZE not set)")
+        self.info = rt.init_process_group(self.cfg.backend, timeout_s=self.cfg.timeout_s)
+
+    def is_main_process(self) -> bool:
+        return rt.is_main_process()
+
+    def world_size(self) -> int:
+        return rt.world_size()
+
+    def rank(self) -> int:
+        return rt.rank()
+
+    def barrier(self) -> None:
+        rt.barrier()
+
+    def teardown(self) -> None:
+        rt.destroy_process_group()
+
+    def unwrap_model(self, model: nn.Module) -> nn.Module:
+        return getattr(model, "module", model)
+
+
+class DDPStrategy(_ProcessGroupStrategy):
+    """Replicated parameters; bucketed gradient all-reduce after accumulation (Trainer-driven)."""
+
+    name = "ddp"
+
+    def wrap_model(self, model: nn.Module) -> nn.Module:
+        if not rt.is_initialized():
+            raise DistributedConfigError("call setup() before wrap_model()")
+        if rt.world_size() == 1:
+            return model
+        from torch.nn.parallel import DistributedDataParallel as DDP
+
+        ids = [self.info.local_rank] if self.info and torch.cuda.is_available() else None
+        return DDP(model, device_ids=ids, find_unused_parameters=True)
+
+
+class DeepSpeedStrategy(_ProcessGroupStrategy):
+    name = "deepspeed"
+
+    def __init__(self, cfg: DistributedConfig):
+        super().__init__(cfg)
+        self.config_path = cfg.deepspeed_config
+
+    @staticmethod
+    def load_config(path: str) -> dict:
+        import json
+        from pathlib import Path
+
+        p = Path(path)
+        if not p.exists():
+            raise DistributedConfigError(f"deepspeed config not found: {path}")
+        data = json.loads(p.read_text())
+        if "zero_optimization" not in data:
+            raise DistributedConfigError("deepspeed config must contain zero_optimization")
+        return data
+
+    def initialize(self, model: nn.Module, optimizer=None) -> Any:
+        try:
+            import deepspeed
+        except ImportError as exc:
+            raise OptionalDependencyError("deepspeed is not installed",
+                                          hint="Use strategy=zero2 (the native ZeRO-2) instead.") from exc
+        engine, _, _, _ = deepspeed.initialize(model=model, optimizer=optimizer, config=self.load_config(self.config_path),
+                                               model_parameters=[p for p in model.parameters() if p.requires_grad])
+        return engine
+
+    def wrap_model(self, model: nn.Module) -> nn.Module:
+        return self.initialize(model)
+
+
+def _lazy(name: str):
+    def make(cfg: DistributedConfig):
+        if name == "fsdp":
+            from rl_project_b200.parallel.fsdp import FSDPStrategy
+
+            return FSDPStrategy(cfg)
+        if name == "zero2":
+            from rl_project_b200.parallel.fsdp import FSDPStrategy
+
+            return FSDPStrategy(cfg, reshard_params=False, name="zero2")
+        if name in ("tensor_parallel", "pipeline_parallel", "hybrid"):
+            from rl_project_b200.parallel.mesh_strategies import MeshStrategy
+
+            return MeshStrategy(cfg, name)
+        if name == "expert_parallel":
+            from rl_project_b200.parallel.expert import ExpertParallelStrategy
+
+            return ExpertParallelStrategy(cfg)
+        raise DistributedConfigError(f"unknown strategy {name!r}")
+
+    return make
+
+
+STRATEGIES = {
+    "single": SingleProcessStrategy,
+    "ddp": DDPStrategy,
+    "deepspeed": DeepSpeedStrategy,
+    "fsdp": _lazy("fsdp"),
+    "zero2": _lazy("zero2"),
+    "tensor_parallel": _lazy("tensor_parallel"),
+    "pipeline_parallel": _lazy("pipeline_parallel"),
+    "hybrid": _lazy("hybrid"),
+    "expert_parallel": _lazy("expert_parallel"),
+}
+
+
+def build_strategy(cfg: DistributedConfig):
+    cfg.validate()
+    if cfg.strategy not in STRATEGIES:
+        raise DistributedConfigError(f"unknown strategy {cfg.strategy!r}")
+    return STRATEGIES[cfg.strategy](cfg)
