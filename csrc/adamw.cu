@@ -57,12 +57,17 @@ __global__ void __launch_bounds__(256) sumsq_kernel(const AdamTensor* __restrict
 
 // clip_coef = min(1, max_norm / (norm + 1e-6)) (torch.nn.utils.clip_grad_norm_), also
 // records the norm.  max_norm <= 0 disables clipping (coef 1).
-__global__ void finish_norm_kernel(const float* __restrict__ partial, int parts, float max_norm, float inv_scale,
-                                   float* __restrict__ norm_out, float* __restrict__ coef_out) {
+// (no __restrict__: the distributed finish reads and writes norm_coef in place)
+__global__ void finish_norm_kernel(const float* partial, int parts, float max_norm, float inv_scale, float* norm_out,
+                                   float* coef_out, int squared_only) {
   __shared__ float scratch[32];
   float acc = 0.f;
   for (int i = threadIdx.x; i < parts; i += blockDim.x) acc += partial[i];
   acc = block_sum(acc, scratch);
+  if (threadIdx.x == 0 && squared_only) {
+    norm_out[0] = acc;  // sum of squares of this rank's shards; the host all-reduces it, then finishes
+    return;
+  }
   if (threadIdx.x == 0) {
     const float norm = sqrtf(acc) * inv_scale;
     norm_out[0] = norm;
@@ -108,9 +113,15 @@ int rlb_adam_chunk_size() { return kChunk; }
 // `tensors`/`chunks` are device arrays (built once by the host).  `partial`
 // holds >= grid floats; `norm_coef` 2 floats: [norm, coef].
 cudaError_t rlb_grad_norm(const void* tensors, const void* chunks, int nchunks, float* partial, int grid,
-                          float max_norm, float inv_scale, float* norm_coef, cudaStream_t s) {
+                          float max_norm, float inv_scale, float* norm_coef, int squared_only, cudaStream_t s) {
   sumsq_kernel<<<grid, 256, 0, s>>>((const AdamTensor*)tensors, (const ChunkRef*)chunks, nchunks, partial);
-  finish_norm_kernel<<<1, 1024, 0, s>>>(partial, grid, max_norm, inv_scale, norm_coef, norm_coef + 1);
+  finish_norm_kernel<<<1, 1024, 0, s>>>(partial, grid, max_norm, inv_scale, norm_coef, norm_coef + 1, squared_only);
+  return cudaGetLastError();
+}
+
+// Second half of a distributed norm: norm_coef[0] holds the all-reduced sum of squares.
+cudaError_t rlb_grad_norm_finish(float* norm_coef, float max_norm, float inv_scale, cudaStream_t s) {
+  finish_norm_kernel<<<1, 32, 0, s>>>(norm_coef, 1, max_norm, inv_scale, norm_coef, norm_coef + 1, 0);
   return cudaGetLastError();
 }
 

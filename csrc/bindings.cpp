@@ -219,12 +219,18 @@ void logprob_bwd_(at::Tensor& logits, const c10::optional<at::Tensor>& targets, 
 
 // ---------------------------------------------------------------- AdamW
 void grad_norm(const at::Tensor& tensors, const at::Tensor& chunks, int64_t nchunks, at::Tensor& partial,
-               double max_norm, double inv_scale, at::Tensor& norm_coef) {
+               double max_norm, double inv_scale, at::Tensor& norm_coef, bool squared_only) {
   const c10::cuda::CUDAGuard g(partial.device());
   CHECK_OK(rlb_grad_norm(tensors.data_ptr(), chunks.data_ptr(), (int)nchunks, partial.data_ptr<float>(),
                          (int)partial.numel(), (float)max_norm, (float)inv_scale, norm_coef.data_ptr<float>(),
-                         cur_stream()),
+                         squared_only ? 1 : 0, cur_stream()),
            "grad_norm");
+}
+
+void grad_norm_finish(at::Tensor& norm_coef, double max_norm, double inv_scale) {
+  const c10::cuda::CUDAGuard g(norm_coef.device());
+  CHECK_OK(rlb_grad_norm_finish(norm_coef.data_ptr<float>(), (float)max_norm, (float)inv_scale, cur_stream()),
+           "grad_norm_finish");
 }
 
 void adam_step(const at::Tensor& tensors, const at::Tensor& chunks, int64_t nchunks,
@@ -294,6 +300,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("logprob_fwd", &logprob_fwd);
   m.def("logprob_bwd_", &logprob_bwd_);
   m.def("grad_norm", &grad_norm);
+  m.def("grad_norm_finish", &grad_norm_finish);
   m.def("adam_step", &adam_step);
   m.def("adam_chunk_size", &rlb_adam_chunk_size);
   m.def("adam_tensor_desc_bytes", &rlb_adam_tensor_desc_bytes);

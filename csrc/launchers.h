@@ -33,7 +33,8 @@ cudaError_t rlb_logprob_bwd(void* logits, long long ld, long long rows, int V, c
 int rlb_adam_chunk_size();
 int rlb_adam_tensor_desc_bytes();
 cudaError_t rlb_grad_norm(const void* tensors, const void* chunks, int nchunks, float* partial, int grid,
-                          float max_norm, float inv_scale, float* norm_coef, cudaStream_t s);
+                          float max_norm, float inv_scale, float* norm_coef, int squared_only, cudaStream_t s);
+cudaError_t rlb_grad_norm_finish(float* norm_coef, float max_norm, float inv_scale, cudaStream_t s);
 cudaError_t rlb_adam_step(const void* tensors, const void* chunks, int nchunks, const float* coef, float lr, float b1,
                           float b2, float eps, int step, int decoupled, int grid, cudaStream_t s);
 

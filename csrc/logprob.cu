@@ -104,10 +104,11 @@ __global__ void __launch_bounds__(THREADS) logprob_bwd_kernel(
   const long long r = blockIdx.x;
   __nv_bfloat16* row = logits + r * ld;
   const float L = lse[r];
-  const float a = g_lp ? g_lp[r] * scale : 0.f;
+  const long long tg = tgt ? tgt[r] : -1;
+  // rows with an ignored target output lp = 0 (a constant): no gradient through that term
+  const float a = (g_lp && tg >= 0) ? g_lp[r] * scale : 0.f;
   const float b = g_ent ? g_ent[r] * scale : 0.f;
   const float H = (g_ent && ent) ? ent[r] : 0.f;
-  const long long tg = tgt ? tgt[r] : -1;
   const bool vec = (ld % 8 == 0);
   int tail_start = 0;
   if (vec) {

@@ -47,13 +47,18 @@ class TransformerBlock(nn.Module):
         self.use_moe = bool(spec.use_moe and layer_id >= spec.n_dense_layers)
         self.ffn = MoELayer(spec) if self.use_moe else build_dense_ffn(spec)
 
-    def forward(self, x: torch.Tensor, past_kv: Optional[Any] = None, positions=None):
+    def forward(self, x: torch.Tensor, past_kv: Optional[Any] = None, positions=None, *,
+                pending: Optional[torch.Tensor] = None, fused: bool = False):
+        if fused:
+            return self.forward_fused(x, pending)
         a, present = self.attn(self.ln_1(x), past_kv=past_kv, positions=positions)
         x, h = add_rms_norm(x, a, self.ln_2.weight, self.ln_2.eps)
         return x + self.ffn(h), present
 
     def forward_fused(self, x: torch.Tensor, pending: Optional[torch.Tensor]) -> Tuple[torch.Tensor, torch.Tensor]:
-        """Returns ``(x, f)`` with the block output equal to ``x + f`` (add left pending)."""
+        """Returns ``(x, f)`` with the block output equal to ``x + f`` (add left pending).
+
+        Call it as ``block(x, pending=p, fused=True)`` so module hooks (FSDP gathers) run."""
         if pending is None:
             h = rms_norm(x, self.ln_1.weight, self.ln_1.eps)
         else:

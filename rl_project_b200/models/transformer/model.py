@@ -139,9 +139,10 @@ class TransformerLM(nn.Module):
         ckpt = self.gradient_checkpointing and self.training
         for blk in self.transformer.h:
             if ckpt:
-                x, pending = torch.utils.checkpoint.checkpoint(blk.forward_fused, x, pending, use_reentrant=False)
+                x, pending = torch.utils.checkpoint.checkpoint(blk, x, pending=pending, fused=True,
+                                                               use_reentrant=False)
             else:
-                x, pending = blk.forward_fused(x, pending)
+                x, pending = blk(x, pending=pending, fused=True)
             if blk.use_moe and blk.ffn.aux_loss is not None:
                 self.aux_losses.append(blk.ffn.aux_loss)
         ln_f = self.transformer.ln_f

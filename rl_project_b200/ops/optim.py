@@ -22,10 +22,19 @@ _DESC = struct.Struct("<QQQQQqfi")  # must equal sizeof(AdamTensor) in csrc/adam
 
 class FusedAdamW(torch.optim.Optimizer):
     def __init__(self, params: Iterable, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
-                 weight_decay: float = 0.0, decoupled: bool = True):
+                 weight_decay: float = 0.0, decoupled: bool = True, param16: Optional[dict] = None,
+                 segments: Optional[dict] = None, process_group=None, post_step=None):
+        """``param16``: fp32 parameter -> bf16 tensor rewritten by the update (sharded training).
+        ``segments``: parameter -> [(start, end, weight_decay)] element ranges, each updated with its
+        own decay (flat shards that mix matrices and vectors).  ``process_group``: the gradient norm
+        is summed over it (sharded gradients).  ``post_step``: called after every update."""
         defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
         super().__init__(params, defaults)
         self.decoupled = decoupled
+        self._param16 = dict(param16 or {})
+        self._segments = dict(segments or {})
+        self._group = process_group
+        self._post_step = post_step
         self._flat: Dict[str, torch.Tensor] = {}
         self._desc_key = None
         self._desc = None
@@ -75,26 +84,35 @@ class FusedAdamW(torch.optim.Optimizer):
                     continue
                 ps.append(p)
                 wds.append(float(g["weight_decay"]))
-        key = tuple((p.data_ptr(), p.grad.data_ptr(), p.grad.dtype) for p in ps)
+        key = tuple((p.data_ptr(), p.grad.data_ptr(), p.grad.dtype) for p in ps) + tuple(
+            (a.data_ptr(),) for a in self._param16.values())
         if key == self._desc_key:
             return
-        for i, (p, wd) in enumerate(zip(ps, wds)):
+        entry = 0
+        for p, wd in zip(ps, wds):
             st = self.state[p]
             g = p.grad
             if not g.is_contiguous():
                 raise RuntimeError("FusedAdamW needs contiguous gradients")
-            p16 = p.data_ptr() if p.dtype == torch.bfloat16 else 0
             if p.dtype not in (torch.bfloat16, torch.float32):
                 raise RuntimeError(f"unsupported parameter dtype {p.dtype}")
             if p.dtype == torch.float32:
                 # fp32 parameters: the parameter itself is the master copy
                 st["master"] = p.data
-            raw += _DESC.pack(st["master"].data_ptr(), p16, g.data_ptr(), st["exp_avg"].data_ptr(),
-                              st["exp_avg_sq"].data_ptr(), p.numel(), wd, 1 if g.dtype == torch.bfloat16 else 0)
-            for c in range((p.numel() + chunk - 1) // chunk):
-                chunks.extend((i, c))
+            alias = self._param16.get(p)
+            p16 = alias if alias is not None else (p if p.dtype == torch.bfloat16 else None)
+            gb = 1 if g.dtype == torch.bfloat16 else 0
+            for (a, b, seg_wd) in self._segments.get(p, [(0, p.numel(), wd)]):
+                if b <= a:
+                    continue
+                raw += _DESC.pack(st["master"].data_ptr() + 4 * a, (p16.data_ptr() + 2 * a) if p16 is not None else 0,
+                                  g.data_ptr() + g.element_size() * a, st["exp_avg"].data_ptr() + 4 * a,
+                                  st["exp_avg_sq"].data_ptr() + 4 * a, b - a, float(seg_wd), gb)
+                for c in range((b - a + chunk - 1) // chunk):
+                    chunks.extend((entry, c))
+                entry += 1
         dev = ps[0].device
-        self._desc = torch.frombuffer(bytes(raw), dtype=torch.uint8).to(dev)
+        self._desc = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(dev)
         self._chunks = torch.tensor(chunks, dtype=torch.int32).to(dev)
         self._nchunks = len(chunks) // 2
         self._desc_key = key
@@ -107,8 +125,15 @@ class FusedAdamW(torch.optim.Optimizer):
         Returns a 0-d device tensor with the (unscaled) norm; nothing is synchronised.
         """
         self._build_desc()
-        native().grad_norm(self._desc, self._chunks, self._nchunks, self._partial, float(max_norm),
-                           float(inv_scale), self.norm_coef)
+        if self._group is None or not torch.distributed.is_initialized() or \
+                torch.distributed.get_world_size(self._group) == 1:
+            native().grad_norm(self._desc, self._chunks, self._nchunks, self._partial, float(max_norm),
+                               float(inv_scale), self.norm_coef, False)
+        else:
+            native().grad_norm(self._desc, self._chunks, self._nchunks, self._partial, float(max_norm),
+                               float(inv_scale), self.norm_coef, True)
+            torch.distributed.all_reduce(self.norm_coef[:1], group=self._group)
+            native().grad_norm_finish(self.norm_coef, float(max_norm), float(inv_scale))
         self._armed = True
         return self.norm_coef[0]
 
@@ -133,6 +158,8 @@ class FusedAdamW(torch.optim.Optimizer):
                     self.state[p]["step"] += 1
         native().adam_step(self._desc, self._chunks, self._nchunks, self.norm_coef, float(g0["lr"]), float(b1),
                            float(b2), float(g0["eps"]), self._step, self.decoupled)
+        if self._post_step is not None:
+            self._post_step()
         return loss
 
     def zero_grad(self, set_to_none: bool = True) -> None:
@@ -173,6 +200,8 @@ class FusedAdamW(torch.optim.Optimizer):
             for p in ps:
                 if p.dtype != torch.float32:
                     p.copy_(self.state[p]["master"].to(p.dtype))
+                if p in self._param16:
+                    self._param16[p].copy_(self.state[p]["master"].to(self._param16[p].dtype))
         self._desc_key = None
 
     def master_params(self) -> Dict[torch.nn.Parameter, torch.Tensor]:

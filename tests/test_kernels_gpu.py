@@ -163,7 +163,7 @@ def test_fused_adamw_matches_torch():
     shapes = [(300, 200), (200,), (70000,)]
     masters = [torch.randn(s, device=DEV) for s in shapes]
     p16 = [torch.nn.Parameter(m.to(BF)) for m in masters]
-    p32 = [torch.nn.Parameter(m.clone()) for m in masters]
+    p32 = [torch.nn.Parameter(m.to(BF).float()) for m in masters]  # masters start from the bf16 weights
     opt = FusedAdamW([{"params": p16[:1] + p16[2:], "weight_decay": 0.1}, {"params": p16[1:2], "weight_decay": 0.0}],
                      lr=1e-2, betas=(0.9, 0.95), eps=1e-8)
     ref = torch.optim.AdamW([{"params": p32[:1] + p32[2:], "weight_decay": 0.1},
