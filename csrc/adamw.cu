@@ -38,6 +38,26 @@ RLB_DEVICE float load_grad(const AdamTensor& t, long long i) {
   return t.grad_bf16 ? __bfloat162float(((const __nv_bfloat16*)t.grad)[i]) : ((const float*)t.grad)[i];
 }
 
+RLB_DEVICE bool aligned(const void* p, int bytes) { return (((uintptr_t)p) & (bytes - 1)) == 0; }
+
+// 4 consecutive gradient values (vector load when aligned)
+RLB_DEVICE void load_grad4(const AdamTensor& t, long long i, float* g) {
+  if (t.grad_bf16) {
+    const uint2 u = *(const uint2*)((const __nv_bfloat16*)t.grad + i);
+    const float2 a = __bfloat1622float2(*(const __nv_bfloat162*)&u.x);
+    const float2 b = __bfloat1622float2(*(const __nv_bfloat162*)&u.y);
+    g[0] = a.x; g[1] = a.y; g[2] = b.x; g[3] = b.y;
+  } else {
+    const float4 f = *(const float4*)((const float*)t.grad + i);
+    g[0] = f.x; g[1] = f.y; g[2] = f.z; g[3] = f.w;
+  }
+}
+
+RLB_DEVICE bool vec_ok(const AdamTensor& t) {
+  return aligned(t.master, 16) && aligned(t.m, 16) && aligned(t.v, 16) && aligned(t.grad, t.grad_bf16 ? 8 : 16) &&
+         (t.param16 == nullptr || aligned(t.param16, 8));
+}
+
 __global__ void __launch_bounds__(256) sumsq_kernel(const AdamTensor* __restrict__ ts, const ChunkRef* __restrict__ chunks,
                                                     int nchunks, float* __restrict__ partial) {
   __shared__ float scratch[8];
@@ -46,7 +66,17 @@ __global__ void __launch_bounds__(256) sumsq_kernel(const AdamTensor* __restrict
     const AdamTensor t = ts[chunks[c].tensor];
     const long long base = (long long)chunks[c].chunk * kChunk;
     const long long end = min(base + kChunk, t.n);
-    for (long long i = base + threadIdx.x; i < end; i += blockDim.x) {
+    long long i0 = base;
+    if (vec_ok(t)) {
+      const long long vend = base + ((end - base) & ~3LL);
+      for (long long i = base + 4 * threadIdx.x; i < vend; i += 4 * blockDim.x) {
+        float g[4];
+        load_grad4(t, i, g);
+        acc += g[0] * g[0] + g[1] * g[1] + g[2] * g[2] + g[3] * g[3];
+      }
+      i0 = vend;
+    }
+    for (long long i = i0 + threadIdx.x; i < end; i += blockDim.x) {
       const float g = load_grad(t, i);
       acc += g * g;
     }
@@ -88,7 +118,39 @@ __global__ void __launch_bounds__(256) adam_kernel(const AdamTensor* __restrict_
     const AdamTensor t = ts[chunks[c].tensor];
     const long long base = (long long)chunks[c].chunk * kChunk;
     const long long end = min(base + kChunk, t.n);
-    for (long long i = base + threadIdx.x; i < end; i += blockDim.x) {
+    long long i0 = base;
+    if (vec_ok(t)) {
+      const long long vend = base + ((end - base) & ~3LL);
+      for (long long i = base + 4 * threadIdx.x; i < vend; i += 4 * blockDim.x) {
+        float g[4];
+        load_grad4(t, i, g);
+        float4 p4 = *(float4*)(t.master + i), m4 = *(float4*)(t.m + i), v4 = *(float4*)(t.v + i);
+        float* p = (float*)&p4;
+        float* m = (float*)&m4;
+        float* v = (float*)&v4;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float gk = g[k] * coef;
+          if (decoupled) p[k] -= lr * t.wd * p[k];
+          else gk += t.wd * p[k];
+          m[k] = b1 * m[k] + (1.f - b1) * gk;
+          v[k] = b2 * v[k] + (1.f - b2) * gk * gk;
+          p[k] -= lr * (m[k] / bc1) / (sqrtf(v[k] / bc2) + eps);
+        }
+        *(float4*)(t.master + i) = p4;
+        *(float4*)(t.m + i) = m4;
+        *(float4*)(t.v + i) = v4;
+        if (t.param16) {
+          __nv_bfloat162 lo = __floats2bfloat162_rn(p[0], p[1]), hi = __floats2bfloat162_rn(p[2], p[3]);
+          uint2 u;
+          u.x = *(uint32_t*)&lo;
+          u.y = *(uint32_t*)&hi;
+          *(uint2*)(t.param16 + i) = u;
+        }
+      }
+      i0 = vend;
+    }
+    for (long long i = i0 + threadIdx.x; i < end; i += blockDim.x) {
       float p = t.master[i];
       float g = load_grad(t, i) * coef;
       if (decoupled) p -= lr * t.wd * p;

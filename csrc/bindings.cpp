@@ -77,7 +77,7 @@ std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& h, const at::Tensor& w, co
   const int dim = (int)h.size(-1);
   const long long rows = h.numel() / dim;
   auto dx = at::empty_like(h);
-  const int grid = rlb_rmsnorm_bwd_grid(rows, sm_count());
+  const int grid = rlb_rmsnorm_bwd_parts(rows, dim, sm_count());
   auto part = at::empty({grid, dim}, h.options().dtype(at::kFloat));
   auto dw = at::empty_like(w);
   CHECK_OK(rlb_rmsnorm_bwd(h.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), dy.data_ptr(), opt_ptr(dres),
@@ -285,6 +285,23 @@ at::Tensor nf4_dequant(const at::Tensor& packed, const at::Tensor& absmax, const
   return out;
 }
 
+// ---------------------------------------------------------------- tcgen05 GEMM
+// out[M, N] (bf16 or fp32) = alpha * A B^T with A / B in K-major or MN-major storage.
+void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t a_mn, int64_t b_mn, int64_t epi, int64_t M,
+          int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, double alpha,
+          const c10::optional<at::Tensor>& status) {
+  check_bf16(A, "A");
+  check_bf16(B, "B");
+  check_cuda(out, "out");
+  TORCH_CHECK((epi == 0 && out.scalar_type() == at::kBFloat16) || (epi != 0 && out.scalar_type() == at::kFloat),
+              "gemm output dtype does not match the epilogue");
+  const c10::cuda::CUDAGuard g(A.device());
+  CHECK_OK(rlb_gemm((int)a_mn, (int)b_mn, (int)epi, (int)M, (int)N, (int)K, A.data_ptr(), lda, B.data_ptr(), ldb,
+                    out.data_ptr(), ldc, (float)alpha, status.has_value() ? status->data_ptr<int>() : nullptr,
+                    sm_count(), cur_stream()),
+           "gemm");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -307,4 +324,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_fwd", &embed_fwd);
   m.def("embed_bwd", &embed_bwd);
   m.def("nf4_dequant", &nf4_dequant);
+  m.def("gemm", &gemm);
 }

@@ -1,0 +1,337 @@
+// Persistent tcgen05 GEMM for sm_100a:  C[M, N] = A[M, K] * B[N, K]^T  (bf16 in, fp32 accumulate).
+//
+// Operand layouts (template flags):
+//   A_MN = 0: A stored [M][K] (K contiguous)      A_MN = 1: A stored [K][M] (M contiguous)
+//   B_MN = 0: B stored [N][K] (K contiguous)      B_MN = 1: B stored [K][N] (N contiguous)
+// which covers a linear layer's forward (x W^T: 0/0), input gradient
+// (dy W: 0/1) and weight gradient (dy^T x: 1/1) without any transposes.
+//
+// Structure (one CTA per SM, 192 threads):
+//   warp 0      TMA producer: fills a 4-stage shared-memory ring (A 128x64, B 256x64
+//               bf16 tiles, 128-B swizzle), completion counted on mbarriers.
+//   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators) and one
+//               elected thread issues tcgen05.mma (M=128, N=256, K=16) per 16-wide
+//               K step; tcgen05.commit releases smem stages and publishes finished
+//               accumulators.
+//   warps 2-5   epilogue: tcgen05.ld the accumulator (each warp owns its 32-lane
+//               TMEM quarter), convert, store to global; then hand the TMEM buffer
+//               back so the next tile's MMAs overlap this tile's epilogue.
+// Tiles are visited in M-grouped order so a wave of CTAs shares B tiles in L2.
+// Every mbarrier wait is bounded; on timeout the kernel records an error in
+// `status`, stops all roles, frees its TMEM and returns.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "sm100.cuh"
+
+namespace gemm {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, UMMA_K = 16;
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 512;
+constexpr int GROUP_M = 16;
+constexpr uint32_t WAIT_LIMIT = 1u << 26;  // polls before a wait is declared dead (seconds)
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+
+enum Epi : int { kStoreBF16 = 0, kStoreF32 = 1, kAccumF32 = 2 };
+
+struct Params {
+  int M, N, K;
+  void* C;
+  long long ldc;
+  float alpha;
+  int* status;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m, int& n) {
+  const int per_group = GROUP_M * num_n;
+  const int g = t / per_group;
+  const int first_m = g * GROUP_M;
+  const int gsize = min(num_m - first_m, GROUP_M);
+  const int r = t % per_group;
+  m = first_m + r % gsize;
+  n = r / gsize;
+}
+
+__device__ __forceinline__ void fail(int* status, volatile int* abort_flag, int where) {
+  *abort_flag = 1;
+  if (status) atomicCAS(status, 0, 1 | (where << 8));
+}
+
+template <int A_MN, int B_MN, int EPI>
+__global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
+                                                      const __grid_constant__ CUtensorMap tma_b, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = (uint64_t*)(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = (uint32_t*)(tempty + 2);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      sm100::mbar_init(&tfull[b], 1);
+      sm100::mbar_init(&tempty[b], 4);
+    }
+    *abort_flag = 0;
+    sm100::fence_barrier_init();
+    sm100::prefetch_tensormap(&tma_a);
+    sm100::prefetch_tensormap(&tma_b);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, TMEM_COLS);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, num_m, num_n, tm, tn);
+        const int m0 = tm * BM, n0 = tn * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!sm100::mbar_wait_bounded(&empty[stage], phase ^ 1, WAIT_LIMIT)) {
+            fail(p.status, abort_flag, 1);
+            break;
+          }
+          sm100::mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          uint8_t* a = sA + stage * A_BYTES;
+          uint8_t* b = sB + stage * B_BYTES;
+          const int k0 = kb * BK;
+          if (A_MN) {
+#pragma unroll
+            for (int h = 0; h < BM / 64; ++h) sm100::tma_load_2d(a + h * (BK * 128), &tma_a, &full[stage], m0 + 64 * h, k0);
+          } else {
+            sm100::tma_load_2d(a, &tma_a, &full[stage], k0, m0);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int h = 0; h < BN / 64; ++h) sm100::tma_load_2d(b + h * (BK * 128), &tma_b, &full[stage], n0 + 64 * h, k0);
+          } else {
+            sm100::tma_load_2d(b, &tma_b, &full[stage], k0, n0);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = sm100::idesc_bf16_f32(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        if (!sm100::mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, WAIT_LIMIT)) {
+          fail(p.status, abort_flag, 2);
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        bool dead = false;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!sm100::mbar_wait_bounded(&full[stage], phase, WAIT_LIMIT)) {
+            fail(p.status, abort_flag, 3);
+            dead = true;
+            break;
+          }
+          sm100::tc_fence_after();
+          const uint32_t a = sm100::smem_u32(sA + stage * A_BYTES);
+          const uint32_t b = sm100::smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            // K-major: +32 B per 16-element K step inside the 128-B swizzle row.
+            // MN-major: a 16-element K step spans two 8-row (1024-B) atoms.
+            const uint64_t ad = A_MN ? sm100::desc_mnmajor_sw128(a + k * 2048, BK * 128)
+                                     : sm100::desc_kmajor_sw128(a + k * 32);
+            const uint64_t bd = B_MN ? sm100::desc_mnmajor_sw128(b + k * 2048, BK * 128)
+                                     : sm100::desc_kmajor_sw128(b + k * 32);
+            sm100::mma_f16(d, ad, bd, idesc, (kb | k) != 0);
+          }
+          sm100::mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (dead) break;
+        sm100::mma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(t, num_m, num_n, tm, tn);
+      const int m0 = tm * BM, n0 = tn * BN;
+      if (!sm100::mbar_wait_bounded(&tfull[acc], acc_phase, WAIT_LIMIT)) {
+        fail(p.status, abort_flag, 4);
+        break;
+      }
+      sm100::tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        sm100::tmem_ld32(tbase + c * 32, r);
+        sm100::tmem_ld_wait();
+        const int col0 = n0 + c * 32;
+        if (row < p.M && col0 < p.N) {
+          if (EPI == kStoreBF16) {
+            __nv_bfloat16* out = (__nv_bfloat16*)p.C + (long long)row * p.ldc + col0;
+            if (col0 + 32 <= p.N) {
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                uint4 pk;
+                uint32_t* w = (uint32_t*)&pk;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[v * 8 + 2 * e]) * p.alpha,
+                                                           __uint_as_float(r[v * 8 + 2 * e + 1]) * p.alpha);
+                  w[e] = *(uint32_t*)&h;
+                }
+                *(uint4*)(out + v * 8) = pk;
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e)  // static indexing keeps r[] in registers
+                if (col0 + e < p.N) out[e] = __float2bfloat16(__uint_as_float(r[e]) * p.alpha);
+            }
+          } else {
+            float* out = (float*)p.C + (long long)row * p.ldc + col0;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              if (col0 + e < p.N) {
+                const float v = __uint_as_float(r[e]) * p.alpha;
+                if (EPI == kAccumF32) out[e] += v;
+                else out[e] = v;
+              }
+            }
+          }
+        }
+      }
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major matrix [rows][cols] (cols contiguous), box {64 cols, box_rows}.
+static bool make_map(CUtensorMap* m, const void* ptr, long long rows, long long cols, long long ld, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int A_MN, int B_MN, int EPI>
+static cudaError_t launch(const void* A, long long lda, const void* B, long long ldb, const Params& p, int sms,
+                          cudaStream_t s) {
+  CUtensorMap ma, mb;
+  // A_MN: memory [K][M] (box 64 m x 64 k); else [M][K] (box 64 k x 128 m)
+  const bool ok_a = A_MN ? make_map(&ma, A, p.K, p.M, lda, BK) : make_map(&ma, A, p.M, p.K, lda, BM);
+  const bool ok_b = B_MN ? make_map(&mb, B, p.K, p.N, ldb, BK) : make_map(&mb, B, p.N, p.K, ldb, BN);
+  if (!ok_a || !ok_b) return cudaErrorInvalidValue;
+  auto k = gemm_kernel<A_MN, B_MN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_set = true;
+  }
+  const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+  const int grid = tiles < sms ? tiles : sms;
+  k<<<grid, 192, SMEM_BYTES, s>>>(ma, mb, p);
+  return cudaGetLastError();
+}
+
+}  // namespace gemm
+
+// C = alpha * op(A) op(B)^T.  a_mn / b_mn select the operand storage (see top of file);
+// epi: 0 = store bf16, 1 = store fp32, 2 = accumulate into fp32.
+// Requirements: leading dimensions multiples of 8 elements, 16-B aligned base pointers.
+cudaError_t rlb_gemm(int a_mn, int b_mn, int epi, int M, int N, int K, const void* A, long long lda, const void* B,
+                     long long ldb, void* C, long long ldc, float alpha, int* status, int sms, cudaStream_t s) {
+  using namespace gemm;
+  if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+  if ((lda % 8) || (ldb % 8) || (((uintptr_t)A) & 15) || (((uintptr_t)B) & 15)) return cudaErrorInvalidValue;
+  Params p{M, N, K, C, ldc, alpha, status};
+#define RLB_GEMM_CASE(AM, BMN, E) \
+  if (a_mn == AM && b_mn == BMN && epi == E) return launch<AM, BMN, E>(A, lda, B, ldb, p, sms, s);
+  RLB_GEMM_CASE(0, 0, 0)
+  RLB_GEMM_CASE(0, 1, 0)
+  RLB_GEMM_CASE(1, 1, 0)
+  RLB_GEMM_CASE(1, 1, 1)
+  RLB_GEMM_CASE(1, 1, 2)
+  RLB_GEMM_CASE(0, 0, 1)
+  RLB_GEMM_CASE(0, 0, 2)
+#undef RLB_GEMM_CASE
+  return cudaErrorNotSupported;
+}

@@ -5,6 +5,7 @@
 cudaError_t rlb_rmsnorm_fwd(const void* x, const void* delta, const void* w, void* h_out, void* y, float* rstd,
                             long long rows, int dim, float eps, int sms, cudaStream_t s);
 int rlb_rmsnorm_bwd_grid(long long rows, int sms);
+int rlb_rmsnorm_bwd_parts(long long rows, int dim, int sms);
 cudaError_t rlb_rmsnorm_bwd(const void* h, const void* w, const float* rstd, const void* dy, const void* dres,
                             void* dx, float* dw_part, void* dw_out, int dw_is_f32, long long rows, int dim, int sms,
                             cudaStream_t s);
@@ -45,3 +46,6 @@ cudaError_t rlb_embed_bwd(const long long* sorted_ids, const long long* perm, co
 
 cudaError_t rlb_nf4_dequant(const void* packed, const float* absmax, const float* table, long long n, int block,
                             void* out, int out_bf16, int sms, cudaStream_t s);
+
+cudaError_t rlb_gemm(int a_mn, int b_mn, int epi, int M, int N, int K, const void* A, long long lda, const void* B,
+                     long long ldb, void* C, long long ldc, float alpha, int* status, int sms, cudaStream_t s);

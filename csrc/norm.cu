@@ -1,8 +1,10 @@
 // RMSNorm forward / backward, optionally fused with the residual add that
 // precedes it in a pre-norm block:
 //   h = x (+ delta);  y = h * rsqrt(mean(h^2) + eps) * w
-// One warp owns one row; each lane holds NV 16-byte vectors of the row in
-// registers, so the row is read from HBM exactly once per pass.
+// Widths that are multiples of 256 (the model widths) use one block per row and
+// one 16-byte vector per thread (few registers, full occupancy); other widths use
+// one warp per row with NV vectors per lane.  Rows are read from HBM once per pass;
+// the weight gradient is summed per block, then across blocks in a fixed order.
 // Semantics follow src/forgeline/models/transformer/norm.py:9-17 (fp32 statistics).
 #include "common.cuh"
 
@@ -133,15 +135,120 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
   }
 }
 
-// Column sums of a [parts, dim] fp32 matrix -> dw (bf16 or fp32).
+// ---------------------------------------------------------------------------
+// Wide rows (dim % 256 == 0, dim <= 8192): one block per row, one 16-byte vector
+// per thread (blockDim = dim / 8), a few registers per thread -> full occupancy.
+// The row reduction goes through one float per warp in shared memory.
+RLB_DEVICE float row_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  __syncthreads();
+  return t;
+}
+
+__global__ void rmsnorm_fwd_wide(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ delta,
+                                 const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ h_out,
+                                 __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out, long long rows, int dim,
+                                 float eps) {
+  __shared__ float red[32];
+  const int c = threadIdx.x * 8;
+  float wf[8];
+  unpack8(ldg8(w + c), wf);
+  for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
+    float v[8];
+    unpack8(ldg8(x + row * dim + c), v);
+    if (delta != nullptr) {
+      float d[8];
+      unpack8(ldg8(delta + row * dim + c), d);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] += d[k];
+      bf16x8 hv = pack8(v);
+      stg8(h_out + row * dim + c, hv);
+      unpack8(hv, v);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss += v[k] * v[k];
+    const float r = rsqrtf(row_sum(ss, red) / (float)dim + eps);
+    if (threadIdx.x == 0 && rstd_out) rstd_out[row] = r;
+    float o[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = v[k] * r * wf[k];
+    stg8(y + row * dim + c, pack8(o));
+  }
+}
+
+__global__ void rmsnorm_bwd_wide(const __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ w,
+                                 const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dy,
+                                 const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
+                                 float* __restrict__ dw_part, long long rows, int dim) {
+  __shared__ float red[32];
+  const int c = threadIdx.x * 8;
+  float wf[8], acc[8];
+  unpack8(ldg8(w + c), wf);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+  for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float r = rstd[row];
+    float xh[8], g[8];
+    unpack8(ldg8(h + row * dim + c), xh);
+    unpack8(ldg8(dy + row * dim + c), g);
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      xh[k] *= r;
+      acc[k] += g[k] * xh[k];
+      g[k] *= wf[k];
+      dot += g[k] * xh[k];
+    }
+    dot = row_sum(dot, red) / (float)dim;
+    float o[8];
+    if (dres != nullptr) {
+      float rr[8];
+      unpack8(ldg8(dres + row * dim + c), rr);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[k] = r * (g[k] - xh[k] * dot) + rr[k];
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[k] = r * (g[k] - xh[k] * dot);
+    }
+    stg8(dx + row * dim + c, pack8(o));
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) dw_part[(long long)blockIdx.x * dim + c + k] = acc[k];
+}
+
+// Column sums of a [parts, dim] fp32 matrix -> dw (bf16 or fp32), fixed order:
+// block = 32 columns x 8 row-slices, each slice strides over the parts, then the
+// 8 slice sums are added in shared memory.
 __global__ void colsum_kernel(const float* __restrict__ part, int parts, int dim, float* __restrict__ out_f32,
                               __nv_bfloat16* __restrict__ out_bf16) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= dim) return;
+  __shared__ float tile[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + tx;
   float s = 0.f;
-  for (int p = 0; p < parts; ++p) s += part[(long long)p * dim + c];
-  if (out_f32) out_f32[c] = s;
-  if (out_bf16) out_bf16[c] = __float2bfloat16(s);
+  if (c < dim)
+    for (int p = ty; p < parts; p += 8) s += part[(long long)p * dim + c];
+  tile[ty][tx] = s;
+  __syncthreads();
+  if (ty == 0 && c < dim) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += tile[i][tx];
+    if (out_f32) out_f32[c] = t;
+    if (out_bf16) out_bf16[c] = __float2bfloat16(t);
+  }
+}
+
+static bool wide_ok(int dim) { return dim % 256 == 0 && dim <= 8192; }
+
+static int wide_grid(long long rows, int sms) {
+  long long cap = (long long)sms * 8;
+  return (int)(rows < cap ? (rows < 1 ? 1 : rows) : cap);
 }
 
 static int pick_grid(long long rows, int sms) {
@@ -155,8 +262,6 @@ static int pick_grid(long long rows, int sms) {
     if ((dim) <= 256) { constexpr int NV = 1; KERNEL_CALL; }        \
     else if ((dim) <= 512) { constexpr int NV = 2; KERNEL_CALL; }   \
     else if ((dim) <= 1024) { constexpr int NV = 4; KERNEL_CALL; }  \
-    else if ((dim) <= 2048) { constexpr int NV = 8; KERNEL_CALL; }  \
-    else if ((dim) <= 4096) { constexpr int NV = 16; KERNEL_CALL; } \
     else { return cudaErrorInvalidValue; }          \
   } while (0)
 
@@ -168,6 +273,12 @@ using namespace rlb;
 cudaError_t rlb_rmsnorm_fwd(const void* x, const void* delta, const void* w, void* h_out, void* y, float* rstd,
                             long long rows, int dim, float eps, int sms, cudaStream_t s) {
   if (dim % 8 != 0) return cudaErrorInvalidValue;
+  if (wide_ok(dim)) {
+    rmsnorm_fwd_wide<<<wide_grid(rows, sms), dim / 8, 0, s>>>(
+        (const __nv_bfloat16*)x, (const __nv_bfloat16*)delta, (const __nv_bfloat16*)w, (__nv_bfloat16*)h_out,
+        (__nv_bfloat16*)y, rstd, rows, dim, eps);
+    return cudaGetLastError();
+  }
   const int grid = pick_grid(rows, sms);
   RLB_NV_DISPATCH(dim, (rmsnorm_fwd_kernel<NV><<<grid, 256, 0, s>>>(
                            (const __nv_bfloat16*)x, (const __nv_bfloat16*)delta, (const __nv_bfloat16*)w,
@@ -177,11 +288,23 @@ cudaError_t rlb_rmsnorm_fwd(const void* x, const void* delta, const void* w, voi
 
 // dw_part must hold grid*dim floats where grid = rlb_rmsnorm_bwd_grid(rows, sms).
 int rlb_rmsnorm_bwd_grid(long long rows, int sms) { return pick_grid(rows, sms) < 1 ? 1 : pick_grid(rows, sms); }
+int rlb_rmsnorm_bwd_parts(long long rows, int dim, int sms) {
+  return wide_ok(dim) ? wide_grid(rows, sms) : rlb_rmsnorm_bwd_grid(rows, sms);
+}
 
 cudaError_t rlb_rmsnorm_bwd(const void* h, const void* w, const float* rstd, const void* dy, const void* dres,
                             void* dx, float* dw_part, void* dw_out, int dw_is_f32, long long rows, int dim, int sms,
                             cudaStream_t s) {
   if (dim % 8 != 0) return cudaErrorInvalidValue;
+  if (wide_ok(dim)) {
+    const int g = wide_grid(rows, sms);
+    rmsnorm_bwd_wide<<<g, dim / 8, 0, s>>>((const __nv_bfloat16*)h, (const __nv_bfloat16*)w, rstd,
+                                            (const __nv_bfloat16*)dy, (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx,
+                                            dw_part, rows, dim);
+    colsum_kernel<<<ceil_div(dim, 32), 256, 0, s>>>(dw_part, g, dim, dw_is_f32 ? (float*)dw_out : nullptr,
+                                                    dw_is_f32 ? nullptr : (__nv_bfloat16*)dw_out);
+    return cudaGetLastError();
+  }
   const int grid = rlb_rmsnorm_bwd_grid(rows, sms);
   const size_t smem = (size_t)8 * dim * sizeof(float);
   RLB_NV_DISPATCH(dim, ({
@@ -191,7 +314,7 @@ cudaError_t rlb_rmsnorm_bwd(const void* h, const void* w, const float* rstd, con
                                               (const __nv_bfloat16*)dy, (const __nv_bfloat16*)dres,
                                               (__nv_bfloat16*)dx, dw_part, rows, dim);
                   }));
-  colsum_kernel<<<ceil_div(dim, 256), 256, 0, s>>>(dw_part, grid, dim, dw_is_f32 ? (float*)dw_out : nullptr,
+  colsum_kernel<<<ceil_div(dim, 32), 256, 0, s>>>(dw_part, grid, dim, dw_is_f32 ? (float*)dw_out : nullptr,
                                                    dw_is_f32 ? nullptr : (__nv_bfloat16*)dw_out);
   return cudaGetLastError();
 }

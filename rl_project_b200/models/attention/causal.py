@@ -67,8 +67,11 @@ class CausalSelfAttention(nn.Module):
         B, T, C = x.shape
         qkv = self._qkv(x)
         offset = past_kv[0].shape[2] if past_kv is not None else 0
+        # q/k/v come out token-major [B, T, H, D]; attention reads them through [B, H, T, D]
+        # views so its output is already in the [B, T, H*D] layout the output projection wants
         q, k, v = rope_split_qkv(qkv, self.rope, self.n_head, self.n_kv_head, self.head_dim, offset=offset,
-                                 positions=positions, rotate=self.use_rope)
+                                 positions=positions, rotate=self.use_rope, heads_major=False)
+        q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
         if past_kv is not None:
             k = torch.cat([past_kv[0], k], dim=2)
             v = torch.cat([past_kv[1], v], dim=2)

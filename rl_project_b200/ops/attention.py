@@ -51,16 +51,34 @@ def attention_reference(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, windo
     return (p @ v.float()).to(q.dtype)
 
 
+_GQA_NATIVE: dict = {}
+
+
+def _fused_sdpa(q, k, v, rep, dropout_p, scale):
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    backends = [SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION]
+    key = (q.device.index, q.shape[-1], rep)
+    if rep > 1 and _GQA_NATIVE.get(key, True):
+        try:
+            with sdpa_kernel(backends):
+                out = F.scaled_dot_product_attention(q, k, v, is_causal=True, dropout_p=dropout_p, scale=scale,
+                                                     enable_gqa=True)
+            _GQA_NATIVE[key] = True
+            return out
+        except RuntimeError:
+            _GQA_NATIVE[key] = False  # no fused kernel takes grouped K/V here: expand once
+    with sdpa_kernel(backends):
+        return F.scaled_dot_product_attention(q, _expand_kv(k, rep), _expand_kv(v, rep), is_causal=True,
+                                              dropout_p=dropout_p, scale=scale)
+
+
 def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, window: int = 0, softcap: float = 0.0,
                      scale: Optional[float] = None, dropout_p: float = 0.0) -> torch.Tensor:
-    """Full-sequence causal attention (no cache).  Returns ``[B, Hq, T, D]``."""
+    """Full-sequence causal attention (no cache).  ``q [B, Hq, T, D]`` (any strides) -> ``[B, Hq, T, D]``."""
     rep = q.shape[1] // k.shape[1]
     if q.is_cuda and window == 0 and softcap == 0:
-        from torch.nn.attention import SDPBackend, sdpa_kernel
-
-        with sdpa_kernel([SDPBackend.FLASH_ATTENTION, SDPBackend.CUDNN_ATTENTION, SDPBackend.EFFICIENT_ATTENTION]):
-            return F.scaled_dot_product_attention(q, _expand_kv(k, rep), _expand_kv(v, rep), is_causal=True,
-                                                  dropout_p=dropout_p, scale=scale)
+        return _fused_sdpa(q, k, v, rep, dropout_p, scale)
     if not q.is_cuda and window == 0 and softcap == 0 and dropout_p == 0.0:
         return F.scaled_dot_product_attention(q, _expand_kv(k, rep), _expand_kv(v, rep), is_causal=True, scale=scale)
     out = attention_reference(q, k, v, window=window, softcap=softcap, scale=scale, q_offset=0)

@@ -1,0 +1,148 @@
+"""Kernel micro-benchmarks (CUDA-event timing after warm-up, L2 flushed between timed calls).
+
+    python -m rl_project_b200.ops.bench_kernels [--which gemm,norm,logprob,adam]
+
+Prints one JSON line per case with the achieved TFLOP/s or GB/s and the
+fraction of the measured peaks in MEASURED_PEAKS.json ("of measured").
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def _peaks():
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as fh:
+            d = json.load(fh)
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"])
+    except Exception:
+        return 1590.0, 6650.0
+
+
+_FLUSH = None
+
+
+def _flush():
+    global _FLUSH
+    if _FLUSH is None:
+        _FLUSH = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    _FLUSH.zero_()
+
+
+def time_ms(fn, iters: int = 10, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(iters):
+        _flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        total += a.elapsed_time(b)
+    return total / iters
+
+
+def bench_gemm(shapes):
+    from rl_project_b200.ops import gemm
+
+    peak_tf, _ = _peaks()
+    for (M, N, K, kind) in shapes:
+        if kind == "nt":
+            a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+            b = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+            ours = lambda: gemm.gemm_nt(a, b)
+            ref = lambda: a @ b.t()
+        elif kind == "nn":
+            a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+            b = torch.randn(K, N, device="cuda").to(torch.bfloat16)
+            ours = lambda: gemm.gemm_nn(a, b)
+            ref = lambda: a @ b
+        else:  # tn: a [K, M], b [K, N]
+            a = torch.randn(K, M, device="cuda").to(torch.bfloat16)
+            b = torch.randn(K, N, device="cuda").to(torch.bfloat16)
+            ours = lambda: gemm.gemm_tn(a, b)
+            ref = lambda: a.t() @ b
+        err = ((ours().float() - ref().float()).abs().max() / ref().float().abs().max()).item()
+        t_ours, t_ref = time_ms(ours), time_ms(ref)
+        fl = 2.0 * M * N * K
+        print(json.dumps({"kernel": "gemm_tcgen05", "layout": kind, "M": M, "N": N, "K": K,
+                          "ms": round(t_ours, 4), "tflops": round(fl / t_ours / 1e9, 1),
+                          "frac_of_measured_bf16": round(fl / t_ours / 1e9 / peak_tf, 3),
+                          "cublas_ms": round(t_ref, 4), "cublas_tflops": round(fl / t_ref / 1e9, 1),
+                          "rel_err": err}), flush=True)
+
+
+def bench_memory_bound():
+    from rl_project_b200.ops._ext import native
+
+    _, peak_gbs = _peaks()
+    N, D = 32768, 2048
+    x = torch.randn(N, D, device="cuda").to(torch.bfloat16)
+    d = torch.randn(N, D, device="cuda").to(torch.bfloat16)
+    w = torch.ones(D, device="cuda").to(torch.bfloat16)
+    C = native()
+    t = time_ms(lambda: C.rmsnorm_fwd(x, d, w, 1e-6))
+    print(json.dumps({"kernel": "rmsnorm_fwd+residual", "ms": t, "gbs": 4 * N * D * 2 / t / 1e6,
+                      "frac_of_measured_hbm": 4 * N * D * 2 / t / 1e6 / peak_gbs}), flush=True)
+    y, rstd, h = C.rmsnorm_fwd(x, d, w, 1e-6)
+    t = time_ms(lambda: C.rmsnorm_bwd(h, w, rstd, y, d))
+    print(json.dumps({"kernel": "rmsnorm_bwd+residual", "ms": t, "gbs": 4 * N * D * 2 / t / 1e6,
+                      "frac_of_measured_hbm": 4 * N * D * 2 / t / 1e6 / peak_gbs}), flush=True)
+    V, R = 128256, 8192
+    logits = torch.randn(R, V, device="cuda").to(torch.bfloat16)
+    tg = torch.randint(0, V, (R,), device="cuda")
+    t = time_ms(lambda: C.logprob_fwd(logits, tg, False, None))
+    print(json.dumps({"kernel": "logprob_fwd", "ms": t, "gbs": R * V * 2 / t / 1e6,
+                      "frac_of_measured_hbm": R * V * 2 / t / 1e6 / peak_gbs}), flush=True)
+
+
+def bench_adam():
+    from rl_project_b200.ops.optim import FusedAdamW
+
+    _, peak_gbs = _peaks()
+    p = torch.nn.Parameter(torch.randn(1 << 28, device="cuda").to(torch.bfloat16))
+    opt = FusedAdamW([p], lr=1e-4)
+    p.grad = torch.randn_like(p)
+    n = p.numel()
+
+    def step():
+        opt.clip_grad_norm(1.0)
+        opt.step()
+
+    t = time_ms(step)
+    moved = n * (2 + 4 + 4 + 4 + 4 + 4 + 4 + 2 + 2)  # grad read twice, master/m/v read+write, bf16 write
+    print(json.dumps({"kernel": "adamw+clip", "numel": n, "ms": t, "gbs": moved / t / 1e6,
+                      "frac_of_measured_hbm": moved / t / 1e6 / peak_gbs}), flush=True)
+
+
+MODEL_SHAPES = [
+    (32768, 3072, 2048, "nt"), (32768, 2048, 2048, "nt"), (32768, 16384, 2048, "nt"), (32768, 2048, 8192, "nt"),
+    (32768, 2048, 16384, "nn"), (32768, 8192, 2048, "nn"), (16384, 2048, 32768, "tn"), (2048, 8192, 32768, "tn"),
+]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--which", default="gemm,mem,adam")
+    args = ap.parse_args()
+    which = set(args.which.split(","))
+    if "gemm" in which:
+        bench_gemm(MODEL_SHAPES)
+    if "mem" in which:
+        bench_memory_bound()
+    if "adam" in which:
+        bench_adam()
+
+
+if __name__ == "__main__":
+    main()

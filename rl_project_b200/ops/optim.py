@@ -70,7 +70,7 @@ class FusedAdamW(torch.optim.Optimizer):
             st["step"] = torch.zeros((), dtype=torch.float32)
             off += n
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        self._partial = torch.empty(sms * 4, dtype=torch.float32, device=dev)
+        self._partial = torch.empty(sms * 8, dtype=torch.float32, device=dev)
         self.norm_coef = torch.zeros(2, dtype=torch.float32, device=dev)
 
     def _build_desc(self) -> None:

@@ -228,3 +228,39 @@ def test_model_matches_fp32_reference_forward():
     _, l_cpu = cpu(x, x)
     _, l_gpu = gpu(x.cuda(), x.cuda())
     assert abs(l_cpu.item() - l_gpu.item()) < 2e-2 * max(1.0, l_cpu.item())
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (300, 200, 136), (1024, 3072, 2048)])
+def test_tcgen05_gemm_all_layouts(M, N, K):
+    from rl_project_b200.ops.gemm import gemm_nn, gemm_nt, gemm_tn
+
+    a = torch.randn(M, K, device=DEV).to(BF)
+    b = torch.randn(N, K, device=DEV).to(BF)
+    ref = a.float() @ b.float().t()
+    _close(gemm_nt(a, b), ref, 1e-2)
+    # dgrad form: a [M, K] @ c [K, N]
+    c = torch.randn(K, N, device=DEV).to(BF)
+    _close(gemm_nn(a, c), a.float() @ c.float(), 1e-2)
+    # wgrad form: a[K', M]^T @ d[K', N]
+    d = torch.randn(M, N, device=DEV).to(BF)
+    e = torch.randn(M, K, device=DEV).to(BF)
+    _close(gemm_tn(d, e), d.float().t() @ e.float(), 1e-2)
+    acc = torch.ones(N, K, device=DEV)
+    gemm_tn(d, e, out=acc, accumulate=True)
+    _close(acc, d.float().t() @ e.float() + 1, 1e-2)
+
+
+def test_tcgen05_linear_autograd():
+    from rl_project_b200.ops import gemm
+
+    x = torch.randn(4, 96, 512, device=DEV).to(BF).requires_grad_()
+    w = (0.05 * torch.randn(768, 512, device=DEV)).to(BF).requires_grad_()
+    y = gemm._Linear.apply(x.reshape(-1, 512), w)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    xr, wr = x.detach().float().requires_grad_(), w.detach().float().requires_grad_()
+    yr = xr.reshape(-1, 512) @ wr.t()
+    yr.backward(gy.float())
+    _close(y, yr, 1e-2)
+    _close(x.grad, xr.grad, 2e-2)
+    _close(w.grad, wr.grad, 2e-2)
