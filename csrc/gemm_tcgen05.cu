@@ -299,13 +299,12 @@ static cudaError_t launch(const void* A, long long lda, const void* B, long long
   // A_MN: memory [K][M] (box 64 m x 64 k); else [M][K] (box 64 k x 128 m)
   const bool ok_a = A_MN ? make_map(&ma, A, p.K, p.M, lda, BK) : make_map(&ma, A, p.M, p.K, lda, BM);
   const bool ok_b = B_MN ? make_map(&mb, B, p.K, p.N, ldb, BK) : make_map(&mb, B, p.N, p.K, ldb, BN);
-  if (!ok_a || !ok_b) return cudaErrorInvalidValue;
+  if (!ok_a || !ok_b) return cudaErrorInvalidResourceHandle;  // tensor-map encoding rejected the operand
   auto k = gemm_kernel<A_MN, B_MN, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    attr_set = true;
-  }
+  // (per launch: the attribute is cheap to set and the caller may be any host thread)
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  (void)cudaGetLastError();  // drop a stale, non-sticky error left by unrelated calls on this thread
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < sms ? tiles : sms;
   k<<<grid, 192, SMEM_BYTES, s>>>(ma, mb, p);
@@ -321,7 +320,8 @@ cudaError_t rlb_gemm(int a_mn, int b_mn, int epi, int M, int N, int K, const voi
                      long long ldb, void* C, long long ldc, float alpha, int* status, int sms, cudaStream_t s) {
   using namespace gemm;
   if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
-  if ((lda % 8) || (ldb % 8) || (((uintptr_t)A) & 15) || (((uintptr_t)B) & 15)) return cudaErrorInvalidValue;
+  if ((lda % 8) || (ldb % 8)) return cudaErrorInvalidPitchValue;
+  if ((((uintptr_t)A) & 15) || (((uintptr_t)B) & 15)) return cudaErrorInvalidDevicePointer;
   Params p{M, N, K, C, ldc, alpha, status};
 #define RLB_GEMM_CASE(AM, BMN, E) \
   if (a_mn == AM && b_mn == BMN && epi == E) return launch<AM, BMN, E>(A, lda, B, ldb, p, sms, s);

@@ -136,49 +136,79 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Wide rows (dim % 256 == 0, dim <= 8192): one block per row, one 16-byte vector
-// per thread (blockDim = dim / 8), a few registers per thread -> full occupancy.
-// The row reduction goes through one float per warp in shared memory.
-RLB_DEVICE float row_sum(float v, float* red) {
+// Wide rows (dim % 256 == 0, dim <= 8192): a block owns R rows at a time, one
+// 16-byte vector per thread per row (blockDim = dim / 8).  All R rows' loads are
+// issued before the single block reduction, so each warp keeps R x 2 x 16 B in
+// flight instead of stalling on one row per barrier.
+constexpr int kRows = 4;
+
+template <int R>
+RLB_DEVICE void rows_sum(float (&v)[R], float* red) {  // red: [R][32]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  v = warp_sum(v);
-  if (lane == 0) red[warp] = v;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const float t = warp_sum(v[r]);
+    if (lane == 0) red[r * 32 + warp] = t;
+  }
   __syncthreads();
-  float t = 0.f;
-  for (int i = 0; i < nw; ++i) t += red[i];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    float t = 0.f;
+    for (int i = 0; i < nw; ++i) t += red[r * 32 + i];
+    v[r] = t;
+  }
   __syncthreads();
-  return t;
 }
 
 __global__ void rmsnorm_fwd_wide(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ delta,
                                  const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ h_out,
                                  __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out, long long rows, int dim,
                                  float eps) {
-  __shared__ float red[32];
+  __shared__ float red[kRows * 32];
   const int c = threadIdx.x * 8;
   float wf[8];
   unpack8(ldg8(w + c), wf);
-  for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
-    float v[8];
-    unpack8(ldg8(x + row * dim + c), v);
-    if (delta != nullptr) {
-      float d[8];
-      unpack8(ldg8(delta + row * dim + c), d);
+  for (long long row0 = (long long)blockIdx.x * kRows; row0 < rows; row0 += (long long)gridDim.x * kRows) {
+    float v[kRows][8], ss[kRows];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] += d[k];
-      bf16x8 hv = pack8(v);
-      stg8(h_out + row * dim + c, hv);
-      unpack8(hv, v);
+    for (int r = 0; r < kRows; ++r) {
+      const long long row = row0 + r;
+      ss[r] = 0.f;
+      if (row < rows) {
+        unpack8(ldg8(x + row * dim + c), v[r]);
+        if (delta != nullptr) {
+          float d[8];
+          unpack8(ldg8(delta + row * dim + c), d);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) v[r][k] += d[k];
+        }
+      }
     }
-    float ss = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) ss += v[k] * v[k];
-    const float r = rsqrtf(row_sum(ss, red) / (float)dim + eps);
-    if (threadIdx.x == 0 && rstd_out) rstd_out[row] = r;
-    float o[8];
+    for (int r = 0; r < kRows; ++r) {
+      const long long row = row0 + r;
+      if (row < rows) {
+        if (delta != nullptr) {
+          bf16x8 hv = pack8(v[r]);
+          stg8(h_out + row * dim + c, hv);
+          unpack8(hv, v[r]);  // statistics of the rounded residual stream
+        }
 #pragma unroll
-    for (int k = 0; k < 8; ++k) o[k] = v[k] * r * wf[k];
-    stg8(y + row * dim + c, pack8(o));
+        for (int k = 0; k < 8; ++k) ss[r] += v[r][k] * v[r][k];
+      }
+    }
+    rows_sum<kRows>(ss, red);
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      const long long row = row0 + r;
+      if (row >= rows) continue;
+      const float rs = rsqrtf(ss[r] / (float)dim + eps);
+      if (threadIdx.x == 0 && rstd_out) rstd_out[row] = rs;
+      float o[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[k] = v[r][k] * rs * wf[k];
+      stg8(y + row * dim + c, pack8(o));
+    }
   }
 }
 
@@ -186,37 +216,55 @@ __global__ void rmsnorm_bwd_wide(const __nv_bfloat16* __restrict__ h, const __nv
                                  const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dy,
                                  const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
                                  float* __restrict__ dw_part, long long rows, int dim) {
-  __shared__ float red[32];
+  __shared__ float red[kRows * 32];
   const int c = threadIdx.x * 8;
   float wf[8], acc[8];
   unpack8(ldg8(w + c), wf);
 #pragma unroll
   for (int k = 0; k < 8; ++k) acc[k] = 0.f;
-  for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
-    const float r = rstd[row];
-    float xh[8], g[8];
-    unpack8(ldg8(h + row * dim + c), xh);
-    unpack8(ldg8(dy + row * dim + c), g);
-    float dot = 0.f;
+  for (long long row0 = (long long)blockIdx.x * kRows; row0 < rows; row0 += (long long)gridDim.x * kRows) {
+    float xh[kRows][8], g[kRows][8], dot[kRows], rs[kRows];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      xh[k] *= r;
-      acc[k] += g[k] * xh[k];
-      g[k] *= wf[k];
-      dot += g[k] * xh[k];
+    for (int r = 0; r < kRows; ++r) {
+      const long long row = row0 + r;
+      dot[r] = 0.f;
+      rs[r] = 0.f;
+      if (row < rows) {
+        rs[r] = rstd[row];
+        unpack8(ldg8(h + row * dim + c), xh[r]);
+        unpack8(ldg8(dy + row * dim + c), g[r]);
+      }
     }
-    dot = row_sum(dot, red) / (float)dim;
-    float o[8];
-    if (dres != nullptr) {
-      float rr[8];
-      unpack8(ldg8(dres + row * dim + c), rr);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) o[k] = r * (g[k] - xh[k] * dot) + rr[k];
-    } else {
+    for (int r = 0; r < kRows; ++r) {
+      if (row0 + r < rows) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) o[k] = r * (g[k] - xh[k] * dot);
+        for (int k = 0; k < 8; ++k) {
+          xh[r][k] *= rs[r];
+          acc[k] += g[r][k] * xh[r][k];
+          g[r][k] *= wf[k];
+          dot[r] += g[r][k] * xh[r][k];
+        }
+      }
     }
-    stg8(dx + row * dim + c, pack8(o));
+    rows_sum<kRows>(dot, red);
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      const long long row = row0 + r;
+      if (row >= rows) continue;
+      const float m = dot[r] / (float)dim;
+      float o[8];
+      if (dres != nullptr) {
+        float rr[8];
+        unpack8(ldg8(dres + row * dim + c), rr);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = rs[r] * (g[r][k] - xh[r][k] * m) + rr[k];
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = rs[r] * (g[r][k] - xh[r][k] * m);
+      }
+      stg8(dx + row * dim + c, pack8(o));
+    }
   }
 #pragma unroll
   for (int k = 0; k < 8; ++k) dw_part[(long long)blockIdx.x * dim + c + k] = acc[k];
@@ -247,8 +295,9 @@ __global__ void colsum_kernel(const float* __restrict__ part, int parts, int dim
 static bool wide_ok(int dim) { return dim % 256 == 0 && dim <= 8192; }
 
 static int wide_grid(long long rows, int sms) {
-  long long cap = (long long)sms * 8;
-  return (int)(rows < cap ? (rows < 1 ? 1 : rows) : cap);
+  const long long want = (rows + kRows - 1) / kRows;
+  const long long cap = (long long)sms * 8;
+  return (int)(want < cap ? (want < 1 ? 1 : want) : cap);
 }
 
 static int pick_grid(long long rows, int sms) {
