@@ -212,10 +212,13 @@ __global__ void rmsnorm_fwd_wide(const __nv_bfloat16* __restrict__ x, const __nv
   }
 }
 
+constexpr int kRowsBwd = 2;  // the backward keeps 3 input vectors per row live
+
 __global__ void rmsnorm_bwd_wide(const __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ w,
                                  const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dy,
                                  const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
                                  float* __restrict__ dw_part, long long rows, int dim) {
+  constexpr int kRows = kRowsBwd;
   __shared__ float red[kRows * 32];
   const int c = threadIdx.x * 8;
   float wf[8], acc[8];
@@ -224,6 +227,7 @@ __global__ void rmsnorm_bwd_wide(const __nv_bfloat16* __restrict__ h, const __nv
   for (int k = 0; k < 8; ++k) acc[k] = 0.f;
   for (long long row0 = (long long)blockIdx.x * kRows; row0 < rows; row0 += (long long)gridDim.x * kRows) {
     float xh[kRows][8], g[kRows][8], dot[kRows], rs[kRows];
+    bf16x8 rres[kRows];
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
       const long long row = row0 + r;
@@ -233,6 +237,7 @@ __global__ void rmsnorm_bwd_wide(const __nv_bfloat16* __restrict__ h, const __nv
         rs[r] = rstd[row];
         unpack8(ldg8(h + row * dim + c), xh[r]);
         unpack8(ldg8(dy + row * dim + c), g[r]);
+        if (dres != nullptr) rres[r] = ldg8(dres + row * dim + c);  // issued with the others: one round trip
       }
     }
 #pragma unroll
@@ -256,7 +261,7 @@ __global__ void rmsnorm_bwd_wide(const __nv_bfloat16* __restrict__ h, const __nv
       float o[8];
       if (dres != nullptr) {
         float rr[8];
-        unpack8(ldg8(dres + row * dim + c), rr);
+        unpack8(rres[r], rr);
 #pragma unroll
         for (int k = 0; k < 8; ++k) o[k] = rs[r] * (g[r][k] - xh[r][k] * m) + rr[k];
       } else {
@@ -295,7 +300,7 @@ __global__ void colsum_kernel(const float* __restrict__ part, int parts, int dim
 static bool wide_ok(int dim) { return dim % 256 == 0 && dim <= 8192; }
 
 static int wide_grid(long long rows, int sms) {
-  const long long want = (rows + kRows - 1) / kRows;
+  const long long want = (rows + kRowsBwd - 1) / kRowsBwd;
   const long long cap = (long long)sms * 8;
   return (int)(want < cap ? (want < 1 ? 1 : want) : cap);
 }

@@ -93,6 +93,33 @@ class PostTrainingAlgorithm(ABC):
     def on_step_end(self, step: int, result: StepResult) -> None:
         pass
 
+    # data-position state, saved with every checkpoint so a resumed run draws the
+    # same batches an uninterrupted run would (generators, shuffles, counters)
+    _data_attrs = ("gen", "rng", "_order", "tokens_seen", "ema_loss")
+
+    def data_state(self) -> Dict[str, Any]:
+        out: Dict[str, Any] = {}
+        for name in self._data_attrs:
+            if not hasattr(self, name):
+                continue
+            val = getattr(self, name)
+            if isinstance(val, torch.Generator):
+                out[name] = ("torch_gen", val.get_state())
+            elif hasattr(val, "getstate") and hasattr(val, "setstate"):
+                out[name] = ("py_rng", val.getstate())
+            elif isinstance(val, (int, float, list, type(None))):
+                out[name] = ("value", list(val) if isinstance(val, list) else val)
+        return out
+
+    def load_data_state(self, state: Mapping[str, Any]) -> None:
+        for name, (kind, val) in (state or {}).items():
+            if kind == "torch_gen" and hasattr(self, name):
+                getattr(self, name).set_state(val)
+            elif kind == "py_rng" and hasattr(self, name):
+                getattr(self, name).setstate(val)
+            elif kind == "value":
+                setattr(self, name, list(val) if isinstance(val, list) else val)
+
 
 def _as_tensor(v: Any, device: torch.device) -> torch.Tensor:
     if isinstance(v, torch.Tensor):
@@ -317,7 +344,8 @@ class Trainer:
             state = CheckpointState(model_state={"sharded": True}, step=self.step, algorithm=self.alg.name,
                                     model_spec=self.alg.model_spec(), scaler_state=self.precision.state_dict(),
                                     rng_state=rng_state(),
-                                    trainer_state={"best_metric": self.best_metric, "history_len": len(self.history)},
+                                    trainer_state={"best_metric": self.best_metric, "history_len": len(self.history),
+                                                   "data_state": self.alg.data_state()},
                                     tokenizer_meta=self.alg.tokenizer_meta(), experiment=self.ctx.manifest.to_dict(),
                                     shards=shards)
             path = self.checkpoints.save(state, name=name, is_best=is_best)
@@ -332,7 +360,8 @@ class Trainer:
         state = CheckpointState(model_state=model_state, step=self.step, algorithm=self.alg.name,
                                 model_spec=self.alg.model_spec(), optimizer_state=opt_state,
                                 scaler_state=self.precision.state_dict(), rng_state=rng_state(),
-                                trainer_state={"best_metric": self.best_metric, "history_len": len(self.history)},
+                                trainer_state={"best_metric": self.best_metric, "history_len": len(self.history),
+                                               "data_state": self.alg.data_state()},
                                 tokenizer_meta=self.alg.tokenizer_meta(), experiment=self.ctx.manifest.to_dict())
         path = self.checkpoints.save(state, name=name, is_best=is_best)
         self.ctx.metrics.event(Event.CHECKPOINT_SAVED.value, {"path": str(path), "step": self.step})
@@ -396,6 +425,8 @@ class Trainer:
             set_rng_state(state.rng_state)
         self.step = state.step
         self.best_metric = float((state.trainer_state or {}).get("best_metric", math.inf))
+        if (state.trainer_state or {}).get("data_state"):
+            self.alg.load_data_state(state.trainer_state["data_state"])
         self.ctx.metrics.event(Event.CHECKPOINT_LOADED.value, {"path": target, "step": self.step})
         self.log.info("resumed", path=target, step=self.step)
         return True

@@ -1,0 +1,236 @@
+"""Group Relative Policy Optimization (single-turn and tool-using agent mode).
+
+Semantics of ``src/forgeline/training/grpo.py``: G samples per prompt,
+advantages ``(r - mean) / (std + eps)`` within the group, ``objective``
+``clipped`` (PPO surrogate + ``kl_coef * clamp(mean(ref - new), 0)`` with the
+clamp applied AFTER averaging over the group) or ``reinforce``
+(``-A * sum log pi``), ``ratio_level`` ``sequence_mean`` | ``token``,
+``kl_estimator`` ``logprob_diff`` | ``k3``.
+
+B200-first changes: every prompt x G sample of a step is generated in one
+batched call per prompt length (``RolloutEngine.rollout_many``; the reference
+loops prompts one by one), and the old-policy log-probs recorded during the
+rollout are reused instead of being recomputed by a second forward pass.
+"""
+
+from __future__ import annotations
+
+import random
+from dataclasses import dataclass
+from typing import Any, Dict, List, Mapping, Optional, Sequence
+
+import torch
+import torch.nn as nn
+
+from rl_project_b200.core.errors import ConfigError
+from rl_project_b200.core.protocols import RewardProvider, Trajectory
+from rl_project_b200.rollouts.agent import AgentRolloutConfig, AgentRolloutEngine
+from rl_project_b200.rollouts.engine import RolloutConfig, RolloutEngine, stack_group, stack_old_logprobs
+from rl_project_b200.rollouts.rewards.composite import score_trajectories
+from rl_project_b200.training.common.advantages import group_relative_advantages
+from rl_project_b200.training.common.logprobs import kl_k3, kl_logprob_diff, masked_mean, masked_sum
+from rl_project_b200.training.common.trainer import PostTrainingAlgorithm
+from rl_project_b200.training.ppo import ppo_clipped_objective
+
+
+@dataclass
+class GRPOConfig:
+    group_size: int = 4
+    prompts_per_step: int = 2
+    clip_ratio: float = 0.2
+    kl_coef: float = 0.04
+    objective: str = "clipped"
+    ratio_level: str = "sequence_mean"
+    kl_estimator: str = "logprob_diff"
+    advantage_eps: float = 1e-8
+    skip_zero_variance_groups: bool = False
+    agent: bool = False
+    seed: int = 0
+
+    def validate(self) -> None:
+        if self.group_size < 2:
+            raise ConfigError("GRPO group_size must be >= 2 (group-relative advantages need variance)")
+        if self.objective not in ("clipped", "reinforce"):
+            raise ConfigError("objective must be clipped|reinforce")
+        if self.ratio_level not in ("sequence_mean", "token"):
+            raise ConfigError("ratio_level must be sequence_mean|token")
+        if self.kl_estimator not in ("logprob_diff", "k3"):
+            raise ConfigError("kl_estimator must be logprob_diff|k3")
+
+
+@dataclass
+class GRPOGroup:
+    trajectories: List[Trajectory]
+    rewards: torch.Tensor
+    advantages: torch.Tensor
+    old_logprobs: Optional[torch.Tensor] = None
+    ref_logprobs: Optional[torch.Tensor] = None
+    skipped: bool = False
+
+
+class GRPOAlgorithm(PostTrainingAlgorithm):
+    name = "grpo"
+
+    def __init__(self, policy, prompts, reward: RewardProvider, config: GRPOConfig,
+                 rollout: Optional[RolloutConfig] = None, tasks: Optional[Sequence[Dict[str, Any]]] = None,
+                 agent_rollout: Optional[AgentRolloutConfig] = None):
+        config.validate()
+        self.policy = policy
+        self.cfg = config
+        self.reward = reward
+        self.rng = random.Random(config.seed)
+        if config.objective == "clipped" and config.kl_coef > 0 and not policy.has_adapter \
+                and policy.reference_model is None:
+            policy.with_frozen_reference()
+        if config.agent:
+            self.tasks = list(prompts)
+            self.agent_engine = AgentRolloutEngine(policy, agent_rollout or AgentRolloutConfig())
+            self.prompts: List[torch.Tensor] = []
+        else:
+            self.prompts = list(prompts)
+            self.tasks = list(tasks) if tasks else [{} for _ in self.prompts]
+            rc = rollout or RolloutConfig()
+            rc.group_size = config.group_size
+            self.rollouts = RolloutEngine(policy, rc)
+        self._last_stats: Dict[str, float] = {}
+
+    def parameters(self) -> List[nn.Parameter]:
+        return self.policy.trainable_parameters()
+
+    def modules(self):
+        return (self.policy.model,)
+
+    def frozen_modules(self):
+        return (self.policy.reference_model,) if self.policy.reference_model is not None else ()
+
+    # ---------------------------------------------------------------- collection
+    @torch.no_grad()
+    def collect(self, step: int) -> List[GRPOGroup]:
+        n = len(self.tasks if self.cfg.agent else self.prompts)
+        idx = [self.rng.randrange(n) for _ in range(self.cfg.prompts_per_step)]
+        if self.cfg.agent:
+            traj_groups = [self.agent_engine.rollout(self.tasks[i], self.cfg.group_size) for i in idx]
+        else:
+            traj_groups = self.rollouts.rollout_many([self.prompts[i] for i in idx], [self.tasks[i] for i in idx])
+        groups, skipped = [], 0
+        for trajs in traj_groups:
+            rewards = torch.tensor(score_trajectories(self.reward, trajs), dtype=torch.float32)
+            grp = GRPOGroup(trajs, rewards, group_relative_advantages(rewards, eps=self.cfg.advantage_eps))
+            if self.cfg.skip_zero_variance_groups and float(rewards.std()) < 1e-6:
+                grp.skipped = True
+                skipped += 1
+            elif self.cfg.objective == "clipped":
+                self._attach_logprobs(grp)
+            groups.append(grp)
+        all_r = torch.cat([g.rewards for g in groups])
+        n_traj = sum(len(g.trajectories) for g in groups)
+        self._last_stats = {
+            "reward_mean": float(all_r.mean()), "reward_std": float(all_r.std()) if all_r.numel() > 1 else 0.0,
+            "group_std": float(torch.stack([g.rewards.std() for g in groups]).mean()),
+            "groups_skipped": float(skipped),
+            "response_len": float(sum(t.response_length for g in groups for t in g.trajectories) / max(1, n_traj)),
+        }
+        if self.cfg.agent:
+            self._last_stats["tool_calls"] = float(sum(len(t.tool_results) for g in groups for t in g.trajectories))
+        return groups
+
+    @torch.no_grad()
+    def _attach_logprobs(self, grp: GRPOGroup) -> None:
+        if self.cfg.agent:
+            old = torch.stack([self.agent_engine.trajectory_logprob(t) for t in grp.trajectories]).float().cpu()
+            with self.policy.reference():
+                ref = torch.stack([self.agent_engine.trajectory_logprob(t) for t in grp.trajectories]).float().cpu()
+            grp.old_logprobs, grp.ref_logprobs = old, ref
+            return
+        prompt, resp, mask = stack_group(grp.trajectories, self.policy.pad_token_id)
+        if all(t.old_logprobs is not None for t in grp.trajectories):
+            old = stack_old_logprobs(grp.trajectories) * mask  # recorded at sampling time: same weights
+        else:
+            old = self.policy.logprobs(prompt, resp).float().cpu() * mask
+        with self.policy.reference():
+            ref = self.policy.logprobs(prompt, resp).float().cpu() * mask
+        grp.old_logprobs, grp.ref_logprobs = old, ref
+
+    # ---------------------------------------------------------------- objective
+    def loss(self, groups: List[GRPOGroup], micro_step: int, n_micro: int):
+        chunk = groups[micro_step::n_micro] if n_micro > 1 else groups
+        dev = self.policy.device
+        total = torch.zeros((), device=dev)
+        used, kl_acc, pl_acc = 0, torch.zeros((), device=dev), torch.zeros((), device=dev)
+        for grp in chunk:
+            if grp.skipped:
+                continue
+            adv = grp.advantages.to(dev)
+            if self.cfg.objective == "reinforce":
+                loss, kl = self._reinforce_loss(grp, adv), torch.zeros((), device=dev)
+            else:
+                loss, kl = self._clipped_loss(grp, adv)
+            total = total + loss
+            pl_acc = pl_acc + loss.detach()
+            kl_acc = kl_acc + kl.detach()
+            used += 1
+        if used == 0:
+            zero = sum(p.sum() for p in self.parameters()) * 0.0
+            return zero, {**self._last_stats, "policy_loss": 0.0, "kl": 0.0}
+        return total / used, {**self._last_stats, "policy_loss": pl_acc / used, "kl": kl_acc / used}
+
+    def _kl(self, ref, new, mask):
+        if self.cfg.kl_estimator == "k3":
+            return kl_k3(ref, new, mask).mean()
+        return kl_logprob_diff(ref, new, mask, clamp_min=None).mean().clamp(min=0)
+
+    def _clipped_loss(self, grp: GRPOGroup, adv: torch.Tensor):
+        dev = self.policy.device
+        if self.cfg.agent:
+            new = torch.stack([self.agent_engine.trajectory_logprob(t) for t in grp.trajectories]).float()
+            old, ref = grp.old_logprobs.to(dev), grp.ref_logprobs.to(dev)
+            pl = ppo_clipped_objective(torch.exp(new - old), adv, self.cfg.clip_ratio).mean()
+            kl = (ref - new).clamp(min=0).mean()
+            return pl + self.cfg.kl_coef * kl, kl
+        prompt, resp, mask = stack_group(grp.trajectories, self.policy.pad_token_id)
+        mask = mask.to(dev)
+        new = self.policy.logprobs(prompt, resp).float() * mask
+        old, ref = grp.old_logprobs.to(dev), grp.ref_logprobs.to(dev)
+        if self.cfg.ratio_level == "sequence_mean":
+            pl = ppo_clipped_objective(torch.exp(masked_mean(new - old, mask)), adv, self.cfg.clip_ratio).mean()
+        else:
+            per_tok = ppo_clipped_objective(torch.exp(new - old), adv[:, None], self.cfg.clip_ratio)
+            pl = masked_mean(per_tok, mask).mean()
+        kl = self._kl(ref, new, mask)
+        return pl + self.cfg.kl_coef * kl, kl
+
+    def _reinforce_loss(self, grp: GRPOGroup, adv: torch.Tensor) -> torch.Tensor:
+        if self.cfg.agent:
+            lp = torch.stack([self.agent_engine.trajectory_logprob(t) for t in grp.trajectories]).float()
+            return (-adv * lp).sum()
+        prompt, resp, mask = stack_group(grp.trajectories, self.policy.pad_token_id)
+        seq_lp = masked_sum(self.policy.logprobs(prompt, resp).float(), mask.to(self.policy.device))
+        return (-adv * seq_lp).sum()
+
+    # ---------------------------------------------------------------- evaluation
+    @torch.no_grad()
+    def evaluate(self, step: int) -> Dict[str, float]:
+        n = min(8, len(self.tasks if self.cfg.agent else self.prompts))
+        passed = total = 0
+        rsum = 0.0
+        for i in range(n):
+            trajs = (self.agent_engine.rollout(self.tasks[i], 1, temperature=0.0) if self.cfg.agent
+                     else self.rollouts.rollout(self.prompts[i], self.tasks[i], group_size=1))
+            for t in trajs:
+                r = self.reward.score(t)
+                rsum += r.value
+                passed += int(bool(r.passed))
+                total += 1
+        return {"reward": rsum / max(total, 1), "pass_rate": passed / max(total, 1)}
+
+    def state(self) -> Dict[str, Any]:
+        return self.policy.state_for_checkpoint()
+
+    def load_state(self, state: Mapping[str, Any]) -> None:
+        self.policy.load_checkpoint_state(state)
+
+    def model_spec(self) -> Dict[str, Any]:
+        return self.policy.spec.to_dict()
+
+    def tokenizer_meta(self):
+        return self.policy.tokenizer.metadata()

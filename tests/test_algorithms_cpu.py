@@ -1,0 +1,183 @@
+"""Every post-training algorithm runs through the shared Trainer on CPU and learns what it should."""
+
+import math
+
+import pytest
+import torch
+
+from rl_project_b200.core.config import AdapterConfig, model_spec_from_preset
+from rl_project_b200.data.preference import PreferenceDataset
+from rl_project_b200.data.pretraining import MemmapCorpus
+from rl_project_b200.data.records import PreferenceRecord, SFTRecord, VerifiableTask
+from rl_project_b200.data.supervised import SupervisedDataset
+from rl_project_b200.models.policy import NativePolicy
+from rl_project_b200.models.reward import SequenceRewardModel
+from rl_project_b200.models.transformer.model import TransformerLM
+from rl_project_b200.rollouts.agent import AgentRolloutConfig, AgentRolloutEngine
+from rl_project_b200.rollouts.engine import RolloutConfig
+from rl_project_b200.rollouts.rewards import ConstantReward, LengthReward, VerifierReward, build_reward_provider
+from rl_project_b200.rollouts.verifiers import MathVerifier
+from rl_project_b200.training import (DAPOAlgorithm, DAPOConfig, DistillationAlgorithm, DistillConfig, DPOAlgorithm,
+                                      DPOConfig, GRPOAlgorithm, GRPOConfig, PPOAlgorithm, PPOConfig, PretrainAlgorithm,
+                                      PretrainConfig, RewardModelAlgorithm, RewardModelConfig, RLVRConfig, SFTAlgorithm,
+                                      SFTConfig, Trainer, build_rlvr_algorithm)
+
+
+def ok(summary):
+    return summary["final_loss"] is not None and math.isfinite(summary["final_loss"])
+
+
+def test_pretrain_reduces_val_loss(make_ctx, cspec, corpus_dir):
+    alg = PretrainAlgorithm(TransformerLM(cspec), MemmapCorpus(corpus_dir, "train", 64), PretrainConfig(batch_size=8),
+                            MemmapCorpus(corpus_dir, "val", 64))
+    before = alg.evaluate(0)["val_loss"]
+    Trainer(make_ctx("pretrain", max_steps=40, batch_size=8, eval_every=0, save_every=0, lr=3e-3), alg).fit()
+    assert alg.evaluate(0)["val_loss"] < before
+
+
+@pytest.mark.parametrize("method", ["none", "lora", "qlora"])
+def test_sft_adapters_keep_base_frozen(make_ctx, cspec, char_tok, method):
+    recs = [SFTRecord(f"Q: {i}+1?", f" {i + 1}") for i in range(16)]
+    adapter = AdapterConfig(method=method, rank=4) if method != "none" else None
+    pol = NativePolicy(TransformerLM(cspec), char_tok, adapter=adapter)
+    frozen = {n: p.detach().clone() for n, p in pol.model.named_parameters() if not p.requires_grad}
+    assert ok(Trainer(make_ctx("sft"), SFTAlgorithm(pol, SupervisedDataset(recs, char_tok, 32), SFTConfig(batch_size=4))).fit())
+    for n, p in pol.model.named_parameters():
+        if n in frozen:
+            assert torch.equal(frozen[n], p)
+
+
+@pytest.mark.parametrize("reduction", ["sum", "mean"])
+def test_dpo_margin_grows(make_ctx, cspec, char_tok, reduction):
+    prefs = [PreferenceRecord(f"Q{i}:", " yes", " no") for i in range(8)]
+    alg = DPOAlgorithm(NativePolicy(TransformerLM(cspec), char_tok), PreferenceDataset(prefs, char_tok, 16, 8),
+                       DPOConfig(batch_size=4, beta=0.5, logprob_reduction=reduction))
+    m0 = alg.evaluate(0)["reward_margin"]
+    Trainer(make_ctx("dpo", max_steps=15, eval_every=0, save_every=0, lr=5e-3), alg).fit()
+    ev = alg.evaluate(0)
+    assert ev["reward_margin"] > m0 and ev["preference_accuracy"] == 1.0
+
+
+def test_batched_dpo_equals_per_example(cspec, char_tok):
+    """Right-padded batched log-probs equal one forward per example."""
+    from rl_project_b200.training.dpo import sequence_logprobs
+
+    pol = NativePolicy(TransformerLM(cspec), char_tok)
+    pol.eval()
+    pairs = [(char_tok.encode("Q1: what"), char_tok.encode(" yes")), (char_tok.encode("Q22:"), char_tok.encode(" no!!"))]
+    batched = sequence_logprobs(pol, pairs, "sum")
+    single = torch.stack([pol.logprobs(torch.tensor(p)[None], torch.tensor(r)[None]).sum() for p, r in pairs])
+    assert torch.allclose(batched, single, atol=1e-5)
+
+
+def test_reward_model_ranks(make_ctx, cspec, char_tok):
+    prefs = [PreferenceRecord(f"Q{i}:", " good good good", " bad") for i in range(8)]
+    alg = RewardModelAlgorithm(SequenceRewardModel(cspec), PreferenceDataset(prefs, char_tok, 16, 16),
+                               RewardModelConfig(batch_size=4))
+    Trainer(make_ctx("reward_model", max_steps=20, eval_every=0, save_every=0, lr=3e-3), alg).fit()
+    assert alg.evaluate(0)["accuracy"] == 1.0
+
+
+@pytest.mark.parametrize("ratio_level,kl_mode,entropy_mode", [("sequence_mean", "monitor", "sampled_logprob"),
+                                                              ("token", "penalty", "full"),
+                                                              ("sequence_mean", "reward", "sampled_logprob")])
+def test_ppo_modes(make_ctx, cspec, char_tok, ratio_level, kl_mode, entropy_mode):
+    pol = NativePolicy(TransformerLM(cspec), char_tok, value_head=True)
+    prompts = [torch.tensor(char_tok.encode(f"Q{i}:")) for i in range(4)]
+    alg = PPOAlgorithm(pol, prompts, LengthReward(6),
+                       PPOConfig(prompts_per_step=2, samples_per_prompt=2, ppo_epochs=2, ratio_level=ratio_level,
+                                 kl_mode=kl_mode, entropy_mode=entropy_mode), RolloutConfig(max_new_tokens=6))
+    assert ok(Trainer(make_ctx("ppo", eval_every=0), alg).fit())
+    assert "kl" in alg.loss(alg.collect(0), 0, 1)[1]
+
+
+@pytest.mark.parametrize("objective,ratio_level", [("clipped", "sequence_mean"), ("clipped", "token"),
+                                                   ("reinforce", "sequence_mean")])
+def test_grpo_objectives(make_ctx, cspec, char_tok, objective, ratio_level):
+    tasks = [{"prompt": f"What is {i}+1?", "answer": str(i + 1)} for i in range(4)]
+    prompts = [torch.tensor(char_tok.encode(t["prompt"])) for t in tasks]
+    alg = GRPOAlgorithm(NativePolicy(TransformerLM(cspec), char_tok), prompts, VerifierReward(MathVerifier()),
+                        GRPOConfig(group_size=3, prompts_per_step=2, objective=objective, ratio_level=ratio_level),
+                        RolloutConfig(max_new_tokens=6), tasks=tasks)
+    assert ok(Trainer(make_ctx("grpo"), alg).fit())
+
+
+def test_grpo_reuses_rollout_logprobs(cspec, char_tok):
+    """Old log-probs recorded at sampling time equal a fresh old-policy pass (so the second pass is skipped)."""
+    pol = NativePolicy(TransformerLM(cspec), char_tok)
+    prompts = [torch.tensor(char_tok.encode("Q1:")), torch.tensor(char_tok.encode("Q2:"))]
+    alg = GRPOAlgorithm(pol, prompts, LengthReward(4), GRPOConfig(group_size=2, prompts_per_step=2),
+                        RolloutConfig(max_new_tokens=5))
+    from rl_project_b200.rollouts.engine import stack_group
+
+    for grp in alg.collect(0):
+        p, r, m = stack_group(grp.trajectories)
+        fresh = pol.logprobs(p, r).float() * m
+        assert torch.allclose(grp.old_logprobs, fresh, atol=1e-5)
+
+
+def test_agent_grpo_with_tools(make_ctx, char_tok):
+    spec = model_spec_from_preset("tiny", vocab_size=char_tok.vocab_size, block_size=256)
+    alg = GRPOAlgorithm(NativePolicy(TransformerLM(spec), char_tok), [{"prompt": "Compute 12 * 3.", "answer": "36"}],
+                        build_reward_provider({"type": "tagged"}), GRPOConfig(group_size=2, prompts_per_step=1, agent=True),
+                        agent_rollout=AgentRolloutConfig(max_turns=1, max_new_tokens=6, max_context_tokens=200))
+    assert ok(Trainer(make_ctx("grpo", max_steps=1, eval_every=0), alg).fit())
+
+
+def test_agent_engine_injects_tool_results(char_tok):
+    outputs = ['<tool_call>{"name": "python_executor", "args": {"code": "print(12*3)"}}</tool_call>',
+               "<final_answer>36</final_answer>"]
+
+    class Scripted:
+        device = torch.device("cpu")
+        pad_token_id = 0
+
+        def __init__(self):
+            self.n = 0
+            self.seen = []
+
+        def encode(self, t):
+            return char_tok.encode(t)
+
+        def decode(self, ids):
+            return outputs[self.n - 1]
+
+        def generate(self, ids, settings):
+            self.seen.append(char_tok.decode(ids[0].tolist()))
+            self.n += 1
+            return torch.zeros(1, 1, dtype=torch.long)
+
+    pol = Scripted()
+    segs, blocks, final = AgentRolloutEngine(pol, AgentRolloutConfig(max_context_tokens=100000)).run_episode("Solve")
+    assert len(segs) == 2 and "36" in blocks[0] and "<tool_result>" in pol.seen[1] and final.endswith("</final_answer>")
+
+
+def test_dapo_skips_zero_variance_groups(make_ctx, cspec, char_tok):
+    pol = NativePolicy(TransformerLM(cspec), char_tok)
+    prompts = [torch.tensor(char_tok.encode("Q:"))]
+    alg = DAPOAlgorithm(pol, prompts, ConstantReward(1.0), DAPOConfig(group_size=3, prompts_per_step=2),
+                        RolloutConfig(max_new_tokens=4))
+    groups = alg.collect(0)
+    assert all(g.skipped for g in groups)
+    loss, metrics = alg.loss(groups, 0, 1)
+    assert loss.item() == 0.0 and metrics["groups_skipped"] == 2.0
+    alg2 = DAPOAlgorithm(pol, prompts, LengthReward(2), DAPOConfig(group_size=4, prompts_per_step=2, entropy_coef=0.01),
+                         RolloutConfig(max_new_tokens=6, temperature=1.5))
+    assert ok(Trainer(make_ctx("dapo"), alg2).fit())
+
+
+def test_rlvr_both_optimizers(make_ctx, cspec, char_tok):
+    pol = NativePolicy(TransformerLM(cspec), char_tok)
+    tasks = [VerifiableTask(prompt=f"What is {i}+1?", answer=str(i + 1)) for i in range(4)]
+    for opt in ("dapo", "grpo"):
+        cfg = RLVRConfig(optimizer=opt, require_format=True, dapo=DAPOConfig(group_size=2, prompts_per_step=1),
+                         grpo=GRPOConfig(group_size=2, prompts_per_step=1))
+        alg = build_rlvr_algorithm(pol, tasks, cfg, RolloutConfig(max_new_tokens=8))
+        assert alg.name == "rlvr" and ok(Trainer(make_ctx("rlvr", max_steps=2, run=opt), alg).fit())
+
+
+def test_distillation_with_features(make_ctx, cspec, corpus_dir):
+    student = TransformerLM(model_spec_from_preset("tiny", vocab_size=cspec.vocab_size, block_size=64, n_layer=1))
+    alg = DistillationAlgorithm(student, TransformerLM(cspec), MemmapCorpus(corpus_dir, "train", 64),
+                                DistillConfig(batch_size=4, feature_weight=0.1))
+    assert ok(Trainer(make_ctx("distill", eval_every=0), alg).fit())
