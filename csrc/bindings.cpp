@@ -302,6 +302,51 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t a_m
            "gemm");
 }
 
+// ---------------------------------------------------------------- paged KV decode
+// q [B, Hq, D]; pools [num_blocks, Hkv, 16, D]; block_tables [B, max_blocks] int32; ctx_lens [B] int32
+at::Tensor paged_decode(const at::Tensor& q, const at::Tensor& k_pool, const at::Tensor& v_pool,
+                        const at::Tensor& block_tables, const at::Tensor& ctx_lens, int64_t split_tokens,
+                        double scale, double softcap, int64_t window, const c10::optional<at::Tensor>& status) {
+  check_bf16(q, "q");
+  check_bf16(k_pool, "k_pool");
+  check_contig(q, "q");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && ctx_lens.scalar_type() == at::kInt, "int32 tables");
+  const c10::cuda::CUDAGuard g(q.device());
+  const int B = (int)q.size(0), Hq = (int)q.size(1), D = (int)q.size(2);
+  const int num_blocks = (int)k_pool.size(0), Hkv = (int)k_pool.size(1);
+  const int max_blocks = (int)block_tables.size(1);
+  const int max_ctx = max_blocks * 16;
+  int n_splits = 1;
+  if (split_tokens > 0) n_splits = (int)((max_ctx + split_tokens - 1) / split_tokens);
+  if (n_splits < 1) n_splits = 1;
+  auto out = at::empty_like(q);
+  at::Tensor pa, pm;
+  if (n_splits > 1) {
+    pa = at::empty({(int64_t)B * Hq * n_splits * D}, q.options().dtype(at::kFloat));
+    pm = at::empty({(int64_t)B * Hq * n_splits * 2}, q.options().dtype(at::kFloat));
+  }
+  CHECK_OK(rlb_paged_decode(q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), block_tables.data_ptr<int>(),
+                            ctx_lens.data_ptr<int>(), out.data_ptr(), n_splits > 1 ? pa.data_ptr<float>() : nullptr,
+                            n_splits > 1 ? pm.data_ptr<float>() : nullptr, B, Hq, Hkv, D, max_blocks, num_blocks,
+                            n_splits > 1 ? (int)split_tokens : max_ctx, n_splits, (float)scale, (float)softcap,
+                            (int)window, status.has_value() ? status->data_ptr<int>() : nullptr, cur_stream()),
+           "paged_decode");
+  return out;
+}
+
+void paged_write(const at::Tensor& k_new, const at::Tensor& v_new, at::Tensor& k_pool, at::Tensor& v_pool,
+                 const at::Tensor& slot_block, const at::Tensor& slot_off, const c10::optional<at::Tensor>& status) {
+  check_bf16(k_new, "k_new");
+  check_contig(k_new, "k_new");
+  check_contig(v_new, "v_new");
+  const c10::cuda::CUDAGuard g(k_new.device());
+  CHECK_OK(rlb_paged_write(k_new.data_ptr(), v_new.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+                           slot_block.data_ptr<int>(), slot_off.data_ptr<int>(), (int)k_new.size(0),
+                           (int)k_pool.size(1), (int)k_pool.size(3), (int)k_pool.size(0),
+                           status.has_value() ? status->data_ptr<int>() : nullptr, sm_count(), cur_stream()),
+           "paged_write");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -325,4 +370,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_bwd", &embed_bwd);
   m.def("nf4_dequant", &nf4_dequant);
   m.def("gemm", &gemm);
+  m.def("paged_decode", &paged_decode);
+  m.def("paged_write", &paged_write);
 }
