@@ -57,3 +57,13 @@ cudaError_t rlb_paged_decode(const void* q, const void* k_pool, const void* v_po
 cudaError_t rlb_paged_write(const void* k_new, const void* v_new, void* k_pool, void* v_pool, const int* slot_block,
                             const int* slot_off, int B, int Hkv, int D, int num_blocks, int* status, int sms,
                             cudaStream_t s);
+
+// RMSNorm backward that allocates nothing (no counterpart in the reference):
+// the dw partial sums live in a fixed 4 MiB file-scope __device__ array per
+// device instead of a caller-allocated buffer.  Returns a cudaError_t value;
+// dims that are not a multiple of 256 or exceed 8192 give cudaErrorInvalidValue.
+// Overlapping calls on one device race on the shared scratch.
+extern "C" int rlb_rmsnorm_bwd_noalloc(const void* h, const void* w, const float* rstd, const void* dy,
+                                       const void* dres, void* dx, void* dw_out, int dw_is_f32, long long rows,
+                                       int dim, cudaStream_t stream);
+extern "C" long long rlb_rmsnorm_bwd_noalloc_scratch_bytes();
