@@ -9,6 +9,8 @@ with the head split (csrc/rope.cu).
 
 from __future__ import annotations
 
+import math
+from dataclasses import dataclass
 from typing import Optional, Tuple
 
 import torch
@@ -17,9 +19,29 @@ import torch.nn as nn
 from rl_project_b200.core.config import ModelSpec
 from rl_project_b200.ops.attention import attention_reference, causal_attention
 from rl_project_b200.ops.linear import linear
+from rl_project_b200.ops.paged_attention import paged_decode, paged_write
 from rl_project_b200.ops.rope import RopeTable, rope_split_qkv
 
 KVCache = Tuple[torch.Tensor, torch.Tensor]
+
+
+@dataclass
+class PagedDecodeMeta:
+    """Per-step addressing of a batch of sequences decoding one token each.
+
+    ``positions [B, 1]`` is each new token's position (= cached tokens before
+    it); its K/V go to block ``slot_block[b]``, offset ``slot_off[b]``; attention
+    then covers ``ctx_lens[b] = positions[b] + 1`` tokens through
+    ``block_tables [B, max_blocks]``.  All int32 on the model's device.
+    """
+
+    positions: torch.Tensor
+    max_pos: int
+    block_tables: torch.Tensor
+    ctx_lens: torch.Tensor
+    slot_block: torch.Tensor
+    slot_off: torch.Tensor
+    split_tokens: int = 0
 
 
 def layer_window(spec: ModelSpec, layer_id: int) -> int:
@@ -84,3 +106,15 @@ class CausalSelfAttention(nn.Module):
                                     q_offset=k.shape[2] - T)
         y = y.transpose(1, 2).reshape(B, T, C)
         return self._out(y), present
+
+    def forward_paged(self, x: torch.Tensor, kv: KVCache, meta: PagedDecodeMeta) -> torch.Tensor:
+        """One new token per sequence (``x [B, 1, C]``) against this layer's paged K/V pools."""
+        B = x.shape[0]
+        qkv = self._qkv(x)
+        q, k, v = rope_split_qkv(qkv, self.rope, self.n_head, self.n_kv_head, self.head_dim,
+                                 positions=meta.positions, rotate=self.use_rope, heads_major=False,
+                                 max_pos=meta.max_pos)
+        paged_write(k[:, 0], v[:, 0], kv[0], kv[1], meta.slot_block, meta.slot_off)
+        y = paged_decode(q[:, 0], kv[0], kv[1], meta.block_tables, meta.ctx_lens, 1.0 / math.sqrt(self.head_dim),
+                         self.attn_logit_cap, self.window_size, meta.split_tokens)
+        return self._out(y.reshape(B, 1, self.n_embd))

@@ -55,6 +55,12 @@ class TransformerBlock(nn.Module):
         x, h = add_rms_norm(x, a, self.ln_2.weight, self.ln_2.eps)
         return x + self.ffn(h), present
 
+    def forward_paged(self, x: torch.Tensor, kv, meta) -> torch.Tensor:
+        """Decode step over the paged KV pools (``CausalSelfAttention`` layers only)."""
+        a = self.attn.forward_paged(self.ln_1(x), kv, meta)
+        x, h = add_rms_norm(x, a, self.ln_2.weight, self.ln_2.eps)
+        return x + self.ffn(h)
+
     def forward_fused(self, x: torch.Tensor, pending: Optional[torch.Tensor]) -> Tuple[torch.Tensor, torch.Tensor]:
         """Returns ``(x, f)`` with the block output equal to ``x + f`` (add left pending).
 

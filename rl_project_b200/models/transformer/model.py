@@ -217,6 +217,27 @@ class TransformerLM(nn.Module):
         h = self.transformer.ln_f(x)
         return self.logits(h[:, -1, :]), new_cache
 
+    def supports_paged_decode(self) -> bool:
+        """True when every layer is grouped-query attention (the paged KV kernels' layout)."""
+        from rl_project_b200.models.attention.causal import CausalSelfAttention
+
+        return all(type(b.attn) is CausalSelfAttention for b in self.transformer.h)
+
+    def kv_layout(self) -> Tuple[int, int, int]:
+        """``(n_layer, n_kv_head, head_dim)`` of the KV cache."""
+        return self.spec.n_layer, self.spec.n_kv_head, self.spec.n_embd // self.spec.n_head
+
+    @torch.no_grad()
+    def decode_paged(self, tokens: torch.Tensor, cache: Any, meta: Any) -> torch.Tensor:
+        """Logits ``[B, V]`` for one new token per sequence; K/V go into ``cache`` (a ``PagedKVCache``)."""
+        x = embedding(tokens.view(-1, 1), self.transformer.wte.weight)
+        if self.wpe is not None:
+            x = x + self.wpe(meta.positions.long())
+        for i, blk in enumerate(self.transformer.h):
+            x = blk.forward_paged(x, cache.layer(i), meta)
+        h = self.transformer.ln_f(x)
+        return self.logits(h[:, 0])
+
     @torch.no_grad()
     def generate(self, idx: torch.Tensor, max_new_tokens: int, temperature: float = 1.0, top_k: Optional[int] = None,
                  top_p: Optional[float] = None, min_p: Optional[float] = None, repetition_penalty: float = 1.0,

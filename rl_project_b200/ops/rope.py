@@ -94,13 +94,18 @@ class _RopeQKV(torch.autograd.Function):
 
 def rope_split_qkv(qkv: torch.Tensor, table: RopeTable, n_head: int, n_kv_head: int, head_dim: int,
                    offset: int = 0, positions: Optional[torch.Tensor] = None, heads_major: bool = True,
-                   rotate: bool = True):
+                   rotate: bool = True, max_pos: Optional[int] = None):
     """Split ``qkv [B, T, (Hq+2Hkv)*D]`` into q/k/v (RoPE applied to q and k).
 
     Returns tensors of shape ``[B, H, T, D]`` (``heads_major``) or ``[B, T, H, D]``.
+    ``max_pos`` (an upper bound of ``positions``, known to the caller) avoids
+    reading the positions back from the device.
     """
     B, T, _ = qkv.shape
-    need = (int(positions.max().item()) + 1) if positions is not None else offset + T
+    if positions is not None:
+        need = (max_pos if max_pos is not None else int(positions.max().item())) + 1
+    else:
+        need = offset + T
     if qkv.is_cuda and qkv.dtype == torch.bfloat16 and head_dim % 16 == 0 and rotate:
         cos, sin = table.tables(need, qkv.device)
         pos = positions.to(torch.int32).contiguous() if positions is not None else None

@@ -1,10 +1,16 @@
 """Rollout engine: sample completions from a policy into ``Trajectory`` objects
 (``src/forgeline/rollouts/engine.py`` contract).
 
-Differences by design: ``rollout_many`` batches every prompt x G sample into
-one generation call per prompt length (the reference loops prompts one at a
-time), and ``old_logprobs`` are recorded here once so algorithms need not run a
-second old-policy pass.
+Differences by design: ``rollout_many`` generates every prompt x G sample in
+one pass (the reference loops prompts one at a time), and ``old_logprobs`` are
+recorded here once so algorithms need not run a second old-policy pass.
+
+Generation backend (``RolloutConfig.engine``): ``"auto"`` uses the paged-KV
+continuous-batching ``InferenceEngine`` when the policy's model supports it on
+a GPU -- all sequences of a rollout decode together whatever their length, and
+the G samples of a prompt share one prefill and its KV blocks -- and falls back
+to ``policy.generate`` otherwise; ``"generate"`` forces the fallback.  The
+inference engine runs the live policy weights, so nothing has to be synced.
 """
 
 from __future__ import annotations
@@ -32,12 +38,73 @@ class RolloutConfig:
     max_prompt_length: int = 128
     record_old_logprobs: bool = True
     stop_token_ids: Sequence[int] = ()
+    engine: str = "auto"  # "auto" | "paged" | "generate"
+    engine_max_batch: int = 256  # sequences decoding at once in the paged engine
+    engine_kv_blocks: Optional[int] = None  # KV pool size in 16-token blocks (default: enough for max_batch)
 
 
 class RolloutEngine:
     def __init__(self, policy: PolicyModel, config: RolloutConfig):
         self.policy = policy
         self.cfg = config
+        self._engine: Any = None
+
+    # ------------------------------------------------------------ paged inference backend
+    def _paged_model(self) -> Any:
+        if self.cfg.engine == "generate":
+            return None
+        model = getattr(self.policy, "model", None)
+        ok = model is not None and hasattr(model, "supports_paged_decode") and model.supports_paged_decode()
+        if self.cfg.engine == "paged":
+            if not ok:
+                raise RolloutError("engine='paged' needs a grouped-query TransformerLM policy")
+            return model
+        return model if ok and next(model.parameters()).is_cuda else None
+
+    def inference_engine(self) -> Any:
+        """The paged inference engine over the policy's model (built on first use), or None."""
+        if self._engine is None:
+            model = self._paged_model()
+            if model is None:
+                return None
+            from rl_project_b200.inference.engine import InferenceEngine
+
+            per_seq = (model.spec.block_size + 15) // 16 + 1
+            self._engine = InferenceEngine(model, max_batch=self.cfg.engine_max_batch,
+                                           max_blocks=self.cfg.engine_kv_blocks or self.cfg.engine_max_batch * per_seq)
+        return self._engine
+
+    def release_engine(self) -> None:
+        """Free the paged engine's KV pool (it is rebuilt on the next rollout)."""
+        self._engine = None
+
+    def _generate_paged(self, engine: Any, prompts: List[List[int]], G: int,
+                        temperature: Optional[float]) -> List[List[int]]:
+        from rl_project_b200.inference.requests import SamplingParams
+
+        temp = self.cfg.temperature if temperature is None else temperature
+        limit = engine.max_seq_len
+        reqs = []
+        for p in prompts:
+            params = SamplingParams(max_tokens=max(1, min(self.cfg.max_new_tokens, limit - len(p))), temperature=temp,
+                                    top_k=self.cfg.top_k, top_p=self.cfg.top_p,
+                                    stop_token_ids=[int(t) for t in self.cfg.stop_token_ids])
+            reqs.extend(engine.submit(p, params) for _ in range(G))
+        was_training = engine.model.training
+        try:
+            while not all(r.finished for r in reqs):
+                engine.step()
+        finally:
+            engine.model.train(was_training)
+        failed = [r for r in reqs if r.error]
+        if failed:
+            raise RolloutError(f"generation failed: {failed[0].error}")
+        return [r.generated_tokens for r in reqs]
+
+    def _old_logprobs(self, prompts: torch.Tensor, responses: torch.Tensor) -> Optional[torch.Tensor]:
+        if not self.cfg.record_old_logprobs:
+            return None
+        return self.policy.logprobs(prompts, responses).detach()
 
     def _settings(self, temperature: Optional[float] = None) -> GenerationSettings:
         return GenerationSettings(max_new_tokens=self.cfg.max_new_tokens,
@@ -65,10 +132,10 @@ class RolloutEngine:
         old = self.policy.logprobs(prompts, responses).detach() if self.cfg.record_old_logprobs else None
         return responses, old
 
-    def _to_trajs(self, prompt_ids, responses, old, task, prompt_text) -> List[Trajectory]:
+    def _to_trajs(self, prompt_ids, responses, old, task, prompt_text, lengths=None) -> List[Trajectory]:
         out = []
         for g in range(responses.shape[0]):
-            resp = self._trim(responses[g])
+            resp = responses[g, : lengths[g]] if lengths is not None else self._trim(responses[g])
             out.append(Trajectory(prompt_ids=prompt_ids.detach().cpu(), response_ids=resp.detach().cpu(),
                                   prompt_text=prompt_text, response_text=self._decode(resp), task=dict(task or {}),
                                   truncated=bool(resp.numel() >= self.cfg.max_new_tokens),
@@ -83,6 +150,12 @@ class RolloutEngine:
         if prompt_ids.numel() == 0:
             raise RolloutError("empty prompt")
         batch = prompt_ids.unsqueeze(0).repeat(G, 1).to(self.policy.device)
+        engine = self.inference_engine()
+        if engine is not None:
+            gen = self._generate_paged(engine, [prompt_ids.tolist()], G, temperature)
+            responses = _pad(gen, batch.device)
+            return self._to_trajs(prompt_ids, responses, self._old_logprobs(batch, responses), task, prompt_text,
+                                  lengths=[len(g) for g in gen])
         responses, old = self._sample(batch, temperature)
         return self._to_trajs(prompt_ids, responses, old, task, prompt_text)
 
@@ -99,6 +172,21 @@ class RolloutEngine:
                 raise RolloutError("empty prompt")
             by_len[p.numel()].append(i)
         out: List[Optional[List[Trajectory]]] = [None] * len(prompts)
+        engine = self.inference_engine()
+        if engine is not None:
+            gen = self._generate_paged(engine, [p.tolist() for p in clipped], G, None)
+            dev = self.policy.device
+            for _, idx in sorted(by_len.items()):
+                rows = [gen[i * G + g] for i in idx for g in range(G)]
+                responses = _pad(rows, dev)
+                batch = torch.cat([clipped[i].unsqueeze(0).repeat(G, 1) for i in idx], 0).to(dev)
+                old = self._old_logprobs(batch, responses)
+                for j, i in enumerate(idx):
+                    sl = slice(j * G, (j + 1) * G)
+                    out[i] = self._to_trajs(clipped[i], responses[sl], old[sl] if old is not None else None,
+                                            tasks[i] if tasks else None, prompt_texts[i] if prompt_texts else "",
+                                            lengths=[len(r) for r in rows[sl]])
+            return out  # type: ignore[return-value]
         for _, idx in sorted(by_len.items()):
             batch = torch.cat([clipped[i].unsqueeze(0).repeat(G, 1) for i in idx], 0).to(self.policy.device)
             responses, old = self._sample(batch)
@@ -111,6 +199,14 @@ class RolloutEngine:
     def _decode(self, ids: torch.Tensor) -> str:
         dec = getattr(self.policy, "decode", None)
         return dec(ids) if dec is not None else ""
+
+
+def _pad(rows: List[List[int]], device: torch.device) -> torch.Tensor:
+    R = max(len(r) for r in rows)
+    out = torch.zeros((len(rows), R), dtype=torch.long)
+    for i, r in enumerate(rows):
+        out[i, : len(r)] = torch.as_tensor(r, dtype=torch.long)
+    return out.to(device, non_blocking=True)
 
 
 def stack_group(trajectories: Sequence[Trajectory], pad_value: int = 0):
