@@ -1,6 +1,6 @@
 """Kernel micro-benchmarks (CUDA-event timing after warm-up, L2 flushed between timed calls).
 
-    python -m rl_project_b200.ops.bench_kernels [--which gemm,norm,logprob,adam]
+    python -m rl_project_b200.ops.bench_kernels [--which gemm,mem,adam,paged]
 
 Prints one JSON line per case with the achieved TFLOP/s or GB/s and the
 fraction of the measured peaks in MEASURED_PEAKS.json ("of measured").
@@ -125,6 +125,31 @@ def bench_adam():
                       "frac_of_measured_hbm": moved / t / 1e6 / peak_gbs}), flush=True)
 
 
+def bench_paged(cases=((64, 1536, 32, 8, 128), (256, 1024, 32, 8, 128), (8, 4096, 32, 8, 128),
+                        (512, 512, 32, 8, 64))):
+    """Paged decode attention: (sequences, context, Hq, Hkv, D); bytes = K and V of every context read once."""
+    import math
+
+    from rl_project_b200.ops.paged_attention import paged_decode
+
+    _, peak_gbs = _peaks()
+    for B, ctx, Hq, Hkv, D in cases:
+        nb = ctx // 16
+        k_pool = torch.randn(B * nb, Hkv, 16, D, device="cuda").to(torch.bfloat16)
+        v_pool = torch.randn_like(k_pool)
+        tables = torch.randperm(B * nb, device="cuda").int().view(B, nb)
+        lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+        q = torch.randn(B, Hq, D, device="cuda").to(torch.bfloat16)
+        sms = torch.cuda.get_device_properties(0).multi_processor_count
+        splits = max(1, min((2 * sms + B * Hkv - 1) // (B * Hkv), ctx // 128))
+        split = 0 if splits == 1 else (ctx // splits + 15) // 16 * 16
+        t = time_ms(lambda: paged_decode(q, k_pool, v_pool, tables, lens, 1 / math.sqrt(D), split_tokens=split))
+        moved = 2 * B * ctx * Hkv * D * 2
+        print(json.dumps({"kernel": "paged_decode", "seqs": B, "ctx": ctx, "Hq": Hq, "Hkv": Hkv, "D": D,
+                          "split_tokens": split, "ms": round(t, 4), "gbs": round(moved / t / 1e6, 1),
+                          "frac_of_measured_hbm": round(moved / t / 1e6 / peak_gbs, 3)}), flush=True)
+
+
 MODEL_SHAPES = [
     (32768, 3072, 2048, "nt"), (32768, 2048, 2048, "nt"), (32768, 16384, 2048, "nt"), (32768, 2048, 8192, "nt"),
     (32768, 2048, 16384, "nn"), (32768, 8192, 2048, "nn"), (16384, 2048, 32768, "tn"), (2048, 8192, 32768, "tn"),
@@ -133,9 +158,11 @@ MODEL_SHAPES = [
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--which", default="gemm,mem,adam")
+    ap.add_argument("--which", default="gemm,mem,adam,paged")
     args = ap.parse_args()
     which = set(args.which.split(","))
+    if "paged" in which:
+        bench_paged()
     if "gemm" in which:
         bench_gemm(MODEL_SHAPES)
     if "mem" in which:
