@@ -172,3 +172,23 @@ def build_strategy(cfg: DistributedConfig):
     if cfg.strategy not in STRATEGIES:
         raise DistributedConfigError(f"unknown strategy {cfg.strategy!r}")
     return STRATEGIES[cfg.strategy](cfg)
+
+
+def validate_distributed_config(cfg: DistributedConfig, world_size: Optional[int] = None) -> dict:
+    """CPU-only check of a distributed config: returns the implied topology or raises
+    ``DistributedConfigError`` (``src/forgeline/distributed/strategies.py:221-232`` contract,
+    extended with the expert-parallel degree)."""
+    from rl_project_b200.parallel import runtime as rt
+
+    cfg.validate()
+    ws = world_size if world_size is not None else rt.read_launcher_env().world_size
+    dp = rt.validate_topology(ws, cfg.tensor_parallel_size, cfg.pipeline_parallel_size, cfg.expert_parallel_size)
+    needs = {"tensor_parallel": cfg.tensor_parallel_size, "pipeline_parallel": cfg.pipeline_parallel_size,
+             "expert_parallel": cfg.expert_parallel_size}
+    if cfg.strategy in needs and needs[cfg.strategy] == 1:
+        raise DistributedConfigError(f"{cfg.strategy} strategy needs {cfg.strategy}_size > 1")
+    if cfg.strategy == "deepspeed":
+        DeepSpeedStrategy.load_config(cfg.deepspeed_config)
+    return {"world_size": ws, "tensor_parallel": cfg.tensor_parallel_size,
+            "pipeline_parallel": cfg.pipeline_parallel_size, "expert_parallel": cfg.expert_parallel_size,
+            "data_parallel": dp}
