@@ -1,0 +1,262 @@
+"""Read-only views over what the framework writes to disk (the data layer of the dashboard).
+
+Sources: run directories (``metrics.jsonl`` / ``events.jsonl`` of the local
+metrics sink, the run's ``manifest.yaml``, checkpoint directories, evaluation
+result files), the candidate registry JSON, and ``benchmarks/**/results.json``
+evidence records.  The same views as ``src/forgeline/dashboard/data.py:26-295``.
+Everything is plain file IO, testable and exportable without the HTTP server.
+Checkpoints are loaded (``torch.load`` runs pickled code) only when they lie
+under a configured runs root, never from an arbitrary request path.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import time
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any, Dict, Iterable, Iterator, List, Optional
+
+MAX_POINTS = 1500
+_SKIP = {".git", "__pycache__", "node_modules", ".venv", "site-packages"}
+_NOT_RESULTS = {"manifest.json", "experiment.json", "metrics.jsonl", "events.jsonl"}
+
+
+def _run_id(path: Path) -> str:
+    return hashlib.sha1(str(path.resolve()).encode()).hexdigest()[:10]
+
+
+def _read_jsonl(path: Path, limit: Optional[int] = None) -> List[Dict[str, Any]]:
+    if not path.exists():
+        return []
+    rows = []
+    with path.open() as fh:
+        for line in fh:
+            line = line.strip()
+            if line:
+                try:
+                    rows.append(json.loads(line))
+                except json.JSONDecodeError:
+                    pass  # a half-written last line of a live run
+    return rows[-limit:] if limit else rows
+
+
+def _safe_json(path: Path) -> Dict[str, Any]:
+    try:
+        return json.loads(path.read_text())
+    except Exception:  # noqa: BLE001
+        return {}
+
+
+def _dirs(root: Path, max_depth: int) -> Iterator[Path]:
+    root = root.resolve()
+    base = len(root.parts)
+    for dirpath, dirnames, _ in os.walk(root):
+        here = Path(dirpath)
+        dirnames[:] = [d for d in dirnames if d not in _SKIP and not d.endswith(".tmp")]
+        if len(here.parts) - base >= max_depth:
+            dirnames[:] = []
+        yield here
+
+
+def downsample(points: List[List[float]], limit: int = MAX_POINTS) -> List[List[float]]:
+    """At most ``limit`` evenly spaced points, always keeping the last one."""
+    if len(points) <= limit:
+        return points
+    stride = len(points) / limit
+    out = [points[int(i * stride)] for i in range(limit)]
+    out[-1] = points[-1]
+    return out
+
+
+def _load_manifest(run_dir: Path) -> Dict[str, Any]:
+    for name in ("manifest.yaml", "manifest.yml", "manifest.json"):
+        p = run_dir / name
+        if p.exists():
+            try:
+                from rl_project_b200.core.config import load_config
+
+                return dict(load_config(p))
+            except Exception:  # noqa: BLE001 - show the run even if its manifest no longer parses
+                return {}
+    return {}
+
+
+def _status(events: List[Dict[str, Any]]) -> str:
+    names = {e.get("event") for e in events}
+    for name, status in (("run.failed", "failed"), ("run.finished", "finished"), ("run.started", "running")):
+        if name in names:
+            return status
+    return "unknown"
+
+
+def discover_runs(roots: Iterable[str | Path], max_depth: int = 4) -> List[Dict[str, Any]]:
+    """Every directory under the roots holding ``metrics.jsonl`` or ``events.jsonl``, newest first."""
+    runs: Dict[str, Dict[str, Any]] = {}
+    for root in map(Path, roots):
+        if not root.exists():
+            continue
+        for d in _dirs(root, max_depth):
+            mpath, epath = d / "metrics.jsonl", d / "events.jsonl"
+            if not (mpath.exists() or epath.exists()):
+                continue
+            events = _read_jsonl(epath)
+            manifest = _load_manifest(d)
+            last = _read_jsonl(mpath, limit=1)
+            mtime = max((p.stat().st_mtime for p in (mpath, epath) if p.exists()), default=0.0)
+            status = _status(events)
+            runs[_run_id(d)] = {
+                "id": _run_id(d), "name": manifest.get("name") or d.name, "path": str(d),
+                "algorithm": manifest.get("algorithm") or next((e["algorithm"] for e in events
+                                                                 if e.get("algorithm")), ""),
+                "model_preset": manifest.get("model_preset", ""),
+                "strategy": (manifest.get("distributed") or {}).get("strategy", ""),
+                "orchestration": (manifest.get("orchestration") or {}).get("type", "local") if manifest else "",
+                "status": status, "last_step": last[0].get("step") if last else None, "n_events": len(events),
+                "updated_at": mtime, "live": status == "running" and time.time() - mtime < 120}
+    return sorted(runs.values(), key=lambda r: r["updated_at"], reverse=True)
+
+
+def run_detail(run_dir: str | Path) -> Dict[str, Any]:
+    d = Path(run_dir)
+    series: Dict[str, List[List[float]]] = {}
+    for row in _read_jsonl(d / "metrics.jsonl"):
+        step = row.get("step")
+        for k, v in row.items():
+            if k not in ("step", "ts") and isinstance(v, (int, float)) and not isinstance(v, bool):
+                series.setdefault(k, []).append([step, v])
+    events = _read_jsonl(d / "events.jsonl")
+    return {"id": _run_id(d), "path": str(d), "manifest": _load_manifest(d), "status": _status(events),
+            "series": {k: downsample(v) for k, v in sorted(series.items())}, "events": events[-500:],
+            "summary": next((e for e in reversed(events) if e.get("event") == "run.finished"), None),
+            "checkpoints": list_checkpoints(d), "evaluations": list_evaluations(d)}
+
+
+def list_checkpoints(root: str | Path, max_depth: int = 3) -> List[Dict[str, Any]]:
+    from rl_project_b200.checkpoints.manager import CheckpointManager
+
+    root = Path(root)
+    if not root.exists():
+        return []
+    out = []
+    for d in _dirs(root, max_depth):
+        if not ((d / "manifest.json").exists() and (d / "model.pt").exists()):
+            continue
+        try:
+            manifest, valid, error = CheckpointManager.validate(d), True, ""
+        except Exception as exc:  # noqa: BLE001
+            manifest, valid, error = _safe_json(d / "manifest.json"), False, str(exc)
+        latest = d.parent / "LATEST"
+        spec = manifest.get("model_spec") or {}
+        files = manifest.get("files") or {}
+        out.append({"path": str(d), "name": d.name, "step": manifest.get("step"),
+                    "algorithm": manifest.get("algorithm", ""), "created_at": manifest.get("created_at"),
+                    "valid": valid, "error": error, "size_bytes": sum(int(f.get("size", 0)) for f in files.values()),
+                    "files": sorted(files), "is_best": d.name == "best",
+                    "is_latest": latest.exists() and latest.read_text().strip() == d.name,
+                    "model": {k: spec[k] for k in ("n_layer", "n_head", "n_kv_head", "n_embd", "vocab_size",
+                                                   "block_size") if k in spec}})
+    return sorted(out, key=lambda c: (c["step"] is None, c["step"] or 0))
+
+
+def list_evaluations(root: str | Path, max_depth: int = 3) -> List[Dict[str, Any]]:
+    """Result files written by ``save_results``."""
+    from rl_project_b200.evaluation.results import load_results
+
+    root = Path(root)
+    if not root.exists():
+        return []
+    out = []
+    for d in _dirs(root, max_depth):
+        for p in sorted(d.glob("*.json")) + sorted(d.glob("*.jsonl")):
+            if p.name in _NOT_RESULTS or p.stat().st_size > 20_000_000:
+                continue
+            try:
+                results = load_results(p)
+            except Exception:  # noqa: BLE001 - not an evaluation file
+                continue
+            if results:
+                out.append({"path": str(p), "results": [{"suite": r.suite, "metrics": r.metrics,
+                                                         "n_samples": r.n_samples, "details": r.details}
+                                                        for r in results]})
+    return out
+
+
+def registry_view(path: str | Path) -> Dict[str, Any]:
+    p = Path(path)
+    if not p.exists():
+        return {"path": str(p), "exists": False, "models": {}}
+    from rl_project_b200.deployment.registry import CandidateRegistry
+
+    models: Dict[str, List[Dict[str, Any]]] = {}
+    for c in CandidateRegistry(p).list():
+        models.setdefault(c.name, []).append(c.to_dict())
+    return {"path": str(p), "exists": True, "models": models}
+
+
+def benchmark_records(root: str | Path) -> List[Dict[str, Any]]:
+    root = Path(root)
+    if not root.exists():
+        return []
+    out = []
+    for res in sorted(root.rglob("results.json")):
+        data = _safe_json(res)
+        summary = res.parent / "summary.md"
+        out.append({"record": str(res.parent.relative_to(root)), "evidence": data.get("evidence", ""),
+                    "revalidation_required": bool(data.get("revalidation_required", False)),
+                    "revalidation_recommended": bool(data.get("revalidation_recommended", False)),
+                    "published": data.get("published", True), "metrics": data.get("metrics", {}),
+                    "notes": data.get("notes", []), "summary": summary.read_text() if summary.exists() else ""})
+    return out
+
+
+def inspect_checkpoint(path: str | Path, text: str = "", max_tokens: int = 48,
+                       data_dir: Optional[str] = None) -> Dict[str, Any]:
+    import torch
+
+    from rl_project_b200.evaluation.inspection import (activation_flow, attention_patterns, layer_summary,
+                                                       weight_statistics)
+    from rl_project_b200.models.loading import load_model_from_checkpoint, resolve_tokenizer_for_checkpoint
+
+    model, spec, state = load_model_from_checkpoint(path, "cpu")
+    model = model.float().eval()
+    stats = weight_statistics(model)
+    out: Dict[str, Any] = {"checkpoint": str(path), "step": state.step, "algorithm": state.algorithm,
+                           "spec": spec.to_dict(), "parameters": sum(s["numel"] for s in stats),
+                           "layers": layer_summary(spec), "weights": stats}
+    if text:
+        try:
+            tok = resolve_tokenizer_for_checkpoint(state, data_dir)
+            ids = torch.tensor([tok.encode(text)[-max_tokens:]], dtype=torch.long)
+            out["tokens"] = [tok.decode([i]) for i in ids[0].tolist()]
+            out["attention"] = attention_patterns(model, ids, max_tokens=max_tokens)
+            out["activations"] = activation_flow(model, ids)
+        except Exception as exc:  # noqa: BLE001
+            out["inspection_error"] = f"{type(exc).__name__}: {exc}"
+    return out
+
+
+@dataclass
+class DashboardSources:
+    runs: List[str] = field(default_factory=lambda: ["runs"])
+    registry: str = "registry/candidates.json"
+    benchmarks: str = "benchmarks"
+
+    def checkpoint_allowed(self, path: str | Path) -> bool:
+        """Only checkpoint directories under a configured runs root may be loaded."""
+        target = Path(path).resolve()
+        for root in self.runs:
+            r = Path(root).resolve()
+            if (r == target or r in target.parents) and (target / "manifest.json").exists():
+                return True
+        return False
+
+
+def snapshot(sources: DashboardSources, include_runs_detail: bool = True) -> Dict[str, Any]:
+    runs = discover_runs(sources.runs)
+    return {"generated_at": time.time(),
+            "sources": {"runs": sources.runs, "registry": sources.registry, "benchmarks": sources.benchmarks},
+            "runs": runs, "run_details": {r["id"]: run_detail(r["path"]) for r in runs} if include_runs_detail else {},
+            "registry": registry_view(sources.registry), "benchmarks": benchmark_records(sources.benchmarks)}
