@@ -154,7 +154,7 @@ def cmd_train(args: argparse.Namespace) -> int:
         summary = trainer.fit()
     finally:
         if (manifest.orchestration or {}).get("type") == "ray":
-            from rl_project_b200.orchestration.ray_backend import shutdown_pools
+            from rl_project_b200.orchestration.pools import shutdown_pools
 
             shutdown_pools()
         ctx.close()
@@ -220,10 +220,11 @@ def cmd_evaluate(args: argparse.Namespace) -> int:
     policy = None
     if args.ray_workers:
         from rl_project_b200.orchestration.config import RayConfig
-        from rl_project_b200.orchestration.ray_backend import RayEvaluator
+        from rl_project_b200.orchestration.pools import EvaluatorPool
 
-        cfg = RayConfig(address=args.ray_address, cpus_per_worker=args.ray_cpus_per_worker)
-        with RayEvaluator(args.checkpoint, args.ray_workers, cfg, data_dir=args.data_dir) as evaluator:
+        cfg = RayConfig(address=args.ray_address, cpus_per_worker=args.ray_cpus_per_worker,
+                        backend=args.worker_backend)
+        with EvaluatorPool(args.checkpoint, args.ray_workers, cfg, data_dir=args.data_dir) as evaluator:
             for name in args.suites:
                 results.append(evaluator.run(name, max_new_tokens=args.max_tokens, n_shot=args.n_shot,
                                              max_tasks=args.max_tasks, offline=args.offline))
@@ -559,6 +560,8 @@ def build_parser() -> argparse.ArgumentParser:
             s.add_argument("--ray-workers", type=int, default=0)
             s.add_argument("--ray-address", default=None)
             s.add_argument("--ray-cpus-per-worker", type=float, default=1.0)
+            s.add_argument("--worker-backend", default="ray", choices=["ray", "threads"],
+                           help="where --ray-workers run: Ray actors or in-process threads")
         else:
             s.add_argument("--host", default="127.0.0.1")
             s.add_argument("--port", type=int, default=8000)

@@ -36,8 +36,11 @@ class RayConfig:
     task_timeout_s: Optional[float] = None
     worker_torch_threads: int = 1
     namespace: str = "forgeline"
+    backend: str = "ray"  # "ray" actors, or "threads": in-process workers (single node, tests)
 
     def validate(self) -> None:
+        if self.backend not in ("ray", "threads"):
+            raise ConfigError("orchestration.backend must be 'ray' or 'threads'")
         if self.address is not None and (self.num_cpus is not None or self.num_gpus is not None):
             raise ConfigError("orchestration.num_cpus/num_gpus apply only when Ray is started locally (address unset)")
         if min(self.rollout_workers, self.reward_workers) < 0:

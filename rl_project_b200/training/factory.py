@@ -54,7 +54,7 @@ def _attach_orchestration(algorithm, manifest, reward_cfg):
     orch = manifest.orchestration or {}
     if orch.get("type", "local") != "ray":
         return algorithm
-    from rl_project_b200.orchestration.ray_backend import attach_to_algorithm
+    from rl_project_b200.orchestration.pools import attach_to_algorithm
 
     attach_to_algorithm(algorithm, orch, reward_cfg, seed=manifest.trainer.seed)
     return algorithm
