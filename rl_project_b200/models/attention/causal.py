@@ -69,6 +69,7 @@ class CausalSelfAttention(nn.Module):
         self.resid_dropout = nn.Dropout(spec.dropout)
         self.rope = RopeTable(self.head_dim, spec.rope_theta, spec.rope_scaling_type, spec.rope_scaling_factor,
                               spec.block_size)
+        self.tp_group = None  # set by tensor parallelism (heads then divided over the group)
 
     def _qkv(self, x: torch.Tensor) -> torch.Tensor:
         mods = (self.q_proj, self.k_proj, self.v_proj)
@@ -79,7 +80,11 @@ class CausalSelfAttention(nn.Module):
         return torch.cat([m(x) for m in mods], dim=-1)
 
     def _out(self, y: torch.Tensor) -> torch.Tensor:
-        if type(self.c_proj) is nn.Linear:
+        if self.tp_group is not None:
+            from rl_project_b200.parallel.tensor_parallel import row_parallel_out
+
+            y = row_parallel_out(y, self.c_proj, self.tp_group)
+        elif type(self.c_proj) is nn.Linear:
             y = linear(y, self.c_proj.weight, self.c_proj.bias)
         else:
             y = self.c_proj(y)
@@ -87,6 +92,10 @@ class CausalSelfAttention(nn.Module):
 
     def forward(self, x: torch.Tensor, past_kv: Optional[KVCache] = None, positions: Optional[torch.Tensor] = None):
         B, T, C = x.shape
+        if self.tp_group is not None:
+            from rl_project_b200.parallel.tensor_parallel import copy_to_tp
+
+            x = copy_to_tp(x, self.tp_group)
         qkv = self._qkv(x)
         offset = past_kv[0].shape[2] if past_kv is not None else 0
         # q/k/v come out token-major [B, T, H, D]; attention reads them through [B, H, T, D]
@@ -104,7 +113,7 @@ class CausalSelfAttention(nn.Module):
         else:
             y = attention_reference(q, k, v, window=self.window_size, softcap=self.attn_logit_cap,
                                     q_offset=k.shape[2] - T)
-        y = y.transpose(1, 2).reshape(B, T, C)
+        y = y.transpose(1, 2).reshape(B, T, self.n_head * self.head_dim)
         return self._out(y), present
 
     def forward_paged(self, x: torch.Tensor, kv: KVCache, meta: PagedDecodeMeta) -> torch.Tensor:
@@ -117,4 +126,4 @@ class CausalSelfAttention(nn.Module):
         paged_write(k[:, 0], v[:, 0], kv[0], kv[1], meta.slot_block, meta.slot_off)
         y = paged_decode(q[:, 0], kv[0], kv[1], meta.block_tables, meta.ctx_lens, 1.0 / math.sqrt(self.head_dim),
                          self.attn_logit_cap, self.window_size, meta.split_tokens)
-        return self._out(y.reshape(B, 1, self.n_embd))
+        return self._out(y.reshape(B, 1, self.n_head * self.head_dim))

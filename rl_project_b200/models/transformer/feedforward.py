@@ -32,17 +32,25 @@ class SwiGLUFeedForward(nn.Module):
         self.w2 = nn.Linear(hidden_dim, dim, bias=bias)
         self.w3 = nn.Linear(dim, hidden_dim, bias=bias)
         self.dropout = nn.Dropout(dropout)
+        self.tp_group = None  # set by tensor parallelism (hidden width then split over the group)
 
     def _fusable(self) -> bool:
         return type(self.w1) is nn.Linear and type(self.w3) is nn.Linear and self.w1.bias is None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.tp_group is not None:
+            from rl_project_b200.parallel.tensor_parallel import copy_to_tp, row_parallel_out
+
+            x = copy_to_tp(x, self.tp_group)
         if self._fusable():
             w13 = torch.cat([self.w1.weight, self.w3.weight], dim=0)
             a = swiglu(linear(x, w13))
         else:  # adapters wrap w1/w3: run them as modules
             a = swiglu(torch.cat([self.w1(x), self.w3(x)], dim=-1))
-        out = self.w2(a) if type(self.w2) is not nn.Linear else linear(a, self.w2.weight, self.w2.bias)
+        if self.tp_group is not None:
+            out = row_parallel_out(a, self.w2, self.tp_group)
+        else:
+            out = self.w2(a) if type(self.w2) is not nn.Linear else linear(a, self.w2.weight, self.w2.bias)
         return self.dropout(out)
 
 
@@ -53,9 +61,15 @@ class GELUFeedForward(nn.Module):
         self.c_fc = nn.Linear(dim, hidden_dim, bias=bias)
         self.c_proj = nn.Linear(hidden_dim, dim, bias=bias)
         self.dropout = nn.Dropout(dropout)
+        self.tp_group = None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return self.dropout(self.c_proj(gelu_tanh(self.c_fc(x))))
+        if self.tp_group is None:
+            return self.dropout(self.c_proj(gelu_tanh(self.c_fc(x))))
+        from rl_project_b200.parallel.tensor_parallel import copy_to_tp, row_parallel_out
+
+        h = gelu_tanh(self.c_fc(copy_to_tp(x, self.tp_group)))
+        return self.dropout(row_parallel_out(h, self.c_proj, self.tp_group))
 
 
 def make_ffn(spec: ModelSpec, hidden_dim: Optional[int] = None) -> nn.Module:

@@ -138,6 +138,15 @@ class FusedAdamW(torch.optim.Optimizer):
         return self.norm_coef[0]
 
     @torch.no_grad()
+    def arm_clip(self, norm: torch.Tensor, max_norm: float) -> None:
+        """Use a norm computed elsewhere (model-parallel reductions) for the next ``step``'s clip coefficient:
+        ``min(1, max_norm / (norm + 1e-6))``, or 0 (skip the update) when the norm is not finite."""
+        self.norm_coef[0] = norm
+        coef = (max_norm / (norm + 1e-6)).clamp(max=1.0) if max_norm > 0 else torch.ones_like(norm)
+        self.norm_coef[1] = torch.where(torch.isfinite(norm), coef, torch.zeros_like(coef))
+        self._armed = True
+
+    @torch.no_grad()
     def step(self, closure=None):
         loss = closure() if closure is not None else None
         self._build_desc()

@@ -1,0 +1,224 @@
+"""Tensor-, pipeline- and 3-D-parallel training (strategies ``tensor_parallel``,
+``pipeline_parallel`` and ``hybrid``).
+
+One process per GPU.  ``setup`` builds the ``ParallelMesh`` (TP innermost);
+``prepare_training`` shards the algorithm's model over the TP group
+(``apply_tensor_parallel``) and cuts it into pipeline stages
+(``partition_model``).  With more than one stage the trainer hands each step's
+micro-batches to ``run_micro_batches`` (1F1B schedule, real backward on every
+stage).  ``finish_gradients`` averages gradients over the data-parallel group
+(bucketed all-reduce) and sums the tied-embedding gradient of the first and
+last stage.  ``clip_grad_norm`` computes the global norm over the model-parallel
+ranks with every parameter counted once (TP-sharded weights on every TP rank,
+replicated ones on TP rank 0 only, the tied embedding on the first stage
+only).  Checkpoints are per-rank shards gathered on rank 0.
+
+Reference: ``src/forgeline/distributed/{topology,tensor_parallel,pipeline_parallel}.py``
+(whose TP kept global head counts and whose PP had no backward on non-last
+stages); this module trains the same 3-D configurations correctly.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Any, Dict, List, Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from rl_project_b200.core.config import DistributedConfig
+from rl_project_b200.core.errors import DistributedConfigError
+from rl_project_b200.parallel import runtime as rt
+from rl_project_b200.parallel.data_parallel import _buckets
+from rl_project_b200.parallel.pipeline import PipelineRunner, partition_model
+from rl_project_b200.parallel.tensor_parallel import apply_tensor_parallel
+from rl_project_b200.parallel.topology import ParallelMesh
+
+_ACTIVE_MESH: Optional[ParallelMesh] = None
+
+
+def active_mesh() -> Optional[ParallelMesh]:
+    return _ACTIVE_MESH
+
+
+def data_parallel_rank() -> int:
+    """Rank that decides which data a process sees: the DP rank under a mesh, else the global rank."""
+    if _ACTIVE_MESH is not None:
+        return _ACTIVE_MESH.dp_rank
+    return dist.get_rank() if dist.is_available() and dist.is_initialized() else 0
+
+
+def _find_model(alg: Any) -> nn.Module:
+    for owner in (getattr(alg, "policy", None), alg):
+        m = getattr(owner, "model", None) if owner is not None else None
+        if isinstance(m, nn.Module) and hasattr(m, "transformer"):
+            return m
+    raise DistributedConfigError(f"{type(alg).__name__} has no TransformerLM to parallelise")
+
+
+class MeshStrategy:
+    def __init__(self, cfg: DistributedConfig, name: str = "hybrid"):
+        self.cfg = cfg
+        self.name = name
+        self.mesh: Optional[ParallelMesh] = None
+        self.model: Optional[nn.Module] = None
+        self.runner: Optional[PipelineRunner] = None
+        self.owns_grad_clip = True
+
+    # ------------------------------------------------------------ process group
+    def setup(self) -> None:
+        global _ACTIVE_MESH
+        rt.init_process_group(self.cfg.backend, timeout_s=self.cfg.timeout_s)
+        tp, pp = self.cfg.tensor_parallel_size, self.cfg.pipeline_parallel_size
+        if self.name == "tensor_parallel" and tp == 1:
+            raise DistributedConfigError("tensor_parallel strategy needs tensor_parallel_size > 1")
+        if self.name == "pipeline_parallel" and pp == 1:
+            raise DistributedConfigError("pipeline_parallel strategy needs pipeline_parallel_size > 1")
+        from datetime import timedelta
+
+        self.mesh = ParallelMesh(rt.world_size(), tp, pp, 1, rt.rank()).build_groups(
+            timeout=timedelta(seconds=self.cfg.timeout_s))
+        _ACTIVE_MESH = self.mesh
+
+    def teardown(self) -> None:
+        global _ACTIVE_MESH
+        _ACTIVE_MESH = None
+        rt.destroy_process_group()
+
+    def world_size(self) -> int:
+        return rt.world_size()
+
+    def rank(self) -> int:
+        return rt.rank()
+
+    def is_main_process(self) -> bool:
+        return rt.rank() == 0
+
+    def barrier(self) -> None:
+        rt.barrier()
+
+    def _group(self, name: str):
+        return self.mesh.groups.get(name) if self.mesh is not None else None
+
+    # ------------------------------------------------------------ model
+    def prepare_training(self, trainer) -> None:
+        if self.mesh is None:
+            raise DistributedConfigError("call setup() before building the trainer")
+        m = self.mesh
+        model = _find_model(trainer.alg)
+        if m.tp_size > 1:
+            apply_tensor_parallel(model, self._group("tp"), m.tp_rank, m.tp_size)
+            for blk in model.transformer.h:
+                for p in list(blk.attn.q_proj.parameters()) + list(blk.attn.k_proj.parameters()) + \
+                        list(blk.attn.v_proj.parameters()) + [blk.attn.c_proj.weight]:
+                    p._tp_sharded = True
+                for p in blk.ffn.parameters():
+                    if p.dim() == 2:
+                        p._tp_sharded = True
+        if m.pp_size > 1:
+            if not hasattr(trainer.alg, "pipeline_inputs"):
+                raise DistributedConfigError(f"pipeline parallelism needs an algorithm with pipeline_inputs "
+                                             f"(pretrain, sft); got {trainer.alg.name}")
+            partition_model(model, m.pp_rank, m.pp_size)
+            self.runner = PipelineRunner(model, m.pp_rank, m.pp_size, m.prev_stage, m.next_stage)
+        self.model = model
+        if m.dp_size > 1:
+            src = m.dp_ranks()[0]
+            with torch.no_grad():
+                for p in model.parameters():
+                    dist.broadcast(p.data, src=src, group=self._group("dp"))
+
+    # ------------------------------------------------------------ step
+    def run_micro_batches(self, trainer, batch: Any, n_micro: int):
+        """Pipeline schedule for one step: returns (losses, metrics) like the trainer's own loop."""
+        if self.runner is None:
+            return None
+        alg = trainer.alg
+        micro = [alg.pipeline_inputs(batch, i, n_micro) for i in range(n_micro)]
+        idx0 = micro[0][0]
+        C = self.model.spec.n_embd
+        dtype = next(p for p in self.model.parameters()).dtype
+        device = idx0.device
+        total = self.runner.run(micro, (idx0.shape[0], idx0.shape[1], C), dtype, device, 1.0 / n_micro)
+        pp = self._group("pp")
+        dist.all_reduce(total, group=pp)  # the last stage's loss, on every stage (for logging and the finite check)
+        return [total], {}
+
+    def finish_gradients(self, trainer) -> None:
+        params = [p for p in trainer.params]
+        for p in params:
+            if p.grad is None:
+                p.grad = torch.zeros_like(p)
+        m = self.mesh
+        if m.pp_size > 1 and getattr(self.model, "pipeline_tied", False) and (m.is_first_stage or m.is_last_stage):
+            dist.all_reduce(self.model.transformer.wte.weight.grad, group=self._group("embed"))
+        if m.dp_size > 1:
+            dp = self._group("dp")
+            for bucket in _buckets(params, 256 << 20, lambda p: p.grad):
+                grads = [p.grad for p in bucket]
+                flat = torch.cat([g.reshape(-1) for g in grads]) if len(grads) > 1 else grads[0].reshape(-1)
+                flat.div_(m.dp_size)
+                dist.all_reduce(flat, group=dp)
+                if len(grads) > 1:
+                    off = 0
+                    for g in grads:
+                        g.copy_(flat[off:off + g.numel()].view_as(g))
+                        off += g.numel()
+
+    def _counts_in_norm(self, p: torch.nn.Parameter) -> bool:
+        m = self.mesh
+        if m.tp_size > 1 and not getattr(p, "_tp_sharded", False) and m.tp_rank != 0:
+            return False
+        if m.pp_size > 1 and not m.is_first_stage and self.model is not None and \
+                self.model.transformer.wte is not None and p is getattr(self.model.transformer.wte, "weight", None):
+            return False
+        return True
+
+    @torch.no_grad()
+    def clip_grad_norm(self, params, max_norm: float, optimizer=None) -> torch.Tensor:
+        counted = [p.grad for p in params if p.grad is not None and self._counts_in_norm(p)]
+        dev = next(iter(params)).device
+        sq = torch.zeros((), device=dev, dtype=torch.float32)
+        if counted:
+            norms = torch._foreach_norm([g.float() for g in counted])
+            sq = torch.stack(norms).pow(2).sum()
+        for name in ("tp", "pp"):
+            g = self._group(name)
+            if g is not None and dist.get_world_size(g) > 1:
+                dist.all_reduce(sq, group=g)
+        norm = sq.sqrt()
+        if max_norm > 0:
+            if optimizer is not None and hasattr(optimizer, "arm_clip"):
+                optimizer.arm_clip(norm, max_norm)
+            else:
+                coef = (max_norm / (norm + 1e-6)).clamp(max=1.0)
+                coef = torch.where(torch.isfinite(norm), coef, torch.zeros_like(coef))
+                torch._foreach_mul_([p.grad for p in params if p.grad is not None], coef)
+        return norm
+
+    # ------------------------------------------------------------ checkpoints
+    def layout(self) -> Dict[str, Any]:
+        return {"strategy": self.name, "world_size": rt.world_size(), **self.mesh.describe()}
+
+    def sharded_checkpoint_state(self, trainer) -> Dict[str, Any]:
+        from rl_project_b200.training.common.trainer import _cpu_state
+
+        mine = _cpu_state(trainer._master_state(trainer.alg.state()))
+        opt = trainer.optimizer.state_dict()
+        world = rt.world_size()
+        models: List[Any] = [None] * world
+        opts: List[Any] = [None] * world
+        dist.all_gather_object(models, mine)
+        dist.all_gather_object(opts, opt)
+        return {"model": models, "optimizer": opts, "layout": self.layout()}
+
+    def load_sharded_checkpoint_state(self, trainer, shards: Dict[str, Any]) -> None:
+        layout = shards["layout"]
+        for k in ("world_size", "tp", "pp"):
+            if int(layout.get(k, -1)) != int(self.layout()[k]):
+                raise DistributedConfigError(f"checkpoint layout {layout} does not match this run's {self.layout()}")
+        r = rt.rank()
+        trainer.alg.load_state(shards["model"][r])
+        if shards["optimizer"][r]:
+            trainer.optimizer.load_state_dict(shards["optimizer"][r])

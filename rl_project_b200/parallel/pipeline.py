@@ -1,0 +1,143 @@
+"""Pipeline parallelism: contiguous block stages and a 1F1B schedule with a real backward.
+
+``partition_model`` keeps on each stage only its contiguous slice of blocks
+(the others become empty placeholders, so parameter names stay global and
+checkpoints of all stages tile the full model); the first stage keeps the
+embedding, the last the final norm and LM head (and, with tied embeddings, a
+copy of the embedding whose gradient is summed with the first stage's).
+
+``run_1f1b`` drives ``n_micro`` micro-batches through the pipeline: stage s
+runs ``min(P - s - 1, n_micro)`` warm-up forwards, then alternates one forward
+/ one backward, then drains the remaining backwards.  Activations go forward
+and activation gradients go backward as point-to-point messages (non-blocking
+sends, blocking receives, tagged by micro-batch), so every stage's parameters
+receive gradients -- unlike ``src/forgeline/distributed/pipeline_parallel.py``,
+whose scheduler ran the backward on the last stage only.  Messages use the
+compute dtype (bf16 on GPU).
+"""
+
+from __future__ import annotations
+
+from typing import Any, Callable, Dict, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from rl_project_b200.core.errors import DistributedConfigError
+
+
+class _Placeholder(nn.Module):
+    """Stands in for a block owned by another stage."""
+
+
+def stage_bounds(n_layer: int, n_stages: int, stage: int) -> Tuple[int, int]:
+    """Blocks ``[lo, hi)`` of ``stage``: near-equal contiguous slices, earlier stages take the remainder."""
+    if n_stages > n_layer:
+        raise DistributedConfigError(f"pipeline_parallel {n_stages} exceeds the {n_layer} layers")
+    q, r = divmod(n_layer, n_stages)
+    lo = stage * q + min(stage, r)
+    return lo, lo + q + (1 if stage < r else 0)
+
+
+def partition_model(model: nn.Module, stage: int, n_stages: int) -> nn.Module:
+    """Drop the modules this stage does not own (in place)."""
+    if n_stages == 1:
+        return model
+    L = len(model.transformer.h)
+    lo, hi = stage_bounds(L, n_stages, stage)
+    for i in range(L):
+        if not lo <= i < hi:
+            model.transformer.h[i] = _Placeholder()
+    first, last = stage == 0, stage == n_stages - 1
+    tied = model.lm_head.weight is model.transformer.wte.weight
+    if not last:
+        model.lm_head = None
+        model.transformer.ln_f = _Placeholder()
+        model.mtp_modules = None
+    if not first and not (last and tied):
+        model.transformer.wte = _Placeholder()
+    if not first and getattr(model, "wpe", None) is not None:
+        model.wpe = None
+    model.pipeline_stage = (stage, n_stages, lo, hi)
+    model.pipeline_tied = tied  # first and last stage then sum the embedding gradient
+    return model
+
+
+def stage_forward(model: nn.Module, x: torch.Tensor, first: bool) -> torch.Tensor:
+    """Embedding (first stage) then this stage's blocks."""
+    if first:
+        x = model._embed(x)
+    for blk in model.transformer.h:
+        if not isinstance(blk, _Placeholder):
+            x, _ = blk(x)
+    return x
+
+
+def stage_loss(model: nn.Module, h: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+    from rl_project_b200.ops.logprob import linear_cross_entropy
+
+    h = model.transformer.ln_f(h)
+    return linear_cross_entropy(h.reshape(-1, h.shape[-1]), model.head_weight(), targets.reshape(-1))
+
+
+def schedule_1f1b(n_micro: int, stage: int, n_stages: int) -> List[Tuple[str, int]]:
+    """The ordered ("F" | "B", micro-batch) steps of one stage."""
+    warm = min(n_stages - stage - 1, n_micro)
+    steps = [("F", i) for i in range(warm)]
+    for i in range(n_micro - warm):
+        steps += [("F", warm + i), ("B", i)]
+    steps += [("B", i) for i in range(n_micro - warm, n_micro)]
+    return steps
+
+
+class PipelineRunner:
+    """Runs the 1F1B schedule of one stage for one optimiser step."""
+
+    def __init__(self, model: nn.Module, stage: int, n_stages: int, prev_rank: Optional[int],
+                 next_rank: Optional[int], group: Any = None):
+        self.model, self.stage, self.n_stages = model, stage, n_stages
+        self.prev, self.next, self.group = prev_rank, next_rank, group
+        self.first, self.last = stage == 0, stage == n_stages - 1
+
+    def _recv(self, shape, dtype, device, src: int, tag: int) -> torch.Tensor:
+        t = torch.empty(shape, dtype=dtype, device=device)
+        dist.recv(t, src=src, tag=tag)
+        return t
+
+    def run(self, micro_inputs: Sequence[Tuple[torch.Tensor, torch.Tensor]], act_shape: Tuple[int, ...],
+            dtype: torch.dtype, device: torch.device, scale: float) -> torch.Tensor:
+        """``micro_inputs[i] = (idx, targets)``; returns the summed scaled loss (last stage) or 0."""
+        n = len(micro_inputs)
+        inputs: Dict[int, torch.Tensor] = {}
+        outputs: Dict[int, torch.Tensor] = {}
+        sends: List[Any] = []
+        total = torch.zeros((), device=device, dtype=torch.float32)
+        for kind, i in schedule_1f1b(n, self.stage, self.n_stages):
+            if kind == "F":
+                if self.first:
+                    x_in = micro_inputs[i][0]
+                else:
+                    x_in = self._recv(act_shape, dtype, device, self.prev, tag=2 * i).requires_grad_(True)
+                out = stage_forward(self.model, x_in, self.first)
+                if self.last:
+                    loss = stage_loss(self.model, out, micro_inputs[i][1]) * scale
+                    total += loss.detach().float()
+                    outputs[i] = loss
+                else:
+                    sends.append(dist.isend(out.detach().contiguous(), dst=self.next, tag=2 * i))
+                    outputs[i] = out
+                inputs[i] = x_in
+            else:
+                out = outputs.pop(i)
+                if self.last:
+                    out.backward()
+                else:
+                    grad = self._recv(out.shape, out.dtype, device, self.next, tag=2 * i + 1)
+                    out.backward(grad)
+                x_in = inputs.pop(i)
+                if not self.first:
+                    sends.append(dist.isend(x_in.grad.contiguous(), dst=self.prev, tag=2 * i + 1))
+        for s in sends:
+            s.wait()
+        return total

@@ -127,6 +127,17 @@ def _as_tensor(v: Any, device: torch.device) -> torch.Tensor:
     return torch.tensor(float(v), device=device)
 
 
+def _cpu_state(obj: Any) -> Any:
+    """Detached CPU copies of every tensor in a nested state."""
+    if isinstance(obj, torch.Tensor):
+        return obj.detach().cpu().clone()
+    if isinstance(obj, dict):
+        return {k: _cpu_state(v) for k, v in obj.items()}
+    if isinstance(obj, (list, tuple)):
+        return type(obj)(_cpu_state(v) for v in obj)
+    return obj
+
+
 class Trainer:
     def __init__(self, ctx: RunContext, algorithm: PostTrainingAlgorithm, config: Optional[TrainerConfig] = None,
                  checkpoint_manager: Optional[CheckpointManager] = None, strategy: Any = None):
@@ -147,8 +158,9 @@ class Trainer:
                     fn()
         name = getattr(strategy, "name", "") if strategy is not None else ""
         world = strategy.world_size() if strategy is not None else 1
-        self._sharded = name in ("fsdp", "zero2") and world > 1
-        self._sync_grads = name in ("ddp", "hybrid") and world > 1
+        self._sharded = name in ("fsdp", "zero2", "tensor_parallel", "pipeline_parallel", "hybrid",
+                                 "expert_parallel") and world > 1
+        self._sync_grads = name == "ddp" and world > 1
         if strategy is not None and hasattr(strategy, "prepare_training"):
             strategy.prepare_training(self)
         self.params = [p for p in algorithm.parameters() if p.requires_grad]
@@ -210,7 +222,15 @@ class Trainer:
         dev = self.ctx.device
         losses: List[torch.Tensor] = []
         metric_vals: Dict[str, List[torch.Tensor]] = {}
-        for micro in range(n_micro):
+        scheduled = None
+        if self.strategy is not None and hasattr(self.strategy, "run_micro_batches"):
+            with self.precision.autocast():
+                scheduled = self.strategy.run_micro_batches(self, batch, n_micro)  # e.g. a pipeline schedule
+        if scheduled is not None:
+            losses = [t.detach().float() for t in scheduled[0]]
+            for k, v in scheduled[1].items():
+                metric_vals.setdefault(k, []).append(_as_tensor(v, dev))
+        for micro in range(n_micro if scheduled is None else 0):
             if self.strategy is not None and hasattr(self.strategy, "micro_step_context"):
                 cm = self.strategy.micro_step_context(micro, n_micro)
             else:
@@ -234,7 +254,12 @@ class Trainer:
         max_norm = self.cfg.optimizer.grad_clip
         norm_t: Optional[torch.Tensor] = None
         fused = hasattr(self.optimizer, "clip_grad_norm")
-        if fused:
+        if getattr(self.strategy, "owns_grad_clip", False):
+            # norm over model-parallel shards, each parameter counted once
+            self.precision.unscale(self.optimizer)
+            norm_t = self.strategy.clip_grad_norm(self.params, max_norm, self.optimizer)
+            fused = True
+        elif fused:
             norm_t = self.optimizer.clip_grad_norm(max_norm if max_norm > 0 else 0.0)
         elif max_norm > 0:
             self.precision.unscale(self.optimizer)

@@ -141,9 +141,10 @@ def _tasks(manifest: ExperimentManifest) -> List[VerifiableTask]:
 
 
 def _rank() -> int:
-    import torch.distributed as dist
+    """Data rank: the data-parallel rank under a TP / PP mesh (all ranks of a replica see the same data)."""
+    from rl_project_b200.parallel.mesh_strategies import data_parallel_rank
 
-    return dist.get_rank() if dist.is_available() and dist.is_initialized() else 0
+    return data_parallel_rank()
 
 
 def build_algorithm(manifest: ExperimentManifest, ctx: RunContext) -> PostTrainingAlgorithm:

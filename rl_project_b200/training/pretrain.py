@@ -59,6 +59,14 @@ class PretrainAlgorithm(PostTrainingAlgorithm):
         self.tokens_seen += int(x.numel())
         return loss, {"tokens_seen": float(self.tokens_seen)}
 
+    def pipeline_inputs(self, batch, micro_step: int, n_micro: int):
+        """``(input ids, targets)`` of one micro-batch, for pipeline-parallel schedules."""
+        x, y = batch
+        if n_micro > 1:
+            x, y = x[micro_step::n_micro], y[micro_step::n_micro]
+        self.tokens_seen += int(x.numel())
+        return x, y
+
     def on_step_end(self, step: int, result) -> None:
         self.ema_loss = result.loss if self.ema_loss is None else 0.95 * self.ema_loss + 0.05 * result.loss
         result.metrics["ema_loss"] = self.ema_loss

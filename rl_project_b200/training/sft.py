@@ -82,6 +82,12 @@ class SFTAlgorithm(PostTrainingAlgorithm):
         loss = self._ce(batch)
         return loss, {"response_tokens": (batch.targets != IGNORE_INDEX).sum()}
 
+    def pipeline_inputs(self, batch: SupervisedBatch, micro_step: int, n_micro: int):
+        """``(input ids, targets)`` of one micro-batch, for pipeline-parallel schedules."""
+        if n_micro > 1:
+            batch = batch.micro(micro_step, n_micro)
+        return batch.input_ids, batch.targets
+
     @torch.no_grad()
     def evaluate(self, step: int) -> Dict[str, float]:
         ds = self.eval_dataset or self.dataset
