@@ -39,6 +39,7 @@ class ExpertGate(nn.Module):
             self.register_buffer("expert_bias", torch.zeros(spec.n_experts, dtype=torch.float32))
         self._aux_loss: Optional[torch.Tensor] = None
         self.last_counts: Optional[torch.Tensor] = None
+        self.count_group = None  # data-parallel group: bias updates then use global counts (identical on all ranks)
 
     @property
     def aux_loss(self) -> Optional[torch.Tensor]:
@@ -69,6 +70,9 @@ class ExpertGate(nn.Module):
         self.last_counts = counts
         if self.training and self.aux_loss_free:
             with torch.no_grad():
+                if self.count_group is not None:
+                    counts = counts.clone()
+                    torch.distributed.all_reduce(counts, group=self.count_group)
                 self.expert_bias += self.bias_update_speed * (counts.mean() - counts)
             self._aux_loss = x.new_zeros((), dtype=torch.float32)
         elif self.training:

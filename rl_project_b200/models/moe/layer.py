@@ -43,6 +43,7 @@ class MoELayer(nn.Module):
         self.shared_experts = (make_ffn(spec, hidden * max(1, spec.n_shared_experts) if spec.moe_d_ff else None)
                                if spec.n_shared_experts > 0 else None)
         self.expert_group = None  # set by the expert-parallel strategy
+        self.local_experts = list(range(spec.n_experts))
 
     @property
     def aux_loss(self):
