@@ -9,6 +9,7 @@ multi-GPU number in this framework is reported.
 from __future__ import annotations
 
 import time
+from collections import deque
 from contextlib import contextmanager
 from dataclasses import dataclass, field
 from typing import Dict, Iterator, List, Optional
@@ -30,8 +31,13 @@ class Span:
 
 
 class Tracer:
-    def __init__(self) -> None:
-        self.spans: List[Span] = []
+    """Named spans.  The most recent ``keep`` spans are kept for inspection; the per-name
+    aggregates (count / total / max) cover every span ever recorded, so a long-running
+    server's memory stays bounded."""
+
+    def __init__(self, keep: int = 10_000) -> None:
+        self.spans: "deque[Span]" = deque(maxlen=keep)
+        self._agg: Dict[str, Dict[str, float]] = {}
 
     @contextmanager
     def span(self, name: str, **attributes: object) -> Iterator[Span]:
@@ -41,21 +47,20 @@ class Tracer:
         finally:
             s.end = time.time()
             self.spans.append(s)
+            row = self._agg.setdefault(name, {"count": 0.0, "total_ms": 0.0, "max_ms": 0.0})
+            d = s.duration_ms
+            row["count"] += 1
+            row["total_ms"] += d
+            row["max_ms"] = max(row["max_ms"], d)
 
     def durations(self, name: str) -> List[float]:
         return [s.duration_ms for s in self.spans if s.name == name and s.end is not None]
 
     def summary(self) -> Dict[str, Dict[str, float]]:
-        agg: Dict[str, Dict[str, float]] = {}
-        for s in self.spans:
-            row = agg.setdefault(s.name, {"count": 0.0, "total_ms": 0.0, "max_ms": 0.0})
-            d = s.duration_ms
-            row["count"] += 1
-            row["total_ms"] += d
-            row["max_ms"] = max(row["max_ms"], d)
-        for row in agg.values():
+        out = {k: dict(v) for k, v in self._agg.items()}
+        for row in out.values():
             row["mean_ms"] = row["total_ms"] / max(1.0, row["count"])
-        return agg
+        return out
 
 
 _TRACER = Tracer()

@@ -257,7 +257,7 @@ def build_algorithm(manifest: ExperimentManifest, ctx: RunContext) -> PostTraini
 
             rows, _ = _trajectory_split(manifest)
             tasks = [dict(t, prompt=build_synthesis_prompt(t)) for t in rows]
-        elif manifest.data.kind == "verifiable":
+        elif manifest.data.kind == "verifiable" and str(manifest.data.path) != "synthetic:random_prompts":
             tasks = [t.to_dict() for t in _tasks(manifest)]
         if str(manifest.data.path) == "synthetic:random_prompts":
             from rl_project_b200.data.synthetic import random_prompts
