@@ -347,6 +347,24 @@ void paged_write(const at::Tensor& k_new, const at::Tensor& v_new, at::Tensor& k
            "paged_write");
 }
 
+// ---------------------------------------------------------------- sampler
+std::vector<at::Tensor> sample(const at::Tensor& logits, const at::Tensor& temperature, int64_t seed) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(-1) == 1, "logits must be [rows, V] with unit inner stride");
+  TORCH_CHECK(logits.scalar_type() == at::kBFloat16 || logits.scalar_type() == at::kFloat, "bf16 or fp32 logits");
+  TORCH_CHECK(temperature.scalar_type() == at::kFloat && temperature.numel() == logits.size(0),
+              "one fp32 temperature per row");
+  TORCH_CHECK(temperature.device() == logits.device(), "temperature must be on the logits' device");
+  const c10::cuda::CUDAGuard g(logits.device());
+  auto tokens = at::empty({logits.size(0)}, logits.options().dtype(at::kLong));
+  auto lp = at::empty({logits.size(0)}, logits.options().dtype(at::kFloat));
+  auto temp = temperature.contiguous();
+  CHECK_OK(rlb_sample(logits.data_ptr(), logits.scalar_type() == at::kBFloat16, logits.stride(0),
+                      (int)logits.size(0), (int)logits.size(1), temp.data_ptr<float>(),
+                      (unsigned long long)seed, lptr(tokens), lp.data_ptr<float>(), cur_stream()),
+           "sample");
+  return {tokens, lp};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -372,4 +390,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm);
   m.def("paged_decode", &paged_decode);
   m.def("paged_write", &paged_write);
+  m.def("sample", &sample);
 }

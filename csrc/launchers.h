@@ -58,6 +58,10 @@ cudaError_t rlb_paged_write(const void* k_new, const void* v_new, void* k_pool, 
                             const int* slot_off, int B, int Hkv, int D, int num_blocks, int* status, int sms,
                             cudaStream_t s);
 
+// Fused temperature sampler (Gumbel-max) with the sampled token's log-probability.
+cudaError_t rlb_sample(const void* logits, int is_bf16, long long ld, int rows, int V, const float* temperature,
+                       unsigned long long seed, long long* tokens, float* logprobs, cudaStream_t s);
+
 // RMSNorm backward that allocates nothing (no counterpart in the reference):
 // the dw partial sums live in a fixed 4 MiB file-scope __device__ array per
 // device instead of a caller-allocated buffer.  Returns a cudaError_t value;

@@ -6,8 +6,8 @@
 // per sequence.  One CTA handles (kv head h, sequence b, split s): it loads each
 // K/V row ONCE and scores it against all G = Hq/Hkv query heads that share the
 // KV head (GQA packing), with an online softmax per query head.  4 warps take
-// tokens round-robin; their partial (max, sum, acc) are merged in shared
-// memory.  With several splits per sequence (long contexts, few sequences)
+// whole 16-token blocks round-robin; their partial (max, sum, acc) are merged
+// in shared memory.  With several splits per sequence (long contexts, few sequences)
 // each split writes unnormalised partials and a second kernel merges them
 // (flash-decoding).  Optional sliding window (last `window` positions) and
 // tanh soft-cap, as in src/forgeline/models/attention/causal.py:106-130.
@@ -20,6 +20,15 @@ namespace rlb {
 constexpr int kBlock = 16;
 constexpr int kWarps = 4;
 
+// Lane layout: a K/V row of D bf16 is D/8 16-byte vectors, so LPT = D/8 lanes
+// cover one token row and a warp covers TPP = 32/LPT tokens per pass; a
+// 16-token block takes PASSES = 16/TPP passes.  Lane (tok_in_pass, slice)
+// holds dims [8 slice, 8 slice + 8) of its tokens.  Scores reduce over the LPT
+// lanes of a token (log2 LPT shuffles); the softmax statistics (max, sum) are
+// kept per lane over that lane's own tokens and merged once at the end, as are
+// the P.V partial sums -- the only per-block cross-lane traffic is the score
+// reduction.  Each warp takes whole blocks round-robin, so every load is a
+// 16-byte vector and a warp has 2 x PASSES of them in flight per block.
 template <int D, int G>
 __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_pool,
@@ -27,73 +36,109 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(
     __nv_bfloat16* __restrict__ out, float* __restrict__ part_acc, float* __restrict__ part_ml, int Hkv,
     int max_blocks, int num_blocks, int split_tokens, int n_splits, float scale, float softcap, int window,
     int* status) {
-  constexpr int EPL = D / 32;  // elements per lane
+  constexpr int LPT = D / 8;          // lanes per token row
+  constexpr int TPP = 32 / LPT;       // tokens per pass
+  constexpr int PASSES = kBlock / TPP;
   const int h = blockIdx.x, b = blockIdx.y, sp = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slice = lane % LPT, tip = lane / LPT;
   const int Hq = Hkv * G;
   const int len = ctx_lens[b];
-  int t_begin = (window > 0 && len > window) ? len - window : 0;
+  const int t_begin = (window > 0 && len > window) ? len - window : 0;
   const int t0 = t_begin + sp * split_tokens;
   const int t1 = min(len, t0 + split_tokens);
 
-  float qf[G][EPL];
+  float qf[G][8];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    const __nv_bfloat16* qp = q + ((long long)b * Hq + h * G + g) * D + lane * EPL;
+    unpack8(ldg8(q + ((long long)b * Hq + h * G + g) * D + slice * 8), qf[g]);
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) qf[g][e] = __bfloat162float(qp[e]) * scale;
+    for (int e = 0; e < 8; ++e) qf[g][e] *= scale;
   }
-  float m[G], l[G], acc[G][EPL];
+  float m[G], l[G], acc[G][8];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     m[g] = -INFINITY;
     l[g] = 0.f;
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) acc[g][e] = 0.f;
+    for (int e = 0; e < 8; ++e) acc[g][e] = 0.f;
   }
   const int* bt = block_tables + (long long)b * max_blocks;
-  for (int t = t0 + warp; t < t1; t += kWarps) {
-    const int blk = bt[t / kBlock];
-    if (blk < 0 || blk >= num_blocks) {
-      if (lane == 0) report(status, kBadIndex);
-      continue;
+  if (t1 > t0) {
+    const int jb0 = t0 / kBlock, jb1 = (t1 - 1) / kBlock;
+    for (int jb = jb0 + warp; jb <= jb1; jb += kWarps) {
+      const int blk = bt[jb];
+      if (blk < 0 || blk >= num_blocks) {
+        if (lane == 0) report(status, kBadIndex);
+        continue;
+      }
+      const long long base = (((long long)blk * Hkv + h) * kBlock) * D + slice * 8;
+      bf16x8 kv[PASSES], vv[PASSES];
+#pragma unroll
+      for (int p = 0; p < PASSES; ++p) {  // all loads of the block issued before any use
+        const long long off = base + (long long)(p * TPP + tip) * D;
+        kv[p] = ldg8(k_pool + off);
+        vv[p] = ldg8(v_pool + off);
+      }
+#pragma unroll
+      for (int p = 0; p < PASSES; ++p) {
+        const int t = jb * kBlock + p * TPP + tip;
+        const bool valid = t >= t0 && t < t1;
+        float kf[8], vf[8];
+        unpack8(kv[p], kf);
+        unpack8(vv[p], vf);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float s = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) s += qf[g][e] * kf[e];
+#pragma unroll
+          for (int o = 1; o < LPT; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+          if (softcap > 0.f) s = tanhf(s / softcap) * softcap;
+          if (!valid) continue;
+          const float mn = fmaxf(m[g], s);
+          const float corr = __expf(m[g] - mn);
+          const float pr = __expf(s - mn);
+          l[g] = l[g] * corr + pr;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[g][e] = acc[g][e] * corr + pr * vf[e];
+          m[g] = mn;
+        }
+      }
     }
-    const long long row = (((long long)blk * Hkv + h) * kBlock + (t % kBlock)) * D + lane * EPL;
-    float kf[EPL], vf[EPL];
+  }
+  // merge the TPP token lanes of each slice inside the warp, then the warps in shared memory
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-      kf[e] = __bfloat162float(k_pool[row + e]);
-      vf[e] = __bfloat162float(v_pool[row + e]);
-    }
+  for (int g = 0; g < G; ++g) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float s = 0.f;
+    for (int o = LPT; o < 32; o <<= 1) {
+      const float mo = __shfl_xor_sync(0xffffffffu, m[g], o);
+      const float lo = __shfl_xor_sync(0xffffffffu, l[g], o);
+      const float mn = fmaxf(m[g], mo);
+      const float ca = mn == -INFINITY ? 0.f : __expf(m[g] - mn);
+      const float cb = mn == -INFINITY ? 0.f : __expf(mo - mn);
+      l[g] = l[g] * ca + lo * cb;
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) s += qf[g][e] * kf[e];
-      s = warp_sum(s);
-      if (softcap > 0.f) s = tanhf(s / softcap) * softcap;
-      const float mn = fmaxf(m[g], s);
-      const float corr = __expf(m[g] - mn);
-      const float p = __expf(s - mn);
-      l[g] = l[g] * corr + p;
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) acc[g][e] = acc[g][e] * corr + p * vf[e];
+      for (int e = 0; e < 8; ++e) {
+        const float ao = __shfl_xor_sync(0xffffffffu, acc[g][e], o);
+        acc[g][e] = acc[g][e] * ca + ao * cb;
+      }
       m[g] = mn;
     }
   }
-  // merge the warps
   __shared__ float sm_m[kWarps][G], sm_l[kWarps][G];
   __shared__ float sm_acc[kWarps][G][D];
-  if (lane == 0)
+  if (tip == 0) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      sm_m[warp][g] = m[g];
-      sm_l[warp][g] = l[g];
+      if (slice == 0) {
+        sm_m[warp][g] = m[g];
+        sm_l[warp][g] = l[g];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sm_acc[warp][g][slice * 8 + e] = acc[g][e];
     }
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) sm_acc[warp][g][lane * EPL + e] = acc[g][e];
+  }
   __syncthreads();
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
     const int g = i / D, d = i % D;

@@ -30,6 +30,7 @@ import time
 from collections import defaultdict
 from typing import Any, Dict, List, Optional, Tuple
 
+import numpy as np
 import torch
 
 from rl_project_b200.core.errors import ServingError
@@ -39,6 +40,7 @@ from rl_project_b200.inference.scheduler import Scheduler
 from rl_project_b200.models.generation.sampling import apply_sampling_filters, sample_from_logits
 from rl_project_b200.observability.logging import get_logger
 from rl_project_b200.observability.tracing import Tracer
+from rl_project_b200.ops.paged_attention import paged_write
 
 log = get_logger("forgeline.inference")
 
@@ -57,7 +59,7 @@ class _Seq:
 class InferenceEngine:
     def __init__(self, model: Any, *, max_batch: int = 8, max_seq_len: Optional[int] = None, block_size: int = 16,
                  max_blocks: Optional[int] = None, device: Optional[torch.device] = None,
-                 eos_token_id: Optional[int] = None, share_prefixes: bool = True):
+                 eos_token_id: Optional[int] = None, share_prefixes: bool = True, profile: bool = False):
         self.model = model.eval()
         self.device = device or next(model.parameters()).device
         self.max_seq_len = min(max_seq_len or model.spec.block_size, model.spec.block_size)
@@ -85,6 +87,10 @@ class InferenceEngine:
         self.shared_prefills = 0
         self.decode_steps = 0
         self._pinned: Optional[torch.Tensor] = None
+        self.profile = profile and self.device.type == "cuda"
+        self._prof: Dict[str, float] = {}
+        self._base_seed = int(torch.initial_seed())
+        self._sample_calls = 0
         self._thread: Optional[threading.Thread] = None
         self._stop = threading.Event()
         self._lock = threading.Lock()
@@ -120,8 +126,11 @@ class InferenceEngine:
             return produced
 
     # ------------------------------------------------------------ prefill
+    PREFILL_BUCKET = 64  # prompts are right-padded to a multiple of this and prefilled together
+    PREFILL_TOKENS = 1 << 16  # tokens per prefill forward
+
     def _prefill(self, reqs: List[GenerationRequest]) -> int:
-        fresh: Dict[int, List[_Seq]] = defaultdict(list)
+        fresh: List[_Seq] = []
         shared: List[Tuple[_Seq, _Seq]] = []
         for req in reqs:
             st = _Seq(req)
@@ -134,21 +143,21 @@ class InferenceEngine:
             else:
                 if self.share_prefixes:
                     self._prefix_owner[key] = req.id
-                fresh[len(req.prompt_tokens)].append(st)
-        produced = 0
-        for T, group in fresh.items():
+                fresh.append(st)
+        for group in self._prefill_batches(fresh):
+            n_tok = sum(len(st.req.prompt_tokens) for st in group)
             try:
-                with self.tracer.span("prefill", tokens=T * len(group), batch=len(group)):
-                    self._prefill_group(group, T)
-                self.prefill_tokens += T * len(group)
+                with self.tracer.span("prefill", tokens=n_tok, batch=len(group)):
+                    self._prefill_group(group)
+                self.prefill_tokens += n_tok
             except Exception as exc:  # noqa: BLE001
                 for st in group:
                     self._fail(st, exc)
         for st, owner in shared:
-            if owner.req.id not in self.states or self.states[owner.req.id] is not owner:
-                # the prompt's owner retired in this step before its copy was taken: prefill normally
+            if self.states.get(owner.req.id) is not owner or owner.req.id not in self._prompt_logits:
+                # the prompt's owner failed in this step before its prefix could be shared: prefill normally
                 try:
-                    self._prefill_group([st], len(st.req.prompt_tokens))
+                    self._prefill_group([st])
                 except Exception as exc:  # noqa: BLE001
                     self._fail(st, exc)
                 continue
@@ -157,75 +166,142 @@ class InferenceEngine:
             st.last_logits = self._prompt_logits[owner.req.id]
             self.shared_prefills += 1
         # first token of every newly admitted sequence, from its prompt logits
-        new = [st for st in (s for g in fresh.values() for s in g) if st.req.id in self.states]
+        new = [st for st in fresh if st.req.id in self.states and st.last_logits is not None]
         new += [st for st, _ in shared if st.req.id in self.states and st.last_logits is not None]
+        produced = 0
         if new:
             produced += self._sample_and_emit(new, torch.cat([st.last_logits for st in new], 0))
             for st in new:
                 st.last_logits = None
         return produced
 
-    def _prefill_group(self, group: List[_Seq], T: int) -> None:
-        ids = torch.tensor([st.req.prompt_tokens for st in group], dtype=torch.long).to(self.device,
-                                                                                         non_blocking=True)
-        logits, cache = self.model.prefill(ids)
+    def _prefill_batches(self, seqs: List[_Seq]) -> List[List[_Seq]]:
+        """Paged: prompts grouped by padded length (a multiple of PREFILL_BUCKET), at most PREFILL_TOKENS
+        per forward.  Contiguous caches: grouped by exact length (no padding may enter the cache)."""
+        q = self.PREFILL_BUCKET
+        buckets: Dict[int, List[_Seq]] = defaultdict(list)
+        for st in seqs:
+            n = len(st.req.prompt_tokens)
+            buckets[min(-(-n // q) * q, self.max_seq_len) if self.paged else n].append(st)
+        out: List[List[_Seq]] = []
+        for L, group in sorted(buckets.items()):
+            per = max(1, self.PREFILL_TOKENS // max(L, 1))
+            out.extend(group[i:i + per] for i in range(0, len(group), per))
+        return out
+
+    def _prefill_group(self, group: List[_Seq]) -> None:
+        lens = [len(st.req.prompt_tokens) for st in group]
+        L = max(lens)
+        if self.paged:
+            L = min(-(-L // self.PREFILL_BUCKET) * self.PREFILL_BUCKET, self.max_seq_len)
+        rows = torch.zeros(len(group), L, dtype=torch.long)
+        for i, st in enumerate(group):
+            rows[i, :lens[i]] = torch.as_tensor(st.req.prompt_tokens, dtype=torch.long)
+        ids = rows.to(self.device, non_blocking=True)
+        last = torch.as_tensor([n - 1 for n in lens], dtype=torch.long)
+        logits, cache = self.model.prefill(ids, last_positions=last)
         logits = logits.float()
         for i, st in enumerate(group):
-            st.position = T
+            st.position = lens[i]
             st.last_logits = logits[i:i + 1]
             self._prompt_logits[st.req.id] = st.last_logits
-            if self.paged:
-                table = self.allocator.tables[st.req.id]
-                for layer, (k, v) in enumerate(cache):
-                    self.kv.write_prefix(layer, k[i], v[i], table)
-            else:
+            if not self.paged:
                 st.cache = [tuple(t[i:i + 1] for t in c) if isinstance(c, tuple) else c[i:i + 1] for c in cache]
+        if not self.paged:
+            return
+        # one gather and one slot write per layer for every prompt token of the batch
+        bs = self.allocator.block_size
+        flat, blocks, offs = [], [], []
+        for i, st in enumerate(group):
+            pos = torch.arange(lens[i])
+            flat.append(pos + i * L)
+            blocks.append(torch.as_tensor(self.allocator.tables[st.req.id], dtype=torch.int64)[pos // bs])
+            offs.append(pos % bs)
+        packed = torch.cat([torch.cat(flat), torch.cat(blocks), torch.cat(offs)]).to(self.device, non_blocking=True)
+        n_tok = packed.numel() // 3
+        flat_d = packed[:n_tok]
+        blk_d, off_d = packed[n_tok:2 * n_tok].to(torch.int32), packed[2 * n_tok:].to(torch.int32)
+        for layer, (k, v) in enumerate(cache):
+            B, H, _, D = k.shape
+            kk = k.transpose(1, 2).reshape(B * L, H, D).index_select(0, flat_d)
+            vv = v.transpose(1, 2).reshape(B * L, H, D).index_select(0, flat_d)
+            kl, vl = self.kv.layer(layer)
+            paged_write(kk, vv, kl, vl, blk_d, off_d)
+
+    # ------------------------------------------------------------ profiling (CUDA events per decode step)
+    @staticmethod
+    def _event():
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    def reset_profile(self) -> None:
+        self._prof = {}
+
+    def profile_summary(self) -> Dict[str, float]:
+        n = max(1.0, self._prof.get("steps", 0.0))
+        out = {k: v / n for k, v in self._prof.items() if k != "steps"}
+        out["steps"] = self._prof.get("steps", 0.0)
+        return out
+
+    def _account(self, evs: List[Any], t_host0: float) -> None:
+        torch.cuda.synchronize(self.device)
+        p = self._prof
+        p["forward_ms"] = p.get("forward_ms", 0.0) + evs[0].elapsed_time(evs[1])
+        p["sampling_ms"] = p.get("sampling_ms", 0.0) + evs[2].elapsed_time(evs[3])
+        p["step_wall_ms"] = p.get("step_wall_ms", 0.0) + (time.perf_counter() - t_host0) * 1e3
+        p["steps"] = p.get("steps", 0.0) + 1
 
     # ------------------------------------------------------------ decode
     def _decode(self, seqs: List[_Seq]) -> int:
+        t_host0 = time.perf_counter()
         B = len(seqs)
         bs = self.allocator.block_size
-        width = max(len(self.allocator.tables[s.req.id]) for s in seqs)
+        tables = [self.allocator.tables[s.req.id] for s in seqs]
+        width = max(len(t) for t in tables)
         n = 5 * B + B * width
         if self._pinned is None or self._pinned.numel() < n:
             self._pinned = torch.empty(max(n, 1024), dtype=torch.int32,
                                        pin_memory=self.device.type == "cuda")
         host = self._pinned[:n]
         hv = host.numpy()
-        hv[:] = 0
-        max_pos = 0
-        max_ctx = 0
-        for b, s in enumerate(seqs):
-            table = self.allocator.tables[s.req.id]
-            pos = s.position
-            hv[b] = s.tokens[-1]
-            hv[B + b] = pos
-            hv[2 * B + b] = pos + 1
-            hv[3 * B + b] = table[pos // bs]
-            hv[4 * B + b] = pos % bs
-            hv[5 * B + b * width: 5 * B + b * width + len(table)] = table
-            max_pos = max(max_pos, pos)
-            max_ctx = max(max_ctx, pos + 1)
+        pos = np.fromiter((s.position for s in seqs), dtype=np.int64, count=B)
+        hv[:B] = np.fromiter((s.tokens[-1] for s in seqs), dtype=np.int64, count=B)
+        hv[B:2 * B] = pos
+        hv[2 * B:3 * B] = pos + 1
+        hv[4 * B:5 * B] = pos % bs
+        grid = hv[5 * B:].reshape(B, width)
+        grid[:] = 0
+        for b, t in enumerate(tables):
+            grid[b, :len(t)] = t
+        hv[3 * B:4 * B] = grid[np.arange(B), pos // bs]
+        max_pos = int(pos.max())
         dev = host.to(self.device, non_blocking=True)
         from rl_project_b200.models.attention.causal import PagedDecodeMeta
 
         meta = PagedDecodeMeta(positions=dev[B:2 * B].view(B, 1), max_pos=max_pos, ctx_lens=dev[2 * B:3 * B],
                                slot_block=dev[3 * B:4 * B], slot_off=dev[4 * B:5 * B],
                                block_tables=dev[5 * B:].view(B, width),
-                               split_tokens=self._split_tokens(B, max_ctx))
+                               split_tokens=self._split_tokens(B, max_pos + 1))
+        evs = [self._event()] if self.profile else None
         try:
             with self.tracer.span("decode", batch=B):
-                logits = self.model.decode_paged(dev[:B].long(), self.kv, meta).float()
+                logits = self.model.decode_paged(dev[:B].long(), self.kv, meta)
         except Exception as exc:  # noqa: BLE001
             if self.device.type == "cuda":
                 torch.cuda.current_stream(self.device).synchronize()  # the pinned buffer is reused next step
             for s in seqs:
                 self._fail(s, exc)
             return 0
+        if evs is not None:
+            evs.append(self._event())
         self.decode_steps += 1
         for s in seqs:
             s.position += 1
-        return self._sample_and_emit(seqs, logits)
+        produced = self._sample_and_emit(seqs, logits, evs)
+        if evs is not None:
+            self._account(evs, t_host0)
+        return produced
 
     def _split_tokens(self, B: int, max_ctx: int) -> int:
         """Split long contexts over several CTAs when the batch alone cannot fill the GPU."""
@@ -265,25 +341,48 @@ class InferenceEngine:
             for b, s in enumerate(group):
                 s.cache = [tuple(t[b:b + 1] for t in c) if isinstance(c, tuple) else c[b:b + 1] for c in new_cache]
                 s.position += 1
-            produced += self._sample_and_emit(group, logits.float())
+            produced += self._sample_and_emit(group, logits)
         return produced
 
     # ------------------------------------------------------------ sampling
-    def _sample_and_emit(self, seqs: List[_Seq], logits: torch.Tensor) -> int:
+    @staticmethod
+    def _plain(p: SamplingParams) -> bool:
+        """Temperature-only sampling: the fused sampler's domain."""
+        return (not p.top_k) and p.top_p in (None, 1.0) and not p.min_p and p.repetition_penalty == 1.0
+
+    def _sample_and_emit(self, seqs: List[_Seq], logits: torch.Tensor, evs: Optional[List[Any]] = None) -> int:
         B = len(seqs)
+        if evs is not None:
+            evs.append(self._event())
+        self._sample_calls += 1
+        seed = (self._base_seed * 1_000_003 + self._sample_calls) & ((1 << 62) - 1)
         out = torch.empty(B, dtype=torch.long, device=logits.device)
+        fused = [i for i, s in enumerate(seqs) if self._plain(s.req.params)] if logits.is_cuda else []
+        if fused:
+            from rl_project_b200.ops.sampling import sample_tokens
+
+            temps = torch.tensor([seqs[i].req.params.temperature for i in fused], dtype=torch.float32)
+            if len(fused) == B:
+                out, _ = sample_tokens(logits, temps.to(logits.device, non_blocking=True), seed)
+            else:
+                idx = torch.as_tensor(fused, device=logits.device)
+                tok, _ = sample_tokens(logits.index_select(0, idx), temps.to(logits.device), seed)
+                out.index_copy_(0, idx, tok)
+        fused_set = set(fused)
         groups: Dict[tuple, List[int]] = defaultdict(list)
         for i, s in enumerate(seqs):
+            if i in fused_set:
+                continue
             p = s.req.params
             if p.repetition_penalty != 1.0:
-                f = apply_sampling_filters(logits[i:i + 1], p.temperature, p.top_k, p.top_p, p.min_p,
+                f = apply_sampling_filters(logits[i:i + 1].float(), p.temperature, p.top_k, p.top_p, p.min_p,
                                            p.repetition_penalty, s.tokens)
                 out[i] = sample_from_logits(f, p.temperature).view(())
             else:
                 groups[p.filter_key()].append(i)
         for (temp, top_k, top_p, min_p), rows in groups.items():
             idx = torch.as_tensor(rows, device=logits.device)
-            sub = logits if len(rows) == B else logits.index_select(0, idx)
+            sub = (logits if len(rows) == B else logits.index_select(0, idx)).float()
             if temp <= 0:
                 tok = sub.argmax(-1)
             else:
@@ -292,6 +391,8 @@ class InferenceEngine:
                 out = tok
             else:
                 out.index_copy_(0, idx, tok)
+        if evs is not None:
+            evs.append(self._event())
         tokens = out.tolist()
         produced = 0
         for s, tok in zip(seqs, tokens):

@@ -198,14 +198,18 @@ class TransformerLM(nn.Module):
 
     # ------------------------------------------------------------ incremental decoding
     @torch.no_grad()
-    def prefill(self, idx: torch.Tensor) -> Tuple[torch.Tensor, List[Any]]:
+    def prefill(self, idx: torch.Tensor, last_positions: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, List[Any]]:
+        """Logits at the last position (or at ``last_positions[b]`` for right-padded rows) and the per-layer cache."""
         x = self._embed(idx)
         cache: List[Any] = []
         for blk in self.transformer.h:
             x, present = blk(x)
             cache.append(present)
-        h = self.transformer.ln_f(x)
-        return self.logits(h[:, -1, :]), cache
+        if last_positions is None:
+            last = x[:, -1, :]
+        else:
+            last = x[torch.arange(x.shape[0], device=x.device), last_positions.to(x.device)]
+        return self.logits(self.transformer.ln_f(last)), cache
 
     @torch.no_grad()
     def step(self, next_ids: torch.Tensor, cache: List[Any], position: int) -> Tuple[torch.Tensor, List[Any]]:

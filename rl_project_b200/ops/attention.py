@@ -57,8 +57,13 @@ _GQA_NATIVE: dict = {}
 def _fused_sdpa(q, k, v, rep, dropout_p, scale):
     from torch.nn.attention import SDPBackend, sdpa_kernel
 
-    backends = [SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION]
-    key = (q.device.index, q.shape[-1], rep)
+    if torch.is_grad_enabled():
+        # training: fixed shapes, cuDNN's per-shape plans amortise and its kernels are the fastest here
+        backends = [SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION]
+    else:
+        # inference prefill: shapes vary per call; the flash kernels need no per-shape plan
+        backends = [SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION, SDPBackend.CUDNN_ATTENTION]
+    key = (q.device.index, q.shape[-1], rep, torch.is_grad_enabled())
     if rep > 1 and _GQA_NATIVE.get(key, True):
         try:
             with sdpa_kernel(backends):
