@@ -62,6 +62,20 @@ def main():
     ap.add_argument("--device", default="cuda")
     args = ap.parse_args()
     trainer, alg = build(args)
+    collect_s: list = []
+    inner_collect = alg.collect
+
+    def timed_collect(step):  # rollout + rewards + old / reference log-probs, timed on the device
+        if args.device == "cuda":
+            torch.cuda.synchronize()
+        t = time.perf_counter()
+        out = inner_collect(step)
+        if args.device == "cuda":
+            torch.cuda.synchronize()
+        collect_s.append(time.perf_counter() - t)
+        return out
+
+    alg.collect = timed_collect
     for _ in range(args.warmup):
         trainer.train_step()
     times, tokens, gen_tokens, rollout_s = [], [], [], []
@@ -88,9 +102,11 @@ def main():
         tokens.append(n * (rl + plen))
         rollout_s.append(st.get("spans", {}).get("decode", {}).get("total_ms", 0.0) / 1e3)
     step_s = sum(times) / len(times)
+    coll = collect_s[-args.steps:]
+    breakdown = {"collect_ms": 1e3 * sum(coll) / len(coll), "update_ms": 1e3 * (step_s - sum(coll) / len(coll))}
     out = {"metric": "GRPO rollout+update tokens/s", "value": sum(tokens) / sum(times), "unit": "tokens/s",
            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
-           "generated_tokens_per_s": sum(gen_tokens) / sum(times), "dtype": "bf16",
+           "generated_tokens_per_s": sum(gen_tokens) / sum(times), "breakdown": breakdown, "dtype": "bf16",
            "data": "synthetic (uniform token ids, prompt lengths uniform; random-init weights)",
            "config": {"model": args.preset, "prompts_per_step": args.prompts, "group_size": args.group,
                       "prompt_len": [args.min_prompt, args.max_prompt], "max_new_tokens": args.max_new,

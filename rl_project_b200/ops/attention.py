@@ -61,8 +61,9 @@ def _fused_sdpa(q, k, v, rep, dropout_p, scale):
         # training: fixed shapes, cuDNN's per-shape plans amortise and its kernels are the fastest here
         backends = [SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION]
     else:
-        # inference prefill: shapes vary per call; the flash kernels need no per-shape plan
-        backends = [SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION, SDPBackend.CUDNN_ATTENTION]
+        # inference prefill: shapes vary per call; the flash / memory-efficient kernels need no per-shape plan
+        # (cuDNN builds one per new shape, which dominated batched prefill)
+        backends = [SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION]
     key = (q.device.index, q.shape[-1], rep, torch.is_grad_enabled())
     if rep > 1 and _GQA_NATIVE.get(key, True):
         try:

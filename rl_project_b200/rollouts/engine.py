@@ -153,7 +153,7 @@ class RolloutEngine:
         engine = self.inference_engine()
         if engine is not None:
             gen = self._generate_paged(engine, [prompt_ids.tolist()], G, temperature)
-            responses = _pad(gen, batch.device)
+            responses = _pad(gen, batch.device, batch.shape[1], SEQ_ALIGN)
             return self._to_trajs(prompt_ids, responses, self._old_logprobs(batch, responses), task, prompt_text,
                                   lengths=[len(g) for g in gen])
         responses, old = self._sample(batch, temperature)
@@ -178,7 +178,7 @@ class RolloutEngine:
             dev = self.policy.device
             for _, idx in sorted(by_len.items()):
                 rows = [gen[i * G + g] for i in idx for g in range(G)]
-                responses = _pad(rows, dev)
+                responses = _pad(rows, dev, clipped[idx[0]].numel(), SEQ_ALIGN)
                 batch = torch.cat([clipped[i].unsqueeze(0).repeat(G, 1) for i in idx], 0).to(dev)
                 old = self._old_logprobs(batch, responses)
                 for j, i in enumerate(idx):
@@ -201,18 +201,30 @@ class RolloutEngine:
         return dec(ids) if dec is not None else ""
 
 
-def _pad(rows: List[List[int]], device: torch.device) -> torch.Tensor:
-    R = max(len(r) for r in rows)
+SEQ_ALIGN = 64  # prompt + response batches are right-padded to a multiple of this length
+
+
+def _aligned_width(prompt_len: int, resp_len: int, align: int) -> int:
+    """Response width such that ``prompt_len + width`` is a multiple of ``align``: the attention kernels
+    then see few distinct sequence lengths across steps (their per-shape set-up is reused)."""
+    if align <= 1:
+        return resp_len
+    return -(-(prompt_len + resp_len) // align) * align - prompt_len
+
+
+def _pad(rows: List[List[int]], device: torch.device, prompt_len: int = 0, align: int = 1) -> torch.Tensor:
+    R = _aligned_width(prompt_len, max(len(r) for r in rows), align)
     out = torch.zeros((len(rows), R), dtype=torch.long)
     for i, r in enumerate(rows):
         out[i, : len(r)] = torch.as_tensor(r, dtype=torch.long)
     return out.to(device, non_blocking=True)
 
 
-def stack_group(trajectories: Sequence[Trajectory], pad_value: int = 0):
-    """``(prompt [G, P], responses [G, R], mask [G, R])`` for a group sharing one prompt."""
+def stack_group(trajectories: Sequence[Trajectory], pad_value: int = 0, align: int = SEQ_ALIGN):
+    """``(prompt [G, P], responses [G, R], mask [G, R])`` for a group sharing one prompt; ``R`` is padded
+    so that ``P + R`` is a multiple of ``align`` (the mask marks the real tokens)."""
     prompt = trajectories[0].prompt_ids.unsqueeze(0)
-    R = max(t.response_length for t in trajectories)
+    R = _aligned_width(prompt.shape[1], max(t.response_length for t in trajectories), align)
     G = len(trajectories)
     resp = torch.full((G, R), pad_value, dtype=torch.long)
     mask = torch.zeros((G, R), dtype=torch.float32)
@@ -222,8 +234,8 @@ def stack_group(trajectories: Sequence[Trajectory], pad_value: int = 0):
     return prompt.repeat(G, 1), resp, mask
 
 
-def stack_old_logprobs(trajectories: Sequence[Trajectory]) -> torch.Tensor:
-    R = max(t.response_length for t in trajectories)
+def stack_old_logprobs(trajectories: Sequence[Trajectory], width: Optional[int] = None) -> torch.Tensor:
+    R = width if width is not None else max(t.response_length for t in trajectories)
     out = torch.zeros((len(trajectories), R), dtype=torch.float32)
     for i, t in enumerate(trajectories):
         if t.old_logprobs is not None:

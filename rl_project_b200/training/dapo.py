@@ -99,7 +99,7 @@ class DAPOAlgorithm(PostTrainingAlgorithm):
                     t.truncated = True
             prompt, resp, mask = stack_group(trajs, self.policy.pad_token_id)
             if all(t.old_logprobs is not None for t in trajs):
-                old = stack_old_logprobs(trajs) * mask
+                old = stack_old_logprobs(trajs, resp.shape[1]) * mask
             else:
                 old = self.policy.logprobs(prompt, resp).float().cpu() * mask
             if self.cfg.kl_coef > 0:

@@ -144,7 +144,7 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
             return
         prompt, resp, mask = stack_group(grp.trajectories, self.policy.pad_token_id)
         if all(t.old_logprobs is not None for t in grp.trajectories):
-            old = stack_old_logprobs(grp.trajectories) * mask  # recorded at sampling time: same weights
+            old = stack_old_logprobs(grp.trajectories, resp.shape[1]) * mask  # recorded at sampling time: same weights
         else:
             old = self.policy.logprobs(prompt, resp).float().cpu() * mask
         with self.policy.reference():
