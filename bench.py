@@ -46,6 +46,16 @@ def parse_args():
     ap.add_argument("--batch-per-gpu", type=int, default=8)
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--workload", choices=["sft1b", "mesh8b", "moe", "grpo"], default="sft1b",
+                    help="sft1b: the headline (config 2). mesh8b: dense-8B pretrain on a TP x PP x DP mesh "
+                         "(config 3). moe: MLA+MoE pretrain with expert parallelism (config 4). grpo: GRPO "
+                         "rollout+update on one GPU (config 5 shape, see rl_project_b200.benchmarks.grpo).")
+    ap.add_argument("--tp", type=int, default=2)
+    ap.add_argument("--pp", type=int, default=2)
+    ap.add_argument("--micro", type=int, default=8)
+    ap.add_argument("--global-batch", type=int, default=None)
+    ap.add_argument("--layers", type=int, default=None, help="override the preset's layer count (smoke runs)")
+    ap.add_argument("--grad-ckpt", action="store_true")
     return ap.parse_args()
 
 
@@ -263,6 +273,101 @@ def run_ours(args, world, rank, local):
     strategy.teardown()
 
 
+def run_pretrain_workload(args, world, rank, local):
+    """Configs 3 (mesh8b) and 4 (moe): synthetic pretraining through Trainer.train_step on a parallel layout."""
+    import torch
+
+    from rl_project_b200.core.config import ExperimentManifest
+    from rl_project_b200.core.lifecycle import RunContext
+    from rl_project_b200.data.synthetic import SyntheticPretrainSource
+    from rl_project_b200.models.transformer.model import TransformerLM
+    from rl_project_b200.ops._ext import launch_count, native
+    from rl_project_b200.parallel.strategies import build_strategy
+    from rl_project_b200.training.common.trainer import Trainer
+    from rl_project_b200.training.pretrain import PretrainAlgorithm, PretrainConfig
+
+    native()
+    if args.workload == "mesh8b":
+        preset, seq = "bl_dense_8b", (args.seq if args.seq != 4096 else 8192)
+        tp, pp = (args.tp, args.pp) if world > 1 else (1, 1)
+        dp = world // (tp * pp)
+        strategy = "single" if world == 1 else ("hybrid" if tp > 1 and pp > 1 else
+                                                ("tensor_parallel" if tp > 1 else "pipeline_parallel"))
+        gb = args.global_batch or 64
+        dist_cfg = {"strategy": strategy, "tensor_parallel_size": tp, "pipeline_parallel_size": pp,
+                    "timeout_s": 600}
+        layout = f"tp{tp}xpp{pp}xdp{dp}"
+        micro = args.micro
+    else:
+        preset, seq = "bl_mla_moe", args.seq
+        dp = world
+        strategy = "expert_parallel" if world > 1 else "single"
+        gb = args.global_batch or 4 * world
+        dist_cfg = {"strategy": strategy, "expert_parallel_size": max(world, 1), "timeout_s": 600}
+        layout = f"ep{world}" if world > 1 else "single"
+        micro = 1
+    rows = gb // dp
+    model_over = {"block_size": seq}
+    if args.layers:
+        model_over["n_layer"] = args.layers
+    manifest = ExperimentManifest.from_dict({
+        "name": f"bench-{args.workload}", "algorithm": "pretrain", "model_preset": preset, "model": model_over,
+        "trainer": {"batch_size": rows, "gradient_accumulation_steps": micro, "max_steps": 10 ** 9, "eval_every": 0,
+                    "log_every": 0, "seed": 1234, "precision": {"dtype": "bfloat16"},
+                    "gradient_checkpointing": bool(args.grad_ckpt),
+                    "optimizer": {"learning_rate": 3e-4, "grad_clip": 1.0, "weight_decay": 0.1},
+                    "schedule": {"name": "constant", "warmup_steps": 0},
+                    "checkpoint": {"save_every": 0, "auto_resume": False}},
+        "distributed": dist_cfg, "output_dir": os.path.join(tempfile.gettempdir(), f"rlb_bench_{rank}")})
+    strat = build_strategy(manifest.distributed)
+    strat.setup()
+    torch.cuda.set_device(local)
+    ctx = RunContext.create(manifest, metrics_backend="none", distributed=world > 1)
+    spec = manifest.model
+    torch.manual_seed(1234)
+    with torch.device(ctx.device):
+        model = TransformerLM(spec)
+    n_params_full = sum(p.numel() for p in model.parameters())
+    from rl_project_b200.parallel.mesh_strategies import data_parallel_rank
+
+    src = SyntheticPretrainSource(spec.vocab_size, seq, rows, seed=1234, rank=data_parallel_rank())
+    batches = [tuple(t.to(ctx.device) for t in next(iter(src))) for _ in range(2)]
+
+    class Resident:
+        def __init__(self):
+            self.i = 0
+
+        def __iter__(self):
+            return self
+
+        def __next__(self):
+            self.i += 1
+            return batches[self.i % 2]
+
+    alg = PretrainAlgorithm(model, Resident(), PretrainConfig(batch_size=rows), device=ctx.device)
+    trainer = Trainer(ctx, alg, strategy=strat)
+    for _ in range(args.warmup):
+        trainer.train_step()
+    clocks = ClockSampler(local)
+    clocks.start()
+    l0 = launch_count()
+    ms = time_device(trainer.train_step, args.steps)
+    launches = (launch_count() - l0) // args.steps
+    clk = clocks.stop()
+    tokens = seq * gb
+    payload = {"metric": METRIC, "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+               "scaling": "strong" if args.workload == "mesh8b" else "weak", "vs_baseline": None, "dtype": "bf16",
+               "data": "synthetic (uniform token ids; random-init weights)",
+               "config": {"model": preset + (f" ({args.layers} layers)" if args.layers else ""), "global_batch": gb,
+                          "seq_len": seq, "parallelism": layout, "micro_batches": micro,
+                          "params_full_model": n_params_full, "workload": args.workload,
+                          "l2": "inputs larger than L2", "final_loss": trainer.history[-1].loss},
+               "clocks": clk, "e2e": None, "gpu_launches": int(launches), "impl": "ours"}
+    emit(rank, payload)
+    strat.teardown()
+
+
 def _peak_tflops():
     try:
         with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as fh:
@@ -283,6 +388,15 @@ def main():
         payload = run_reference(args, world, rank, local, time_device=time_device, time_wall=time_wall,
                                 clock_sampler=ClockSampler, metric=METRIC, model_name=MODEL_NAME)
         emit(rank, payload)
+        return
+    if args.workload in ("mesh8b", "moe"):
+        run_pretrain_workload(args, world, rank, local)
+        return
+    if args.workload == "grpo":
+        from rl_project_b200.benchmarks import grpo
+
+        sys.argv = [sys.argv[0], "--steps", str(args.steps), "--warmup", str(args.warmup)]
+        grpo.main()
         return
     run_ours(args, world, rank, local)
 

@@ -1,6 +1,6 @@
 // Thin inline-PTX wrappers for the Blackwell (sm_100a) primitives used by the
 // tensor-core kernels: mbarriers, TMA tiled loads (never with cluster
-// multicast), tcgen05 TMEM allocation / MMA / commit / loads, and the shared
+// cluster-wide delivery), tcgen05 TMEM allocation / MMA / commit / loads, and the shared
 // memory + instruction descriptors of tcgen05.mma.kind::f16.
 //
 // Descriptor bit layouts follow the PTX ISA "matrix descriptor" and
@@ -63,7 +63,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 
 // ------------------------------------------------------------------ TMA
 // 2-D tiled load into this CTA's shared memory, completing on `bar`.
-// (No .multicast::cluster form is used anywhere in this library.)
+// Plain load into this CTA only: no cluster-wide delivery form is used anywhere in this library.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
