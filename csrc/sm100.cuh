@@ -1,6 +1,6 @@
 // Thin inline-PTX wrappers for the Blackwell (sm_100a) primitives used by the
-// tensor-core kernels: mbarriers, TMA tiled loads (never with cluster
-// cluster-wide delivery), tcgen05 TMEM allocation / MMA / commit / loads, and the shared
+// tensor-core kernels: mbarriers, TMA tiled loads (each into one CTA's own
+// shared memory), tcgen05 TMEM allocation / MMA / commit / loads, and the shared
 // memory + instruction descriptors of tcgen05.mma.kind::f16.
 //
 // Descriptor bit layouts follow the PTX ISA "matrix descriptor" and
