@@ -150,6 +150,21 @@ def bench_paged(cases=((64, 1536, 32, 8, 128), (256, 1024, 32, 8, 128), (8, 4096
                           "frac_of_measured_hbm": round(moved / t / 1e6 / peak_gbs, 3)}), flush=True)
 
 
+def bench_sample(rows: int = 512, V: int = 128256):
+    """Fused Gumbel-max sampler: bytes = the bf16 logits read once."""
+    from rl_project_b200.ops.sampling import sample_tokens
+
+    _, peak_gbs = _peaks()
+    x = torch.randn(rows, V, device="cuda").to(torch.bfloat16)
+    t = torch.ones(rows, device="cuda")
+    ms = time_ms(lambda: sample_tokens(x, t, 1))
+    moved = rows * V * 2
+    print(json.dumps({"kernel": "sample (gumbel-max)", "rows": rows, "V": V, "ms": round(ms, 4),
+                      "gbs": round(moved / ms / 1e6, 1), "frac_of_measured_hbm": round(moved / ms / 1e6 / peak_gbs, 3),
+                      "torch_multinomial_ms": round(time_ms(lambda: torch.multinomial(
+                          torch.softmax(x.float(), -1), 1)), 4)}), flush=True)
+
+
 MODEL_SHAPES = [
     (32768, 3072, 2048, "nt"), (32768, 2048, 2048, "nt"), (32768, 16384, 2048, "nt"), (32768, 2048, 8192, "nt"),
     (32768, 2048, 16384, "nn"), (32768, 8192, 2048, "nn"), (16384, 2048, 32768, "tn"), (2048, 8192, 32768, "tn"),
@@ -158,11 +173,13 @@ MODEL_SHAPES = [
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--which", default="gemm,mem,adam,paged")
+    ap.add_argument("--which", default="gemm,mem,adam,paged,sample")
     args = ap.parse_args()
     which = set(args.which.split(","))
     if "paged" in which:
         bench_paged()
+    if "sample" in which:
+        bench_sample()
     if "gemm" in which:
         bench_gemm(MODEL_SHAPES)
     if "mem" in which:
