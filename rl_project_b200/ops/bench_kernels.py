@@ -182,6 +182,8 @@ def main():
         bench_sample()
     if "gemm" in which:
         bench_gemm(MODEL_SHAPES)
+    if "gemm1" in which:  # one mid-size shape (profiling case)
+        bench_gemm([(16384, 4096, 4096, "nt")])
     if "mem" in which:
         bench_memory_bound()
     if "adam" in which:
