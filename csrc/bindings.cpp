@@ -365,6 +365,37 @@ std::vector<at::Tensor> sample(const at::Tensor& logits, const at::Tensor& tempe
   return {tokens, lp};
 }
 
+// ---------------------------------------------------------------- fused reduce-scatter over peer memory
+void signal_peers(const at::Tensor& flag_ptrs, int64_t rank, int64_t slot, int64_t epoch) {
+  check_cuda(flag_ptrs, "flag_ptrs");
+  TORCH_CHECK(flag_ptrs.scalar_type() == at::kLong && flag_ptrs.dim() == 1, "flag_ptrs: int64 [world]");
+  const c10::cuda::CUDAGuard g(flag_ptrs.device());
+  CHECK_OK(rlb_signal_peers(reinterpret_cast<const unsigned long long*>(flag_ptrs.data_ptr<int64_t>()),
+                            (int)flag_ptrs.numel(), (int)rank, (int)slot, (int)epoch, cur_stream()),
+           "signal_peers");
+}
+
+void fused_reduce_scatter(const at::Tensor& buf_ptrs, int64_t mc_base, const at::Tensor& my_flags, int64_t rank,
+                          int64_t slot, int64_t epoch, int64_t shard, double scale, const at::Tensor& out,
+                          bool accumulate, const c10::optional<at::Tensor>& sumsq, const at::Tensor& status,
+                          int64_t limit_ns, int64_t ctas) {
+  check_cuda(buf_ptrs, "buf_ptrs");
+  TORCH_CHECK(buf_ptrs.scalar_type() == at::kLong && buf_ptrs.dim() == 1, "buf_ptrs: int64 [world]");
+  TORCH_CHECK(my_flags.scalar_type() == at::kInt && my_flags.is_cuda(), "my_flags: int32 CUDA tensor");
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() == shard, "out: fp32 [shard]");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0, "out must be 16-byte aligned");
+  TORCH_CHECK(shard % 8 == 0, "shard must be a multiple of 8 elements");
+  TORCH_CHECK(status.scalar_type() == at::kInt && status.is_cuda(), "status: int32 CUDA tensor");
+  if (sumsq.has_value()) TORCH_CHECK(sumsq->scalar_type() == at::kFloat && sumsq->is_cuda(), "sumsq: fp32 CUDA");
+  const c10::cuda::CUDAGuard g(out.device());
+  CHECK_OK(rlb_fused_reduce_scatter(reinterpret_cast<const unsigned long long*>(buf_ptrs.data_ptr<int64_t>()),
+                                    (unsigned long long)mc_base, my_flags.data_ptr<int>(), (int)buf_ptrs.numel(),
+                                    (int)rank, (int)slot, (int)epoch, shard, (float)scale, out.data_ptr<float>(),
+                                    accumulate ? 1 : 0, sumsq.has_value() ? sumsq->data_ptr<float>() : nullptr,
+                                    status.data_ptr<int>(), (unsigned long long)limit_ns, (int)ctas, cur_stream()),
+           "fused_reduce_scatter");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -391,4 +422,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_decode", &paged_decode);
   m.def("paged_write", &paged_write);
   m.def("sample", &sample);
+  m.def("signal_peers", &signal_peers);
+  m.def("fused_reduce_scatter", &fused_reduce_scatter);
 }

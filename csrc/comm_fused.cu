@@ -1,0 +1,192 @@
+// Reduce-scatter fused with the fp32 cast, the 1/world scale, gradient
+// accumulation and the squared-norm partial, reading the peers' gradient
+// buffers directly over NVLink: the gradient path of sharded data parallel.
+//
+// Every rank holds its bf16 gradient for one parameter unit in a slot of a
+// symmetric buffer (one allocation mapped on every GPU of the node).  Rank r
+// owns elements [r S, (r + 1) S) of the slot.  After a rank has filled its slot
+// it raises its flag for the slot in every peer's flag array (system-scope
+// release).  The reduce kernel on rank r waits (bounded) until every peer's
+// flag reached the slot's epoch, then for each owned element sums the world
+// copies -- with one `multimem.ld_reduce` through the slot's NVLink multicast
+// address (the switch adds the copies in fp32; each GPU receives S values
+// instead of (world - 1) S) or with plain peer loads -- scales by 1/world and
+// writes or adds the fp32 shard gradient, optionally adding the squares of the
+// final values into a norm accumulator.  No NCCL call, no bf16 reduce-scatter
+// output and no separate cast / scale / accumulate / norm kernels.
+//
+// Waits are bounded: a flag that does not arrive within the time limit sets
+// `status` (kTimeout | slot << 8) and the kernel returns without writing.
+// Slot reuse is made safe by the caller's ordering (one communication stream,
+// a ring of slots, and the rule that a slot is refilled only after this rank's
+// reduce three uses back finished): the ordering argument is in
+// rl_project_b200/parallel/fused_comm.py.
+#include "common.cuh"
+
+namespace rlb {
+
+RLB_DEVICE int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+RLB_DEVICE void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+RLB_DEVICE unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Thread p raises this rank's flag for `slot` on rank p: flags_p[slot * world + rank] = epoch.
+__global__ void signal_peers_kernel(const unsigned long long* __restrict__ flag_ptrs, int world, int rank, int slot,
+                                    int epoch) {
+  const int p = threadIdx.x;
+  if (p >= world) return;
+  __threadfence_system();
+  int* f = reinterpret_cast<int*>(flag_ptrs[p]) + (long long)slot * world + rank;
+  st_release_sys(f, epoch);
+}
+
+// Bounded wait by one thread for every peer's flag of `slot` to reach `epoch`.
+RLB_DEVICE bool wait_flags(const int* my_flags, int world, int slot, int epoch, unsigned long long limit_ns,
+                           int* status) {
+  const unsigned long long t0 = globaltimer_ns();
+  const long long max_polls = (long long)(limit_ns / 32) + 1024;  // caps the loop even if the timer stalls
+  for (int p = 0; p < world; ++p) {
+    const int* f = my_flags + (long long)slot * world + p;
+    long long polls = 0;
+    while (ld_acquire_sys(f) < epoch) {
+      if (++polls > max_polls || globaltimer_ns() - t0 > limit_ns) {
+        report(status, kTimeout | (slot << 8));
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+  return true;
+}
+
+// 8 bf16 of every rank at one address through the multicast mapping, summed in fp32 by the switch.
+RLB_DEVICE void multimem_sum8(const __nv_bfloat16* mc, float* out) {
+  uint32_t r0, r1, r2, r3;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "l"(mc)
+               : "memory");
+  const uint32_t r[4] = {r0, r1, r2, r3};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = __uint_as_float(r[i] << 16);
+    out[2 * i + 1] = __uint_as_float(r[i] & 0xffff0000u);
+  }
+}
+
+// Plain 16-byte load (not the read-only path: the slot is rewritten by its owner between launches).
+RLB_DEVICE uint4 ld16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+RLB_DEVICE void add8(const uint4& raw, float* acc) {
+  float f[8];
+  unpack8(*reinterpret_cast<const bf16x8*>(&raw), f);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) acc[k] += f[k];
+}
+
+constexpr int kRsThreads = 512;
+constexpr int kRsUnroll = 2;
+
+template <bool MULTIMEM>
+__global__ void __launch_bounds__(kRsThreads) fused_rs_kernel(
+    const unsigned long long* __restrict__ buf_ptrs, unsigned long long mc_base, const int* __restrict__ my_flags,
+    int world, int rank, int slot, int epoch, long long shard, float scale, float* __restrict__ out, int accumulate,
+    float* __restrict__ sumsq, int* status, unsigned long long limit_ns) {
+  __shared__ int ok;
+  __shared__ float red[kRsThreads / 32];
+  if (threadIdx.x == 0) ok = wait_flags(my_flags, world, slot, epoch, limit_ns, status) ? 1 : 0;
+  __syncthreads();
+  if (!ok) return;
+  const long long lo = (long long)rank * shard;
+  const long long nvec = shard / 8;
+  const long long stride = (long long)gridDim.x * kRsThreads;
+  float sq = 0.f;
+  for (long long v0 = (long long)blockIdx.x * kRsThreads + threadIdx.x; v0 < nvec; v0 += stride * kRsUnroll) {
+    float acc[kRsUnroll][8];
+#pragma unroll
+    for (int u = 0; u < kRsUnroll; ++u) {
+      const long long v = v0 + u * stride;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[u][k] = 0.f;
+      if (v >= nvec) continue;
+      const long long e = lo + v * 8;
+      if constexpr (MULTIMEM) {
+        multimem_sum8(reinterpret_cast<const __nv_bfloat16*>(mc_base) + e, acc[u]);
+      } else {
+        // up to 8 peers' loads in flight before the first add, any further peers one by one
+        uint4 raw[8];
+#pragma unroll
+        for (int p = 0; p < 8; ++p)
+          if (p < world) raw[p] = ld16(reinterpret_cast<const __nv_bfloat16*>(buf_ptrs[p]) + e);
+#pragma unroll
+        for (int p = 0; p < 8; ++p)
+          if (p < world) add8(raw[p], acc[u]);
+        for (int p = 8; p < world; ++p) add8(ld16(reinterpret_cast<const __nv_bfloat16*>(buf_ptrs[p]) + e), acc[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kRsUnroll; ++u) {
+      const long long v = v0 + u * stride;
+      if (v >= nvec) continue;
+      float4* o = reinterpret_cast<float4*>(out + v * 8);
+      float4 a = make_float4(acc[u][0] * scale, acc[u][1] * scale, acc[u][2] * scale, acc[u][3] * scale);
+      float4 b = make_float4(acc[u][4] * scale, acc[u][5] * scale, acc[u][6] * scale, acc[u][7] * scale);
+      if (accumulate) {
+        const float4 pa = o[0], pb = o[1];
+        a.x += pa.x; a.y += pa.y; a.z += pa.z; a.w += pa.w;
+        b.x += pb.x; b.y += pb.y; b.z += pb.z; b.w += pb.w;
+      }
+      o[0] = a;
+      o[1] = b;
+      sq += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w + b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
+    }
+  }
+  if (sumsq != nullptr) {
+    sq = block_sum(sq, red);
+    if (threadIdx.x == 0) atomicAdd(sumsq, sq);
+  }
+}
+
+}  // namespace rlb
+
+using namespace rlb;
+
+cudaError_t rlb_signal_peers(const unsigned long long* flag_ptrs, int world, int rank, int slot, int epoch,
+                             cudaStream_t s) {
+  if (world < 1 || world > 32) return cudaErrorInvalidValue;
+  signal_peers_kernel<<<1, 32, 0, s>>>(flag_ptrs, world, rank, slot, epoch);
+  return cudaGetLastError();
+}
+
+cudaError_t rlb_fused_reduce_scatter(const unsigned long long* buf_ptrs, unsigned long long mc_base,
+                                     const int* my_flags, int world, int rank, int slot, int epoch, long long shard,
+                                     float scale, float* out, int accumulate, float* sumsq, int* status,
+                                     unsigned long long limit_ns, int ctas, cudaStream_t s) {
+  if (shard % 8 != 0 || world < 1 || world > 32 || ctas < 1) return cudaErrorInvalidValue;
+  const long long nvec = shard / 8;
+  long long grid = (nvec + (long long)kRsThreads * kRsUnroll - 1) / ((long long)kRsThreads * kRsUnroll);
+  if (grid > ctas) grid = ctas;
+  if (grid < 1) grid = 1;
+  if (mc_base)
+    fused_rs_kernel<true><<<(int)grid, kRsThreads, 0, s>>>(buf_ptrs, mc_base, my_flags, world, rank, slot, epoch,
+                                                           shard, scale, out, accumulate, sumsq, status, limit_ns);
+  else
+    fused_rs_kernel<false><<<(int)grid, kRsThreads, 0, s>>>(buf_ptrs, mc_base, my_flags, world, rank, slot, epoch,
+                                                            shard, scale, out, accumulate, sumsq, status, limit_ns);
+  return cudaGetLastError();
+}

@@ -62,6 +62,14 @@ cudaError_t rlb_paged_write(const void* k_new, const void* v_new, void* k_pool, 
 cudaError_t rlb_sample(const void* logits, int is_bf16, long long ld, int rows, int V, const float* temperature,
                        unsigned long long seed, long long* tokens, float* logprobs, cudaStream_t s);
 
+// Reduce-scatter over peer memory fused with cast, scale, accumulation and the squared-norm partial.
+cudaError_t rlb_signal_peers(const unsigned long long* flag_ptrs, int world, int rank, int slot, int epoch,
+                             cudaStream_t s);
+cudaError_t rlb_fused_reduce_scatter(const unsigned long long* buf_ptrs, unsigned long long mc_base,
+                                     const int* my_flags, int world, int rank, int slot, int epoch, long long shard,
+                                     float scale, float* out, int accumulate, float* sumsq, int* status,
+                                     unsigned long long limit_ns, int ctas, cudaStream_t s);
+
 // RMSNorm backward that allocates nothing (no counterpart in the reference):
 // the dw partial sums live in a fixed 4 MiB file-scope __device__ array per
 // device instead of a caller-allocated buffer.  Returns a cudaError_t value;

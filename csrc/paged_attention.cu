@@ -28,9 +28,9 @@ constexpr int kWarps = 4;
 // kept per lane over that lane's own tokens and merged once at the end, as are
 // the P.V partial sums -- the only per-block cross-lane traffic is the score
 // reduction.  Each warp takes whole blocks round-robin, so every load is a
-// 16-byte vector and a warp has 2 x PASSES of them in flight per block.
+// 16-byte vector and a warp has 2 x min(PASSES, 4) of them in flight at a time.
 template <int D, int G>
-__global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(
+__global__ void __launch_bounds__(kWarps * 32, (G <= 4 ? 4 : 2)) paged_decode_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_pool,
     const __nv_bfloat16* __restrict__ v_pool, const int* __restrict__ block_tables, const int* __restrict__ ctx_lens,
     __nv_bfloat16* __restrict__ out, float* __restrict__ part_acc, float* __restrict__ part_ml, int Hkv,
@@ -73,36 +73,42 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(
         continue;
       }
       const long long base = (((long long)blk * Hkv + h) * kBlock) * D + slice * 8;
-      bf16x8 kv[PASSES], vv[PASSES];
+      // loads go out CH passes at a time (all K and V vectors of a chunk before any use): enough
+      // bytes in flight per warp while the register count stays low enough for 4 CTAs per SM
+      constexpr int CH = PASSES < 4 ? PASSES : 4;
 #pragma unroll
-      for (int p = 0; p < PASSES; ++p) {  // all loads of the block issued before any use
-        const long long off = base + (long long)(p * TPP + tip) * D;
-        kv[p] = ldg8(k_pool + off);
-        vv[p] = ldg8(v_pool + off);
-      }
+      for (int c0 = 0; c0 < PASSES; c0 += CH) {
+        bf16x8 kv[CH], vv[CH];
 #pragma unroll
-      for (int p = 0; p < PASSES; ++p) {
-        const int t = jb * kBlock + p * TPP + tip;
-        const bool valid = t >= t0 && t < t1;
-        float kf[8], vf[8];
-        unpack8(kv[p], kf);
-        unpack8(vv[p], vf);
+        for (int c = 0; c < CH; ++c) {
+          const long long off = base + (long long)((c0 + c) * TPP + tip) * D;
+          kv[c] = ldg8(k_pool + off);
+          vv[c] = ldg8(v_pool + off);
+        }
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          float s = 0.f;
+        for (int c = 0; c < CH; ++c) {
+          const int t = jb * kBlock + (c0 + c) * TPP + tip;
+          const bool valid = t >= t0 && t < t1;
+          float kf[8], vf[8];
+          unpack8(kv[c], kf);
+          unpack8(vv[c], vf);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) s += qf[g][e] * kf[e];
+          for (int g = 0; g < G; ++g) {
+            float s = 0.f;
 #pragma unroll
-          for (int o = 1; o < LPT; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-          if (softcap > 0.f) s = tanhf(s / softcap) * softcap;
-          if (!valid) continue;
-          const float mn = fmaxf(m[g], s);
-          const float corr = __expf(m[g] - mn);
-          const float pr = __expf(s - mn);
-          l[g] = l[g] * corr + pr;
+            for (int e = 0; e < 8; ++e) s += qf[g][e] * kf[e];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[g][e] = acc[g][e] * corr + pr * vf[e];
-          m[g] = mn;
+            for (int o = 1; o < LPT; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (softcap > 0.f) s = tanhf(s / softcap) * softcap;
+            if (!valid) continue;
+            const float mn = fmaxf(m[g], s);
+            const float corr = __expf(m[g] - mn);
+            const float pr = __expf(s - mn);
+            l[g] = l[g] * corr + pr;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[g][e] = acc[g][e] * corr + pr * vf[e];
+            m[g] = mn;
+          }
         }
       }
     }

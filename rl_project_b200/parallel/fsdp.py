@@ -68,7 +68,8 @@ class _Unit:
             self.offsets.append(off)
             off += n
         self.total = off
-        self.padded = (off + world - 1) // world * world
+        quantum = world * 8  # whole 16-byte vectors of bf16 per shard (fused reduce-scatter, vector loads)
+        self.padded = (off + quantum - 1) // quantum * quantum
         self.shard = self.padded // world
         self.world, self.rank = world, rank
         self.device = device
@@ -87,6 +88,8 @@ class _Unit:
         self.gather_event: Optional[torch.cuda.Event] = None
         self.pending_grads = 0
         self.rs_event = None
+        self.grad_buf: Optional[torch.Tensor] = None  # persistent fp32 shard gradient (fused path)
+        self.norm_counted = False  # the fused reduce added this unit's final gradient to the norm
         self._point_params_at_full()
         del full32
 
@@ -118,6 +121,9 @@ class FSDPStrategy(_ProcessGroupStrategy):
         self.comm_stream = None
         self.group = None
         self._hooks: list = []
+        self.fused = None  # FusedReduceScatter when gradients are reduced over peer memory
+        self.owns_grad_clip = False
+        self._final_micro = True
 
     # ---------------------------------------------------------------- setup
     def _gloo(self) -> bool:
@@ -157,6 +163,7 @@ class FSDPStrategy(_ProcessGroupStrategy):
                 self.root = u
         if device.type == "cuda":
             self.comm_stream = torch.cuda.Stream(device=device)
+            self._setup_fused(device, dtype)
         for u in self.units:
             self._install_hooks(u)
         # params start gathered (full buffers hold the initial weights) -> release the block units
@@ -170,6 +177,29 @@ class FSDPStrategy(_ProcessGroupStrategy):
         else:
             for u in self.units:
                 u.gathered = True
+
+    def _setup_fused(self, device: torch.device, dtype: torch.dtype) -> None:
+        """Reduce gradients with the fused peer-memory kernel (``fused_comm`` auto/on) when every rank is a GPU
+        of this node on NCCL; ``off`` and ``nccl_baseline`` keep NCCL's reduce-scatter."""
+        from rl_project_b200.parallel import fused_comm as fc
+
+        mode = getattr(self.cfg, "fused_comm", "auto")
+        world = dist.get_world_size(self.group)
+        if mode in ("off", "nccl_baseline") or world == 1:
+            return
+        ok = fc.available(self.group) and dtype == torch.bfloat16
+        if not ok:
+            if mode == "on":
+                raise DistributedConfigError("fused_comm=on needs bf16 gradients on NCCL ranks of one node")
+            return
+        # slots sized for the largest block unit; larger units (the root) go through in chunks
+        blocks = [u for u in self.units if u is not self.root] or self.units
+        chunk = max(u.shard for u in blocks)
+        self.fused = fc.FusedReduceScatter(self.group, chunk * world, device,
+                                           timeout_s=min(float(self.cfg.timeout_s), 300.0))
+        for u in self.units:
+            u.grad_buf = torch.zeros(u.shard, dtype=torch.float32, device=device)
+        self.owns_grad_clip = True
 
     # ---------------------------------------------------------------- collectives
     def _all_gather(self, u: _Unit) -> None:
@@ -211,6 +241,9 @@ class FSDPStrategy(_ProcessGroupStrategy):
         for p, n in zip(u.params, u.numels):
             g = p.grad
             grads.append(g.reshape(-1) if g is not None else torch.zeros(n, dtype=u.dtype, device=u.device))
+        if self.fused is not None:
+            self._fused_reduce_scatter(u, grads)
+            return
         pad = u.padded - u.total
         if pad:
             grads.append(torch.zeros(pad, dtype=grads[0].dtype, device=u.device))
@@ -240,6 +273,41 @@ class FSDPStrategy(_ProcessGroupStrategy):
         with torch.cuda.stream(self.comm_stream):
             run()
         flat.record_stream(self.comm_stream)
+
+    def _fused_reduce_scatter(self, u: _Unit, grads: List[torch.Tensor]) -> None:
+        """Pack the unit's bf16 gradients into symmetric slots and reduce the owned slice over peer memory into
+        the persistent fp32 shard gradient (cast, 1/world, accumulation and squared norm in the same kernel)."""
+        fr = self.fused
+        cur = torch.cuda.current_stream()
+        accumulate = u.master.grad is not None
+        if not accumulate:
+            u.master.grad = u.grad_buf
+        norm = self._final_micro
+        C = fr.slot_elems // u.world
+        if u.shard <= C:
+            slot = fr.next_slot(u.padded)
+            torch.cat(grads, out=slot[:u.total])
+            if u.padded > u.total:
+                slot[u.total:].zero_()
+            for p in u.params:
+                p.grad = None
+            self.comm_stream.wait_stream(cur)
+            fr.reduce(u.shard, u.grad_buf, accumulate, norm, stream=self.comm_stream)
+        else:
+            flat = torch.cat(grads)
+            if u.padded > u.total:
+                flat = torch.cat([flat, flat.new_zeros(u.padded - u.total)])
+            for p in u.params:
+                p.grad = None
+            rows = flat.view(u.world, u.shard)
+            for c0 in range(0, u.shard, C):
+                L = min(C, u.shard - c0)
+                slot = fr.next_slot(u.world * L)
+                slot.view(u.world, L).copy_(rows[:, c0:c0 + L])
+                self.comm_stream.wait_stream(cur)
+                fr.reduce(L, u.grad_buf[c0:c0 + L], accumulate, norm, stream=self.comm_stream)
+            flat.record_stream(self.comm_stream)
+        u.norm_counted = norm
 
     # ---------------------------------------------------------------- hooks
     def _install_hooks(self, u: _Unit) -> None:
@@ -294,6 +362,12 @@ class FSDPStrategy(_ProcessGroupStrategy):
 
         for u in self.units:
             u.pending_grads = len(u.params)
+        self._final_micro = micro == n_micro - 1
+        if self.fused is not None and micro == 0:
+            self.fused.check()  # a timed-out wait of the previous step fails the run here
+            self.fused.reset_norm()
+            for u in self.units:
+                u.norm_counted = False
         return nullcontext()
 
     def finish_gradients(self, trainer) -> None:
@@ -351,7 +425,9 @@ class FSDPStrategy(_ProcessGroupStrategy):
                 u.gathered = False
                 self.gather(u)
 
-    def clip_grad_norm(self, params, max_norm: float) -> torch.Tensor:
+    def clip_grad_norm(self, params, max_norm: float, optimizer=None) -> torch.Tensor:
+        if self.fused is not None:
+            return self._fused_clip(max_norm, optimizer)
         sq = sum(u.master.grad.float().pow(2).sum() for u in self.units)
         dist.all_reduce(sq, group=self.group)
         norm = sq.sqrt()
@@ -359,6 +435,34 @@ class FSDPStrategy(_ProcessGroupStrategy):
         for u in self.units:
             u.master.grad.mul_(coef)
         return norm
+
+    def _fused_clip(self, max_norm: float, optimizer) -> torch.Tensor:
+        """Global gradient norm from the squares the fused reduce already summed (one float all-reduced); a
+        rank whose reduce timed out contributes +inf, so every rank skips the update."""
+        fr = self.fused
+        sq = fr.sumsq.clone()
+        for u in self.units:
+            if not u.norm_counted:
+                sq += u.master.grad.float().pow(2).sum()
+        sq = torch.where(fr.status != 0, torch.full_like(sq, float("inf")), sq)
+        fr.poll_status()
+        dist.all_reduce(sq, group=self.group)
+        norm = sq.sqrt()[0]
+        if optimizer is not None and hasattr(optimizer, "arm_clip"):
+            optimizer.arm_clip(norm, max_norm)
+        elif max_norm > 0:
+            coef = (max_norm / (norm + 1e-6)).clamp(max=1.0)
+            coef = torch.where(torch.isfinite(norm), coef, torch.zeros_like(coef))
+            for u in self.units:
+                u.master.grad.mul_(coef)
+        return norm
+
+    def teardown(self) -> None:
+        if self.fused is not None:
+            torch.cuda.synchronize()
+            self.fused.close()
+            self.fused = None
+        super().teardown()
 
     # ---------------------------------------------------------------- checkpoints
     def layout(self) -> Dict[str, Any]:

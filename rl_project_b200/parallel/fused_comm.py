@@ -1,0 +1,162 @@
+"""Reduce-scatter of sharded-data-parallel gradients over NVLink peer memory,
+fused with the fp32 cast, the 1/world average, accumulation into the shard
+gradient and the squared-norm partial (kernel: csrc/comm_fused.cu).
+
+The reference reduces FSDP gradients through torch FSDP's NCCL reduce-scatter
+(``src/forgeline/training/common/trainer.py:108-170`` wraps the model in
+``FullyShardedDataParallel``), then casts, averages and clips in separate
+passes.  Here one kernel per unit reads the owned slice of every rank's bf16
+gradient straight out of the peers' memory -- or has the NVSwitch add the
+copies (``multimem.ld_reduce`` through the buffer's multicast address) -- and
+writes the fp32 shard gradient and its squared norm.
+
+Buffers.  A symmetric allocation (``torch.distributed._symmetric_memory``,
+mapped on every GPU of the group) holds ``NSLOTS`` gradient slots of
+``slot_elems`` bf16 each, and a symmetric int32 flag array ``[NSLOTS, world]``.
+Units take slots round-robin by a sequence number ``q`` that every rank
+advances identically (collectives are issued in the same order on all ranks,
+as NCCL requires too); the slot's epoch is ``q // NSLOTS + 1``.
+
+Protocol for unit ``q`` on rank ``r`` (slot ``s = q % NSLOTS``):
+
+1. compute stream: wait for this rank's reduce ``q - LAG`` (an event), then
+   pack the gradients into slot ``s``;
+2. communication stream (after the compute stream): ``signal`` stores the
+   epoch into flag ``[s, r]`` of every rank (release, system scope), then the
+   reduce waits (bounded) until flag ``[s, p] >= epoch`` for every ``p`` and
+   reads slice ``r`` of slot ``s`` from every rank.
+
+Why a slot is never overwritten while a peer still reads it: rank A refills
+slot ``s`` for ``q`` only after A's reduce ``q - 3`` finished, which needed
+peer B's signal ``q - 3``; B issues that signal on its communication stream
+after its reduce ``q - 4`` -- the last reader of slot ``s`` before ``q`` -- has
+finished.  With ``NSLOTS = 4`` and ``LAG = 3`` the compute stream never waits
+on the reduce that was just issued, only on one three units back.
+Conversely B cannot refill slot ``s`` (for ``q + 4``) before A's reduce ``q``
+finished, since that needs A's signal ``q + 1``, issued after A's reduce ``q``.
+
+Every wait in the kernel is bounded by ``timeout_s``; a timeout leaves the
+output untouched and sets a status word that ``check`` raises as
+``DistributedTimeoutError`` (and that turns the gradient norm into NaN, so
+the optimizer skips the step).
+"""
+
+from __future__ import annotations
+
+from typing import Dict, Optional
+
+import torch
+import torch.distributed as dist
+
+from rl_project_b200.core.errors import DistributedConfigError, DistributedTimeoutError
+from rl_project_b200.ops._ext import native
+
+NSLOTS = 4
+LAG = 3
+ALIGN = 8  # elements: a shard is a whole number of 16-byte vectors
+
+
+def available(group=None) -> bool:
+    """True when the group's ranks are CUDA devices of one node that torch symmetric memory can map."""
+    if not (dist.is_available() and dist.is_initialized() and torch.cuda.is_available()):
+        return False
+    if dist.get_backend(group) != "nccl":
+        return False
+    try:
+        import torch.distributed._symmetric_memory  # noqa: F401
+    except ImportError:
+        return False
+    return True
+
+
+class FusedReduceScatter:
+    """Ring of symmetric bf16 gradient slots plus flags; one fused reduce per unit."""
+
+    def __init__(self, group, slot_elems: int, device: torch.device, multicast: str = "auto",
+                 timeout_s: float = 120.0, ctas: int = 32):
+        import torch.distributed._symmetric_memory as symm
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if slot_elems % (ALIGN * self.world):
+            raise DistributedConfigError(f"slot size {slot_elems} is not a multiple of {ALIGN} x world")
+        self.slot_elems = int(slot_elems)
+        self.device = device
+        self.buf = symm.empty(NSLOTS * self.slot_elems, dtype=torch.bfloat16, device=device)
+        self.buf.zero_()
+        self.h = symm.rendezvous(self.buf, group)
+        self.flags = symm.empty(NSLOTS * self.world, dtype=torch.int32, device=device)
+        self.flags.zero_()
+        self.hf = symm.rendezvous(self.flags, group)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)  # every rank's flags are zero before anyone signals
+        bytes_per_slot = self.slot_elems * 2
+        self.ptrs = torch.tensor([[int(self.h.buffer_ptrs[p]) + s * bytes_per_slot for p in range(self.world)]
+                                  for s in range(NSLOTS)], dtype=torch.int64, device=device)
+        self.flag_ptrs = torch.tensor([int(x) for x in self.hf.buffer_ptrs], dtype=torch.int64, device=device)
+        mc = int(getattr(self.h, "multicast_ptr", 0) or 0)
+        if multicast == "off":
+            mc = 0
+        elif multicast == "on" and not mc:
+            raise DistributedConfigError("NVLink multicast was requested but the buffer has no multicast mapping")
+        self.mc = mc
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self._status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self.sumsq = torch.zeros(1, dtype=torch.float32, device=device)
+        self.limit_ns = int(timeout_s * 1e9)
+        self.ctas = int(ctas)
+        self.seq = 0
+        self.events: Dict[int, torch.cuda.Event] = {}
+
+    @property
+    def uses_multicast(self) -> bool:
+        return self.mc != 0
+
+    def next_slot(self, numel: int) -> torch.Tensor:
+        """The slot the next unit packs its gradients into (``numel`` elements), after the compute stream
+        waited for the reduce that last used ... three units back."""
+        if numel > self.slot_elems:
+            raise DistributedConfigError(f"unit of {numel} elements exceeds the slot size {self.slot_elems}")
+        ev = self.events.pop(self.seq - LAG, None)
+        if ev is not None:
+            torch.cuda.current_stream(self.device).wait_event(ev)
+        s = self.seq % NSLOTS
+        return self.buf[s * self.slot_elems: s * self.slot_elems + numel]
+
+    def reduce(self, shard: int, out: torch.Tensor, accumulate: bool, norm: bool,
+               stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Signal the peers that this rank's slot is filled, then reduce slice ``rank`` of it into ``out``
+        (fp32, ``shard`` elements): ``out (+)= sum_p slot_p / world``; squares added to ``sumsq`` if ``norm``."""
+        C = native()
+        q = self.seq
+        s = q % NSLOTS
+        epoch = q // NSLOTS + 1
+        stream = stream or torch.cuda.current_stream(self.device)
+        with torch.cuda.stream(stream):
+            C.signal_peers(self.flag_ptrs, self.rank, s, epoch)
+            mc = self.mc + s * self.slot_elems * 2 if self.mc else 0
+            C.fused_reduce_scatter(self.ptrs[s], mc, self.flags, self.rank, s, epoch, shard, 1.0 / self.world, out,
+                                   accumulate, self.sumsq if norm else None, self.status, self.limit_ns, self.ctas)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+        self.events[q] = ev
+        self.seq += 1
+
+    def reset_norm(self) -> None:
+        self.sumsq.zero_()
+
+    def poll_status(self) -> None:
+        """Queue a copy of the status word to pinned host memory (read by ``check`` after the next sync)."""
+        self._status_host.copy_(self.status, non_blocking=True)
+
+    def check(self) -> None:
+        code = int(self._status_host.item())
+        if code:
+            raise DistributedTimeoutError(
+                f"fused reduce-scatter: a peer's gradient flag did not arrive within the time limit "
+                f"(status 0x{code:x}, slot {code >> 8})",
+                hint="A rank stopped or fell behind; check the other ranks' logs.")
+
+    def close(self) -> None:
+        self.events.clear()

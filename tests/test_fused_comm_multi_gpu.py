@@ -1,0 +1,127 @@
+"""Fused peer-memory reduce-scatter on 2 GPUs (NCCL ranks): the kernel against
+NCCL's reduce_scatter, and FSDP training with fused gradients against the same
+run on NCCL's reduce-scatter."""
+import os
+import tempfile
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from rl_project_b200.parallel.runtime import free_port
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multi_gpu]
+WORLD = 2
+STEPS = 3
+
+
+def _env(rank, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(WORLD),
+                      LOCAL_RANK=str(rank))
+
+
+def _kernel_worker(rank, port, out):
+    import datetime
+
+    import torch.distributed as dist
+
+    from rl_project_b200.parallel.fused_comm import FusedReduceScatter
+
+    _env(rank, port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    res = {}
+    for mc in ("off", "auto"):
+        shard = 1 << 18
+        fr = FusedReduceScatter(None, shard * WORLD, torch.device("cuda", rank), multicast=mc, timeout_s=20.0)
+        errs = []
+        for it in range(6):  # more uses than slots: exercises the ring and its reuse rule
+            g = torch.Generator(device="cuda").manual_seed(100 * it + rank)
+            x = torch.randn(WORLD * shard, device="cuda", generator=g).bfloat16()
+            slot = fr.next_slot(WORLD * shard)
+            slot.copy_(x)
+            outp = torch.empty(shard, device="cuda")
+            fr.reduce(shard, outp, False, True)
+            ref = torch.empty(shard, dtype=torch.float32, device="cuda")
+            dist.reduce_scatter_tensor(ref, x.float())
+            ref /= WORLD
+            errs.append(float((outp - ref).abs().max()))
+        torch.cuda.synchronize()
+        fr.poll_status()
+        torch.cuda.synchronize()
+        fr.check()
+        res[mc] = {"err": max(errs), "multicast": fr.uses_multicast}
+        fr.close()
+        del fr
+    torch.save(res, os.path.join(out, f"k{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_fused_kernel_matches_nccl():
+    with tempfile.TemporaryDirectory() as out:
+        mp.start_processes(_kernel_worker, args=(free_port(), out), nprocs=WORLD, join=True, start_method="spawn")
+        for r in range(WORLD):
+            res = torch.load(os.path.join(out, f"k{r}.pt"))
+            for mc, v in res.items():
+                assert v["err"] < 1e-5, (r, mc, v)
+
+
+def _train_worker(rank, port, out, mode):
+    from rl_project_b200.core.config import ExperimentManifest
+    from rl_project_b200.core.lifecycle import RunContext
+    from rl_project_b200.models.transformer.model import TransformerLM
+    from rl_project_b200.parallel.strategies import build_strategy
+    from rl_project_b200.training.common.trainer import Trainer
+    from rl_project_b200.training.pretrain import PretrainAlgorithm, PretrainConfig
+
+    _env(rank, port)
+    torch.cuda.set_device(rank)
+    m = ExperimentManifest.from_dict({
+        "name": "t", "algorithm": "pretrain", "model_preset": "tiny", "model": {"vocab_size": 128, "block_size": 64},
+        "trainer": {"device": f"cuda:{rank}", "precision": {"dtype": "bfloat16"}, "eval_every": 0, "log_every": 0,
+                    "max_steps": STEPS, "batch_size": 4, "gradient_accumulation_steps": 2,
+                    "optimizer": {"learning_rate": 1e-3, "grad_clip": 0.5},
+                    "schedule": {"name": "constant", "warmup_steps": 0}, "checkpoint": {"save_every": 0}},
+        "distributed": {"strategy": "fsdp", "backend": "nccl", "timeout_s": 60, "fused_comm": mode},
+        "output_dir": os.path.join(out, f"{mode}{rank}")})
+    strat = build_strategy(m.distributed)
+    strat.setup()
+    ctx = RunContext.create(m, metrics_backend="none", distributed=False, device_override=f"cuda:{rank}")
+    torch.manual_seed(0)
+    model = TransformerLM(m.model).to(ctx.device)
+    g = torch.Generator().manual_seed(11 + rank)
+
+    class It:
+        def __iter__(self):
+            return self
+
+        def __next__(self):
+            b = torch.randint(0, 128, (4, 65), generator=g)
+            return b[:, :-1].to(ctx.device), b[:, 1:].to(ctx.device)
+
+    alg = PretrainAlgorithm(model, It(), PretrainConfig(batch_size=4))
+    trainer = Trainer(ctx, alg, strategy=strat)
+    res = [trainer.train_step() for _ in range(STEPS)]
+    fused = strat.fused is not None
+    state = strat.full_state_dict()
+    torch.save({"losses": [r.loss for r in res], "norms": [r.metrics["grad_norm"] for r in res], "state": state,
+                "fused": fused}, os.path.join(out, f"{mode}{rank}.pt"))
+    strat.teardown()
+
+
+def test_fsdp_fused_gradients_match_nccl():
+    with tempfile.TemporaryDirectory() as out:
+        for mode in ("on", "nccl_baseline"):
+            mp.start_processes(_train_worker, args=(free_port(), out, mode), nprocs=WORLD, join=True,
+                               start_method="spawn")
+        a = torch.load(os.path.join(out, "on0.pt"))
+        b = torch.load(os.path.join(out, "nccl_baseline0.pt"))
+    assert a["fused"] and not b["fused"]
+    for x, y in zip(a["losses"], b["losses"]):
+        assert abs(x - y) < 2e-2 * max(1.0, abs(y))
+    for x, y in zip(a["norms"], b["norms"]):
+        assert abs(x - y) < 2e-2 * max(1.0, abs(y))
+    for k, v in b["state"].items():
+        d = (a["state"][k] - v).abs().max().item()
+        assert d < 5e-3, (k, d)
