@@ -56,6 +56,10 @@ def parse_args():
     ap.add_argument("--global-batch", type=int, default=None)
     ap.add_argument("--layers", type=int, default=None, help="override the preset's layer count (smoke runs)")
     ap.add_argument("--grad-ckpt", action="store_true")
+    ap.add_argument("--fused-comm", choices=["auto", "on", "off", "nccl_baseline"], default="auto",
+                    help="FSDP gradient reduce-scatter: fused peer-memory kernel (auto/on) or NCCL")
+    ap.add_argument("--fused-multicast", choices=["off", "on", "symm"], default="off",
+                    help="fused reduce-scatter transport: CUDA IPC peer loads (off) or NVLink multicast (on)")
     return ap.parse_args()
 
 
@@ -198,7 +202,8 @@ def run_ours(args, world, rank, local):
                     "optimizer": {"learning_rate": 3e-4, "grad_clip": 1.0, "weight_decay": 0.1},
                     "schedule": {"name": "constant", "warmup_steps": 0},
                     "checkpoint": {"save_every": 0, "auto_resume": False}},
-        "distributed": {"strategy": strategy_name, "timeout_s": 300},
+        "distributed": {"strategy": strategy_name, "timeout_s": 300, "fused_comm": args.fused_comm,
+                        "fused_multicast": args.fused_multicast},
         "output_dir": os.path.join(tempfile.gettempdir(), f"rlb_bench_{rank}"),
     })
     strategy = build_strategy(manifest.distributed)
@@ -266,7 +271,12 @@ def run_ours(args, world, rank, local):
                    "model_tflops_per_gpu": flops_tok * args.seq * args.batch_per_gpu / (ms / 1e3) / 1e12,
                    "mfu_vs_measured_bf16": (flops_tok * args.seq * args.batch_per_gpu / (ms / 1e3) / 1e12 / peak)
                    if peak else None,
-                   "final_loss": last.loss},
+                   "final_loss": last.loss, "first_loss": trainer.history[0].loss,
+                   "final_grad_norm": last.metrics.get("grad_norm"),
+                   "grad_reduce": ("fused peer-memory reduce-scatter" + (" (NVLink multicast)"
+                                   if getattr(strategy, "fused", None) is not None and strategy.fused.uses_multicast
+                                   else "") if getattr(strategy, "fused", None) is not None
+                                   else ("nccl reduce-scatter" if world > 1 else "none"))},
         "clocks": clk, "e2e": e2e, "gpu_launches": int(launches), "impl": "ours",
     }
     emit(rank, payload)

@@ -4,6 +4,7 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "launchers.h"
@@ -40,6 +41,15 @@ inline void check_bf16(const at::Tensor& t, const char* name) {
 inline void check_contig(const at::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
 }
+// Every tensor a kernel dereferences must live on the device of the tensor that picks the launch device; a
+// host tensor handed to a kernel is an illegal address on the GPU.
+inline void check_dev(const at::Tensor& t, const at::Tensor& ref, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.device() == ref.device(), name, " must be a CUDA tensor on ", ref.device(),
+              ", got ", t.device());
+}
+inline void check_dev(const c10::optional<at::Tensor>& t, const at::Tensor& ref, const char* name) {
+  if (t.has_value()) check_dev(*t, ref, name);
+}
 inline long long* lptr(const at::Tensor& t) { return reinterpret_cast<long long*>(t.data_ptr<int64_t>()); }
 inline const void* opt_ptr(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr() : nullptr; }
 
@@ -48,6 +58,8 @@ std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at:
                                     double eps) {
   check_bf16(x, "x");
   check_bf16(w, "w");
+  check_dev(w, x, "w");
+  check_dev(delta, x, "delta");
   check_contig(x, "x");
   const c10::cuda::CUDAGuard g(x.device());
   const int dim = (int)x.size(-1);
@@ -71,6 +83,9 @@ std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& h, const at::Tensor& w, co
                                     const at::Tensor& dy, const c10::optional<at::Tensor>& dres) {
   check_bf16(h, "h");
   check_bf16(dy, "dy");
+  check_dev(w, h, "w");
+  check_dev(rstd, h, "rstd");
+  check_dev(dy, h, "dy");
   check_contig(h, "h");
   check_contig(dy, "dy");
   const c10::cuda::CUDAGuard g(h.device());
@@ -93,6 +108,9 @@ std::vector<at::Tensor> rope_qkv_fwd(const at::Tensor& qkv, const at::Tensor& co
                                      int64_t Hkv, int64_t D, int64_t pos_offset, bool heads_major) {
   check_bf16(qkv, "qkv");
   TORCH_CHECK(qkv.stride(-1) == 1, "qkv inner stride must be 1");
+  check_dev(cos_t, qkv, "cos");
+  check_dev(sin_t, qkv, "sin");
+  check_dev(positions, qkv, "positions");
   const c10::cuda::CUDAGuard g(qkv.device());
   auto opts = qkv.options();
   at::Tensor q, k, v;
@@ -119,6 +137,11 @@ at::Tensor rope_qkv_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Te
                         int64_t Hq, int64_t Hkv, int64_t D, int64_t pos_offset, bool heads_major) {
   check_bf16(dq, "dq");
   check_contig(dq, "dq");
+  check_dev(dk, dq, "dk");
+  check_dev(dv, dq, "dv");
+  check_dev(cos_t, dq, "cos");
+  check_dev(sin_t, dq, "sin");
+  check_dev(positions, dq, "positions");
   check_contig(dk, "dk");
   check_contig(dv, "dv");
   const c10::cuda::CUDAGuard g(dq.device());
@@ -136,6 +159,9 @@ void rope_inplace(at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_
   // x viewed as [B, T, H, D] with arbitrary outer strides, inner stride 1
   check_bf16(x, "x");
   TORCH_CHECK(x.dim() == 4 && x.stride(3) == 1, "rope_inplace expects [B,T,H,D] with unit inner stride");
+  check_dev(cos_t, x, "cos");
+  check_dev(sin_t, x, "sin");
+  check_dev(positions, x, "positions");
   const c10::cuda::CUDAGuard g(x.device());
   CHECK_OK(rlb_rope_inplace(x.data_ptr(), (int)x.size(0), (int)x.size(1), (int)x.size(2), (int)x.size(3),
                             x.stride(0), x.stride(1), x.stride(2), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
@@ -184,6 +210,8 @@ std::vector<at::Tensor> logprob_fwd(const at::Tensor& logits, const c10::optiona
                                     bool with_entropy, const c10::optional<at::Tensor>& status) {
   check_bf16(logits, "logits");
   TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be [N, V] with unit inner stride");
+  check_dev(targets, logits, "targets");
+  check_dev(status, logits, "status");
   const c10::cuda::CUDAGuard g(logits.device());
   const long long rows = logits.size(0);
   const int V = (int)logits.size(1);
@@ -208,6 +236,11 @@ void logprob_bwd_(at::Tensor& logits, const c10::optional<at::Tensor>& targets, 
                   const c10::optional<at::Tensor>& g_lp, const c10::optional<at::Tensor>& ent,
                   const c10::optional<at::Tensor>& g_ent, double scale) {
   check_bf16(logits, "logits");
+  check_dev(targets, logits, "targets");
+  check_dev(lse, logits, "lse");
+  check_dev(g_lp, logits, "g_lp");
+  check_dev(ent, logits, "ent");
+  check_dev(g_ent, logits, "g_ent");
   const c10::cuda::CUDAGuard g(logits.device());
   CHECK_OK(rlb_logprob_bwd(logits.data_ptr(), logits.stride(0), logits.size(0), (int)logits.size(1),
                            targets.has_value() ? lptr(*targets) : nullptr, lse.data_ptr<float>(),
@@ -220,6 +253,10 @@ void logprob_bwd_(at::Tensor& logits, const c10::optional<at::Tensor>& targets, 
 // ---------------------------------------------------------------- AdamW
 void grad_norm(const at::Tensor& tensors, const at::Tensor& chunks, int64_t nchunks, at::Tensor& partial,
                double max_norm, double inv_scale, at::Tensor& norm_coef, bool squared_only) {
+  check_cuda(partial, "partial");
+  check_dev(tensors, partial, "tensors");
+  check_dev(chunks, partial, "chunks");
+  check_dev(norm_coef, partial, "norm_coef");
   const c10::cuda::CUDAGuard g(partial.device());
   CHECK_OK(rlb_grad_norm(tensors.data_ptr(), chunks.data_ptr(), (int)nchunks, partial.data_ptr<float>(),
                          (int)partial.numel(), (float)max_norm, (float)inv_scale, norm_coef.data_ptr<float>(),
@@ -228,6 +265,7 @@ void grad_norm(const at::Tensor& tensors, const at::Tensor& chunks, int64_t nchu
 }
 
 void grad_norm_finish(at::Tensor& norm_coef, double max_norm, double inv_scale) {
+  check_cuda(norm_coef, "norm_coef");
   const c10::cuda::CUDAGuard g(norm_coef.device());
   CHECK_OK(rlb_grad_norm_finish(norm_coef.data_ptr<float>(), (float)max_norm, (float)inv_scale, cur_stream()),
            "grad_norm_finish");
@@ -236,6 +274,9 @@ void grad_norm_finish(at::Tensor& norm_coef, double max_norm, double inv_scale) 
 void adam_step(const at::Tensor& tensors, const at::Tensor& chunks, int64_t nchunks,
                const c10::optional<at::Tensor>& coef, double lr, double b1, double b2, double eps, int64_t step,
                bool decoupled) {
+  check_cuda(tensors, "tensors");
+  check_dev(chunks, tensors, "chunks");
+  check_dev(coef, tensors, "coef");
   const c10::cuda::CUDAGuard g(tensors.device());
   const int grid = std::min<int64_t>(nchunks, (int64_t)sm_count() * 8);
   CHECK_OK(rlb_adam_step(tensors.data_ptr(), chunks.data_ptr(), (int)nchunks,
@@ -248,6 +289,8 @@ void adam_step(const at::Tensor& tensors, const at::Tensor& chunks, int64_t nchu
 at::Tensor embed_fwd(const at::Tensor& idx, const at::Tensor& W, const c10::optional<at::Tensor>& status) {
   check_bf16(W, "W");
   TORCH_CHECK(idx.scalar_type() == at::kLong && idx.is_contiguous(), "idx must be contiguous int64");
+  check_dev(idx, W, "idx");
+  check_dev(status, W, "status");
   const c10::cuda::CUDAGuard g(W.device());
   auto sizes = idx.sizes().vec();
   sizes.push_back(W.size(1));
@@ -262,6 +305,7 @@ at::Tensor embed_bwd(const at::Tensor& idx, const at::Tensor& dy, int64_t vocab)
   check_bf16(dy, "dy");
   const c10::cuda::CUDAGuard g(dy.device());
   auto flat = idx.reshape({-1});
+  check_dev(idx, dy, "idx");
   auto sorted = at::sort(flat);
   auto ids = std::get<0>(sorted).contiguous();
   auto perm = std::get<1>(sorted).contiguous();
@@ -277,6 +321,8 @@ at::Tensor embed_bwd(const at::Tensor& idx, const at::Tensor& dy, int64_t vocab)
 at::Tensor nf4_dequant(const at::Tensor& packed, const at::Tensor& absmax, const at::Tensor& table, int64_t n,
                        int64_t block, bool bf16) {
   check_cuda(packed, "packed");
+  check_dev(absmax, packed, "absmax");
+  check_dev(table, packed, "table");
   const c10::cuda::CUDAGuard g(packed.device());
   auto out = at::empty({n}, packed.options().dtype(bf16 ? at::kBFloat16 : at::kFloat));
   CHECK_OK(rlb_nf4_dequant(packed.data_ptr(), absmax.data_ptr<float>(), table.data_ptr<float>(), n, (int)block,
@@ -292,6 +338,9 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t a_m
           const c10::optional<at::Tensor>& status) {
   check_bf16(A, "A");
   check_bf16(B, "B");
+  check_dev(B, A, "B");
+  check_dev(out, A, "out");
+  check_dev(status, A, "status");
   check_cuda(out, "out");
   TORCH_CHECK((epi == 0 && out.scalar_type() == at::kBFloat16) || (epi != 0 && out.scalar_type() == at::kFloat),
               "gemm output dtype does not match the epilogue");
@@ -309,6 +358,11 @@ at::Tensor paged_decode(const at::Tensor& q, const at::Tensor& k_pool, const at:
                         double scale, double softcap, int64_t window, const c10::optional<at::Tensor>& status) {
   check_bf16(q, "q");
   check_bf16(k_pool, "k_pool");
+  check_dev(k_pool, q, "k_pool");
+  check_dev(v_pool, q, "v_pool");
+  check_dev(block_tables, q, "block_tables");
+  check_dev(ctx_lens, q, "ctx_lens");
+  check_dev(status, q, "status");
   check_contig(q, "q");
   TORCH_CHECK(block_tables.scalar_type() == at::kInt && ctx_lens.scalar_type() == at::kInt, "int32 tables");
   const c10::cuda::CUDAGuard g(q.device());
@@ -338,6 +392,12 @@ void paged_write(const at::Tensor& k_new, const at::Tensor& v_new, at::Tensor& k
                  const at::Tensor& slot_block, const at::Tensor& slot_off, const c10::optional<at::Tensor>& status) {
   check_bf16(k_new, "k_new");
   check_contig(k_new, "k_new");
+  check_dev(v_new, k_new, "v_new");
+  check_dev(k_pool, k_new, "k_pool");
+  check_dev(v_pool, k_new, "v_pool");
+  check_dev(slot_block, k_new, "slot_block");
+  check_dev(slot_off, k_new, "slot_off");
+  check_dev(status, k_new, "status");
   check_contig(v_new, "v_new");
   const c10::cuda::CUDAGuard g(k_new.device());
   CHECK_OK(rlb_paged_write(k_new.data_ptr(), v_new.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
@@ -363,6 +423,60 @@ std::vector<at::Tensor> sample(const at::Tensor& logits, const at::Tensor& tempe
                       (unsigned long long)seed, lptr(tokens), lp.data_ptr<float>(), cur_stream()),
            "sample");
   return {tokens, lp};
+}
+
+// ---------------------------------------------------------------- peer memory (CUDA IPC, no multicast object)
+// A buffer allocated with cudaMalloc outside torch's caching allocator and rounded up to whole 2 MiB pages, so
+// that the driver gives it pages of its own.  An IPC handle always names a whole allocation, so peer_handle
+// exports the allocation's base (cuMemGetAddressRange) together with the buffer's offset from it, and peer_open
+// adds the offset back: a pointer that is not an allocation base would otherwise map the wrong memory.
+constexpr int64_t kPeerPage = 2 << 20;
+
+at::Tensor peer_alloc(int64_t nbytes, int64_t device) {
+  TORCH_CHECK(nbytes > 0, "peer_alloc: nbytes must be positive");
+  const c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  const int64_t rounded = (nbytes + kPeerPage - 1) / kPeerPage * kPeerPage;
+  void* p = nullptr;
+  CHECK_OK(cudaMalloc(&p, (size_t)rounded), "peer_alloc");
+  CHECK_OK(cudaMemset(p, 0, (size_t)rounded), "peer_alloc memset");
+  CHECK_OK(cudaDeviceSynchronize(), "peer_alloc sync");
+  auto opts = at::TensorOptions().dtype(at::kByte).device(at::kCUDA, (c10::DeviceIndex)device);
+  return torch::from_blob(p, {nbytes}, [device](void* q) {
+    const c10::cuda::CUDAGuard gg((c10::DeviceIndex)device);
+    cudaFree(q);
+  }, opts);
+}
+
+// -> (64-byte handle of the allocation that contains buf, byte offset of buf in it)
+std::tuple<py::bytes, int64_t> peer_handle(const at::Tensor& buf) {
+  check_cuda(buf, "buf");
+  const c10::cuda::CUDAGuard g(buf.device());
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  TORCH_CHECK(cuMemGetAddressRange(&base, &size, (CUdeviceptr)buf.data_ptr()) == CUDA_SUCCESS,
+              "peer_handle: cuMemGetAddressRange failed");
+  const int64_t offset = (int64_t)((CUdeviceptr)buf.data_ptr() - base);
+  TORCH_CHECK(offset >= 0 && (size_t)(offset + buf.nbytes()) <= size, "peer_handle: buffer outside its allocation");
+  cudaIpcMemHandle_t h;
+  CHECK_OK(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)), "peer_handle");
+  return {py::bytes(reinterpret_cast<const char*>(&h), sizeof(h)), offset};
+}
+
+// -> base of the mapping (what peer_close takes); the buffer itself is at base + offset
+int64_t peer_open(const py::bytes& handle, int64_t device) {
+  std::string raw = handle;
+  TORCH_CHECK(raw.size() == sizeof(cudaIpcMemHandle_t), "peer_open: bad handle size");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, raw.data(), sizeof(h));
+  const c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  void* p = nullptr;
+  CHECK_OK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "peer_open");
+  return (int64_t)(uintptr_t)p;
+}
+
+void peer_close(int64_t base, int64_t device) {
+  const c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  CHECK_OK(cudaIpcCloseMemHandle(reinterpret_cast<void*>((uintptr_t)base)), "peer_close");
 }
 
 // ---------------------------------------------------------------- fused reduce-scatter over peer memory
@@ -422,6 +536,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_decode", &paged_decode);
   m.def("paged_write", &paged_write);
   m.def("sample", &sample);
+  m.def("peer_alloc", &peer_alloc);
+  m.def("peer_handle", &peer_handle);
+  m.def("peer_open", &peer_open);
+  m.def("peer_close", &peer_close);
   m.def("signal_peers", &signal_peers);
   m.def("fused_reduce_scatter", &fused_reduce_scatter);
 }

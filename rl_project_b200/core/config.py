@@ -315,6 +315,7 @@ class DistributedConfig:
     context_parallel_size: int = 1
     reshard_after_forward: bool = True
     fused_comm: str = "auto"  # auto | on | off | nccl_baseline
+    fused_multicast: str = "off"  # off (CUDA IPC, peer loads) | on (NVLink multicast reduce) | symm
     timeout_s: float = 600.0
 
     def validate(self) -> None:
@@ -326,6 +327,7 @@ class DistributedConfig:
                "deepspeed strategy requires deepspeed_config path")
         _check(self.fused_comm in ("auto", "on", "off", "nccl_baseline"),
                "fused_comm must be auto|on|off|nccl_baseline")
+        _check(self.fused_multicast in ("off", "on", "symm"), "fused_multicast must be off|on|symm")
         _check(self.pipeline_micro_batches >= 1, "pipeline_micro_batches must be >= 1")
 
 

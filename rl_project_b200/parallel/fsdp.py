@@ -196,6 +196,7 @@ class FSDPStrategy(_ProcessGroupStrategy):
         blocks = [u for u in self.units if u is not self.root] or self.units
         chunk = max(u.shard for u in blocks)
         self.fused = fc.FusedReduceScatter(self.group, chunk * world, device,
+                                           multicast=getattr(self.cfg, "fused_multicast", "off"),
                                            timeout_s=min(float(self.cfg.timeout_s), 300.0))
         for u in self.units:
             u.grad_buf = torch.zeros(u.shard, dtype=torch.float32, device=device)
@@ -391,7 +392,8 @@ class FSDPStrategy(_ProcessGroupStrategy):
 
             opt = FusedAdamW([{"params": masters, "weight_decay": cfg.weight_decay}], lr=cfg.learning_rate,
                              betas=(cfg.beta1, cfg.beta2), eps=cfg.eps, decoupled=(cfg.name == "adamw"),
-                             param16={u.master: u.shard16 for u in self.units}, process_group=self.group,
+                             param16={u.master: u.shard16 for u in self.units},
+                             process_group=self.group if self.group is not None else dist.group.WORLD,
                              segments={u.master: self._segments(u, cfg) for u in self.units},
                              post_step=self.after_optimizer_step)
         else:

@@ -10,9 +10,10 @@ gradient straight out of the peers' memory -- or has the NVSwitch add the
 copies (``multimem.ld_reduce`` through the buffer's multicast address) -- and
 writes the fp32 shard gradient and its squared norm.
 
-Buffers.  A symmetric allocation (``torch.distributed._symmetric_memory``,
-mapped on every GPU of the group) holds ``NSLOTS`` gradient slots of
-``slot_elems`` bf16 each, and a symmetric int32 flag array ``[NSLOTS, world]``.
+Buffers.  A peer-visible allocation (plain cudaMalloc memory mapped into the
+other ranks with CUDA IPC, or torch symmetric memory when the NVLink multicast
+address is wanted) holds ``NSLOTS`` gradient slots of ``slot_elems`` bf16
+each, and a peer-visible int32 flag array ``[NSLOTS, world]``.
 Units take slots round-robin by a sequence number ``q`` that every rank
 advances identically (collectives are issued in the same order on all ranks,
 as NCCL requires too); the slot's epoch is ``q // NSLOTS + 1``.
@@ -57,48 +58,112 @@ ALIGN = 8  # elements: a shard is a whole number of 16-byte vectors
 
 
 def available(group=None) -> bool:
-    """True when the group's ranks are CUDA devices of one node that torch symmetric memory can map."""
+    """True when the group's ranks are NCCL ranks on CUDA devices of this node (peer-mappable memory)."""
     if not (dist.is_available() and dist.is_initialized() and torch.cuda.is_available()):
         return False
     if dist.get_backend(group) != "nccl":
         return False
-    try:
-        import torch.distributed._symmetric_memory  # noqa: F401
-    except ImportError:
-        return False
-    return True
+    import os
+
+    world = dist.get_world_size(group)
+    return int(os.environ.get("LOCAL_WORLD_SIZE", world)) >= world  # torchrun sets it; one node assumed otherwise
+
+
+class _IpcBuffers:
+    """Slots and flags in plain cudaMalloc allocations of whole 2 MiB pages, mapped into every peer with CUDA
+    IPC (no multicast object is bound to them, so only peer loads are possible).  A handle names the whole
+    allocation; each rank sends its buffer's offset in it along with the handle."""
+
+    def __init__(self, group, nbytes_buf: int, nbytes_flags: int, device: torch.device):
+        C = native()
+        self.device = device
+        dev = device.index if device.index is not None else torch.cuda.current_device()
+        self.dev = dev
+        self.buf_raw = C.peer_alloc(nbytes_buf, dev)
+        self.flags_raw = C.peer_alloc(nbytes_flags, dev)
+        mine = (C.peer_handle(self.buf_raw), C.peer_handle(self.flags_raw))
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        handles: list = [None] * world
+        dist.all_gather_object(handles, mine, group=group)
+        self.opened = []
+        self.buffer_ptrs, self.flag_ptrs = [], []
+        for p, ((hb, ob), (hf, of)) in enumerate(handles):
+            if p == rank:
+                self.buffer_ptrs.append(self.buf_raw.data_ptr())
+                self.flag_ptrs.append(self.flags_raw.data_ptr())
+            else:
+                pb, pf = C.peer_open(hb, dev), C.peer_open(hf, dev)  # mapping bases; buffers sit at an offset
+                self.opened += [pb, pf]
+                self.buffer_ptrs.append(pb + ob)
+                self.flag_ptrs.append(pf + of)
+        for ptr in self.buffer_ptrs + self.flag_ptrs:
+            if ptr % 16:
+                raise DistributedConfigError(f"peer buffer at 0x{ptr:x} is not 16-byte aligned")
+        self.multicast_ptr = 0
+        self.group = group
+
+    def close(self) -> None:
+        C = native()
+        torch.cuda.synchronize(self.device)
+        for ptr in self.opened:
+            C.peer_close(ptr, self.dev)
+        self.opened = []
+        dist.barrier(group=self.group)  # no peer maps this rank's buffers any more
+
+
+class _SymmBuffers:
+    """Slots and flags in torch symmetric memory (with an NVLink multicast mapping when the node has one)."""
+
+    def __init__(self, group, nbytes_buf: int, nbytes_flags: int, device: torch.device):
+        import torch.distributed._symmetric_memory as symm
+
+        self.buf_raw = symm.empty(nbytes_buf, dtype=torch.uint8, device=device)
+        self.buf_raw.zero_()
+        self.h = symm.rendezvous(self.buf_raw, group)
+        self.flags_raw = symm.empty(nbytes_flags, dtype=torch.uint8, device=device)
+        self.flags_raw.zero_()
+        self.hf = symm.rendezvous(self.flags_raw, group)
+        self.buffer_ptrs = [int(x) for x in self.h.buffer_ptrs]
+        self.flag_ptrs = [int(x) for x in self.hf.buffer_ptrs]
+        self.multicast_ptr = int(getattr(self.h, "multicast_ptr", 0) or 0)
+        self.group = group
+        self.device = device
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
 
 
 class FusedReduceScatter:
-    """Ring of symmetric bf16 gradient slots plus flags; one fused reduce per unit."""
+    """Ring of peer-visible bf16 gradient slots plus flags; one fused reduce per unit.
 
-    def __init__(self, group, slot_elems: int, device: torch.device, multicast: str = "auto",
+    ``multicast``: ``off`` (default) maps the peers' buffers with CUDA IPC and sums with peer loads; ``on``
+    allocates torch symmetric memory and sums through its NVLink multicast address (``multimem.ld_reduce``);
+    ``symm`` uses symmetric memory with peer loads."""
+
+    def __init__(self, group, slot_elems: int, device: torch.device, multicast: str = "off",
                  timeout_s: float = 120.0, ctas: int = 32):
-        import torch.distributed._symmetric_memory as symm
-
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if slot_elems % (ALIGN * self.world):
             raise DistributedConfigError(f"slot size {slot_elems} is not a multiple of {ALIGN} x world")
+        if multicast not in ("off", "on", "symm"):
+            raise DistributedConfigError(f"multicast must be off|on|symm, got {multicast!r}")
         self.slot_elems = int(slot_elems)
         self.device = device
-        self.buf = symm.empty(NSLOTS * self.slot_elems, dtype=torch.bfloat16, device=device)
-        self.buf.zero_()
-        self.h = symm.rendezvous(self.buf, group)
-        self.flags = symm.empty(NSLOTS * self.world, dtype=torch.int32, device=device)
-        self.flags.zero_()
-        self.hf = symm.rendezvous(self.flags, group)
+        nb, nf = NSLOTS * self.slot_elems * 2, NSLOTS * self.world * 4
+        self.mem = _IpcBuffers(group, nb, nf, device) if multicast == "off" else _SymmBuffers(group, nb, nf, device)
+        self.buf = self.mem.buf_raw.view(torch.bfloat16)
+        self.flags = self.mem.flags_raw.view(torch.int32)
         torch.cuda.synchronize(device)
         dist.barrier(group=group)  # every rank's flags are zero before anyone signals
         bytes_per_slot = self.slot_elems * 2
-        self.ptrs = torch.tensor([[int(self.h.buffer_ptrs[p]) + s * bytes_per_slot for p in range(self.world)]
+        self.ptrs = torch.tensor([[self.mem.buffer_ptrs[p] + s * bytes_per_slot for p in range(self.world)]
                                   for s in range(NSLOTS)], dtype=torch.int64, device=device)
-        self.flag_ptrs = torch.tensor([int(x) for x in self.hf.buffer_ptrs], dtype=torch.int64, device=device)
-        mc = int(getattr(self.h, "multicast_ptr", 0) or 0)
-        if multicast == "off":
-            mc = 0
-        elif multicast == "on" and not mc:
+        self.flag_ptrs = torch.tensor(self.mem.flag_ptrs, dtype=torch.int64, device=device)
+        mc = self.mem.multicast_ptr if multicast == "on" else 0
+        if multicast == "on" and not mc:
             raise DistributedConfigError("NVLink multicast was requested but the buffer has no multicast mapping")
         self.mc = mc
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
@@ -114,8 +179,8 @@ class FusedReduceScatter:
         return self.mc != 0
 
     def next_slot(self, numel: int) -> torch.Tensor:
-        """The slot the next unit packs its gradients into (``numel`` elements), after the compute stream
-        waited for the reduce that last used ... three units back."""
+        """The slot the next unit packs its gradients into (``numel`` elements), after the current stream
+        waited for this rank's reduce ``LAG`` units back."""
         if numel > self.slot_elems:
             raise DistributedConfigError(f"unit of {numel} elements exceeds the slot size {self.slot_elems}")
         ev = self.events.pop(self.seq - LAG, None)
@@ -128,6 +193,9 @@ class FusedReduceScatter:
                stream: Optional[torch.cuda.Stream] = None) -> None:
         """Signal the peers that this rank's slot is filled, then reduce slice ``rank`` of it into ``out``
         (fp32, ``shard`` elements): ``out (+)= sum_p slot_p / world``; squares added to ``sumsq`` if ``norm``."""
+        if shard % ALIGN or shard * self.world > self.slot_elems or out.numel() != shard:
+            raise DistributedConfigError(f"fused reduce of {shard} x {self.world} elements does not fit the slot "
+                                         f"({self.slot_elems}) or the output ({out.numel()})")
         C = native()
         q = self.seq
         s = q % NSLOTS
@@ -159,4 +227,8 @@ class FusedReduceScatter:
                 hint="A rank stopped or fell behind; check the other ranks' logs.")
 
     def close(self) -> None:
+        """Collective: unmap the peers' buffers on every rank before any rank frees its own."""
         self.events.clear()
+        if self.mem is not None:
+            self.mem.close()
+            self.mem = None
