@@ -16,7 +16,8 @@
 // output and no separate cast / scale / accumulate / norm kernels.
 //
 // Waits are bounded: a flag that does not arrive within the time limit sets
-// `status` (kTimeout | slot << 8) and the kernel returns without writing.
+// `status` (kTimeout | slot << 8); the data kernel then returns without
+// writing, as does every later reduce until the caller clears the status.
 // Slot reuse is made safe by the caller's ordering (one communication stream,
 // a ring of slots, and the rule that a slot is refilled only after this rank's
 // reduce three uses back finished): the ordering argument is in
@@ -99,17 +100,25 @@ RLB_DEVICE void add8(const uint4& raw, float* acc) {
   for (int k = 0; k < 8; ++k) acc[k] += f[k];
 }
 
-constexpr int kRsThreads = 512;
-constexpr int kRsUnroll = 2;
+// One thread waits (bounded) for every peer's flag; the data kernel that follows in the stream starts only
+// once the wait kernel has returned, so no SM is held by spinning CTAs while a peer is still computing.
+__global__ void wait_peers_kernel(const int* __restrict__ my_flags, int world, int slot, int epoch,
+                                  unsigned long long limit_ns, int* status) {
+  if (threadIdx.x == 0) wait_flags(my_flags, world, slot, epoch, limit_ns, status);
+}
+
+constexpr int kRsThreads = 256;
+constexpr int kRsUnroll = 4;
 
 template <bool MULTIMEM>
 __global__ void __launch_bounds__(kRsThreads) fused_rs_kernel(
-    const unsigned long long* __restrict__ buf_ptrs, unsigned long long mc_base, const int* __restrict__ my_flags,
-    int world, int rank, int slot, int epoch, long long shard, float scale, float* __restrict__ out, int accumulate,
-    float* __restrict__ sumsq, int* status, unsigned long long limit_ns) {
+    const unsigned long long* __restrict__ buf_ptrs, unsigned long long mc_base, int world, int rank,
+    long long shard, float scale, float* __restrict__ out, int accumulate, float* __restrict__ sumsq,
+    const int* status) {
   __shared__ int ok;
   __shared__ float red[kRsThreads / 32];
-  if (threadIdx.x == 0) ok = wait_flags(my_flags, world, slot, epoch, limit_ns, status) ? 1 : 0;
+  // a failed wait (this launch's or an earlier one's) leaves every later reduce of the step undone
+  if (threadIdx.x == 0) ok = *reinterpret_cast<const volatile int*>(status) == 0;
   __syncthreads();
   if (!ok) return;
   const long long lo = (long long)rank * shard;
@@ -118,25 +127,40 @@ __global__ void __launch_bounds__(kRsThreads) fused_rs_kernel(
   float sq = 0.f;
   for (long long v0 = (long long)blockIdx.x * kRsThreads + threadIdx.x; v0 < nvec; v0 += stride * kRsUnroll) {
     float acc[kRsUnroll][8];
+    if constexpr (MULTIMEM) {
 #pragma unroll
-    for (int u = 0; u < kRsUnroll; ++u) {
-      const long long v = v0 + u * stride;
+      for (int u = 0; u < kRsUnroll; ++u) {
+        const long long v = v0 + u * stride;
+        if (v < nvec) {
+          multimem_sum8(reinterpret_cast<const __nv_bfloat16*>(mc_base) + lo + v * 8, acc[u]);
+        } else {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) acc[u][k] = 0.f;
-      if (v >= nvec) continue;
-      const long long e = lo + v * 8;
-      if constexpr (MULTIMEM) {
-        multimem_sum8(reinterpret_cast<const __nv_bfloat16*>(mc_base) + e, acc[u]);
-      } else {
-        // up to 8 peers' loads in flight before the first add, any further peers one by one
-        uint4 raw[8];
+          for (int k = 0; k < 8; ++k) acc[u][k] = 0.f;
+        }
+      }
+    } else {
 #pragma unroll
-        for (int p = 0; p < 8; ++p)
-          if (p < world) raw[p] = ld16(reinterpret_cast<const __nv_bfloat16*>(buf_ptrs[p]) + e);
+      for (int u = 0; u < kRsUnroll; ++u)
 #pragma unroll
-        for (int p = 0; p < 8; ++p)
-          if (p < world) add8(raw[p], acc[u]);
-        for (int p = 8; p < world; ++p) add8(ld16(reinterpret_cast<const __nv_bfloat16*>(buf_ptrs[p]) + e), acc[u]);
+        for (int k = 0; k < 8; ++k) acc[u][k] = 0.f;
+      // peers in pairs: 2 x kRsUnroll 16-byte loads in flight per thread before the adds
+      for (int p0 = 0; p0 < world; p0 += 2) {
+        uint4 raw[2][kRsUnroll];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int p = p0 + j;
+          const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(buf_ptrs[p < world ? p : p0]) + lo;
+#pragma unroll
+          for (int u = 0; u < kRsUnroll; ++u) {
+            const long long v = v0 + u * stride;
+            if (p < world && v < nvec) raw[j][u] = ld16(src + v * 8);
+            else raw[j][u] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int u = 0; u < kRsUnroll; ++u) add8(raw[j][u], acc[u]);
       }
     }
 #pragma unroll
@@ -178,15 +202,17 @@ cudaError_t rlb_fused_reduce_scatter(const unsigned long long* buf_ptrs, unsigne
                                      float scale, float* out, int accumulate, float* sumsq, int* status,
                                      unsigned long long limit_ns, int ctas, cudaStream_t s) {
   if (shard % 8 != 0 || world < 1 || world > 32 || ctas < 1) return cudaErrorInvalidValue;
+  wait_peers_kernel<<<1, 32, 0, s>>>(my_flags, world, slot, epoch, limit_ns, status);
   const long long nvec = shard / 8;
-  long long grid = (nvec + (long long)kRsThreads * kRsUnroll - 1) / ((long long)kRsThreads * kRsUnroll);
+  const long long per_cta = (long long)kRsThreads * kRsUnroll;
+  long long grid = (nvec + per_cta - 1) / per_cta;
   if (grid > ctas) grid = ctas;
   if (grid < 1) grid = 1;
   if (mc_base)
-    fused_rs_kernel<true><<<(int)grid, kRsThreads, 0, s>>>(buf_ptrs, mc_base, my_flags, world, rank, slot, epoch,
-                                                           shard, scale, out, accumulate, sumsq, status, limit_ns);
+    fused_rs_kernel<true><<<(int)grid, kRsThreads, 0, s>>>(buf_ptrs, mc_base, world, rank, shard, scale, out,
+                                                           accumulate, sumsq, status);
   else
-    fused_rs_kernel<false><<<(int)grid, kRsThreads, 0, s>>>(buf_ptrs, mc_base, my_flags, world, rank, slot, epoch,
-                                                            shard, scale, out, accumulate, sumsq, status, limit_ns);
+    fused_rs_kernel<false><<<(int)grid, kRsThreads, 0, s>>>(buf_ptrs, mc_base, world, rank, shard, scale, out,
+                                                            accumulate, sumsq, status);
   return cudaGetLastError();
 }

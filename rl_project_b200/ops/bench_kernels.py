@@ -165,6 +165,34 @@ def bench_sample(rows: int = 512, V: int = 128256):
                           torch.softmax(x.float(), -1), 1)), 4)}), flush=True)
 
 
+def bench_fused_rs(world: int = 8, shard_mib: int = 32):
+    """Fused reduce-scatter kernel on one GPU with ``world`` emulated ranks (local buffers in the pointer
+    table, every flag raised before the launch).  Bytes = world bf16 shards read + one fp32 shard written:
+    the HBM-side cost of the kernel; the NVLink-side figure comes from rl_project_b200.benchmarks.comm."""
+    from rl_project_b200.ops._ext import native
+
+    C = native()
+    _, peak_gbs = _peaks()
+    shard = (shard_mib << 20) // 2
+    bufs = [torch.randn(world * shard, device="cuda").to(torch.bfloat16) for _ in range(world)]
+    flags = torch.zeros(world, dtype=torch.int32, device="cuda")
+    fptrs = torch.tensor([flags.data_ptr()] * world, dtype=torch.int64, device="cuda")
+    for r in range(world):
+        C.signal_peers(fptrs, r, 0, 1)
+    ptrs = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
+    out = torch.empty(shard, device="cuda")
+    sq = torch.zeros(1, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for ctas in (32, 148, 296):
+        ms = time_ms(lambda: C.fused_reduce_scatter(ptrs, 0, flags, 0, 0, 1, shard, 1.0 / world, out, False, sq,
+                                                    status, int(5e9), ctas))
+        moved = world * shard * 2 + shard * 4
+        print(json.dumps({"kernel": "fused_reduce_scatter (emulated ranks, peer loads)", "world": world,
+                          "shard_elems": shard, "ctas": ctas, "ms": round(ms, 4), "gbs": round(moved / ms / 1e6, 1),
+                          "frac_of_measured_hbm": round(moved / ms / 1e6 / peak_gbs, 3)}), flush=True)
+    assert int(status.item()) == 0
+
+
 MODEL_SHAPES = [
     (32768, 3072, 2048, "nt"), (32768, 2048, 2048, "nt"), (32768, 16384, 2048, "nt"), (32768, 2048, 8192, "nt"),
     (32768, 2048, 16384, "nn"), (32768, 8192, 2048, "nn"), (16384, 2048, 32768, "tn"), (2048, 8192, 32768, "tn"),
@@ -188,6 +216,8 @@ def main():
         bench_memory_bound()
     if "adam" in which:
         bench_adam()
+    if "rs" in which:
+        bench_fused_rs()
 
 
 if __name__ == "__main__":

@@ -117,6 +117,7 @@ class _SymmBuffers:
     def __init__(self, group, nbytes_buf: int, nbytes_flags: int, device: torch.device):
         import torch.distributed._symmetric_memory as symm
 
+        group = group if group is not None else dist.group.WORLD
         self.buf_raw = symm.empty(nbytes_buf, dtype=torch.uint8, device=device)
         self.buf_raw.zero_()
         self.h = symm.rendezvous(self.buf_raw, group)
