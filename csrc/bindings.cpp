@@ -351,6 +351,34 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t a_m
            "gemm");
 }
 
+// Grouped GEMM (mixture-of-experts): see rlb_gemm_grouped for the two modes.
+void gemm_grouped(int64_t mode, int64_t b_mn, int64_t epi, const at::Tensor& A, const at::Tensor& B, at::Tensor& out,
+                  int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, double alpha,
+                  int64_t groups, const c10::optional<at::Tensor>& tile_group,
+                  const c10::optional<at::Tensor>& k_begin, const c10::optional<at::Tensor>& k_len, int64_t k_total,
+                  const c10::optional<at::Tensor>& status) {
+  check_bf16(A, "A");
+  check_bf16(B, "B");
+  check_dev(B, A, "B");
+  check_dev(out, A, "out");
+  check_dev(tile_group, A, "tile_group");
+  check_dev(k_begin, A, "k_begin");
+  check_dev(k_len, A, "k_len");
+  check_dev(status, A, "status");
+  for (const auto* t : {&tile_group, &k_begin, &k_len})
+    if (t->has_value()) TORCH_CHECK((*t)->scalar_type() == at::kInt && (*t)->is_contiguous(), "int32 tables");
+  TORCH_CHECK((epi == 0 && out.scalar_type() == at::kBFloat16) || (epi != 0 && out.scalar_type() == at::kFloat),
+              "gemm_grouped output dtype does not match the epilogue");
+  const c10::cuda::CUDAGuard g(A.device());
+  CHECK_OK(rlb_gemm_grouped((int)mode, (int)b_mn, (int)epi, (int)M, (int)N, (int)K, A.data_ptr(), lda, B.data_ptr(),
+                            ldb, out.data_ptr(), ldc, (float)alpha, (int)groups,
+                            tile_group.has_value() ? tile_group->data_ptr<int>() : nullptr,
+                            k_begin.has_value() ? k_begin->data_ptr<int>() : nullptr,
+                            k_len.has_value() ? k_len->data_ptr<int>() : nullptr, k_total,
+                            status.has_value() ? status->data_ptr<int>() : nullptr, sm_count(), cur_stream()),
+           "gemm_grouped");
+}
+
 // ---------------------------------------------------------------- paged KV decode
 // q [B, Hq, D]; pools [num_blocks, Hkv, 16, D]; block_tables [B, max_blocks] int32; ctx_lens [B] int32
 at::Tensor paged_decode(const at::Tensor& q, const at::Tensor& k_pool, const at::Tensor& v_pool,
@@ -533,6 +561,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_bwd", &embed_bwd);
   m.def("nf4_dequant", &nf4_dequant);
   m.def("gemm", &gemm);
+  m.def("gemm_grouped", &gemm_grouped);
   m.def("paged_decode", &paged_decode);
   m.def("paged_write", &paged_write);
   m.def("sample", &sample);

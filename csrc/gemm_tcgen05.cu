@@ -43,7 +43,49 @@ struct Params {
   long long ldc;
   float alpha;
   int* status;
+  // grouped problems (one launch for every expert of an MoE layer)
+  int mode;               // kPlain, kGroupM or kGroupK
+  const int* tile_group;  // kGroupM: group of each BM-row tile of A and C (-1: tile unused, skipped)
+  int b_group_rows;       // kGroupM: rows of B's tensor map per group (N if B is [N][K], K if [K][N])
+  const int* k_begin;     // kGroupK: first reduction row of each group
+  const int* k_len;       // kGroupK: reduction rows of each group (a multiple of BK; 0 gives a zero tile)
+  int groups;             // kGroupK: number of groups; group g's C starts at C + g * M * ldc
 };
+
+// kGroupM: C rows are grouped in BM-row tiles, each tile multiplies with its group's B.
+// kGroupK: each group reduces over its own range of rows of A and B (weight gradients per expert).
+enum Mode : int { kPlain = 0, kGroupM = 1, kGroupK = 2 };
+
+struct Tile {
+  int m0, n0;
+  int g;       // group (0 for plain)
+  int kfirst;  // first reduction element
+  int nk;      // BK steps (0: nothing to multiply)
+  bool skip;   // kGroupM tile of unused rows
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m, int& n);
+
+__device__ __forceinline__ Tile tile_at(const Params& p, int t, int num_m, int num_n, int nk) {
+  Tile r{0, 0, 0, 0, nk, false};
+  int tm, tn;
+  if (p.mode == kGroupK) {
+    const int per = num_m * num_n;
+    r.g = t / per;
+    tile_coords(t % per, num_m, num_n, tm, tn);
+    r.kfirst = p.k_begin[r.g];
+    r.nk = p.k_len[r.g] / BK;
+  } else {
+    tile_coords(t, num_m, num_n, tm, tn);
+    if (p.mode == kGroupM) {
+      r.g = p.tile_group[tm];
+      r.skip = r.g < 0;
+    }
+  }
+  r.m0 = tm * BM;
+  r.n0 = tn * BN;
+  return r;
+}
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m, int& n) {
   const int per_group = GROUP_M * num_n;
@@ -76,7 +118,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
+  const int num_tiles = num_m * num_n * (p.mode == kGroupK ? p.groups : 1);
   const int nk = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -108,10 +150,13 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
-        int tm, tn;
-        tile_coords(t, num_m, num_n, tm, tn);
-        const int m0 = tm * BM, n0 = tn * BN;
-        for (int kb = 0; kb < nk; ++kb) {
+        const Tile tl = tile_at(p, t, num_m, num_n, nk);
+        if (tl.skip) continue;
+        const int m0 = tl.m0;
+        // B rows of this tile's group: along N for [N][K] storage, along K for [K][N]
+        const int n0 = tl.n0 + (p.mode == kGroupM && !B_MN ? tl.g * p.b_group_rows : 0);
+        const int kb_off = (p.mode == kGroupM && B_MN) ? tl.g * p.b_group_rows : 0;
+        for (int kb = 0; kb < tl.nk; ++kb) {
           if (!sm100::mbar_wait_bounded(&empty[stage], phase ^ 1, WAIT_LIMIT)) {
             fail(p.status, abort_flag, 1);
             break;
@@ -119,7 +164,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
           sm100::mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
           uint8_t* a = sA + stage * A_BYTES;
           uint8_t* b = sB + stage * B_BYTES;
-          const int k0 = kb * BK;
+          const int k0 = tl.kfirst + kb * BK;
           if (A_MN) {
 #pragma unroll
             for (int h = 0; h < BM / 64; ++h) sm100::tma_load_2d(a + h * (BK * 128), &tma_a, &full[stage], m0 + 64 * h, k0);
@@ -128,7 +173,8 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
           }
           if (B_MN) {
 #pragma unroll
-            for (int h = 0; h < BN / 64; ++h) sm100::tma_load_2d(b + h * (BK * 128), &tma_b, &full[stage], n0 + 64 * h, k0);
+            for (int h = 0; h < BN / 64; ++h)
+              sm100::tma_load_2d(b + h * (BK * 128), &tma_b, &full[stage], n0 + 64 * h, k0 + kb_off);
           } else {
             sm100::tma_load_2d(b, &tma_b, &full[stage], k0, n0);
           }
@@ -148,6 +194,8 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        const Tile tl = tile_at(p, t, num_m, num_n, nk);
+        if (tl.skip || tl.nk == 0) continue;  // no accumulator used (the epilogue skips or zero-fills)
         if (!sm100::mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, WAIT_LIMIT)) {
           fail(p.status, abort_flag, 2);
           break;
@@ -155,7 +203,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
         sm100::tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
         bool dead = false;
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = 0; kb < tl.nk; ++kb) {
           if (!sm100::mbar_wait_bounded(&full[stage], phase, WAIT_LIMIT)) {
             fail(p.status, abort_flag, 3);
             dead = true;
@@ -194,15 +242,26 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
-      int tm, tn;
-      tile_coords(t, num_m, num_n, tm, tn);
-      const int m0 = tm * BM, n0 = tn * BN;
+      const Tile tl = tile_at(p, t, num_m, num_n, nk);
+      if (tl.skip) continue;
+      const int m0 = tl.m0, n0 = tl.n0;
+      const int row = m0 + q * 32 + lane;
+      const long long c_off = p.mode == kGroupK ? (long long)tl.g * p.M * p.ldc : 0;
+      if (tl.nk == 0) {
+        // empty reduction (an expert without tokens): the product is zero
+        if (EPI != kAccumF32 && row < p.M) {
+          for (int col = n0; col < n0 + BN && col < p.N; ++col) {
+            if (EPI == kStoreBF16) ((__nv_bfloat16*)p.C)[c_off + (long long)row * p.ldc + col] = __float2bfloat16(0.f);
+            else ((float*)p.C)[c_off + (long long)row * p.ldc + col] = 0.f;
+          }
+        }
+        continue;
+      }
       if (!sm100::mbar_wait_bounded(&tfull[acc], acc_phase, WAIT_LIMIT)) {
         fail(p.status, abort_flag, 4);
         break;
       }
       sm100::tc_fence_after();
-      const int row = m0 + q * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -212,7 +271,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
         const int col0 = n0 + c * 32;
         if (row < p.M && col0 < p.N) {
           if (EPI == kStoreBF16) {
-            __nv_bfloat16* out = (__nv_bfloat16*)p.C + (long long)row * p.ldc + col0;
+            __nv_bfloat16* out = (__nv_bfloat16*)p.C + c_off + (long long)row * p.ldc + col0;
             if (col0 + 32 <= p.N) {
 #pragma unroll
               for (int v = 0; v < 4; ++v) {
@@ -232,7 +291,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
                 if (col0 + e < p.N) out[e] = __float2bfloat16(__uint_as_float(r[e]) * p.alpha);
             }
           } else {
-            float* out = (float*)p.C + (long long)row * p.ldc + col0;
+            float* out = (float*)p.C + c_off + (long long)row * p.ldc + col0;
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               if (col0 + e < p.N) {
@@ -294,18 +353,21 @@ static bool make_map(CUtensorMap* m, const void* ptr, long long rows, long long 
 
 template <int A_MN, int B_MN, int EPI>
 static cudaError_t launch(const void* A, long long lda, const void* B, long long ldb, const Params& p, int sms,
-                          cudaStream_t s) {
+                          cudaStream_t s, long long a_rows = 0, long long b_rows = 0) {
   CUtensorMap ma, mb;
-  // A_MN: memory [K][M] (box 64 m x 64 k); else [M][K] (box 64 k x 128 m)
-  const bool ok_a = A_MN ? make_map(&ma, A, p.K, p.M, lda, BK) : make_map(&ma, A, p.M, p.K, lda, BM);
-  const bool ok_b = B_MN ? make_map(&mb, B, p.K, p.N, ldb, BK) : make_map(&mb, B, p.N, p.K, ldb, BN);
+  // A_MN: memory [K][M] (box 64 m x 64 k); else [M][K] (box 64 k x 128 m).  a_rows / b_rows override the
+  // row extent of a map (grouped operands span every group's rows).
+  const long long ar = a_rows ? a_rows : (A_MN ? p.K : p.M);
+  const long long br = b_rows ? b_rows : (B_MN ? p.K : p.N);
+  const bool ok_a = A_MN ? make_map(&ma, A, ar, p.M, lda, BK) : make_map(&ma, A, ar, p.K, lda, BM);
+  const bool ok_b = B_MN ? make_map(&mb, B, br, p.N, ldb, BK) : make_map(&mb, B, br, p.K, ldb, BN);
   if (!ok_a || !ok_b) return cudaErrorInvalidResourceHandle;  // tensor-map encoding rejected the operand
   auto k = gemm_kernel<A_MN, B_MN, EPI>;
   // (per launch: the attribute is cheap to set and the caller may be any host thread)
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) return e;
   (void)cudaGetLastError();  // drop a stale, non-sticky error left by unrelated calls on this thread
-  const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+  const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN) * (p.mode == kGroupK ? p.groups : 1);
   const int grid = tiles < sms ? tiles : sms;
   k<<<grid, 192, SMEM_BYTES, s>>>(ma, mb, p);
   return cudaGetLastError();
@@ -322,7 +384,7 @@ cudaError_t rlb_gemm(int a_mn, int b_mn, int epi, int M, int N, int K, const voi
   if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
   if ((lda % 8) || (ldb % 8)) return cudaErrorInvalidPitchValue;
   if ((((uintptr_t)A) & 15) || (((uintptr_t)B) & 15)) return cudaErrorInvalidDevicePointer;
-  Params p{M, N, K, C, ldc, alpha, status};
+  Params p{M, N, K, C, ldc, alpha, status, kPlain, nullptr, 0, nullptr, nullptr, 0};
 #define RLB_GEMM_CASE(AM, BMN, E) \
   if (a_mn == AM && b_mn == BMN && epi == E) return launch<AM, BMN, E>(A, lda, B, ldb, p, sms, s);
   RLB_GEMM_CASE(0, 0, 0)
@@ -334,4 +396,38 @@ cudaError_t rlb_gemm(int a_mn, int b_mn, int epi, int M, int N, int K, const voi
   RLB_GEMM_CASE(0, 0, 2)
 #undef RLB_GEMM_CASE
   return cudaErrorNotSupported;
+}
+
+// Grouped GEMMs for mixture-of-experts layers (one launch per layer and pass).
+//   mode 1 (M-grouped): rows of A / C are tokens sorted by expert with every expert's segment padded to a
+//     multiple of 128 rows; tile_group[i] is the expert of rows [128 i, 128 i + 128) (-1: unused, skipped).
+//     b_mn = 0: B holds groups x [N][K] (x W_e^T, forward);  b_mn = 1: B holds groups x [K][N] (dy W_e,
+//     input gradient; K must then be a multiple of 64).  C is [M][N].
+//   mode 2 (K-grouped): A [K_total][M] and B [K_total][N] (both MN-major); group g reduces rows
+//     [k_begin[g], k_begin[g] + k_len[g]) (k_len a multiple of 64) into C_g = C + g M ldc (weight gradients).
+cudaError_t rlb_gemm_grouped(int mode, int b_mn, int epi, int M, int N, int K, const void* A, long long lda,
+                             const void* B, long long ldb, void* C, long long ldc, float alpha, int groups,
+                             const int* tile_group, const int* k_begin, const int* k_len, long long k_total,
+                             int* status, int sms, cudaStream_t s) {
+  using namespace gemm;
+  if (M <= 0 || N <= 0 || K <= 0 || groups <= 0) return cudaSuccess;
+  if ((lda % 8) || (ldb % 8)) return cudaErrorInvalidPitchValue;
+  if ((((uintptr_t)A) & 15) || (((uintptr_t)B) & 15)) return cudaErrorInvalidDevicePointer;
+  if (mode == kGroupM) {
+    if (!tile_group || (b_mn && K % BK)) return cudaErrorInvalidValue;
+    Params p{M, N, K, C, ldc, alpha, status, kGroupM, tile_group, b_mn ? K : N, nullptr, nullptr, 0};
+    const long long brows = (long long)groups * (b_mn ? K : N);
+    if (b_mn == 0 && epi == kStoreBF16) return launch<0, 0, kStoreBF16>(A, lda, B, ldb, p, sms, s, 0, brows);
+    if (b_mn == 1 && epi == kStoreBF16) return launch<0, 1, kStoreBF16>(A, lda, B, ldb, p, sms, s, 0, brows);
+    return cudaErrorNotSupported;
+  }
+  if (mode == kGroupK) {
+    if (!k_begin || !k_len || k_total <= 0) return cudaErrorInvalidValue;
+    Params p{M, N, K, C, ldc, alpha, status, kGroupK, nullptr, 0, k_begin, k_len, groups};
+    if (epi == kStoreBF16) return launch<1, 1, kStoreBF16>(A, lda, B, ldb, p, sms, s, k_total, k_total);
+    if (epi == kStoreF32) return launch<1, 1, kStoreF32>(A, lda, B, ldb, p, sms, s, k_total, k_total);
+    if (epi == kAccumF32) return launch<1, 1, kAccumF32>(A, lda, B, ldb, p, sms, s, k_total, k_total);
+    return cudaErrorNotSupported;
+  }
+  return cudaErrorInvalidValue;
 }

@@ -50,6 +50,11 @@ cudaError_t rlb_nf4_dequant(const void* packed, const float* absmax, const float
 cudaError_t rlb_gemm(int a_mn, int b_mn, int epi, int M, int N, int K, const void* A, long long lda, const void* B,
                      long long ldb, void* C, long long ldc, float alpha, int* status, int sms, cudaStream_t s);
 
+cudaError_t rlb_gemm_grouped(int mode, int b_mn, int epi, int M, int N, int K, const void* A, long long lda,
+                             const void* B, long long ldb, void* C, long long ldc, float alpha, int groups,
+                             const int* tile_group, const int* k_begin, const int* k_len, long long k_total,
+                             int* status, int sms, cudaStream_t s);
+
 cudaError_t rlb_paged_decode(const void* q, const void* k_pool, const void* v_pool, const int* block_tables,
                              const int* ctx_lens, void* out, float* part_acc, float* part_ml, int B, int Hq, int Hkv,
                              int D, int max_blocks, int num_blocks, int split_tokens, int n_splits, float scale,
