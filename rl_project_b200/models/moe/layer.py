@@ -14,6 +14,7 @@ the reference checkpoints.
 
 from __future__ import annotations
 
+import os
 from typing import List, Optional
 
 import torch
@@ -58,6 +59,8 @@ class MoELayer(nn.Module):
         from rl_project_b200.ops._ext import available
 
         if not (xs.is_cuda and xs.dtype == torch.bfloat16 and available()):
+            return False
+        if os.environ.get("RLB_MOE_GROUPED", "1") == "0":  # per-expert loop, for A/B measurements
             return False
         m = next((e for e in self.experts if isinstance(e, SwiGLUFeedForward)), None)
         if m is None or not m._fusable() or type(m.w2) is not nn.Linear or m.w2.bias is not None:
