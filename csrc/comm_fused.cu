@@ -86,12 +86,10 @@ RLB_DEVICE void multimem_sum8(const __nv_bfloat16* mc, float* out) {
   }
 }
 
-// Plain 16-byte load (not the read-only path: the slot is rewritten by its owner between launches).
-RLB_DEVICE uint4 ld16(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-  return v;
-}
+// 16-byte load of a peer's (or this rank's) slot.  The data kernel starts after the wait kernel observed every
+// peer's flag, and the slot does not change while the kernel runs, so ordinary loads that the compiler may
+// batch freely are enough.
+RLB_DEVICE uint4 ld16(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
 RLB_DEVICE void add8(const uint4& raw, float* acc) {
   float f[8];
@@ -108,9 +106,10 @@ __global__ void wait_peers_kernel(const int* __restrict__ my_flags, int world, i
 }
 
 constexpr int kRsThreads = 256;
-constexpr int kRsUnroll = 4;
 
-template <bool MULTIMEM>
+// PB peers are loaded together, U vectors per peer: PB * U 16-byte loads in flight per thread before the
+// adds (16 for every world size: PB = min(world, 8) rounded up to 2 / 4 / 8, U = 16 / PB).
+template <int PB, int U, bool MULTIMEM>
 __global__ void __launch_bounds__(kRsThreads) fused_rs_kernel(
     const unsigned long long* __restrict__ buf_ptrs, unsigned long long mc_base, int world, int rank,
     long long shard, float scale, float* __restrict__ out, int accumulate, float* __restrict__ sumsq,
@@ -125,46 +124,40 @@ __global__ void __launch_bounds__(kRsThreads) fused_rs_kernel(
   const long long nvec = shard / 8;
   const long long stride = (long long)gridDim.x * kRsThreads;
   float sq = 0.f;
-  for (long long v0 = (long long)blockIdx.x * kRsThreads + threadIdx.x; v0 < nvec; v0 += stride * kRsUnroll) {
-    float acc[kRsUnroll][8];
+  for (long long v0 = (long long)blockIdx.x * kRsThreads + threadIdx.x; v0 < nvec; v0 += stride * U) {
+    float acc[U][8];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[u][k] = 0.f;
     if constexpr (MULTIMEM) {
 #pragma unroll
-      for (int u = 0; u < kRsUnroll; ++u) {
+      for (int u = 0; u < U; ++u) {
         const long long v = v0 + u * stride;
-        if (v < nvec) {
-          multimem_sum8(reinterpret_cast<const __nv_bfloat16*>(mc_base) + lo + v * 8, acc[u]);
-        } else {
-#pragma unroll
-          for (int k = 0; k < 8; ++k) acc[u][k] = 0.f;
-        }
+        if (v < nvec) multimem_sum8(reinterpret_cast<const __nv_bfloat16*>(mc_base) + lo + v * 8, acc[u]);
       }
     } else {
+      for (int p0 = 0; p0 < world; p0 += PB) {
+        uint4 raw[PB][U];
 #pragma unroll
-      for (int u = 0; u < kRsUnroll; ++u)
-#pragma unroll
-        for (int k = 0; k < 8; ++k) acc[u][k] = 0.f;
-      // peers in pairs: 2 x kRsUnroll 16-byte loads in flight per thread before the adds
-      for (int p0 = 0; p0 < world; p0 += 2) {
-        uint4 raw[2][kRsUnroll];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
+        for (int j = 0; j < PB; ++j) {
           const int p = p0 + j;
           const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(buf_ptrs[p < world ? p : p0]) + lo;
 #pragma unroll
-          for (int u = 0; u < kRsUnroll; ++u) {
+          for (int u = 0; u < U; ++u) {
             const long long v = v0 + u * stride;
             if (p < world && v < nvec) raw[j][u] = ld16(src + v * 8);
             else raw[j][u] = make_uint4(0u, 0u, 0u, 0u);
           }
         }
 #pragma unroll
-        for (int j = 0; j < 2; ++j)
+        for (int j = 0; j < PB; ++j)
 #pragma unroll
-          for (int u = 0; u < kRsUnroll; ++u) add8(raw[j][u], acc[u]);
+          for (int u = 0; u < U; ++u) add8(raw[j][u], acc[u]);
       }
     }
 #pragma unroll
-    for (int u = 0; u < kRsUnroll; ++u) {
+    for (int u = 0; u < U; ++u) {
       const long long v = v0 + u * stride;
       if (v >= nvec) continue;
       float4* o = reinterpret_cast<float4*>(out + v * 8);
@@ -204,15 +197,17 @@ cudaError_t rlb_fused_reduce_scatter(const unsigned long long* buf_ptrs, unsigne
   if (shard % 8 != 0 || world < 1 || world > 32 || ctas < 1) return cudaErrorInvalidValue;
   wait_peers_kernel<<<1, 32, 0, s>>>(my_flags, world, slot, epoch, limit_ns, status);
   const long long nvec = shard / 8;
-  const long long per_cta = (long long)kRsThreads * kRsUnroll;
+  const int U = mc_base ? 8 : (world <= 2 ? 8 : world <= 4 ? 4 : 2);
+  const long long per_cta = (long long)kRsThreads * U;
   long long grid = (nvec + per_cta - 1) / per_cta;
   if (grid > ctas) grid = ctas;
   if (grid < 1) grid = 1;
-  if (mc_base)
-    fused_rs_kernel<true><<<(int)grid, kRsThreads, 0, s>>>(buf_ptrs, mc_base, world, rank, shard, scale, out,
-                                                           accumulate, sumsq, status);
-  else
-    fused_rs_kernel<false><<<(int)grid, kRsThreads, 0, s>>>(buf_ptrs, mc_base, world, rank, shard, scale, out,
-                                                            accumulate, sumsq, status);
+  const dim3 g((unsigned)grid), b(kRsThreads);
+#define RLB_RS_ARGS buf_ptrs, mc_base, world, rank, shard, scale, out, accumulate, sumsq, status
+  if (mc_base) fused_rs_kernel<1, 8, true><<<g, b, 0, s>>>(RLB_RS_ARGS);
+  else if (world <= 2) fused_rs_kernel<2, 8, false><<<g, b, 0, s>>>(RLB_RS_ARGS);
+  else if (world <= 4) fused_rs_kernel<4, 4, false><<<g, b, 0, s>>>(RLB_RS_ARGS);
+  else fused_rs_kernel<8, 2, false><<<g, b, 0, s>>>(RLB_RS_ARGS);
+#undef RLB_RS_ARGS
   return cudaGetLastError();
 }

@@ -99,15 +99,39 @@ class MoELayer(nn.Module):
         self._pack = {"key": (first, n), "w13": w13, "w2": w2, "ptrs": [p.data_ptr() for p in params]}
         return w13, w2, params
 
+    def _experts_grouped(self, xp: torch.Tensor, layout, first: int, n: int) -> torch.Tensor:
+        from rl_project_b200.ops.grouped_gemm import grouped_swiglu_experts
+
+        w13, w2, params = self._stacked(first, n)
+        sink = self._pack if params else None
+        return grouped_swiglu_experts(xp, layout, w13, w2, params, sink)
+
     def _run_grouped(self, xs: torch.Tensor, counts: torch.Tensor, sorted_experts: torch.Tensor,
                      first: int) -> torch.Tensor:
-        from rl_project_b200.ops.grouped_gemm import grouped_layout, grouped_swiglu_experts
+        """Rows already sorted by expert (expert-parallel receive buffer) through the grouped experts."""
+        from rl_project_b200.ops.grouped_gemm import grouped_layout
+        from rl_project_b200.ops.moe_dispatch import combine, dispatch, row_maps
 
         layout = grouped_layout(sorted_experts, counts)
-        xp = xs.new_zeros(layout.rows, xs.shape[1]).index_copy(0, layout.dest, xs)
-        w13, w2, params = self._stacked(first, counts.numel())
-        y = grouped_swiglu_experts(xp, layout, w13, w2, params)
-        return y.index_select(0, layout.dest)
+        order = torch.arange(xs.shape[0], device=xs.device)
+        maps = row_maps(order, layout.dest, layout.rows, 1)
+        y = self._experts_grouped(dispatch(xs, maps), layout, first, counts.numel())
+        return combine(y, torch.ones(xs.shape[0], 1, device=xs.device, dtype=torch.float32), maps)
+
+    def _forward_grouped(self, xf: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+        """Route, dispatch into the padded expert-sorted buffer, run the grouped experts and combine: every
+        step is a device op (no host synchronisation) and both directions are gathers (no atomics)."""
+        from rl_project_b200.ops.grouped_gemm import grouped_layout
+        from rl_project_b200.ops.moe_dispatch import combine, dispatch, row_maps
+
+        k = indices.shape[1]
+        flat = indices.reshape(-1)
+        order = torch.sort(flat, stable=True).indices
+        counts = torch.bincount(flat, minlength=self.n_experts)
+        layout = grouped_layout(flat.index_select(0, order), counts)
+        maps = row_maps(order, layout.dest, layout.rows, k)
+        y = self._experts_grouped(dispatch(xf, maps), layout, 0, self.n_experts)
+        return combine(y, weights, maps)
 
     def run_experts(self, xs: torch.Tensor, counts: List[int], first_expert: int = 0) -> torch.Tensor:
         if self._grouped_ready(xs):
@@ -132,13 +156,12 @@ class MoELayer(nn.Module):
             from rl_project_b200.parallel.expert import expert_parallel_moe
 
             y = expert_parallel_moe(self, xf, weights, indices)
+        elif self._grouped_ready(xf):
+            y = self._forward_grouped(xf, weights, indices)
         else:
             order, tok, counts = sort_by_expert(indices, self.n_experts)
             xs = xf.index_select(0, tok)
-            if self._grouped_ready(xs):  # one grouped launch per GEMM, no host synchronisation
-                ys = self._run_grouped(xs, counts, indices.reshape(-1).index_select(0, order), 0)
-            else:
-                ys = self.run_experts(xs, counts.tolist())
+            ys = self.run_experts(xs, counts.tolist())
             w = weights.reshape(-1).index_select(0, order).unsqueeze(-1).to(ys.dtype)
             y = torch.zeros_like(xf).index_add_(0, tok, ys * w)
         if self.shared_experts is not None:

@@ -80,13 +80,16 @@ def grouped_nn(dy: torch.Tensor, w: torch.Tensor, tile_group: torch.Tensor) -> t
     return out
 
 
-def grouped_tn(dy: torch.Tensor, x: torch.Tensor, seg_start: torch.Tensor, seg_len: torch.Tensor) -> torch.Tensor:
+def grouped_tn(dy: torch.Tensor, x: torch.Tensor, seg_start: torch.Tensor, seg_len: torch.Tensor,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Per expert e: ``dy[seg]^T x[seg]`` -> ``[E, N, K]`` (zero for experts without rows)."""
     R, N = dy.shape
     R2, K = x.shape
     assert R == R2
     E = seg_start.numel()
-    out = torch.empty(E, N, K, dtype=torch.bfloat16, device=dy.device)
+    if out is None:
+        out = torch.empty(E, N, K, dtype=torch.bfloat16, device=dy.device)
+    assert out.shape == (E, N, K) and out.is_contiguous() and out.dtype == torch.bfloat16
     native().gemm_grouped(2, 1, 0, dy, x, out, N, K, R, N, K, K, 1.0, E, None, seg_start, seg_len, R, None)
     return out
 
@@ -94,19 +97,22 @@ def grouped_tn(dy: torch.Tensor, x: torch.Tensor, seg_start: torch.Tensor, seg_l
 class _GroupedSwiGLU(torch.autograd.Function):
     """SwiGLU experts over a padded grouped layout: ``y = (silu(x W1^T) * (x W3^T)) W2^T`` per expert.
 
-    Inputs: the padded rows ``xp [R, C]``, the layout, the stacked ``w13 [E, 2F, C]`` / ``w2 [E, C, F]`` and
-    the per-expert parameters they hold (``params`` receive the weight gradients as views of the stacked
-    gradients)."""
+    Inputs: the padded rows ``xp [R, C]``, the layout, the stacked ``w13 [E, 2F, C]`` / ``w2 [E, C, F]``, a
+    gradient ``sink`` and the per-expert parameters the stacked weights hold, ordered
+    ``[w1_0..w1_{E-1}, w3_0.., w2_0..]``.  With a sink the weight gradients are written by the grouped kernel
+    straight into two packed buffers kept in the sink, and each parameter's ``.grad`` is a view into them
+    (accumulated in place on later micro-batches) -- no per-expert copies.  Without parameters the stacked
+    weights came from differentiable ops and receive the gradients themselves."""
 
     @staticmethod
-    def forward(ctx, xp, tile_group, seg_start, seg_len, w13, w2, n_experts, *params):
+    def forward(ctx, xp, tile_group, seg_start, seg_len, w13, w2, sink, *params):
         C = native()
         h13 = grouped_nt(xp, w13, tile_group)
         a = C.swiglu_fwd(h13)
         y = grouped_nt(a, w2, tile_group)
         ctx.save_for_backward(xp, tile_group, seg_start, seg_len, w13, w2, h13, a)
-        ctx.n_experts = n_experts
-        ctx.n_params = len(params)
+        ctx.sink = sink
+        ctx.params = params
         return y
 
     @staticmethod
@@ -116,18 +122,34 @@ class _GroupedSwiGLU(torch.autograd.Function):
         dy = dy.contiguous()
         da = grouped_nn(dy, w2, tile_group)
         dh13 = C.swiglu_bwd(h13, da)
-        dxp = grouped_nn(dh13, w13, tile_group)
-        dw2 = grouped_tn(dy, a, seg_start, seg_len)
-        dw13 = grouped_tn(dh13, xp, seg_start, seg_len)
-        E = ctx.n_experts
-        F = w2.shape[2]
-        if not ctx.n_params:  # stacked weights built from the parameters by differentiable ops
-            return dxp, None, None, None, dw13, dw2, None
-        # params ordered [w1_0..w1_{E-1}, w3_0.., w2_0..]
-        grads = [dw13[e, :F] for e in range(E)] + [dw13[e, F:] for e in range(E)] + [dw2[e] for e in range(E)]
-        return (dxp, None, None, None, None, None, None, *grads)
+        dxp = grouped_nn(dh13, w13, tile_group) if ctx.needs_input_grad[0] else None
+        ps = ctx.params
+        if not ps:  # stacked weights built from the parameters by differentiable ops
+            return (dxp, None, None, None, grouped_tn(dh13, xp, seg_start, seg_len),
+                    grouped_tn(dy, a, seg_start, seg_len), None)
+        E, F = w13.shape[0], w2.shape[2]
+        sink = ctx.sink
+        g13, g2 = sink.get("g13"), sink.get("g2")
+        if g13 is None:
+            g13, g2 = torch.empty_like(w13), torch.empty_like(w2)
+            sink["g13"], sink["g2"] = g13, g2
+        views = [g13[e, :F] for e in range(E)] + [g13[e, F:] for e in range(E)] + [g2[e] for e in range(E)]
+        if all(p.grad is None for p in ps):
+            grouped_tn(dh13, xp, seg_start, seg_len, out=g13)
+            grouped_tn(dy, a, seg_start, seg_len, out=g2)
+            for p, v in zip(ps, views):
+                p.grad = v
+        elif all(p.grad is not None and p.grad.data_ptr() == v.data_ptr() for p, v in zip(ps, views)):
+            g13.add_(grouped_tn(dh13, xp, seg_start, seg_len))
+            g2.add_(grouped_tn(dy, a, seg_start, seg_len))
+        else:  # gradients rebound elsewhere: accumulate parameter by parameter
+            d13, d2 = grouped_tn(dh13, xp, seg_start, seg_len), grouped_tn(dy, a, seg_start, seg_len)
+            new = [d13[e, :F] for e in range(E)] + [d13[e, F:] for e in range(E)] + [d2[e] for e in range(E)]
+            for p, d in zip(ps, new):
+                p.grad = d.clone() if p.grad is None else p.grad.add_(d)
+        return (dxp, None, None, None, None, None, None) + (None,) * len(ps)
 
 
-def grouped_swiglu_experts(xp, layout: GroupedLayout, w13, w2, params=()):
-    return _GroupedSwiGLU.apply(xp, layout.tile_group, layout.seg_start, layout.seg_len, w13, w2, w13.shape[0],
-                                *params)
+def grouped_swiglu_experts(xp, layout: GroupedLayout, w13, w2, params=(), sink=None):
+    return _GroupedSwiGLU.apply(xp, layout.tile_group, layout.seg_start, layout.seg_len, w13, w2,
+                                sink if sink is not None else {}, *params)
