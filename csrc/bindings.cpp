@@ -453,6 +453,34 @@ std::vector<at::Tensor> sample(const at::Tensor& logits, const at::Tensor& tempe
   return {tokens, lp};
 }
 
+// ---------------------------------------------------------------- fused RL loss
+// -> {pl_row [G], kl_row [G], dpl [G, R], dkl [G, R]}; all inputs fp32 [G, R] (adv [G]).
+std::vector<at::Tensor> rl_loss(const at::Tensor& lp_new, const at::Tensor& lp_old, const at::Tensor& lp_ref,
+                                const at::Tensor& mask, const at::Tensor& adv, double eps, bool token_level,
+                                bool k3) {
+  check_cuda(lp_new, "lp_new");
+  for (const at::Tensor* t : {&lp_old, &lp_ref, &mask}) {
+    check_dev(*t, lp_new, "log-prob / mask");
+    TORCH_CHECK(t->sizes() == lp_new.sizes() && t->scalar_type() == at::kFloat && t->is_contiguous(),
+                "log-probs and mask: fp32 contiguous [G, R]");
+  }
+  check_dev(adv, lp_new, "adv");
+  TORCH_CHECK(lp_new.dim() == 2 && lp_new.scalar_type() == at::kFloat && lp_new.is_contiguous(), "lp_new: fp32 [G, R]");
+  TORCH_CHECK(adv.scalar_type() == at::kFloat && adv.numel() == lp_new.size(0) && adv.is_contiguous(), "adv: fp32 [G]");
+  const c10::cuda::CUDAGuard g(lp_new.device());
+  const int G = (int)lp_new.size(0), R = (int)lp_new.size(1);
+  auto pl = at::empty({G}, lp_new.options());
+  auto kl = at::empty({G}, lp_new.options());
+  auto dpl = at::empty_like(lp_new);
+  auto dkl = at::empty_like(lp_new);
+  CHECK_OK(rlb_rl_loss(lp_new.data_ptr<float>(), lp_old.data_ptr<float>(), lp_ref.data_ptr<float>(),
+                       mask.data_ptr<float>(), adv.data_ptr<float>(), G, R, (float)eps, token_level ? 1 : 0, k3 ? 1 : 0,
+                       pl.data_ptr<float>(), kl.data_ptr<float>(), dpl.data_ptr<float>(), dkl.data_ptr<float>(),
+                       cur_stream()),
+           "rl_loss");
+  return {pl, kl, dpl, dkl};
+}
+
 // ---------------------------------------------------------------- peer memory (CUDA IPC, no multicast object)
 // A buffer allocated with cudaMalloc outside torch's caching allocator and rounded up to whole 2 MiB pages, so
 // that the driver gives it pages of its own.  An IPC handle always names a whole allocation, so peer_handle
@@ -565,6 +593,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_decode", &paged_decode);
   m.def("paged_write", &paged_write);
   m.def("sample", &sample);
+  m.def("rl_loss", &rl_loss);
   m.def("peer_alloc", &peer_alloc);
   m.def("peer_handle", &peer_handle);
   m.def("peer_open", &peer_open);

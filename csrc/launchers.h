@@ -75,6 +75,11 @@ cudaError_t rlb_fused_reduce_scatter(const unsigned long long* buf_ptrs, unsigne
                                      float scale, float* out, int accumulate, float* sumsq, int* status,
                                      unsigned long long limit_ns, int ctas, cudaStream_t s);
 
+// Fused clipped-surrogate + KL loss over per-token log-probs (GRPO / PPO), with the gradient wrt lp_new.
+cudaError_t rlb_rl_loss(const float* lp_new, const float* lp_old, const float* lp_ref, const float* mask,
+                        const float* adv, int G, int R, float eps, int token_level, int k3, float* pl_row,
+                        float* kl_row, float* dpl, float* dkl, cudaStream_t s);
+
 // RMSNorm backward that allocates nothing (no counterpart in the reference):
 // the dw partial sums live in a fixed 4 MiB file-scope __device__ array per
 // device instead of a caller-allocated buffer.  Returns a cudaError_t value;

@@ -193,6 +193,45 @@ def bench_fused_rs(world: int = 8, shard_mib: int = 32):
     assert int(status.item()) == 0
 
 
+def bench_grouped(E: int = 64, tokens: int = 8192, k: int = 6, C: int = 2048, F: int = 1408):
+    """Grouped expert GEMMs at the MLA+MoE expert shape (64 experts, top-6, d 2048, expert width 1408):
+    forward W13 ([R, C] x [E, 2F, C]^T), input grad through W13 and weight grad, against the same
+    FLOPs run as one cuBLAS matmul per expert (torch.matmul loop)."""
+    from rl_project_b200.ops.grouped_gemm import grouped_layout, grouped_nn, grouped_nt, grouped_tn
+
+    peak_tf, _ = _peaks()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    idx = torch.randint(0, E, (tokens * k,), device="cuda", generator=g)
+    counts = torch.bincount(idx, minlength=E)
+    se = torch.sort(idx).values
+    lay = grouped_layout(se, counts)
+    xp = torch.randn(lay.rows, C, device="cuda").to(torch.bfloat16)
+    w13 = (torch.randn(E, 2 * F, C, device="cuda") * 0.02).to(torch.bfloat16)
+    dh = torch.randn(lay.rows, 2 * F, device="cuda").to(torch.bfloat16)
+    flops = 2.0 * tokens * k * C * 2 * F
+    cl = counts.tolist()
+    segs = []
+    s0 = 0
+    for c in cl:
+        segs.append((s0, c))
+        s0 += (c + 127) // 128 * 128
+    cases = {
+        "fwd x W13^T": (lambda: grouped_nt(xp, w13, lay.tile_group),
+                        lambda: [xp[a:a + c] @ w13[e].t() for e, (a, c) in enumerate(segs)]),
+        "dgrad dh W13": (lambda: grouped_nn(dh, w13, lay.tile_group),
+                         lambda: [dh[a:a + c] @ w13[e] for e, (a, c) in enumerate(segs)]),
+        "wgrad dh^T x": (lambda: grouped_tn(dh, xp, lay.seg_start, lay.seg_len),
+                         lambda: [dh[a:a + c].t() @ xp[a:a + c] for e, (a, c) in enumerate(segs)]),
+    }
+    for name, (ours, loop) in cases.items():
+        ms = time_ms(ours)
+        ms_loop = time_ms(loop)
+        print(json.dumps({"kernel": f"grouped GEMM {name}", "experts": E, "routed_rows": tokens * k, "C": C,
+                          "F": F, "ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1),
+                          "frac_of_measured_bf16": round(flops / ms / 1e9 / peak_tf, 3),
+                          "cublas_per_expert_loop_ms": round(ms_loop, 4)}), flush=True)
+
+
 MODEL_SHAPES = [
     (32768, 3072, 2048, "nt"), (32768, 2048, 2048, "nt"), (32768, 16384, 2048, "nt"), (32768, 2048, 8192, "nt"),
     (32768, 2048, 16384, "nn"), (32768, 8192, 2048, "nn"), (16384, 2048, 32768, "tn"), (2048, 8192, 32768, "tn"),
@@ -218,6 +257,8 @@ def main():
         bench_adam()
     if "rs" in which:
         bench_fused_rs()
+    if "grouped" in which:
+        bench_grouped()
 
 
 if __name__ == "__main__":

@@ -28,6 +28,7 @@ from rl_project_b200.rollouts.agent import AgentRolloutConfig, AgentRolloutEngin
 from rl_project_b200.rollouts.engine import RolloutConfig, RolloutEngine, stack_group, stack_old_logprobs
 from rl_project_b200.rollouts.rewards.composite import score_trajectories
 from rl_project_b200.training.common.advantages import group_relative_advantages
+from rl_project_b200.ops.rl_loss import clipped_kl_loss
 from rl_project_b200.training.common.logprobs import kl_k3, kl_logprob_diff, masked_mean, masked_sum
 from rl_project_b200.training.common.trainer import PostTrainingAlgorithm
 from rl_project_b200.training.ppo import ppo_clipped_objective
@@ -191,13 +192,10 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
         mask = mask.to(dev)
         new = self.policy.logprobs(prompt, resp).float() * mask
         old, ref = grp.old_logprobs.to(dev), grp.ref_logprobs.to(dev)
-        if self.cfg.ratio_level == "sequence_mean":
-            pl = ppo_clipped_objective(torch.exp(masked_mean(new - old, mask)), adv, self.cfg.clip_ratio).mean()
-        else:
-            per_tok = ppo_clipped_objective(torch.exp(new - old), adv[:, None], self.cfg.clip_ratio)
-            pl = masked_mean(per_tok, mask).mean()
-        kl = self._kl(ref, new, mask)
-        return pl + self.cfg.kl_coef * kl, kl
+        # surrogate + KL (and their gradient) in one fused op; same formulas as _kl / ppo_clipped_objective
+        loss, _, kl = clipped_kl_loss(new, old, ref, mask, adv, self.cfg.clip_ratio, self.cfg.kl_coef,
+                                      self.cfg.ratio_level, "k3" if self.cfg.kl_estimator == "k3" else "logprob_diff")
+        return loss, kl
 
     def _reinforce_loss(self, grp: GRPOGroup, adv: torch.Tensor) -> torch.Tensor:
         if self.cfg.agent:

@@ -23,6 +23,7 @@ from rl_project_b200.core.protocols import RewardProvider, Trajectory
 from rl_project_b200.rollouts.engine import RolloutConfig, RolloutEngine
 from rl_project_b200.rollouts.rewards.composite import score_trajectories
 from rl_project_b200.training.common.advantages import normalize_advantages
+from rl_project_b200.ops.rl_loss import clipped_kl_loss
 from rl_project_b200.training.common.logprobs import kl_logprob_diff, masked_mean
 from rl_project_b200.training.common.trainer import PostTrainingAlgorithm
 
@@ -152,11 +153,9 @@ class PPOAlgorithm(PostTrainingAlgorithm):
                 new_lp, values = self.policy.logprobs_and_values(batch.prompt_ids, batch.response_ids)
                 ent_tok = None
             new_lp = new_lp.float()
-            if self.cfg.ratio_level == "sequence_mean":
-                pl = ppo_clipped_objective(torch.exp(masked_mean(new_lp - old_lp, mask)), adv, self.cfg.clip_ratio).mean()
-            else:
-                per_tok = ppo_clipped_objective(torch.exp(new_lp - old_lp), adv[:, None], self.cfg.clip_ratio)
-                pl = masked_mean(per_tok, mask).mean()
+            # surrogate and (penalty mode) KL in one fused op; the KL penalty is added below
+            pl, _, _ = clipped_kl_loss(new_lp, old_lp, ref_lp, mask, adv, self.cfg.clip_ratio, 0.0,
+                                       self.cfg.ratio_level, "logprob_diff_rows")
             vl = F.mse_loss(values.float(), returns)
             if self.cfg.kl_mode == "penalty":
                 kl = kl_logprob_diff(ref_lp, new_lp, mask).mean()
