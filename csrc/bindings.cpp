@@ -453,6 +453,14 @@ std::vector<at::Tensor> sample(const at::Tensor& logits, const at::Tensor& tempe
   return {tokens, lp};
 }
 
+void multimem_bcast(const at::Tensor& src, int64_t mc_dst, int64_t nbytes) {
+  check_cuda(src, "src");
+  TORCH_CHECK(src.is_contiguous() && (int64_t)src.nbytes() >= nbytes, "src: contiguous, at least nbytes");
+  const c10::cuda::CUDAGuard g(src.device());
+  CHECK_OK(rlb_multimem_bcast(src.data_ptr(), (unsigned long long)mc_dst, nbytes, sm_count(), cur_stream()),
+           "multimem_bcast");
+}
+
 // ---------------------------------------------------------------- fused RL loss
 // -> {pl_row [G], kl_row [G], dpl [G, R], dkl [G, R]}; all inputs fp32 [G, R] (adv [G]).
 std::vector<at::Tensor> rl_loss(const at::Tensor& lp_new, const at::Tensor& lp_old, const at::Tensor& lp_ref,
@@ -599,5 +607,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_open", &peer_open);
   m.def("peer_close", &peer_close);
   m.def("signal_peers", &signal_peers);
+  m.def("multimem_bcast", &multimem_bcast);
   m.def("fused_reduce_scatter", &fused_reduce_scatter);
 }

@@ -179,9 +179,36 @@ __global__ void __launch_bounds__(kRsThreads) fused_rs_kernel(
   }
 }
 
+// Broadcast through NVSwitch: the source rank stores each 16-byte vector once to the multicast
+// address and the switch writes it into every rank's copy of the buffer (source egress = one copy,
+// whatever the world size).  Ends with a system-scope fence so the stores are ordered before the
+// barrier the caller issues next.
+__global__ void __launch_bounds__(256) multimem_bcast_kernel(const uint4* __restrict__ src,
+                                                             unsigned long long mc_dst, long long n16) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += stride) {
+    const uint4 v = src[i];
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_dst + 16ull * i),
+                 "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+  }
+  __threadfence_system();
+}
+
 }  // namespace rlb
 
 using namespace rlb;
+
+cudaError_t rlb_multimem_bcast(const void* src, unsigned long long mc_dst, long long nbytes, int sms,
+                               cudaStream_t s) {
+  if (nbytes <= 0) return cudaSuccess;
+  if (nbytes % 16 || (reinterpret_cast<uintptr_t>(src) & 15) || (mc_dst & 15)) return cudaErrorInvalidValue;
+  const long long n16 = nbytes / 16;
+  long long grid = (n16 + 255) / 256;
+  if (grid > 2LL * sms) grid = 2LL * sms;
+  multimem_bcast_kernel<<<(int)grid, 256, 0, s>>>(reinterpret_cast<const uint4*>(src), mc_dst, n16);
+  return cudaGetLastError();
+}
 
 cudaError_t rlb_signal_peers(const unsigned long long* flag_ptrs, int world, int rank, int slot, int epoch,
                              cudaStream_t s) {

@@ -80,6 +80,10 @@ cudaError_t rlb_rl_loss(const float* lp_new, const float* lp_old, const float* l
                         const float* adv, int G, int R, float eps, int token_level, int k3, float* pl_row,
                         float* kl_row, float* dpl, float* dkl, cudaStream_t s);
 
+// NVLS broadcast: store `nbytes` (multiple of 16) from local `src` through the multicast address `mc_dst`.
+cudaError_t rlb_multimem_bcast(const void* src, unsigned long long mc_dst, long long nbytes, int sms,
+                               cudaStream_t s);
+
 // RMSNorm backward that allocates nothing (no counterpart in the reference):
 // the dw partial sums live in a fixed 4 MiB file-scope __device__ array per
 // device instead of a caller-allocated buffer.  Returns a cudaError_t value;

@@ -16,16 +16,11 @@ import torch.distributed as dist
 
 
 def broadcast_parameters(params: Sequence[torch.nn.Parameter], strategy=None, src: int = 0) -> None:
-    with torch.no_grad():
-        for bucket in _buckets(list(params), 256 << 20, lambda p: p.data):
-            flat = torch.cat([p.data.reshape(-1) for p in bucket]) if len(bucket) > 1 else bucket[0].data.reshape(-1)
-            dist.broadcast(flat, src=src)
-            if len(bucket) > 1:
-                off = 0
-                for p in bucket:
-                    n = p.numel()
-                    p.data.copy_(flat[off:off + n].view_as(p))
-                    off += n
+    """Start every rank from ``src``'s weights: packed chunks through NVSwitch multicast or one NCCL broadcast
+    per chunk (rl_project_b200/parallel/weight_sync.py)."""
+    from rl_project_b200.parallel.weight_sync import broadcast_parameters as _bcast
+
+    _bcast([p.data for p in params], src=src)
 
 
 def _buckets(params: List[torch.nn.Parameter], cap_bytes: int, get) -> List[List[torch.nn.Parameter]]:

@@ -146,13 +146,13 @@ class ExpertParallelStrategy:
         if n == 0:
             raise DistributedConfigError("expert_parallel needs a model with MoE layers")
         self.model = model
+        from rl_project_b200.parallel.weight_sync import broadcast_parameters
+
         with torch.no_grad():  # replicated weights start identical; experts of each EP slot too
             for p in model.parameters():
-                if getattr(p, "_expert_parallel", False):
-                    if self.cfg.expert_parallel_size < rt.world_size():
-                        dist.broadcast(p.data, src=rt.rank() % ep, group=self.expert_dp_group)
-                else:
-                    dist.broadcast(p.data, src=0)
+                if getattr(p, "_expert_parallel", False) and self.cfg.expert_parallel_size < rt.world_size():
+                    dist.broadcast(p.data, src=rt.rank() % ep, group=self.expert_dp_group)
+        broadcast_parameters([p.data for p in model.parameters() if not getattr(p, "_expert_parallel", False)])
 
     def finish_gradients(self, trainer) -> None:
         world = rt.world_size()

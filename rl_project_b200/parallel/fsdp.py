@@ -139,11 +139,9 @@ class FSDPStrategy(_ProcessGroupStrategy):
         if not mods:
             raise DistributedConfigError("fsdp needs the algorithm to expose its trained modules")
         # rank 0's initial weights everywhere (the same contract as DDP's broadcast)
-        with torch.no_grad():
-            for m in mods:
-                for p in m.parameters():
-                    if p.requires_grad:
-                        dist.broadcast(p.data, src=0)
+        from rl_project_b200.parallel.weight_sync import broadcast_parameters
+
+        broadcast_parameters([p.data for m in mods for p in m.parameters() if p.requires_grad], self.group)
         seen = set()
         for mi, m in enumerate(mods):
             blocks = list(m.transformer.h) if hasattr(m, "transformer") and hasattr(m.transformer, "h") else []

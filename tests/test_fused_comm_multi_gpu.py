@@ -126,3 +126,39 @@ def test_fsdp_fused_gradients_match_nccl():
     for k, v in b["state"].items():
         d = (a["state"][k] - v).abs().max().item()
         assert d < 5e-3, (k, d)
+
+
+def _bcast_worker(rank, port, out):
+    import datetime
+
+    import torch.distributed as dist
+
+    from rl_project_b200.parallel.weight_sync import ParameterBroadcaster
+
+    _env(rank, port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    res = {}
+    for mc in ("on", "off"):
+        g = torch.Generator(device="cuda").manual_seed(7 + rank)
+        ts = [torch.randn(1000003, device="cuda", generator=g).bfloat16(),
+              torch.randn(257, 129, device="cuda", generator=g),
+              torch.randint(0, 1 << 30, (4097,), device="cuda", generator=g)]
+        b = ParameterBroadcaster(None, device=torch.device("cuda", rank), chunk_bytes=1 << 20, multicast=mc)
+        b.broadcast_(ts, src=1)
+        torch.cuda.synchronize()
+        res[mc] = {"mode": b.mode, "sums": [float(t.double().sum()) for t in ts],
+                   "first": [t.reshape(-1)[:4].double().tolist() for t in ts]}
+        del b
+    torch.save(res, os.path.join(out, f"b{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_parameter_broadcast_nvls_and_nccl():
+    with tempfile.TemporaryDirectory() as out:
+        mp.start_processes(_bcast_worker, args=(free_port(), out), nprocs=WORLD, join=True, start_method="spawn")
+        r0, r1 = torch.load(os.path.join(out, "b0.pt")), torch.load(os.path.join(out, "b1.pt"))
+    assert r0["on"]["mode"] == "nvls" and r0["off"]["mode"] == "nccl"
+    for mc in ("on", "off"):
+        assert r0[mc]["sums"] == r1[mc]["sums"] and r0[mc]["first"] == r1[mc]["first"], mc
