@@ -11,9 +11,10 @@ import torch.multiprocessing as mp
 from rl_project_b200.parallel.runtime import free_port
 
 pytestmark = [pytest.mark.gpu, pytest.mark.multi_gpu]
-WORLD = 2
+# every GPU of the box (2 to 8); one rank per GPU
+WORLD = max(2, min(8, torch.cuda.device_count())) if torch.cuda.is_available() else 2
 STEPS = 3
-MODES = ("off",)  # CUDA IPC mappings and peer loads
+MODES = ("off", "on")  # CUDA IPC mappings + peer loads; symmetric memory + NVLink multicast reduce
 
 
 def _env(rank, port):
@@ -46,7 +47,9 @@ def _kernel_worker(rank, port, out):
             ref = torch.empty(shard, dtype=torch.float32, device="cuda")
             dist.reduce_scatter_tensor(ref, x.float())
             ref /= WORLD
-            errs.append(float((outp - ref).abs().max()))
+            # the multicast reduce returns bf16 sums (fp32 accumulation): allow one bf16 ulp of the result
+            tol = 1e-5 if mc == "off" else 2.0 ** -7 * max(1.0, float(ref.abs().max()))
+            errs.append(float((outp - ref).abs().max()) / tol)
         torch.cuda.synchronize()
         fr.poll_status()
         torch.cuda.synchronize()
@@ -65,7 +68,7 @@ def test_fused_kernel_matches_nccl():
         for r in range(WORLD):
             res = torch.load(os.path.join(out, f"k{r}.pt"))
             for mc, v in res.items():
-                assert v["err"] < 1e-5, (r, mc, v)
+                assert v["err"] <= 1.0, (r, mc, v)
 
 
 def _train_worker(rank, port, out, mode):
