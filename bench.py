@@ -58,6 +58,8 @@ def parse_args():
     ap.add_argument("--grad-ckpt", action="store_true")
     ap.add_argument("--fused-comm", choices=["auto", "on", "off", "nccl_baseline"], default="auto",
                     help="FSDP gradient reduce-scatter: fused peer-memory kernel (auto/on) or NCCL")
+    ap.add_argument("--fused-rs-ctas", type=int, default=32,
+                    help="CTAs of each fused reduce-scatter that overlaps backward")
     ap.add_argument("--fused-multicast", choices=["off", "on", "symm"], default="off",
                     help="fused reduce-scatter transport: CUDA IPC peer loads (off) or NVLink multicast (on)")
     return ap.parse_args()
@@ -203,7 +205,7 @@ def run_ours(args, world, rank, local):
                     "schedule": {"name": "constant", "warmup_steps": 0},
                     "checkpoint": {"save_every": 0, "auto_resume": False}},
         "distributed": {"strategy": strategy_name, "timeout_s": 300, "fused_comm": args.fused_comm,
-                        "fused_multicast": args.fused_multicast},
+                        "fused_multicast": args.fused_multicast, "fused_rs_ctas": args.fused_rs_ctas},
         "output_dir": os.path.join(tempfile.gettempdir(), f"rlb_bench_{rank}"),
     })
     strategy = build_strategy(manifest.distributed)

@@ -6,9 +6,10 @@ Per size (bf16 elements per rank) every arm runs ``--iters`` times after
 ``--warmup`` untimed calls; each call is timed with CUDA events on the
 launching stream and the reported time is the median over calls of the MAX
 over ranks.  Bytes: every rank receives (world - 1) / world of the buffer
-from its peers (peer loads; ``multicast`` receives one reduced copy), which
-is the figure compared with the measured 770 GB/s per-direction peer-copy
-bandwidth of this pool.
+from its peers, and with multicast the switch reads the same share of every
+rank's buffer, so (world - 1) / world of the buffer crosses each GPU's NVLink
+in both modes: the figure compared with the measured 770 GB/s per-direction
+peer-copy bandwidth of this pool.
 
     python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \\
         -m rl_project_b200.benchmarks.comm --sizes 16,64,256
@@ -57,7 +58,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--modes", default="off", help="comma list of fused transports: off (peer loads), on, symm")
-    ap.add_argument("--ctas", type=int, default=32)
+    ap.add_argument("--ctas", default="32", help="comma list of grid sizes to time for the fused kernel")
     args = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
@@ -81,8 +82,9 @@ def main():
         t = sorted(_max_over_ranks(_time(nccl, args.iters, args.warmup, stream)))
         res["nccl_ms"] = t[len(t) // 2]
         ref = out32.clone()
-        for mode in args.modes.split(","):
-            fr = FusedReduceScatter(None, n, torch.device("cuda", local), multicast=mode, ctas=args.ctas)
+        for mode, ctas in ((m, int(c)) for m in args.modes.split(",") for c in args.ctas.split(",")):
+            fr = FusedReduceScatter(None, n, torch.device("cuda", local), multicast=mode, ctas=ctas)
+            mode = f"{mode}{ctas}"
             slot_holder = {}
 
             def fused():
@@ -100,7 +102,9 @@ def main():
             ms = t[len(t) // 2]
             res[f"fused_{mode}_ms"] = ms
             res[f"fused_{mode}_max_abs_err"] = float((out32 - ref).abs().max())
-            wire = (shard * 2) if fr.uses_multicast else (world - 1) * shard * 2
+            # each GPU's NVLink carries (world - 1) / world of its buffer either way: peers read its slices
+            # (peer loads), or the switch reads them for the other ranks' reduces (multicast)
+            wire = (world - 1) * shard * 2
             res[f"fused_{mode}_nvlink_gbs"] = wire / (ms / 1e3) / 1e9
             res[f"fused_{mode}_frac_of_measured_nvlink"] = res[f"fused_{mode}_nvlink_gbs"] / NVLINK_GBS
             fr.close()

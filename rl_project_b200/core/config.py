@@ -316,6 +316,7 @@ class DistributedConfig:
     reshard_after_forward: bool = True
     fused_comm: str = "auto"  # auto | on | off | nccl_baseline
     fused_multicast: str = "off"  # off (CUDA IPC, peer loads) | on (NVLink multicast reduce) | symm
+    fused_rs_ctas: int = 32  # CTAs of a fused reduce-scatter that overlaps backward compute
     timeout_s: float = 600.0
 
     def validate(self) -> None:
@@ -328,6 +329,7 @@ class DistributedConfig:
         _check(self.fused_comm in ("auto", "on", "off", "nccl_baseline"),
                "fused_comm must be auto|on|off|nccl_baseline")
         _check(self.fused_multicast in ("off", "on", "symm"), "fused_multicast must be off|on|symm")
+        _check(self.fused_rs_ctas >= 1, "fused_rs_ctas must be >= 1")
         _check(self.pipeline_micro_batches >= 1, "pipeline_micro_batches must be >= 1")
 
 

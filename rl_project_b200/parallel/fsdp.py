@@ -124,6 +124,8 @@ class FSDPStrategy(_ProcessGroupStrategy):
         self.fused = None  # FusedReduceScatter when gradients are reduced over peer memory
         self.owns_grad_clip = False
         self._final_micro = True
+        self._in_backward = True  # False inside finish_gradients
+        self._rs_ctas_overlap = int(getattr(cfg, "fused_rs_ctas", 32))
 
     # ---------------------------------------------------------------- setup
     def _gloo(self) -> bool:
@@ -282,6 +284,10 @@ class FSDPStrategy(_ProcessGroupStrategy):
         if not accumulate:
             u.master.grad = u.grad_buf
         norm = self._final_micro
+        # reduces issued during backward share the SMs with it: a narrow grid (NCCL-like footprint);
+        # the reduces issued after backward (finish_gradients) are on the critical path: the full grid
+        ctas = self._rs_ctas_overlap if self._in_backward else 2 * torch.cuda.get_device_properties(
+            u.device).multi_processor_count
         C = fr.slot_elems // u.world
         if u.shard <= C:
             slot = fr.next_slot(u.padded)
@@ -291,7 +297,7 @@ class FSDPStrategy(_ProcessGroupStrategy):
             for p in u.params:
                 p.grad = None
             self.comm_stream.wait_stream(cur)
-            fr.reduce(u.shard, u.grad_buf, accumulate, norm, stream=self.comm_stream)
+            fr.reduce(u.shard, u.grad_buf, accumulate, norm, stream=self.comm_stream, ctas=ctas)
         else:
             flat = torch.cat(grads)
             if u.padded > u.total:
@@ -304,7 +310,7 @@ class FSDPStrategy(_ProcessGroupStrategy):
                 slot = fr.next_slot(u.world * L)
                 slot.view(u.world, L).copy_(rows[:, c0:c0 + L])
                 self.comm_stream.wait_stream(cur)
-                fr.reduce(L, u.grad_buf[c0:c0 + L], accumulate, norm, stream=self.comm_stream)
+                fr.reduce(L, u.grad_buf[c0:c0 + L], accumulate, norm, stream=self.comm_stream, ctas=ctas)
             flat.record_stream(self.comm_stream)
         u.norm_counted = norm
 
@@ -370,11 +376,13 @@ class FSDPStrategy(_ProcessGroupStrategy):
         return nullcontext()
 
     def finish_gradients(self, trainer) -> None:
+        self._in_backward = False
         if self.root is not None:
             self._reduce_scatter(self.root)
         for u in self.units:
             if u is not self.root and any(p.grad is not None for p in u.params):
                 self._reduce_scatter(u)  # units whose hooks did not fire (unused params)
+        self._in_backward = True
         if self.comm_stream is not None:
             torch.cuda.current_stream().wait_stream(self.comm_stream)
         for u in self.units:

@@ -191,7 +191,7 @@ class FusedReduceScatter:
         return self.buf[s * self.slot_elems: s * self.slot_elems + numel]
 
     def reduce(self, shard: int, out: torch.Tensor, accumulate: bool, norm: bool,
-               stream: Optional[torch.cuda.Stream] = None) -> None:
+               stream: Optional[torch.cuda.Stream] = None, ctas: Optional[int] = None) -> None:
         """Signal the peers that this rank's slot is filled, then reduce slice ``rank`` of it into ``out``
         (fp32, ``shard`` elements): ``out (+)= sum_p slot_p / world``; squares added to ``sumsq`` if ``norm``."""
         if shard % ALIGN or shard * self.world > self.slot_elems or out.numel() != shard:
@@ -206,7 +206,8 @@ class FusedReduceScatter:
             C.signal_peers(self.flag_ptrs, self.rank, s, epoch)
             mc = self.mc + s * self.slot_elems * 2 if self.mc else 0
             C.fused_reduce_scatter(self.ptrs[s], mc, self.flags, self.rank, s, epoch, shard, 1.0 / self.world, out,
-                                   accumulate, self.sumsq if norm else None, self.status, self.limit_ns, self.ctas)
+                                   accumulate, self.sumsq if norm else None, self.status, self.limit_ns,
+                                   int(ctas or self.ctas))
             ev = torch.cuda.Event()
             ev.record(stream)
         self.events[q] = ev
