@@ -299,6 +299,13 @@ def run_pretrain_workload(args, world, rank, local):
     from rl_project_b200.training.pretrain import PretrainAlgorithm, PretrainConfig
 
     native()
+
+    def tp_fused_used() -> bool:
+        from rl_project_b200.parallel import tp_fused
+
+        return any(r is not None and r.launches > 0 for r in tp_fused._REDUCERS.values())
+
+    tp = 1
     if args.workload == "mesh8b":
         preset, seq = "bl_dense_8b", (args.seq if args.seq != 4096 else 8192)
         tp, pp = (args.tp, args.pp) if world > 1 else (1, 1)
@@ -307,7 +314,7 @@ def run_pretrain_workload(args, world, rank, local):
                                                 ("tensor_parallel" if tp > 1 else "pipeline_parallel"))
         gb = args.global_batch or 64
         dist_cfg = {"strategy": strategy, "tensor_parallel_size": tp, "pipeline_parallel_size": pp,
-                    "timeout_s": 600}
+                    "timeout_s": 600, "fused_comm": args.fused_comm}
         layout = f"tp{tp}xpp{pp}xdp{dp}"
         micro = args.micro
     else:
@@ -315,7 +322,8 @@ def run_pretrain_workload(args, world, rank, local):
         dp = world
         strategy = "expert_parallel" if world > 1 else "single"
         gb = args.global_batch or 4 * world
-        dist_cfg = {"strategy": strategy, "expert_parallel_size": max(world, 1), "timeout_s": 600}
+        dist_cfg = {"strategy": strategy, "expert_parallel_size": max(world, 1), "timeout_s": 600,
+                    "fused_comm": args.fused_comm}
         layout = f"ep{world}" if world > 1 else "single"
         micro = 1
     rows = gb // dp
@@ -374,7 +382,10 @@ def run_pretrain_workload(args, world, rank, local):
                "config": {"model": preset + (f" ({args.layers} layers)" if args.layers else ""), "global_batch": gb,
                           "seq_len": seq, "parallelism": layout, "micro_batches": micro,
                           "params_full_model": n_params_full, "workload": args.workload,
-                          "l2": "inputs larger than L2", "final_loss": trainer.history[-1].loss},
+                          "l2": "inputs larger than L2", "final_loss": trainer.history[-1].loss,
+                          "tp_allreduce": (("fused tcgen05 GEMM epilogue over peer memory"
+                                            if tp_fused_used() else "nccl") if args.workload == "mesh8b"
+                                           and world > 1 and tp > 1 else None)},
                "clocks": clk, "e2e": None, "gpu_launches": int(launches), "impl": "ours"}
     emit(rank, payload)
     strat.teardown()

@@ -379,6 +379,31 @@ void gemm_grouped(int64_t mode, int64_t b_mn, int64_t epi, const at::Tensor& A, 
            "gemm_grouped");
 }
 
+// out [M, N] = sum over the TP ranks of A_r [M, K] @ B_r [N, K]^T, reduced in the GEMM epilogue over peer memory.
+void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, const std::vector<int64_t>& part,
+                    const std::vector<int64_t>& flag, int64_t rank, int64_t epoch, double alpha,
+                    const at::Tensor& status, int64_t grid) {
+  check_bf16(A, "A");
+  check_bf16(B, "B");
+  check_dev(B, A, "B");
+  check_dev(out, A, "out");
+  check_dev(status, A, "status");
+  check_contig(A, "A");
+  check_contig(B, "B");
+  check_contig(out, "out");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && A.dim() == 2 && B.dim() == 2 && out.dim() == 2, "2-D bf16");
+  TORCH_CHECK(A.size(1) == B.size(1) && out.size(0) == A.size(0) && out.size(1) == B.size(0), "shape mismatch");
+  TORCH_CHECK(part.size() == flag.size() && !part.empty() && part.size() <= 8, "one partial / flag slot per rank");
+  TORCH_CHECK(status.scalar_type() == at::kInt, "status: int32");
+  std::vector<unsigned long long> pp(part.begin(), part.end()), ff(flag.begin(), flag.end());
+  const c10::cuda::CUDAGuard g(A.device());
+  CHECK_OK(rlb_gemm_allreduce((int)A.size(0), (int)B.size(0), (int)A.size(1), A.data_ptr(), A.size(1), B.data_ptr(),
+                              B.size(1), out.data_ptr(), out.size(1), (float)alpha, pp.data(), ff.data(),
+                              (int)part.size(), (int)rank, (int)epoch, status.data_ptr<int>(), (int)grid,
+                              cur_stream()),
+           "gemm_allreduce");
+}
+
 // ---------------------------------------------------------------- paged KV decode
 // q [B, Hq, D]; pools [num_blocks, Hkv, 16, D]; block_tables [B, max_blocks] int32; ctx_lens [B] int32
 at::Tensor paged_decode(const at::Tensor& q, const at::Tensor& k_pool, const at::Tensor& v_pool,
@@ -598,6 +623,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nf4_dequant", &nf4_dequant);
   m.def("gemm", &gemm);
   m.def("gemm_grouped", &gemm_grouped);
+  m.def("gemm_allreduce", &gemm_allreduce);
   m.def("paged_decode", &paged_decode);
   m.def("paged_write", &paged_write);
   m.def("sample", &sample);

@@ -35,7 +35,61 @@ constexpr int GROUP_M = 16;
 constexpr uint32_t WAIT_LIMIT = 1u << 26;  // polls before a wait is declared dead (seconds)
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 
-enum Epi : int { kStoreBF16 = 0, kStoreF32 = 1, kAccumF32 = 2 };
+enum Epi : int { kStoreBF16 = 0, kStoreF32 = 1, kAccumF32 = 2, kAllReduceBF16 = 3 };
+
+__device__ __forceinline__ int ld_acquire_sys_i32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys_i32(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+constexpr unsigned long long AR_WAIT_NS = 20ull * 1000 * 1000 * 1000;  // a peer's tile may take this long
+
+// Barrier over the four epilogue warps with a bounded wait (a hardware named barrier would wait forever
+// if one warp had left the tile loop on an abort): every warp adds one to a shared counter and waits
+// until it reaches the warp's running target.  Returns false (after recording the failure) on timeout.
+__device__ __forceinline__ bool epilogue_sync(volatile int* ctr, int& target, int* status, volatile int* abort_flag,
+                                              int lane) {
+  target += 4;
+  __syncwarp();
+  int ok = 1;
+  if (lane == 0) {
+    __threadfence();
+    atomicAdd((int*)ctr, 1);
+    long long polls = 0;
+    while (*ctr < target) {
+      if (++polls > (long long)(AR_WAIT_NS / 32)) {
+        ok = 0;
+        *abort_flag = 1;
+        if (status) atomicCAS(status, 0, 1 | (6 << 8));
+        break;
+      }
+      __nanosleep(32);
+    }
+    __threadfence();
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
 
 struct Params {
   int M, N, K;
@@ -50,6 +104,12 @@ struct Params {
   const int* k_begin;     // kGroupK: first reduction row of each group
   const int* k_len;       // kGroupK: reduction rows of each group (a multiple of BK; 0 gives a zero tile)
   int groups;             // kGroupK: number of groups; group g's C starts at C + g * M * ldc
+  // kAllReduceBF16 epilogue (tensor-parallel row-parallel output): this launch's slot of every rank's
+  // bf16 partial buffer ([M][N], ld N) and flag array (int32 [tiles][world]); all ranks run the same
+  // launch sequence with the same shapes and grid.
+  unsigned long long ar_part[8];
+  unsigned long long ar_flag[8];
+  int ar_world, ar_rank, ar_epoch;
 };
 
 // kGroupM: C rows are grouped in BM-row tiles, each tile multiplies with its group's B.
@@ -115,6 +175,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = (uint32_t*)(tempty + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  volatile int* ep_ctr = abort_flag + 1;  // epilogue-warp barrier counter (all-reduce epilogue)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
@@ -131,6 +192,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
       sm100::mbar_init(&tempty[b], 4);
     }
     *abort_flag = 0;
+    *ep_ctr = 0;
     sm100::fence_barrier_init();
     sm100::prefetch_tensormap(&tma_a);
     sm100::prefetch_tensormap(&tma_b);
@@ -241,6 +303,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int acc = 0;
     uint32_t acc_phase = 0;
+    int ep_target = 0;
     for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
       const Tile tl = tile_at(p, t, num_m, num_n, nk);
       if (tl.skip) continue;
@@ -263,6 +326,114 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
       }
       sm100::tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+      if constexpr (EPI == kAllReduceBF16) {
+        // pass 1: this rank's bf16 partial of the tile into its own buffer, then the accumulator is free
+        __nv_bfloat16* mine = (__nv_bfloat16*)p.ar_part[p.ar_rank];
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          sm100::tmem_ld32(tbase + c * 32, r);
+          sm100::tmem_ld_wait();
+          const int col0 = n0 + c * 32;
+          if (row < p.M && col0 < p.N) {
+            __nv_bfloat16* out = mine + (long long)row * p.N + col0;
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 pk;
+              uint32_t* w = (uint32_t*)&pk;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[v * 8 + 2 * e]) * p.alpha,
+                                                         __uint_as_float(r[v * 8 + 2 * e + 1]) * p.alpha);
+                w[e] = *(uint32_t*)&h;
+              }
+              *(uint4*)(out + v * 8) = pk;
+            }
+          }
+        }
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&tempty[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        // publish the tile to every rank, then wait (bounded) for every rank's partial of it
+        if (!epilogue_sync(ep_ctr, ep_target, p.status, abort_flag, lane)) break;
+        const int tile = t;
+        if (warp == 2 && lane == 0) {
+          __threadfence_system();
+          for (int r2 = 0; r2 < p.ar_world; ++r2)
+            st_release_sys_i32((int*)p.ar_flag[r2] + (long long)tile * p.ar_world + p.ar_rank, p.ar_epoch);
+          const int* fl = (const int*)p.ar_flag[p.ar_rank] + (long long)tile * p.ar_world;
+          const unsigned long long t0 = now_ns();
+          long long polls = 0;
+          for (int r2 = 0; r2 < p.ar_world && !*abort_flag; ++r2) {
+            while (ld_acquire_sys_i32(fl + r2) < p.ar_epoch) {
+              if (++polls > (long long)(AR_WAIT_NS / 32) || now_ns() - t0 > AR_WAIT_NS) {
+                fail(p.status, abort_flag, 5);
+                break;
+              }
+              __nanosleep(32);
+            }
+          }
+        }
+        if (!epilogue_sync(ep_ctr, ep_target, p.status, abort_flag, lane)) break;
+        if (*abort_flag) break;
+        // pass 2: sum every rank's bf16 partial in rank order (identical on all ranks), store bf16.  Two
+        // 32-column chunks per round: 8 loads of 16 B in flight per rank before the adds (peer loads are
+        // NVLink round trips).  Plain loads: the flag acquire and the barrier above order them after
+        // the peers' stores, and no address of this tile was read earlier in this launch.
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; c += 2) {
+          const int col0 = n0 + c * 32;
+          if (row >= p.M || col0 >= p.N) continue;
+          const bool two = col0 + 32 < p.N;
+          float sacc[2][32];
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) sacc[h][e] = 0.f;
+          for (int r2 = 0; r2 < p.ar_world; ++r2) {
+            const __nv_bfloat16* src = (const __nv_bfloat16*)p.ar_part[r2] + (long long)row * p.N + col0;
+            uint4 raw[2][4];
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int v = 0; v < 4; ++v)
+                raw[h][v] = (h == 0 || two) ? *(const uint4*)(src + h * 32 + v * 8) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                const __nv_bfloat162* hv = (const __nv_bfloat162*)&raw[h][v];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f = __bfloat1622float2(hv[e]);
+                  sacc[h][v * 8 + 2 * e] += f.x;
+                  sacc[h][v * 8 + 2 * e + 1] += f.y;
+                }
+              }
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (h == 1 && !two) break;
+            __nv_bfloat16* out = (__nv_bfloat16*)p.C + (long long)row * p.ldc + col0 + h * 32;
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 pk;
+              uint32_t* w = (uint32_t*)&pk;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                __nv_bfloat162 hh = __floats2bfloat162_rn(sacc[h][v * 8 + 2 * e], sacc[h][v * 8 + 2 * e + 1]);
+                w[e] = *(uint32_t*)&hh;
+              }
+              *(uint4*)(out + v * 8) = pk;
+            }
+          }
+        }
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -384,7 +555,8 @@ cudaError_t rlb_gemm(int a_mn, int b_mn, int epi, int M, int N, int K, const voi
   if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
   if ((lda % 8) || (ldb % 8)) return cudaErrorInvalidPitchValue;
   if ((((uintptr_t)A) & 15) || (((uintptr_t)B) & 15)) return cudaErrorInvalidDevicePointer;
-  Params p{M, N, K, C, ldc, alpha, status, kPlain, nullptr, 0, nullptr, nullptr, 0};
+  Params p{};
+  p.M = M; p.N = N; p.K = K; p.C = C; p.ldc = ldc; p.alpha = alpha; p.status = status; p.mode = kPlain;
 #define RLB_GEMM_CASE(AM, BMN, E) \
   if (a_mn == AM && b_mn == BMN && epi == E) return launch<AM, BMN, E>(A, lda, B, ldb, p, sms, s);
   RLB_GEMM_CASE(0, 0, 0)
@@ -415,7 +587,9 @@ cudaError_t rlb_gemm_grouped(int mode, int b_mn, int epi, int M, int N, int K, c
   if ((((uintptr_t)A) & 15) || (((uintptr_t)B) & 15)) return cudaErrorInvalidDevicePointer;
   if (mode == kGroupM) {
     if (!tile_group || (b_mn && K % BK)) return cudaErrorInvalidValue;
-    Params p{M, N, K, C, ldc, alpha, status, kGroupM, tile_group, b_mn ? K : N, nullptr, nullptr, 0};
+    Params p{};
+    p.M = M; p.N = N; p.K = K; p.C = C; p.ldc = ldc; p.alpha = alpha; p.status = status;
+    p.mode = kGroupM; p.tile_group = tile_group; p.b_group_rows = b_mn ? K : N;
     const long long brows = (long long)groups * (b_mn ? K : N);
     if (b_mn == 0 && epi == kStoreBF16) return launch<0, 0, kStoreBF16>(A, lda, B, ldb, p, sms, s, 0, brows);
     if (b_mn == 1 && epi == kStoreBF16) return launch<0, 1, kStoreBF16>(A, lda, B, ldb, p, sms, s, 0, brows);
@@ -423,11 +597,40 @@ cudaError_t rlb_gemm_grouped(int mode, int b_mn, int epi, int M, int N, int K, c
   }
   if (mode == kGroupK) {
     if (!k_begin || !k_len || k_total <= 0) return cudaErrorInvalidValue;
-    Params p{M, N, K, C, ldc, alpha, status, kGroupK, nullptr, 0, k_begin, k_len, groups};
+    Params p{};
+    p.M = M; p.N = N; p.K = K; p.C = C; p.ldc = ldc; p.alpha = alpha; p.status = status;
+    p.mode = kGroupK; p.k_begin = k_begin; p.k_len = k_len; p.groups = groups;
     if (epi == kStoreBF16) return launch<1, 1, kStoreBF16>(A, lda, B, ldb, p, sms, s, k_total, k_total);
     if (epi == kStoreF32) return launch<1, 1, kStoreF32>(A, lda, B, ldb, p, sms, s, k_total, k_total);
     if (epi == kAccumF32) return launch<1, 1, kAccumF32>(A, lda, B, ldb, p, sms, s, k_total, k_total);
     return cudaErrorNotSupported;
   }
   return cudaErrorInvalidValue;
+}
+
+// Tensor-parallel row-parallel linear with the all-reduce in the epilogue: C = sum over ranks of
+// alpha * A_r B_r^T (A [M][K], B [N][K], both K-major; C bf16 [M][ldc]).  part / flag: this launch's
+// slot of every rank's partial buffer (bf16 [M][N]) and tile-flag array (int32 [tiles][world]); epoch
+// grows by one per use of the slot.  N must be a multiple of 32 and every rank must make the same call
+// (same shapes, same grid) in the same order.
+cudaError_t rlb_gemm_allreduce(int M, int N, int K, const void* A, long long lda, const void* B, long long ldb,
+                               void* C, long long ldc, float alpha, const unsigned long long* part,
+                               const unsigned long long* flag, int world, int rank, int epoch, int* status,
+                               int grid, cudaStream_t s) {
+  using namespace gemm;
+  if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+  if ((lda % 8) || (ldb % 8) || (N % 32) || (ldc % 8)) return cudaErrorInvalidPitchValue;
+  if ((((uintptr_t)A) & 15) || (((uintptr_t)B) & 15) || (((uintptr_t)C) & 15)) return cudaErrorInvalidDevicePointer;
+  if (world < 1 || world > 8 || rank < 0 || rank >= world || grid < 1) return cudaErrorInvalidValue;
+  Params p{};
+  p.M = M; p.N = N; p.K = K; p.C = C; p.ldc = ldc; p.alpha = alpha; p.status = status; p.mode = kPlain;
+  for (int r = 0; r < world; ++r) {
+    if ((part[r] & 15) || (flag[r] & 3)) return cudaErrorInvalidDevicePointer;
+    p.ar_part[r] = part[r];
+    p.ar_flag[r] = flag[r];
+  }
+  p.ar_world = world;
+  p.ar_rank = rank;
+  p.ar_epoch = epoch;
+  return launch<0, 0, kAllReduceBF16>(A, lda, B, ldb, p, grid, s);
 }

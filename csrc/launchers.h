@@ -55,6 +55,12 @@ cudaError_t rlb_gemm_grouped(int mode, int b_mn, int epi, int M, int N, int K, c
                              const int* tile_group, const int* k_begin, const int* k_len, long long k_total,
                              int* status, int sms, cudaStream_t s);
 
+// Row-parallel linear with the tensor-parallel all-reduce fused into the GEMM epilogue.
+cudaError_t rlb_gemm_allreduce(int M, int N, int K, const void* A, long long lda, const void* B, long long ldb,
+                               void* C, long long ldc, float alpha, const unsigned long long* part,
+                               const unsigned long long* flag, int world, int rank, int epoch, int* status,
+                               int grid, cudaStream_t s);
+
 cudaError_t rlb_paged_decode(const void* q, const void* k_pool, const void* v_pool, const int* block_tables,
                              const int* ctx_lens, void* out, float* part_acc, float* part_ml, int B, int Hq, int Hkv,
                              int D, int max_blocks, int num_blocks, int split_tokens, int n_splits, float scale,

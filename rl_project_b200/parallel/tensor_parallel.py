@@ -14,7 +14,9 @@
 Each sharded module gets ``tp_group``: its forward applies ``copy_to_tp``
 (identity forward, all-reduce of the input gradient backward) on entry and
 ``reduce_from_tp`` (all-reduce forward, identity backward) after the row-split
-projection, adding a bias once after the reduction.  Norms, embeddings and the
+projection, adding a bias once after the reduction.  On NCCL GPU ranks the
+row-split projection and its all-reduce are one tcgen05 GEMM that reduces
+over peer memory in its epilogue (parallel/tp_fused.py).  Norms, embeddings and the
 LM head stay replicated: their inputs and gradients are identical on every TP
 rank, so they need no synchronisation.  Every rank of a TP group must see the
 same micro-batch.
@@ -137,8 +139,13 @@ def apply_tensor_parallel(model: nn.Module, group: Any, rank: int, size: int) ->
 def row_parallel_out(x: torch.Tensor, lin: nn.Module, group: Any) -> torch.Tensor:
     """``lin(x)`` for a column-split ``lin``: local GEMM, all-reduce over the group, bias once."""
     from rl_project_b200.ops.linear import linear
+    from rl_project_b200.parallel.tp_fused import reducer_for, row_parallel_linear_fused
 
     if type(lin) is nn.Linear:
+        reducer = reducer_for(group, x.reshape(-1, x.shape[-1]), lin.weight.shape[0])
+        if reducer is not None:  # GEMM with the all-reduce in its epilogue (peer memory, tile by tile)
+            y = row_parallel_linear_fused(x, lin.weight, reducer)
+            return y + lin.bias if lin.bias is not None else y
         y = linear(x, lin.weight, None)
     else:
         y = nn.functional.linear(x, lin.weight)

@@ -165,3 +165,46 @@ def test_parameter_broadcast_nvls_and_nccl():
     assert r0["on"]["mode"] == "nvls" and r0["off"]["mode"] == "nccl"
     for mc in ("on", "off"):
         assert r0[mc]["sums"] == r1[mc]["sums"] and r0[mc]["first"] == r1[mc]["first"], mc
+
+
+def _tp_worker(rank, port, out):
+    import datetime
+
+    import torch.distributed as dist
+
+    from rl_project_b200.parallel.tp_fused import GemmAllReduce
+
+    _env(rank, port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    red = GemmAllReduce(None, 4096 * 1024, torch.device("cuda", rank))
+    res = []
+    for it, (M, N, K) in enumerate([(1000, 512, 256), (4096, 1024, 384), (130, 288, 64), (4096, 1024, 384),
+                                    (1000, 512, 256)]):  # more launches than slots, mixed shapes
+        g = torch.Generator(device="cuda").manual_seed(1000 * it + rank)
+        x = (torch.randn(M, K, device="cuda", generator=g) / K ** 0.5).bfloat16()
+        w = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+        y = red(x, w)
+        part = (x.float() @ w.float().t()).bfloat16().float()  # each rank's partial, rounded like the kernel's
+        ref = part.clone()
+        dist.all_reduce(ref)
+        err = float((y.float() - ref).abs().max() / ref.abs().max())
+        digest = torch.tensor([float(y.float().double().sum())], device="cuda", dtype=torch.float64)
+        all_d = [torch.zeros_like(digest) for _ in range(WORLD)]
+        dist.all_gather(all_d, digest)
+        res.append({"err": err, "identical": len({float(d) for d in all_d}) == 1})
+    torch.cuda.synchronize()
+    red.check()
+    red.close()
+    torch.save(res, os.path.join(out, f"tp{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_gemm_allreduce_matches_nccl():
+    with tempfile.TemporaryDirectory() as out:
+        mp.start_processes(_tp_worker, args=(free_port(), out), nprocs=WORLD, join=True, start_method="spawn")
+        res = torch.load(os.path.join(out, "tp0.pt"))
+    for r in res:
+        assert r["identical"], res
+        assert r["err"] < 2e-2, res  # bf16 partials: the kernel's and cuBLAS's roundings may differ by an ulp
