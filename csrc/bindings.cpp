@@ -478,6 +478,36 @@ std::vector<at::Tensor> sample(const at::Tensor& logits, const at::Tensor& tempe
   return {tokens, lp};
 }
 
+void wait_peers(const at::Tensor& my_flags, int64_t world, int64_t slot, int64_t epoch, int64_t limit_ns,
+                const at::Tensor& status) {
+  check_cuda(my_flags, "my_flags");
+  check_dev(status, my_flags, "status");
+  TORCH_CHECK(my_flags.scalar_type() == at::kInt && status.scalar_type() == at::kInt, "int32 flags / status");
+  TORCH_CHECK(my_flags.numel() >= (slot + 1) * world, "flags too small for the slot");
+  const c10::cuda::CUDAGuard g(my_flags.device());
+  CHECK_OK(rlb_wait_peers(my_flags.data_ptr<int>(), (int)world, (int)slot, (int)epoch, (unsigned long long)limit_ns,
+                          status.data_ptr<int>(), cur_stream()),
+           "wait_peers");
+}
+
+// dst [rows, C] bf16: row i = row src_row[i] of rank src_rank[i]'s buffer (zeros where src_rank < 0)
+void gather_rows(const at::Tensor& src_base, const at::Tensor& src_rank, const at::Tensor& src_row,
+                 at::Tensor& dst, int64_t cap_rows, const at::Tensor& status) {
+  check_bf16(dst, "dst");
+  check_contig(dst, "dst");
+  for (const at::Tensor* t : {&src_base, &src_rank, &src_row, &status}) check_dev(*t, dst, "gather table");
+  TORCH_CHECK(src_base.scalar_type() == at::kLong && src_rank.scalar_type() == at::kInt &&
+                  src_row.scalar_type() == at::kInt && status.scalar_type() == at::kInt,
+              "gather tables: int64 bases, int32 ranks / rows / status");
+  TORCH_CHECK(src_rank.numel() == dst.size(0) && src_row.numel() == dst.size(0), "one source per row");
+  const c10::cuda::CUDAGuard g(dst.device());
+  CHECK_OK(rlb_gather_rows(reinterpret_cast<const unsigned long long*>(src_base.data_ptr<int64_t>()),
+                           src_rank.data_ptr<int>(), src_row.data_ptr<int>(), dst.size(0), (int)dst.size(1),
+                           cap_rows, (int)src_base.numel(), dst.data_ptr(), status.data_ptr<int>(), sm_count(),
+                           cur_stream()),
+           "gather_rows");
+}
+
 void multimem_bcast(const at::Tensor& src, int64_t mc_dst, int64_t nbytes) {
   check_cuda(src, "src");
   TORCH_CHECK(src.is_contiguous() && (int64_t)src.nbytes() >= nbytes, "src: contiguous, at least nbytes");
@@ -634,5 +664,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_close", &peer_close);
   m.def("signal_peers", &signal_peers);
   m.def("multimem_bcast", &multimem_bcast);
+  m.def("wait_peers", &wait_peers);
+  m.def("gather_rows", &gather_rows);
   m.def("fused_reduce_scatter", &fused_reduce_scatter);
 }

@@ -179,6 +179,44 @@ __global__ void __launch_bounds__(kRsThreads) fused_rs_kernel(
   }
 }
 
+// Row gather over peer memory (expert-parallel dispatch / combine): dst row i = row src_row[i] of rank
+// src_rank[i]'s buffer (C bf16 per row), or zeros where src_rank[i] < 0.  A row index outside the source's
+// capacity is reported (kBadIndex) and its row left zero.
+__global__ void __launch_bounds__(256) gather_rows_kernel(const unsigned long long* __restrict__ src_base,
+                                                          const int* __restrict__ src_rank,
+                                                          const int* __restrict__ src_row, long long rows, int C,
+                                                          long long cap_rows, int world,
+                                                          __nv_bfloat16* __restrict__ dst, int* status) {
+  const int vec = C / 8;
+  const long long total = rows * vec;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride * 4) {
+    uint4 v[4];
+    long long di[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long j = i + u * stride;
+      di[u] = -1;
+      v[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (j >= total) continue;
+      const long long r = j / vec;
+      const int c = (int)(j % vec);
+      di[u] = r * C + c * 8;
+      const int sr = src_rank[r];
+      const int row = src_row[r];
+      if (sr < 0) continue;
+      if (sr >= world || row < 0 || row >= cap_rows) {
+        report(status, kBadIndex);
+        continue;
+      }
+      v[u] = ld16(reinterpret_cast<const __nv_bfloat16*>(src_base[sr]) + (long long)row * C + c * 8);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (di[u] >= 0) *reinterpret_cast<uint4*>(dst + di[u]) = v[u];
+  }
+}
+
 // Broadcast through NVSwitch: the source rank stores each 16-byte vector once to the multicast
 // address and the switch writes it into every rank's copy of the buffer (source egress = one copy,
 // whatever the world size).  Ends with a system-scope fence so the stores are ordered before the
@@ -236,5 +274,26 @@ cudaError_t rlb_fused_reduce_scatter(const unsigned long long* buf_ptrs, unsigne
   else if (world <= 4) fused_rs_kernel<4, 4, false><<<g, b, 0, s>>>(RLB_RS_ARGS);
   else fused_rs_kernel<8, 2, false><<<g, b, 0, s>>>(RLB_RS_ARGS);
 #undef RLB_RS_ARGS
+  return cudaGetLastError();
+}
+
+cudaError_t rlb_wait_peers(const int* my_flags, int world, int slot, int epoch, unsigned long long limit_ns,
+                           int* status, cudaStream_t s) {
+  if (world < 1 || world > 32) return cudaErrorInvalidValue;
+  wait_peers_kernel<<<1, 32, 0, s>>>(my_flags, world, slot, epoch, limit_ns, status);
+  return cudaGetLastError();
+}
+
+cudaError_t rlb_gather_rows(const unsigned long long* src_base, const int* src_rank, const int* src_row,
+                            long long rows, int C, long long cap_rows, int world, void* dst, int* status, int sms,
+                            cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  if (C % 8 || (reinterpret_cast<uintptr_t>(dst) & 15)) return cudaErrorInvalidValue;
+  const long long total = rows * (C / 8);
+  long long grid = (total + 1023) / 1024;
+  if (grid > 4LL * sms) grid = 4LL * sms;
+  if (grid < 1) grid = 1;
+  gather_rows_kernel<<<(int)grid, 256, 0, s>>>(src_base, src_rank, src_row, rows, C, cap_rows, world,
+                                               reinterpret_cast<__nv_bfloat16*>(dst), status);
   return cudaGetLastError();
 }

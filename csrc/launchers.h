@@ -86,6 +86,13 @@ cudaError_t rlb_rl_loss(const float* lp_new, const float* lp_old, const float* l
                         const float* adv, int G, int R, float eps, int token_level, int k3, float* pl_row,
                         float* kl_row, float* dpl, float* dkl, cudaStream_t s);
 
+// Bounded wait for every peer's flag of `slot`; row gather from peer buffers (expert-parallel exchange).
+cudaError_t rlb_wait_peers(const int* my_flags, int world, int slot, int epoch, unsigned long long limit_ns,
+                           int* status, cudaStream_t s);
+cudaError_t rlb_gather_rows(const unsigned long long* src_base, const int* src_rank, const int* src_row,
+                            long long rows, int C, long long cap_rows, int world, void* dst, int* status, int sms,
+                            cudaStream_t s);
+
 // NVLS broadcast: store `nbytes` (multiple of 16) from local `src` through the multicast address `mc_dst`.
 cudaError_t rlb_multimem_bcast(const void* src, unsigned long long mc_dst, long long nbytes, int sms,
                                cudaStream_t s);

@@ -22,9 +22,11 @@ over the replicas that own the same expert (several EP groups).  The
 aux-loss-free router bias is updated from global counts so it stays identical
 on every rank.
 
-Communication is NCCL all-to-all today (the fused router-permutation +
-all-to-all + grouped-GEMM kernel over NVLink peer memory is the planned
-replacement).
+On NCCL GPU ranks the exchange runs over NVLink peer memory instead
+(parallel/expert_p2p.py: one gather kernel per exchange pulls rows straight
+into the grouped-GEMM layout, no all-to-all and no re-permutation); the NCCL
+all-to-all path below is the fallback (gloo, ``fused_comm`` off, buffers too
+small).
 """
 
 from __future__ import annotations
@@ -49,7 +51,12 @@ class _NoExpert(nn.Module):
 def expert_parallel_moe(layer: nn.Module, xf: torch.Tensor, weights: torch.Tensor,
                         indices: torch.Tensor) -> torch.Tensor:
     from rl_project_b200.models.moe.layer import sort_by_expert
+    from rl_project_b200.parallel import expert_p2p
 
+    if expert_p2p.usable(layer, xf):  # peer-memory pulls straight into the grouped-GEMM layout
+        out = expert_p2p.expert_parallel_moe_p2p(layer, xf, weights, indices)
+        if out is not None:
+            return out
     group = layer.expert_group
     ep = dist.get_world_size(group)
     E = layer.n_experts
@@ -115,8 +122,16 @@ class ExpertParallelStrategy:
             g = dist.new_group(list(range(i, world, ep)))
             if rank % ep == i:
                 self.expert_dp_group = g
+        from rl_project_b200.parallel import expert_p2p
+
+        expert_p2p.set_enabled(getattr(self.cfg, "fused_comm", "auto") not in ("off", "nccl_baseline"))
 
     def teardown(self) -> None:
+        from rl_project_b200.parallel import expert_p2p
+
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+        expert_p2p.close_all()
         rt.destroy_process_group()
 
     def world_size(self) -> int:

@@ -208,3 +208,59 @@ def test_gemm_allreduce_matches_nccl():
     for r in res:
         assert r["identical"], res
         assert r["err"] < 2e-2, res  # bf16 partials: the kernel's and cuBLAS's roundings may differ by an ulp
+
+
+def _ep_worker(rank, port, out):
+    import datetime
+
+    import torch.distributed as dist
+
+    from rl_project_b200.core.config import model_spec_from_preset
+    from rl_project_b200.models.moe.layer import MoELayer
+    from rl_project_b200.parallel import expert_p2p
+    from rl_project_b200.parallel.expert import shard_experts
+
+    _env(rank, port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    torch.manual_seed(0)
+    spec = model_spec_from_preset("tiny", vocab_size=97, use_moe=True, n_experts=8, n_experts_active=2,
+                                  n_embd=128, moe_d_ff=192, n_shared_experts=1)
+    layer = MoELayer(spec).cuda().bfloat16()
+    shard_experts(layer, dist.group.WORLD, rank, WORLD)
+    g = torch.Generator(device="cuda").manual_seed(rank)
+    x = torch.randn(2, 96, 128, device="cuda", generator=g).bfloat16()
+    dy = torch.randn(2, 96, 128, device="cuda", generator=g).bfloat16()
+    res = {}
+    for mode in (True, False, True):
+        expert_p2p.set_enabled(mode)
+        layer.zero_grad(set_to_none=True)
+        xi = x.clone().requires_grad_(True)
+        y = layer(xi)
+        y.backward(dy)
+        res.setdefault(mode, []).append((y.float(), xi.grad.float(),
+                                         {n: p.grad.float().clone() for n, p in layer.named_parameters()
+                                          if p.grad is not None}))
+    torch.cuda.synchronize()
+    used = bool(expert_p2p._RINGS)
+    for r in expert_p2p._RINGS.values():
+        r.check()
+    expert_p2p.close_all()
+    (yp, dxp, gp), (yn, dxn, gn) = res[True][0], res[False][0]
+    errs = {"y": float((yp - yn).abs().max()), "dx": float((dxp - dxn).abs().max()),
+            "params": max(float((gp[n] - gn[n]).abs().max() / (gn[n].abs().max() + 1e-6)) for n in gn),
+            "same_params": set(gp) == set(gn), "used": used,
+            "repeat": float((res[True][1][0] - yp).abs().max())}
+    torch.save(errs, os.path.join(out, f"ep{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_expert_parallel_p2p_matches_nccl():
+    with tempfile.TemporaryDirectory() as out:
+        mp.start_processes(_ep_worker, args=(free_port(), out), nprocs=WORLD, join=True, start_method="spawn")
+        errs = [torch.load(os.path.join(out, f"ep{r}.pt")) for r in range(WORLD)]
+    for e in errs:
+        assert e["used"] and e["same_params"], e
+        assert e["y"] < 1e-2 and e["dx"] < 1e-2 and e["repeat"] == 0.0, e
+        assert e["params"] < 2e-2, e
