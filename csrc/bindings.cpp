@@ -516,6 +516,29 @@ void multimem_bcast(const at::Tensor& src, int64_t mc_dst, int64_t nbytes) {
            "multimem_bcast");
 }
 
+// ---------------------------------------------------------------- MoE router
+// -> {scores [N, E] fp32, w [N, k] fp32, idx [N, k] int64, counts [E] int32}
+std::vector<at::Tensor> moe_route(const at::Tensor& logits, const c10::optional<at::Tensor>& bias, int64_t k,
+                                  int64_t groups, int64_t limited, bool sigmoid, double route_scale) {
+  check_cuda(logits, "logits");
+  check_dev(bias, logits, "bias");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.is_contiguous(), "logits: fp32 [N, E]");
+  if (bias.has_value()) TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == logits.size(1), "bias: fp32 [E]");
+  const c10::cuda::CUDAGuard g(logits.device());
+  const long long N = logits.size(0);
+  const int E = (int)logits.size(1);
+  auto scores = at::empty_like(logits);
+  auto w = at::empty({N, k}, logits.options());
+  auto idx = at::empty({N, k}, logits.options().dtype(at::kLong));
+  auto counts = at::zeros({E}, logits.options().dtype(at::kInt));
+  CHECK_OK(rlb_moe_route(logits.data_ptr<float>(), bias.has_value() ? bias->data_ptr<float>() : nullptr, N, E,
+                         (int)k, (int)groups, (int)limited, sigmoid ? 1 : 0, (float)route_scale,
+                         scores.data_ptr<float>(), w.data_ptr<float>(), lptr(idx), counts.data_ptr<int>(),
+                         cur_stream()),
+           "moe_route");
+  return {scores, w, idx, counts};
+}
+
 // ---------------------------------------------------------------- fused RL loss
 // -> {pl_row [G], kl_row [G], dpl [G, R], dkl [G, R]}; all inputs fp32 [G, R] (adv [G]).
 std::vector<at::Tensor> rl_loss(const at::Tensor& lp_new, const at::Tensor& lp_old, const at::Tensor& lp_ref,
@@ -658,6 +681,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_write", &paged_write);
   m.def("sample", &sample);
   m.def("rl_loss", &rl_loss);
+  m.def("moe_route", &moe_route);
   m.def("peer_alloc", &peer_alloc);
   m.def("peer_handle", &peer_handle);
   m.def("peer_open", &peer_open);

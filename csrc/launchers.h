@@ -97,6 +97,11 @@ cudaError_t rlb_gather_rows(const unsigned long long* src_base, const int* src_r
 cudaError_t rlb_multimem_bcast(const void* src, unsigned long long mc_dst, long long nbytes, int sms,
                                cudaStream_t s);
 
+// Fused MoE router after the router GEMM: scores, group-limited top-k, weights, per-expert counts.
+cudaError_t rlb_moe_route(const float* logits, const float* bias, long long N, int E, int k, int groups,
+                          int limited, int sigmoid, float route_scale, float* scores, float* w, long long* idx,
+                          int* counts, cudaStream_t s);
+
 // RMSNorm backward that allocates nothing (no counterpart in the reference):
 // the dw partial sums live in a fixed 4 MiB file-scope __device__ array per
 // device instead of a caller-allocated buffer.  Returns a cudaError_t value;

@@ -45,8 +45,24 @@ class ExpertGate(nn.Module):
     def aux_loss(self) -> Optional[torch.Tensor]:
         return self._aux_loss
 
+    def _fused_ok(self, x: torch.Tensor) -> bool:
+        from rl_project_b200.ops._ext import available
+
+        return (x.is_cuda and available() and self.n_experts <= 256 and self.topk <= 16
+                and self.n_expert_groups <= 32 and self.n_experts % self.n_expert_groups == 0)
+
     def route(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-        """Return ``(weights [N,k] fp32, indices [N,k], scores [N,E] fp32)``."""
+        """Return ``(weights [N,k] fp32, indices [N,k], scores [N,E] fp32)``.  On CUDA everything after the
+        router GEMM is one kernel (csrc/moe_router.cu); its counts are kept for ``forward``."""
+        if self._fused_ok(x):
+            logits = F.linear(x.float(), self.weight.float())
+            bias = self.expert_bias.float() if self.aux_loss_free else None  # the buffer follows .to(dtype)
+            w, idx, scores, counts = _FusedRoute.apply(
+                logits, bias, self.topk, self.n_expert_groups,
+                self.n_limited_groups, self.score_func == "sigmoid", float(self.route_scale))
+            self._fused_counts = counts
+            return w, idx, scores
+        self._fused_counts = None
         scores = F.linear(x.float(), self.weight.float())
         scores = scores.softmax(-1) if self.score_func == "softmax" else scores.sigmoid()
         select = scores + self.expert_bias if self.aux_loss_free else scores
@@ -66,7 +82,8 @@ class ExpertGate(nn.Module):
 
     def forward(self, x: torch.Tensor):
         w, idx, scores = self.route(x)
-        counts = torch.bincount(idx.reshape(-1), minlength=self.n_experts).float()
+        fc = getattr(self, "_fused_counts", None)
+        counts = fc.float() if fc is not None else torch.bincount(idx.reshape(-1), minlength=self.n_experts).float()
         self.last_counts = counts
         if self.training and self.aux_loss_free:
             with torch.no_grad():
@@ -82,3 +99,35 @@ class ExpertGate(nn.Module):
         else:
             self._aux_loss = x.new_zeros((), dtype=torch.float32)
         return w.type_as(x), idx
+
+
+class _FusedRoute(torch.autograd.Function):
+    """Router kernel forward; backward recomputes the (small) score -> weight graph in PyTorch."""
+
+    @staticmethod
+    def forward(ctx, logits, bias, k, groups, limited, sigmoid, route_scale):
+        from rl_project_b200.ops._ext import native
+
+        scores, w, idx, counts = native().moe_route(logits.contiguous(), bias, k, groups, limited, sigmoid,
+                                                     route_scale)
+        ctx.save_for_backward(logits, idx)
+        ctx.sigmoid, ctx.route_scale = sigmoid, route_scale
+        ctx.mark_non_differentiable(idx, counts)
+        return w, idx, scores, counts
+
+    @staticmethod
+    def backward(ctx, dw, didx, dscores, dcounts):
+        logits, idx = ctx.saved_tensors
+        with torch.enable_grad():
+            lg = logits.detach().requires_grad_(True)
+            s = lg.sigmoid() if ctx.sigmoid else lg.softmax(-1)
+            w = s.gather(1, idx)
+            if ctx.sigmoid:
+                w = w / (w.sum(-1, keepdim=True) + 1e-8)
+            w = w * ctx.route_scale
+            outs, grads = [w], [dw if dw is not None else torch.zeros_like(w)]
+            if dscores is not None:
+                outs.append(s)
+                grads.append(dscores)
+            (g,) = torch.autograd.grad(outs, [lg], grads)
+        return g, None, None, None, None, None, None
