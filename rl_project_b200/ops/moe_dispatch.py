@@ -55,7 +55,7 @@ class _Dispatch(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dxp):
         m = ctx.maps
-        dx = dxp.index_select(0, m.row_of_slot).view(ctx.n, m.k, -1).sum(1)
+        dx = dxp.index_select(0, m.row_of_slot).view(ctx.n, m.k, dxp.shape[1]).sum(1)
         return dx, None
 
 
@@ -63,7 +63,7 @@ class _Combine(torch.autograd.Function):
     @staticmethod
     def forward(ctx, y, w, maps: RowMaps):
         n = w.shape[0]
-        ys = y.index_select(0, maps.row_of_slot).view(n, maps.k, -1)
+        ys = y.index_select(0, maps.row_of_slot).view(n, maps.k, y.shape[1])
         ctx.save_for_backward(ys, w)
         ctx.maps = maps
         return (ys.float() * w.unsqueeze(-1).float()).sum(1).to(y.dtype)

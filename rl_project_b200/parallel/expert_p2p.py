@@ -156,6 +156,7 @@ def build_maps(cnt_all: np.ndarray, me: int, El: int) -> Dict[str, np.ndarray]:
 
 
 _RINGS: Dict[Any, ExchangeRing] = {}
+_RETIRED: list = []  # rings replaced by larger ones, kept until teardown (pending backward passes use them)
 _ENABLED = os.environ.get("RLB_EP_P2P", "1") != "0"
 
 
@@ -170,26 +171,29 @@ def usable(layer, xf: torch.Tensor) -> bool:
             and dist.get_backend(g) == "nccl" and layer._grouped_ready(xf))
 
 
-def _ring_for(group, rows_needed: int, C: int, device) -> Optional[ExchangeRing]:
+def _ring_for(group, rows_needed: int, C: int, device) -> ExchangeRing:
+    """The group's ring, replaced by a larger one when this call needs more rows (routing can concentrate
+    on a few ranks).  Every rank computes ``rows_needed`` from the same all-gathered counts, so creating a
+    ring -- a collective -- happens on every rank at the same call."""
     key = group if group is not None else "world"
     r = _RINGS.get(key)
-    if r is None:
-        # sized once with headroom; every rank computes rows_needed from the same global counts
+    if r is None or r.C != C or rows_needed > r.slot_rows:
+        if r is not None:
+            _RETIRED.append(r)
         r = ExchangeRing(group, max(2 * rows_needed, 4096), C, device)
         _RINGS[key] = r
-    return r if (r.C == C and rows_needed <= r.slot_rows) else None
+    return r
 
 
 def close_all() -> None:
-    for r in _RINGS.values():
+    for r in list(_RINGS.values()) + _RETIRED:
         r.close()
     _RINGS.clear()
+    _RETIRED.clear()
 
 
 def expert_parallel_moe_p2p(layer, xf: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor):
-    """MoE layer over an expert-parallel group with peer-memory dispatch / combine; None if the exchange
-    buffers cannot hold this call (the caller then runs the NCCL path -- the decision is the same on every
-    rank, since it depends only on the all-gathered counts)."""
+    """MoE layer over an expert-parallel group with peer-memory dispatch / combine."""
     from rl_project_b200.ops.grouped_gemm import GroupedLayout
     from rl_project_b200.ops.moe_dispatch import RowMaps, combine, dispatch
 
@@ -210,8 +214,6 @@ def expert_parallel_moe_p2p(layer, xf: torch.Tensor, weights: torch.Tensor, indi
     m = build_maps(cnt_np, me, El)
     need = int(max(cnt_np.sum(1).max(), m["rows_all"].max()))
     ring = _ring_for(group, need, C, dev)
-    if ring is None:
-        return None
     host = np.concatenate([m["d_rank"], m["d_row"], m["c_rank"], m["c_row"], m["tile_group"], m["seg_start"],
                            m["seg_len"]]).astype(np.int32)
     tab = torch.from_numpy(host).pin_memory().to(dev, non_blocking=True)
