@@ -317,6 +317,8 @@ class DistributedConfig:
     fused_comm: str = "auto"  # auto | on | off | nccl_baseline
     fused_multicast: str = "off"  # off (CUDA IPC, peer loads) | on (NVLink multicast reduce) | symm
     fused_rs_ctas: int = 32  # CTAs of a fused reduce-scatter that overlaps backward compute
+    heartbeat_interval_s: float = 1.0  # rank liveness beats through the job's store (0 disables)
+    heartbeat_timeout_s: float = 60.0  # a peer silent this long fails the next step's health check
     timeout_s: float = 600.0
 
     def validate(self) -> None:

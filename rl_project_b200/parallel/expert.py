@@ -125,6 +125,9 @@ class ExpertParallelStrategy:
         from rl_project_b200.parallel import expert_p2p
 
         expert_p2p.set_enabled(getattr(self.cfg, "fused_comm", "auto") not in ("off", "nccl_baseline"))
+        from rl_project_b200.parallel import health
+
+        health.attach(self, self.cfg)
 
     def teardown(self) -> None:
         from rl_project_b200.parallel import expert_p2p
@@ -132,7 +135,14 @@ class ExpertParallelStrategy:
         if torch.cuda.is_available():
             torch.cuda.synchronize()
         expert_p2p.close_all()
+        from rl_project_b200.parallel import health
+
+        health.detach(self)
         rt.destroy_process_group()
+
+    def check_health(self) -> None:
+        if getattr(self, "monitor", None) is not None:
+            self.monitor.check()
 
     def world_size(self) -> int:
         return rt.world_size()

@@ -85,6 +85,9 @@ class MeshStrategy:
         # opt-in: at tensor-parallel 2 over NVLink 5 NCCL's all-reduce is short enough that the fused
         # epilogue measured ~2 % slower per step (its GEMM trails cuBLAS by more than the all-reduce it hides)
         tp_fused.set_enabled(getattr(self.cfg, "fused_comm", "auto") == "on")
+        from rl_project_b200.parallel import health
+
+        health.attach(self, self.cfg)
 
     def teardown(self) -> None:
         global _ACTIVE_MESH
@@ -94,7 +97,14 @@ class MeshStrategy:
         if torch.cuda.is_available():
             torch.cuda.synchronize()
         tp_fused.close_all()
+        from rl_project_b200.parallel import health
+
+        health.detach(self)
         rt.destroy_process_group()
+
+    def check_health(self) -> None:
+        if getattr(self, "monitor", None) is not None:
+            self.monitor.check()
 
     def world_size(self) -> int:
         return rt.world_size()

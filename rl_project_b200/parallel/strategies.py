@@ -61,6 +61,19 @@ class _ProcessGroupStrategy(SingleProcessStrategy):
         if not env.launched and not self.allow_single_process:
             raise DistributedConfigError(f"{self.name} strategy requires a torchrun launch (RANK/WORLD_SIZE not set)")
         self.info = rt.init_process_group(self.cfg.backend, timeout_s=self.cfg.timeout_s)
+        self.start_health_monitor()
+
+    def start_health_monitor(self) -> None:
+        from rl_project_b200.parallel.health import monitor_for_process_group
+
+        iv = float(getattr(self.cfg, "heartbeat_interval_s", 0.0) or 0.0)
+        self.monitor = monitor_for_process_group(iv, float(getattr(self.cfg, "heartbeat_timeout_s", 60.0))) \
+            if iv > 0 else None
+
+    def check_health(self) -> None:
+        """Raise DistributedTimeoutError if a peer rank stopped beating (called between steps)."""
+        if getattr(self, "monitor", None) is not None:
+            self.monitor.check()
 
     def is_main_process(self) -> bool:
         return rt.is_main_process()
@@ -75,6 +88,9 @@ class _ProcessGroupStrategy(SingleProcessStrategy):
         rt.barrier()
 
     def teardown(self) -> None:
+        if getattr(self, "monitor", None) is not None:
+            self.monitor.stop("teardown")
+            self.monitor = None
         rt.destroy_process_group()
 
     def unwrap_model(self, model: nn.Module) -> nn.Module:

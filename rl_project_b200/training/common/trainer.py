@@ -213,6 +213,8 @@ class Trainer:
 
     # ------------------------------------------------------------ one optimizer step
     def train_step(self) -> StepResult:
+        if self.strategy is not None and hasattr(self.strategy, "check_health"):
+            self.strategy.check_health()  # a dead peer fails here, before the step's first collective
         lr = self.current_lr()
         self._set_lr(lr)
         self._set_train_mode(True)
