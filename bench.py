@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Headline benchmark: dense-1B SFT training tokens/s on N B200 GPUs.
 
-Config: 16 layers, d_model 2048, 32 query / 8 KV heads,
+Config (the dense-1B SFT headline): 16 layers, d_model 2048, 32 query / 8 KV heads,
 head_dim 64, SwiGLU d_ff 8192, RMSNorm, RoPE theta 500000, vocab 128256, tied
 embeddings; seq 4096, 8 sequences per GPU (weak scaling), first 25% of each
 sequence prompt-masked; bf16; synthetic uniform token ids; random init.
@@ -33,7 +33,7 @@ sys.path.insert(0, HERE)
 
 METRIC = "train tokens/s (FSDP/TP/EP) + GRPO tokens/s at 1/2/4/8 B200 vs ref NCCL build"
 MODEL_NAME = "dense-1B (16L d2048 32q/8kv hd64 ff8192 V128256 tied, RoPE 5e5)"
-BASELINE_VALUE = None  # BASELINE.json "published" is empty for this config
+BASELINE_VALUE = None  # the reference published no number for this configuration
 
 
 def parse_args():
@@ -47,9 +47,9 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--workload", choices=["sft1b", "mesh8b", "moe", "grpo"], default="sft1b",
-                    help="sft1b: the headline (config 2). mesh8b: dense-8B pretrain on a TP x PP x DP mesh "
-                         "(config 3). moe: MLA+MoE pretrain with expert parallelism (config 4). grpo: GRPO "
-                         "rollout+update on one GPU (config 5 shape, see rl_project_b200.benchmarks.grpo).")
+                    help="sft1b: the headline (dense 1B SFT). mesh8b: dense-8B pretrain on a TP x PP x DP "
+                         "mesh (1F1B). moe: MLA+MoE pretrain with expert parallelism. grpo: GRPO rollout+update "
+                         "on one GPU (see rl_project_b200.benchmarks.grpo).")
     ap.add_argument("--tp", type=int, default=2)
     ap.add_argument("--pp", type=int, default=2)
     ap.add_argument("--micro", type=int, default=8)

@@ -1,4 +1,4 @@
-"""GRPO rollout + update throughput (BASELINE config 5 shape, scaled by flags).
+"""GRPO rollout + update throughput (the GRPO benchmark shape -- 8B, 256 prompts x 16 -- scaled by flags).
 
 One GRPO step = sample ``prompts x group`` completions with the paged-KV
 inference engine (prefix sharing: one prefill per prompt), score them with the
