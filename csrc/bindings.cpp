@@ -508,6 +508,17 @@ void gather_rows(const at::Tensor& src_base, const at::Tensor& src_rank, const a
            "gather_rows");
 }
 
+void allgather_pull(const at::Tensor& src_base, int64_t S, at::Tensor& dst) {
+  check_bf16(dst, "dst");
+  check_contig(dst, "dst");
+  check_dev(src_base, dst, "src_base");
+  TORCH_CHECK(src_base.scalar_type() == at::kLong && dst.numel() == S * src_base.numel(), "dst: [world * S] bf16");
+  const c10::cuda::CUDAGuard g(dst.device());
+  CHECK_OK(rlb_allgather_pull(reinterpret_cast<const unsigned long long*>(src_base.data_ptr<int64_t>()), S,
+                              (int)src_base.numel(), dst.data_ptr(), sm_count(), cur_stream()),
+           "allgather_pull");
+}
+
 void multimem_bcast(const at::Tensor& src, int64_t mc_dst, int64_t nbytes) {
   check_cuda(src, "src");
   TORCH_CHECK(src.is_contiguous() && (int64_t)src.nbytes() >= nbytes, "src: contiguous, at least nbytes");
@@ -688,6 +699,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_close", &peer_close);
   m.def("signal_peers", &signal_peers);
   m.def("multimem_bcast", &multimem_bcast);
+  m.def("allgather_pull", &allgather_pull);
   m.def("wait_peers", &wait_peers);
   m.def("gather_rows", &gather_rows);
   m.def("fused_reduce_scatter", &fused_reduce_scatter);

@@ -217,6 +217,27 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const unsigned long lo
   }
 }
 
+// All-gather over peer memory: dst[r * S + i] = rank r's shard[i] (bf16, S a multiple of 8).
+__global__ void __launch_bounds__(256) allgather_pull_kernel(const unsigned long long* __restrict__ src_base,
+                                                             long long S, int world, __nv_bfloat16* __restrict__ dst) {
+  const long long per = S / 8;
+  const long long total = per * world;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride * 4) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long j = i + u * stride;
+      if (j < total) v[u] = ld16(reinterpret_cast<const __nv_bfloat16*>(src_base[j / per]) + (j % per) * 8);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long j = i + u * stride;
+      if (j < total) *reinterpret_cast<uint4*>(dst + j * 8) = v[u];
+    }
+  }
+}
+
 // Broadcast through NVSwitch: the source rank stores each 16-byte vector once to the multicast
 // address and the switch writes it into every rank's copy of the buffer (source egress = one copy,
 // whatever the world size).  Ends with a system-scope fence so the stores are ordered before the
@@ -295,5 +316,17 @@ cudaError_t rlb_gather_rows(const unsigned long long* src_base, const int* src_r
   if (grid < 1) grid = 1;
   gather_rows_kernel<<<(int)grid, 256, 0, s>>>(src_base, src_rank, src_row, rows, C, cap_rows, world,
                                                reinterpret_cast<__nv_bfloat16*>(dst), status);
+  return cudaGetLastError();
+}
+
+cudaError_t rlb_allgather_pull(const unsigned long long* src_base, long long S, int world, void* dst, int sms,
+                               cudaStream_t s) {
+  if (S <= 0) return cudaSuccess;
+  if (S % 8 || world < 1 || world > 32 || (reinterpret_cast<uintptr_t>(dst) & 15)) return cudaErrorInvalidValue;
+  const long long total = S / 8 * world;
+  long long grid = (total + 1023) / 1024;
+  if (grid > 2LL * sms) grid = 2LL * sms;
+  if (grid < 1) grid = 1;
+  allgather_pull_kernel<<<(int)grid, 256, 0, s>>>(src_base, S, world, reinterpret_cast<__nv_bfloat16*>(dst));
   return cudaGetLastError();
 }

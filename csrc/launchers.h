@@ -93,6 +93,10 @@ cudaError_t rlb_gather_rows(const unsigned long long* src_base, const int* src_r
                             long long rows, int C, long long cap_rows, int world, void* dst, int* status, int sms,
                             cudaStream_t s);
 
+// All-gather of equal bf16 shards from every rank's peer-visible buffer into dst [world * S].
+cudaError_t rlb_allgather_pull(const unsigned long long* src_base, long long S, int world, void* dst, int sms,
+                               cudaStream_t s);
+
 // NVLS broadcast: store `nbytes` (multiple of 16) from local `src` through the multicast address `mc_dst`.
 cudaError_t rlb_multimem_bcast(const void* src, unsigned long long mc_dst, long long nbytes, int sms,
                                cudaStream_t s);

@@ -122,6 +122,7 @@ class FSDPStrategy(_ProcessGroupStrategy):
         self.group = None
         self._hooks: list = []
         self.fused = None  # FusedReduceScatter when gradients are reduced over peer memory
+        self.fused_ag = None  # FusedAllGather when parameters are gathered over peer memory
         self.owns_grad_clip = False
         self._final_micro = True
         self._in_backward = True  # False inside finish_gradients
@@ -205,6 +206,9 @@ class FSDPStrategy(_ProcessGroupStrategy):
         for u in self.units:
             u.grad_buf = torch.zeros(u.shard, dtype=torch.float32, device=device)
         self.owns_grad_clip = True
+        if mode == "on":  # parameter all-gather over peer memory too (opt-in)
+            self.fused_ag = fc.FusedAllGather(self.group, max(u.shard for u in self.units), device,
+                                              timeout_s=min(float(self.cfg.timeout_s), 300.0))
 
     # ---------------------------------------------------------------- collectives
     def _all_gather(self, u: _Unit) -> None:
@@ -213,6 +217,8 @@ class FSDPStrategy(_ProcessGroupStrategy):
         u.ensure_storage()
         if u.world == 1:
             u.full.copy_(u.shard16)
+        elif self.fused_ag is not None:
+            self.fused_ag.gather(u.shard16, u.full)
         elif self._gloo():
             parts = list(u.full.view(u.world, u.shard).unbind(0))
             dist.all_gather(parts, u.shard16)
@@ -470,10 +476,14 @@ class FSDPStrategy(_ProcessGroupStrategy):
         return norm
 
     def teardown(self) -> None:
-        if self.fused is not None:
+        if self.fused is not None or self.fused_ag is not None:
             torch.cuda.synchronize()
+        if self.fused is not None:
             self.fused.close()
             self.fused = None
+        if self.fused_ag is not None:
+            self.fused_ag.close()
+            self.fused_ag = None
         super().teardown()
 
     # ---------------------------------------------------------------- checkpoints

@@ -234,3 +234,57 @@ class FusedReduceScatter:
         if self.mem is not None:
             self.mem.close()
             self.mem = None
+
+
+class FusedAllGather:
+    """All-gather of equal bf16 shards over peer memory (FSDP parameter gather).
+
+    Each call copies this rank's shard into its slot of a CUDA-IPC ring, raises its flag for the slot on
+    every rank, waits (bounded, one thread) for every peer's flag and pulls all shards into the full
+    buffer with one kernel.  Calls are issued in the same order on every rank and on one stream, so a
+    rank refills a slot only after its previous pull -- which needed every peer's newer signal, raised
+    after that peer's own earlier pulls -- finished."""
+
+    def __init__(self, group, max_shard: int, device: torch.device, timeout_s: float = 120.0):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.max_shard = (int(max_shard) + ALIGN - 1) // ALIGN * ALIGN
+        self.device = device
+        self.mem = _IpcBuffers(group, NSLOTS * self.max_shard * 2, NSLOTS * self.world * 4, device)
+        self.buf = self.mem.buf_raw.view(torch.bfloat16).view(NSLOTS, self.max_shard)
+        self.flags = self.mem.flags_raw.view(torch.int32)
+        self.flags.zero_()
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)
+        slot_bytes = self.max_shard * 2
+        self.bases = torch.tensor([[b + s * slot_bytes for b in self.mem.buffer_ptrs] for s in range(NSLOTS)],
+                                  dtype=torch.int64, device=device)
+        self.flag_ptrs = torch.tensor(self.mem.flag_ptrs, dtype=torch.int64, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.limit_ns = int(timeout_s * 1e9)
+        self.seq = 0
+
+    def gather(self, shard: torch.Tensor, full: torch.Tensor) -> None:
+        """``full [world * S] = cat(every rank's shard [S])`` on the current stream."""
+        C = native()
+        S = shard.numel()
+        if S > self.max_shard or S % ALIGN or full.numel() != S * self.world:
+            raise DistributedConfigError(f"all-gather of {S} x {self.world} does not fit ({self.max_shard})")
+        q = self.seq
+        s, epoch = q % NSLOTS, q // NSLOTS + 1
+        self.seq += 1
+        self.buf[s, :S].copy_(shard.reshape(-1))
+        C.signal_peers(self.flag_ptrs, self.rank, s, epoch)
+        C.wait_peers(self.flags, self.world, s, epoch, self.limit_ns, self.status)
+        C.allgather_pull(self.bases[s], S, full.reshape(-1))
+
+    def check(self) -> None:
+        if int(self.status.item()):
+            raise DistributedTimeoutError("fused all-gather: a peer's flag did not arrive in time",
+                                          hint="A rank stopped or fell behind; check the other ranks' logs.")
+
+    def close(self) -> None:
+        if self.mem is not None:
+            self.mem.close()
+            self.mem = None
