@@ -1,27 +1,25 @@
-// Reduce-scatter fused with the fp32 cast, the 1/world scale, gradient
-// accumulation and the squared-norm partial, reading the peers' gradient
-// buffers directly over NVLink: the gradient path of sharded data parallel.
+// Communication kernels over NVLink peer memory (every buffer a peer reads is a CUDA-IPC mapping of
+// the owner's allocation, or the NVLink multicast address of a torch symmetric buffer):
 //
-// Every rank holds its bf16 gradient for one parameter unit in a slot of a
-// symmetric buffer (one allocation mapped on every GPU of the node).  Rank r
-// owns elements [r S, (r + 1) S) of the slot.  After a rank has filled its slot
-// it raises its flag for the slot in every peer's flag array (system-scope
-// release).  The reduce kernel on rank r waits (bounded) until every peer's
-// flag reached the slot's epoch, then for each owned element sums the world
-// copies -- with one `multimem.ld_reduce` through the slot's NVLink multicast
-// address (the switch adds the copies in fp32; each GPU receives S values
-// instead of (world - 1) S) or with plain peer loads -- scales by 1/world and
-// writes or adds the fp32 shard gradient, optionally adding the squares of the
-// final values into a norm accumulator.  No NCCL call, no bf16 reduce-scatter
-// output and no separate cast / scale / accumulate / norm kernels.
+// * fused_rs_kernel: sharded-data-parallel gradient reduce-scatter fused with the fp32 cast, the
+//   1/world scale, accumulation and the squared-norm partial.  The reference reduces through torch
+//   FSDP's NCCL reduce-scatter (src/forgeline/distributed/strategies.py:100-122) and DDP's
+//   per-parameter all-reduce (src/forgeline/training/common/trainer.py:122-139), then casts, averages
+//   and clips in separate passes.  Rank r owns elements [r S, (r + 1) S) of every rank's slot; it sums
+//   the world copies -- plain peer loads, or one `multimem.ld_reduce` through the multicast address
+//   (fp32 accumulation in the switch) -- and writes or adds the fp32 shard gradient.
+// * gather_rows_kernel: expert-parallel dispatch / combine, a row gather from the peers' slots
+//   straight into the grouped expert GEMM's layout (the reference runs experts in a Python loop on
+//   every rank: src/forgeline/models/moe/layer.py:32-38).
+// * allgather_pull_kernel: FSDP parameter all-gather by pulls.
+// * multimem_bcast_kernel: weight broadcast through NVSwitch multicast (the reference ships full
+//   state_dicts through Ray's object store: src/forgeline/orchestration/ray_backend.py:408-417).
 //
-// Waits are bounded: a flag that does not arrive within the time limit sets
-// `status` (kTimeout | slot << 8); the data kernel then returns without
-// writing, as does every later reduce until the caller clears the status.
-// Slot reuse is made safe by the caller's ordering (one communication stream,
-// a ring of slots, and the rule that a slot is refilled only after this rank's
-// reduce three uses back finished): the ordering argument is in
-// rl_project_b200/parallel/fused_comm.py.
+// Every exchange is "pack into my slot, raise my flag in every rank's flag array (system-scope
+// release), one thread waits (bounded) for every peer's flag, then pull".  A wait that runs out sets
+// `status` (kTimeout | slot << 8) and the data kernels that follow return without writing, as does
+// every later one until the caller clears the status.  Slot reuse is made safe by the callers'
+// ordering (rl_project_b200/parallel/fused_comm.py, expert_p2p.py).
 #include "common.cuh"
 
 namespace rlb {

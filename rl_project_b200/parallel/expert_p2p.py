@@ -1,6 +1,8 @@
 """Expert-parallel dispatch and combine over NVLink peer memory (comm path 4).
 
-The NCCL path (parallel/expert.py) exchanges counts, synchronises the host for
+The reference has no expert parallelism: every rank holds every expert and
+dispatch is a Python mask loop (``src/forgeline/models/moe/layer.py:32-38``).
+This framework's NCCL path (parallel/expert.py) exchanges counts, synchronises the host for
 split sizes, runs ``all_to_all_single`` twice per layer and pass, and
 re-permutes the received rows by expert on both sides.  Here every exchange is
 one pull:
