@@ -41,6 +41,11 @@ def row_maps(order: torch.Tensor, dest: torch.Tensor, rows: int, k: int) -> RowM
     return RowMaps(rows, k, row_of_slot, slot_of_row, torch.div(slot_of_row, k, rounding_mode="floor"))
 
 
+def _acc_dtype(dt: torch.dtype) -> torch.dtype:
+    """fp32 accumulation for 16-bit rows, the rows' own precision otherwise."""
+    return torch.float32 if dt in (torch.bfloat16, torch.float16) else dt
+
+
 def _with_zero_row(x: torch.Tensor) -> torch.Tensor:
     return torch.cat([x, x.new_zeros(1, x.shape[1])], 0)
 
@@ -66,14 +71,16 @@ class _Combine(torch.autograd.Function):
         ys = y.index_select(0, maps.row_of_slot).view(n, maps.k, y.shape[1])
         ctx.save_for_backward(ys, w)
         ctx.maps = maps
-        return (ys.float() * w.unsqueeze(-1).float()).sum(1).to(y.dtype)
+        acc = _acc_dtype(y.dtype)
+        return (ys.to(acc) * w.unsqueeze(-1).to(acc)).sum(1).to(y.dtype)
 
     @staticmethod
     def backward(ctx, dout):
         ys, w = ctx.saved_tensors
         m = ctx.maps
         n, k = w.shape
-        dw = (ys.float() * dout.float().unsqueeze(1)).sum(-1).to(w.dtype) if ctx.needs_input_grad[1] else None
+        acc = _acc_dtype(ys.dtype)
+        dw = (ys.to(acc) * dout.to(acc).unsqueeze(1)).sum(-1).to(w.dtype) if ctx.needs_input_grad[1] else None
         dy = None
         if ctx.needs_input_grad[0]:
             dslot = (dout.unsqueeze(1) * w.unsqueeze(-1).to(dout.dtype)).reshape(n * k, -1)
