@@ -604,9 +604,21 @@ at::Tensor peer_alloc(int64_t nbytes, int64_t device) {
 std::tuple<py::bytes, int64_t> peer_handle(const at::Tensor& buf) {
   check_cuda(buf, "buf");
   const c10::cuda::CUDAGuard g(buf.device());
+  // the driver entry point is looked up at run time (no link-time dependency on the driver library, so
+  // the extension also imports on machines without a GPU driver)
+  typedef CUresult (*AddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static AddressRangeFn address_range = nullptr;
+  if (!address_range) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    TORCH_CHECK(cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+                    q == cudaDriverEntryPointSuccess && fn != nullptr,
+                "peer_handle: cuMemGetAddressRange is not available from the driver");
+    address_range = (AddressRangeFn)fn;
+  }
   CUdeviceptr base = 0;
   size_t size = 0;
-  TORCH_CHECK(cuMemGetAddressRange(&base, &size, (CUdeviceptr)buf.data_ptr()) == CUDA_SUCCESS,
+  TORCH_CHECK(address_range(&base, &size, (CUdeviceptr)buf.data_ptr()) == CUDA_SUCCESS,
               "peer_handle: cuMemGetAddressRange failed");
   const int64_t offset = (int64_t)((CUdeviceptr)buf.data_ptr() - base);
   TORCH_CHECK(offset >= 0 && (size_t)(offset + buf.nbytes()) <= size, "peer_handle: buffer outside its allocation");
