@@ -195,7 +195,8 @@ def close_all() -> None:
 
 
 def expert_parallel_moe_p2p(layer, xf: torch.Tensor, weights: torch.Tensor, indices: torch.Tensor):
-    """MoE layer over an expert-parallel group with peer-memory dispatch / combine."""
+    """MoE layer over an expert-parallel group with peer-memory dispatch / combine (None: the exchange
+    buffers could not be created on this node; the caller runs the NCCL path)."""
     from rl_project_b200.ops.grouped_gemm import GroupedLayout
     from rl_project_b200.ops.moe_dispatch import RowMaps, combine, dispatch
 
@@ -215,7 +216,14 @@ def expert_parallel_moe_p2p(layer, xf: torch.Tensor, weights: torch.Tensor, indi
     cnt_np = cnt_all.cpu().numpy().astype(np.int64)  # the layer's one host synchronisation
     m = build_maps(cnt_np, me, El)
     need = int(max(cnt_np.sum(1).max(), m["rows_all"].max()))
-    ring = _ring_for(group, need, C, dev)
+    try:
+        ring = _ring_for(group, need, C, dev)
+    except Exception as e:  # no peer mapping on this node: fails alike on every rank, before its collectives
+        import warnings
+
+        warnings.warn(f"peer-memory expert exchange unavailable ({e}); using NCCL all-to-all")
+        set_enabled(False)
+        return None
     host = np.concatenate([m["d_rank"], m["d_row"], m["c_rank"], m["c_row"], m["tile_group"], m["seg_start"],
                            m["seg_len"]]).astype(np.int32)
     tab = torch.from_numpy(host).pin_memory().to(dev, non_blocking=True)

@@ -200,9 +200,18 @@ class FSDPStrategy(_ProcessGroupStrategy):
         # slots sized for the largest block unit; larger units (the root) go through in chunks
         blocks = [u for u in self.units if u is not self.root] or self.units
         chunk = max(u.shard for u in blocks)
-        self.fused = fc.FusedReduceScatter(self.group, chunk * world, device,
-                                           multicast=getattr(self.cfg, "fused_multicast", "off"),
-                                           timeout_s=min(float(self.cfg.timeout_s), 300.0))
+        try:
+            self.fused = fc.FusedReduceScatter(self.group, chunk * world, device,
+                                               multicast=getattr(self.cfg, "fused_multicast", "off"),
+                                               timeout_s=min(float(self.cfg.timeout_s), 300.0))
+        except Exception as e:  # e.g. no peer mapping on this node: the same on every rank, before any collective
+            if mode == "on":
+                raise
+            import warnings
+
+            warnings.warn(f"fused reduce-scatter unavailable ({e}); using NCCL's")
+            self.fused = None
+            return
         for u in self.units:
             u.grad_buf = torch.zeros(u.shard, dtype=torch.float32, device=device)
         self.owns_grad_clip = True
