@@ -233,6 +233,31 @@ class StepArrays:
     quality: np.ndarray
 
 
+@dataclass
+class StepContext:
+    """One episode's raw per-step scalars (``src/forgeline/domains/allocation/policies.py:41-51`` fields);
+    ``StepArrays`` holds the same for a batch of episodes."""
+
+    t: int
+    horizon: int
+    remaining: float
+    budget: float
+    cum_spend: float
+    value: float
+    cost: float
+    quality: float
+
+    @classmethod
+    def from_arrays(cls, a: "StepArrays", i: int = 0) -> "StepContext":
+        return cls(a.t, a.horizon, float(a.remaining[i]), float(a.budget), float(a.cum_spend[i]),
+                   float(a.value[i]), float(a.cost[i]), float(a.quality[i]))
+
+    def to_arrays(self) -> "StepArrays":
+        one = lambda v: np.asarray([v], dtype=np.float64)  # noqa: E731
+        return StepArrays(self.t, self.horizon, one(self.remaining), self.budget, one(self.cum_spend),
+                          one(self.value), one(self.cost), one(self.quality))
+
+
 class BudgetedAllocationEnv:
     """Single-episode view over a one-episode ``VectorEnv``."""
 

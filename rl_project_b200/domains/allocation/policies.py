@@ -23,7 +23,7 @@ import torch
 import torch.nn as nn
 
 from rl_project_b200.core.errors import ConfigError
-from rl_project_b200.domains.allocation.env import OBS_DIM, AllocationEnvConfig, StepArrays
+from rl_project_b200.domains.allocation.env import OBS_DIM, AllocationEnvConfig, StepArrays, StepContext  # noqa: F401
 
 
 def one_hot(actions: np.ndarray, n: int) -> np.ndarray:

@@ -215,3 +215,12 @@ class NativePolicy(nn.Module):
         if self.reference_model is not None:
             self.reference_model.to(*args, **kwargs)
         return self
+
+
+
+def has_lora_modules(model: nn.Module) -> bool:
+    """True when ``model`` carries LoRA / QLoRA adapter layers (src/forgeline/models/policy.py:421-422)."""
+    from rl_project_b200.models.adapters.lora import LoRALinear
+    from rl_project_b200.models.adapters.qlora import QLoRALinear
+
+    return any(isinstance(m, (LoRALinear, QLoRALinear)) for m in model.modules())

@@ -242,3 +242,18 @@ class MeshStrategy:
         trainer.alg.load_state(shards["model"][r])
         if shards["optimizer"][r]:
             trainer.optimizer.load_state_dict(shards["optimizer"][r])
+
+
+
+class TensorParallelStrategy(MeshStrategy):
+    """``strategy: tensor_parallel`` (reference class name, src/forgeline/distributed/strategies.py:161)."""
+
+    def __init__(self, cfg: DistributedConfig):
+        super().__init__(cfg, "tensor_parallel")
+
+
+class PipelineParallelStrategy(MeshStrategy):
+    """``strategy: pipeline_parallel`` (reference class name, src/forgeline/distributed/strategies.py:182)."""
+
+    def __init__(self, cfg: DistributedConfig):
+        super().__init__(cfg, "pipeline_parallel")

@@ -141,3 +141,58 @@ class PipelineRunner:
         for s in sends:
             s.wait()
         return total
+
+
+# ---------------------------------------------------------------- reference-compatible names
+# (src/forgeline/distributed/pipeline_parallel.py:16-110: PipelineStage, build_pipeline_stage,
+# one_f_one_b_schedule, PipelineScheduler), built on the runner above -- which, unlike the reference's
+# scheduler, also sends activation gradients back so every stage trains.
+
+def one_f_one_b_schedule(n_micro: int, pp_rank: int, pp_size: int) -> List[Tuple[str, int]]:
+    """The 1F1B action list of one rank: ``("F", i)`` / ``("B", i)`` over micro-batch indices."""
+    return schedule_1f1b(n_micro, pp_rank, pp_size)
+
+
+class PipelineStage(nn.Module):
+    """This rank's slice of a ``TransformerLM`` (the whole model object, other stages' blocks replaced by
+    placeholders): the first stage embeds, the last applies the final norm and the LM head."""
+
+    def __init__(self, model: nn.Module, pp_rank: int, pp_size: int):
+        super().__init__()
+        self.model = partition_model(model, pp_rank, pp_size)
+        self.pp_rank, self.pp_size = pp_rank, pp_size
+        self.is_first, self.is_last = pp_rank == 0, pp_rank == pp_size - 1
+
+    def forward(self, x: torch.Tensor, targets: Optional[torch.Tensor] = None):
+        h = stage_forward(self.model, x, self.is_first)
+        if self.is_last and targets is not None:
+            return h, stage_loss(self.model, h, targets)
+        return h, None
+
+
+def build_pipeline_stage(model: nn.Module, mesh: Any) -> PipelineStage:
+    """Stage ``mesh.pp_rank`` of ``mesh.pp_size`` (tensor-parallel sharding first when ``mesh.tp_size > 1``)."""
+    if getattr(mesh, "tp_size", 1) > 1:
+        from rl_project_b200.parallel.tensor_parallel import apply_tensor_parallel
+
+        apply_tensor_parallel(model, mesh.groups.get("tp"), mesh.tp_rank, mesh.tp_size)
+    return PipelineStage(model, mesh.pp_rank, mesh.pp_size)
+
+
+class PipelineScheduler:
+    """Runs 1F1B for one stage over ``n_micro`` chunks of a batch (forward and backward, activations and
+    their gradients exchanged with the neighbouring stages); returns the summed loss on the last stage."""
+
+    def __init__(self, stage: PipelineStage, mesh: Any, n_micro: int = 4):
+        self.stage, self.mesh, self.n_micro = stage, mesh, n_micro
+        self.runner = PipelineRunner(stage.model, mesh.pp_rank, mesh.pp_size, mesh.prev_stage, mesh.next_stage)
+
+    def run(self, inputs: torch.Tensor, targets: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if targets is None:
+            raise ValueError("the pipeline schedule trains: targets are required")
+        xs, ys = inputs.chunk(self.n_micro), targets.chunk(self.n_micro)
+        model = self.stage.model
+        dev = inputs.device
+        dtype = next(p for p in model.parameters()).dtype
+        act = (xs[0].shape[0], xs[0].shape[1], model.spec.n_embd)
+        return self.runner.run(list(zip(xs, ys)), act, dtype, dev, 1.0 / self.n_micro)

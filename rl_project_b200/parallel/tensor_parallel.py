@@ -151,3 +151,81 @@ def row_parallel_out(x: torch.Tensor, lin: nn.Module, group: Any) -> torch.Tenso
         y = nn.functional.linear(x, lin.weight)
     y = reduce_from_tp(y, group)
     return y + lin.bias if getattr(lin, "bias", None) is not None else y
+
+
+# ---------------------------------------------------------------- reference-compatible layer API
+# (src/forgeline/distributed/tensor_parallel.py:39-129 names: all_reduce_forward / all_reduce_backward,
+# ColumnParallelLinear, RowParallelLinear with ``from_linear``), built on the collectives above.
+
+def all_reduce_forward(x: torch.Tensor, group: Any) -> torch.Tensor:
+    """All-reduce in forward, identity in backward (the row-parallel output)."""
+    return reduce_from_tp(x, group)
+
+
+def all_reduce_backward(x: torch.Tensor, group: Any) -> torch.Tensor:
+    """Identity in forward, all-reduce of the gradient in backward (the column-parallel input)."""
+    return copy_to_tp(x, group)
+
+
+class ColumnParallelLinear(nn.Module):
+    """Linear layer whose output features are split over the TP group (rank r keeps rows
+    ``[r out/tp, (r+1) out/tp)``); ``gather_output`` concatenates the shards (differentiable)."""
+
+    def __init__(self, in_features: int, out_features: int, tp_group: Any, tp_size: int, bias: bool = False,
+                 gather_output: bool = False):
+        super().__init__()
+        if out_features % tp_size:
+            raise DistributedConfigError(f"out_features {out_features} not divisible by tensor_parallel {tp_size}")
+        self.in_features, self.out_features = in_features, out_features
+        self.tp_group, self.tp_size, self.gather_output = tp_group, tp_size, gather_output
+        self.weight = nn.Parameter(torch.empty(out_features // tp_size, in_features))
+        self.bias = nn.Parameter(torch.zeros(out_features // tp_size)) if bias else None
+        nn.init.kaiming_uniform_(self.weight, a=5 ** 0.5)
+
+    @classmethod
+    def from_linear(cls, linear: nn.Linear, tp_group: Any, tp_size: int, tp_rank: int) -> "ColumnParallelLinear":
+        layer = cls(linear.in_features, linear.out_features, tp_group, tp_size, linear.bias is not None)
+        src = _rows(linear, tp_rank, tp_size)
+        with torch.no_grad():
+            layer.weight.copy_(src.weight)
+            if layer.bias is not None:
+                layer.bias.copy_(src.bias)
+        return layer.to(linear.weight.device, linear.weight.dtype)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        from rl_project_b200.ops.linear import linear
+
+        y = linear(copy_to_tp(x, self.tp_group), self.weight, self.bias)
+        if self.gather_output and self.tp_size > 1:
+            import torch.distributed.nn.functional as dnnf
+
+            y = torch.cat(dnnf.all_gather(y.contiguous(), group=self.tp_group), dim=-1)
+        return y
+
+
+class RowParallelLinear(nn.Module):
+    """Linear layer whose input features are split over the TP group: local product, all-reduce (the fused
+    GEMM epilogue on GPU ranks when enabled), bias added once."""
+
+    def __init__(self, in_features: int, out_features: int, tp_group: Any, tp_size: int, bias: bool = False):
+        super().__init__()
+        if in_features % tp_size:
+            raise DistributedConfigError(f"in_features {in_features} not divisible by tensor_parallel {tp_size}")
+        self.in_features, self.out_features = in_features, out_features
+        self.tp_group, self.tp_size = tp_group, tp_size
+        self.weight = nn.Parameter(torch.empty(out_features, in_features // tp_size))
+        self.bias = nn.Parameter(torch.zeros(out_features)) if bias else None
+        nn.init.kaiming_uniform_(self.weight, a=5 ** 0.5)
+
+    @classmethod
+    def from_linear(cls, linear: nn.Linear, tp_group: Any, tp_size: int, tp_rank: int) -> "RowParallelLinear":
+        layer = cls(linear.in_features, linear.out_features, tp_group, tp_size, linear.bias is not None)
+        src = _cols(linear, tp_rank, tp_size)
+        with torch.no_grad():
+            layer.weight.copy_(src.weight)
+            if layer.bias is not None:
+                layer.bias.copy_(src.bias)
+        return layer.to(linear.weight.device, linear.weight.dtype)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return row_parallel_out(x, self, self.tp_group)
