@@ -84,6 +84,7 @@ class HFPolicy(nn.Module):
                 base.enable_input_require_grads()
             base.gradient_checkpointing_enable()
         self.model = base
+        self.reference_model = None  # set by with_frozen_reference() when no adapter provides the reference
         self.value_head: Optional[ValueHead] = (ValueHead(self.model.config.hidden_size).to(self.device)
                                                 if value_head else None)
         self.pad_token_id = int(self.hf_tokenizer.pad_token_id)
@@ -145,6 +146,41 @@ class HFPolicy(nn.Module):
         lp = logprobs_from_logits(out.logits[:, :-1], full[:, 1:])[:, prompt_ids.shape[1] - 1:]
         return lp * response_mask.to(lp.device, lp.dtype) if response_mask is not None else lp
 
+    def token_logprobs(self, input_ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """Per-position ``log p(targets | input_ids)`` ``[B, T]``; 0 where ``targets == -1``."""
+        logits = self.token_logits(input_ids).float()
+        tg = targets.to(logits.device)
+        lp = torch.log_softmax(logits, -1).gather(-1, tg.clamp(min=0)[..., None])[..., 0]
+        return lp * (tg >= 0)
+
+    def token_ce(self, input_ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """Mean next-token cross-entropy over ``targets != -1`` (the SFT / pretrain loss)."""
+        logits = self.token_logits(input_ids)
+        return nn.functional.cross_entropy(logits.float().reshape(-1, logits.shape[-1]),
+                                           targets.to(logits.device).reshape(-1), ignore_index=-1)
+
+    def logprobs_with_entropy(self, prompt_ids, response_ids):
+        """Response-token log-probs and the policy's entropy at each response position."""
+        full, out = self._forward(prompt_ids, response_ids)
+        logits = out.logits[:, prompt_ids.shape[1] - 1:-1].float()
+        logp = torch.log_softmax(logits, -1)
+        lp = logp.gather(-1, full[:, prompt_ids.shape[1]:, None])[..., 0]
+        ent = -(logp.exp() * logp).sum(-1)
+        return lp, ent
+
+    def with_frozen_reference(self) -> "HFPolicy":
+        """A frozen copy of the initial weights as the KL reference when no adapter is attached (with LoRA the
+        reference is the base model with the adapter disabled)."""
+        if self._has_adapter:
+            return self
+        import copy
+
+        ref = copy.deepcopy(self.model).eval()
+        for p in ref.parameters():
+            p.requires_grad = False
+        self.reference_model = ref
+        return self
+
     def values(self, prompt_ids, response_ids) -> torch.Tensor:
         if self.value_head is None:
             raise ConfigError("values() requires value_head=True on the policy")
@@ -159,10 +195,19 @@ class HFPolicy(nn.Module):
 
     @contextmanager
     def reference(self) -> Iterator["HFPolicy"]:
-        if not self._has_adapter:
-            raise ConfigError("HFPolicy reference requires LoRA adapters (use_lora=True)")
-        with self.model.disable_adapter():
+        if self._has_adapter:
+            with self.model.disable_adapter():
+                yield self
+            return
+        ref = getattr(self, "reference_model", None)
+        if ref is None:
+            raise ConfigError("HFPolicy reference needs LoRA adapters (use_lora=True) or with_frozen_reference()")
+        live = self.model
+        self.model = ref
+        try:
             yield self
+        finally:
+            self.model = live
 
     def state_for_checkpoint(self) -> Dict[str, Any]:
         st: Dict[str, Any] = {}

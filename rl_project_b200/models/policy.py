@@ -112,6 +112,10 @@ class NativePolicy(nn.Module):
     def token_logits(self, input_ids: torch.Tensor) -> torch.Tensor:
         return self.model.full_logits(input_ids.to(self.device))
 
+    def token_logprobs(self, input_ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """Per-position ``log p(targets | input_ids)`` ``[B, T]`` (fused LM-head kernel on CUDA)."""
+        return self.model.token_logprobs(input_ids.to(self.device), targets.to(self.device))
+
     def token_ce(self, input_ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         """Mean next-token CE over ``targets != -1`` through the fused LM-head kernel."""
         from rl_project_b200.ops.logprob import linear_cross_entropy

@@ -71,7 +71,7 @@ def sequence_logprobs(policy, pairs, reduction: str) -> torch.Tensor:
     inputs, targets = pack_prompt_response(pairs, policy.pad_token_id)
     dev = policy.device
     targets = targets.to(dev)
-    lp = policy.model.token_logprobs(inputs.to(dev), targets).float()
+    lp = policy.token_logprobs(inputs.to(dev), targets).float()
     if reduction == "sum":
         return lp.sum(1)
     return lp.sum(1) / (targets >= 0).sum(1).clamp(min=1)
