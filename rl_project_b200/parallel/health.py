@@ -49,6 +49,10 @@ class HeartbeatMonitor:
         return f"{self.prefix}/{r}"
 
     def start(self) -> "HeartbeatMonitor":
+        try:  # a departure mark left in a store that outlived an earlier run of this rank
+            self.store.delete_key(f"{self._key(self.rank)}/left")
+        except Exception:
+            pass
         self._beat()
         self._thread = threading.Thread(target=self._run, name=f"heartbeat-{self.rank}", daemon=True)
         self._thread.start()

@@ -362,7 +362,25 @@ class Trainer:
 
         return swap(state)
 
+    def _rank_states(self) -> Optional[List[Dict[str, Any]]]:
+        """Every rank's RNG and data-position state, gathered on every rank (collective).
+
+        Data-parallel ranks draw different batches and samples; restoring the main rank's
+        state on every rank would make a resumed run replay one stream on all of them."""
+        if self.strategy is None or self.strategy.world_size() <= 1:
+            return None
+        import torch.distributed as dist
+
+        if not dist.is_initialized():
+            return None
+        out: List[Any] = [None] * dist.get_world_size()
+        dist.all_gather_object(out, {"rng": rng_state(), "data_state": self.alg.data_state()})
+        return out
+
     def save_checkpoint(self, name: Optional[str] = None, is_best: bool = False):
+        """Write a checkpoint.  Collective on every rank of a multi-rank run, except the
+        ``is_best`` save, which only the main rank of an unsharded run makes."""
+        ranks = None if is_best else self._rank_states()
         if self._sharded and hasattr(self.strategy, "sharded_checkpoint_state"):
             shards = self.strategy.sharded_checkpoint_state(self)
             if not self._is_main():
@@ -372,7 +390,7 @@ class Trainer:
                                     model_spec=self.alg.model_spec(), scaler_state=self.precision.state_dict(),
                                     rng_state=rng_state(),
                                     trainer_state={"best_metric": self.best_metric, "history_len": len(self.history),
-                                                   "data_state": self.alg.data_state()},
+                                                   "data_state": self.alg.data_state(), "rank_states": ranks},
                                     tokenizer_meta=self.alg.tokenizer_meta(), experiment=self.ctx.manifest.to_dict(),
                                     shards=shards)
             path = self.checkpoints.save(state, name=name, is_best=is_best)
@@ -388,7 +406,7 @@ class Trainer:
                                 model_spec=self.alg.model_spec(), optimizer_state=opt_state,
                                 scaler_state=self.precision.state_dict(), rng_state=rng_state(),
                                 trainer_state={"best_metric": self.best_metric, "history_len": len(self.history),
-                                               "data_state": self.alg.data_state()},
+                                               "data_state": self.alg.data_state(), "rank_states": ranks},
                                 tokenizer_meta=self.alg.tokenizer_meta(), experiment=self.ctx.manifest.to_dict())
         path = self.checkpoints.save(state, name=name, is_best=is_best)
         self.ctx.metrics.event(Event.CHECKPOINT_SAVED.value, {"path": str(path), "step": self.step})
@@ -448,12 +466,18 @@ class Trainer:
                         m.copy_(p.float())
         if state.scaler_state:
             self.precision.load_state_dict(state.scaler_state)
-        if state.rng_state:
-            set_rng_state(state.rng_state)
+        ts = state.trainer_state or {}
+        rng, data = state.rng_state, ts.get("data_state")
+        ranks = ts.get("rank_states")
+        if ranks and self.strategy is not None and len(ranks) == self.strategy.world_size():
+            mine = ranks[self.strategy.rank()]  # this rank's own streams (same world size only)
+            rng, data = mine["rng"], mine["data_state"]
+        if rng:
+            set_rng_state(rng)
         self.step = state.step
-        self.best_metric = float((state.trainer_state or {}).get("best_metric", math.inf))
-        if (state.trainer_state or {}).get("data_state"):
-            self.alg.load_data_state(state.trainer_state["data_state"])
+        self.best_metric = float(ts.get("best_metric", math.inf))
+        if data:
+            self.alg.load_data_state(data)
         self.ctx.metrics.event(Event.CHECKPOINT_LOADED.value, {"path": target, "step": self.step})
         self.log.info("resumed", path=target, step=self.step)
         return True

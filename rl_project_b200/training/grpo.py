@@ -80,8 +80,9 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
         self.cfg = config
         self.reward = reward
         self.rng = random.Random(config.seed)
-        if config.objective == "clipped" and config.kl_coef > 0 and not policy.has_adapter \
-                and policy.reference_model is None:
+        # the frozen reference only enters the clipped objective's KL term
+        self._needs_ref = config.objective == "clipped" and config.kl_coef > 0
+        if self._needs_ref and not policy.has_adapter and policy.reference_model is None:
             policy.with_frozen_reference()
         if config.agent:
             self.tasks = list(prompts)
@@ -139,8 +140,10 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
     def _attach_logprobs(self, grp: GRPOGroup) -> None:
         if self.cfg.agent:
             old = torch.stack([self.agent_engine.trajectory_logprob(t) for t in grp.trajectories]).float().cpu()
-            with self.policy.reference():
-                ref = torch.stack([self.agent_engine.trajectory_logprob(t) for t in grp.trajectories]).float().cpu()
+            ref = old
+            if self._needs_ref:
+                with self.policy.reference():
+                    ref = torch.stack([self.agent_engine.trajectory_logprob(t) for t in grp.trajectories]).float().cpu()
             grp.old_logprobs, grp.ref_logprobs = old, ref
             return
         prompt, resp, mask = stack_group(grp.trajectories, self.policy.pad_token_id)
@@ -148,8 +151,10 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
             old = stack_old_logprobs(grp.trajectories, resp.shape[1]) * mask  # recorded at sampling time: same weights
         else:
             old = self.policy.logprobs(prompt, resp).float().cpu() * mask
-        with self.policy.reference():
-            ref = self.policy.logprobs(prompt, resp).float().cpu() * mask
+        ref = old  # without a KL term the logged "kl" is the drift from the sampling policy
+        if self._needs_ref:
+            with self.policy.reference():
+                ref = self.policy.logprobs(prompt, resp).float().cpu() * mask
         grp.old_logprobs, grp.ref_logprobs = old, ref
 
     # ---------------------------------------------------------------- objective
