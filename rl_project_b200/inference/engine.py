@@ -132,10 +132,15 @@ class InferenceEngine:
     def _prefill(self, reqs: List[GenerationRequest]) -> int:
         fresh: List[_Seq] = []
         shared: List[Tuple[_Seq, _Seq]] = []
+        vocab = int(self.model.spec.vocab_size)
         for req in reqs:
             st = _Seq(req)
             self.states[req.id] = st
             req.started_at = time.time()
+            if min(req.prompt_tokens) < 0 or max(req.prompt_tokens) >= vocab:
+                # fail this request alone, before its ids reach a batched forward with other requests
+                self._fail(st, ServingError(f"prompt token id outside the vocabulary [0, {vocab})"))
+                continue
             key = tuple(req.prompt_tokens)
             owner = self.states.get(self._prefix_owner.get(key, "")) if self.share_prefixes else None
             if owner is not None and owner.req.id != req.id:
