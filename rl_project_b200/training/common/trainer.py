@@ -262,6 +262,8 @@ class Trainer:
             norm_t = self.strategy.clip_grad_norm(self.params, max_norm, self.optimizer)
             fused = True
         elif fused:
+            # fp16: the clip coefficient must see unscaled gradients (GradScaler then skips its own unscale)
+            self.precision.unscale(self.optimizer)
             norm_t = self.optimizer.clip_grad_norm(max_norm if max_norm > 0 else 0.0)
         elif max_norm > 0:
             self.precision.unscale(self.optimizer)

@@ -73,3 +73,54 @@ def test_memorises_a_batch_like_fp32():
         lgs.append(l2.item())
     assert lcs[-1] < lcs[0] - 1.0
     assert abs(lgs[-1] - lcs[-1]) < 0.1 * lcs[0], (lcs, lgs)
+
+
+def test_fp16_grad_scaler_trainer_matches_torch_loop(tmp_path):
+    """fp16 on CUDA: fp32 parameters under autocast with a GradScaler; the fused AdamW's clip
+    coefficient sees unscaled gradients, so the Trainer makes the same updates as torch's
+    AdamW + GradScaler loop (a clip computed on scaled gradients shrinks them ~1e4x)."""
+    from rl_project_b200.core.config import ExperimentManifest
+    from rl_project_b200.core.lifecycle import RunContext
+    from rl_project_b200.models.transformer.model import TransformerLM
+    from rl_project_b200.ops.optim import FusedAdamW
+    from rl_project_b200.training.common.trainer import Trainer
+    from rl_project_b200.training.pretrain import PretrainAlgorithm, PretrainConfig
+
+    torch.manual_seed(0)
+    spec = _spec()
+    ref = TransformerLM(spec).cuda()
+    ours = TransformerLM(spec).cuda()
+    ours.load_state_dict(ref.state_dict())
+    g = torch.Generator().manual_seed(1)
+    batches = [torch.randint(0, spec.vocab_size, (4, 257), generator=g).cuda() for _ in range(4)]
+    clip, lr = 0.05, 1e-3
+    m = ExperimentManifest.from_dict({
+        "name": "fp16", "algorithm": "pretrain", "model": spec.to_dict(), "output_dir": str(tmp_path),
+        "trainer": {"device": "cuda", "precision": {"dtype": "float16"}, "max_steps": 4, "batch_size": 4,
+                    "eval_every": 0, "log_every": 0, "checkpoint": {"save_every": 0},
+                    "optimizer": {"learning_rate": lr, "grad_clip": clip, "weight_decay": 0.0},
+                    "schedule": {"name": "constant", "warmup_steps": 0}}})
+    ctx = RunContext.create(m, metrics_backend="none")
+    alg = PretrainAlgorithm(ours, iter([(b[:, :-1], b[:, 1:]) for b in batches]), PretrainConfig(batch_size=4),
+                            device=ctx.device)
+    trainer = Trainer(ctx, alg)
+    assert trainer.precision.scaler.is_enabled() and isinstance(trainer.optimizer, FusedAdamW)
+    losses = [trainer.train_step().loss for _ in batches]
+
+    opt = torch.optim.AdamW(ref.parameters(), lr=lr, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0)
+    scaler = torch.amp.GradScaler("cuda")
+    ref_losses = []
+    for b in batches:
+        opt.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.float16):
+            _, loss = ref(b[:, :-1], b[:, 1:])
+        scaler.scale(loss).backward()
+        scaler.unscale_(opt)
+        torch.nn.utils.clip_grad_norm_(ref.parameters(), clip)
+        scaler.step(opt)
+        scaler.update()
+        ref_losses.append(loss.item())
+    assert max(abs(a - b) for a, b in zip(losses, ref_losses)) < 1e-2 * ref_losses[0], (losses, ref_losses)
+    for (n, a), b in zip(ref.named_parameters(), ours.parameters()):
+        d = (a.detach() - b.detach()).abs().max().item()
+        assert d < 3e-4, (n, d)  # 4 steps of lr 1e-3: a shrunken update would differ by ~4e-3
