@@ -379,10 +379,11 @@ void gemm_grouped(int64_t mode, int64_t b_mn, int64_t epi, const at::Tensor& A, 
            "gemm_grouped");
 }
 
-// out [M, N] = sum over the TP ranks of A_r [M, K] @ B_r [N, K]^T, reduced in the GEMM epilogue over peer memory.
+// out [M, N] = sum over the TP ranks of A_r [M, K] @ op(B_r), reduced in the GEMM epilogue over peer memory:
+// b_mn = 0: B [N, K] (op = transpose, row-parallel output);  b_mn = 1: B [K, N] (column-parallel input gradient).
 void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, const std::vector<int64_t>& part,
                     const std::vector<int64_t>& flag, int64_t rank, int64_t epoch, double alpha,
-                    const at::Tensor& status, int64_t grid) {
+                    const at::Tensor& status, int64_t grid, int64_t b_mn) {
   check_bf16(A, "A");
   check_bf16(B, "B");
   check_dev(B, A, "B");
@@ -392,13 +393,14 @@ void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, c
   check_contig(B, "B");
   check_contig(out, "out");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && A.dim() == 2 && B.dim() == 2 && out.dim() == 2, "2-D bf16");
-  TORCH_CHECK(A.size(1) == B.size(1) && out.size(0) == A.size(0) && out.size(1) == B.size(0), "shape mismatch");
+  const int64_t n = b_mn ? B.size(1) : B.size(0), kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(A.size(1) == kb && out.size(0) == A.size(0) && out.size(1) == n, "shape mismatch");
   TORCH_CHECK(part.size() == flag.size() && !part.empty() && part.size() <= 8, "one partial / flag slot per rank");
   TORCH_CHECK(status.scalar_type() == at::kInt, "status: int32");
   std::vector<unsigned long long> pp(part.begin(), part.end()), ff(flag.begin(), flag.end());
   const c10::cuda::CUDAGuard g(A.device());
-  CHECK_OK(rlb_gemm_allreduce((int)A.size(0), (int)B.size(0), (int)A.size(1), A.data_ptr(), A.size(1), B.data_ptr(),
-                              B.size(1), out.data_ptr(), out.size(1), (float)alpha, pp.data(), ff.data(),
+  CHECK_OK(rlb_gemm_allreduce((int)b_mn, (int)A.size(0), (int)n, (int)A.size(1), A.data_ptr(), A.size(1),
+                              B.data_ptr(), B.size(1), out.data_ptr(), out.size(1), (float)alpha, pp.data(), ff.data(),
                               (int)part.size(), (int)rank, (int)epoch, status.data_ptr<int>(), (int)grid,
                               cur_stream()),
            "gemm_allreduce");

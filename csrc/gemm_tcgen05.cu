@@ -608,13 +608,14 @@ cudaError_t rlb_gemm_grouped(int mode, int b_mn, int epi, int M, int N, int K, c
   return cudaErrorInvalidValue;
 }
 
-// Tensor-parallel row-parallel linear with the all-reduce in the epilogue: C = sum over ranks of
-// alpha * A_r B_r^T (A [M][K], B [N][K], both K-major; C bf16 [M][ldc]).  part / flag: this launch's
-// slot of every rank's partial buffer (bf16 [M][N]) and tile-flag array (int32 [tiles][world]); epoch
-// grows by one per use of the slot.  N must be a multiple of 32 and every rank must make the same call
-// (same shapes, same grid) in the same order.
-cudaError_t rlb_gemm_allreduce(int M, int N, int K, const void* A, long long lda, const void* B, long long ldb,
-                               void* C, long long ldc, float alpha, const unsigned long long* part,
+// Tensor-parallel GEMM with the all-reduce in the epilogue: C = sum over ranks of alpha * A_r op(B_r)
+// (A [M][K] K-major; C bf16 [M][ldc]).  b_mn = 0: B [N][K] (row-parallel output, x W^T);  b_mn = 1:
+// B [K][N] (column-parallel input gradient, dy W).  part / flag: this launch's slot of every rank's
+// partial buffer (bf16 [M][N]) and tile-flag array (int32 [tiles][world]); epoch grows by one per use
+// of the slot.  N must be a multiple of 32 and every rank must make the same call (same shapes, same
+// grid) in the same order.
+cudaError_t rlb_gemm_allreduce(int b_mn, int M, int N, int K, const void* A, long long lda, const void* B,
+                               long long ldb, void* C, long long ldc, float alpha, const unsigned long long* part,
                                const unsigned long long* flag, int world, int rank, int epoch, int* status,
                                int grid, cudaStream_t s) {
   using namespace gemm;
@@ -632,5 +633,6 @@ cudaError_t rlb_gemm_allreduce(int M, int N, int K, const void* A, long long lda
   p.ar_world = world;
   p.ar_rank = rank;
   p.ar_epoch = epoch;
+  if (b_mn) return launch<0, 1, kAllReduceBF16>(A, lda, B, ldb, p, grid, s);
   return launch<0, 0, kAllReduceBF16>(A, lda, B, ldb, p, grid, s);
 }

@@ -56,8 +56,8 @@ cudaError_t rlb_gemm_grouped(int mode, int b_mn, int epi, int M, int N, int K, c
                              int* status, int sms, cudaStream_t s);
 
 // Row-parallel linear with the tensor-parallel all-reduce fused into the GEMM epilogue.
-cudaError_t rlb_gemm_allreduce(int M, int N, int K, const void* A, long long lda, const void* B, long long ldb,
-                               void* C, long long ldc, float alpha, const unsigned long long* part,
+cudaError_t rlb_gemm_allreduce(int b_mn, int M, int N, int K, const void* A, long long lda, const void* B,
+                               long long ldb, void* C, long long ldc, float alpha, const unsigned long long* part,
                                const unsigned long long* flag, int world, int rank, int epoch, int* status,
                                int grid, cudaStream_t s);
 

@@ -72,11 +72,20 @@ class CausalSelfAttention(nn.Module):
         self.tp_group = None  # set by tensor parallelism (heads then divided over the group)
 
     def _qkv(self, x: torch.Tensor) -> torch.Tensor:
+        """q|k|v projections as one GEMM; under tensor parallelism ``x`` is the replicated block
+        input and the input-gradient all-reduce belongs to this projection."""
         mods = (self.q_proj, self.k_proj, self.v_proj)
-        if all(type(m) is nn.Linear for m in mods):
+        fused = all(type(m) is nn.Linear for m in mods)
+        if self.tp_group is not None:
+            from rl_project_b200.parallel.tensor_parallel import column_parallel_in, copy_to_tp
+        if fused:
             w = torch.cat([m.weight for m in mods], 0)
             b = torch.cat([m.bias for m in mods], 0) if self.q_proj.bias is not None else None
+            if self.tp_group is not None:
+                return column_parallel_in(x, w, b, self.tp_group)
             return linear(x, w, b)
+        if self.tp_group is not None:
+            x = copy_to_tp(x, self.tp_group)
         return torch.cat([m(x) for m in mods], dim=-1)
 
     def _out(self, y: torch.Tensor) -> torch.Tensor:
@@ -92,10 +101,6 @@ class CausalSelfAttention(nn.Module):
 
     def forward(self, x: torch.Tensor, past_kv: Optional[KVCache] = None, positions: Optional[torch.Tensor] = None):
         B, T, C = x.shape
-        if self.tp_group is not None:
-            from rl_project_b200.parallel.tensor_parallel import copy_to_tp
-
-            x = copy_to_tp(x, self.tp_group)
         qkv = self._qkv(x)
         offset = past_kv[0].shape[2] if past_kv is not None else 0
         # q/k/v come out token-major [B, T, H, D]; attention reads them through [B, H, T, D]

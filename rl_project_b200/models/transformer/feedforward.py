@@ -39,13 +39,14 @@ class SwiGLUFeedForward(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.tp_group is not None:
-            from rl_project_b200.parallel.tensor_parallel import copy_to_tp, row_parallel_out
-
-            x = copy_to_tp(x, self.tp_group)
+            from rl_project_b200.parallel.tensor_parallel import column_parallel_in, copy_to_tp, row_parallel_out
         if self._fusable():
             w13 = torch.cat([self.w1.weight, self.w3.weight], dim=0)
-            a = swiglu(linear(x, w13))
+            h13 = column_parallel_in(x, w13, None, self.tp_group) if self.tp_group is not None else linear(x, w13)
+            a = swiglu(h13)
         else:  # adapters wrap w1/w3: run them as modules
+            if self.tp_group is not None:
+                x = copy_to_tp(x, self.tp_group)
             a = swiglu(torch.cat([self.w1(x), self.w3(x)], dim=-1))
         if self.tp_group is not None:
             out = row_parallel_out(a, self.w2, self.tp_group)
@@ -66,9 +67,12 @@ class GELUFeedForward(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.tp_group is None:
             return self.dropout(self.c_proj(gelu_tanh(self.c_fc(x))))
-        from rl_project_b200.parallel.tensor_parallel import copy_to_tp, row_parallel_out
+        from rl_project_b200.parallel.tensor_parallel import column_parallel_in, copy_to_tp, row_parallel_out
 
-        h = gelu_tanh(self.c_fc(copy_to_tp(x, self.tp_group)))
+        if type(self.c_fc) is nn.Linear:
+            h = gelu_tanh(column_parallel_in(x, self.c_fc.weight, self.c_fc.bias, self.tp_group))
+        else:
+            h = gelu_tanh(self.c_fc(copy_to_tp(x, self.tp_group)))
         return self.dropout(row_parallel_out(h, self.c_proj, self.tp_group))
 
 

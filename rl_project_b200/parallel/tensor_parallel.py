@@ -153,6 +153,19 @@ def row_parallel_out(x: torch.Tensor, lin: nn.Module, group: Any) -> torch.Tenso
     return y + lin.bias if getattr(lin, "bias", None) is not None else y
 
 
+def column_parallel_in(x: torch.Tensor, w: torch.Tensor, bias: Any, group: Any) -> torch.Tensor:
+    """``copy_to_tp(x) @ w^T (+ bias)`` for a row-split ``w``: on NCCL GPU ranks with the fused reducer,
+    the backward all-reduce of ``dx`` runs inside the dgrad GEMM's epilogue."""
+    from rl_project_b200.ops.linear import linear
+    from rl_project_b200.parallel.tp_fused import column_parallel_linear_fused, reducer_for
+
+    reducer = reducer_for(group, x.reshape(-1, x.shape[-1]), x.shape[-1]) if w.dtype == torch.bfloat16 else None
+    if reducer is not None:
+        y = column_parallel_linear_fused(x, w, reducer)
+        return y + bias if bias is not None else y
+    return linear(copy_to_tp(x, group), w, bias)
+
+
 # ---------------------------------------------------------------- reference-compatible layer API
 # (src/forgeline/distributed/tensor_parallel.py:39-129 names: all_reduce_forward / all_reduce_backward,
 # ColumnParallelLinear, RowParallelLinear with ``from_linear``), built on the collectives above.

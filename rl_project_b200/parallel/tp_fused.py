@@ -21,8 +21,16 @@ after its launch k + 1 finished, which needed every peer's flags of launch
 k + 1, which a peer raises only after its own launch k -- the last reader of
 that slot -- finished.
 
-The backward of the all-reduce is the identity, so the layer's backward is the
-ordinary local dgrad / wgrad.
+The backward of the all-reduce is the identity, so the row-parallel layer's
+backward is the ordinary local dgrad / wgrad.  The column-parallel layers that
+open each block (q/k/v, w1/w3) have the mirror-image pattern: identity forward,
+all-reduce of the input gradient backward.  ``column_parallel_linear_fused``
+runs that backward as one GEMM (``dy @ W``, B operand stored [K][N]) with the
+same epilogue all-reduce, instead of a local GEMM followed by an NCCL
+all-reduce (``src/forgeline/distributed/tensor_parallel.py:39-70`` is the
+reference's pair of collectives).  Forward and backward launches share the two
+slots; every rank issues them in the same order (autograd's order is the same
+on every rank of the group).
 """
 
 from __future__ import annotations
@@ -66,17 +74,23 @@ class GemmAllReduce:
     def fits(self, M: int, N: int) -> bool:
         return M * N <= self.max_elems and N % 32 == 0 and _tiles(M, N) <= self.max_tiles
 
-    def __call__(self, x2: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-        M, K = x2.shape
-        N = w.shape[0]
+    def _launch(self, a: torch.Tensor, b: torch.Tensor, N: int, b_mn: int) -> torch.Tensor:
         slot = self.launches % 2
         epoch = self.launches // 2 + 1
         self.launches += 1
         part = [p + slot * self.max_elems * 2 for p in self.mem.buffer_ptrs]
         flag = [f + slot * self.max_tiles * self.world * 4 for f in self.mem.flag_ptrs]
-        out = torch.empty(M, N, dtype=torch.bfloat16, device=x2.device)
-        native().gemm_allreduce(x2, w, out, part, flag, self.rank, epoch, 1.0, self.status, self.grid)
+        out = torch.empty(a.shape[0], N, dtype=torch.bfloat16, device=a.device)
+        native().gemm_allreduce(a, b, out, part, flag, self.rank, epoch, 1.0, self.status, self.grid, b_mn)
         return out
+
+    def __call__(self, x2: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """``sum over ranks of x2 @ w^T`` (``w [N, K]``): the row-parallel output."""
+        return self._launch(x2, w, w.shape[0], 0)
+
+    def dgrad(self, g2: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """``sum over ranks of g2 @ w`` (``w [N_local, C]``): the column-parallel input gradient."""
+        return self._launch(g2, w, w.shape[1], 1)
 
     def check(self) -> None:
         code = int(self.status.item())
@@ -140,4 +154,32 @@ class _RowParallelAR(torch.autograd.Function):
 def row_parallel_linear_fused(x: torch.Tensor, w: torch.Tensor, reducer: GemmAllReduce) -> torch.Tensor:
     shape = x.shape
     y = _RowParallelAR.apply(x.reshape(-1, shape[-1]), w, reducer)
+    return y.view(*shape[:-1], w.shape[0])
+
+
+class _ColumnParallelAR(torch.autograd.Function):
+    """Column-parallel linear whose input-gradient all-reduce is fused into the dgrad GEMM."""
+
+    @staticmethod
+    def forward(ctx, x2, w, reducer):
+        from rl_project_b200.ops.linear import linear
+
+        ctx.save_for_backward(x2, w)
+        ctx.reducer = reducer
+        return linear(x2, w)
+
+    @staticmethod
+    def backward(ctx, g):
+        x2, w = ctx.saved_tensors
+        g = g.contiguous()
+        dx = ctx.reducer.dgrad(g, w.contiguous()) if ctx.needs_input_grad[0] else None
+        dw = g.t() @ x2 if ctx.needs_input_grad[1] else None
+        return dx, dw, None
+
+
+def column_parallel_linear_fused(x: torch.Tensor, w: torch.Tensor, reducer: GemmAllReduce) -> torch.Tensor:
+    """``x @ w^T`` for a row-split ``w [N_local, C]`` whose input ``x`` is replicated over the group:
+    forward is the local GEMM; backward all-reduces ``dx`` inside the dgrad GEMM's epilogue."""
+    shape = x.shape
+    y = _ColumnParallelAR.apply(x.reshape(-1, shape[-1]), w, reducer)
     return y.view(*shape[:-1], w.shape[0])

@@ -184,15 +184,17 @@ def _tp_worker(rank, port, out):
         g = torch.Generator(device="cuda").manual_seed(1000 * it + rank)
         x = (torch.randn(M, K, device="cuda", generator=g) / K ** 0.5).bfloat16()
         w = torch.randn(N, K, device="cuda", generator=g).bfloat16()
-        y = red(x, w)
-        part = (x.float() @ w.float().t()).bfloat16().float()  # each rank's partial, rounded like the kernel's
-        ref = part.clone()
-        dist.all_reduce(ref)
-        err = float((y.float() - ref).abs().max() / ref.abs().max())
-        digest = torch.tensor([float(y.float().double().sum())], device="cuda", dtype=torch.float64)
-        all_d = [torch.zeros_like(digest) for _ in range(WORLD)]
-        dist.all_gather(all_d, digest)
-        res.append({"err": err, "identical": len({float(d) for d in all_d}) == 1})
+        dy = (torch.randn(M, N, device="cuda", generator=g) / N ** 0.5).bfloat16()
+        y = red(x, w)  # row-parallel output: sum_r x_r @ w_r^T
+        dx = red.dgrad(dy, w)  # column-parallel input gradient: sum_r dy_r @ w_r (B stored [K][N])
+        for out_, part in ((y, x.float() @ w.float().t()), (dx, dy.float() @ w.float())):
+            ref = part.bfloat16().float()  # each rank's partial, rounded like the kernel's
+            dist.all_reduce(ref)
+            err = float((out_.float() - ref).abs().max() / ref.abs().max())
+            digest = torch.tensor([float(out_.float().double().sum())], device="cuda", dtype=torch.float64)
+            all_d = [torch.zeros_like(digest) for _ in range(WORLD)]
+            dist.all_gather(all_d, digest)
+            res.append({"err": err, "identical": len({float(d) for d in all_d}) == 1, "shape": (M, N, K)})
     torch.cuda.synchronize()
     red.check()
     red.close()
@@ -208,6 +210,66 @@ def test_gemm_allreduce_matches_nccl():
     for r in res:
         assert r["identical"], res
         assert r["err"] < 2e-2, res  # bf16 partials: the kernel's and cuBLAS's roundings may differ by an ulp
+
+
+def _tp_model_worker(rank, port, out):
+    """Tensor parallelism over every rank: fused epilogue all-reduces (row-parallel forward and
+    column-parallel input gradients) against NCCL all-reduces, same weights and batch."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from rl_project_b200.core.config import model_spec_from_preset
+    from rl_project_b200.models.transformer.model import TransformerLM
+    from rl_project_b200.parallel import tp_fused
+    from rl_project_b200.parallel.tensor_parallel import apply_tensor_parallel
+
+    _env(rank, port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    spec = model_spec_from_preset("bl_tiny", n_layer=2, n_head=8, n_kv_head=8, n_embd=512, d_ff=1024,
+                                  block_size=256, vocab_size=1024, dropout=0.0)
+    torch.manual_seed(0)
+    base = TransformerLM(spec)
+    x = torch.randint(0, spec.vocab_size, (2, 256), generator=torch.Generator().manual_seed(5)).cuda()
+    y = torch.roll(x, -1, 1)
+    runs = {}
+    for fused in (False, True):
+        tp_fused.set_enabled(fused)
+        m = TransformerLM(spec)
+        m.load_state_dict(base.state_dict())
+        m = apply_tensor_parallel(m, dist.group.WORLD, rank, WORLD).cuda().to(torch.bfloat16)
+        _, loss = m(x, y)
+        loss.backward()
+        runs[fused] = (float(loss), {n: p.grad.float().clone() for n, p in m.named_parameters()})
+        torch.cuda.synchronize()
+    red = tp_fused._REDUCERS.get(dist.group.WORLD)
+    used = red is not None and red.launches > 0
+    if red is not None:
+        red.check()
+    tp_fused.close_all()
+    tp_fused.set_enabled(True)
+    worst = 0.0
+    for n, g0 in runs[False][1].items():
+        g1 = runs[True][1][n]
+        worst = max(worst, float((g1 - g0).norm() / g0.norm().clamp(min=1e-12)))
+    torch.save({"loss": (runs[False][0], runs[True][0]), "grad_rel": worst, "used": used,
+                "launches": red.launches if red is not None else 0}, os.path.join(out, f"tpm{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_tensor_parallel_model_fused_matches_nccl():
+    with tempfile.TemporaryDirectory() as out:
+        mp.start_processes(_tp_model_worker, args=(free_port(), out), nprocs=WORLD, join=True, start_method="spawn")
+        res = [torch.load(os.path.join(out, f"tpm{r}.pt")) for r in range(WORLD)]
+    for r in res:
+        assert r["used"], res
+        # 2 layers x (q|k|v dgrad, w1|w3 dgrad, attention-out and w2 forward) fused launches per step
+        assert r["launches"] == 2 * 4, res
+        a, b = r["loss"]
+        assert abs(a - b) < 1e-2 * abs(a), res
+        assert r["grad_rel"] < 3e-2, res
 
 
 def _ep_worker(rank, port, out):
