@@ -379,6 +379,40 @@ void gemm_grouped(int64_t mode, int64_t b_mn, int64_t epi, const at::Tensor& A, 
            "gemm_grouped");
 }
 
+// Attention forward: q [B, T, Hq, D], k / v [B, T, Hkv, D] (token-major, contiguous bf16) -> out (same layout as
+// q); lse [B, Hq, T] fp32 when defined (numel > 0).
+void fmha_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& out, at::Tensor& lse,
+              bool causal, double scale, const at::Tensor& status) {
+  check_bf16(q, "q");
+  check_bf16(k, "k");
+  check_bf16(v, "v");
+  check_dev(k, q, "k");
+  check_dev(v, q, "v");
+  check_dev(out, q, "out");
+  check_dev(status, q, "status");
+  check_contig(q, "q");
+  check_contig(k, "k");
+  check_contig(v, "v");
+  check_contig(out, "out");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "q, k, v: [B, T, H, D]");
+  TORCH_CHECK(k.sizes() == v.sizes() && k.size(0) == q.size(0) && k.size(1) == q.size(1) && k.size(3) == q.size(3),
+              "k / v shapes do not match q");
+  TORCH_CHECK(out.sizes() == q.sizes() && out.scalar_type() == at::kBFloat16, "out: bf16 like q");
+  TORCH_CHECK(status.scalar_type() == at::kInt, "status: int32");
+  float* lse_p = nullptr;
+  if (lse.numel() > 0) {
+    check_dev(lse, q, "lse");
+    TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.is_contiguous() && lse.numel() == q.size(0) * q.size(2) * q.size(1),
+                "lse: fp32 [B, Hq, T]");
+    lse_p = lse.data_ptr<float>();
+  }
+  const c10::cuda::CUDAGuard g(q.device());
+  CHECK_OK(rlb_fmha_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse_p, (int)q.size(0),
+                        (int)q.size(1), (int)q.size(2), (int)k.size(2), (int)q.size(3), causal ? 1 : 0, (float)scale,
+                        status.data_ptr<int>(), cur_stream()),
+           "fmha_fwd");
+}
+
 // out [M, N] = sum over the TP ranks of A_r [M, K] @ op(B_r), reduced in the GEMM epilogue over peer memory:
 // b_mn = 0: B [N, K] (op = transpose, row-parallel output);  b_mn = 1: B [K, N] (column-parallel input gradient).
 void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, const std::vector<int64_t>& part,
@@ -702,6 +736,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_allreduce", &gemm_allreduce);
+  m.def("fmha_fwd", &fmha_fwd);
   m.def("paged_decode", &paged_decode);
   m.def("paged_write", &paged_write);
   m.def("sample", &sample);

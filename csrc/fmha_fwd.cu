@@ -1,0 +1,463 @@
+// Fused multi-head attention, forward, for sm_100a: tcgen05 MMAs with TMEM accumulators, TMA tile loads.
+//
+//   out[b, t, h, :] = softmax(scale * q[b, t, h, :] . k[b, s, h / G, :]^T  (+ causal mask)) v[b, s, h / G, :]
+//
+// q, k, v and out are token-major [B, T, H, D] bf16 (the layout the fused RoPE kernel writes), D = 64 or
+// 128, grouped-query heads G = Hq / Hkv.  Optionally also writes lse[b, h, t] = log sum_s exp(scale q.k)
+// (natural log) for a backward pass.  The reference runs attention through PyTorch
+// (``src/forgeline/models/attention/causal.py:79-134``); this is the B200 kernel behind the same op.
+//
+// One CTA (192 threads) per (128-query tile, head, batch); causal CTAs start with the longest rows.
+//   warp 0      TMA producer: the Q tile once, then K and V tiles (128 keys) through two-stage rings.
+//   warp 1      TMEM owner (all 512 columns) and MMA issuer (one elected thread):
+//                 S_j = Q K_j^T      M=128, N=128, K=D    -> TMEM S[j % 2]   (columns 0..255)
+//                 O_j = P_j V_j      M=128, N=D,   K=128  -> TMEM O[j % 2]   (columns 256..511)
+//               S_{j+1} is issued before O_j, so the tensor core computes the next scores while the
+//               softmax warps work on the current ones.
+//   warps 2-5   softmax: thread r owns query row r of the tile (warp w reads TMEM lanes 32 (w % 4)..).
+//               Per key tile: row max of S_j (first read of the row), fold the previous tile's O_{j-1}
+//               into the register accumulator with the online-softmax rescale, then exponentiate
+//               (second read of the row), write P_j as bf16 into shared memory in the 128-byte-swizzled
+//               K-major layout the MMA reads, and hand S[j % 2] back.  The final O is divided by the
+//               softmax denominator and stored.
+// P V accumulates per tile in TMEM and is folded into registers, so no TMEM accumulator is ever
+// rescaled in place.  Every mbarrier wait is bounded: on timeout the kernel records an error in
+// `status`, stops every role, waits (bounded) for its own TMA loads and MMAs, frees TMEM and returns.
+// No load uses cluster delivery.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "sm100.cuh"
+
+namespace fmha {
+
+constexpr int BQ = 128, BKV = 128;
+constexpr int SUB_BYTES = 128 * 64 * 2;  // one [128 rows][64 columns] bf16 box, 128-B swizzled: 16 KB
+constexpr int TMEM_COLS = 512;
+constexpr uint32_t WAIT_LIMIT = 1u << 26;  // polls before a wait is declared dead (seconds)
+constexpr float LN2 = 0.6931471805599453f;
+
+template <int D>
+struct Layout {
+  static constexpr int DSUB = D / 64;  // 64-column boxes per row of Q / K / V
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + DSUB * SUB_BYTES;
+  static constexpr int V_OFF = K_OFF + 2 * DSUB * SUB_BYTES;
+  static constexpr int P_OFF = V_OFF + 2 * DSUB * SUB_BYTES;
+  static constexpr int BAR_OFF = P_OFF + 2 * SUB_BYTES;  // P: [128 queries][128 keys] as two boxes
+  static constexpr int BYTES = BAR_OFF + 256;
+};
+// Every launch asks for the D = 128 footprint, so at most one CTA is resident per SM (a CTA allocates
+// all 512 TMEM columns).
+constexpr int SMEM_REQUEST = Layout<128>::BYTES + 1024;
+
+struct Params {
+  __nv_bfloat16* out;  // [B][T][Hq][D]
+  float* lse;          // [B][Hq][T] or nullptr
+  int B, T, Hq, Hkv;
+  float scale_log2;  // softmax scale * log2(e)
+  int causal;
+  int* status;
+};
+
+__device__ __forceinline__ void fail(int* status, volatile int* abort_flag, int where) {
+  *abort_flag = 1;
+  if (status) atomicCAS(status, 0, 1 | (where << 8));
+}
+
+__device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity) {
+  return sm100::mbar_wait_bounded(bar, parity, WAIT_LIMIT);
+}
+
+template <int D>
+__global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant__ CUtensorMap mq,
+                                                          const __grid_constant__ CUtensorMap mk,
+                                                          const __grid_constant__ CUtensorMap mv, Params p) {
+  using L = Layout<D>;
+  constexpr int DSUB = L::DSUB;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sQ = smem + L::Q_OFF;
+  uint8_t* sK = smem + L::K_OFF;
+  uint8_t* sV = smem + L::V_OFF;
+  uint8_t* sP = smem + L::P_OFF;
+  uint64_t* bars = (uint64_t*)(smem + L::BAR_OFF);
+  uint64_t* qfull = bars;
+  uint64_t* kfull = bars + 1;
+  uint64_t* kempty = bars + 3;
+  uint64_t* vfull = bars + 5;
+  uint64_t* vempty = bars + 7;
+  uint64_t* sfull = bars + 9;
+  uint64_t* sempty = bars + 11;
+  uint64_t* pfull = bars + 13;
+  uint64_t* ofull = bars + 14;
+  uint64_t* oempty = bars + 16;
+  uint64_t* drain = bars + 18;
+  uint32_t* tmem_slot = (uint32_t*)(bars + 20);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_qt = (p.T + BQ - 1) / BQ;
+  const int qt = num_qt - 1 - (int)blockIdx.x;  // longest causal rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int q0 = qt * BQ;
+  const int nkv_all = (p.T + BKV - 1) / BKV;
+  const int n = p.causal ? min(qt + 1, nkv_all) : nkv_all;  // key tiles this query tile reads
+
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(qfull, 1);
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(&kfull[i], 1);
+      sm100::mbar_init(&kempty[i], 1);
+      sm100::mbar_init(&vfull[i], 1);
+      sm100::mbar_init(&vempty[i], 1);
+      sm100::mbar_init(&sfull[i], 1);
+      sm100::mbar_init(&sempty[i], 4);
+      sm100::mbar_init(&ofull[i], 1);
+      sm100::mbar_init(&oempty[i], 4);
+    }
+    sm100::mbar_init(pfull, 4);
+    sm100::mbar_init(drain, 1);
+    *abort_flag = 0;
+    sm100::fence_barrier_init();
+    sm100::prefetch_tensormap(&mq);
+    sm100::prefetch_tensormap(&mk);
+    sm100::prefetch_tensormap(&mv);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, TMEM_COLS);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int k_issued = 0, v_issued = 0;  // key tiles whose K / V loads were issued
+      sm100::mbar_arrive_expect_tx(qfull, DSUB * SUB_BYTES);
+#pragma unroll
+      for (int s = 0; s < DSUB; ++s) sm100::tma_load_3d(sQ + s * SUB_BYTES, &mq, qfull, h * D + 64 * s, q0, b);
+      for (int j = 0; j < n && !*abort_flag; ++j) {
+        const int buf = j & 1;
+        const uint32_t par = (j >> 1) & 1;
+        if (!wait(&kempty[buf], par ^ 1)) {
+          fail(p.status, abort_flag, 1);
+          break;
+        }
+        sm100::mbar_arrive_expect_tx(&kfull[buf], DSUB * SUB_BYTES);
+#pragma unroll
+        for (int s = 0; s < DSUB; ++s)
+          sm100::tma_load_3d(sK + (buf * DSUB + s) * SUB_BYTES, &mk, &kfull[buf], hk * D + 64 * s, j * BKV, b);
+        k_issued = j + 1;
+        if (!wait(&vempty[buf], par ^ 1)) {
+          fail(p.status, abort_flag, 2);
+          break;
+        }
+        sm100::mbar_arrive_expect_tx(&vfull[buf], DSUB * SUB_BYTES);
+#pragma unroll
+        for (int s = 0; s < DSUB; ++s)
+          sm100::tma_load_3d(sV + (buf * DSUB + s) * SUB_BYTES, &mv, &vfull[buf], hk * D + 64 * s, j * BKV, b);
+        v_issued = j + 1;
+      }
+      // every load issued here lands before the CTA exits (a buffer's earlier loads were consumed
+      // before its next one was issued, so waiting for the last load of each buffer is enough)
+      wait(qfull, 0);
+      for (int t = 0; t < 2; ++t) {
+        const int jk = k_issued - 1 - t, jv = v_issued - 1 - t;
+        if (jk >= 0) wait(&kfull[jk & 1], (jk >> 1) & 1);
+        if (jv >= 0) wait(&vfull[jv & 1], (jv >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_s = sm100::idesc_bf16_f32(BQ, BKV, 0, 0);  // Q, K both K-major
+      constexpr uint32_t id_o = sm100::idesc_bf16_f32(BQ, D, 0, 1);    // P K-major, V [keys][D]: MN-major
+      bool ok = wait(qfull, 0);
+      if (!ok) fail(p.status, abort_flag, 3);
+      const uint32_t qa = sm100::smem_u32(sQ), pa = sm100::smem_u32(sP);
+      for (int j = 0; ok && j <= n && !*abort_flag; ++j) {
+        if (j < n) {
+          const int buf = j & 1;
+          const uint32_t par = (j >> 1) & 1;
+          if (!wait(&kfull[buf], par)) {
+            fail(p.status, abort_flag, 4);
+            break;
+          }
+          if (!wait(&sempty[buf], par ^ 1)) {
+            fail(p.status, abort_flag, 5);
+            break;
+          }
+          sm100::tc_fence_after();
+          const uint32_t ka = sm100::smem_u32(sK + buf * DSUB * SUB_BYTES);
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            // 16 columns of D per MMA: box k / 4, +32 B per step inside the 128-B swizzle row
+            const uint32_t off = (uint32_t)(k >> 2) * SUB_BYTES + (uint32_t)(k & 3) * 32;
+            sm100::mma_f16(tmem + buf * BKV, sm100::desc_kmajor_sw128(qa + off), sm100::desc_kmajor_sw128(ka + off),
+                           id_s, k > 0);
+          }
+          sm100::mma_commit(&kempty[buf]);
+          sm100::mma_commit(&sfull[buf]);
+        }
+        if (j >= 1) {
+          const int i = j - 1, ib = i & 1;
+          const uint32_t ipar = (i >> 1) & 1;
+          if (!wait(pfull, i & 1)) {
+            fail(p.status, abort_flag, 6);
+            break;
+          }
+          if (!wait(&vfull[ib], ipar)) {
+            fail(p.status, abort_flag, 7);
+            break;
+          }
+          if (!wait(&oempty[ib], ipar ^ 1)) {
+            fail(p.status, abort_flag, 8);
+            break;
+          }
+          sm100::tc_fence_after();
+          const uint32_t va = sm100::smem_u32(sV + ib * DSUB * SUB_BYTES);
+#pragma unroll
+          for (int k = 0; k < BKV / 16; ++k) {
+            // P: 16 keys per MMA (K-major, like Q);  V: 16 key rows = two 8-row 1024-B atoms, the
+            // 64-column boxes along D one SUB_BYTES apart
+            const uint32_t poff = (uint32_t)(k >> 2) * SUB_BYTES + (uint32_t)(k & 3) * 32;
+            sm100::mma_f16(tmem + 2 * BKV + ib * D, sm100::desc_kmajor_sw128(pa + poff),
+                           sm100::desc_mnmajor_sw128(va + k * 2048, SUB_BYTES), id_o, k > 0);
+          }
+          sm100::mma_commit(&vempty[ib]);
+          sm100::mma_commit(&ofull[ib]);
+        }
+      }
+      // every MMA issued here completes before TMEM is released
+      sm100::mma_commit(drain);
+      wait(drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax (warps 2..5)
+    const int qq = warp & 3;
+    const int row = qq * 32 + lane;
+    const int rq = q0 + row;
+    const uint32_t lanes = tmem + ((uint32_t)(qq * 32) << 16);
+    const float sl2 = p.scale_log2;
+    float O[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) O[d] = 0.f;
+    float m = -INFINITY, l = 0.f;  // running row max (log2 units) and denominator
+    float m_o = -INFINITY;         // max the register accumulator O is scaled to
+    float m_p = -INFINITY;         // max the last P written was scaled to
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (*abort_flag) {
+        ok = false;
+        break;
+      }
+      const int buf = j & 1;
+      const uint32_t par = (j >> 1) & 1;
+      if (!wait(&sfull[buf], par)) {
+        fail(p.status, abort_flag, 9);
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      const uint32_t ts = lanes + buf * BKV;
+      const int kv0 = j * BKV;
+      const bool masked = (kv0 + BKV > p.T) || (p.causal && kv0 + BKV - 1 > rq - row);
+      // pass 1: row max over this key tile
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint32_t r[32];
+        sm100::tmem_ld32(ts + c * 32, r);
+        sm100::tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int col = kv0 + c * 32 + e;
+          const bool valid = !masked || (col < p.T && (!p.causal || col <= rq));
+          mx = valid ? fmaxf(mx, __uint_as_float(r[e])) : mx;
+        }
+      }
+      const float m_new = fmaxf(m, mx * sl2);
+      // fold the previous tile's P V into the accumulator (both brought to the max P_{j-1} used)
+      if (j >= 1) {
+        const int i = j - 1, ib = i & 1;
+        if (!wait(&ofull[ib], (i >> 1) & 1)) {
+          fail(p.status, abort_flag, 10);
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const float a = (m_o == -INFINITY) ? 0.f : exp2f(m_o - m_p);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          sm100::tmem_ld32(lanes + 2 * BKV + ib * D + c * 32, r);
+          sm100::tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) O[c * 32 + e] = fmaf(O[c * 32 + e], a, __uint_as_float(r[e]));
+        }
+        m_o = m_p;
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&oempty[ib]);
+      }
+      // pass 2: probabilities, row sum, bf16 P into shared memory (the previous P V has finished reading it)
+      const float moff = (m_new == -INFINITY) ? 0.f : m_new;
+      float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint32_t r[32];
+        sm100::tmem_ld32(ts + c * 32, r);
+        sm100::tmem_ld_wait();
+        // row `row` of the box holding keys [64 (c / 2), 64 (c / 2) + 64): 8-row atoms of 1024 B, 16-B
+        // chunk k of a 128-B row stored at chunk k ^ (row % 8) (the TMA / UMMA 128-B swizzle)
+        uint8_t* prow = sP + (c >> 1) * SUB_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          float f[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int col = kv0 + c * 32 + v * 8 + e;
+            const bool valid = !masked || (col < p.T && (!p.causal || col <= rq));
+            f[e] = valid ? exp2f(fmaf(__uint_as_float(r[v * 8 + e]), sl2, -moff)) : 0.f;
+            rs += f[e];
+          }
+          uint4 pk;
+          uint32_t* w = (uint32_t*)&pk;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 hh = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+            w[e] = *(uint32_t*)&hh;
+          }
+          const int chunk = (c & 1) * 4 + v;
+          *(uint4*)(prow + ((chunk ^ (row & 7)) << 4)) = pk;
+        }
+      }
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&sempty[buf]);
+      sm100::fence_async_shared();  // P (generic-proxy stores) visible to the tensor core
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(pfull);
+      l = (m == -INFINITY ? 0.f : l * exp2f(m - m_new)) + rs;
+      m = m_new;
+      m_p = m_new;
+    }
+    if (ok && n > 0) {
+      const int i = n - 1, ib = i & 1;
+      if (wait(&ofull[ib], (i >> 1) & 1)) {
+        sm100::tc_fence_after();
+        const float a = (m_o == -INFINITY) ? 0.f : exp2f(m_o - m_p);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          sm100::tmem_ld32(lanes + 2 * BKV + ib * D + c * 32, r);
+          sm100::tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) O[c * 32 + e] = fmaf(O[c * 32 + e], a, __uint_as_float(r[e]));
+        }
+        sm100::tc_fence_before();
+        if (rq < p.T) {
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+          __nv_bfloat16* dst = p.out + (((long long)b * p.T + rq) * p.Hq + h) * D;
+#pragma unroll
+          for (int v = 0; v < D / 8; ++v) {
+            uint4 pk;
+            uint32_t* w = (uint32_t*)&pk;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              __nv_bfloat162 hh = __floats2bfloat162_rn(O[v * 8 + 2 * e] * inv, O[v * 8 + 2 * e + 1] * inv);
+              w[e] = *(uint32_t*)&hh;
+            }
+            *(uint4*)(dst + v * 8) = pk;
+          }
+          if (p.lse) p.lse[((long long)b * p.Hq + h) * p.T + rq] = (m + log2f(l)) * LN2;
+        }
+      } else {
+        fail(p.status, abort_flag, 11);
+      }
+    }
+  }
+
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)ptr;
+  }
+  return fn;
+}
+
+// [B][T][H * D] bf16 viewed as a 3-D map (columns, tokens, batch); box = 64 columns x 128 tokens x 1.
+// Rows past T read as zeros, so a tile never spills into the next sequence.
+static bool make_map(CUtensorMap* m, const void* ptr, int B, int T, int HD) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)HD * 2, (cuuint64_t)T * HD * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)BQ, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int D>
+static cudaError_t launch(const void* q, const void* k, const void* v, const Params& p, cudaStream_t s) {
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, q, p.B, p.T, p.Hq * D) || !make_map(&mk, k, p.B, p.T, p.Hkv * D) ||
+      !make_map(&mv, v, p.B, p.T, p.Hkv * D))
+    return cudaErrorInvalidResourceHandle;
+  auto kern = fmha_fwd_kernel<D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_REQUEST);
+  if (e != cudaSuccess) return e;
+  (void)cudaGetLastError();
+  const dim3 grid((p.T + BQ - 1) / BQ, p.Hq, p.B);
+  kern<<<grid, 192, SMEM_REQUEST, s>>>(mq, mk, mv, p);
+  return cudaGetLastError();
+}
+
+}  // namespace fmha
+
+// q [B][T][Hq][D], k / v [B][T][Hkv][D], out [B][T][Hq][D] (bf16, contiguous); lse [B][Hq][T] fp32 or null.
+cudaError_t rlb_fmha_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int B, int T, int Hq,
+                         int Hkv, int D, int causal, float scale, int* status, cudaStream_t s) {
+  if (B <= 0 || T <= 0) return cudaSuccess;
+  if ((D != 64 && D != 128) || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Hq > 65535 || B > 65535)
+    return cudaErrorInvalidValue;
+  if ((((uintptr_t)q) | ((uintptr_t)k) | ((uintptr_t)v) | ((uintptr_t)out)) & 15) return cudaErrorInvalidDevicePointer;
+  fmha::Params p{};
+  p.out = (__nv_bfloat16*)out;
+  p.lse = lse;
+  p.B = B;
+  p.T = T;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.causal = causal;
+  p.status = status;
+  return D == 128 ? fmha::launch<128>(q, k, v, p, s) : fmha::launch<64>(q, k, v, p, s);
+}

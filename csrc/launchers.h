@@ -61,6 +61,11 @@ cudaError_t rlb_gemm_allreduce(int b_mn, int M, int N, int K, const void* A, lon
                                const unsigned long long* flag, int world, int rank, int epoch, int* status,
                                int grid, cudaStream_t s);
 
+// Fused attention forward (tcgen05): q [B][T][Hq][D], k / v [B][T][Hkv][D], out [B][T][Hq][D] bf16; lse
+// [B][Hq][T] fp32 (natural log) or null.  D = 64 or 128.
+cudaError_t rlb_fmha_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int B, int T, int Hq,
+                         int Hkv, int D, int causal, float scale, int* status, cudaStream_t s);
+
 cudaError_t rlb_paged_decode(const void* q, const void* k_pool, const void* v_pool, const int* block_tables,
                              const int* ctx_lens, void* out, float* part_acc, float* part_ml, int B, int Hq, int Hkv,
                              int D, int max_blocks, int num_blocks, int split_tokens, int n_splits, float scale,

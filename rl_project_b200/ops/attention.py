@@ -6,14 +6,19 @@
 ``src/forgeline/models/attention/causal.py:79-134``.
 
 On CUDA, the un-windowed, un-capped case runs torch's fused SDPA kernel
-(flash backend) while the sm_100a FMHA kernel is being brought up; every
-other case and the CPU path use the explicit masked-softmax reference below.
+(cuDNN / flash backends); every other case and the CPU path use the explicit
+masked-softmax reference below.  ``fmha_forward`` is this library's own
+sm_100a forward kernel (csrc/fmha_fwd.cu: tcgen05 MMAs, TMEM accumulators,
+TMA loads); ``RLB_ATTN=tcgen05`` routes gradient-free calls (inference
+prefill, rollout log-probabilities) through it.  It has no backward yet, so
+training keeps the SDPA path.
 """
 
 from __future__ import annotations
 
 import math
-from typing import Optional
+import os
+from typing import Optional, Tuple
 
 import torch
 import torch.nn.functional as F
@@ -79,10 +84,62 @@ def _fused_sdpa(q, k, v, rep, dropout_p, scale):
                                               dropout_p=dropout_p, scale=scale)
 
 
+_ATTN = os.environ.get("RLB_ATTN", "sdpa")
+
+
+def _token_major(x: torch.Tensor) -> torch.Tensor:
+    """``[B, H, T, D]`` view -> the ``[B, T, H, D]`` tensor behind it (a copy only if it is not token-major)."""
+    t = x.transpose(1, 2)
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def fmha_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
+                 scale: Optional[float] = None, with_lse: bool = False) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Attention forward on the sm_100a kernel.  ``q [B, Hq, T, D]``, ``k, v [B, Hkv, T, D]`` (bf16, D 64 or
+    128; token-major storage avoids a copy) -> ``(out [B, Hq, T, D]`` as a view of ``[B, T, Hq, D]`` storage,
+    ``lse [B, Hq, T]`` fp32 natural-log softmax denominators or None)."""
+    from rl_project_b200.core.errors import KernelError
+    from rl_project_b200.ops._ext import native
+
+    B, Hq, T, D = q.shape
+    if D not in (64, 128) or q.dtype != torch.bfloat16 or Hq % k.shape[1]:
+        raise KernelError(f"fmha_forward: unsupported shape / dtype (D={D}, {q.dtype}, Hq={Hq}, Hkv={k.shape[1]})")
+    qt, kt, vt = _token_major(q), _token_major(k), _token_major(v)
+    out = torch.empty_like(qt)
+    lse = torch.empty(B, Hq, T, dtype=torch.float32, device=q.device) if with_lse else torch.empty(0, device=q.device)
+    native().fmha_fwd(qt, kt, vt, out, lse, bool(causal), float(scale if scale is not None else D ** -0.5),
+                      _status(q.device))
+    return out.transpose(1, 2), (lse if with_lse else None)
+
+
+_STATUS: dict = {}
+
+
+def _status(device: torch.device) -> torch.Tensor:
+    """Per-device status word the attention kernels report a timed-out wait into (first error kept)."""
+    key = device.index
+    if key not in _STATUS:
+        _STATUS[key] = torch.zeros(1, dtype=torch.int32, device=device)
+    return _STATUS[key]
+
+
+def fmha_check(device: torch.device) -> None:
+    """Raise ``KernelError`` if an attention kernel on ``device`` gave up a wait (synchronises)."""
+    from rl_project_b200.core.errors import KernelError
+
+    code = int(_status(device).item())
+    if code:
+        raise KernelError(f"fmha kernel: a bounded wait ran out (status 0x{code:x})",
+                          hint="The GPU stalled or a kernel bug left a barrier unarrived; the output is invalid.")
+
+
 def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, window: int = 0, softcap: float = 0.0,
                      scale: Optional[float] = None, dropout_p: float = 0.0) -> torch.Tensor:
     """Full-sequence causal attention (no cache).  ``q [B, Hq, T, D]`` (any strides) -> ``[B, Hq, T, D]``."""
     rep = q.shape[1] // k.shape[1]
+    if (_ATTN == "tcgen05" and q.is_cuda and not torch.is_grad_enabled() and window == 0 and softcap == 0
+            and q.dtype == torch.bfloat16 and q.shape[-1] in (64, 128)):
+        return fmha_forward(q, k, v, True, scale)[0]
     if q.is_cuda and window == 0 and softcap == 0:
         return _fused_sdpa(q, k, v, rep, dropout_p, scale)
     if not q.is_cuda and window == 0 and softcap == 0 and dropout_p == 0.0:

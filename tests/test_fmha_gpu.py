@@ -1,0 +1,43 @@
+"""Own tcgen05 attention forward (csrc/fmha_fwd.cu) against an fp32 PyTorch reference of the same op.
+
+The kernel has not run on a B200 yet, so this module only runs when RLB_FMHA_TEST=1 is set; the
+default attention path (SDPA) does not use it.
+"""
+
+import os
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(os.environ.get("RLB_FMHA_TEST") != "1",
+                                 reason="own FMHA kernel not yet validated on a GPU (set RLB_FMHA_TEST=1)")]
+
+
+@pytest.mark.parametrize("B,T,Hq,Hkv,D,causal", [
+    (1, 128, 1, 1, 128, True),
+    (2, 256, 4, 2, 128, True),
+    (1, 300, 2, 1, 64, True),      # ragged last tile (zero-filled rows past T)
+    (2, 384, 8, 8, 64, False),
+    (1, 1024, 4, 1, 128, True),
+])
+def test_fmha_forward_matches_fp32(B, T, Hq, Hkv, D, causal):
+    from rl_project_b200.ops.attention import attention_reference, fmha_check, fmha_forward
+
+    g = torch.Generator(device="cuda").manual_seed(T + D)
+    # token-major storage, as the fused RoPE kernel writes it
+    q = torch.randn(B, T, Hq, D, device="cuda", generator=g).bfloat16().transpose(1, 2)
+    k = torch.randn(B, T, Hkv, D, device="cuda", generator=g).bfloat16().transpose(1, 2)
+    v = torch.randn(B, T, Hkv, D, device="cuda", generator=g).bfloat16().transpose(1, 2)
+    out, lse = fmha_forward(q, k, v, causal=causal, with_lse=True)
+    torch.cuda.synchronize()
+    fmha_check(q.device)
+    ref = attention_reference(q.float(), k.float(), v.float(), causal=causal, q_offset=0).float()
+    err = (out.float() - ref).abs().max().item()
+    assert err < 2e-2, err
+    rep = Hq // Hkv
+    kk = k.float().repeat_interleave(rep, 1)
+    s = (q.float() @ kk.transpose(-1, -2)) * D ** -0.5
+    if causal:
+        s = s.masked_fill(torch.ones(T, T, device="cuda", dtype=torch.bool).triu(1), float("-inf"))
+    assert (lse - torch.logsumexp(s, -1)).abs().max().item() < 1e-2
