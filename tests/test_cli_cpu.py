@@ -85,3 +85,32 @@ def test_bad_manifest_reports_error(tmp_path, capsys):
     bad.write_text(yaml.safe_dump({"name": "x", "algorithm": "nope"}))
     assert main(["validate", str(bad)]) == 1
     assert "error" in capsys.readouterr().err
+
+
+def test_data_prepare_shard_and_validate(tmp_path, capsys):
+    import numpy as np
+
+    text = tmp_path / "corpus.txt"
+    text.write_text("the quick brown fox jumps over the lazy dog. " * 200)
+    out = tmp_path / "prepared"
+    assert main(["data", "prepare", "--input", str(text), "--output", str(out), "--tokenizer", "char",
+                 "--val-fraction", "0.1"]) == 0
+    capsys.readouterr()
+    assert (out / "train.bin").exists() and (out / "val.bin").exists() and (out / "meta.pkl").exists()
+    n_train = (out / "train.bin").stat().st_size
+    n_val = (out / "val.bin").stat().st_size
+    assert n_val > 0 and 0.05 < n_val / (n_train + n_val) < 0.15  # the validation tail
+
+    shards = tmp_path / "shards"
+    assert main(["data", "shard", "--input", str(out / "train.bin"), "--output", str(shards), "--n-shards", "3"]) == 0
+    paths = json.loads(capsys.readouterr().out)
+    assert len(paths) == 3
+    whole = np.fromfile(out / "train.bin", dtype=np.uint16)
+    joined = np.concatenate([np.fromfile(p, dtype=np.uint16) for p in sorted(paths)])
+    assert np.array_equal(joined, whole)  # shards partition the token stream in order
+
+    jl = tmp_path / "sft.jsonl"
+    jl.write_text(json.dumps({"prompt": "a", "response": "b"}) + "\n" + json.dumps({"prompt": 3}) + "\n")
+    assert main(["data", "validate", "--input", str(jl), "--kind", "supervised"]) == 0
+    rep = json.loads(capsys.readouterr().out)
+    assert rep["valid"] == 1 and rep["skipped"] == 1 and rep["errors"][0][0] == 2  # (line, reason)
