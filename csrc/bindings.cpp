@@ -413,6 +413,32 @@ void fmha_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
            "fmha_fwd");
 }
 
+// Attention backward (same layouts as fmha_fwd): dq fp32 like q (zeroed here, accumulated by the kernel), dk / dv
+// bf16 like k; lse / delta fp32 [B, Hq, T].
+void fmha_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& dout,
+              const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dq, at::Tensor& dk, at::Tensor& dv,
+              bool causal, double scale, const at::Tensor& status) {
+  using Ts = std::initializer_list<const at::Tensor*>;
+  for (const at::Tensor* t : Ts{&q, &k, &v, &dout}) check_bf16(*t, "q/k/v/dout");
+  for (const at::Tensor* t : Ts{&k, &v, &dout, &lse, &delta, &dq, &dk, &dv, &status}) check_dev(*t, q, "fmha_bwd operand");
+  for (const at::Tensor* t : Ts{&q, &k, &v, &dout, &lse, &delta, &dq, &dk, &dv}) check_contig(*t, "fmha_bwd operand");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && k.sizes() == v.sizes() && dout.sizes() == q.sizes(), "[B, T, H, D] operands");
+  TORCH_CHECK(dq.sizes() == q.sizes() && dq.scalar_type() == at::kFloat, "dq: fp32 like q");
+  TORCH_CHECK(dk.sizes() == k.sizes() && dv.sizes() == k.sizes() && dk.scalar_type() == at::kBFloat16 &&
+              dv.scalar_type() == at::kBFloat16, "dk / dv: bf16 like k");
+  const int64_t rows = q.size(0) * q.size(2) * q.size(1);
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && delta.scalar_type() == at::kFloat && lse.numel() == rows &&
+              delta.numel() == rows, "lse / delta: fp32 [B, Hq, T]");
+  TORCH_CHECK(status.scalar_type() == at::kInt, "status: int32");
+  const c10::cuda::CUDAGuard g(q.device());
+  dq.zero_();
+  CHECK_OK(rlb_fmha_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), dout.data_ptr(), lse.data_ptr<float>(),
+                        delta.data_ptr<float>(), dq.data_ptr<float>(), dk.data_ptr(), dv.data_ptr(), (int)q.size(0),
+                        (int)q.size(1), (int)q.size(2), (int)k.size(2), (int)q.size(3), causal ? 1 : 0, (float)scale,
+                        status.data_ptr<int>(), cur_stream()),
+           "fmha_bwd");
+}
+
 // out [M, N] = sum over the TP ranks of A_r [M, K] @ op(B_r), reduced in the GEMM epilogue over peer memory:
 // b_mn = 0: B [N, K] (op = transpose, row-parallel output);  b_mn = 1: B [K, N] (column-parallel input gradient).
 void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, const std::vector<int64_t>& part,
@@ -737,6 +763,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("fmha_fwd", &fmha_fwd);
+  m.def("fmha_bwd", &fmha_bwd);
   m.def("paged_decode", &paged_decode);
   m.def("paged_write", &paged_write);
   m.def("sample", &sample);

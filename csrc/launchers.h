@@ -65,6 +65,11 @@ cudaError_t rlb_gemm_allreduce(int b_mn, int M, int N, int K, const void* A, lon
 // [B][Hq][T] fp32 (natural log) or null.  D = 64 or 128.
 cudaError_t rlb_fmha_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int B, int T, int Hq,
                          int Hkv, int D, int causal, float scale, int* status, cudaStream_t s);
+// Fused attention backward: dq fp32 [B][T][Hq][D] (zeroed by the caller, accumulated), dk / dv bf16
+// [B][T][Hkv][D]; lse / delta fp32 [B][Hq][T] (delta = rowsum(dout * out)).
+cudaError_t rlb_fmha_bwd(const void* q, const void* k, const void* v, const void* dout, const float* lse,
+                         const float* delta, float* dq, void* dk, void* dv, int B, int T, int Hq, int Hkv, int D,
+                         int causal, float scale, int* status, cudaStream_t s);
 
 cudaError_t rlb_paged_decode(const void* q, const void* k_pool, const void* v_pool, const int* block_tables,
                              const int* ctx_lens, void* out, float* part_acc, float* part_ml, int B, int Hq, int Hkv,

@@ -9,9 +9,9 @@ On CUDA, the un-windowed, un-capped case runs torch's fused SDPA kernel
 (cuDNN / flash backends); every other case and the CPU path use the explicit
 masked-softmax reference below.  ``fmha_forward`` is this library's own
 sm_100a forward kernel (csrc/fmha_fwd.cu: tcgen05 MMAs, TMEM accumulators,
-TMA loads); ``RLB_ATTN=tcgen05`` routes gradient-free calls (inference
-prefill, rollout log-probabilities) through it.  It has no backward yet, so
-training keeps the SDPA path.
+TMA loads) and ``fmha_backward`` its backward (csrc/fmha_bwd.cu);
+``RLB_ATTN=tcgen05`` routes attention through them (``fmha``, autograd).
+The default stays SDPA until the kernels have been measured against it.
 """
 
 from __future__ import annotations
@@ -112,6 +112,44 @@ def fmha_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool
     return out.transpose(1, 2), (lse if with_lse else None)
 
 
+def fmha_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, dout: torch.Tensor,
+                  lse: torch.Tensor, causal: bool = True, scale: Optional[float] = None):
+    """Gradients of ``fmha_forward`` on the sm_100a kernel (csrc/fmha_bwd.cu): ``(dq, dk, dv)`` shaped like
+    ``q, k, v`` (``[B, H, T, D]`` views of token-major storage)."""
+    from rl_project_b200.ops._ext import native
+
+    D = q.shape[-1]
+    qt, kt, vt, dot = _token_major(q), _token_major(k), _token_major(v), _token_major(dout.to(torch.bfloat16))
+    # Delta_t = sum_d dO * O  (the softmax-gradient row term), fp32 [B, Hq, T]
+    delta = (dout.float() * out.float()).sum(-1).contiguous()
+    dq = torch.empty(qt.shape, dtype=torch.float32, device=q.device)
+    dk, dv = torch.empty_like(kt), torch.empty_like(vt)
+    native().fmha_bwd(qt, kt, vt, dot, lse.contiguous(), delta, dq, dk, dv, bool(causal),
+                      float(scale if scale is not None else D ** -0.5), _status(q.device))
+    return dq.to(torch.bfloat16).transpose(1, 2), dk.transpose(1, 2), dv.transpose(1, 2)
+
+
+class _FMHA(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, causal, scale):
+        out, lse = fmha_forward(q, k, v, causal, scale, with_lse=True)
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.causal, ctx.scale = causal, scale
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, out, lse = ctx.saved_tensors
+        dq, dk, dv = fmha_backward(q, k, v, out, dout, lse, ctx.causal, ctx.scale)
+        return dq, dk, dv, None, None
+
+
+def fmha(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
+         scale: Optional[float] = None) -> torch.Tensor:
+    """Differentiable attention on the sm_100a forward and backward kernels."""
+    return _FMHA.apply(q, k, v, causal, scale)
+
+
 _STATUS: dict = {}
 
 
@@ -137,8 +175,10 @@ def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, window: 
                      scale: Optional[float] = None, dropout_p: float = 0.0) -> torch.Tensor:
     """Full-sequence causal attention (no cache).  ``q [B, Hq, T, D]`` (any strides) -> ``[B, Hq, T, D]``."""
     rep = q.shape[1] // k.shape[1]
-    if (_ATTN == "tcgen05" and q.is_cuda and not torch.is_grad_enabled() and window == 0 and softcap == 0
+    if (_ATTN == "tcgen05" and q.is_cuda and window == 0 and softcap == 0 and dropout_p == 0.0
             and q.dtype == torch.bfloat16 and q.shape[-1] in (64, 128)):
+        if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
+            return fmha(q, k, v, True, scale)
         return fmha_forward(q, k, v, True, scale)[0]
     if q.is_cuda and window == 0 and softcap == 0:
         return _fused_sdpa(q, k, v, rep, dropout_p, scale)
