@@ -4,6 +4,8 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <mutex>
+#include <unordered_map>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -102,6 +104,35 @@ std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& h, const at::Tensor& w, co
   return {dx, dw};
 }
 
+// ---------------------------------------------------------------- index-error word
+// One int32 per device that kernels without a caller-supplied status word report index errors into
+// (first error kept).  bounds_status() reads it (synchronising) and optionally clears it.
+static int* bounds_word(const at::Device& d) {
+  static std::mutex mu;
+  static std::unordered_map<int, at::Tensor> words;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = words.find(d.index());
+  if (it == words.end()) {
+    // the word must outlive any graph: memory taken during stream capture belongs to the graph's pool
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    C10_CUDA_CHECK(cudaStreamIsCapturing(c10::cuda::getCurrentCUDAStream(d.index()).stream(), &cap));
+    TORCH_CHECK(cap == cudaStreamCaptureStatusNone,
+                "the first RoPE call on a device allocates its index-error word: make it before stream capture");
+    it = words.emplace(d.index(), at::zeros({1}, at::TensorOptions().dtype(at::kInt).device(d))).first;
+  }
+  return it->second.data_ptr<int>();
+}
+
+int64_t bounds_status(int64_t device, bool clear) {
+  const at::Device d(at::kCUDA, (c10::DeviceIndex)device);
+  const c10::cuda::CUDAGuard g(d);
+  int* w = bounds_word(d);
+  int v = 0;
+  C10_CUDA_CHECK(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost));
+  if (clear && v) C10_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
+  return v;
+}
+
 // ---------------------------------------------------------------- RoPE
 std::vector<at::Tensor> rope_qkv_fwd(const at::Tensor& qkv, const at::Tensor& cos_t, const at::Tensor& sin_t,
                                      const c10::optional<at::Tensor>& positions, int64_t B, int64_t T, int64_t Hq,
@@ -127,7 +158,8 @@ std::vector<at::Tensor> rope_qkv_fwd(const at::Tensor& qkv, const at::Tensor& co
   CHECK_OK(rlb_rope_qkv_fwd(qkv.data_ptr(), row_stride, q.data_ptr(), k.data_ptr(), v.data_ptr(),
                             cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
                             positions.has_value() ? positions->data_ptr<int>() : nullptr, (int)B, (int)T, (int)Hq,
-                            (int)Hkv, (int)D, (int)pos_offset, heads_major ? 1 : 0, sm_count(), cur_stream()),
+                            (int)Hkv, (int)D, (int)pos_offset, heads_major ? 1 : 0, (int)cos_t.size(0),
+                            bounds_word(qkv.device()), sm_count(), cur_stream()),
            "rope_qkv_fwd");
   return {q, k, v};
 }
@@ -149,7 +181,8 @@ at::Tensor rope_qkv_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Te
   CHECK_OK(rlb_rope_qkv_bwd(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dqkv.data_ptr(), (Hq + 2 * Hkv) * D,
                             cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
                             positions.has_value() ? positions->data_ptr<int>() : nullptr, (int)B, (int)T, (int)Hq,
-                            (int)Hkv, (int)D, (int)pos_offset, heads_major ? 1 : 0, sm_count(), cur_stream()),
+                            (int)Hkv, (int)D, (int)pos_offset, heads_major ? 1 : 0, (int)cos_t.size(0),
+                            bounds_word(dq.device()), sm_count(), cur_stream()),
            "rope_qkv_bwd");
   return dqkv;
 }
@@ -166,7 +199,7 @@ void rope_inplace(at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_
   CHECK_OK(rlb_rope_inplace(x.data_ptr(), (int)x.size(0), (int)x.size(1), (int)x.size(2), (int)x.size(3),
                             x.stride(0), x.stride(1), x.stride(2), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
                             positions.has_value() ? positions->data_ptr<int>() : nullptr, (int)pos_offset,
-                            inverse ? 1 : 0, sm_count(), cur_stream()),
+                            inverse ? 1 : 0, (int)cos_t.size(0), bounds_word(x.device()), sm_count(), cur_stream()),
            "rope_inplace");
 }
 
@@ -763,6 +796,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("fmha_fwd", &fmha_fwd);
+  m.def("bounds_status", &bounds_status);
   m.def("fmha_bwd", &fmha_bwd);
   m.def("paged_decode", &paged_decode);
   m.def("paged_write", &paged_write);

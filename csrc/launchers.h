@@ -10,15 +10,17 @@ cudaError_t rlb_rmsnorm_bwd(const void* h, const void* w, const float* rstd, con
                             void* dx, float* dw_part, void* dw_out, int dw_is_f32, long long rows, int dim, int sms,
                             cudaStream_t s);
 
+// table_rows: rows of the cos / sin tables; a position outside them is reported in `status` (kBadIndex).
 cudaError_t rlb_rope_qkv_fwd(const void* qkv, long long row_stride, void* q, void* k, void* v, const float* cos_t,
                              const float* sin_t, const int* positions, int B, int T, int Hq, int Hkv, int D,
-                             int pos_offset, int heads_major, int sms, cudaStream_t s);
+                             int pos_offset, int heads_major, int table_rows, int* status, int sms, cudaStream_t s);
 cudaError_t rlb_rope_qkv_bwd(const void* dq, const void* dk, const void* dv, void* dqkv, long long row_stride,
                              const float* cos_t, const float* sin_t, const int* positions, int B, int T, int Hq,
-                             int Hkv, int D, int pos_offset, int heads_major, int sms, cudaStream_t s);
+                             int Hkv, int D, int pos_offset, int heads_major, int table_rows, int* status, int sms,
+                             cudaStream_t s);
 cudaError_t rlb_rope_inplace(void* x, int B, int T, int H, int D, long long sb, long long st, long long sh,
                              const float* cos_t, const float* sin_t, const int* positions, int pos_offset,
-                             int inverse, int sms, cudaStream_t s);
+                             int inverse, int table_rows, int* status, int sms, cudaStream_t s);
 
 cudaError_t rlb_swiglu_fwd(const void* h13, void* out, long long rows, int F, int sms, cudaStream_t s);
 cudaError_t rlb_swiglu_bwd(const void* h13, const void* da, void* dh13, long long rows, int F, int sms,

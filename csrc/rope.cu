@@ -8,8 +8,10 @@
 // Pair (i, i + D/2) is rotated by angle pos * inv_freq[i]:
 //   o_i = x_i c - x_{i+h} s,   o_{i+h} = x_{i+h} c + x_i s
 // which is x*cos + rotate_half(x)*sin of src/forgeline/models/attention/rotary.py:68-76.
-// The cos/sin table is [max_pos, D/2] fp32 built on the host from inv_freq
-// (base theta, linear or YaRN scaling already folded in).
+// The cos/sin table is [table_rows, D/2] fp32 built on the host from inv_freq
+// (base theta, linear or YaRN scaling already folded in).  A position outside
+// the table is reported in `status` (kBadIndex) and that pair is passed through
+// unrotated instead of reading past the table.
 #include "common.cuh"
 
 namespace rlb {
@@ -28,6 +30,7 @@ struct RopeArgs {
   const int* positions;        // optional [B*T]
   int B, T, Hq, Hkv, D, pos_offset, heads_major, table_rows;
   long long row_stride;        // elements between consecutive tokens of qkv
+  int* status;                 // index errors (first kept)
 };
 
 RLB_DEVICE long long head_offset(const RopeArgs& a, int b, int t, int head, int H) {
@@ -70,8 +73,12 @@ __global__ void rope_qkv_kernel(RopeArgs a) {
       dptr = a.dst + fused_off;
     }
     bf16x8 lo = ldg8(sptr + i0), hi = ldg8(sptr + i0 + half);
+    const int pos = rotate ? (a.positions ? a.positions[tok] : t + a.pos_offset) : 0;
+    if (rotate && (pos < 0 || pos >= a.table_rows)) {
+      report(a.status, kBadIndex);
+      rotate = false;
+    }
     if (rotate) {
-      const int pos = a.positions ? a.positions[tok] : t + a.pos_offset;
       const float* ct = a.cos_t + (long long)pos * half + i0;
       const float* st = a.sin_t + (long long)pos * half + i0;
       float xl[8], xh[8], ol[8], oh[8];
@@ -95,7 +102,7 @@ __global__ void rope_qkv_kernel(RopeArgs a) {
 // In-place rotation of x[b, t, h, 0:D] addressed with explicit strides.
 __global__ void rope_inplace_kernel(__nv_bfloat16* x, int B, int T, int H, int D, long long sb, long long st,
                                     long long sh, const float* cos_t, const float* sin_t, const int* positions,
-                                    int pos_offset, int inverse) {
+                                    int pos_offset, int inverse, int table_rows, int* status) {
   const int half = D >> 1;
   const long long total = (long long)B * T * H * half;
   for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -106,6 +113,10 @@ __global__ void rope_inplace_kernel(__nv_bfloat16* x, int B, int T, int H, int D
     r /= H;
     const int t = (int)(r % T), b = (int)(r / T);
     const int pos = positions ? positions[(long long)b * T + t] : t + pos_offset;
+    if (pos < 0 || pos >= table_rows) {
+      if (i == 0) report(status, kBadIndex);
+      continue;  // left unrotated
+    }
     __nv_bfloat16* p = x + b * sb + t * st + h * sh;
     const float xl = __bfloat162float(p[i]), xh = __bfloat162float(p[i + half]);
     const float cs = cos_t[(long long)pos * half + i];
@@ -127,7 +138,7 @@ static int grid_for(long long work, int sms) {
 
 cudaError_t rlb_rope_qkv_fwd(const void* qkv, long long row_stride, void* q, void* k, void* v, const float* cos_t,
                              const float* sin_t, const int* positions, int B, int T, int Hq, int Hkv, int D,
-                             int pos_offset, int heads_major, int sms, cudaStream_t s) {
+                             int pos_offset, int heads_major, int table_rows, int* status, int sms, cudaStream_t s) {
   if (D % 16 != 0) return cudaErrorInvalidValue;
   RopeArgs a{};
   a.src = (const __nv_bfloat16*)qkv;
@@ -139,6 +150,8 @@ cudaError_t rlb_rope_qkv_fwd(const void* qkv, long long row_stride, void* q, voi
   a.positions = positions;
   a.B = B; a.T = T; a.Hq = Hq; a.Hkv = Hkv; a.D = D; a.pos_offset = pos_offset; a.heads_major = heads_major;
   a.row_stride = row_stride;
+  a.table_rows = table_rows;
+  a.status = status;
   const long long work = (long long)B * T * (Hq + 2 * Hkv) * (D / 16);
   rope_qkv_kernel<false><<<grid_for(work, sms), 256, 0, s>>>(a);
   return cudaGetLastError();
@@ -146,7 +159,8 @@ cudaError_t rlb_rope_qkv_fwd(const void* qkv, long long row_stride, void* q, voi
 
 cudaError_t rlb_rope_qkv_bwd(const void* dq, const void* dk, const void* dv, void* dqkv, long long row_stride,
                              const float* cos_t, const float* sin_t, const int* positions, int B, int T, int Hq,
-                             int Hkv, int D, int pos_offset, int heads_major, int sms, cudaStream_t s) {
+                             int Hkv, int D, int pos_offset, int heads_major, int table_rows, int* status, int sms,
+                             cudaStream_t s) {
   if (D % 16 != 0) return cudaErrorInvalidValue;
   RopeArgs a{};
   a.q_src = (const __nv_bfloat16*)dq;
@@ -158,6 +172,8 @@ cudaError_t rlb_rope_qkv_bwd(const void* dq, const void* dk, const void* dv, voi
   a.positions = positions;
   a.B = B; a.T = T; a.Hq = Hq; a.Hkv = Hkv; a.D = D; a.pos_offset = pos_offset; a.heads_major = heads_major;
   a.row_stride = row_stride;
+  a.table_rows = table_rows;
+  a.status = status;
   const long long work = (long long)B * T * (Hq + 2 * Hkv) * (D / 16);
   rope_qkv_kernel<true><<<grid_for(work, sms), 256, 0, s>>>(a);
   return cudaGetLastError();
@@ -165,10 +181,10 @@ cudaError_t rlb_rope_qkv_bwd(const void* dq, const void* dk, const void* dv, voi
 
 cudaError_t rlb_rope_inplace(void* x, int B, int T, int H, int D, long long sb, long long st, long long sh,
                              const float* cos_t, const float* sin_t, const int* positions, int pos_offset,
-                             int inverse, int sms, cudaStream_t s) {
+                             int inverse, int table_rows, int* status, int sms, cudaStream_t s) {
   if (D % 2 != 0) return cudaErrorInvalidValue;
   const long long work = (long long)B * T * H * (D / 2);
   rope_inplace_kernel<<<grid_for(work, sms), 256, 0, s>>>((__nv_bfloat16*)x, B, T, H, D, sb, st, sh, cos_t, sin_t,
-                                                         positions, pos_offset, inverse);
+                                                         positions, pos_offset, inverse, table_rows, status);
   return cudaGetLastError();
 }

@@ -24,7 +24,7 @@ except BaseException as exc:  # noqa: BLE001
 
 
 # kernels launched by each binding (launch accounting for benchmarks)
-_LAUNCHES = {"rmsnorm_bwd": 2, "grad_norm": 2, "adam_chunk_size": 0, "adam_tensor_desc_bytes": 0}
+_LAUNCHES = {"rmsnorm_bwd": 2, "grad_norm": 2, "adam_chunk_size": 0, "adam_tensor_desc_bytes": 0, "bounds_status": 0}
 
 
 class _Counted:
@@ -94,3 +94,14 @@ def sm_count(device: torch.device) -> int:
 
 def debug_checks() -> bool:
     return os.environ.get("RLB_DEBUG_BOUNDS", "0") == "1"
+
+
+def check_bounds(device: torch.device, clear: bool = True) -> None:
+    """Raise ``KernelError`` if a kernel on ``device`` reported an out-of-range index into the shared
+    index-error word (RoPE positions outside the cos / sin table).  Synchronises with the device."""
+    from rl_project_b200.core.errors import KernelError
+
+    code = int(native().bounds_status(int(torch.device(device).index or 0), clear))
+    if code:
+        raise KernelError(f"a kernel reported an out-of-range index (status {code})",
+                          hint="A position, token or block id exceeded its table; the affected rows were skipped.")
