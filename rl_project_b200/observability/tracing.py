@@ -1,6 +1,8 @@
 """Timing: host spans (``Tracer``), CUDA-event device timers and NVTX ranges.
 
 ``Tracer`` keeps the reference's span API (``src/forgeline/observability/tracing.py:11-57``).
+``nvtx_range`` / ``nvtx_annotate`` name the fused communication paths and the
+phases of a training step for a profiler (``RLB_NVTX=1``).
 ``CudaTimer`` measures on the device with CUDA events; ``max_over_ranks``
 reduces a per-rank device time to the slowest rank, which is how every
 multi-GPU number in this framework is reported.
@@ -8,11 +10,13 @@ multi-GPU number in this framework is reported.
 
 from __future__ import annotations
 
+import functools
+import os
 import time
 from collections import deque
 from contextlib import contextmanager
 from dataclasses import dataclass, field
-from typing import Dict, Iterator, List, Optional
+from typing import Callable, Dict, Iterator, List, Optional
 
 import torch
 
@@ -70,9 +74,24 @@ def global_tracer() -> Tracer:
     return _TRACER
 
 
+# NVTX ranges cost a host call each, so they are off unless RLB_NVTX=1 (or set_nvtx(True)): a profiler
+# that reads NVTX then sees every fused communication path and the phases of a training step by name.
+_NVTX = os.environ.get("RLB_NVTX", "0") == "1"
+
+
+def set_nvtx(enabled: bool) -> None:
+    global _NVTX
+    _NVTX = bool(enabled)
+
+
+def nvtx_enabled() -> bool:
+    return _NVTX and torch.cuda.is_available()
+
+
 @contextmanager
 def nvtx_range(name: str) -> Iterator[None]:
-    if torch.cuda.is_available():
+    """A named NVTX range around the block (no-op unless NVTX ranges are enabled)."""
+    if nvtx_enabled():
         torch.cuda.nvtx.range_push(name)
         try:
             yield
@@ -80,6 +99,22 @@ def nvtx_range(name: str) -> Iterator[None]:
             torch.cuda.nvtx.range_pop()
     else:
         yield
+
+
+def nvtx_annotate(name: str) -> Callable:
+    """Decorator form of ``nvtx_range`` (the enable switch is read at call time)."""
+
+    def wrap(fn: Callable) -> Callable:
+        @functools.wraps(fn)
+        def inner(*a, **k):
+            if not _NVTX:
+                return fn(*a, **k)
+            with nvtx_range(name):
+                return fn(*a, **k)
+
+        return inner
+
+    return wrap
 
 
 class CudaTimer:

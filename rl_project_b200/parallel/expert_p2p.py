@@ -43,6 +43,7 @@ import torch.distributed as dist
 
 from rl_project_b200.core.errors import DistributedTimeoutError
 from rl_project_b200.ops._ext import available, native
+from rl_project_b200.observability.tracing import nvtx_annotate
 
 NSLOTS = 4
 ALIGN = 128  # the grouped GEMM's M tile: expert segments are padded to it
@@ -73,6 +74,7 @@ class ExchangeRing:
         self.limit_ns = int(timeout_s * 1e9)
         self.seq = 0
 
+    @nvtx_annotate("rlb/ep_exchange")
     def exchange(self, local: torch.Tensor, src_rank: torch.Tensor, src_row: torch.Tensor) -> torch.Tensor:
         """Offer ``local`` [n, C] to the group and return rows ``(src_rank[i], src_row[i])`` of the ranks' offers."""
         C = native()

@@ -51,6 +51,7 @@ import torch.distributed as dist
 
 from rl_project_b200.core.errors import DistributedConfigError, DistributedTimeoutError
 from rl_project_b200.ops._ext import native
+from rl_project_b200.observability.tracing import nvtx_annotate
 
 NSLOTS = 4
 LAG = 3
@@ -190,6 +191,7 @@ class FusedReduceScatter:
         s = self.seq % NSLOTS
         return self.buf[s * self.slot_elems: s * self.slot_elems + numel]
 
+    @nvtx_annotate("rlb/fused_reduce_scatter")
     def reduce(self, shard: int, out: torch.Tensor, accumulate: bool, norm: bool,
                stream: Optional[torch.cuda.Stream] = None, ctas: Optional[int] = None) -> None:
         """Signal the peers that this rank's slot is filled, then reduce slice ``rank`` of it into ``out``
@@ -265,6 +267,7 @@ class FusedAllGather:
         self.limit_ns = int(timeout_s * 1e9)
         self.seq = 0
 
+    @nvtx_annotate("rlb/fused_all_gather")
     def gather(self, shard: torch.Tensor, full: torch.Tensor) -> None:
         """``full [world * S] = cat(every rank's shard [S])`` on the current stream."""
         C = native()

@@ -43,6 +43,7 @@ import torch.distributed as dist
 
 from rl_project_b200.core.errors import DistributedTimeoutError
 from rl_project_b200.ops._ext import available, native
+from rl_project_b200.observability.tracing import nvtx_annotate
 
 BM, BN = 128, 256  # the GEMM's tile
 
@@ -74,6 +75,7 @@ class GemmAllReduce:
     def fits(self, M: int, N: int) -> bool:
         return M * N <= self.max_elems and N % 32 == 0 and _tiles(M, N) <= self.max_tiles
 
+    @nvtx_annotate("rlb/gemm_allreduce")
     def _launch(self, a: torch.Tensor, b: torch.Tensor, N: int, b_mn: int) -> torch.Tensor:
         slot = self.launches % 2
         epoch = self.launches // 2 + 1

@@ -26,6 +26,7 @@ import torch
 import torch.distributed as dist
 
 from rl_project_b200.ops._ext import native
+from rl_project_b200.observability.tracing import nvtx_annotate
 
 
 def _byte_view(t: torch.Tensor) -> torch.Tensor:
@@ -82,6 +83,7 @@ class ParameterBroadcaster:
             yield cur
 
     @torch.no_grad()
+    @nvtx_annotate("rlb/param_broadcast")
     def broadcast_(self, tensors: Iterable[torch.Tensor], src: int = 0) -> None:
         tensors = [t for t in tensors]
         if self.world == 1 or not tensors:

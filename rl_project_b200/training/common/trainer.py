@@ -37,6 +37,7 @@ from rl_project_b200.core.lifecycle import RunContext
 from rl_project_b200.core.runtime import rng_state, set_rng_state
 from rl_project_b200.observability.events import Event
 from rl_project_b200.observability.metrics import device_memory_metrics
+from rl_project_b200.observability.tracing import nvtx_range
 from rl_project_b200.training.common.optim import build_optimizer
 from rl_project_b200.training.common.precision import Precision
 from rl_project_b200.training.common.schedule import learning_rate_at
@@ -239,7 +240,7 @@ class Trainer:
                 from contextlib import nullcontext
 
                 cm = nullcontext()
-            with cm:
+            with cm, nvtx_range("rlb/forward_backward"):
                 with self.precision.autocast():
                     loss, metrics = self.alg.loss(batch, micro, n_micro)
                 if not loss.is_cuda and not bool(torch.isfinite(loss)):
@@ -249,10 +250,11 @@ class Trainer:
             losses.append(loss.detach().float())
             for k, v in metrics.items():
                 metric_vals.setdefault(k, []).append(_as_tensor(v, dev))
-        if self.strategy is not None and hasattr(self.strategy, "finish_gradients"):
-            self.strategy.finish_gradients(self)
-        elif self._sync_grads:
-            self._all_reduce_gradients()
+        with nvtx_range("rlb/gradient_sync"):
+            if self.strategy is not None and hasattr(self.strategy, "finish_gradients"):
+                self.strategy.finish_gradients(self)
+            elif self._sync_grads:
+                self._all_reduce_gradients()
         max_norm = self.cfg.optimizer.grad_clip
         norm_t: Optional[torch.Tensor] = None
         fused = hasattr(self.optimizer, "clip_grad_norm")
@@ -275,7 +277,8 @@ class Trainer:
         if not fused and not bool(torch.isfinite(loss_mean)):
             raise ConfigError(f"non-finite loss at step {self.step}: {float(loss_mean)}",
                               hint="Lower the learning rate or check the reward / data pipeline.")
-        self.precision.step(self.optimizer)
+        with nvtx_range("rlb/optimizer_step"):
+            self.precision.step(self.optimizer)
         # the single host synchronisation of the step
         keys = sorted(metric_vals)
         packed = [loss_mean.to(dev)] + [torch.stack(metric_vals[k]).to(dev).mean() for k in keys]

@@ -228,3 +228,25 @@ def test_core_import_does_not_import_ray():
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
     assert out.returncode == 0, out.stderr
     assert out.stdout.strip() == "False"
+
+
+def test_nvtx_ranges_are_off_by_default_and_switchable():
+    from rl_project_b200.observability import tracing
+
+    calls = []
+
+    @tracing.nvtx_annotate("rlb/test")
+    def f(x):
+        calls.append(x)
+        return x + 1
+
+    before = tracing.nvtx_enabled()
+    try:
+        tracing.set_nvtx(True)  # without CUDA the range is still a no-op, the call goes through
+        assert f(1) == 2
+        with tracing.nvtx_range("rlb/block"):
+            calls.append("block")
+    finally:
+        tracing.set_nvtx(before)
+    assert f(2) == 3 and calls == [1, "block", 2]
+    assert f.__name__ == "f"
