@@ -155,6 +155,7 @@ __global__ void __launch_bounds__(192, 1) fmha_bwd_kernel(const __grid_constant_
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
+      if (!RLB_TMA_X_OK(hk * D) || !RLB_TMA_X_OK(hk * G * D)) fail(p.status, abort_flag, 8);
       sm100::mbar_arrive_expect_tx(kvfull, 2 * DSUB * SUB_BYTES);
 #pragma unroll
       for (int s = 0; s < DSUB; ++s) {

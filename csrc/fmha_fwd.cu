@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int k_issued = 0, v_issued = 0;  // key tiles whose K / V loads were issued
+      if (!RLB_TMA_X_OK(h * D) || !RLB_TMA_X_OK(hk * D)) fail(p.status, abort_flag, 12);
       sm100::mbar_arrive_expect_tx(qfull, DSUB * SUB_BYTES);
 #pragma unroll
       for (int s = 0; s < DSUB; ++s) sm100::tma_load_3d(sQ + s * SUB_BYTES, &mq, qfull, h * D + 64 * s, q0, b);

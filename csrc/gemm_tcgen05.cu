@@ -223,6 +223,11 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
             fail(p.status, abort_flag, 1);
             break;
           }
+          // innermost (x) coordinates of the loads below: K for K-major operands, M / N for MN-major ones
+          if (!RLB_TMA_X_OK(A_MN ? m0 : tl.kfirst + kb * BK) || !RLB_TMA_X_OK(B_MN ? n0 : tl.kfirst + kb * BK)) {
+            fail(p.status, abort_flag, 7);
+            break;
+          }
           sm100::mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
           uint8_t* a = sA + stage * A_BYTES;
           uint8_t* b = sB + stage * B_BYTES;

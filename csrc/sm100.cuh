@@ -71,6 +71,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Built with RLB_DEBUG_BOUNDS, producers check each tiled load's innermost coordinate before issuing it:
+// x * sizeof(bf16) must be a multiple of 16 bytes, else the copy faults on B200.  A failing check is
+// recorded in the kernel's status word and the kernel stops (no load is issued).  Without the flag the
+// check compiles away (every coordinate in this library is a multiple of 64 elements by construction).
+#ifdef RLB_DEBUG_BOUNDS
+#define RLB_TMA_X_OK(x) ((((x) * 2) & 15) == 0)
+#else
+#define RLB_TMA_X_OK(x) true
+#endif
+
 // 3-D tiled load (x innermost) into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
   asm volatile(
