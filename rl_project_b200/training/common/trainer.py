@@ -22,6 +22,7 @@ Design differences (B200-first):
 from __future__ import annotations
 
 import math
+import os
 import time
 from abc import ABC, abstractmethod
 from dataclasses import dataclass, field
@@ -36,7 +37,7 @@ from rl_project_b200.core.errors import CheckpointNotFoundError, ConfigError
 from rl_project_b200.core.lifecycle import RunContext
 from rl_project_b200.core.runtime import rng_state, set_rng_state
 from rl_project_b200.observability.events import Event
-from rl_project_b200.observability.metrics import device_memory_metrics
+from rl_project_b200.observability.metrics import device_memory_metrics, perf_metrics
 from rl_project_b200.observability.tracing import nvtx_range
 from rl_project_b200.training.common.optim import build_optimizer
 from rl_project_b200.training.common.precision import Precision
@@ -93,6 +94,23 @@ class PostTrainingAlgorithm(ABC):
 
     def on_step_end(self, step: int, result: StepResult) -> None:
         pass
+
+    def tokens_in(self, batch: Any) -> int:
+        """Tokens one step processes (the ``perf/*`` metrics).  Read from tensor shapes only, so it never
+        synchronises: a tensor, or the first tensor of a tuple / list / dict batch; lists of groups of
+        trajectories count prompt + response tokens.  0 when the batch says nothing (no perf metrics)."""
+        if isinstance(batch, torch.Tensor):
+            return int(batch.numel())
+        if isinstance(batch, dict):
+            batch = list(batch.values())
+        if isinstance(batch, (list, tuple)) and batch:
+            first = batch[0]
+            if isinstance(first, torch.Tensor):
+                return int(first.numel())
+            trajs = [t for g in batch for t in (getattr(g, "trajectories", None) or [])]
+            return sum(int(t.prompt_ids.numel()) + int(t.response_ids.numel()) for t in trajs
+                       if hasattr(t, "prompt_ids") and hasattr(t, "response_ids"))
+        return 0
 
     # data-position state, saved with every checkpoint so a resumed run draws the
     # same batches an uninterrupted run would (generators, shuffles, counters)
@@ -181,6 +199,8 @@ class Trainer:
         self.step = 0
         self.best_metric: float = math.inf
         self.history: List[StepResult] = []
+        self._tokens = 0  # tokens processed by this rank since the last perf log
+        self._n_params = sum(p.numel() for p in self.params)
 
     # ------------------------------------------------------------ setup helpers
     def _compile_modules(self) -> None:
@@ -220,6 +240,7 @@ class Trainer:
         self._set_lr(lr)
         self._set_train_mode(True)
         batch = self.alg.collect(self.step)
+        self._tokens += self.alg.tokens_in(batch)
         self.optimizer.zero_grad(set_to_none=True)
         n_micro = self.cfg.gradient_accumulation_steps
         dev = self.ctx.device
@@ -301,6 +322,7 @@ class Trainer:
         max_steps = self.cfg.max_steps if max_steps is None else max_steps
         self.ctx.metrics.event(Event.RUN_STARTED.value, {"algorithm": self.alg.name, "max_steps": max_steps})
         t0 = time.time()
+        t_log, self._tokens = time.time(), 0
         last_eval: Dict[str, float] = {}
         try:
             while self.step < max_steps:
@@ -313,6 +335,12 @@ class Trainer:
                 if self.cfg.log_every and self.step % self.cfg.log_every == 0 and self._is_main():
                     payload = {"train/loss": result.loss, **{f"train/{k}": v for k, v in result.metrics.items()}}
                     payload.update(device_memory_metrics(self.ctx.device))
+                    now = time.time()
+                    # this rank's throughput since the last log (the step ends with one host sync, so the
+                    # wall clock covers the device work); the data-parallel total is world x this
+                    payload.update(perf_metrics(self._tokens, now - t_log, self._n_params,
+                                                float(os.environ.get("RLB_PEAK_TFLOPS", "0") or 0.0)))
+                    t_log, self._tokens = now, 0
                     self.ctx.metrics.log(payload, step=self.step)
                     self.log.info("step", step=self.step, loss=round(result.loss, 5),
                                   **{k: round(v, 5) for k, v in result.metrics.items() if isinstance(v, float)})

@@ -250,3 +250,23 @@ def test_nvtx_ranges_are_off_by_default_and_switchable():
         tracing.set_nvtx(before)
     assert f(2) == 3 and calls == [1, "block", 2]
     assert f.__name__ == "f"
+
+
+def test_trainer_logs_perf_metrics(make_ctx, cspec, corpus_dir):
+    import json as _json
+
+    from rl_project_b200.data.pretraining import MemmapCorpus
+    from rl_project_b200.models.transformer.model import TransformerLM
+    from rl_project_b200.training.common.trainer import Trainer
+    from rl_project_b200.training.pretrain import PretrainAlgorithm, PretrainConfig
+
+    ctx = make_ctx("pretrain", max_steps=3, eval_every=0, save_every=0)
+    model = TransformerLM(cspec)
+    alg = PretrainAlgorithm(model, MemmapCorpus(corpus_dir, "train", cspec.block_size), PretrainConfig(batch_size=2))
+    Trainer(ctx, alg).fit()
+    rows = [_json.loads(x) for x in (ctx.output_dir / "metrics.jsonl").read_text().splitlines()]
+    perf = [r for r in rows if "perf/tokens_per_s" in r]
+    assert len(perf) == 3 and all(r["perf/tokens_per_s"] > 0 for r in perf)
+    n = sum(p.numel() for p in model.parameters())
+    r = perf[-1]
+    assert r["perf/model_tflops"] == pytest.approx(6 * n * r["perf/tokens_per_s"] / 1e12, rel=1e-6)
