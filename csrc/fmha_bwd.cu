@@ -76,6 +76,12 @@ __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity) {
   return sm100::mbar_wait_bounded(bar, parity, WAIT_LIMIT);
 }
 
+// The same wait with one answer for the whole warp (the compute warps' TMEM loads are warp-collective,
+// so a warp must never split on a wait that ran out for some lanes only).
+__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, wait(bar, parity));
+}
+
 // 8 fp32 values -> 8 bf16 in one 16-B chunk of row `row` of a 128-B-swizzled [128][64] box.
 __device__ __forceinline__ void store_chunk(uint8_t* box, int row, int chunk, const float* f) {
   uint4 pk;
@@ -240,13 +246,13 @@ __global__ void __launch_bounds__(192, 1) fmha_bwd_kernel(const __grid_constant_
     const uint32_t lanes = (uint32_t)(qq * 32) << 16;
     bool ok = true;
     for (int t = 0; t < steps; ++t) {
-      if (*abort_flag) {
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) {
         ok = false;
         break;
       }
       const int h = hk * G + t / nq, qi = first_i + t % nq, q0 = qi * BQ;
       const uint32_t par = t & 1;
-      if (!wait(sfull, par)) {
+      if (!wait_warp(sfull, par)) {
         fail(p.status, abort_flag, 5);
         ok = false;
         break;
@@ -288,7 +294,7 @@ __global__ void __launch_bounds__(192, 1) fmha_bwd_kernel(const __grid_constant_
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(pfull);
       // dQ_i rows (TMEM lane = query of the tile) into the fp32 accumulator
-      if (!wait(dqfull, par)) {
+      if (!wait_warp(dqfull, par)) {
         fail(p.status, abort_flag, 6);
         ok = false;
         break;
@@ -311,9 +317,10 @@ __global__ void __launch_bounds__(192, 1) fmha_bwd_kernel(const __grid_constant_
       if (lane == 0) sm100::mbar_arrive(dqfree);
     }
     if (ok && steps > 0) {
-      if (wait(done, 0)) {
+      if (wait_warp(done, 0)) {
         sm100::tc_fence_after();
-        if (key < p.T) {
+        {
+          // every lane runs the (warp-collective) TMEM loads; only rows of real keys are stored
           const long long o = (((long long)b * p.T + key) * p.Hkv + hk) * D;
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
@@ -321,6 +328,7 @@ __global__ void __launch_bounds__(192, 1) fmha_bwd_kernel(const __grid_constant_
             sm100::tmem_ld32(tDV + lanes + c * 32, rv);
             sm100::tmem_ld32(tDK + lanes + c * 32, rk);
             sm100::tmem_ld_wait();
+            if (key >= p.T) continue;
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               uint4 pv, pk;

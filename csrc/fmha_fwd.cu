@@ -72,6 +72,12 @@ __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity) {
   return sm100::mbar_wait_bounded(bar, parity, WAIT_LIMIT);
 }
 
+// The same wait with one answer for the whole warp (the compute warps' TMEM loads are warp-collective,
+// so a warp must never split on a wait that ran out for some lanes only).
+__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, wait(bar, parity));
+}
+
 template <int D>
 __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant__ CUtensorMap mq,
                                                           const __grid_constant__ CUtensorMap mk,
@@ -256,13 +262,13 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
     float m_p = -INFINITY;         // max the last P written was scaled to
     bool ok = true;
     for (int j = 0; j < n; ++j) {
-      if (*abort_flag) {
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) {
         ok = false;
         break;
       }
       const int buf = j & 1;
       const uint32_t par = (j >> 1) & 1;
-      if (!wait(&sfull[buf], par)) {
+      if (!wait_warp(&sfull[buf], par)) {
         fail(p.status, abort_flag, 9);
         ok = false;
         break;
@@ -289,7 +295,7 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
       // fold the previous tile's P V into the accumulator (both brought to the max P_{j-1} used)
       if (j >= 1) {
         const int i = j - 1, ib = i & 1;
-        if (!wait(&ofull[ib], (i >> 1) & 1)) {
+        if (!wait_warp(&ofull[ib], (i >> 1) & 1)) {
           fail(p.status, abort_flag, 10);
           ok = false;
           break;
@@ -353,7 +359,7 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
     }
     if (ok && n > 0) {
       const int i = n - 1, ib = i & 1;
-      if (wait(&ofull[ib], (i >> 1) & 1)) {
+      if (wait_warp(&ofull[ib], (i >> 1) & 1)) {
         sm100::tc_fence_after();
         const float a = (m_o == -INFINITY) ? 0.f : exp2f(m_o - m_p);
 #pragma unroll
