@@ -21,10 +21,20 @@ built differently:
 
 Models whose attention is not grouped-query (MLA, NSA) decode through the
 model's own contiguous ``step`` cache, grouped by length as in the reference.
+
+With ``decode_graphs=True`` (or ``RLB_DECODE_GRAPHS=1``) the paged decode step
+is replayed from CUDA graphs instead of launching its ~10 kernels per layer from
+the host: one graph per (batch, block-table width) bucket, both rounded up to a
+power of two, captured on first use.  Padding rows decode a dummy token into a
+block reserved for them, so they never touch a live sequence's K/V.  Graphs
+hold the model's weight and KV-pool addresses: call ``reset_graphs()`` after
+replacing (not updating in place) a weight tensor.  Not yet measured on a GPU,
+so off by default.
 """
 
 from __future__ import annotations
 
+import os
 import threading
 import time
 from collections import defaultdict
@@ -59,7 +69,8 @@ class _Seq:
 class InferenceEngine:
     def __init__(self, model: Any, *, max_batch: int = 8, max_seq_len: Optional[int] = None, block_size: int = 16,
                  max_blocks: Optional[int] = None, device: Optional[torch.device] = None,
-                 eos_token_id: Optional[int] = None, share_prefixes: bool = True, profile: bool = False):
+                 eos_token_id: Optional[int] = None, share_prefixes: bool = True, profile: bool = False,
+                 decode_graphs: Optional[bool] = None):
         self.model = model.eval()
         self.device = device or next(model.parameters()).device
         self.max_seq_len = min(max_seq_len or model.spec.block_size, model.spec.block_size)
@@ -94,6 +105,17 @@ class InferenceEngine:
         self._thread: Optional[threading.Thread] = None
         self._stop = threading.Event()
         self._lock = threading.Lock()
+        # CUDA-graph decode (paged models on CUDA only)
+        if decode_graphs is None:
+            decode_graphs = os.environ.get("RLB_DECODE_GRAPHS", "0") == "1"
+        self.max_batch = max_batch
+        self._graphs: Dict[Tuple[int, int], Any] = {}
+        self._graph_pool: Any = None
+        self._graph_fail: set = set()
+        self._pad_block = -1
+        self.decode_graphs = bool(decode_graphs) and self.paged and self.device.type == "cuda"
+        if self.decode_graphs:
+            self._pad_block = self.allocator.allocate("__graph_padding__", 1)[0]
 
     # ------------------------------------------------------------ submission
     def submit(self, prompt_tokens: List[int], params: Optional[SamplingParams] = None,
@@ -259,6 +281,16 @@ class InferenceEngine:
 
     # ------------------------------------------------------------ decode
     def _decode(self, seqs: List[_Seq]) -> int:
+        if self.decode_graphs and not self.profile:
+            try:
+                done = self._decode_graph(seqs)
+            except Exception as exc:  # noqa: BLE001
+                torch.cuda.current_stream(self.device).synchronize()
+                for s in seqs:
+                    self._fail(s, exc)
+                return 0
+            if done is not None:
+                return done
         t_host0 = time.perf_counter()
         B = len(seqs)
         bs = self.allocator.block_size
@@ -307,6 +339,100 @@ class InferenceEngine:
         if evs is not None:
             self._account(evs, t_host0)
         return produced
+
+    # ------------------------------------------------------------ CUDA-graph decode
+    @staticmethod
+    def _pow2(n: int, cap: int) -> int:
+        b = 1
+        while b < n:
+            b *= 2
+        return max(n, min(b, cap))
+
+    def reset_graphs(self) -> None:
+        """Drop the captured decode graphs (they are captured again on use)."""
+        self._graphs.clear()
+        self._graph_fail.clear()
+
+    def _capture(self, Bb: int, Wb: int) -> Optional[Dict[str, Any]]:
+        """Capture the decode step of a (batch, width) bucket; None if the model cannot be captured."""
+        from rl_project_b200.models.attention.causal import PagedDecodeMeta
+
+        dev = self.device
+        # the RoPE tables must not grow (reallocate) inside the graph: size them for the longest sequence
+        for blk in self.model.transformer.h:
+            rope = getattr(getattr(blk, "attn", None), "rope", None)
+            if rope is not None:
+                rope.tables(self.max_seq_len + 1, dev)
+        buf = torch.zeros(5 * Bb + Bb * Wb, dtype=torch.int32, device=dev)
+        buf[2 * Bb:3 * Bb] = 1  # padding rows: context of one token...
+        buf[3 * Bb:4 * Bb] = self._pad_block  # ...written into the padding block
+        buf[5 * Bb:].view(Bb, Wb)[:, 0] = self._pad_block
+        meta = PagedDecodeMeta(positions=buf[Bb:2 * Bb].view(Bb, 1), max_pos=self.max_seq_len - 1,
+                               ctx_lens=buf[2 * Bb:3 * Bb], slot_block=buf[3 * Bb:4 * Bb], slot_off=buf[4 * Bb:5 * Bb],
+                               block_tables=buf[5 * Bb:].view(Bb, Wb),
+                               split_tokens=self._split_tokens(Bb, Wb * self.allocator.block_size))
+        cur = torch.cuda.current_stream(dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(cur)
+        try:
+            with torch.cuda.stream(side):  # warm-up: lazy allocations and one-time set-up happen outside capture
+                for _ in range(2):
+                    self.model.decode_paged(buf[:Bb].long(), self.kv, meta)
+            cur.wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, pool=self._graph_pool):
+                logits = self.model.decode_paged(buf[:Bb].long(), self.kv, meta)
+        except Exception as exc:  # noqa: BLE001 - e.g. a host synchronisation inside the model's decode
+            torch.cuda.synchronize(dev)
+            log.warning("decode_graph_capture_failed", batch=Bb, width=Wb, error=repr(exc))
+            return None
+        if self._graph_pool is None:
+            self._graph_pool = graph.pool()
+        return {"graph": graph, "buf": buf, "logits": logits}
+
+    def _decode_graph(self, seqs: List[_Seq]) -> Optional[int]:
+        """The paged decode step replayed from a captured graph; None when no graph serves this bucket."""
+        B = len(seqs)
+        bs = self.allocator.block_size
+        tables = [self.allocator.tables[s.req.id] for s in seqs]
+        width = max(len(t) for t in tables)
+        Bb = self._pow2(B, self.max_batch)
+        Wb = self._pow2(width, (self.max_seq_len + bs - 1) // bs + 1)
+        key = (Bb, Wb)
+        if key in self._graph_fail:
+            return None
+        gr = self._graphs.get(key)
+        if gr is None:
+            gr = self._capture(Bb, Wb)
+            if gr is None:
+                self._graph_fail.add(key)
+                return None
+            self._graphs[key] = gr
+        n = 5 * Bb + Bb * Wb
+        if self._pinned is None or self._pinned.numel() < n:
+            self._pinned = torch.empty(max(n, 1024), dtype=torch.int32, pin_memory=True)
+        host = self._pinned[:n]
+        hv = host.numpy()
+        hv[:] = 0
+        pos = np.fromiter((s.position for s in seqs), dtype=np.int64, count=B)
+        hv[:B] = np.fromiter((s.tokens[-1] for s in seqs), dtype=np.int64, count=B)
+        hv[Bb:Bb + B] = pos
+        hv[2 * Bb:3 * Bb] = 1
+        hv[2 * Bb:2 * Bb + B] = pos + 1
+        hv[3 * Bb:4 * Bb] = self._pad_block
+        hv[4 * Bb:4 * Bb + B] = pos % bs
+        grid = hv[5 * Bb:].reshape(Bb, Wb)
+        grid[:, 0] = self._pad_block
+        for b, t in enumerate(tables):
+            grid[b, :len(t)] = t
+        hv[3 * Bb:3 * Bb + B] = grid[np.arange(B), pos // bs]
+        gr["buf"].copy_(host, non_blocking=True)
+        with self.tracer.span("decode", batch=B, graph=1):
+            gr["graph"].replay()
+        self.decode_steps += 1
+        for s in seqs:
+            s.position += 1
+        return self._sample_and_emit(seqs, gr["logits"][:B], None)
 
     def _split_tokens(self, B: int, max_ctx: int) -> int:
         """Split long contexts over several CTAs when the batch alone cannot fill the GPU."""

@@ -61,3 +61,21 @@ def test_engine_prefix_sharing_gpu():
     for r in sampled:
         assert len(r.generated_tokens) == 10 and all(0 <= t < 512 for t in r.generated_tokens)
     assert eng.allocator.used_blocks == 0
+
+
+@pytest.mark.skipif(__import__("os").environ.get("RLB_GRAPH_TEST") != "1",
+                    reason="CUDA-graph decode not yet validated on a GPU (set RLB_GRAPH_TEST=1)")
+def test_graph_decode_matches_eager_decode():
+    """The same greedy requests decoded eagerly and from captured graphs give the same tokens, across
+    batch sizes that hit several (batch, width) buckets and with padding rows in play."""
+    model = _model(512, 4, 2)
+    prompts = [[1, 2, 3], list(range(5, 205)), [7], list(range(40, 57)), list(range(100, 180))]
+    outs = {}
+    for graphs in (False, True):
+        eng = InferenceEngine(model, max_batch=8, decode_graphs=graphs)
+        reqs = eng.generate_batch(prompts, SamplingParams(max_tokens=24, temperature=0.0, top_k=None))
+        outs[graphs] = [r.generated_tokens for r in reqs]
+        if graphs:
+            assert eng._graphs, "no decode graph was captured"
+            assert eng.allocator.used_blocks == 1  # only the padding block stays reserved
+    assert outs[True] == outs[False]
