@@ -412,8 +412,8 @@ void gemm_grouped(int64_t mode, int64_t b_mn, int64_t epi, const at::Tensor& A, 
            "gemm_grouped");
 }
 
-// Attention forward: q [B, T, Hq, D], k / v [B, T, Hkv, D] (token-major, contiguous bf16) -> out (same layout as
-// q); lse [B, Hq, T] fp32 when defined (numel > 0).
+// Attention forward: q [B, T, Hq, D], k [B, T, Hkv, D], v [B, T, Hkv, DV] (token-major, contiguous bf16) -> out
+// [B, T, Hq, DV]; lse [B, Hq, T] fp32 when defined (numel > 0).
 void fmha_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& out, at::Tensor& lse,
               bool causal, double scale, const at::Tensor& status) {
   check_bf16(q, "q");
@@ -428,9 +428,10 @@ void fmha_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
   check_contig(v, "v");
   check_contig(out, "out");
   TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "q, k, v: [B, T, H, D]");
-  TORCH_CHECK(k.sizes() == v.sizes() && k.size(0) == q.size(0) && k.size(1) == q.size(1) && k.size(3) == q.size(3),
-              "k / v shapes do not match q");
-  TORCH_CHECK(out.sizes() == q.sizes() && out.scalar_type() == at::kBFloat16, "out: bf16 like q");
+  TORCH_CHECK(k.size(0) == q.size(0) && k.size(1) == q.size(1) && k.size(3) == q.size(3) && v.size(0) == k.size(0) &&
+              v.size(1) == k.size(1) && v.size(2) == k.size(2), "k / v shapes do not match q");
+  TORCH_CHECK(out.size(0) == q.size(0) && out.size(1) == q.size(1) && out.size(2) == q.size(2) &&
+              out.size(3) == v.size(3) && out.scalar_type() == at::kBFloat16, "out: bf16 [B, T, Hq, d_v]");
   TORCH_CHECK(status.scalar_type() == at::kInt, "status: int32");
   float* lse_p = nullptr;
   if (lse.numel() > 0) {
@@ -441,8 +442,8 @@ void fmha_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
   }
   const c10::cuda::CUDAGuard g(q.device());
   CHECK_OK(rlb_fmha_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse_p, (int)q.size(0),
-                        (int)q.size(1), (int)q.size(2), (int)k.size(2), (int)q.size(3), causal ? 1 : 0, (float)scale,
-                        status.data_ptr<int>(), cur_stream()),
+                        (int)q.size(1), (int)q.size(2), (int)k.size(2), (int)q.size(3), (int)v.size(3), causal ? 1 : 0,
+                        (float)scale, status.data_ptr<int>(), cur_stream()),
            "fmha_fwd");
 }
 

@@ -2,8 +2,9 @@
 //
 //   out[b, t, h, :] = softmax(scale * q[b, t, h, :] . k[b, s, h / G, :]^T  (+ causal mask)) v[b, s, h / G, :]
 //
-// q, k, v and out are token-major [B, T, H, D] bf16 (the layout the fused RoPE kernel writes), D = 64 or
-// 128, grouped-query heads G = Hq / Hkv.  Optionally also writes lse[b, h, t] = log sum_s exp(scale q.k)
+// q, k, v and out are token-major [B, T, H, D] bf16 (the layout the fused RoPE kernel writes).  Head
+// dims: D = 64 or 128 for q, k, v alike, or d_qk = 192 with d_v = 128 (multi-head latent attention with
+// its decoupled RoPE part, prefill / training shape); grouped-query heads G = Hq / Hkv.  Optionally also writes lse[b, h, t] = log sum_s exp(scale q.k)
 // (natural log) for a backward pass.  The reference runs attention through PyTorch
 // (``src/forgeline/models/attention/causal.py:79-134``); this is the B200 kernel behind the same op.
 //
@@ -40,19 +41,25 @@ constexpr int TMEM_COLS = 512;
 constexpr uint32_t WAIT_LIMIT = 1u << 26;  // polls before a wait is declared dead (seconds)
 constexpr float LN2 = 0.6931471805599453f;
 
-template <int D>
+template <int D, int DV>
 struct Layout {
-  static constexpr int DSUB = D / 64;  // 64-column boxes per row of Q / K / V
+  static constexpr int DSUB = D / 64;   // 64-column boxes per row of Q / K
+  static constexpr int VSUB = DV / 64;  // ... of V
+  // V stages: two when they fit in shared memory, one for the 192-wide Q / K tiles
+  static constexpr int VST = (3 * DSUB + 2 * VSUB + 2) * SUB_BYTES + 256 + 1024 <= 232448 ? 2 : 1;
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + DSUB * SUB_BYTES;
   static constexpr int V_OFF = K_OFF + 2 * DSUB * SUB_BYTES;
-  static constexpr int P_OFF = V_OFF + 2 * DSUB * SUB_BYTES;
+  static constexpr int P_OFF = V_OFF + VST * VSUB * SUB_BYTES;
   static constexpr int BAR_OFF = P_OFF + 2 * SUB_BYTES;  // P: [128 queries][128 keys] as two boxes
   static constexpr int BYTES = BAR_OFF + 256;
 };
-// Every launch asks for the D = 128 footprint, so at most one CTA is resident per SM (a CTA allocates
-// all 512 TMEM columns).
-constexpr int SMEM_REQUEST = Layout<128>::BYTES + 1024;
+// Every launch asks for at least the D = 128 footprint, so at most one CTA is resident per SM (a CTA
+// allocates all 512 TMEM columns).
+template <int D, int DV>
+constexpr int smem_request() {
+  return (Layout<D, DV>::BYTES > Layout<128, 128>::BYTES ? Layout<D, DV>::BYTES : Layout<128, 128>::BYTES) + 1024;
+}
 
 struct Params {
   __nv_bfloat16* out;  // [B][T][Hq][D]
@@ -78,12 +85,12 @@ __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, wait(bar, parity));
 }
 
-template <int D>
+template <int D, int DV>
 __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant__ CUtensorMap mq,
                                                           const __grid_constant__ CUtensorMap mk,
                                                           const __grid_constant__ CUtensorMap mv, Params p) {
-  using L = Layout<D>;
-  constexpr int DSUB = L::DSUB;
+  using L = Layout<D, DV>;
+  constexpr int DSUB = L::DSUB, VSUB = L::VSUB, VST = L::VST;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sQ = smem + L::Q_OFF;
@@ -147,7 +154,7 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int k_issued = 0, v_issued = 0;  // key tiles whose K / V loads were issued
-      if (!RLB_TMA_X_OK(h * D) || !RLB_TMA_X_OK(hk * D)) fail(p.status, abort_flag, 12);
+      if (!RLB_TMA_X_OK(h * D) || !RLB_TMA_X_OK(hk * D) || !RLB_TMA_X_OK(hk * DV)) fail(p.status, abort_flag, 12);
       sm100::mbar_arrive_expect_tx(qfull, DSUB * SUB_BYTES);
 #pragma unroll
       for (int s = 0; s < DSUB; ++s) sm100::tma_load_3d(sQ + s * SUB_BYTES, &mq, qfull, h * D + 64 * s, q0, b);
@@ -163,14 +170,15 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
         for (int s = 0; s < DSUB; ++s)
           sm100::tma_load_3d(sK + (buf * DSUB + s) * SUB_BYTES, &mk, &kfull[buf], hk * D + 64 * s, j * BKV, b);
         k_issued = j + 1;
-        if (!wait(&vempty[buf], par ^ 1)) {
+        const int vb = j % VST;
+        if (!wait(&vempty[vb], ((j / VST) & 1) ^ 1)) {
           fail(p.status, abort_flag, 2);
           break;
         }
-        sm100::mbar_arrive_expect_tx(&vfull[buf], DSUB * SUB_BYTES);
+        sm100::mbar_arrive_expect_tx(&vfull[vb], VSUB * SUB_BYTES);
 #pragma unroll
-        for (int s = 0; s < DSUB; ++s)
-          sm100::tma_load_3d(sV + (buf * DSUB + s) * SUB_BYTES, &mv, &vfull[buf], hk * D + 64 * s, j * BKV, b);
+        for (int s = 0; s < VSUB; ++s)
+          sm100::tma_load_3d(sV + (vb * VSUB + s) * SUB_BYTES, &mv, &vfull[vb], hk * DV + 64 * s, j * BKV, b);
         v_issued = j + 1;
       }
       // every load issued here lands before the CTA exits (a buffer's earlier loads were consumed
@@ -179,14 +187,14 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
       for (int t = 0; t < 2; ++t) {
         const int jk = k_issued - 1 - t, jv = v_issued - 1 - t;
         if (jk >= 0) wait(&kfull[jk & 1], (jk >> 1) & 1);
-        if (jv >= 0) wait(&vfull[jv & 1], (jv >> 1) & 1);
+        if (jv >= 0 && t < VST) wait(&vfull[jv % VST], (jv / VST) & 1);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t id_s = sm100::idesc_bf16_f32(BQ, BKV, 0, 0);  // Q, K both K-major
-      constexpr uint32_t id_o = sm100::idesc_bf16_f32(BQ, D, 0, 1);    // P K-major, V [keys][D]: MN-major
+      constexpr uint32_t id_o = sm100::idesc_bf16_f32(BQ, DV, 0, 1);   // P K-major, V [keys][DV]: MN-major
       bool ok = wait(qfull, 0);
       if (!ok) fail(p.status, abort_flag, 3);
       const uint32_t qa = sm100::smem_u32(sQ), pa = sm100::smem_u32(sP);
@@ -221,7 +229,7 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
             fail(p.status, abort_flag, 6);
             break;
           }
-          if (!wait(&vfull[ib], ipar)) {
+          if (!wait(&vfull[i % VST], (i / VST) & 1)) {
             fail(p.status, abort_flag, 7);
             break;
           }
@@ -230,16 +238,16 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
             break;
           }
           sm100::tc_fence_after();
-          const uint32_t va = sm100::smem_u32(sV + ib * DSUB * SUB_BYTES);
+          const uint32_t va = sm100::smem_u32(sV + (i % VST) * VSUB * SUB_BYTES);
 #pragma unroll
           for (int k = 0; k < BKV / 16; ++k) {
             // P: 16 keys per MMA (K-major, like Q);  V: 16 key rows = two 8-row 1024-B atoms, the
             // 64-column boxes along D one SUB_BYTES apart
             const uint32_t poff = (uint32_t)(k >> 2) * SUB_BYTES + (uint32_t)(k & 3) * 32;
-            sm100::mma_f16(tmem + 2 * BKV + ib * D, sm100::desc_kmajor_sw128(pa + poff),
+            sm100::mma_f16(tmem + 2 * BKV + ib * DV, sm100::desc_kmajor_sw128(pa + poff),
                            sm100::desc_mnmajor_sw128(va + k * 2048, SUB_BYTES), id_o, k > 0);
           }
-          sm100::mma_commit(&vempty[ib]);
+          sm100::mma_commit(&vempty[i % VST]);
           sm100::mma_commit(&ofull[ib]);
         }
       }
@@ -254,9 +262,9 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
     const int rq = q0 + row;
     const uint32_t lanes = tmem + ((uint32_t)(qq * 32) << 16);
     const float sl2 = p.scale_log2;
-    float O[D];
+    float O[DV];
 #pragma unroll
-    for (int d = 0; d < D; ++d) O[d] = 0.f;
+    for (int d = 0; d < DV; ++d) O[d] = 0.f;
     float m = -INFINITY, l = 0.f;  // running row max (log2 units) and denominator
     float m_o = -INFINITY;         // max the register accumulator O is scaled to
     float m_p = -INFINITY;         // max the last P written was scaled to
@@ -303,9 +311,9 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
         sm100::tc_fence_after();
         const float a = (m_o == -INFINITY) ? 0.f : exp2f(m_o - m_p);
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < DV / 32; ++c) {
           uint32_t r[32];
-          sm100::tmem_ld32(lanes + 2 * BKV + ib * D + c * 32, r);
+          sm100::tmem_ld32(lanes + 2 * BKV + ib * DV + c * 32, r);
           sm100::tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 32; ++e) O[c * 32 + e] = fmaf(O[c * 32 + e], a, __uint_as_float(r[e]));
@@ -363,9 +371,9 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
         sm100::tc_fence_after();
         const float a = (m_o == -INFINITY) ? 0.f : exp2f(m_o - m_p);
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < DV / 32; ++c) {
           uint32_t r[32];
-          sm100::tmem_ld32(lanes + 2 * BKV + ib * D + c * 32, r);
+          sm100::tmem_ld32(lanes + 2 * BKV + ib * DV + c * 32, r);
           sm100::tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 32; ++e) O[c * 32 + e] = fmaf(O[c * 32 + e], a, __uint_as_float(r[e]));
@@ -373,9 +381,9 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
         sm100::tc_fence_before();
         if (rq < p.T) {
           const float inv = l > 0.f ? 1.f / l : 0.f;
-          __nv_bfloat16* dst = p.out + (((long long)b * p.T + rq) * p.Hq + h) * D;
+          __nv_bfloat16* dst = p.out + (((long long)b * p.T + rq) * p.Hq + h) * DV;
 #pragma unroll
-          for (int v = 0; v < D / 8; ++v) {
+          for (int v = 0; v < DV / 8; ++v) {
             uint4 pk;
             uint32_t* w = (uint32_t*)&pk;
 #pragma unroll
@@ -432,29 +440,31 @@ static bool make_map(CUtensorMap* m, const void* ptr, int B, int T, int HD) {
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int D>
+template <int D, int DV>
 static cudaError_t launch(const void* q, const void* k, const void* v, const Params& p, cudaStream_t s) {
   CUtensorMap mq, mk, mv;
   if (!make_map(&mq, q, p.B, p.T, p.Hq * D) || !make_map(&mk, k, p.B, p.T, p.Hkv * D) ||
-      !make_map(&mv, v, p.B, p.T, p.Hkv * D))
+      !make_map(&mv, v, p.B, p.T, p.Hkv * DV))
     return cudaErrorInvalidResourceHandle;
-  auto kern = fmha_fwd_kernel<D>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_REQUEST);
+  auto kern = fmha_fwd_kernel<D, DV>;
+  constexpr int smem = smem_request<D, DV>();
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   (void)cudaGetLastError();
   const dim3 grid((p.T + BQ - 1) / BQ, p.Hq, p.B);
-  kern<<<grid, 192, SMEM_REQUEST, s>>>(mq, mk, mv, p);
+  kern<<<grid, 192, smem, s>>>(mq, mk, mv, p);
   return cudaGetLastError();
 }
 
 }  // namespace fmha
 
-// q [B][T][Hq][D], k / v [B][T][Hkv][D], out [B][T][Hq][D] (bf16, contiguous); lse [B][Hq][T] fp32 or null.
+// q [B][T][Hq][D], k [B][T][Hkv][D], v [B][T][Hkv][DV], out [B][T][Hq][DV] (bf16, contiguous); lse
+// [B][Hq][T] fp32 or null.  (D, DV) = (64, 64), (128, 128) or (192, 128).
 cudaError_t rlb_fmha_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int B, int T, int Hq,
-                         int Hkv, int D, int causal, float scale, int* status, cudaStream_t s) {
+                         int Hkv, int D, int DV, int causal, float scale, int* status, cudaStream_t s) {
   if (B <= 0 || T <= 0) return cudaSuccess;
-  if ((D != 64 && D != 128) || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Hq > 65535 || B > 65535)
-    return cudaErrorInvalidValue;
+  const bool shape_ok = (D == 64 && DV == 64) || (D == 128 && DV == 128) || (D == 192 && DV == 128);
+  if (!shape_ok || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Hq > 65535 || B > 65535) return cudaErrorInvalidValue;
   if ((((uintptr_t)q) | ((uintptr_t)k) | ((uintptr_t)v) | ((uintptr_t)out)) & 15) return cudaErrorInvalidDevicePointer;
   fmha::Params p{};
   p.out = (__nv_bfloat16*)out;
@@ -466,5 +476,6 @@ cudaError_t rlb_fmha_fwd(const void* q, const void* k, const void* v, void* out,
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
   p.status = status;
-  return D == 128 ? fmha::launch<128>(q, k, v, p, s) : fmha::launch<64>(q, k, v, p, s);
+  if (D == 192) return fmha::launch<192, 128>(q, k, v, p, s);
+  return D == 128 ? fmha::launch<128, 128>(q, k, v, p, s) : fmha::launch<64, 64>(q, k, v, p, s);
 }

@@ -63,10 +63,10 @@ cudaError_t rlb_gemm_allreduce(int b_mn, int M, int N, int K, const void* A, lon
                                const unsigned long long* flag, int world, int rank, int epoch, int* status,
                                int grid, cudaStream_t s);
 
-// Fused attention forward (tcgen05): q [B][T][Hq][D], k / v [B][T][Hkv][D], out [B][T][Hq][D] bf16; lse
-// [B][Hq][T] fp32 (natural log) or null.  D = 64 or 128.
+// Fused attention forward (tcgen05): q [B][T][Hq][D], k [B][T][Hkv][D], v [B][T][Hkv][DV], out [B][T][Hq][DV]
+// bf16; lse [B][Hq][T] fp32 (natural log) or null.  (D, DV) = (64, 64), (128, 128) or (192, 128).
 cudaError_t rlb_fmha_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int B, int T, int Hq,
-                         int Hkv, int D, int causal, float scale, int* status, cudaStream_t s);
+                         int Hkv, int D, int DV, int causal, float scale, int* status, cudaStream_t s);
 // Fused attention backward: dq fp32 [B][T][Hq][D] (zeroed by the caller, accumulated), dk / dv bf16
 // [B][T][Hkv][D]; lse / delta fp32 [B][Hq][T] (delta = rowsum(dout * out)).
 cudaError_t rlb_fmha_bwd(const void* q, const void* k, const void* v, const void* dout, const float* lse,

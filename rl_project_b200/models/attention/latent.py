@@ -57,6 +57,11 @@ class MultiHeadLatentAttention(nn.Module):
         k = torch.cat([k_nope.transpose(1, 2), k_rope.expand(-1, self.n_heads, -1, -1)], dim=-1)
         q = torch.cat([q_nope.transpose(1, 2), q_rope], dim=-1)
         v = v.transpose(1, 2)
+        if q.is_cuda and self.attn_logit_cap == 0 and T == k.shape[2] and not torch.is_grad_enabled():
+            from rl_project_b200.ops import attention as A
+
+            if A._ATTN == "tcgen05" and q.dtype == torch.bfloat16 and (q.shape[-1], v.shape[-1]) in A.FMHA_SHAPES:
+                return A.fmha_forward(q, k, v, True, self.softmax_scale)[0]  # own kernel (prefill; forward only)
         if q.is_cuda and self.attn_logit_cap == 0 and T == k.shape[2]:
             import torch.nn.functional as F
 

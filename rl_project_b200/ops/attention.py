@@ -85,6 +85,7 @@ def _fused_sdpa(q, k, v, rep, dropout_p, scale):
 
 
 _ATTN = os.environ.get("RLB_ATTN", "sdpa")
+FMHA_SHAPES = ((64, 64), (128, 128), (192, 128))  # (d_qk, d_v) of the forward kernel; the backward: d_qk == d_v
 
 
 def _token_major(x: torch.Tensor) -> torch.Tensor:
@@ -95,17 +96,20 @@ def _token_major(x: torch.Tensor) -> torch.Tensor:
 
 def fmha_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
                  scale: Optional[float] = None, with_lse: bool = False) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
-    """Attention forward on the sm_100a kernel.  ``q [B, Hq, T, D]``, ``k, v [B, Hkv, T, D]`` (bf16, D 64 or
-    128; token-major storage avoids a copy) -> ``(out [B, Hq, T, D]`` as a view of ``[B, T, Hq, D]`` storage,
-    ``lse [B, Hq, T]`` fp32 natural-log softmax denominators or None)."""
+    """Attention forward on the sm_100a kernel.  ``q [B, Hq, T, D]``, ``k [B, Hkv, T, D]``, ``v [B, Hkv, T, DV]``
+    (bf16; (D, DV) = (64, 64), (128, 128) or MLA's (192, 128); token-major storage avoids a copy) ->
+    ``(out [B, Hq, T, DV]`` as a view of ``[B, T, Hq, DV]`` storage, ``lse [B, Hq, T]`` fp32 natural-log
+    softmax denominators or None)."""
     from rl_project_b200.core.errors import KernelError
     from rl_project_b200.ops._ext import native
 
     B, Hq, T, D = q.shape
-    if D not in (64, 128) or q.dtype != torch.bfloat16 or Hq % k.shape[1]:
-        raise KernelError(f"fmha_forward: unsupported shape / dtype (D={D}, {q.dtype}, Hq={Hq}, Hkv={k.shape[1]})")
+    DV = v.shape[-1]
+    if (D, DV) not in FMHA_SHAPES or q.dtype != torch.bfloat16 or Hq % k.shape[1]:
+        raise KernelError(f"fmha_forward: unsupported shape / dtype (D={D}, DV={DV}, {q.dtype}, Hq={Hq}, "
+                          f"Hkv={k.shape[1]})")
     qt, kt, vt = _token_major(q), _token_major(k), _token_major(v)
-    out = torch.empty_like(qt)
+    out = torch.empty(B, T, Hq, DV, dtype=q.dtype, device=q.device)
     lse = torch.empty(B, Hq, T, dtype=torch.float32, device=q.device) if with_lse else torch.empty(0, device=q.device)
     native().fmha_fwd(qt, kt, vt, out, lse, bool(causal), float(scale if scale is not None else D ** -0.5),
                       _status(q.device))

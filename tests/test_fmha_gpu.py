@@ -67,3 +67,21 @@ def test_fmha_backward_matches_fp32_autograd(B, T, Hq, Hkv, D, causal):
     for name, a, r in (("dq", qs.grad, q32.grad), ("dk", ks.grad, k32.grad), ("dv", vs.grad, v32.grad)):
         rel = ((a.float() - r).norm() / r.norm()).item()
         assert rel < 2e-2, (name, rel)
+
+
+@pytest.mark.parametrize("T,causal", [(256, True), (200, False)])
+def test_fmha_forward_mla_shape(T, causal):
+    """d_qk 192 (128 no-RoPE + 64 RoPE dims) with d_v 128: the prefill shape of multi-head latent attention."""
+    from rl_project_b200.ops.attention import attention_reference, fmha_check, fmha_forward
+
+    g = torch.Generator(device="cuda").manual_seed(T)
+    B, H = 1, 4
+    q = torch.randn(B, T, H, 192, device="cuda", generator=g).bfloat16().transpose(1, 2)
+    k = torch.randn(B, T, H, 192, device="cuda", generator=g).bfloat16().transpose(1, 2)
+    v = torch.randn(B, T, H, 128, device="cuda", generator=g).bfloat16().transpose(1, 2)
+    out, _ = fmha_forward(q, k, v, causal=causal)
+    torch.cuda.synchronize()
+    fmha_check(q.device)
+    ref = attention_reference(q.float(), k.float(), v.float(), causal=causal, q_offset=0).float()
+    assert out.shape == (B, H, T, 128)
+    assert (out.float() - ref).abs().max().item() < 2e-2
