@@ -133,6 +133,31 @@ int64_t bounds_status(int64_t device, bool clear) {
   return v;
 }
 
+// ---------------------------------------------------------------- NF4 GEMM
+// mode 0: x [M, K] -> x W^T [M, N];  mode 1: dy [M, N] -> dy W [M, K].  W [N, K] given as NF4 packed bytes +
+// absmax; K % 64 == 0.
+at::Tensor nf4_gemm(const at::Tensor& A, const at::Tensor& packed, const at::Tensor& absmax, const at::Tensor& table,
+                    int64_t mode, int64_t N, int64_t K, const at::Tensor& status) {
+  check_bf16(A, "A");
+  check_contig(A, "A");
+  check_dev(packed, A, "packed");
+  check_dev(absmax, A, "absmax");
+  check_dev(table, A, "table");
+  check_dev(status, A, "status");
+  TORCH_CHECK(A.dim() == 2 && A.size(1) == (mode == 0 ? K : N), "A: [M, K] (mode 0) or [M, N] (mode 1)");
+  TORCH_CHECK(packed.scalar_type() == at::kByte && packed.numel() * 2 >= N * K, "packed: uint8, N*K/2 bytes");
+  TORCH_CHECK(absmax.scalar_type() == at::kFloat && absmax.numel() * 64 >= N * K, "absmax: fp32 per 64 elements");
+  TORCH_CHECK(table.scalar_type() == at::kFloat && table.numel() == 16, "table: 16 fp32 levels");
+  TORCH_CHECK(status.scalar_type() == at::kInt, "status: int32");
+  const c10::cuda::CUDAGuard g(A.device());
+  auto out = at::empty({A.size(0), mode == 0 ? N : K}, A.options());
+  CHECK_OK(rlb_nf4_gemm((int)mode, (int)A.size(0), (int)N, (int)K, A.data_ptr(), packed.data_ptr(),
+                        absmax.data_ptr<float>(), table.data_ptr<float>(), out.data_ptr(), status.data_ptr<int>(),
+                        cur_stream()),
+           "nf4_gemm");
+  return out;
+}
+
 // ---------------------------------------------------------------- RoPE
 std::vector<at::Tensor> rope_qkv_fwd(const at::Tensor& qkv, const at::Tensor& cos_t, const at::Tensor& sin_t,
                                      const c10::optional<at::Tensor>& positions, int64_t B, int64_t T, int64_t Hq,
@@ -793,6 +818,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_fwd", &embed_fwd);
   m.def("embed_bwd", &embed_bwd);
   m.def("nf4_dequant", &nf4_dequant);
+  m.def("nf4_gemm", &nf4_gemm);
   m.def("gemm", &gemm);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_allreduce", &gemm_allreduce);

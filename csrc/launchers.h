@@ -63,6 +63,11 @@ cudaError_t rlb_gemm_allreduce(int b_mn, int M, int N, int K, const void* A, lon
                                const unsigned long long* flag, int world, int rank, int epoch, int* status,
                                int grid, cudaStream_t s);
 
+// NF4-weight GEMM with dequantisation in the tcgen05 main loop: mode 0 C[M][N] = A[M][K] W^T, mode 1
+// C[M][K] = A[M][N] W; W [N][K] as NF4 (packed bytes, fp32 absmax per 64 elements, 16-level table).
+cudaError_t rlb_nf4_gemm(int mode, int M, int N, int K, const void* A, const void* packed, const float* absmax,
+                         const float* table, void* C, int* status, cudaStream_t s);
+
 // Fused attention forward (tcgen05): q [B][T][Hq][D], k [B][T][Hkv][D], v [B][T][Hkv][DV], out [B][T][Hq][DV]
 // bf16; lse [B][Hq][T] fp32 (natural log) or null.  (D, DV) = (64, 64), (128, 128) or (192, 128).
 cudaError_t rlb_fmha_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int B, int T, int Hq,

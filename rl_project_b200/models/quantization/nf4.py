@@ -4,11 +4,15 @@ two indices per byte, high nibble first (``src/forgeline/models/quantization/nf4
 The 16 NF4 levels are the QLoRA paper's normal-quantile table (Dettmers et
 al., 2023), the same data the reference ships.  On CUDA, ``NF4Linear``
 dequantises in the sm_100a kernel csrc/nf4.cu straight to bf16 in one pass
-(the reference dequantises through fp32 index tensors on every forward).
+(the reference dequantises through fp32 index tensors on every forward); with
+``RLB_NF4_GEMM=1`` the forward and input gradient instead run csrc/nf4_gemm.cu,
+which expands the weight tile by tile inside the tcgen05 GEMM (written, not yet
+run on a GPU).
 """
 
 from __future__ import annotations
 
+import os
 from typing import Tuple
 
 import torch
@@ -59,6 +63,40 @@ def dequantize_nf4(packed: torch.Tensor, absmax: torch.Tensor, shape: torch.Size
     return vals.reshape(-1)[:n].view(shape).to(dtype)
 
 
+_NF4_GEMM = os.environ.get("RLB_NF4_GEMM", "0") == "1"
+_STATUS: dict = {}
+
+
+def _status(device: torch.device) -> torch.Tensor:
+    if device.index not in _STATUS:
+        _STATUS[device.index] = torch.zeros(1, dtype=torch.int32, device=device)
+    return _STATUS[device.index]
+
+
+class _NF4Matmul(torch.autograd.Function):
+    """``x @ W^T`` with the NF4 weight expanded inside the tcgen05 GEMM (csrc/nf4_gemm.cu); the backward
+    is the same kernel's ``dy @ W`` (the quantised base weight is frozen: no weight gradient)."""
+
+    @staticmethod
+    def forward(ctx, x2, lin):
+        from rl_project_b200.ops._ext import native
+
+        ctx.lin = lin
+        N, K = lin.weight_shape
+        return native().nf4_gemm(x2, lin.weight_packed, lin.weight_absmax.float(), lin._table(x2.device), 0, N, K,
+                                 _status(x2.device))
+
+    @staticmethod
+    def backward(ctx, dy):
+        from rl_project_b200.ops._ext import native
+
+        lin = ctx.lin
+        N, K = lin.weight_shape
+        dx = native().nf4_gemm(dy.contiguous(), lin.weight_packed, lin.weight_absmax.float(), lin._table(dy.device), 1, N, K,
+                               _status(dy.device))
+        return dx, None
+
+
 class NF4Linear(nn.Module):
     def __init__(self, original: nn.Linear):
         super().__init__()
@@ -75,7 +113,18 @@ class NF4Linear(nn.Module):
     def dequantized_weight(self, dtype: torch.dtype = torch.float32) -> torch.Tensor:
         return dequantize_nf4(self.weight_packed, self.weight_absmax, torch.Size(self.weight_shape), dtype)
 
+    def _table(self, device: torch.device) -> torch.Tensor:
+        t = getattr(self, "_table_dev", None)
+        if t is None or t.device != device:
+            t = self._table_dev = NF4_TABLE.to(device)
+        return t
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if (_NF4_GEMM and x.is_cuda and x.dtype == torch.bfloat16 and self.in_features % 64 == 0
+                and self.out_features % 8 == 0):
+            shape = x.shape
+            y = _NF4Matmul.apply(x.reshape(-1, shape[-1]).contiguous(), self).view(*shape[:-1], self.out_features)
+            return y + self.bias.to(y.dtype) if self.bias is not None else y
         w = self.dequantized_weight(x.dtype if x.is_cuda else torch.float32).to(x.device, x.dtype)
         b = self.bias.to(x.dtype) if self.bias is not None else None
         return F.linear(x, w, b)

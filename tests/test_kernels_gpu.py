@@ -264,3 +264,27 @@ def test_tcgen05_linear_autograd():
     _close(y, yr, 1e-2)
     _close(x.grad, xr.grad, 2e-2)
     _close(w.grad, wr.grad, 2e-2)
+
+
+@pytest.mark.skipif(__import__("os").environ.get("RLB_NF4_TEST") != "1",
+                    reason="NF4 main-loop GEMM not yet validated on a GPU (set RLB_NF4_TEST=1)")
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (300, 520, 192), (64, 256, 1024)])
+def test_nf4_gemm_matches_dequantised_matmul(M, N, K):
+    from rl_project_b200.models.quantization.nf4 import NF4_TABLE, dequantize_nf4, quantize_nf4
+    from rl_project_b200.ops._ext import native
+
+    g = torch.Generator().manual_seed(M + N)
+    w = torch.randn(N, K, generator=g) * 0.05
+    packed, absmax, shape = quantize_nf4(w)
+    wd = dequantize_nf4(packed, absmax, shape).cuda()  # fp32 oracle of the quantised weight
+    packed, absmax, table = packed.cuda(), absmax.float().cuda(), NF4_TABLE.cuda()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    x = torch.randn(M, K, generator=g).cuda().bfloat16()
+    dy = torch.randn(M, N, generator=g).cuda().bfloat16()
+    y = native().nf4_gemm(x, packed, absmax, table, 0, N, K, status)
+    dx = native().nf4_gemm(dy, packed, absmax, table, 1, N, K, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    for got, ref in ((y, x.float() @ wd.t()), (dx, dy.float() @ wd)):
+        rel = ((got.float() - ref).norm() / ref.norm()).item()
+        assert rel < 1e-2, rel
