@@ -325,6 +325,9 @@ class DistributedConfig:
         _check(self.strategy in STRATEGIES, f"distributed strategy must be one of {STRATEGIES}, got {self.strategy!r}")
         _check(min(self.tensor_parallel_size, self.pipeline_parallel_size, self.expert_parallel_size,
                    self.context_parallel_size) >= 1, "parallel sizes must be >= 1")
+        # reserved for a context-parallel attention path; sequences up to block_size fit one GPU today
+        _check(self.context_parallel_size == 1,
+               "context_parallel_size > 1 is not supported: sequences are not split across GPUs (keep it at 1)")
         _check(self.backend in ("auto", "nccl", "gloo"), "backend must be auto|nccl|gloo")
         _check(not (self.strategy == "deepspeed" and not self.deepspeed_config),
                "deepspeed strategy requires deepspeed_config path")

@@ -172,6 +172,8 @@ def test_topology_validation():
                     "data_parallel": 2}
     with pytest.raises(DistributedConfigError):  # a tensor-parallel strategy with tp = 1
         validate_distributed_config(DistributedConfig(strategy="tensor_parallel"), world_size=2)
+    with pytest.raises(ConfigError):  # accepted by the schema, refused instead of silently ignored
+        DistributedConfig(strategy="fsdp", context_parallel_size=2).validate()
 
 
 def test_build_strategy_and_env(monkeypatch):
