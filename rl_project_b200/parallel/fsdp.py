@@ -14,9 +14,11 @@ Forward: a pre-forward hook all-gathers the unit's bf16 shards into the full
 flat buffer on a communication stream and points every parameter's ``.data``
 at its slice; the gather of unit ``i+1`` is issued when unit ``i`` starts
 (prefetch), so NCCL traffic overlaps compute.  With ``reshard_after_forward``
-the full buffer's storage is released after the unit's forward and
+(the default) the full buffer's storage is released after the unit's forward and
 re-gathered when its backward starts (the storage object is kept, so tensors
-saved for backward stay valid).
+saved for backward stay valid); with it off, the gathered parameters stay
+until the unit's gradients are reduced, trading memory for one all-gather per
+unit and step.
 
 Backward: when every parameter of a unit has accumulated its gradient
 (``register_post_accumulate_grad_hook``), the gradients are packed into one
@@ -116,6 +118,8 @@ class FSDPStrategy(_ProcessGroupStrategy):
         super().__init__(cfg)
         self.name = name
         self.shard_params = reshard_params  # zero2 keeps full bf16 params between steps
+        # False: a unit's gathered parameters stay until its backward (no re-gather; more memory)
+        self.reshard_after_forward = bool(getattr(cfg, "reshard_after_forward", True))
         self.units: List[_Unit] = []
         self.root: Optional[_Unit] = None
         self.comm_stream = None
@@ -350,7 +354,8 @@ class FSDPStrategy(_ProcessGroupStrategy):
                 for o in outs:
                     if isinstance(o, torch.Tensor) and o.requires_grad:
                         o.register_hook(lambda g, _u=u: self._pre_backward(_u, g))
-                self._release_after_forward(u)
+                if self.reshard_after_forward:
+                    self._release_after_forward(u)
             elif self.shard_params and u is not self.root:
                 self._release_after_forward(u)
             return output

@@ -23,7 +23,8 @@ def _manifest(strategy: str, out: str):
         "trainer": {"device": "cpu", "precision": {"dtype": "float32"}, "eval_every": 0, "log_every": 0,
                     "max_steps": STEPS, "batch_size": 2, "optimizer": {"learning_rate": 1e-2, "grad_clip": 0.5},
                     "schedule": {"name": "constant", "warmup_steps": 0}, "checkpoint": {"save_every": 0}},
-        "distributed": {"strategy": strategy, "backend": "gloo", "timeout_s": 120},
+        "distributed": {"strategy": strategy.replace("_keep", ""), "backend": "gloo", "timeout_s": 120,
+                        "reshard_after_forward": not strategy.endswith("_keep")},
         "output_dir": out})
 
 
@@ -63,7 +64,7 @@ def _train(strategy_name: str, rank: int, world: int, out: str):
     alg = PretrainAlgorithm(model, _Iter(_global_batches(), rows), PretrainConfig(batch_size=4 // world))
     trainer = Trainer(ctx, alg, strategy=strat)
     losses = [trainer.train_step().loss for _ in range(STEPS)]
-    if strat is not None and strategy_name in ("fsdp", "zero2"):
+    if strat is not None and strategy_name in ("fsdp", "zero2", "fsdp_keep"):
         state = strat.full_state_dict()
     else:
         state = {k: v.detach().clone() for k, v in model.state_dict().items()}
@@ -79,7 +80,7 @@ def _worker(rank, world, port, out, strategy_name):
     strat.teardown()
 
 
-@pytest.mark.parametrize("strategy_name", ["ddp", "fsdp", "zero2"])
+@pytest.mark.parametrize("strategy_name", ["ddp", "fsdp", "zero2", "fsdp_keep"])  # _keep: no reshard after forward
 def test_two_process_matches_single_process(strategy_name):
     with tempfile.TemporaryDirectory() as out:
         mp.start_processes(_worker, args=(2, free_port(), out, strategy_name), nprocs=2, join=True,
