@@ -116,28 +116,53 @@ class PostTrainingAlgorithm(ABC):
     # same batches an uninterrupted run would (generators, shuffles, counters)
     _data_attrs = ("gen", "rng", "_order", "tokens_seen", "ema_loss")
 
+    # the same kind of state on the algorithm's data source (``train`` / ``dataset``): a source that draws
+    # from its own generator or walks its own cursor is restored too, saved as "<source>.<attr>"
+    _source_names = ("train", "dataset")
+    _source_attrs = ("gen", "rng", "_order", "_i", "i", "pos", "_pos", "epoch")
+
+    @staticmethod
+    def _capture(val: Any):
+        if isinstance(val, torch.Generator):
+            return ("torch_gen", val.get_state())
+        if hasattr(val, "getstate") and hasattr(val, "setstate"):
+            return ("py_rng", val.getstate())
+        if isinstance(val, (int, float, list, type(None))):
+            return ("value", list(val) if isinstance(val, list) else val)
+        return None
+
     def data_state(self) -> Dict[str, Any]:
         out: Dict[str, Any] = {}
         for name in self._data_attrs:
-            if not hasattr(self, name):
+            if hasattr(self, name):
+                c = self._capture(getattr(self, name))
+                if c is not None:
+                    out[name] = c
+        for src_name in self._source_names:
+            src = getattr(self, src_name, None)
+            if src is None or isinstance(src, (torch.Tensor, list, tuple, dict)):
                 continue
-            val = getattr(self, name)
-            if isinstance(val, torch.Generator):
-                out[name] = ("torch_gen", val.get_state())
-            elif hasattr(val, "getstate") and hasattr(val, "setstate"):
-                out[name] = ("py_rng", val.getstate())
-            elif isinstance(val, (int, float, list, type(None))):
-                out[name] = ("value", list(val) if isinstance(val, list) else val)
+            for name in self._source_attrs:
+                if hasattr(src, name):
+                    c = self._capture(getattr(src, name))
+                    if c is not None:
+                        out[f"{src_name}.{name}"] = c
         return out
 
     def load_data_state(self, state: Mapping[str, Any]) -> None:
-        for name, (kind, val) in (state or {}).items():
-            if kind == "torch_gen" and hasattr(self, name):
-                getattr(self, name).set_state(val)
-            elif kind == "py_rng" and hasattr(self, name):
-                getattr(self, name).setstate(val)
+        for key, (kind, val) in (state or {}).items():
+            obj, name = self, key
+            if "." in key:
+                src_name, name = key.split(".", 1)
+                obj = getattr(self, src_name, None)
+                if obj is None:
+                    continue
+            if kind == "torch_gen" and hasattr(obj, name):
+                getattr(obj, name).set_state(val)
+            elif kind == "py_rng" and hasattr(obj, name):
+                getattr(obj, name).setstate(val)
             elif kind == "value":
-                setattr(self, name, list(val) if isinstance(val, list) else val)
+                setattr(obj, name, list(val) if isinstance(val, list) else val)
 
 
 def _as_tensor(v: Any, device: torch.device) -> torch.Tensor:
