@@ -100,7 +100,6 @@ class InferenceEngine:
         self._pinned: Optional[torch.Tensor] = None
         self.profile = profile and self.device.type == "cuda"
         self._prof: Dict[str, float] = {}
-        self._base_seed = int(torch.initial_seed())
         self._sample_calls = 0
         self._thread: Optional[threading.Thread] = None
         self._stop = threading.Event()
@@ -486,7 +485,9 @@ class InferenceEngine:
         if evs is not None:
             evs.append(self._event())
         self._sample_calls += 1
-        seed = (self._base_seed * 1_000_003 + self._sample_calls) & ((1 << 62) - 1)
+        # the step's sampling seed comes from torch's host generator, so a checkpoint's RNG state (which
+        # holds that generator) also fixes every sample drawn after a resume
+        seed = int(torch.randint(0, 1 << 62, (1,)).item())
         out = torch.empty(B, dtype=torch.long, device=logits.device)
         fused = [i for i, s in enumerate(seqs) if self._plain(s.req.params)] if logits.is_cuda else []
         if fused:
