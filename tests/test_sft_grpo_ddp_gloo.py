@@ -86,11 +86,13 @@ def _worker(rank, port, out, phase):
         else:
             res = _run(_manifest("sft", os.path.join(out, phase), 6, strategy, save_every=3))
     else:
-        res = _run(_manifest("grpo", os.path.join(out, "grpo"), 24, lr=3e-2,
+        resumed = phase == "grpo_resumed"
+        res = _run(_manifest("grpo", os.path.join(out, phase), 24, lr=3e-2, save_every=0 if resumed else 12,
                              checkpoint_path=os.path.join(out, "sft", "ckpt", "final"),
                              reward={"type": "verifier", "verifier": "last_token_parity"},
                              algorithm_params={"group_size": 4, "prompts_per_step": 2, "kl_coef": 0.0,
-                                               "rollout": {"max_new_tokens": 6, "temperature": 1.0}}))
+                                               "rollout": {"max_new_tokens": 6, "temperature": 1.0}}),
+                   resume=os.path.join(out, "grpo", "ckpt", "step_00000012") if resumed else None)
     torch.save(res, os.path.join(out, f"{phase}{rank}.pt"))
 
 
@@ -103,7 +105,8 @@ def _phase(out, phase):
 @pytest.fixture(scope="module")
 def runs(tmp_path_factory):
     out = str(tmp_path_factory.mktemp("ddp_sft_grpo"))
-    return {ph: _phase(out, ph) for ph in ("sft", "sft_resumed", "grpo", "sft_fsdp", "sft_fsdp_resumed")}
+    return {ph: _phase(out, ph) for ph in ("sft", "sft_resumed", "grpo", "grpo_resumed", "sft_fsdp",
+                                           "sft_fsdp_resumed")}
 
 
 @pytest.mark.parametrize("job", ["sft", "sft_fsdp"])
@@ -130,3 +133,12 @@ def test_grpo_replicas_identical_and_reward_rises(runs):
     reward = [(a["reward_mean"] + b["reward_mean"]) / 2 for a, b in zip(m0, m1)]
     first, last = sum(reward[:8]) / 8, sum(reward[-8:]) / 8
     assert last > first + 0.15, reward
+
+
+def test_grpo_resume_is_exact_on_every_rank(runs):
+    """Prompt choice, sampled rollouts and updates after the step-12 checkpoint repeat exactly."""
+    for r in range(WORLD):
+        full_losses, _, w_full = runs["grpo"][r]
+        res_losses, _, w_res = runs["grpo_resumed"][r]
+        assert res_losses == full_losses[12:], (r, res_losses, full_losses[12:])
+        assert torch.equal(w_res, w_full), r
