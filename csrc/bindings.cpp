@@ -106,21 +106,27 @@ std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& h, const at::Tensor& w, co
 
 // ---------------------------------------------------------------- index-error word
 // One int32 per device that kernels without a caller-supplied status word report index errors into
-// (first error kept).  bounds_status() reads it (synchronising) and optionally clears it.
+// (first error kept).  bounds_status() reads it (synchronising) and optionally clears it.  The word is a
+// plain cudaMalloc kept until the process exits (no tensor with static lifetime, which would be freed
+// after the caching allocator during interpreter shutdown).
 static int* bounds_word(const at::Device& d) {
   static std::mutex mu;
-  static std::unordered_map<int, at::Tensor> words;
+  static std::unordered_map<int, int*> words;
   std::lock_guard<std::mutex> lock(mu);
   auto it = words.find(d.index());
   if (it == words.end()) {
-    // the word must outlive any graph: memory taken during stream capture belongs to the graph's pool
+    const c10::cuda::CUDAGuard g(d);
+    // allocated outside any stream capture: the first RoPE call on a device must come before capture
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     C10_CUDA_CHECK(cudaStreamIsCapturing(c10::cuda::getCurrentCUDAStream(d.index()).stream(), &cap));
     TORCH_CHECK(cap == cudaStreamCaptureStatusNone,
                 "the first RoPE call on a device allocates its index-error word: make it before stream capture");
-    it = words.emplace(d.index(), at::zeros({1}, at::TensorOptions().dtype(at::kInt).device(d))).first;
+    int* w = nullptr;
+    C10_CUDA_CHECK(cudaMalloc(&w, sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
+    it = words.emplace(d.index(), w).first;
   }
-  return it->second.data_ptr<int>();
+  return it->second;
 }
 
 int64_t bounds_status(int64_t device, bool clear) {
