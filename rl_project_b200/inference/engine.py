@@ -620,7 +620,7 @@ class InferenceEngine:
     def stats(self) -> Dict[str, Any]:
         out = {**self.scheduler.stats(), "total_tokens": self.total_tokens, "prefill_tokens": self.prefill_tokens,
                "shared_prefills": self.shared_prefills, "decode_steps": self.decode_steps, "paged": self.paged,
-               "spans": self.tracer.summary()}
+               "decode_graphs": len(self._graphs) if self.decode_graphs else 0, "spans": self.tracer.summary()}
         if self.kv is not None:
             out["kv_cache_bytes"] = self.kv.nbytes
         return out

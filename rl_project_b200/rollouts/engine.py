@@ -41,6 +41,7 @@ class RolloutConfig:
     engine: str = "auto"  # "auto" | "paged" | "generate"
     engine_max_batch: int = 256  # sequences decoding at once in the paged engine
     engine_kv_blocks: Optional[int] = None  # KV pool size in 16-token blocks (default: enough for max_batch)
+    engine_decode_graphs: Optional[bool] = None  # replay decode steps from CUDA graphs (None: RLB_DECODE_GRAPHS)
 
 
 class RolloutEngine:
@@ -71,7 +72,8 @@ class RolloutEngine:
 
             per_seq = (model.spec.block_size + 15) // 16 + 1
             self._engine = InferenceEngine(model, max_batch=self.cfg.engine_max_batch,
-                                           max_blocks=self.cfg.engine_kv_blocks or self.cfg.engine_max_batch * per_seq)
+                                           max_blocks=self.cfg.engine_kv_blocks or self.cfg.engine_max_batch * per_seq,
+                                           decode_graphs=self.cfg.engine_decode_graphs)
         return self._engine
 
     def release_engine(self) -> None:
