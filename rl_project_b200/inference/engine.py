@@ -347,6 +347,27 @@ class InferenceEngine:
             b *= 2
         return max(n, min(b, cap))
 
+    @staticmethod
+    def stage_graph_inputs(hv: np.ndarray, tokens: List[int], positions: List[int], tables: List[List[int]],
+                           Bb: int, Wb: int, pad_block: int, bs: int) -> None:
+        """Fill the int32 staging buffer of a (Bb, Wb) decode graph: tokens, positions, context lengths,
+        slot blocks, slot offsets ([Bb] each), then the [Bb, Wb] block tables.  Rows past the real batch
+        decode token 0 at position 0 with a one-token context in ``pad_block``."""
+        B = len(tokens)
+        hv[:5 * Bb + Bb * Wb] = 0
+        pos = np.asarray(positions, dtype=np.int64)
+        hv[:B] = np.asarray(tokens, dtype=np.int64)
+        hv[Bb:Bb + B] = pos
+        hv[2 * Bb:3 * Bb] = 1
+        hv[2 * Bb:2 * Bb + B] = pos + 1
+        hv[3 * Bb:4 * Bb] = pad_block
+        hv[4 * Bb:4 * Bb + B] = pos % bs
+        grid = hv[5 * Bb:5 * Bb + Bb * Wb].reshape(Bb, Wb)
+        grid[:, 0] = pad_block
+        for b, t in enumerate(tables):
+            grid[b, :len(t)] = t
+        hv[3 * Bb:3 * Bb + B] = grid[np.arange(B), pos // bs]
+
     def reset_graphs(self) -> None:
         """Drop the captured decode graphs (they are captured again on use)."""
         self._graphs.clear()
@@ -411,20 +432,8 @@ class InferenceEngine:
         if self._pinned is None or self._pinned.numel() < n:
             self._pinned = torch.empty(max(n, 1024), dtype=torch.int32, pin_memory=True)
         host = self._pinned[:n]
-        hv = host.numpy()
-        hv[:] = 0
-        pos = np.fromiter((s.position for s in seqs), dtype=np.int64, count=B)
-        hv[:B] = np.fromiter((s.tokens[-1] for s in seqs), dtype=np.int64, count=B)
-        hv[Bb:Bb + B] = pos
-        hv[2 * Bb:3 * Bb] = 1
-        hv[2 * Bb:2 * Bb + B] = pos + 1
-        hv[3 * Bb:4 * Bb] = self._pad_block
-        hv[4 * Bb:4 * Bb + B] = pos % bs
-        grid = hv[5 * Bb:].reshape(Bb, Wb)
-        grid[:, 0] = self._pad_block
-        for b, t in enumerate(tables):
-            grid[b, :len(t)] = t
-        hv[3 * Bb:3 * Bb + B] = grid[np.arange(B), pos // bs]
+        self.stage_graph_inputs(host.numpy(), [s.tokens[-1] for s in seqs], [s.position for s in seqs], tables,
+                                Bb, Wb, self._pad_block, bs)
         gr["buf"].copy_(host, non_blocking=True)
         with self.tracer.span("decode", batch=B, graph=1):
             gr["graph"].replay()

@@ -157,3 +157,21 @@ def test_rollouts_through_paged_engine_match_generate():
         for a, b in zip(ga, gb):
             assert a.response_ids.tolist() == b.response_ids.tolist()
             torch.testing.assert_close(a.old_logprobs, b.old_logprobs)
+
+
+def test_graph_decode_staging_layout():
+    """The host staging of a CUDA-graph decode step (checked on the host; the graphs themselves need CUDA)."""
+    import numpy as np
+
+    from rl_project_b200.inference.engine import InferenceEngine
+
+    assert [InferenceEngine._pow2(n, 64) for n in (1, 2, 3, 5, 64, 70)] == [1, 2, 4, 8, 64, 70]
+    Bb, Wb, pad, bs = 4, 4, 99, 16
+    hv = np.full(5 * Bb + Bb * Wb, -7, dtype=np.int32)
+    InferenceEngine.stage_graph_inputs(hv, [11, 12], [5, 17], [[3], [4, 8]], Bb, Wb, pad, bs)
+    tok, pos, ctx, sblk, soff = (hv[i * Bb:(i + 1) * Bb].tolist() for i in range(5))
+    tables = hv[5 * Bb:].reshape(Bb, Wb).tolist()
+    assert tok == [11, 12, 0, 0] and pos == [5, 17, 0, 0] and ctx == [6, 18, 1, 1]
+    assert sblk == [3, 8, pad, pad]  # block holding each new token: position // 16 of the table
+    assert soff == [5, 1, 0, 0]
+    assert tables == [[3, 0, 0, 0], [4, 8, 0, 0], [pad, 0, 0, 0], [pad, 0, 0, 0]]
