@@ -93,3 +93,23 @@ def test_moe_sort_dispatch_matches_mask_loop():
             if sel.any():
                 ref[sel] += w[sel, k:k + 1] * layer.experts[e](xf[sel])
     assert torch.allclose(y.reshape(-1, spec.n_embd), ref, atol=1e-5)
+
+
+def test_fmha_wrapper_shapes_and_layout():
+    """Host-side checks of the tcgen05 attention wrapper (the kernels themselves need a GPU)."""
+    from rl_project_b200.core.errors import KernelError
+    from rl_project_b200.ops.attention import FMHA_SHAPES, _token_major, fmha_forward
+
+    assert (128, 128) in FMHA_SHAPES and (192, 128) in FMHA_SHAPES and (96, 96) not in FMHA_SHAPES
+    x = torch.randn(2, 5, 3, 8)                 # token-major storage [B, T, H, D]
+    v = x.transpose(1, 2)                        # the [B, H, T, D] view attention receives
+    assert _token_major(v).data_ptr() == x.data_ptr()  # no copy for token-major views
+    heads_major = torch.randn(2, 3, 5, 8)
+    assert _token_major(heads_major).is_contiguous() and torch.equal(_token_major(heads_major),
+                                                                     heads_major.transpose(1, 2))
+    q = torch.zeros(1, 2, 4, 96, dtype=torch.bfloat16)
+    with pytest.raises(KernelError):
+        fmha_forward(q, q, q)
+    with pytest.raises(KernelError):  # 3 query heads do not group over 2 key/value heads
+        fmha_forward(torch.zeros(1, 3, 4, 64, dtype=torch.bfloat16), torch.zeros(1, 2, 4, 64, dtype=torch.bfloat16),
+                     torch.zeros(1, 2, 4, 64, dtype=torch.bfloat16))
