@@ -272,3 +272,19 @@ def test_trainer_logs_perf_metrics(make_ctx, cspec, corpus_dir):
     n = sum(p.numel() for p in model.parameters())
     r = perf[-1]
     assert r["perf/model_tflops"] == pytest.approx(6 * n * r["perf/tokens_per_s"] / 1e12, rel=1e-6)
+
+
+def test_tokens_in_reads_batch_shapes():
+    from types import SimpleNamespace
+
+    from rl_project_b200.core.protocols import Trajectory
+    from rl_project_b200.training.common.trainer import PostTrainingAlgorithm
+
+    tokens_in = PostTrainingAlgorithm.tokens_in
+    assert tokens_in(None, torch.zeros(3, 7)) == 21
+    assert tokens_in(None, (torch.zeros(2, 5), torch.zeros(2, 5))) == 10
+    assert tokens_in(None, {"input_ids": torch.zeros(4, 4)}) == 16
+    t = Trajectory(prompt_ids=torch.zeros(6, dtype=torch.long), response_ids=torch.zeros(3, dtype=torch.long))
+    groups = [SimpleNamespace(trajectories=[t, t]), SimpleNamespace(trajectories=[t])]
+    assert tokens_in(None, groups) == 3 * 9
+    assert tokens_in(None, "opaque") == 0
