@@ -367,6 +367,11 @@ class Trainer:
                                                 float(os.environ.get("RLB_PEAK_TFLOPS", "0") or 0.0)))
                     t_log, self._tokens = now, 0
                     self.ctx.metrics.log(payload, step=self.step)
+                    if self.ctx.device.type == "cuda":
+                        from rl_project_b200.ops._ext import available, check_bounds
+
+                        if available():
+                            check_bounds(self.ctx.device)  # an out-of-range index a kernel skipped fails here
                     self.log.info("step", step=self.step, loss=round(result.loss, 5),
                                   **{k: round(v, 5) for k, v in result.metrics.items() if isinstance(v, float)})
             if self.cfg.eval_every and (self._is_main() or self._sharded):
