@@ -357,15 +357,21 @@ class Trainer:
                         and self.step % self.cfg.checkpoint.save_every == 0):
                     self.save_checkpoint()
                 result = self.train_step()
-                if self.cfg.log_every and self.step % self.cfg.log_every == 0 and self._is_main():
+                log_step = bool(self.cfg.log_every) and self.step % self.cfg.log_every == 0
+                if log_step:  # on every rank: the interval, its max over ranks (collective), the token count
+                    now = time.time()
+                    elapsed, tokens = now - t_log, self._tokens
+                    slowest = self._slowest_rank_seconds(elapsed)
+                    t_log, self._tokens = now, 0
+                if log_step and self._is_main():
                     payload = {"train/loss": result.loss, **{f"train/{k}": v for k, v in result.metrics.items()}}
                     payload.update(device_memory_metrics(self.ctx.device))
-                    now = time.time()
                     # this rank's throughput since the last log (the step ends with one host sync, so the
                     # wall clock covers the device work); the data-parallel total is world x this
-                    payload.update(perf_metrics(self._tokens, now - t_log, self._n_params,
+                    payload.update(perf_metrics(tokens, elapsed, self._n_params,
                                                 float(os.environ.get("RLB_PEAK_TFLOPS", "0") or 0.0)))
-                    t_log, self._tokens = now, 0
+                    if slowest is not None:
+                        payload["perf/seconds_since_log_max_over_ranks"] = slowest
                     self.ctx.metrics.log(payload, step=self.step)
                     if self.ctx.device.type == "cuda":
                         from rl_project_b200.ops._ext import available, check_bounds
@@ -387,6 +393,19 @@ class Trainer:
                    "best_metric": None if math.isinf(self.best_metric) else self.best_metric, "eval": last_eval}
         self.ctx.metrics.event(Event.RUN_FINISHED.value, summary)
         return summary
+
+    def _slowest_rank_seconds(self, seconds: float) -> Optional[float]:
+        """Max over ranks of this rank's time since the last log (a collective; None when single-process)."""
+        if self.strategy is None or self.strategy.world_size() <= 1:
+            return None
+        import torch.distributed as dist
+
+        if not dist.is_initialized():
+            return None
+        dev = self.ctx.device if dist.get_backend() == "nccl" else torch.device("cpu")
+        t = torch.tensor([float(seconds)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     def _is_main(self) -> bool:
         return self.strategy is None or self.strategy.is_main_process()

@@ -33,7 +33,7 @@ def _manifest(alg: str, out: str, steps: int, strategy: str = "ddp", **extra):
         "name": alg, "algorithm": alg, "model_preset": "tiny", "model": {"vocab_size": 256, "block_size": 64},
         "data": data,
         "trainer": {"device": "cpu", "precision": {"dtype": "float32"}, "max_steps": steps, "batch_size": 4,
-                    "eval_every": 0, "log_every": 0, "seed": 3,
+                    "eval_every": 0, "log_every": 1, "seed": 3,
                     "optimizer": {"learning_rate": extra.pop("lr", 3e-3), "grad_clip": 1.0},
                     "schedule": {"name": "constant", "warmup_steps": 0},
                     "checkpoint": {"save_every": extra.pop("save_every", 0), "directory": "ckpt", "keep_last": 5}},
