@@ -132,3 +132,6 @@ extern "C" int rlb_rmsnorm_bwd_noalloc(const void* h, const void* w, const float
                                        const void* dres, void* dx, void* dw_out, int dw_is_f32, long long rows,
                                        int dim, cudaStream_t stream);
 extern "C" long long rlb_rmsnorm_bwd_noalloc_scratch_bytes();
+// Per-device setup of the above for the current device, done ahead of time (a caller that will run the
+// backward from an out-of-memory path calls it while memory is still free).  Returns a cudaError_t value.
+extern "C" int rlb_rmsnorm_bwd_noalloc_init();

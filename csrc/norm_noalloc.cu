@@ -25,7 +25,12 @@
 // array's device address with cudaGetSymbolAddress, which may load this
 // library's device code onto the device, and reads the SM count; both are
 // cached per device.  Make that first call before any stream capture that will
-// contain later calls.
+// contain later calls.  Under lazy module loading (the CUDA default) that
+// lookup is also the moment the 4 MiB array gets its device memory, so it can
+// fail with cudaErrorMemoryAllocation when the device is full.  A caller that
+// will run the backward from an out-of-memory path must therefore do the setup
+// beforehand, while memory is still free: call rlb_rmsnorm_bwd_noalloc_init()
+// once per device (with that device current), or make one ordinary call.
 //
 // Concurrency: every call on a device shares that device's single scratch
 // array.  Calls issued on one stream run in order and are safe; calls that
@@ -95,6 +100,19 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 }  // namespace
 
 extern "C" long long rlb_rmsnorm_bwd_noalloc_scratch_bytes() { return kScratchFloats * (long long)sizeof(float); }
+
+// Runs the per-device setup for the current device now (address lookup, which
+// brings the scratch array into device memory, and the SM count) and returns
+// its cudaError_t value.  Idempotent; later calls on the device return at once.
+extern "C" int rlb_rmsnorm_bwd_noalloc_init() {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  float* scratch = nullptr;
+  int sms = 0;
+  return device_scratch(dev, &scratch, &sms);
+}
 
 extern "C" int rlb_rmsnorm_bwd_noalloc(const void* h, const void* w, const float* rstd, const void* dy,
                                        const void* dres, void* dx, void* dw_out, int dw_is_f32, long long rows,

@@ -96,12 +96,22 @@ def debug_checks() -> bool:
     return os.environ.get("RLB_DEBUG_BOUNDS", "0") == "1"
 
 
-def check_bounds(device: torch.device, clear: bool = True) -> None:
-    """Raise ``KernelError`` if a kernel on ``device`` reported an out-of-range index into the shared
-    index-error word (RoPE positions outside the cos / sin table).  Synchronises with the device."""
+def bounds_code(device: torch.device, clear: bool = True) -> int:
+    """The shared index-error word of ``device`` (0: no kernel skipped an out-of-range index).
+    Synchronises with the device; ``clear`` resets the word after reading it."""
+    return int(native().bounds_status(int(torch.device(device).index or 0), clear))
+
+
+def raise_bounds_error(code: int) -> None:
+    """Raise the ``KernelError`` that a non-zero index-error word stands for (no-op for 0)."""
     from rl_project_b200.core.errors import KernelError
 
-    code = int(native().bounds_status(int(torch.device(device).index or 0), clear))
     if code:
         raise KernelError(f"a kernel reported an out-of-range index (status {code})",
                           hint="A position, token or block id exceeded its table; the affected rows were skipped.")
+
+
+def check_bounds(device: torch.device, clear: bool = True) -> None:
+    """Raise ``KernelError`` if a kernel on ``device`` reported an out-of-range index into the shared
+    index-error word (RoPE positions outside the cos / sin table).  Synchronises with the device."""
+    raise_bounds_error(bounds_code(device, clear))

@@ -26,7 +26,7 @@ import os
 import time
 from abc import ABC, abstractmethod
 from dataclasses import dataclass, field
-from typing import Any, Dict, Iterable, List, Mapping, Optional
+from typing import Any, Dict, Iterable, List, Mapping, Optional, Tuple
 
 import torch
 import torch.nn as nn
@@ -361,8 +361,15 @@ class Trainer:
                 if log_step:  # on every rank: the interval, its max over ranks (collective), the token count
                     now = time.time()
                     elapsed, tokens = now - t_log, self._tokens
-                    slowest = self._slowest_rank_seconds(elapsed)
+                    # every rank reads its own index-error word; the code rides the same MAX all-reduce as
+                    # the interval, so an out-of-range index skipped on any rank fails all ranks together
+                    code = self._bounds_code()
+                    slowest, code = self._slowest_rank_seconds(elapsed, code)
                     t_log, self._tokens = now, 0
+                    if code:
+                        from rl_project_b200.ops._ext import raise_bounds_error
+
+                        raise_bounds_error(code)
                 if log_step and self._is_main():
                     payload = {"train/loss": result.loss, **{f"train/{k}": v for k, v in result.metrics.items()}}
                     payload.update(device_memory_metrics(self.ctx.device))
@@ -373,11 +380,6 @@ class Trainer:
                     if slowest is not None:
                         payload["perf/seconds_since_log_max_over_ranks"] = slowest
                     self.ctx.metrics.log(payload, step=self.step)
-                    if self.ctx.device.type == "cuda":
-                        from rl_project_b200.ops._ext import available, check_bounds
-
-                        if available():
-                            check_bounds(self.ctx.device)  # an out-of-range index a kernel skipped fails here
                     self.log.info("step", step=self.step, loss=round(result.loss, 5),
                                   **{k: round(v, 5) for k, v in result.metrics.items() if isinstance(v, float)})
             if self.cfg.eval_every and (self._is_main() or self._sharded):
@@ -394,18 +396,28 @@ class Trainer:
         self.ctx.metrics.event(Event.RUN_FINISHED.value, summary)
         return summary
 
-    def _slowest_rank_seconds(self, seconds: float) -> Optional[float]:
-        """Max over ranks of this rank's time since the last log (a collective; None when single-process)."""
+    def _bounds_code(self) -> int:
+        """This rank's index-error word (read and cleared; 0 off CUDA or without the extension)."""
+        if self.ctx.device.type != "cuda":
+            return 0
+        from rl_project_b200.ops._ext import available, bounds_code
+
+        return bounds_code(self.ctx.device) if available() else 0
+
+    def _slowest_rank_seconds(self, seconds: float, code: int = 0) -> Tuple[Optional[float], int]:
+        """Max over ranks of (this rank's time since the last log, its index-error code): one collective
+        every rank makes at log steps.  Single-process: ``(None, code)``."""
         if self.strategy is None or self.strategy.world_size() <= 1:
-            return None
+            return None, code
         import torch.distributed as dist
 
         if not dist.is_initialized():
-            return None
+            return None, code
         dev = self.ctx.device if dist.get_backend() == "nccl" else torch.device("cpu")
-        t = torch.tensor([float(seconds)], dtype=torch.float64, device=dev)
+        t = torch.tensor([float(seconds), float(code)], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        vals = t.tolist()
+        return float(vals[0]), int(vals[1])
 
     def _is_main(self) -> bool:
         return self.strategy is None or self.strategy.is_main_process()

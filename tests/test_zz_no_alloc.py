@@ -24,6 +24,7 @@ def _lib():
     fn.restype = ctypes.c_int
     fn.argtypes = [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_longlong, ctypes.c_int, ctypes.c_void_p]
     lib.rlb_rmsnorm_bwd_noalloc_scratch_bytes.restype = ctypes.c_longlong
+    lib.rlb_rmsnorm_bwd_noalloc_init.restype = ctypes.c_int
     return mod, lib
 
 
@@ -53,9 +54,11 @@ def _inputs(rows, dim, seed):
     (4096, 2048, torch.bfloat16, True),
     (3001, 4096, torch.float32, False),
     (1, 256, torch.bfloat16, False),
+    (20000, 8192, torch.float32, True),  # the scratch cap binds: 128 partial rows, each block strides over many rows
 ])
 def test_noalloc_matches_regular_entry_point(rows, dim, dw_dtype, with_res):
     mod, lib = _lib()
+    assert lib.rlb_rmsnorm_bwd_noalloc_init() == 0  # setup ahead of the first call (idempotent)
     assert lib.rlb_rmsnorm_bwd_noalloc_scratch_bytes() == 4 << 20
     for seed in (0, 1):  # two calls in a row; the second reuses the first call's scratch
         h, w, rstd, dy, dres = _inputs(rows, dim, seed)
@@ -78,3 +81,17 @@ def test_noalloc_rejects_dims_beyond_limit():
         rstd = torch.empty(2, device="cuda")
         rc = _call(lib, h, w, rstd, h, None, torch.empty_like(h), torch.empty_like(w))
         assert rc == 1  # cudaErrorInvalidValue, nothing launched
+
+
+@pytest.mark.parametrize("dw_dtype", [torch.bfloat16, torch.float32])
+def test_noalloc_zero_rows_gives_zero_dw(dw_dtype):
+    _, lib = _lib()
+    dim = 1024
+    h = torch.empty(0, dim, device="cuda", dtype=torch.bfloat16)
+    w = torch.ones(dim, device="cuda", dtype=torch.bfloat16)
+    rstd = torch.empty(0, device="cuda")
+    dw = torch.full((dim,), 7.0, device="cuda", dtype=dw_dtype)  # stale values must be overwritten
+    # a pointer of a zero-size tensor may be null, which the alignment check accepts (nothing is read)
+    assert _call(lib, h, w, rstd, h, None, torch.empty_like(h), dw) == 0
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(dw).item() == 0
