@@ -62,6 +62,8 @@ def parse_args():
                     help="CTAs of each fused reduce-scatter that overlaps backward")
     ap.add_argument("--fused-multicast", choices=["off", "on", "symm"], default="off",
                     help="fused reduce-scatter transport: CUDA IPC peer loads (off) or NVLink multicast (on)")
+    ap.add_argument("--gemm", choices=["tcgen05", "cublas"], default="tcgen05",
+                    help="dense linear layers and LM head: this library's 2-SM tcgen05 GEMM or cuBLAS")
     ap.add_argument("--attn", choices=["sdpa", "tcgen05"], default="sdpa",
                     help="training / prefill attention: torch SDPA (cuDNN / flash) or this library's tcgen05 kernels")
     ap.add_argument("--decode-graphs", action="store_true",
@@ -71,12 +73,13 @@ def parse_args():
 
 def apply_kernel_choices(args) -> dict:
     """Route attention / decode as the flags ask (before any model is built); returns the choices."""
-    from rl_project_b200.ops import attention
+    from rl_project_b200.ops import attention, gemm
 
     attention._ATTN = args.attn
+    gemm._MODE = args.gemm
     if args.decode_graphs:
         os.environ["RLB_DECODE_GRAPHS"] = "1"
-    return {"attention": args.attn, "decode_graphs": bool(args.decode_graphs)}
+    return {"attention": args.attn, "gemm": args.gemm, "decode_graphs": bool(args.decode_graphs)}
 
 
 # --------------------------------------------------------------------------- clocks
@@ -287,7 +290,7 @@ def run_ours(args, world, rank, local):
                    "model_tflops_per_gpu": flops_tok * args.seq * args.batch_per_gpu / (ms / 1e3) / 1e12,
                    "mfu_vs_measured_bf16": (flops_tok * args.seq * args.batch_per_gpu / (ms / 1e3) / 1e12 / peak)
                    if peak else None,
-                   "attention": args.attn,
+                   "attention": args.attn, "gemm": args.gemm,
                    "final_loss": last.loss, "first_loss": trainer.history[0].loss,
                    "final_grad_norm": last.metrics.get("grad_norm"),
                    "grad_reduce": ("fused peer-memory reduce-scatter" + (" (NVLink multicast)"
@@ -398,7 +401,7 @@ def run_pretrain_workload(args, world, rank, local):
                           "seq_len": seq, "parallelism": layout, "micro_batches": micro,
                           "params_full_model": n_params_full, "workload": args.workload,
                           "l2": "inputs larger than L2", "final_loss": trainer.history[-1].loss,
-                          "attention": args.attn,
+                          "attention": args.attn, "gemm": args.gemm,
                           "tp_allreduce": (("fused tcgen05 GEMM epilogue over peer memory"
                                             if tp_fused_used() else "nccl") if args.workload == "mesh8b"
                                            and world > 1 and tp > 1 else None)},

@@ -415,6 +415,26 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t a_m
            "gemm");
 }
 
+// The same product on the 2-SM kernel (256 x 256 nsub tiles per CTA pair, TMA-store epilogue); max_ctas > 0
+// caps its persistent grid (0: as many CTA pairs as fit on the device).
+void gemm2(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t a_mn, int64_t b_mn, int64_t epi,
+           int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, double alpha,
+           const c10::optional<at::Tensor>& status, int64_t max_ctas, int64_t nsub) {
+  check_bf16(A, "A");
+  check_bf16(B, "B");
+  check_dev(B, A, "B");
+  check_dev(out, A, "out");
+  check_dev(status, A, "status");
+  check_cuda(out, "out");
+  TORCH_CHECK((epi == 0 && out.scalar_type() == at::kBFloat16) || (epi != 0 && out.scalar_type() == at::kFloat),
+              "gemm2 output dtype does not match the epilogue");
+  const c10::cuda::CUDAGuard g(A.device());
+  CHECK_OK(rlb_gemm2sm((int)a_mn, (int)b_mn, (int)epi, (int)nsub, (int)M, (int)N, (int)K, A.data_ptr(), lda, B.data_ptr(), ldb,
+                       out.data_ptr(), ldc, (float)alpha, status.has_value() ? status->data_ptr<int>() : nullptr,
+                       (int)max_ctas, cur_stream()),
+           "gemm2");
+}
+
 // Grouped GEMM (mixture-of-experts): see rlb_gemm_grouped for the two modes.
 void gemm_grouped(int64_t mode, int64_t b_mn, int64_t epi, const at::Tensor& A, const at::Tensor& B, at::Tensor& out,
                   int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, double alpha,
@@ -826,6 +846,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nf4_dequant", &nf4_dequant);
   m.def("nf4_gemm", &nf4_gemm);
   m.def("gemm", &gemm);
+  m.def("gemm2", &gemm2);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("fmha_fwd", &fmha_fwd);

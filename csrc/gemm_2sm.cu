@@ -1,0 +1,553 @@
+// Persistent 2-SM tcgen05 GEMM for sm_100a:  C[M, N] = alpha * op(A) op(B)^T  (bf16 in, fp32 accumulate).
+//
+// This is the GEMM behind every dense linear layer of the models (the reference runs them through
+// F.linear: src/forgeline/models/transformer/feedforward.py:26, src/forgeline/models/attention/causal.py:81-83).
+//
+// Operand layouts (template flags, as in gemm_tcgen05.cu):
+//   A_MN = 0: A stored [M][K] (K contiguous)      A_MN = 1: A stored [K][M] (M contiguous)
+//   B_MN = 0: B stored [N][K] (K contiguous)      B_MN = 1: B stored [K][N] (N contiguous)
+// covering a linear layer's forward (x W^T: 0/0), input gradient (dy W: 0/1) and weight gradient
+// (dy^T x: 1/1) without transposes.
+//
+// Work unit: one 256 x (256 NSUB) tile of C per CTA pair (a 2-CTA cluster on one TPC).  Each CTA loads its
+// own 128 rows of A and, for each of the NSUB 256-column sub-tiles, its own 128 rows of B (N) for a 64-deep
+// K slice into its shared memory with plain TMA loads (no cluster-wide delivery).  The even CTA's elected
+// thread issues tcgen05.mma.cta_group::2 with M = 256, N = 256, K = 16, which reads both CTAs' halves and
+// writes 128 accumulator rows into each CTA's TMEM.  With NSUB = 2 one A slice feeds two MMAs (a 256 x 512
+// tile), which cuts the operand bytes per FLOP by a quarter against 256 x 256 tiles; the accumulator then
+// fills all 512 TMEM columns, so instead of double-buffering it the epilogue reads it out into registers
+// and hands it back before converting and storing.
+//
+// Roles (one CTA per SM, persistent over tiles):
+//   warp 0        TMA producer (both CTAs): a ring of 32 / 48 KB stages.  Completion of a stage is
+//                 counted on the even CTA's `full` barrier (the even CTA arms it with both CTAs' bytes).
+//   warp 1        TMEM owner (512 columns, allocated as a pair); in the even CTA one elected thread issues
+//                 the MMAs and commits stage releases and finished accumulators to the barriers of both CTAs.
+//   warps 2..     epilogue (both CTAs), 4 NSUB warps: warp w reads TMEM lane quarter w % 4 of one 256-column
+//                 sub-tile.  bf16 output: tcgen05.ld all 256 columns, scale by alpha, pack to bf16 in
+//                 registers, hand the accumulator back (to the even CTA's `tempty` barrier), then write
+//                 128-B swizzled 32-row staging tiles and TMA-store them.  fp32 output: chunk by chunk
+//                 through the staging tile, stored or accumulated into C with a TMA reduce-add.
+// Every mbarrier wait is bounded; on timeout the kernel records an error in `status`, tells the peer
+// CTA to stop, drains its own MMAs and stores, frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "sm100.cuh"
+
+namespace gemm2 {
+
+constexpr int BM = 256, SUBN = 256;  // C rows per CTA pair; columns per MMA / per accumulator sub-tile
+constexpr int HM = 128, HN = 128;    // rows of A / of B (per sub-tile) each CTA holds
+constexpr int BK = 64, UMMA_K = 16;
+constexpr int A_BYTES = HM * BK * 2, B_SUB_BYTES = HN * BK * 2;
+constexpr int EPI_TILE = 32 * 128;  // one warp's staging tile: 32 rows x 128 B
+constexpr int TMEM_COLS = 512;
+constexpr int GROUP_M = 8;
+constexpr uint32_t WAIT_LIMIT = 1u << 26;  // polls before a wait is declared dead (seconds)
+constexpr int BAR_BYTES = 256;
+
+// Per-NSUB configuration: tile width, ring depth, accumulator buffers, epilogue warps, shared memory.
+template <int NSUB>
+struct Cfg {
+  static constexpr int BN = SUBN * NSUB;
+  static constexpr int B_BYTES = B_SUB_BYTES * NSUB;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = NSUB == 1 ? 6 : 4;
+  static constexpr int ACCS = NSUB == 1 ? 2 : 1;  // accumulator buffers (each BN TMEM columns)
+  static constexpr int EPI_WARPS = 4 * NSUB;
+  static constexpr int EPI_BUFS = NSUB == 1 ? 2 : 1;  // staging tiles per epilogue warp
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_TILE;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES + 1024;
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget of one sm_100a CTA");
+  static_assert(ACCS * BN <= TMEM_COLS, "accumulators fit in TMEM");
+};
+
+enum Epi : int { kStoreBF16 = 0, kStoreF32 = 1, kAccumF32 = 2 };
+
+struct Params {
+  int M, N, K;
+  float alpha;
+  int* status;
+  float* c32;     // kAccumF32: C itself, for the ragged edge chunks the threads accumulate directly
+  long long ldc;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m, int& n) {
+  const int per_group = GROUP_M * num_n;
+  const int g = t / per_group;
+  const int first_m = g * GROUP_M;
+  const int gsize = min(num_m - first_m, GROUP_M);
+  const int r = t % per_group;
+  m = first_m + r % gsize;
+  n = r / gsize;
+}
+
+struct Ctl {
+  volatile int* abort_flag;  // this CTA's stop flag
+  uint32_t peer_abort;       // the peer CTA's stop flag (shared::cluster address)
+  int* status;
+};
+
+__device__ __forceinline__ void fail(const Ctl& c, int where) {
+  *c.abort_flag = 1;
+  sm100::st_cluster_u32(c.peer_abort, 1u);
+  if (c.status) atomicCAS(c.status, 0, 1 | (where << 8));
+}
+
+__device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity) {
+  return sm100::mbar_wait_bounded(bar, parity, WAIT_LIMIT);
+}
+
+// fp32 pair -> packed bf16x2
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int A_MN, int B_MN, int EPI, int NSUB>
+__global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __grid_constant__ CUtensorMap tma_a,
+                                                                        const __grid_constant__ CUtensorMap tma_b,
+                                                                        const __grid_constant__ CUtensorMap tma_c,
+                                                                        Params p) {
+  using C = Cfg<NSUB>;
+  constexpr int BN = C::BN, STAGES = C::STAGES, ACCS = C::ACCS;
+  extern __shared__ uint8_t smem_raw[];
+  // identical offsets in both CTAs: the pair MMA addresses the peer's operands at this CTA's offsets
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint8_t* sE = smem + STAGES * C::STAGE_BYTES;
+  uint64_t* full = (uint64_t*)(sE + C::EPI_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const uint32_t rank = sm100::cluster_ctarank();  // 0: the CTA that issues the pair MMAs
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int nk = (p.K + BK - 1) / BK;
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const Ctl ctl{abort_flag, sm100::mapa(sm100::smem_u32((const void*)abort_flag), rank ^ 1u), p.status};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      sm100::mbar_init(&tfull[b], 1);
+      sm100::mbar_init(&tempty[b], 2 * C::EPI_WARPS);  // every epilogue warp of both CTAs
+    }
+    sm100::mbar_init(drain, 1);
+    *abort_flag = 0;
+    sm100::fence_barrier_init();
+    sm100::prefetch_tensormap(&tma_a);
+    sm100::prefetch_tensormap(&tma_b);
+    sm100::prefetch_tensormap(&tma_c);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    sm100::tmem_relinquish_pair();
+  }
+  sm100::tc_fence_before();
+  sm100::cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA traffic
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      const uint32_t full0 = sm100::mapa(sm100::smem_u32(full), 0);
+      for (int t = cluster; t < num_tiles && !*abort_flag; t += nclusters) {
+        int tm, tn;
+        tile_coords(t, num_m, num_n, tm, tn);
+        const int m0 = tm * BM + (int)rank * HM;  // this CTA's rows of A
+        const int nb = tn * BN + (int)rank * HN;  // ... and of B in the first sub-tile
+        bool dead = false;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!wait(&empty[stage], phase ^ 1)) {
+            fail(ctl, 1);
+            dead = true;
+            break;
+          }
+          const int k0 = kb * BK;
+          if (!RLB_TMA_X_OK(A_MN ? m0 : k0) || !RLB_TMA_X_OK(B_MN ? nb : k0)) {
+            fail(ctl, 7);
+            dead = true;
+            break;
+          }
+          if (rank == 0) sm100::mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+          const uint32_t fb = full0 + (uint32_t)stage * 8u;
+          uint8_t* a = sA + stage * A_BYTES;
+          uint8_t* b = sB + stage * C::B_BYTES;
+          if (A_MN) {
+#pragma unroll
+            for (int h = 0; h < HM / 64; ++h) sm100::tma_load_2d_pair(a + h * (BK * 128), &tma_a, fb, m0 + 64 * h, k0);
+          } else {
+            sm100::tma_load_2d_pair(a, &tma_a, fb, k0, m0);
+          }
+#pragma unroll
+          for (int j = 0; j < NSUB; ++j) {
+            uint8_t* bj = b + j * B_SUB_BYTES;
+            const int n0 = nb + j * SUBN;
+            if (B_MN) {
+#pragma unroll
+              for (int h = 0; h < HN / 64; ++h) sm100::tma_load_2d_pair(bj + h * (BK * 128), &tma_b, fb, n0 + 64 * h, k0);
+            } else {
+              sm100::tma_load_2d_pair(bj, &tma_b, fb, k0, n0);
+            }
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (dead) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (even CTA)
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t idesc = sm100::idesc_bf16_f32(BM, SUBN, A_MN, B_MN);
+      const uint32_t empty0 = sm100::mapa(sm100::smem_u32(empty), 0), empty1 = sm100::mapa(sm100::smem_u32(empty), 1);
+      const uint32_t tfull0 = sm100::mapa(sm100::smem_u32(tfull), 0), tfull1 = sm100::mapa(sm100::smem_u32(tfull), 1);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = cluster; t < num_tiles && !*abort_flag; t += nclusters) {
+        if (!wait(&tempty[acc], acc_phase ^ 1)) {
+          fail(ctl, 2);
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        bool dead = false;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!wait(&full[stage], phase)) {
+            fail(ctl, 3);
+            dead = true;
+            break;
+          }
+          sm100::tc_fence_after();
+          const uint32_t a = sm100::smem_u32(sA + stage * A_BYTES);
+          const uint32_t b = sm100::smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            // K-major: +32 B per 16-element K step inside the 128-B swizzle row.
+            // MN-major: a 16-element K step spans two 8-row (1024-B) atoms; 64-wide M / N blocks 8 KB apart.
+            const uint64_t ad = A_MN ? sm100::desc_mnmajor_sw128(a + k * 2048, BK * 128)
+                                     : sm100::desc_kmajor_sw128(a + k * 32);
+#pragma unroll
+            for (int j = 0; j < NSUB; ++j) {
+              const uint32_t bj = b + j * B_SUB_BYTES;
+              const uint64_t bd = B_MN ? sm100::desc_mnmajor_sw128(bj + k * 2048, BK * 128)
+                                       : sm100::desc_kmajor_sw128(bj + k * 32);
+              sm100::mma_f16_pair(d + j * SUBN, ad, bd, idesc, (kb | k) != 0);
+            }
+          }
+          // the stage may be refilled in both CTAs once these MMAs have read it
+          sm100::mma_commit_pair(empty0 + (uint32_t)stage * 8u);
+          sm100::mma_commit_pair(empty1 + (uint32_t)stage * 8u);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (dead) break;
+        sm100::mma_commit_pair(tfull0 + (uint32_t)acc * 8u);
+        sm100::mma_commit_pair(tfull1 + (uint32_t)acc * 8u);
+        if (++acc == ACCS) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      // every MMA issued here completes before either CTA frees TMEM or shared memory
+      sm100::mma_commit_pair(sm100::mapa(sm100::smem_u32(drain), 0));
+      wait(drain, 0);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2.., both CTAs)
+    const int ew = warp - 2;
+    const int q = warp & 3;      // TMEM lane quarter this warp may access
+    const int sub = ew >> 2;     // 256-column sub-tile this warp converts
+    uint8_t* stage_tiles = sE + ew * C::EPI_BUFS * EPI_TILE;
+    const uint32_t tempty0 = sm100::mapa(sm100::smem_u32(tempty), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int ebuf = 0;
+    for (int t = cluster; t < num_tiles; t += nclusters) {
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+      int tm, tn;
+      tile_coords(t, num_m, num_n, tm, tn);
+      const int row0 = tm * BM + (int)rank * HM + q * 32;  // first C row of this warp's 32 rows
+      const int n0 = tn * BN + sub * SUBN;                  // first C column of this warp's sub-tile
+      if (!__all_sync(0xffffffffu, wait(&tfull[acc], acc_phase))) {
+        if (lane == 0) fail(ctl, 4);
+        break;
+      }
+      sm100::tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + sub * SUBN;
+      if constexpr (EPI == kStoreBF16 && NSUB == 2) {
+        // the only accumulator: read the whole 256-column sub-tile into registers (packed bf16), release it
+        // so the next tile's MMAs start, then store
+        uint32_t pk[SUBN / 2];
+#pragma unroll
+        for (int c = 0; c < SUBN / 16; ++c) {
+          uint32_t r[16];
+          sm100::tmem_ld16(tbase + c * 16, r);
+          sm100::tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            pk[c * 8 + e] = pack_bf16(__uint_as_float(r[2 * e]) * p.alpha, __uint_as_float(r[2 * e + 1]) * p.alpha);
+        }
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive_cluster(tempty0 + (uint32_t)acc * 8u);
+#pragma unroll
+        for (int c = 0; c < SUBN / 64; ++c) {
+          uint8_t* tile = stage_tiles + ebuf * EPI_TILE;
+          if (lane == 0) {
+            if (C::EPI_BUFS == 2) sm100::bulk_wait_read<1>();  // this staging tile's previous store has read it
+            else sm100::bulk_wait_read<0>();
+          }
+          __syncwarp();
+          // row `lane`: 8 chunks of 16 B; chunk j stored at j ^ (row % 8) (the TMA 128-B swizzle)
+          uint8_t* rowp = tile + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) =
+                make_uint4(pk[c * 32 + 4 * j], pk[c * 32 + 4 * j + 1], pk[c * 32 + 4 * j + 2], pk[c * 32 + 4 * j + 3]);
+          sm100::fence_async_shared();  // generic-proxy writes visible to the TMA engine
+          __syncwarp();
+          if (lane == 0 && row0 < p.M && n0 + c * 64 < p.N) {
+            sm100::tma_store_2d(&tma_c, tile, n0 + c * 64, row0);  // clipped at M and N by the tensor map
+            sm100::bulk_commit();
+          }
+          if (C::EPI_BUFS == 2) ebuf ^= 1;
+        }
+      } else {
+        // chunk by chunk through the staging tile (64 bf16 or 32 fp32 columns per 128-B row), the accumulator
+        // released after the last read (double-buffered accumulators hide this, or fp32 output)
+        constexpr int COLS = EPI == kStoreBF16 ? 64 : 32;
+#pragma unroll 1
+        for (int c = 0; c < SUBN / COLS; ++c) {
+          uint32_t r[COLS];
+          sm100::tmem_ld32(tbase + c * COLS, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+          if constexpr (COLS == 64) sm100::tmem_ld32(tbase + c * COLS + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+          sm100::tmem_ld_wait();
+          if (c == SUBN / COLS - 1) {
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive_cluster(tempty0 + (uint32_t)acc * 8u);
+          }
+          const int col0 = n0 + c * COLS;
+          if (EPI == kAccumF32 && (row0 + 32 > p.M || col0 + 32 > p.N)) {
+            // A reduce-add box that runs past C's edge lost updates on B200 (tested: columns past the inner
+            // extent), so a clipped chunk is accumulated by the threads: row `lane`, its columns below N.
+            const int row = row0 + lane;
+            if (row < p.M) {
+              float* dst = p.c32 + (long long)row * p.ldc + col0;
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                if (col0 + e < p.N) dst[e] += __uint_as_float(r[e]) * p.alpha;
+            }
+            continue;
+          }
+          uint8_t* tile = stage_tiles + ebuf * EPI_TILE;
+          if (lane == 0) {
+            if (C::EPI_BUFS == 2) sm100::bulk_wait_read<1>();
+            else sm100::bulk_wait_read<0>();
+          }
+          __syncwarp();
+          uint8_t* rowp = tile + lane * 128;  // chunk j of row `lane` stored at j ^ (row % 8)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 v;
+            if constexpr (COLS == 64) {
+              v = make_uint4(pack_bf16(__uint_as_float(r[8 * j + 0]) * p.alpha, __uint_as_float(r[8 * j + 1]) * p.alpha),
+                             pack_bf16(__uint_as_float(r[8 * j + 2]) * p.alpha, __uint_as_float(r[8 * j + 3]) * p.alpha),
+                             pack_bf16(__uint_as_float(r[8 * j + 4]) * p.alpha, __uint_as_float(r[8 * j + 5]) * p.alpha),
+                             pack_bf16(__uint_as_float(r[8 * j + 6]) * p.alpha, __uint_as_float(r[8 * j + 7]) * p.alpha));
+            } else {
+              v = make_uint4(__float_as_uint(__uint_as_float(r[4 * j]) * p.alpha),
+                             __float_as_uint(__uint_as_float(r[4 * j + 1]) * p.alpha),
+                             __float_as_uint(__uint_as_float(r[4 * j + 2]) * p.alpha),
+                             __float_as_uint(__uint_as_float(r[4 * j + 3]) * p.alpha));
+            }
+            *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) = v;
+          }
+          sm100::fence_async_shared();
+          __syncwarp();
+          if (lane == 0 && row0 < p.M && col0 < p.N) {
+            if (EPI == kAccumF32) sm100::tma_reduce_add_2d(&tma_c, tile, col0, row0);
+            else sm100::tma_store_2d(&tma_c, tile, col0, row0);
+            sm100::bulk_commit();
+          }
+          if (C::EPI_BUFS == 2) ebuf ^= 1;
+        }
+      }
+      if (++acc == ACCS) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    if (lane == 0) sm100::bulk_wait_all();  // stores complete before the staging memory goes away
+  }
+
+  __syncwarp();  // reconverge the single-lane roles before the warp-aligned cluster barrier
+  sm100::tc_fence_before();
+  sm100::cluster_sync();  // the peer's MMAs into this CTA's TMEM and reads of its shared memory are done
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)ptr;
+  }
+  return fn;
+}
+
+// 2-D tensor map over a row-major matrix [rows][cols] (cols contiguous, leading dimension `ld` elements),
+// box {box_cols, box_rows}, 128-B swizzle (box_cols * element size == 128 B).
+static bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* ptr, long long rows,
+                     long long cols, long long ld, int box_cols, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * esize)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Clusters of this kernel that can be resident at once on device `dev` (cached per instantiation and
+// device): the persistent grid must not exceed it, or late clusters would run their tiles after the others.
+template <int A_MN, int B_MN, int EPI, int NSUB>
+static int max_clusters(int dev) {
+  static int cache[64] = {0};
+  if (dev < 0 || dev >= 64) return 0;
+  if (cache[dev] > 0) return cache[dev];
+  auto kern = gemm2sm_kernel<A_MN, B_MN, EPI, NSUB>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(Cfg<NSUB>::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Cfg<NSUB>::SMEM_BYTES;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, (void*)kern, &cfg) != cudaSuccess || n <= 0) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  cache[dev] = n;
+  return n;
+}
+
+template <int A_MN, int B_MN, int EPI, int NSUB>
+static cudaError_t launch(const void* A, long long lda, const void* B, long long ldb, void* Cp, long long ldc,
+                          const Params& p, int max_ctas, cudaStream_t s) {
+  using C = Cfg<NSUB>;
+  CUtensorMap ma, mb, mc;
+  const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  // K-major operand: [rows][K], box 64 k x 128 rows.  MN-major: [K][rows], box 64 rows x 64 k.
+  const bool ok_a = A_MN ? make_map(&ma, bf, 2, A, p.K, p.M, lda, 64, BK) : make_map(&ma, bf, 2, A, p.M, p.K, lda, 64, HM);
+  const bool ok_b = B_MN ? make_map(&mb, bf, 2, B, p.K, p.N, ldb, 64, BK) : make_map(&mb, bf, 2, B, p.N, p.K, ldb, 64, HN);
+  const bool ok_c = EPI == kStoreBF16 ? make_map(&mc, bf, 2, Cp, p.M, p.N, ldc, 64, 32)
+                                      : make_map(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Cp, p.M, p.N, ldc, 32, 32);
+  if (!ok_a || !ok_b || !ok_c) return cudaErrorInvalidResourceHandle;  // tensor-map encoding rejected an operand
+  auto kern = gemm2sm_kernel<A_MN, B_MN, EPI, NSUB>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  int dev = 0;
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  int clusters = max_clusters<A_MN, B_MN, EPI, NSUB>(dev);
+  if (clusters <= 0) return cudaErrorNotSupported;
+  if (max_ctas > 0 && clusters > max_ctas / 2) clusters = max_ctas / 2 > 0 ? max_ctas / 2 : 1;
+  const int tiles = ((p.M + BM - 1) / BM) * ((p.N + C::BN - 1) / C::BN);
+  if (clusters > tiles) clusters = tiles;
+  (void)cudaGetLastError();  // drop a stale, non-sticky error left by unrelated calls on this thread
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cfg.blockDim = dim3(C::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, p);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+}  // namespace gemm2
+
+// C = alpha * op(A) op(B)^T on the 2-SM kernel.  a_mn / b_mn select the operand storage (see top of file);
+// epi: 0 = store bf16, 1 = store fp32, 2 = accumulate into fp32.  nsub: 1 = 256 x 256 tiles (double-buffered
+// accumulators), 2 = 256 x 512 tiles (one A slice per two MMAs).  Leading dimensions must be multiples of 8
+// elements (C: 16 bytes), base pointers 16-byte aligned.  max_ctas > 0 caps the grid (CTAs, even).
+cudaError_t rlb_gemm2sm(int a_mn, int b_mn, int epi, int nsub, int M, int N, int K, const void* A, long long lda,
+                        const void* B, long long ldb, void* C, long long ldc, float alpha, int* status, int max_ctas,
+                        cudaStream_t s) {
+  using namespace gemm2;
+  if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+  if ((lda % 8) || (ldb % 8) || ((ldc * (epi == kStoreBF16 ? 2 : 4)) % 16)) return cudaErrorInvalidPitchValue;
+  if ((((uintptr_t)A) | ((uintptr_t)B) | ((uintptr_t)C)) & 15) return cudaErrorInvalidDevicePointer;
+  if (nsub != 1 && nsub != 2) return cudaErrorInvalidValue;
+  Params p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.alpha = alpha;
+  p.status = status;
+  p.c32 = (float*)C;
+  p.ldc = ldc;
+#define RLB_GEMM2_CASE(AM, BMN, E)                                                                         \
+  if (a_mn == AM && b_mn == BMN && epi == E)                                                               \
+    return nsub == 1 ? launch<AM, BMN, E, 1>(A, lda, B, ldb, C, ldc, p, max_ctas, s)                       \
+                     : launch<AM, BMN, E, 2>(A, lda, B, ldb, C, ldc, p, max_ctas, s);
+  RLB_GEMM2_CASE(0, 0, 0)
+  RLB_GEMM2_CASE(0, 1, 0)
+  RLB_GEMM2_CASE(1, 1, 0)
+  RLB_GEMM2_CASE(1, 1, 1)
+  RLB_GEMM2_CASE(1, 1, 2)
+  RLB_GEMM2_CASE(0, 0, 1)
+  RLB_GEMM2_CASE(0, 0, 2)
+#undef RLB_GEMM2_CASE
+  return cudaErrorNotSupported;
+}

@@ -52,6 +52,12 @@ cudaError_t rlb_nf4_dequant(const void* packed, const float* absmax, const float
 cudaError_t rlb_gemm(int a_mn, int b_mn, int epi, int M, int N, int K, const void* A, long long lda, const void* B,
                      long long ldb, void* C, long long ldc, float alpha, int* status, int sms, cudaStream_t s);
 
+// 2-SM variant (CTA pairs, 256 x 256 nsub tiles, nsub 1 or 2): same operands and epilogues; max_ctas > 0
+// caps the grid.
+cudaError_t rlb_gemm2sm(int a_mn, int b_mn, int epi, int nsub, int M, int N, int K, const void* A, long long lda,
+                        const void* B, long long ldb, void* C, long long ldc, float alpha, int* status, int max_ctas,
+                        cudaStream_t s);
+
 cudaError_t rlb_gemm_grouped(int mode, int b_mn, int epi, int M, int N, int K, const void* A, long long lda,
                              const void* B, long long ldb, void* C, long long ldc, float alpha, int groups,
                              const int* tile_group, const int* k_begin, const int* k_len, long long k_total,

@@ -1,4 +1,4 @@
-"""tcgen05/TMEM GEMM (csrc/gemm_tcgen05.cu) and the linear layer built on it.
+"""tcgen05/TMEM GEMMs (csrc/gemm_2sm.cu, csrc/gemm_tcgen05.cu) and the linear layer built on them.
 
 One persistent warp-specialised kernel covers a linear layer's three GEMMs
 without transposing anything:
@@ -8,8 +8,12 @@ without transposing anything:
 * weight grad  ``dW = dy^T x``   A = dy read MN-major,      B = x read MN-major
 
 ``RLB_GEMM`` selects the implementation of the model's plain linear layers:
-``tcgen05`` (this kernel), ``cublas`` (torch.matmul) or ``auto`` (tcgen05
-once the numerics self-check on the first call passed).
+``tcgen05`` (this library's kernels), ``cublas`` (torch.matmul) or ``auto``
+(tcgen05 once the numerics self-check on the first call passed).
+``RLB_GEMM_KERNEL`` picks the kernel: ``2sm`` (default; CTA pairs issuing
+``tcgen05.mma.cta_group::2`` on 256 x 256 tiles, TMA-store epilogue) or
+``1sm`` (one CTA per 128 x 256 tile, register-to-global epilogue; the base of
+the grouped and all-reduce variants).
 """
 
 from __future__ import annotations
@@ -21,8 +25,45 @@ import torch
 
 from rl_project_b200.ops._ext import available, native
 
-_MODE = os.environ.get("RLB_GEMM", "cublas")
+_MODE = os.environ.get("RLB_GEMM", "tcgen05")
+_KERNEL = os.environ.get("RLB_GEMM_KERNEL", "2sm")
+_NSUB = int(os.environ.get("RLB_GEMM_NSUB", "0"))  # 0: per shape; 1: 256 x 256 tiles; 2: 256 x 512 tiles
 _checked: dict = {}
+
+
+_CLUSTERS: dict = {}
+
+
+def _pairs(device_index: int) -> int:
+    if device_index not in _CLUSTERS:
+        _CLUSTERS[device_index] = max(1, torch.cuda.get_device_properties(device_index).multi_processor_count // 2)
+    return _CLUSTERS[device_index]
+
+
+def nsub_for(M: int, N: int, epi: int, device_index: int = 0) -> int:
+    """Tile width of the 2-SM kernel for a product.  256 x 512 tiles (one A slice feeds two MMAs: a quarter
+    fewer operand bytes) unless the output is fp32, too narrow, or their last wave of CTA pairs would leave
+    clearly more of the GPU idle than 256 x 256 tiles (double-buffered accumulators) do."""
+    if _NSUB:
+        return _NSUB
+    if epi != 0 or N <= 256:
+        return 1
+    pairs = _pairs(device_index)
+
+    def wave_fill(bn: int) -> float:
+        tiles = -(-M // 256) * -(-N // bn)
+        waves = -(-tiles // pairs)
+        return tiles / (waves * pairs)
+
+    return 2 if wave_fill(512) + 0.05 >= wave_fill(256) else 1
+
+
+def _run(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha):
+    if _KERNEL == "1sm":
+        native().gemm(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None)
+    else:
+        native().gemm2(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None, 0,
+                       nsub_for(M, N, epi, a.device.index or 0))
 
 
 def _ok_ptr(t: torch.Tensor) -> bool:
@@ -37,7 +78,7 @@ def gemm_nt(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0, out: Optional[
     b = b.contiguous()
     if out is None:
         out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
-    native().gemm(a, b, out, 0, 0, 0, M, N, K, K, K, out.stride(0), alpha, None)
+    _run(a, b, out, 0, 0, 0, M, N, K, K, K, out.stride(0), alpha)
     return out
 
 
@@ -48,7 +89,7 @@ def gemm_nn(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0) -> torch.Tenso
     a = a.contiguous()
     b = b.contiguous()
     out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
-    native().gemm(a, b, out, 0, 1, 0, M, N, K, K, N, N, alpha, None)
+    _run(a, b, out, 0, 1, 0, M, N, K, K, N, N, alpha)
     return out
 
 
@@ -64,7 +105,7 @@ def gemm_tn(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0, out: Optional[
         epi = 0
     else:
         epi = 2 if accumulate else (1 if out.dtype == torch.float32 else 0)
-    native().gemm(a, b, out, 1, 1, epi, M, N, K, M, N, out.stride(0), alpha, None)
+    _run(a, b, out, 1, 1, epi, M, N, K, M, N, out.stride(0), alpha)
     return out
 
 

@@ -1,9 +1,9 @@
 """Dense GEMMs of the model.
 
-``matmul_nt(a, b) = a @ b^T`` is the one entry every linear layer goes
-through.  On sm_100a it runs the tcgen05 GEMM in csrc/gemm_tcgen05.cu when
-that kernel is enabled for the shape, otherwise cuBLAS (a plain library GEMM
-with no fused epilogue).
+``linear`` (every linear layer, with its backward) and ``matmul_nt`` /
+``matmul_nn`` / ``matmul_tn`` (the LM head's products) run this library's
+tcgen05 GEMM (csrc/gemm_2sm.cu) on sm_100a; ``RLB_GEMM=cublas`` routes them
+to cuBLAS instead (the library baseline, no fused epilogue).
 """
 
 from __future__ import annotations
@@ -12,16 +12,41 @@ import os
 
 import torch
 
-_USE_TCGEN05 = os.environ.get("RLB_GEMM", "auto")
+def _own(a: torch.Tensor, b: torch.Tensor) -> bool:
+    if not (a.is_cuda and a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16 and a.dim() == 2 and b.dim() == 2):
+        return False
+    from rl_project_b200.ops import gemm
+
+    return gemm.enabled() and all(x % 8 == 0 for x in (*a.shape, *b.shape)) and \
+        a.data_ptr() % 16 == 0 and b.data_ptr() % 16 == 0
 
 
 def matmul_nt(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    if a.is_cuda and _USE_TCGEN05 != "cublas":
+    """``a [M, K] @ b [N, K]^T``."""
+    if _own(a, b):
         from rl_project_b200.ops import gemm
 
         if gemm.supported(a, b):
             return gemm.gemm_nt(a, b)
     return a @ b.t()
+
+
+def matmul_nn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """``a [M, K] @ b [K, N]`` (b read as stored)."""
+    if _own(a, b):
+        from rl_project_b200.ops import gemm
+
+        return gemm.gemm_nn(a, b)
+    return a @ b
+
+
+def matmul_tn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """``a [K, M]^T @ b [K, N]`` (both read as stored)."""
+    if _own(a, b):
+        from rl_project_b200.ops import gemm
+
+        return gemm.gemm_tn(a, b)
+    return a.t() @ b
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:

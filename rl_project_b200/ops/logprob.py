@@ -26,6 +26,9 @@ KEEP_BUDGET_BYTES = int(float(os.environ.get("RLB_LOGITS_KEEP_GB", "24")) * (1 <
 CHUNK_ROWS = int(os.environ.get("RLB_LOGITS_CHUNK_ROWS", "16384"))
 
 
+from rl_project_b200.ops.linear import matmul_nn, matmul_tn  # noqa: E402
+
+
 def _gemm_nt(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """a [M, K] @ b[N, K]^T -> [M, N]."""
     from rl_project_b200.ops.linear import matmul_nt
@@ -80,8 +83,8 @@ class _LinearLogprob(torch.autograd.Function):
                                   g_lp[s:s + step] if g_lp is not None else None,
                                   ent[s:s + step] if ctx.with_entropy else None,
                                   g_ent[s:s + step] if g_ent is not None else None, 1.0)
-            dh[s:s + step] = logits @ W
-            part = logits.t() @ h[s:s + step]
+            dh[s:s + step] = matmul_nn(logits, W)
+            part = matmul_tn(logits, h[s:s + step])
             if N <= step:
                 dW16 = part
             else:

@@ -1,0 +1,95 @@
+"""The 2-SM tcgen05 GEMM (csrc/gemm_2sm.cu) against a plain fp32 PyTorch product of the same operands.
+
+Covers the three operand layouts a linear layer needs (x W^T, dy W, dy^T x), bf16 and fp32 outputs,
+accumulation into fp32 (TMA reduce-add), ragged M / N / K (tiles that run past the matrix), a strided
+output (ldc > N), alpha, and a grid capped below the device's cluster count (more tiles per pair).
+"""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+BF = torch.bfloat16
+
+
+def _rel(got, ref):
+    return ((got.float() - ref).norm() / ref.norm().clamp_min(1e-12)).item()
+
+
+def _status():
+    return torch.zeros(1, dtype=torch.int32, device="cuda")
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (512, 768, 256), (300, 200, 136), (1000, 1048, 520),
+                                   (4096, 3072, 2048)])
+@pytest.mark.parametrize("layout", ["nt", "nn", "tn"])
+@pytest.mark.parametrize("nsub", [1, 2])
+def test_gemm2sm_matches_fp32(M, N, K, layout, nsub):
+    from rl_project_b200.ops._ext import native
+
+    if layout == "tn" and M % 8:
+        pytest.skip("A stored [K][M] needs M a multiple of 8 (16-byte TMA row pitch)")
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
+    st = _status()
+    if layout == "nt":    # A [M][K], B [N][K]
+        a = torch.randn(M, K, device="cuda", generator=g).to(BF)
+        b = torch.randn(N, K, device="cuda", generator=g).to(BF)
+        ref = a.float() @ b.float().t()
+        args = (0, 0, K, K)
+    elif layout == "nn":  # A [M][K], B [K][N]
+        a = torch.randn(M, K, device="cuda", generator=g).to(BF)
+        b = torch.randn(K, N, device="cuda", generator=g).to(BF)
+        ref = a.float() @ b.float()
+        args = (0, 1, K, N)
+    else:                 # A [K][M], B [K][N]
+        a = torch.randn(K, M, device="cuda", generator=g).to(BF)
+        b = torch.randn(K, N, device="cuda", generator=g).to(BF)
+        ref = a.float().t() @ b.float()
+        args = (1, 1, M, N)
+    a_mn, b_mn, lda, ldb = args
+    out = torch.empty(M, N, device="cuda", dtype=BF)
+    native().gemm2(a, b, out, a_mn, b_mn, 0, M, N, K, lda, ldb, N, 1.0, st, 0, nsub)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    assert _rel(out, ref) < 8e-3
+    if layout != "nn":
+        # fp32 store, then accumulate the same product on top with alpha 0.5 (TMA reduce-add)
+        out32 = torch.empty(M, N, device="cuda", dtype=torch.float32)
+        native().gemm2(a, b, out32, a_mn, b_mn, 1, M, N, K, lda, ldb, N, 1.0, st, 0, nsub)
+        native().gemm2(a, b, out32, a_mn, b_mn, 2, M, N, K, lda, ldb, N, 0.5, st, 0, nsub)
+        torch.cuda.synchronize()
+        assert int(st.item()) == 0
+        assert _rel(out32, 1.5 * ref) < 1e-4
+
+
+@pytest.mark.parametrize("nsub", [1, 2])
+def test_gemm2sm_strided_output_and_small_grid(nsub):
+    """C written into columns [0, N) of a wider buffer; the grid capped at 4 CTAs (2 pairs)."""
+    from rl_project_b200.ops._ext import native
+
+    M, N, K, ldc = 1536, 640, 384, 1024
+    a = torch.randn(M, K, device="cuda").to(BF)
+    b = torch.randn(N, K, device="cuda").to(BF)
+    buf = torch.full((M, ldc), 3.0, device="cuda", dtype=BF)
+    st = _status()
+    native().gemm2(a, b, buf, 0, 0, 0, M, N, K, K, K, ldc, 2.0, st, 4, nsub)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    assert _rel(buf[:, :N], 2.0 * (a.float() @ b.float().t())) < 8e-3
+    assert bool((buf[:, N:] == 3.0).all())  # nothing written past N
+
+
+@pytest.mark.parametrize("nsub", [1, 2])
+def test_gemm2sm_agrees_with_one_sm_kernel(nsub):
+    """The two own kernels give the same product (fp32 accumulation, bf16 output) on the same operands."""
+    from rl_project_b200.ops._ext import native
+
+    for (M, N, K) in [(384, 512, 320), (2048, 2048, 1024)]:
+        a = torch.randn(M, K, device="cuda").to(BF)
+        b = torch.randn(N, K, device="cuda").to(BF)
+        o1 = torch.empty(M, N, device="cuda", dtype=BF)
+        o2 = torch.empty(M, N, device="cuda", dtype=BF)
+        native().gemm(a, b, o1, 0, 0, 0, M, N, K, K, K, N, 1.0, None)
+        native().gemm2(a, b, o2, 0, 0, 0, M, N, K, K, K, N, 1.0, None, 0, nsub)
+        torch.cuda.synchronize()
+        assert _rel(o2, o1.float()) < 4e-3
