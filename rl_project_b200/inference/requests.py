@@ -1,20 +1,24 @@
-"""Request objects of the inference engine.
+"""Requests of the inference engine: sampling parameters, a request's life cycle and its token stream.
 
-Field names, defaults, validation rules and the status life cycle follow
-``src/forgeline/inference/requests.py:15-80`` so serving code written against
-the reference keeps working: a request is PENDING until admitted, RUNNING
-while it decodes, then FINISHED / FAILED / CANCELLED; tokens are streamed
-through ``token_queue`` with a ``None`` sentinel at the end.
+The public fields (``SamplingParams`` knobs and their validation, ``GenerationRequest.prompt_tokens``,
+``params``, ``id``, ``status``, ``generated_tokens``, ``finish_reason``, ``error``, timestamps, ``meta``)
+are the interface serving code addresses (reference: ``src/forgeline/inference/requests.py:15-80``).
+
+Life cycle, enforced by a transition table: PENDING -> RUNNING when the scheduler admits the request,
+then exactly one terminal state (FINISHED, FAILED, CANCELLED); a waiting request may also go straight to a
+terminal state (rejected or cancelled before admission).  Tokens are streamed without a per-token queue:
+the engine appends to ``generated_tokens`` under a condition variable and readers keep a cursor into that
+list (``read_tokens``), so a reader that falls behind receives the backlog in one batch.
 """
 
 from __future__ import annotations
 
-import queue
+import threading
 import time
 import uuid
 from dataclasses import dataclass, field
 from enum import Enum
-from typing import List, Optional
+from typing import Iterator, List, Optional, Tuple
 
 from rl_project_b200.core.errors import ServingError
 
@@ -25,6 +29,17 @@ class RequestStatus(str, Enum):
     FINISHED = "finished"
     FAILED = "failed"
     CANCELLED = "cancelled"
+
+
+_TERMINAL = frozenset({RequestStatus.FINISHED, RequestStatus.FAILED, RequestStatus.CANCELLED})
+_ALLOWED = {
+    RequestStatus.PENDING: frozenset({RequestStatus.RUNNING}) | _TERMINAL,
+    RequestStatus.RUNNING: _TERMINAL,
+}
+
+
+def _in_range(value, lo, hi, lo_open=False) -> bool:
+    return (lo < value if lo_open else lo <= value) and value <= hi
 
 
 @dataclass
@@ -38,29 +53,36 @@ class SamplingParams:
     stop_token_ids: List[int] = field(default_factory=list)
 
     def validate(self) -> None:
+        problems = []
         if self.max_tokens < 1:
-            raise ServingError("max_tokens must be >= 1")
+            problems.append("max_tokens must be >= 1")
         if self.temperature < 0:
-            raise ServingError("temperature must be >= 0")
-        if self.top_p is not None and not 0 < self.top_p <= 1:
-            raise ServingError("top_p must be in (0, 1]")
+            problems.append("temperature must be >= 0")
         if self.top_k is not None and self.top_k < 0:
-            raise ServingError("top_k must be >= 0")
-        if self.min_p is not None and not 0 <= self.min_p <= 1:
-            raise ServingError("min_p must be in [0, 1]")
+            problems.append("top_k must be >= 0")
+        if self.top_p is not None and not _in_range(self.top_p, 0.0, 1.0, lo_open=True):
+            problems.append("top_p must be in (0, 1]")
+        if self.min_p is not None and not _in_range(self.min_p, 0.0, 1.0):
+            problems.append("min_p must be in [0, 1]")
         if self.repetition_penalty <= 0:
-            raise ServingError("repetition_penalty must be > 0")
+            problems.append("repetition_penalty must be > 0")
+        if problems:
+            raise ServingError("; ".join(problems))
 
     def filter_key(self) -> tuple:
         """Rows whose keys are equal can be filtered and sampled as one batch."""
         return (self.temperature, self.top_k, self.top_p, self.min_p)
 
 
-@dataclass
+def _new_id() -> str:
+    return uuid.uuid4().hex
+
+
+@dataclass(eq=False)
 class GenerationRequest:
     prompt_tokens: List[int]
     params: SamplingParams = field(default_factory=SamplingParams)
-    id: str = field(default_factory=lambda: uuid.uuid4().hex)
+    id: str = field(default_factory=_new_id)
     prompt: str = ""
     stream: bool = False
     created_at: float = field(default_factory=time.time)
@@ -70,37 +92,64 @@ class GenerationRequest:
     error: Optional[str] = None
     started_at: Optional[float] = None
     finished_at: Optional[float] = None
-    token_queue: "queue.Queue[Optional[int]]" = field(default_factory=queue.Queue)
     meta: dict = field(default_factory=dict)
+    _cv: threading.Condition = field(default_factory=threading.Condition, repr=False, compare=False)
 
+    # ------------------------------------------------------------ state
     @property
     def finished(self) -> bool:
-        return self.status in (RequestStatus.FINISHED, RequestStatus.FAILED, RequestStatus.CANCELLED)
+        return self.status in _TERMINAL
 
     @property
     def latency_s(self) -> Optional[float]:
         return None if self.finished_at is None else self.finished_at - self.created_at
 
+    def _move(self, to: RequestStatus) -> None:
+        if to not in _ALLOWED.get(self.status, frozenset()):
+            raise ServingError(f"request {self.id}: cannot go from {self.status.value} to {to.value}")
+        self.status = to
+
+    def start(self) -> None:
+        """PENDING -> RUNNING (the scheduler admitted the request)."""
+        with self._cv:
+            self._move(RequestStatus.RUNNING)
+            self.started_at = time.time()
+
     def push_token(self, token: int) -> None:
-        self.generated_tokens.append(token)
-        self.token_queue.put(token)
+        with self._cv:
+            self.generated_tokens.append(int(token))
+            self._cv.notify_all()
 
     def finish(self, reason: str, error: Optional[str] = None) -> None:
-        if error:
-            self.status = RequestStatus.FAILED
-        elif reason == "cancelled":
-            self.status = RequestStatus.CANCELLED
-        else:
-            self.status = RequestStatus.FINISHED
-        self.finish_reason = reason
-        self.error = error
-        self.finished_at = time.time()
-        self.token_queue.put(None)
+        """Enter the terminal state ``reason`` implies: FAILED with an error, CANCELLED for "cancelled",
+        FINISHED otherwise.  Wakes every reader."""
+        to = RequestStatus.FAILED if error else (
+            RequestStatus.CANCELLED if reason == "cancelled" else RequestStatus.FINISHED)
+        with self._cv:
+            self._move(to)
+            self.finish_reason, self.error, self.finished_at = reason, error, time.time()
+            self._cv.notify_all()
 
-    def stream_tokens(self, timeout: Optional[float] = None):
+    # ------------------------------------------------------------ streaming
+    def read_tokens(self, cursor: int, timeout: Optional[float] = None) -> Tuple[List[int], bool]:
+        """Tokens from index ``cursor`` on, waiting (up to ``timeout`` seconds) until there is at least one or
+        the request has finished.  Returns ``(tokens, done)``; ``done`` once the request is terminal and every
+        token has been handed out."""
+        with self._cv:
+            if len(self.generated_tokens) <= cursor and not self.finished:
+                self._cv.wait_for(lambda: len(self.generated_tokens) > cursor or self.finished, timeout)
+            new = self.generated_tokens[cursor:]
+            return list(new), self.finished and cursor + len(new) >= len(self.generated_tokens)
+
+    def has_unread(self, cursor: int) -> bool:
+        return len(self.generated_tokens) > cursor
+
+    def stream_tokens(self, timeout: Optional[float] = None) -> Iterator[int]:
         """Yield generated tokens as they arrive until the request finishes."""
-        while True:
-            tok = self.token_queue.get(timeout=timeout)
-            if tok is None:
-                return
-            yield tok
+        cursor, done = 0, False
+        while not done:
+            new, done = self.read_tokens(cursor, timeout)
+            if not new and not done:
+                raise TimeoutError(f"request {self.id}: no token within {timeout} s")
+            cursor += len(new)
+            yield from new

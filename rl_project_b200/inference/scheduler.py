@@ -1,82 +1,124 @@
-"""Continuous-batching scheduler: FIFO admission bounded by ``max_batch`` and
-the block allocator, retirement, cancellation.
+"""Admission control of the paged inference engine (continuous batching).
 
-Admission rules follow ``src/forgeline/inference/scheduler.py:14-75``: a request
-whose prompt plus ``max_tokens`` exceeds ``max_seq_len`` is rejected (finished
-with an error); the queue head waits while the allocator cannot hold its
-prompt plus one token; running requests are cancelled at their next token.
+Each ``admit()`` call forms the next prefill batch for the engine's step.  Requests wait in arrival order
+and the queue head is never overtaken, so a long prompt cannot be starved by short ones behind it.  The
+head is taken while
+
+* the running set has a free slot (``max_batch``),
+* the batch's prompt tokens stay within ``prefill_token_budget`` (one batched prefill sized so the
+  decode of the running set is not stalled for long; the first request of a batch is always allowed), and
+* the paged KV allocator can hold its prompt plus the first generated token.
+
+A request that can never fit (prompt plus ``max_tokens`` beyond ``max_seq_len``) fails at the head
+without blocking the rest.  Cancelling a waiting request finishes it at once; a running one is flagged
+and the engine retires it at its next token.  Behaviour matches the reference's scheduler
+(``src/forgeline/inference/scheduler.py:14-75``) where it defines one: FIFO, the length rejection, waiting
+for blocks, cancellation.
 """
 
 from __future__ import annotations
 
 import threading
-from collections import deque
-from typing import Deque, Dict, List, Optional
+from collections import Counter, OrderedDict
+from typing import Dict, List, Optional
 
 from rl_project_b200.inference.paged_memory import PagedBlockAllocator
-from rl_project_b200.inference.requests import GenerationRequest, RequestStatus
+from rl_project_b200.inference.requests import GenerationRequest
 
 
 class Scheduler:
-    def __init__(self, allocator: PagedBlockAllocator, max_batch: int = 8, max_seq_len: int = 512):
+    def __init__(self, allocator: PagedBlockAllocator, max_batch: int = 8, max_seq_len: int = 512,
+                 prefill_token_budget: Optional[int] = None):
         self.allocator = allocator
         self.max_batch = max_batch
         self.max_seq_len = max_seq_len
-        self.pending: Deque[GenerationRequest] = deque()
-        self.running: Dict[str, GenerationRequest] = {}
-        self.lock = threading.Lock()
-        self.completed = 0
-        self.rejected = 0
+        self.prefill_token_budget = prefill_token_budget
+        self._waiting: "OrderedDict[str, GenerationRequest]" = OrderedDict()
+        self._active: Dict[str, GenerationRequest] = {}
+        self._tally: Counter = Counter()
+        self._mu = threading.Lock()
 
+    # ------------------------------------------------------------ views
+    @property
+    def pending(self) -> List[GenerationRequest]:
+        with self._mu:
+            return list(self._waiting.values())
+
+    @property
+    def running(self) -> Dict[str, GenerationRequest]:
+        with self._mu:
+            return dict(self._active)
+
+    @property
+    def completed(self) -> int:
+        return self._tally["completed"]
+
+    @property
+    def rejected(self) -> int:
+        return self._tally["rejected"]
+
+    # ------------------------------------------------------------ queue
     def submit(self, req: GenerationRequest) -> None:
-        with self.lock:
-            self.pending.append(req)
+        with self._mu:
+            self._waiting[req.id] = req
+
+    def _never_fits(self, req: GenerationRequest) -> Optional[str]:
+        need = len(req.prompt_tokens) + req.params.max_tokens
+        if need > self.max_seq_len:
+            return f"prompt+max_tokens {need} exceeds max_seq_len {self.max_seq_len}"
+        return None
 
     def admit(self) -> List[GenerationRequest]:
-        admitted: List[GenerationRequest] = []
-        with self.lock:
-            while self.pending and len(self.running) < self.max_batch:
-                req = self.pending[0]
-                total = len(req.prompt_tokens) + req.params.max_tokens
-                if total > self.max_seq_len:
-                    self.pending.popleft()
-                    req.finish("length", error=f"prompt+max_tokens {total} exceeds max_seq_len {self.max_seq_len}")
-                    self.rejected += 1
+        batch: List[GenerationRequest] = []
+        prompt_tokens = 0
+        with self._mu:
+            while self._waiting and len(self._active) < self.max_batch:
+                rid, req = next(iter(self._waiting.items()))
+                why = self._never_fits(req)
+                if why is not None:
+                    del self._waiting[rid]
+                    self._tally["rejected"] += 1
+                    req.finish("length", error=why)
                     continue
-                if not self.allocator.can_allocate(req.id, len(req.prompt_tokens) + 1):
-                    break
-                self.pending.popleft()
-                self.allocator.allocate(req.id, len(req.prompt_tokens))
-                req.status = RequestStatus.RUNNING
-                self.running[req.id] = req
-                admitted.append(req)
-        return admitted
+                n = len(req.prompt_tokens)
+                if batch and self.prefill_token_budget is not None and prompt_tokens + n > self.prefill_token_budget:
+                    break  # the rest waits for the next step's prefill
+                if not self.allocator.can_allocate(rid, n + 1):
+                    break  # head of line waits until blocks are freed
+                del self._waiting[rid]
+                self.allocator.allocate(rid, n)
+                req.start()
+                self._active[rid] = req
+                batch.append(req)
+                prompt_tokens += n
+        return batch
 
     def retire(self, req: GenerationRequest, reason: str, error: Optional[str] = None) -> None:
-        with self.lock:
-            self.running.pop(req.id, None)
-            self.allocator.free(req.id)
-            req.finish(reason, error)
-            self.completed += 1
+        with self._mu:
+            if self._active.pop(req.id, None) is not None:
+                self.allocator.free(req.id)
+            self._tally["completed"] += 1
+        req.finish(reason, error)
 
     def cancel(self, request_id: str) -> bool:
-        with self.lock:
-            for i, r in enumerate(self.pending):
-                if r.id == request_id:
-                    del self.pending[i]
-                    r.finish("cancelled")
-                    return True
-            r = self.running.get(request_id)
-            if r is not None:
-                r.meta["cancel"] = True
+        with self._mu:
+            waiting = self._waiting.pop(request_id, None)
+            if waiting is None:
+                active = self._active.get(request_id)
+                if active is None:
+                    return False
+                active.meta["cancel"] = True  # the engine retires it at its next token
                 return True
-        return False
+        waiting.finish("cancelled")
+        return True
 
     def has_work(self) -> bool:
-        with self.lock:
-            return bool(self.pending or self.running)
+        with self._mu:
+            return bool(self._waiting) or bool(self._active)
 
     def stats(self) -> Dict[str, float]:
-        with self.lock:
-            return {"pending": len(self.pending), "running": len(self.running), "completed": self.completed,
-                    "rejected": self.rejected, **self.allocator.stats()}
+        with self._mu:
+            out = {"pending": len(self._waiting), "running": len(self._active),
+                   "completed": self._tally["completed"], "rejected": self._tally["rejected"]}
+        out.update(self.allocator.stats())
+        return out

@@ -93,14 +93,18 @@ class EngineBackend(_Toggle):
         return self.engine.submit(ids, params, **kwargs)
 
     def _tokens(self, req: GenerationRequest) -> Iterator[int]:
+        """The request's tokens as they are produced: a cursor into its token list, stepping the engine
+        from this thread when no background loop drives it."""
+        cursor = 0
         while True:
-            if not self._background and req.token_queue.empty() and not req.finished:
+            if not self._background and not req.finished and not req.has_unread(cursor):
                 self.engine.step()
                 continue
-            tok = req.token_queue.get()
-            if tok is None:
+            new, done = req.read_tokens(cursor, timeout=None if self._background else 0)
+            cursor += len(new)
+            yield from new
+            if done:
                 return
-            yield tok
 
     def complete(self, prompt: str, params: SamplingParams, request_id: Optional[str] = None,
                  stop: Sequence[str] = ()) -> CompletionResult:

@@ -7,7 +7,8 @@ import torch
 
 from rl_project_b200.core.config import model_spec_from_preset
 from rl_project_b200.core.errors import ServingError
-from rl_project_b200.inference import (InferenceEngine, OutOfBlocksError, PagedBlockAllocator, RequestStatus,
+from rl_project_b200.inference import (GenerationRequest, InferenceEngine, OutOfBlocksError, PagedBlockAllocator,
+                                       RequestStatus,
                                        SamplingParams, Scheduler)
 from rl_project_b200.models.transformer.model import TransformerLM
 
@@ -175,3 +176,39 @@ def test_graph_decode_staging_layout():
     assert sblk == [3, 8, pad, pad]  # block holding each new token: position // 16 of the table
     assert soff == [5, 1, 0, 0]
     assert tables == [[3, 0, 0, 0], [4, 8, 0, 0], [pad, 0, 0, 0], [pad, 0, 0, 0]]
+
+
+def test_scheduler_fifo_budget_rejection_and_cancel():
+    from rl_project_b200.core.errors import ServingError
+
+    alloc = PagedBlockAllocator(block_size=4, max_blocks=64)
+    s = Scheduler(alloc, max_batch=8, max_seq_len=64, prefill_token_budget=10)
+    mk = lambda n, mt=4: GenerationRequest(prompt_tokens=list(range(1, n + 1)), params=SamplingParams(max_tokens=mt))  # noqa: E731
+    a, b, too_long, c, d = mk(6), mk(6), mk(8, mt=100), mk(3), mk(2)
+    for r in (a, b, too_long, c, d):
+        s.submit(r)
+    first = s.admit()  # budget 10: a (6) fits, b would make 12 -> next step
+    assert [r.id for r in first] == [a.id] and a.status == RequestStatus.RUNNING
+    second = s.admit()  # b (6); the over-long request fails at the head; c (3) -> 9; d would make 11
+    assert [r.id for r in second] == [b.id, c.id]
+    assert too_long.status == RequestStatus.FAILED and "max_seq_len" in too_long.error
+    assert s.cancel(d.id) and d.status == RequestStatus.CANCELLED and not s.admit()
+    assert s.cancel(b.id) and b.meta["cancel"] and not s.cancel("nope")
+    s.retire(a, "stop")
+    assert a.status == RequestStatus.FINISHED and list(a.stream_tokens(timeout=1)) == []
+    with pytest.raises(ServingError):
+        a.start()  # a terminal request never runs again
+    st = s.stats()
+    assert st["running"] == 2 and st["pending"] == 0 and st["completed"] == 1 and st["rejected"] == 1
+
+
+def test_request_stream_reads_backlog_in_batches():
+    r = GenerationRequest(prompt_tokens=[1])
+    r.start()
+    for t in (5, 6, 7):
+        r.push_token(t)
+    toks, done = r.read_tokens(0, timeout=0)
+    assert toks == [5, 6, 7] and not done
+    r.finish("length")
+    assert r.read_tokens(3, timeout=0) == ([], True)
+    assert list(r.stream_tokens(timeout=1)) == [5, 6, 7]
