@@ -221,18 +221,52 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
       constexpr uint32_t idesc = sm100::idesc_bf16_f32(BM, SUBN, A_MN, B_MN);
       const uint32_t empty0 = sm100::mapa(sm100::smem_u32(empty), 0), empty1 = sm100::mapa(sm100::smem_u32(empty), 1);
       const uint32_t tfull0 = sm100::mapa(sm100::smem_u32(tfull), 0), tfull1 = sm100::mapa(sm100::smem_u32(tfull), 1);
+      // MMAs of one 64-deep K slice (stage `st`, K block `kb`) into accumulator sub-tile j
+      auto issue = [&](uint32_t d, int st, int kb, int j) {
+        const uint32_t a = sm100::smem_u32(sA + st * A_BYTES);
+        const uint32_t bj = sm100::smem_u32(sB + st * C::B_BYTES) + j * B_SUB_BYTES;
+#pragma unroll
+        for (int k = 0; k < BK / UMMA_K; ++k) {
+          // K-major: +32 B per 16-element K step inside the 128-B swizzle row.
+          // MN-major: a 16-element K step spans two 8-row (1024-B) atoms; 64-wide M / N blocks 8 KB apart.
+          const uint64_t ad = A_MN ? sm100::desc_mnmajor_sw128(a + k * 2048, BK * 128)
+                                   : sm100::desc_kmajor_sw128(a + k * 32);
+          const uint64_t bd = B_MN ? sm100::desc_mnmajor_sw128(bj + k * 2048, BK * 128)
+                                   : sm100::desc_kmajor_sw128(bj + k * 32);
+          sm100::mma_f16_pair(d + j * SUBN, ad, bd, idesc, (kb | k) != 0);
+        }
+      };
+      // the stage may be refilled in both CTAs once the MMAs issued so far have read it
+      auto release = [&](int st) {
+        sm100::mma_commit_pair(empty0 + (uint32_t)st * 8u);
+        sm100::mma_commit_pair(empty1 + (uint32_t)st * 8u);
+      };
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int t = cluster; t < num_tiles && !*abort_flag; t += nclusters) {
+        // NSUB == 2: one accumulator of two sub-tiles whose columns the epilogue hands back one after the
+        // other (tempty[0], tempty[1]).  The sub-tile 0 MMAs of this tile start as soon as sub-tile 0 is
+        // free; K slices whose sub-tile 1 MMAs must wait stay pending (their stages unreleased), at most a
+        // ring's worth, and are caught up in order once sub-tile 1 is free.
         if (!wait(&tempty[acc], acc_phase ^ 1)) {
           fail(ctl, 2);
           break;
         }
         sm100::tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
+        bool sub1_free = NSUB == 1;
+        int pend = 0, pend_kb = 0, pend_st = 0;  // pending K slices: count, first K block, its stage
         bool dead = false;
+        auto catch_up = [&]() {
+          for (int i = 0; i < pend; ++i) {
+            const int st = (pend_st + i) % STAGES;
+            issue(d, st, pend_kb + i, 1);
+            release(st);
+          }
+          pend = 0;
+        };
         for (int kb = 0; kb < nk; ++kb) {
           if (!wait(&full[stage], phase)) {
             fail(ctl, 3);
@@ -240,28 +274,49 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
             break;
           }
           sm100::tc_fence_after();
-          const uint32_t a = sm100::smem_u32(sA + stage * A_BYTES);
-          const uint32_t b = sm100::smem_u32(sB + stage * C::B_BYTES);
-#pragma unroll
-          for (int k = 0; k < BK / UMMA_K; ++k) {
-            // K-major: +32 B per 16-element K step inside the 128-B swizzle row.
-            // MN-major: a 16-element K step spans two 8-row (1024-B) atoms; 64-wide M / N blocks 8 KB apart.
-            const uint64_t ad = A_MN ? sm100::desc_mnmajor_sw128(a + k * 2048, BK * 128)
-                                     : sm100::desc_kmajor_sw128(a + k * 32);
-#pragma unroll
-            for (int j = 0; j < NSUB; ++j) {
-              const uint32_t bj = b + j * B_SUB_BYTES;
-              const uint64_t bd = B_MN ? sm100::desc_mnmajor_sw128(bj + k * 2048, BK * 128)
-                                       : sm100::desc_kmajor_sw128(bj + k * 32);
-              sm100::mma_f16_pair(d + j * SUBN, ad, bd, idesc, (kb | k) != 0);
+          issue(d, stage, kb, 0);
+          if constexpr (NSUB == 2) {
+            if (!sub1_free) {
+              bool now_free = sm100::mbar_test_wait(&tempty[1], acc_phase ^ 1);
+              if (!now_free && pend + 1 == STAGES) {  // every stage is held: sub-tile 1 must be free first
+                if (!wait(&tempty[1], acc_phase ^ 1)) {
+                  fail(ctl, 5);
+                  dead = true;
+                  break;
+                }
+                now_free = true;
+              }
+              if (now_free) {
+                sm100::tc_fence_after();  // sub-tile 1's MMAs after the epilogue's reads of its columns
+                sub1_free = true;
+              }
             }
+            if (!sub1_free) {
+              if (pend == 0) {
+                pend_kb = kb;
+                pend_st = stage;
+              }
+              ++pend;
+            } else {
+              catch_up();
+              issue(d, stage, kb, 1);
+              release(stage);
+            }
+          } else {
+            release(stage);
           }
-          // the stage may be refilled in both CTAs once these MMAs have read it
-          sm100::mma_commit_pair(empty0 + (uint32_t)stage * 8u);
-          sm100::mma_commit_pair(empty1 + (uint32_t)stage * 8u);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
+          }
+        }
+        if (!dead && pend) {  // fewer K slices than stages: finish sub-tile 1 once it is free
+          if (!wait(&tempty[1], acc_phase ^ 1)) {
+            fail(ctl, 5);
+            dead = true;
+          } else {
+            sm100::tc_fence_after();
+            catch_up();
           }
         }
         if (dead) break;
@@ -279,8 +334,10 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2.., both CTAs)
     const int ew = warp - 2;
-    const int q = warp & 3;      // TMEM lane quarter this warp may access
-    const int sub = ew >> 2;     // 256-column sub-tile this warp converts
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // NSUB == 1: warp ew converts the accumulator's 256 columns of its lane quarter.  NSUB == 2: the two warps
+    // of a lane quarter split each sub-tile's columns in halves (`half`), both draining sub-tile 0 first.
+    const int half = ew >> 2;
     uint8_t* stage_tiles = sE + ew * C::EPI_BUFS * EPI_TILE;
     const uint32_t tempty0 = sm100::mapa(sm100::smem_u32(tempty), 0);
     int acc = 0;
@@ -291,55 +348,62 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
       int tm, tn;
       tile_coords(t, num_m, num_n, tm, tn);
       const int row0 = tm * BM + (int)rank * HM + q * 32;  // first C row of this warp's 32 rows
-      const int n0 = tn * BN + sub * SUBN;                  // first C column of this warp's sub-tile
       if (!__all_sync(0xffffffffu, wait(&tfull[acc], acc_phase))) {
         if (lane == 0) fail(ctl, 4);
         break;
       }
       sm100::tc_fence_after();
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + sub * SUBN;
+      const uint32_t lanes = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
       if constexpr (EPI == kStoreBF16 && NSUB == 2) {
-        // the only accumulator: read the whole 256-column sub-tile into registers (packed bf16), release it
-        // so the next tile's MMAs start, then store
-        uint32_t pk[SUBN / 2];
+        // read this warp's 128 columns of sub-tile 0, hand sub-tile 0 back (the next tile's first MMAs may
+        // start), then its 128 columns of sub-tile 1 and hand those back; all kept as packed bf16 in registers
+        uint32_t pk[2][64];
 #pragma unroll
-        for (int c = 0; c < SUBN / 16; ++c) {
-          uint32_t r[16];
-          sm100::tmem_ld16(tbase + c * 16, r);
-          sm100::tmem_ld_wait();
+        for (int sb = 0; sb < 2; ++sb) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            pk[c * 8 + e] = pack_bf16(__uint_as_float(r[2 * e]) * p.alpha, __uint_as_float(r[2 * e + 1]) * p.alpha);
+          for (int c = 0; c < 8; ++c) {
+            uint32_t r[16];
+            sm100::tmem_ld16(lanes + sb * SUBN + half * 128 + c * 16, r);
+            sm100::tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              pk[sb][c * 8 + e] =
+                  pack_bf16(__uint_as_float(r[2 * e]) * p.alpha, __uint_as_float(r[2 * e + 1]) * p.alpha);
+          }
+          sm100::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) sm100::mbar_arrive_cluster(tempty0 + (uint32_t)sb * 8u);
         }
-        sm100::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) sm100::mbar_arrive_cluster(tempty0 + (uint32_t)acc * 8u);
 #pragma unroll
-        for (int c = 0; c < SUBN / 64; ++c) {
-          uint8_t* tile = stage_tiles + ebuf * EPI_TILE;
-          if (lane == 0) {
-            if (C::EPI_BUFS == 2) sm100::bulk_wait_read<1>();  // this staging tile's previous store has read it
-            else sm100::bulk_wait_read<0>();
-          }
-          __syncwarp();
-          // row `lane`: 8 chunks of 16 B; chunk j stored at j ^ (row % 8) (the TMA 128-B swizzle)
-          uint8_t* rowp = tile + lane * 128;
+        for (int sb = 0; sb < 2; ++sb) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) =
-                make_uint4(pk[c * 32 + 4 * j], pk[c * 32 + 4 * j + 1], pk[c * 32 + 4 * j + 2], pk[c * 32 + 4 * j + 3]);
-          sm100::fence_async_shared();  // generic-proxy writes visible to the TMA engine
-          __syncwarp();
-          if (lane == 0 && row0 < p.M && n0 + c * 64 < p.N) {
-            sm100::tma_store_2d(&tma_c, tile, n0 + c * 64, row0);  // clipped at M and N by the tensor map
-            sm100::bulk_commit();
+          for (int c = 0; c < 2; ++c) {
+            const int col0 = tn * BN + sb * SUBN + half * 128 + c * 64;
+            uint8_t* tile = stage_tiles;
+            if (lane == 0) sm100::bulk_wait_read<0>();  // the staging tile's previous store has read it
+            __syncwarp();
+            // row `lane`: 8 chunks of 16 B; chunk j stored at j ^ (row % 8) (the TMA 128-B swizzle)
+            uint8_t* rowp = tile + lane * 128;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) =
+                  make_uint4(pk[sb][c * 32 + 4 * j], pk[sb][c * 32 + 4 * j + 1], pk[sb][c * 32 + 4 * j + 2],
+                             pk[sb][c * 32 + 4 * j + 3]);
+            sm100::fence_async_shared();  // generic-proxy writes visible to the TMA engine
+            __syncwarp();
+            if (lane == 0 && row0 < p.M && col0 < p.N) {
+              sm100::tma_store_2d(&tma_c, tile, col0, row0);  // clipped at M and N by the tensor map
+              sm100::bulk_commit();
+            }
           }
-          if (C::EPI_BUFS == 2) ebuf ^= 1;
         }
       } else {
         // chunk by chunk through the staging tile (64 bf16 or 32 fp32 columns per 128-B row), the accumulator
-        // released after the last read (double-buffered accumulators hide this, or fp32 output)
+        // released after the last read (double-buffered accumulators hide this, or fp32 output).  Warp ew
+        // converts sub-tile `half` (NSUB == 2) and hands back both barriers' worth at its last read.
         constexpr int COLS = EPI == kStoreBF16 ? 64 : 32;
+        const int n0 = tn * BN + half * SUBN;
+        const uint32_t tbase = lanes + half * SUBN;
 #pragma unroll 1
         for (int c = 0; c < SUBN / COLS; ++c) {
           uint32_t r[COLS];
@@ -349,7 +413,14 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
           if (c == SUBN / COLS - 1) {
             sm100::tc_fence_before();
             __syncwarp();
-            if (lane == 0) sm100::mbar_arrive_cluster(tempty0 + (uint32_t)acc * 8u);
+            if (lane == 0) {
+              if (NSUB == 2) {  // both sub-tile barriers count every epilogue warp
+                sm100::mbar_arrive_cluster(tempty0);
+                sm100::mbar_arrive_cluster(tempty0 + 8u);
+              } else {
+                sm100::mbar_arrive_cluster(tempty0 + (uint32_t)acc * 8u);
+              }
+            }
           }
           const int col0 = n0 + c * COLS;
           if (EPI == kAccumF32 && (row0 + 32 > p.M || col0 + 32 > p.N)) {
