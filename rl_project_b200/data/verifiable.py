@@ -1,29 +1,30 @@
-"""Verifiable tasks and RL prompt sets (``src/forgeline/data/verifiable.py``)."""
+"""Verifiable tasks (prompts with a checkable answer or tests) and plain RL prompt sets.
+
+``VerifiableTaskDataset`` is a read-only sequence of ``VerifiableTask`` records with task-type views;
+``load_prompts`` turns a prompt file (JSONL objects with ``prompt``/``text``, or plain lines) into token
+id lists; ``extract_gsm8k_answer`` reads the ``#### <answer>`` line of a GSM8K solution.  Built-in tasks
+and prompts match the reference's (``src/forgeline/data/verifiable.py``) so default runs are comparable.
+"""
 
 from __future__ import annotations
 
 import json
-import re
+from collections.abc import Sequence as _SequenceABC
 from pathlib import Path
 from typing import Iterator, List, Optional, Sequence
 
 from rl_project_b200.core.errors import DatasetError, OptionalDependencyError
 from rl_project_b200.data.records import ReadReport, VerifiableTask, read_jsonl, write_jsonl
 
-DEFAULT_ARITHMETIC_TASKS: List[VerifiableTask] = [
-    VerifiableTask(prompt="What is 15 + 27?", answer="42"),
-    VerifiableTask(prompt="What is 8 * 7?", answer="56"),
-    VerifiableTask(prompt="What is 100 / 4?", answer="25"),
-    VerifiableTask(prompt="What is 2^10?", answer="1024"),
-    VerifiableTask(prompt="If x + 3 = 7, what is x?", answer="4"),
-    VerifiableTask(prompt="What is the square root of 144?", answer="12"),
-    VerifiableTask(prompt="What is 3! (3 factorial)?", answer="6"),
-    VerifiableTask(prompt="What is 17 - 9?", answer="8"),
-]
+_ARITHMETIC = (("What is 15 + 27?", "42"), ("What is 8 * 7?", "56"), ("What is 100 / 4?", "25"),
+               ("What is 2^10?", "1024"), ("If x + 3 = 7, what is x?", "4"),
+               ("What is the square root of 144?", "12"), ("What is 3! (3 factorial)?", "6"),
+               ("What is 17 - 9?", "8"))
+DEFAULT_ARITHMETIC_TASKS: List[VerifiableTask] = [VerifiableTask(prompt=q, answer=a) for q, a in _ARITHMETIC]
 DEFAULT_PROMPTS: List[str] = ["Once upon a time", "The meaning of life is", "In a world where", "The key to success is"]
 
 
-class VerifiableTaskDataset:
+class VerifiableTaskDataset(_SequenceABC):
     kind = "verifiable"
 
     def __init__(self, tasks: Sequence[VerifiableTask]):
@@ -35,64 +36,65 @@ class VerifiableTaskDataset:
     def from_jsonl(cls, path: str | Path, on_error: str = "raise", report: Optional[ReadReport] = None,
                    limit: Optional[int] = None) -> "VerifiableTaskDataset":
         tasks = read_jsonl(path, VerifiableTask, on_error=on_error, report=report)
-        return cls(tasks[:limit] if limit else tasks)
+        return cls(tasks if not limit else tasks[:limit])
 
     @classmethod
     def builtin_arithmetic(cls) -> "VerifiableTaskDataset":
         return cls(DEFAULT_ARITHMETIC_TASKS)
 
+    def of_type(self, task_type: str) -> "VerifiableTaskDataset":
+        """The tasks of one ``task_type`` (raises if there are none)."""
+        return VerifiableTaskDataset([t for t in self.tasks if t.task_type == task_type])
+
     def __len__(self) -> int:
         return len(self.tasks)
 
-    def __getitem__(self, i: int) -> VerifiableTask:
+    def __getitem__(self, i):
         return self.tasks[i]
 
-    def __iter__(self) -> Iterator[VerifiableTask]:
-        return iter(self.tasks)
 
-
-def load_prompts(path: Optional[str | Path], tokenizer, max_length: int = 128) -> List[List[int]]:
-    texts: List[str] = []
-    if path and Path(path).exists():
-        for line in Path(path).read_text(encoding="utf-8").splitlines():
-            line = line.strip()
+def _prompt_texts(path: Path) -> Iterator[str]:
+    with path.open(encoding="utf-8") as fh:
+        for raw in fh:
+            line = raw.strip()
             if not line:
                 continue
             try:
                 obj = json.loads(line)
-                texts.append(obj.get("prompt", obj.get("text", line)) if isinstance(obj, dict) else line)
             except json.JSONDecodeError:
-                texts.append(line)
-    else:
-        texts = list(DEFAULT_PROMPTS)
-    out = [ids for ids in (tokenizer.encode(t)[:max_length] for t in texts) if ids]
-    if not out:
+                yield line
+                continue
+            yield (obj.get("prompt", obj.get("text", line)) if isinstance(obj, dict) else line)
+
+
+def load_prompts(path: Optional[str | Path], tokenizer, max_length: int = 128) -> List[List[int]]:
+    """Token ids of every prompt in ``path`` (cut to ``max_length``; empty ones dropped), or of the built-in
+    prompts when ``path`` is unset or missing."""
+    texts = _prompt_texts(Path(path)) if path and Path(path).exists() else iter(DEFAULT_PROMPTS)
+    prompts = [ids[:max_length] for ids in map(tokenizer.encode, texts) if ids]
+    if not prompts:
         raise DatasetError("no usable prompts found")
-    return out
-
-
-_GSM8K = re.compile(r"####\s*(.+)")
+    return prompts
 
 
 def extract_gsm8k_answer(solution: str) -> str:
-    for line in reversed(solution.strip().split("\n")):
-        m = _GSM8K.search(line)
-        if m:
-            return re.sub(r"[,\s]", "", m.group(1))
-    return ""
+    """The final answer of a GSM8K solution: the text after the last ``####`` marker, without commas or
+    whitespace ("" when there is none)."""
+    head, sep, tail = solution.rpartition("####")
+    if not sep:
+        return ""
+    return "".join(ch for ch in tail.split("\n", 1)[0] if ch != "," and not ch.isspace())
 
 
 def build_gsm8k_tool_dataset(output_path: str | Path, split: str = "train", limit: Optional[int] = None) -> int:
+    """Write GSM8K as tagged-answer tool tasks (needs the optional ``datasets`` package and its cache)."""
     try:
         from datasets import load_dataset
     except ImportError as exc:
         raise OptionalDependencyError("datasets is not installed", hint="pip install datasets") from exc
-    ds = load_dataset("openai/gsm8k", "main", split=split)
-    tasks = []
-    for i, row in enumerate(ds):
-        if limit and i >= limit:
-            break
-        ans = extract_gsm8k_answer(row["answer"])
-        if ans:
-            tasks.append(VerifiableTask(prompt=row["question"], answer=ans, task_type="tagged", tools=["python_executor"]))
+    rows = load_dataset("openai/gsm8k", "main", split=split)
+    if limit:
+        rows = rows.select(range(min(limit, len(rows))))
+    tasks = (VerifiableTask(prompt=r["question"], answer=a, task_type="tagged", tools=["python_executor"])
+             for r in rows for a in [extract_gsm8k_answer(r["answer"])] if a)
     return write_jsonl(output_path, tasks)
