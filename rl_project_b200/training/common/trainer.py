@@ -118,7 +118,7 @@ class PostTrainingAlgorithm(ABC):
 
     # the same kind of state on the algorithm's data source (``train`` / ``dataset``): a source that draws
     # from its own generator or walks its own cursor is restored too, saved as "<source>.<attr>"
-    _source_names = ("train", "dataset")
+    _source_names = ("train", "dataset", "sampler")
     _source_attrs = ("gen", "rng", "_order", "_i", "i", "pos", "_pos", "epoch")
 
     @staticmethod

@@ -1,10 +1,17 @@
-"""Reward-model training with the Bradley-Terry objective (``src/forgeline/training/reward_model.py``)."""
+"""Reward-model training: a scalar head on the policy backbone fitted to preference pairs with the
+Bradley-Terry objective ``-log sigmoid(r_chosen - r_rejected)`` (reference:
+``src/forgeline/training/reward_model.py``).
+
+Each step scores the chosen and the rejected completions of a batch in ONE forward pass: the 2B
+sequences (prompt + response, cut to their last ``max_length`` tokens) are padded into a single batch,
+so the backbone runs once per micro-batch rather than twice.  Batches are drawn without replacement, a
+seeded shuffle per epoch.
+"""
 
 from __future__ import annotations
 
-import random
 from dataclasses import dataclass
-from typing import Any, Dict, List, Mapping, Optional
+from typing import Any, Dict, List, Mapping, Optional, Sequence, Tuple
 
 import torch
 import torch.nn as nn
@@ -12,6 +19,7 @@ import torch.nn as nn
 from rl_project_b200.core.errors import ConfigError
 from rl_project_b200.data.collators import pad_sequences
 from rl_project_b200.models.reward import bradley_terry_loss
+from rl_project_b200.training.common.sampling import EpochSampler
 from rl_project_b200.training.common.trainer import PostTrainingAlgorithm
 
 
@@ -30,13 +38,17 @@ class RewardModelAlgorithm(PostTrainingAlgorithm):
                  tokenizer_meta: Optional[Dict[str, Any]] = None):
         if len(dataset) == 0:
             raise ConfigError("reward-model dataset is empty")
-        self.model, self.dataset, self.eval_dataset, self.cfg = model, dataset, eval_dataset, config
+        self.model = model
+        self.dataset = dataset
+        self.eval_dataset = eval_dataset
+        self.cfg = config
         self.pad = pad_token_id
         self._tok_meta = tokenizer_meta
+        self.sampler = EpochSampler(len(dataset), config.seed)
         if config.freeze_backbone:
             model.freeze_backbone()
-        self.rng = random.Random(config.seed)
 
+    # ------------------------------------------------------------ trainer hooks
     def parameters(self) -> List[nn.Parameter]:
         return [p for p in self.model.parameters() if p.requires_grad]
 
@@ -44,25 +56,31 @@ class RewardModelAlgorithm(PostTrainingAlgorithm):
         return (self.model,)
 
     def collect(self, step: int):
-        return [self.dataset[self.rng.randrange(len(self.dataset))] for _ in range(self.cfg.batch_size)]
+        return [self.dataset[i] for i in self.sampler.take(self.cfg.batch_size)]
 
-    def _scores(self, examples, key: str) -> torch.Tensor:
-        ids, mask = pad_sequences([(e["prompt"] + e[key])[-self.cfg.max_length:] for e in examples], self.pad, "right")
+    def _pair_scores(self, examples: Sequence[Mapping[str, List[int]]]) -> Tuple[torch.Tensor, torch.Tensor]:
+        """(chosen scores, rejected scores) from one forward over both sides of every pair."""
+        keep = self.cfg.max_length
+        seqs = [(e["prompt"] + e[side])[-keep:] for side in ("chosen", "rejected") for e in examples]
+        ids, mask = pad_sequences(seqs, self.pad, "right")
         dev = next(self.model.parameters()).device
-        return self.model(ids.to(dev), mask.to(dev)).float()
+        scores = self.model(ids.to(dev), mask.to(dev)).float()
+        return scores[:len(examples)], scores[len(examples):]
 
     def loss(self, batch, micro_step: int, n_micro: int):
-        chunk = batch[micro_step::n_micro] if n_micro > 1 else batch
-        c, r = self._scores(chunk, "chosen"), self._scores(chunk, "rejected")
-        return bradley_terry_loss(c, r), {"accuracy": (c > r).float().mean(), "margin": (c - r).detach().mean()}
+        part = batch if n_micro <= 1 else batch[micro_step::n_micro]
+        chosen, rejected = self._pair_scores(part)
+        gap = chosen - rejected
+        return bradley_terry_loss(chosen, rejected), {"accuracy": (gap > 0).float().mean(),
+                                                      "margin": gap.detach().mean()}
 
     @torch.no_grad()
     def evaluate(self, step: int) -> Dict[str, float]:
-        ds = self.eval_dataset or self.dataset
-        ex = [ds[i] for i in range(min(len(ds), 32))]
-        c, r = self._scores(ex, "chosen"), self._scores(ex, "rejected")
-        return {"loss": float(bradley_terry_loss(c, r)), "accuracy": float((c > r).float().mean())}
+        ds = self.eval_dataset if self.eval_dataset is not None else self.dataset
+        chosen, rejected = self._pair_scores([ds[i] for i in range(min(len(ds), 32))])
+        return {"loss": float(bradley_terry_loss(chosen, rejected)), "accuracy": float((chosen > rejected).float().mean())}
 
+    # ------------------------------------------------------------ checkpoint contract
     def state(self) -> Dict[str, Any]:
         return self.model.state_for_checkpoint()
 
