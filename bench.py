@@ -46,6 +46,8 @@ def parse_args():
     ap.add_argument("--batch-per-gpu", type=int, default=8)
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--phase-steps", type=int, default=2,
+                    help="untimed steps after the timed region with per-phase CUDA events (0: none)")
     ap.add_argument("--workload", choices=["sft1b", "mesh8b", "moe", "grpo"], default="sft1b",
                     help="sft1b: the headline (dense 1B SFT). mesh8b: dense-8B pretrain on a TP x PP x DP "
                          "mesh (1F1B). moe: MLA+MoE pretrain with expert parallelism. grpo: GRPO rollout+update "
@@ -191,6 +193,22 @@ def time_wall(step, k: int) -> float:
     return max_over_ranks((t1 - t0) * 1e3 / k)
 
 
+def phase_breakdown(trainer, steps: int) -> dict:
+    """Per-phase device time of a training step (ms, mean over `steps` untimed steps run after the timed region,
+    max over ranks per phase): forward, backward (each with the collectives the strategy overlaps into them),
+    grad_sync (the exposed tail of the gradient reduction), clip (global norm, incl. its all-reduce), optimizer,
+    start (the device idle gap between steps).  Every rank takes the same all-reduces in the same order."""
+    if steps <= 0:
+        return {}
+    trainer.phase_events = []
+    for _ in range(steps):
+        trainer.train_step()
+    times = trainer.phase_times(trainer.phase_events)
+    trainer.phase_events = None
+    return {k: round(max_over_ranks(times.get(k, 0.0) / steps), 3)
+            for k in ("forward", "backward", "grad_sync", "clip", "optimizer", "start")}
+
+
 def emit(rank: int, payload: dict) -> None:
     if rank == 0:
         print(json.dumps(payload), flush=True)
@@ -263,6 +281,7 @@ def run_ours(args, world, rank, local):
     clk = clocks.stop()
     tokens_step = args.seq * args.batch_per_gpu * world
     value = tokens_step / (ms / 1e3)
+    phases = phase_breakdown(trainer, args.phase_steps)
 
     e2e = None
     if not args.no_e2e:
@@ -299,6 +318,8 @@ def run_ours(args, world, rank, local):
                                    else ("nccl reduce-scatter" if world > 1 else "none"))},
         "clocks": clk, "e2e": e2e, "gpu_launches": int(launches), "impl": "ours",
     }
+    if phases:
+        payload["config"]["phases_ms"] = phases
     emit(rank, payload)
     strategy.teardown()
 

@@ -466,7 +466,7 @@ void gemm_grouped(int64_t mode, int64_t b_mn, int64_t epi, const at::Tensor& A, 
 // Attention forward: q [B, T, Hq, D], k [B, T, Hkv, D], v [B, T, Hkv, DV] (token-major, contiguous bf16) -> out
 // [B, T, Hq, DV]; lse [B, Hq, T] fp32 when defined (numel > 0).
 void fmha_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& out, at::Tensor& lse,
-              bool causal, double scale, const at::Tensor& status) {
+              bool causal, double scale, int64_t window, double softcap, const at::Tensor& status) {
   check_bf16(q, "q");
   check_bf16(k, "k");
   check_bf16(v, "v");
@@ -494,7 +494,7 @@ void fmha_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
   const c10::cuda::CUDAGuard g(q.device());
   CHECK_OK(rlb_fmha_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse_p, (int)q.size(0),
                         (int)q.size(1), (int)q.size(2), (int)k.size(2), (int)q.size(3), (int)v.size(3), causal ? 1 : 0,
-                        (float)scale, status.data_ptr<int>(), cur_stream()),
+                        (float)scale, (int)window, (float)softcap, status.data_ptr<int>(), cur_stream()),
            "fmha_fwd");
 }
 
@@ -502,7 +502,7 @@ void fmha_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
 // bf16 like k; lse / delta fp32 [B, Hq, T].
 void fmha_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& dout,
               const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dq, at::Tensor& dk, at::Tensor& dv,
-              bool causal, double scale, const at::Tensor& status) {
+              bool causal, double scale, int64_t window, double softcap, const at::Tensor& status) {
   using Ts = std::initializer_list<const at::Tensor*>;
   for (const at::Tensor* t : Ts{&q, &k, &v, &dout}) check_bf16(*t, "q/k/v/dout");
   for (const at::Tensor* t : Ts{&k, &v, &dout, &lse, &delta, &dq, &dk, &dv, &status}) check_dev(*t, q, "fmha_bwd operand");
@@ -520,7 +520,7 @@ void fmha_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   CHECK_OK(rlb_fmha_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), dout.data_ptr(), lse.data_ptr<float>(),
                         delta.data_ptr<float>(), dq.data_ptr<float>(), dk.data_ptr(), dv.data_ptr(), (int)q.size(0),
                         (int)q.size(1), (int)q.size(2), (int)k.size(2), (int)q.size(3), causal ? 1 : 0, (float)scale,
-                        status.data_ptr<int>(), cur_stream()),
+                        (int)window, (float)softcap, status.data_ptr<int>(), cur_stream()),
            "fmha_bwd");
 }
 

@@ -1,8 +1,10 @@
 // Fused multi-head attention, backward, for sm_100a (tcgen05 MMAs, TMEM accumulators, TMA loads).
 //
-// With S = scale Q K^T, P = softmax(S) (recomputed from the forward's log-sum-exp), O = P V:
+// With X = Q K^T, S = f(scale X) (f(x) = x, or cap tanh(x / cap) for a logit soft-cap), P = softmax(S)
+// (recomputed from the forward's log-sum-exp), O = P V:
 //   dV = P^T dO,   dP = dO V^T,   dS = P * (dP - Delta),   Delta = rowsum(dO * O),
-//   dQ = scale dS K,   dK = scale dS^T Q.
+//   dX = scale f'(scale X) dS  (f' = 1 - tanh^2 with the cap, else 1),   dQ = dX K,   dK = dX^T Q.
+// Masks as in the forward: causal and a sliding window; query tiles a key tile cannot reach are skipped.
 // Same token-major [B, T, H, D] layouts, D = 64 or 128, grouped-query heads and causal mask as the forward
 // (csrc/fmha_fwd.cu).  The reference differentiates attention through PyTorch autograd
 // (``src/forgeline/models/attention/causal.py:79-134``).
@@ -64,6 +66,9 @@ struct Params {
   int B, T, Hq, Hkv;
   float scale, scale_log2;
   int causal;
+  int window;      // 0: none; else key s is visible to query t only if t - s < window
+  float cap_in;    // soft-cap: scale / cap
+  float cap_log2;  // soft-cap: cap * log2(e)
   int* status;
 };
 
@@ -94,7 +99,12 @@ __device__ __forceinline__ void store_chunk(uint8_t* box, int row, int chunk, co
   *(uint4*)(box + (row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4)) = pk;
 }
 
-template <int D>
+// 4 fp32 values added into global memory with one vector reduction (no return value).
+__device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+template <int D, bool CAP>
 __global__ void __launch_bounds__(192, 1) fmha_bwd_kernel(const __grid_constant__ CUtensorMap mq,
                                                           const __grid_constant__ CUtensorMap mk,
                                                           const __grid_constant__ CUtensorMap mv,
@@ -128,7 +138,9 @@ __global__ void __launch_bounds__(192, 1) fmha_bwd_kernel(const __grid_constant_
   const int kv0 = j * BKV;
   const int num_qt = (p.T + BQ - 1) / BQ;
   const int first_i = p.causal ? j : 0;  // causal: query tiles at or after the key tile
-  const int nq = num_qt - first_i;
+  // window: the last query that sees any key of this tile is kv0 + BKV - 1 + window - 1
+  const int end_i = p.window > 0 ? min(num_qt, (kv0 + BKV + p.window - 2) / BQ + 1) : num_qt;
+  const int nq = end_i - first_i;  // at least 1: the key tile's own diagonal query tile
   const int steps = G * nq;  // (query head, query tile) pairs, head-major
 
   if (threadIdx.x == 0) {
@@ -260,7 +272,8 @@ __global__ void __launch_bounds__(192, 1) fmha_bwd_kernel(const __grid_constant_
       sm100::tc_fence_after();
       const float* lse = p.lse + ((long long)b * p.Hq + h) * p.T;
       const float* delta = p.delta + ((long long)b * p.Hq + h) * p.T;
-      const bool masked = (p.causal && qi == j) || (q0 + BQ > p.T) || (kv0 + BKV > p.T);
+      const bool masked = (p.causal && qi == j) || (q0 + BQ > p.T) || (kv0 + BKV > p.T) ||
+                          (p.window > 0 && q0 + BQ - 1 - kv0 >= p.window);
 #pragma unroll 1
       for (int c = 0; c < BQ / 32; ++c) {
         uint32_t rs[32], rd[32];
@@ -275,12 +288,22 @@ __global__ void __launch_bounds__(192, 1) fmha_bwd_kernel(const __grid_constant_
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int q = q0 + c * 32 + v * 8 + e;
-            const bool valid = !masked || (q < p.T && key < p.T && (!p.causal || q >= key));
+            const bool valid = !masked || (q < p.T && key < p.T && (!p.causal || q >= key) &&
+                                           (p.window <= 0 || q - key < p.window));
             const float l2 = valid ? __ldg(lse + q) * LOG2E : 0.f;
             const float dl = valid ? __ldg(delta + q) : 0.f;
-            const float pv = valid ? exp2f(fmaf(__uint_as_float(rs[v * 8 + e]), p.scale_log2, -l2)) : 0.f;
+            const float x = __uint_as_float(rs[v * 8 + e]);
+            float pv, dsc;
+            if constexpr (CAP) {
+              const float th = tanhf(x * p.cap_in);
+              pv = valid ? exp2f(fmaf(p.cap_log2, th, -l2)) : 0.f;
+              dsc = p.scale * (1.f - th * th);
+            } else {
+              pv = valid ? exp2f(fmaf(x, p.scale_log2, -l2)) : 0.f;
+              dsc = p.scale;
+            }
             pf[e] = pv;
-            df[e] = pv * (__uint_as_float(rd[v * 8 + e]) - dl) * p.scale;
+            df[e] = pv * (__uint_as_float(rd[v * 8 + e]) - dl) * dsc;
           }
           const int chunk = (c & 1) * 4 + v;
           store_chunk(pbox, row, chunk, pf);
@@ -309,7 +332,9 @@ __global__ void __launch_bounds__(192, 1) fmha_bwd_kernel(const __grid_constant_
         sm100::tmem_ld_wait();
         if (q < p.T) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) atomicAdd(dq + c * 32 + e, __uint_as_float(r[e]));
+          for (int e = 0; e < 32; e += 4)
+            red_add_v4(dq + c * 32 + e, __uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]),
+                       __uint_as_float(r[e + 3]));
         }
       }
       sm100::tc_fence_before();
@@ -399,7 +424,7 @@ static cudaError_t launch(const void* q, const void* k, const void* v, const voi
   if (!make_map(&mq, q, p.B, p.T, p.Hq * D) || !make_map(&mk, k, p.B, p.T, p.Hkv * D) ||
       !make_map(&mv, v, p.B, p.T, p.Hkv * D) || !make_map(&mdo, dout, p.B, p.T, p.Hq * D))
     return cudaErrorInvalidResourceHandle;
-  auto kern = fmha_bwd_kernel<D>;
+  auto kern = p.cap_log2 > 0.f ? fmha_bwd_kernel<D, true> : fmha_bwd_kernel<D, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_REQUEST);
   if (e != cudaSuccess) return e;
   (void)cudaGetLastError();
@@ -414,8 +439,9 @@ static cudaError_t launch(const void* q, const void* k, const void* v, const voi
 // the caller, accumulated); dk, dv [B][T][Hkv][D] bf16 (written).
 cudaError_t rlb_fmha_bwd(const void* q, const void* k, const void* v, const void* dout, const float* lse,
                          const float* delta, float* dq, void* dk, void* dv, int B, int T, int Hq, int Hkv, int D,
-                         int causal, float scale, int* status, cudaStream_t s) {
+                         int causal, float scale, int window, float softcap, int* status, cudaStream_t s) {
   if (B <= 0 || T <= 0) return cudaSuccess;
+  if (window < 0 || softcap < 0.f) return cudaErrorInvalidValue;
   if ((D != 64 && D != 128) || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Hkv > 65535 || B > 65535)
     return cudaErrorInvalidValue;
   if ((((uintptr_t)q) | ((uintptr_t)k) | ((uintptr_t)v) | ((uintptr_t)dout) | ((uintptr_t)dk) | ((uintptr_t)dv)) & 15)
@@ -433,6 +459,9 @@ cudaError_t rlb_fmha_bwd(const void* q, const void* k, const void* v, const void
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
+  p.window = window;
+  p.cap_in = softcap > 0.f ? scale / softcap : 0.f;
+  p.cap_log2 = softcap > 0.f ? softcap * 1.4426950408889634f : 0.f;
   p.status = status;
   return D == 128 ? fmha_bwd::launch<128>(q, k, v, dout, p, s) : fmha_bwd::launch<64>(q, k, v, dout, p, s);
 }

@@ -1,6 +1,9 @@
 // Fused multi-head attention, forward, for sm_100a: tcgen05 MMAs with TMEM accumulators, TMA tile loads.
 //
-//   out[b, t, h, :] = softmax(scale * q[b, t, h, :] . k[b, s, h / G, :]^T  (+ causal mask)) v[b, s, h / G, :]
+//   out[b, t, h, :] = softmax(f(scale * q[b, t, h, :] . k[b, s, h / G, :]^T)  (+ masks)) v[b, s, h / G, :]
+//
+// with f(x) = x, or f(x) = cap * tanh(x / cap) for a logit soft-cap; masks: causal (s <= t) and a sliding
+// window (t - s < window).  Key tiles that a query tile's rows cannot see at all are skipped.
 //
 // q, k, v and out are token-major [B, T, H, D] bf16 (the layout the fused RoPE kernel writes).  Head
 // dims: D = 64 or 128 for q, k, v alike, or d_qk = 192 with d_v = 128 (multi-head latent attention with
@@ -29,6 +32,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <math.h>
+#include <climits>
 #include <stdint.h>
 
 #include "sm100.cuh"
@@ -67,8 +71,18 @@ struct Params {
   int B, T, Hq, Hkv;
   float scale_log2;  // softmax scale * log2(e)
   int causal;
+  int window;        // 0: none; else key s is visible to query t only if t - s < window
+  float cap_in;      // soft-cap: scale / cap (the tanh argument per raw score)
+  float cap_log2;    // soft-cap: cap * log2(e)
   int* status;
 };
+
+// Score of one raw accumulator value in log2 units: scale * x * log2(e), or cap * tanh(scale * x / cap) * log2(e).
+template <bool CAP>
+__device__ __forceinline__ float score_log2(float x, const Params& p) {
+  if constexpr (CAP) return p.cap_log2 * tanhf(x * p.cap_in);
+  else return x * p.scale_log2;
+}
 
 __device__ __forceinline__ void fail(int* status, volatile int* abort_flag, int where) {
   *abort_flag = 1;
@@ -85,7 +99,7 @@ __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, wait(bar, parity));
 }
 
-template <int D, int DV>
+template <int D, int DV, bool CAP>
 __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant__ CUtensorMap mq,
                                                           const __grid_constant__ CUtensorMap mk,
                                                           const __grid_constant__ CUtensorMap mv, Params p) {
@@ -119,7 +133,13 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
   const int hk = h / (p.Hq / p.Hkv);
   const int q0 = qt * BQ;
   const int nkv_all = (p.T + BKV - 1) / BKV;
-  const int n = p.causal ? min(qt + 1, nkv_all) : nkv_all;  // key tiles this query tile reads
+  const int j_end = p.causal ? min(qt + 1, nkv_all) : nkv_all;                   // one past the last key tile
+  const int j0 = p.window > 0 ? min(max(q0 - p.window + 1, 0) / BKV, j_end) : 0;  // first key tile any row sees
+  // key tiles this query tile reads (at least the diagonal one); loop step j reads key tile j0 + j
+  const int n = j_end - j0;
+  // a tile needs per-element masks if it runs past T, crosses the causal diagonal, or reaches below the
+  // window of the tile's last row
+  const int win_lo = p.window > 0 ? q0 + BQ - p.window : INT_MIN;
 
   if (threadIdx.x == 0) {
     sm100::mbar_init(qfull, 1);
@@ -168,7 +188,7 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
         sm100::mbar_arrive_expect_tx(&kfull[buf], DSUB * SUB_BYTES);
 #pragma unroll
         for (int s = 0; s < DSUB; ++s)
-          sm100::tma_load_3d(sK + (buf * DSUB + s) * SUB_BYTES, &mk, &kfull[buf], hk * D + 64 * s, j * BKV, b);
+          sm100::tma_load_3d(sK + (buf * DSUB + s) * SUB_BYTES, &mk, &kfull[buf], hk * D + 64 * s, (j0 + j) * BKV, b);
         k_issued = j + 1;
         const int vb = j % VST;
         if (!wait(&vempty[vb], ((j / VST) & 1) ^ 1)) {
@@ -178,7 +198,7 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
         sm100::mbar_arrive_expect_tx(&vfull[vb], VSUB * SUB_BYTES);
 #pragma unroll
         for (int s = 0; s < VSUB; ++s)
-          sm100::tma_load_3d(sV + (vb * VSUB + s) * SUB_BYTES, &mv, &vfull[vb], hk * DV + 64 * s, j * BKV, b);
+          sm100::tma_load_3d(sV + (vb * VSUB + s) * SUB_BYTES, &mv, &vfull[vb], hk * DV + 64 * s, (j0 + j) * BKV, b);
         v_issued = j + 1;
       }
       // every load issued here lands before the CTA exits (a buffer's earlier loads were consumed
@@ -261,7 +281,6 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
     const int row = qq * 32 + lane;
     const int rq = q0 + row;
     const uint32_t lanes = tmem + ((uint32_t)(qq * 32) << 16);
-    const float sl2 = p.scale_log2;
     float O[DV];
 #pragma unroll
     for (int d = 0; d < DV; ++d) O[d] = 0.f;
@@ -283,8 +302,8 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
       }
       sm100::tc_fence_after();
       const uint32_t ts = lanes + buf * BKV;
-      const int kv0 = j * BKV;
-      const bool masked = (kv0 + BKV > p.T) || (p.causal && kv0 + BKV - 1 > rq - row);
+      const int kv0 = (j0 + j) * BKV;
+      const bool masked = (kv0 + BKV > p.T) || (p.causal && kv0 + BKV - 1 > q0) || (kv0 < win_lo);
       // pass 1: row max over this key tile
       float mx = -INFINITY;
 #pragma unroll 1
@@ -295,11 +314,12 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int col = kv0 + c * 32 + e;
-          const bool valid = !masked || (col < p.T && (!p.causal || col <= rq));
-          mx = valid ? fmaxf(mx, __uint_as_float(r[e])) : mx;
+          const bool valid =
+              !masked || (col < p.T && (!p.causal || col <= rq) && (p.window <= 0 || rq - col < p.window));
+          mx = valid ? fmaxf(mx, score_log2<CAP>(__uint_as_float(r[e]), p)) : mx;
         }
       }
-      const float m_new = fmaxf(m, mx * sl2);
+      const float m_new = fmaxf(m, mx);
       // fold the previous tile's P V into the accumulator (both brought to the max P_{j-1} used)
       if (j >= 1) {
         const int i = j - 1, ib = i & 1;
@@ -340,8 +360,9 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int col = kv0 + c * 32 + v * 8 + e;
-            const bool valid = !masked || (col < p.T && (!p.causal || col <= rq));
-            f[e] = valid ? exp2f(fmaf(__uint_as_float(r[v * 8 + e]), sl2, -moff)) : 0.f;
+            const bool valid =
+                !masked || (col < p.T && (!p.causal || col <= rq) && (p.window <= 0 || rq - col < p.window));
+            f[e] = valid ? exp2f(score_log2<CAP>(__uint_as_float(r[v * 8 + e]), p) - moff) : 0.f;
             rs += f[e];
           }
           uint4 pk;
@@ -393,7 +414,7 @@ __global__ void __launch_bounds__(192, 1) fmha_fwd_kernel(const __grid_constant_
             }
             *(uint4*)(dst + v * 8) = pk;
           }
-          if (p.lse) p.lse[((long long)b * p.Hq + h) * p.T + rq] = (m + log2f(l)) * LN2;
+          if (p.lse) p.lse[((long long)b * p.Hq + h) * p.T + rq] = l > 0.f ? (m + log2f(l)) * LN2 : -INFINITY;
         }
       } else {
         fail(p.status, abort_flag, 11);
@@ -446,7 +467,7 @@ static cudaError_t launch(const void* q, const void* k, const void* v, const Par
   if (!make_map(&mq, q, p.B, p.T, p.Hq * D) || !make_map(&mk, k, p.B, p.T, p.Hkv * D) ||
       !make_map(&mv, v, p.B, p.T, p.Hkv * DV))
     return cudaErrorInvalidResourceHandle;
-  auto kern = fmha_fwd_kernel<D, DV>;
+  auto kern = p.cap_log2 > 0.f ? fmha_fwd_kernel<D, DV, true> : fmha_fwd_kernel<D, DV, false>;
   constexpr int smem = smem_request<D, DV>();
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
@@ -459,10 +480,13 @@ static cudaError_t launch(const void* q, const void* k, const void* v, const Par
 }  // namespace fmha
 
 // q [B][T][Hq][D], k [B][T][Hkv][D], v [B][T][Hkv][DV], out [B][T][Hq][DV] (bf16, contiguous); lse
-// [B][Hq][T] fp32 or null.  (D, DV) = (64, 64), (128, 128) or (192, 128).
+// [B][Hq][T] fp32 or null.  (D, DV) = (64, 64), (128, 128) or (192, 128).  window > 0: sliding window;
+// softcap > 0: tanh logit cap.
 cudaError_t rlb_fmha_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int B, int T, int Hq,
-                         int Hkv, int D, int DV, int causal, float scale, int* status, cudaStream_t s) {
+                         int Hkv, int D, int DV, int causal, float scale, int window, float softcap, int* status,
+                         cudaStream_t s) {
   if (B <= 0 || T <= 0) return cudaSuccess;
+  if (window < 0 || softcap < 0.f) return cudaErrorInvalidValue;
   const bool shape_ok = (D == 64 && DV == 64) || (D == 128 && DV == 128) || (D == 192 && DV == 128);
   if (!shape_ok || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Hq > 65535 || B > 65535) return cudaErrorInvalidValue;
   if ((((uintptr_t)q) | ((uintptr_t)k) | ((uintptr_t)v) | ((uintptr_t)out)) & 15) return cudaErrorInvalidDevicePointer;
@@ -475,6 +499,9 @@ cudaError_t rlb_fmha_fwd(const void* q, const void* k, const void* v, void* out,
   p.Hkv = Hkv;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
+  p.window = window;
+  p.cap_in = softcap > 0.f ? scale / softcap : 0.f;
+  p.cap_log2 = softcap > 0.f ? softcap * 1.4426950408889634f : 0.f;
   p.status = status;
   if (D == 192) return fmha::launch<192, 128>(q, k, v, p, s);
   return D == 128 ? fmha::launch<128, 128>(q, k, v, p, s) : fmha::launch<64, 64>(q, k, v, p, s);

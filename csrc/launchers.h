@@ -76,13 +76,15 @@ cudaError_t rlb_nf4_gemm(int mode, int M, int N, int K, const void* A, const voi
 
 // Fused attention forward (tcgen05): q [B][T][Hq][D], k [B][T][Hkv][D], v [B][T][Hkv][DV], out [B][T][Hq][DV]
 // bf16; lse [B][Hq][T] fp32 (natural log) or null.  (D, DV) = (64, 64), (128, 128) or (192, 128).
+// window > 0: sliding window (t - s < window); softcap > 0: logits cap * tanh(logit / cap).
 cudaError_t rlb_fmha_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int B, int T, int Hq,
-                         int Hkv, int D, int DV, int causal, float scale, int* status, cudaStream_t s);
+                         int Hkv, int D, int DV, int causal, float scale, int window, float softcap, int* status,
+                         cudaStream_t s);
 // Fused attention backward: dq fp32 [B][T][Hq][D] (zeroed by the caller, accumulated), dk / dv bf16
 // [B][T][Hkv][D]; lse / delta fp32 [B][Hq][T] (delta = rowsum(dout * out)).
 cudaError_t rlb_fmha_bwd(const void* q, const void* k, const void* v, const void* dout, const float* lse,
                          const float* delta, float* dq, void* dk, void* dv, int B, int T, int Hq, int Hkv, int D,
-                         int causal, float scale, int* status, cudaStream_t s);
+                         int causal, float scale, int window, float softcap, int* status, cudaStream_t s);
 
 cudaError_t rlb_paged_decode(const void* q, const void* k_pool, const void* v_pool, const int* block_tables,
                              const int* ctx_lens, void* out, float* part_acc, float* part_ml, int B, int Hq, int Hkv,

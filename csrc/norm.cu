@@ -160,7 +160,7 @@ RLB_DEVICE void rows_sum(float (&v)[R], float* red) {  // red: [R][32]
   __syncthreads();
 }
 
-__global__ void rmsnorm_fwd_wide(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ delta,
+__global__ void __launch_bounds__(1024) rmsnorm_fwd_wide(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ delta,
                                  const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ h_out,
                                  __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out, long long rows, int dim,
                                  float eps) {
@@ -214,7 +214,10 @@ __global__ void rmsnorm_fwd_wide(const __nv_bfloat16* __restrict__ x, const __nv
 
 constexpr int kRowsBwd = 2;  // the backward keeps 3 input vectors per row live
 
-__global__ void rmsnorm_bwd_wide(const __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ w,
+// MAXT: the largest block this instantiation is launched with (dim / 8 threads).  Up to dim 4096 the
+// 512-thread bound leaves ptxas the registers it wants; dim 8192 needs 1024 threads, which caps them at 64.
+template <int MAXT>
+__global__ void __launch_bounds__(MAXT) rmsnorm_bwd_wide(const __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ w,
                                  const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dy,
                                  const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
                                  float* __restrict__ dw_part, long long rows, int dim) {
@@ -278,6 +281,7 @@ __global__ void rmsnorm_bwd_wide(const __nv_bfloat16* __restrict__ h, const __nv
 // Column sums of a [parts, dim] fp32 matrix -> dw (bf16 or fp32), fixed order:
 // block = 32 columns x 8 row-slices, each slice strides over the parts, then the
 // 8 slice sums are added in shared memory.
+
 __global__ void colsum_kernel(const float* __restrict__ part, int parts, int dim, float* __restrict__ out_f32,
                               __nv_bfloat16* __restrict__ out_bf16) {
   __shared__ float tile[8][33];
@@ -297,12 +301,22 @@ __global__ void colsum_kernel(const float* __restrict__ part, int parts, int dim
   }
 }
 
+// one thread per 8 columns, up to 1024 threads (dim 8192): the wide kernels are bounded to 64 registers
 static bool wide_ok(int dim) { return dim % 256 == 0 && dim <= 8192; }
 
 static int wide_grid(long long rows, int sms) {
   const long long want = (rows + kRowsBwd - 1) / kRowsBwd;
   const long long cap = (long long)sms * 8;
   return (int)(want < cap ? (want < 1 ? 1 : want) : cap);
+}
+
+// The wide backward with `grid` blocks of dim / 8 threads (dim a multiple of 256, at most 8192), partial
+// column sums of dw into dw_part[grid][dim].  Also used by the allocation-free entry point (norm_noalloc.cu).
+void launch_rmsnorm_bwd_wide(int grid, const __nv_bfloat16* h, const __nv_bfloat16* w, const float* rstd,
+                             const __nv_bfloat16* dy, const __nv_bfloat16* dres, __nv_bfloat16* dx, float* dw_part,
+                             long long rows, int dim, cudaStream_t s) {
+  auto k = dim / 8 > 512 ? rmsnorm_bwd_wide<1024> : rmsnorm_bwd_wide<512>;
+  k<<<grid, dim / 8, 0, s>>>(h, w, rstd, dy, dres, dx, dw_part, rows, dim);
 }
 
 static int pick_grid(long long rows, int sms) {
@@ -352,9 +366,8 @@ cudaError_t rlb_rmsnorm_bwd(const void* h, const void* w, const float* rstd, con
   if (dim % 8 != 0) return cudaErrorInvalidValue;
   if (wide_ok(dim)) {
     const int g = wide_grid(rows, sms);
-    rmsnorm_bwd_wide<<<g, dim / 8, 0, s>>>((const __nv_bfloat16*)h, (const __nv_bfloat16*)w, rstd,
-                                            (const __nv_bfloat16*)dy, (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx,
-                                            dw_part, rows, dim);
+    launch_rmsnorm_bwd_wide(g, (const __nv_bfloat16*)h, (const __nv_bfloat16*)w, rstd, (const __nv_bfloat16*)dy,
+                            (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw_part, rows, dim, s);
     colsum_kernel<<<ceil_div(dim, 32), 256, 0, s>>>(dw_part, g, dim, dw_is_f32 ? (float*)dw_out : nullptr,
                                                     dw_is_f32 ? nullptr : (__nv_bfloat16*)dw_out);
     return cudaGetLastError();

@@ -47,11 +47,10 @@
 #include "launchers.h"
 
 namespace rlb {
-// Defined in norm.cu; launched here through their host stubs.
-__global__ void rmsnorm_bwd_wide(const __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ w,
-                                 const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dy,
-                                 const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
-                                 float* __restrict__ dw_part, long long rows, int dim);
+// Defined in norm.cu: the wide backward's launcher, and the column-sum kernel (launched through its host stub).
+void launch_rmsnorm_bwd_wide(int grid, const __nv_bfloat16* h, const __nv_bfloat16* w, const float* rstd,
+                             const __nv_bfloat16* dy, const __nv_bfloat16* dres, __nv_bfloat16* dx, float* dw_part,
+                             long long rows, int dim, cudaStream_t s);
 __global__ void colsum_kernel(const float* __restrict__ part, int parts, int dim, float* __restrict__ out_f32,
                               __nv_bfloat16* __restrict__ out_bf16);
 }  // namespace rlb
@@ -134,9 +133,9 @@ extern "C" int rlb_rmsnorm_bwd_noalloc(const void* h, const void* w, const float
   if (parts > (long long)sms * 8) parts = (long long)sms * 8;
   if (parts > kScratchFloats / dim) parts = kScratchFloats / dim;
 
-  rlb::rmsnorm_bwd_wide<<<(int)parts, dim / 8, 0, stream>>>(
-      (const __nv_bfloat16*)h, (const __nv_bfloat16*)w, rstd, (const __nv_bfloat16*)dy,
-      (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, scratch, rows, dim);
+  rlb::launch_rmsnorm_bwd_wide((int)parts, (const __nv_bfloat16*)h, (const __nv_bfloat16*)w, rstd,
+                               (const __nv_bfloat16*)dy, (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, scratch, rows,
+                               dim, stream);
   err = cudaGetLastError();
   if (err != cudaSuccess) return err;
   rlb::colsum_kernel<<<(dim + 31) / 32, 256, 0, stream>>>(scratch, (int)parts, dim,

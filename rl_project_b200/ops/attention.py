@@ -5,13 +5,13 @@
 ``q_offset`` for queries that sit after a cached prefix.  Semantics follow
 ``src/forgeline/models/attention/causal.py:79-134``.
 
-On CUDA, the un-windowed, un-capped case runs torch's fused SDPA kernel
-(cuDNN / flash backends); every other case and the CPU path use the explicit
-masked-softmax reference below.  ``fmha_forward`` is this library's own
-sm_100a forward kernel (csrc/fmha_fwd.cu: tcgen05 MMAs, TMEM accumulators,
-TMA loads) and ``fmha_backward`` its backward (csrc/fmha_bwd.cu);
-``RLB_ATTN=tcgen05`` routes attention through them (``fmha``, autograd).
-The default stays SDPA until the kernels have been measured against it.
+``fmha_forward`` is this library's own sm_100a forward kernel (csrc/fmha_fwd.cu:
+tcgen05 MMAs, TMEM accumulators, TMA loads) and ``fmha_backward`` its backward
+(csrc/fmha_bwd.cu); ``fmha`` ties them together for autograd.  On CUDA (bf16,
+head dim 64 or 128) windowed and soft-capped attention always runs on them; the
+plain causal case runs on them when ``RLB_ATTN=tcgen05`` and otherwise on
+torch's fused SDPA kernel (cuDNN / flash backends).  Dropout and the CPU path
+use the explicit masked-softmax reference below.
 """
 
 from __future__ import annotations
@@ -95,11 +95,13 @@ def _token_major(x: torch.Tensor) -> torch.Tensor:
 
 
 def fmha_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
-                 scale: Optional[float] = None, with_lse: bool = False) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+                 scale: Optional[float] = None, with_lse: bool = False, window: int = 0,
+                 softcap: float = 0.0) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
     """Attention forward on the sm_100a kernel.  ``q [B, Hq, T, D]``, ``k [B, Hkv, T, D]``, ``v [B, Hkv, T, DV]``
     (bf16; (D, DV) = (64, 64), (128, 128) or MLA's (192, 128); token-major storage avoids a copy) ->
     ``(out [B, Hq, T, DV]`` as a view of ``[B, T, Hq, DV]`` storage, ``lse [B, Hq, T]`` fp32 natural-log
-    softmax denominators or None)."""
+    softmax denominators or None).  ``window > 0`` keeps keys with ``t - s < window``; ``softcap > 0``
+    replaces each logit ``x`` by ``softcap * tanh(x / softcap)`` (the semantics of ``attention_reference``)."""
     from rl_project_b200.core.errors import KernelError
     from rl_project_b200.ops._ext import native
 
@@ -112,12 +114,13 @@ def fmha_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool
     out = torch.empty(B, T, Hq, DV, dtype=q.dtype, device=q.device)
     lse = torch.empty(B, Hq, T, dtype=torch.float32, device=q.device) if with_lse else torch.empty(0, device=q.device)
     native().fmha_fwd(qt, kt, vt, out, lse, bool(causal), float(scale if scale is not None else D ** -0.5),
-                      _status(q.device))
+                      int(window), float(softcap), _status(q.device))
     return out.transpose(1, 2), (lse if with_lse else None)
 
 
 def fmha_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, dout: torch.Tensor,
-                  lse: torch.Tensor, causal: bool = True, scale: Optional[float] = None):
+                  lse: torch.Tensor, causal: bool = True, scale: Optional[float] = None, window: int = 0,
+                  softcap: float = 0.0):
     """Gradients of ``fmha_forward`` on the sm_100a kernel (csrc/fmha_bwd.cu): ``(dq, dk, dv)`` shaped like
     ``q, k, v`` (``[B, H, T, D]`` views of token-major storage)."""
     from rl_project_b200.ops._ext import native
@@ -129,29 +132,29 @@ def fmha_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.
     dq = torch.empty(qt.shape, dtype=torch.float32, device=q.device)
     dk, dv = torch.empty_like(kt), torch.empty_like(vt)
     native().fmha_bwd(qt, kt, vt, dot, lse.contiguous(), delta, dq, dk, dv, bool(causal),
-                      float(scale if scale is not None else D ** -0.5), _status(q.device))
+                      float(scale if scale is not None else D ** -0.5), int(window), float(softcap), _status(q.device))
     return dq.to(torch.bfloat16).transpose(1, 2), dk.transpose(1, 2), dv.transpose(1, 2)
 
 
 class _FMHA(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, causal, scale):
-        out, lse = fmha_forward(q, k, v, causal, scale, with_lse=True)
+    def forward(ctx, q, k, v, causal, scale, window, softcap):
+        out, lse = fmha_forward(q, k, v, causal, scale, with_lse=True, window=window, softcap=softcap)
         ctx.save_for_backward(q, k, v, out, lse)
-        ctx.causal, ctx.scale = causal, scale
+        ctx.causal, ctx.scale, ctx.window, ctx.softcap = causal, scale, window, softcap
         return out
 
     @staticmethod
     def backward(ctx, dout):
         q, k, v, out, lse = ctx.saved_tensors
-        dq, dk, dv = fmha_backward(q, k, v, out, dout, lse, ctx.causal, ctx.scale)
-        return dq, dk, dv, None, None
+        dq, dk, dv = fmha_backward(q, k, v, out, dout, lse, ctx.causal, ctx.scale, ctx.window, ctx.softcap)
+        return dq, dk, dv, None, None, None, None
 
 
 def fmha(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
-         scale: Optional[float] = None) -> torch.Tensor:
+         scale: Optional[float] = None, window: int = 0, softcap: float = 0.0) -> torch.Tensor:
     """Differentiable attention on the sm_100a forward and backward kernels."""
-    return _FMHA.apply(q, k, v, causal, scale)
+    return _FMHA.apply(q, k, v, causal, scale, int(window), float(softcap))
 
 
 _STATUS: dict = {}
@@ -179,11 +182,14 @@ def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, window: 
                      scale: Optional[float] = None, dropout_p: float = 0.0) -> torch.Tensor:
     """Full-sequence causal attention (no cache).  ``q [B, Hq, T, D]`` (any strides) -> ``[B, Hq, T, D]``."""
     rep = q.shape[1] // k.shape[1]
-    if (_ATTN == "tcgen05" and q.is_cuda and window == 0 and softcap == 0 and dropout_p == 0.0
-            and q.dtype == torch.bfloat16 and q.shape[-1] in (64, 128)):
+    own = (q.is_cuda and dropout_p == 0.0 and q.dtype == torch.bfloat16 and q.shape[-1] in (64, 128)
+           and v.shape[-1] == q.shape[-1])
+    if own and (_ATTN == "tcgen05" or window > 0 or softcap > 0):
+        # windowed / capped attention always runs on the own kernels (the masks are per-element predicates
+        # there, fully masked tiles are skipped); the plain case when RLB_ATTN selects them
         if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
-            return fmha(q, k, v, True, scale)
-        return fmha_forward(q, k, v, True, scale)[0]
+            return fmha(q, k, v, True, scale, window, softcap)
+        return fmha_forward(q, k, v, True, scale, window=window, softcap=softcap)[0]
     if q.is_cuda and window == 0 and softcap == 0:
         return _fused_sdpa(q, k, v, rep, dropout_p, scale)
     if not q.is_cuda and window == 0 and softcap == 0 and dropout_p == 0.0:

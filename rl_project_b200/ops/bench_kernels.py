@@ -238,6 +238,49 @@ MODEL_SHAPES = [
 ]
 
 
+def bench_attention(cases=((8, 4096, 32, 8, 64), (2, 8192, 32, 8, 128))):
+    """Own tcgen05 attention (forward, forward+backward) against torch SDPA (cuDNN) on the model shapes:
+    (batch, T, Hq, Hkv, D).  FLOPs count the causal half: 4 B Hq T^2 D / 2 forward, 2.5x that backward."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    from rl_project_b200.ops import attention as A
+
+    peak_tf, _ = _peaks()
+    for (B, T, Hq, Hkv, D) in cases:
+        mk = lambda h: torch.randn(B, T, h, D, device="cuda").bfloat16().transpose(1, 2)  # noqa: E731
+        q, k, v, do = mk(Hq), mk(Hkv), mk(Hkv), mk(Hq)
+        fl_f = 4.0 * B * Hq * T * T * D / 2
+        fl_b = 2.5 * fl_f
+
+        def ours_f():
+            return A.fmha_forward(q, k, v, True)[0]
+
+        def ref_f():
+            with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+                return torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+
+        out, lse = A.fmha_forward(q, k, v, True, with_lse=True)
+        qs, ks, vs = (x.detach().requires_grad_(True) for x in (q, k, v))
+
+        def ours_b():
+            return A.fmha_backward(q, k, v, out, do, lse, True)
+
+        with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+            ro = torch.nn.functional.scaled_dot_product_attention(qs, ks, vs, is_causal=True, enable_gqa=True)
+
+        def ref_b():
+            return torch.autograd.grad(ro, (qs, ks, vs), do, retain_graph=True)
+
+        err = (ours_f().float() - ref_f().float()).abs().max().item()
+        tf, tr, tbf, tbr = time_ms(ours_f), time_ms(ref_f), time_ms(ours_b), time_ms(ref_b)
+        print(json.dumps({"kernel": "fmha", "B": B, "T": T, "Hq": Hq, "Hkv": Hkv, "D": D, "max_abs_err": err,
+                          "fwd_ms": round(tf, 4), "fwd_tflops": round(fl_f / tf / 1e9, 1),
+                          "fwd_frac_of_measured_bf16": round(fl_f / tf / 1e9 / peak_tf, 3),
+                          "cudnn_fwd_ms": round(tr, 4), "cudnn_fwd_tflops": round(fl_f / tr / 1e9, 1),
+                          "bwd_ms": round(tbf, 4), "bwd_tflops": round(fl_b / tbf / 1e9, 1),
+                          "cudnn_bwd_ms": round(tbr, 4), "cudnn_bwd_tflops": round(fl_b / tbr / 1e9, 1)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--which", default="gemm,mem,adam,paged,sample")
@@ -259,6 +302,10 @@ def main():
         bench_fused_rs()
     if "grouped" in which:
         bench_grouped()
+    if "attn" in which:
+        bench_attention()
+    if "attn1" in which:  # one small case (profiling)
+        bench_attention(((2, 2048, 32, 8, 64),))
 
 
 if __name__ == "__main__":

@@ -205,6 +205,9 @@ class Trainer:
         self._sharded = name in ("fsdp", "zero2", "tensor_parallel", "pipeline_parallel", "hybrid",
                                  "expert_parallel") and world > 1
         self._sync_grads = name == "ddp" and world > 1
+        # per-phase CUDA events of each step (forward, backward, grad_sync, clip, optimizer): off (None) unless a
+        # caller sets a list, which train_step then appends (name, event) pairs to; recording costs no sync
+        self.phase_events: Optional[List[Any]] = None
         if strategy is not None and hasattr(strategy, "prepare_training"):
             strategy.prepare_training(self)
         self.params = [p for p in algorithm.parameters() if p.requires_grad]
@@ -258,6 +261,25 @@ class Trainer:
             m.train(mode)
 
     # ------------------------------------------------------------ one optimizer step
+    def _mark(self, name: str) -> None:
+        if self.phase_events is not None and torch.cuda.is_available() and self.ctx.device.type == "cuda":
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.phase_events.append((name, ev))
+
+    @staticmethod
+    def phase_times(events: List[Any]) -> Dict[str, float]:
+        """Milliseconds per phase from ``phase_events`` (synchronises): the time from each mark to the next is
+        charged to the later mark's phase, summed over steps and micro-batches; ``start`` closes the gap
+        between steps (batch collection, zero_grad)."""
+        if not events:
+            return {}
+        events[-1][1].synchronize()
+        out: Dict[str, float] = {}
+        for (_, a), (name, b) in zip(events, events[1:]):
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return out
+
     def train_step(self) -> StepResult:
         if self.strategy is not None and hasattr(self.strategy, "check_health"):
             self.strategy.check_health()  # a dead peer fails here, before the step's first collective
@@ -267,6 +289,7 @@ class Trainer:
         batch = self.alg.collect(self.step)
         self._tokens += self.alg.tokens_in(batch)
         self.optimizer.zero_grad(set_to_none=True)
+        self._mark("start")
         n_micro = self.cfg.gradient_accumulation_steps
         dev = self.ctx.device
         losses: List[torch.Tensor] = []
@@ -289,10 +312,12 @@ class Trainer:
             with cm, nvtx_range("rlb/forward_backward"):
                 with self.precision.autocast():
                     loss, metrics = self.alg.loss(batch, micro, n_micro)
+                self._mark("forward")
                 if not loss.is_cuda and not bool(torch.isfinite(loss)):
                     raise ConfigError(f"non-finite loss at step {self.step}: {float(loss)}",
                                       hint="Lower the learning rate or check the reward / data pipeline.")
                 self.precision.backward(loss / n_micro)
+                self._mark("backward")
             losses.append(loss.detach().float())
             for k, v in metrics.items():
                 metric_vals.setdefault(k, []).append(_as_tensor(v, dev))
@@ -301,6 +326,7 @@ class Trainer:
                 self.strategy.finish_gradients(self)
             elif self._sync_grads:
                 self._all_reduce_gradients()
+        self._mark("grad_sync")
         max_norm = self.cfg.optimizer.grad_clip
         norm_t: Optional[torch.Tensor] = None
         fused = hasattr(self.optimizer, "clip_grad_norm")
@@ -323,8 +349,10 @@ class Trainer:
         if not fused and not bool(torch.isfinite(loss_mean)):
             raise ConfigError(f"non-finite loss at step {self.step}: {float(loss_mean)}",
                               hint="Lower the learning rate or check the reward / data pipeline.")
+        self._mark("clip")
         with nvtx_range("rlb/optimizer_step"):
             self.precision.step(self.optimizer)
+        self._mark("optimizer")
         # the single host synchronisation of the step
         keys = sorted(metric_vals)
         packed = [loss_mean.to(dev)] + [torch.stack(metric_vals[k]).to(dev).mean() for k in keys]

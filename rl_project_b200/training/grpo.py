@@ -111,7 +111,8 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
         n = len(self.tasks if self.cfg.agent else self.prompts)
         idx = [self.rng.randrange(n) for _ in range(self.cfg.prompts_per_step)]
         if self.cfg.agent:
-            traj_groups = [self.agent_engine.rollout(self.tasks[i], self.cfg.group_size) for i in idx]
+            # every episode of the step advances in one lock-step batch
+            traj_groups = self.agent_engine.rollout_many([self.tasks[i] for i in idx], self.cfg.group_size)
         else:
             traj_groups = self.rollouts.rollout_many([self.prompts[i] for i in idx], [self.tasks[i] for i in idx])
         groups, skipped = [], 0
@@ -139,11 +140,11 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
     @torch.no_grad()
     def _attach_logprobs(self, grp: GRPOGroup) -> None:
         if self.cfg.agent:
-            old = torch.stack([self.agent_engine.trajectory_logprob(t) for t in grp.trajectories]).float().cpu()
+            old = self.agent_engine.trajectories_logprob(grp.trajectories).float().cpu()
             ref = old
             if self._needs_ref:
                 with self.policy.reference():
-                    ref = torch.stack([self.agent_engine.trajectory_logprob(t) for t in grp.trajectories]).float().cpu()
+                    ref = self.agent_engine.trajectories_logprob(grp.trajectories).float().cpu()
             grp.old_logprobs, grp.ref_logprobs = old, ref
             return
         prompt, resp, mask = stack_group(grp.trajectories, self.policy.pad_token_id)
@@ -188,7 +189,7 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
     def _clipped_loss(self, grp: GRPOGroup, adv: torch.Tensor):
         dev = self.policy.device
         if self.cfg.agent:
-            new = torch.stack([self.agent_engine.trajectory_logprob(t) for t in grp.trajectories]).float()
+            new = self.agent_engine.trajectories_logprob(grp.trajectories).float()
             old, ref = grp.old_logprobs.to(dev), grp.ref_logprobs.to(dev)
             pl = ppo_clipped_objective(torch.exp(new - old), adv, self.cfg.clip_ratio).mean()
             kl = (ref - new).clamp(min=0).mean()
@@ -204,7 +205,7 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
 
     def _reinforce_loss(self, grp: GRPOGroup, adv: torch.Tensor) -> torch.Tensor:
         if self.cfg.agent:
-            lp = torch.stack([self.agent_engine.trajectory_logprob(t) for t in grp.trajectories]).float()
+            lp = self.agent_engine.trajectories_logprob(grp.trajectories).float()
             return (-adv * lp).sum()
         prompt, resp, mask = stack_group(grp.trajectories, self.policy.pad_token_id)
         seq_lp = masked_sum(self.policy.logprobs(prompt, resp).float(), mask.to(self.policy.device))

@@ -181,3 +181,57 @@ def test_distillation_with_features(make_ctx, cspec, corpus_dir):
     alg = DistillationAlgorithm(student, TransformerLM(cspec), MemmapCorpus(corpus_dir, "train", 64),
                                 DistillConfig(batch_size=4, feature_weight=0.1))
     assert ok(Trainer(make_ctx("distill", eval_every=0), alg).fit())
+
+
+def test_agent_batched_logprob_matches_per_segment_forwards(char_tok):
+    """One forward over the transcript gives each segment the same log-probs as a forward over its own prefix."""
+    from rl_project_b200.core.protocols import Trajectory
+
+    torch.manual_seed(0)
+    spec = model_spec_from_preset("tiny", vocab_size=char_tok.vocab_size, block_size=256)
+    pol = NativePolicy(TransformerLM(spec), char_tok)
+    eng = AgentRolloutEngine(pol, AgentRolloutConfig(max_context_tokens=100000))
+    trajs = [Trajectory(prompt_ids=torch.zeros(1, dtype=torch.long), response_ids=torch.zeros(1, dtype=torch.long),
+                        prompt_text="Q: 2*3?", response_text="", segments=["<tool_call>x</tool_call>", "ok 6"],
+                        tool_results=["\n<tool_result>\n6\n</tool_result>\n"]),
+             Trajectory(prompt_ids=torch.zeros(1, dtype=torch.long), response_ids=torch.zeros(1, dtype=torch.long),
+                        prompt_text="Q: 1+1, say it", response_text="", segments=["two"], tool_results=[])]
+    got = eng.trajectories_logprob(trajs)
+    with torch.no_grad():
+        for t, g in zip(trajs, got):
+            ctx, seg_means = t.prompt_text, []
+            for i, seg in enumerate(t.segments):
+                q, r = torch.tensor(char_tok.encode(ctx))[None], torch.tensor(char_tok.encode(seg))[None]
+                seg_means.append(pol.logprobs(q, r).float().mean())
+                ctx += seg + (t.tool_results[i] if i < len(t.tool_results) else "")
+            assert abs(float(g) - float(torch.stack(seg_means).mean())) < 1e-4
+    assert abs(float(eng.trajectory_logprob(trajs[1])) - float(got[1])) < 1e-5
+
+
+def test_agent_episodes_advance_in_lockstep_batches(char_tok):
+    """Episodes of equal context length share one generate call per turn; a finished episode drops out."""
+    class Scripted:
+        device = torch.device("cpu")
+        pad_token_id = 0
+
+        def __init__(self):
+            self.batches = []
+
+        def encode(self, t):
+            return char_tok.encode(t)
+
+        def decode(self, ids):
+            return ['<tool_call>{"name": "python_executor", "args": {"code": "print(2)"}}</tool_call>',
+                    "<final_answer>2</final_answer>"][int(ids[0])]
+
+        def generate(self, ids, settings):
+            # turn 1: row 0 calls the tool, row 1 answers; turn 2: the remaining row answers
+            self.batches.append(ids.shape[0])
+            return torch.tensor([[0], [1]] if ids.shape[0] == 2 else [[1]], dtype=torch.long)
+
+    pol = Scripted()
+    out = AgentRolloutEngine(pol, AgentRolloutConfig(max_context_tokens=100000)).run_episodes(["P1", "P2"])
+    assert pol.batches == [2, 1]
+    (segs0, obs0, final0), (segs1, obs1, final1) = out
+    assert len(segs0) == 2 and "2" in obs0[0] and final0.endswith("</final_answer>")
+    assert len(segs1) == 1 and obs1 == []

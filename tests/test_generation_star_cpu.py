@@ -89,25 +89,28 @@ def test_star_answer_extraction():
 
 
 class _ScriptedPolicy:
-    """Answers every prompt with one scripted text per generate call; log-probs come from one parameter."""
+    """Answers the rows of each generate batch with the scripted texts in turn (a row's single token is the index
+    of its text); log-probs come from one parameter."""
 
     device = torch.device("cpu")
     spec = None
 
     def __init__(self, texts):
         self.texts, self.calls = list(texts), 0
+        self.batches = []
         self.w = torch.nn.Parameter(torch.zeros(()))
 
     def encode(self, text):
         return [ord(c) % 97 for c in text]
 
     def decode(self, ids):
-        return self.last
+        return self.texts[int(ids[0])]
 
     def generate(self, ids, settings):
-        self.last = self.texts[self.calls % len(self.texts)]
-        self.calls += 1
-        return torch.zeros(1, 1, dtype=torch.long)
+        self.batches.append(ids.shape[0])
+        rows = [(self.calls + i) % len(self.texts) for i in range(ids.shape[0])]
+        self.calls += ids.shape[0]
+        return torch.tensor(rows, dtype=torch.long)[:, None]
 
     def logprobs(self, q, r):
         return torch.full(r.shape, -1.0) + self.w * 0.0 - (self.w - 1.0) ** 2
@@ -137,6 +140,8 @@ def test_star_keeps_only_correct_rationales(tmp_path):
     kept = tr.generate_rationales()
     # problem "2+3": one of its two samples is right; problem "4+4": neither says 8
     assert [k["answer"] for k in kept] == ["5"] and "<answer>5</answer>" in kept[0]["rationale"]
+    # both problems' prompts have the same length: all four samples came from one batch
+    assert pol.batches == [4]
     w0 = float(pol.w)
     loss = tr.sft_on_rationales(kept)
     assert loss == pytest.approx(2.0) and float(pol.w) > w0  # one step on -mean(logprob) = 1 + (w - 1)^2
