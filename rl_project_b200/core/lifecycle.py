@@ -1,5 +1,11 @@
-"""``RunContext``: seed, device, dtype, output dir, metrics sink and logger of one run
-(``src/forgeline/core/lifecycle.py:19-77``)."""
+"""Run lifecycle: the ``Stage`` names of a post-training pipeline and ``RunContext``, the per-run bundle of
+manifest, seed, device placement, compute dtype, output directory and metrics sink (the contract of
+``src/forgeline/core/lifecycle.py:19-77``).
+
+``RunContext.create`` validates the manifest, seeds every RNG, places the run (device from the manifest or an
+override; the compute dtype the device supports), opens the metrics sink in the output directory and logs one
+``run_context`` line.  A context is also a context manager that closes its sink on exit.
+"""
 
 from __future__ import annotations
 
@@ -7,7 +13,7 @@ import time
 from dataclasses import dataclass, field
 from enum import Enum
 from pathlib import Path
-from typing import Any, Dict, Optional
+from typing import Any, Dict, Optional, Tuple
 
 import torch
 
@@ -16,18 +22,15 @@ from rl_project_b200.core.runtime import resolve_device, resolve_dtype, seed_eve
 from rl_project_b200.observability.logging import get_logger
 from rl_project_b200.observability.metrics import MetricsSink, build_metrics_sink
 
+# pipeline stages, in the order a full run visits them
+Stage = Enum("Stage", [(n.upper(), n) for n in ("data", "pretrain", "sft", "reward_model", "preference", "rl",
+                                                 "evaluation", "export", "serving", "deployment")], type=str)
 
-class Stage(str, Enum):
-    DATA = "data"
-    PRETRAIN = "pretrain"
-    SFT = "sft"
-    REWARD_MODEL = "reward_model"
-    PREFERENCE = "preference"
-    RL = "rl"
-    EVALUATION = "evaluation"
-    EXPORT = "export"
-    SERVING = "serving"
-    DEPLOYMENT = "deployment"
+
+def _placement(manifest: ExperimentManifest, distributed: bool,
+               device_override: Optional[str]) -> Tuple[torch.device, torch.dtype]:
+    device = resolve_device(device_override or manifest.trainer.device, distributed=distributed)
+    return device, resolve_dtype(manifest.trainer.precision.dtype, device)
 
 
 @dataclass
@@ -45,16 +48,16 @@ class RunContext:
     def create(cls, manifest: ExperimentManifest, *, metrics_backend: str = "local", distributed: bool = False,
                device_override: Optional[str] = None) -> "RunContext":
         manifest.validate()
-        seed = manifest.trainer.seed
-        seed_everything(seed)
-        device = resolve_device(device_override or manifest.trainer.device, distributed=distributed)
-        dtype = resolve_dtype(manifest.trainer.precision.dtype, device)
-        out = Path(manifest.output_dir)
-        out.mkdir(parents=True, exist_ok=True)
-        sink = build_metrics_sink(metrics_backend, output_dir=out, run_name=manifest.name, config=manifest.to_dict())
-        get_logger("run").info("run_context", name=manifest.name, algorithm=manifest.algorithm,
-                               device=str(device), dtype=str(dtype), seed=seed, output_dir=str(out))
-        return cls(manifest=manifest, device=device, dtype=dtype, output_dir=out, metrics=sink, seed=seed)
+        seed_everything(manifest.trainer.seed)
+        device, dtype = _placement(manifest, distributed, device_override)
+        root = Path(manifest.output_dir)
+        root.mkdir(parents=True, exist_ok=True)
+        ctx = cls(manifest=manifest, device=device, dtype=dtype, output_dir=root, seed=manifest.trainer.seed,
+                  metrics=build_metrics_sink(metrics_backend, output_dir=root, run_name=manifest.name,
+                                             config=manifest.to_dict()))
+        get_logger("run").info("run_context", name=manifest.name, algorithm=manifest.algorithm, device=str(device),
+                               dtype=str(dtype), seed=ctx.seed, output_dir=str(root))
+        return ctx
 
     @property
     def logger(self):
@@ -65,3 +68,9 @@ class RunContext:
 
     def close(self) -> None:
         self.metrics.close()
+
+    def __enter__(self) -> "RunContext":
+        return self
+
+    def __exit__(self, *exc: Any) -> None:
+        self.close()

@@ -1,14 +1,19 @@
-"""Low-rank adapters ``y = W x + (x A B) * alpha / r`` (``src/forgeline/models/adapters/lora.py``).
+"""Low-rank adapters: ``y = base(x) + scaling * (x A) B`` with ``scaling = alpha / rank`` (the capability of
+``src/forgeline/models/adapters/lora.py``).
 
-``A [in, r]`` Kaiming-initialised, ``B [r, out]`` zero (identity at init);
-``apply_lora`` matches child-module names against ``DEFAULT_TARGET_MODULES``
-by substring and freezes everything else; state is ``{name: {lora_A, lora_B,
-rank, alpha}}``.  Key names are the reference's so adapter checkpoints load.
+``A [in, rank]`` is Kaiming-uniform initialised and ``B [rank, out]`` zero, so a fresh adapter is the identity;
+the parameter names (``lora_A``, ``lora_B``) and the state layout ``{module name: {lora_A, lora_B, rank, alpha}}``
+are the checkpoint format of the reference, so adapter files carry over.
+
+The adapter's contribution joins the base output inside one ``addmm`` (the rank-r product and the add share a
+GEMM epilogue; no separate ``[tokens, out]`` delta tensor is written and re-read).  ``LoRALinear`` and the
+quantised ``QLoRALinear`` share ``LowRankAdapter``; ``swap_linears`` is the one routine that replaces matching
+``nn.Linear`` children, used to attach (``apply_lora``, ``apply_qlora``) and to merge (``merge_lora``).
 """
 
 from __future__ import annotations
 
-from typing import Dict, List, Optional, Sequence
+from typing import Callable, Dict, List, Optional, Sequence
 
 import torch
 import torch.nn as nn
@@ -19,24 +24,40 @@ DEFAULT_TARGET_MODULES: List[str] = ["q_proj", "k_proj", "v_proj", "c_proj", "wq
                                      "wo", "w1", "w2", "w3", "c_fc"]
 
 
-class LoRALinear(nn.Module):
-    def __init__(self, original: nn.Linear, rank: int, alpha: float = 16.0, dropout: float = 0.0):
-        super().__init__()
+class LowRankAdapter(nn.Module):
+    """The trainable low-rank pair around a frozen base layer (``self.base_forward``)."""
+
+    def _init_adapter(self, in_features: int, out_features: int, rank: int, alpha: float, dropout: float,
+                      device, dtype) -> None:
         if rank < 1:
             raise ModelError("LoRA rank must be >= 1")
-        self.original = original
-        self.rank = rank
-        self.alpha = alpha
-        self.scaling = alpha / rank
-        dev, dt = original.weight.device, original.weight.dtype
-        self.lora_A = nn.Parameter(torch.empty(original.in_features, rank, device=dev, dtype=dt))
-        self.lora_B = nn.Parameter(torch.zeros(rank, original.out_features, device=dev, dtype=dt))
-        nn.init.kaiming_uniform_(self.lora_A, a=5 ** 0.5)
-        original.weight.requires_grad = False
-        if original.bias is not None:
-            original.bias.requires_grad = False
+        self.rank, self.alpha, self.scaling = rank, alpha, alpha / rank
+        self.lora_A = nn.Parameter(nn.init.kaiming_uniform_(torch.empty(in_features, rank, device=device, dtype=dtype),
+                                                            a=5 ** 0.5))
+        self.lora_B = nn.Parameter(torch.zeros(rank, out_features, device=device, dtype=dtype))
         self.dropout = nn.Dropout(dropout) if dropout > 0 else nn.Identity()
         self.enabled = True
+
+    def base_forward(self, x: torch.Tensor) -> torch.Tensor:  # pragma: no cover - overridden
+        raise NotImplementedError
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        y = self.base_forward(x)
+        if not self.enabled:
+            return y
+        lead = y.shape[:-1]
+        low = self.dropout(x).reshape(-1, x.shape[-1]) @ self.lora_A.to(x.dtype)
+        out = torch.addmm(y.reshape(-1, y.shape[-1]), low, self.lora_B.to(x.dtype), alpha=self.scaling)
+        return out.view(*lead, out.shape[-1])
+
+
+class LoRALinear(LowRankAdapter):
+    def __init__(self, original: nn.Linear, rank: int, alpha: float = 16.0, dropout: float = 0.0):
+        super().__init__()
+        original.requires_grad_(False)
+        self.original = original
+        w = original.weight
+        self._init_adapter(original.in_features, original.out_features, rank, alpha, dropout, w.device, w.dtype)
 
     @property
     def in_features(self) -> int:
@@ -46,88 +67,86 @@ class LoRALinear(nn.Module):
     def out_features(self) -> int:
         return self.original.out_features
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        y = self.original(x)
-        if not self.enabled:
-            return y
-        return y + (self.dropout(x) @ self.lora_A.to(x.dtype) @ self.lora_B.to(x.dtype)) * self.scaling
+    def base_forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.original(x)
 
     def merge(self) -> nn.Linear:
+        """Fold ``scaling * (A B)^T`` into the base weight and return the base layer."""
         with torch.no_grad():
-            delta = (self.lora_A.float() @ self.lora_B.float()).t() * self.scaling
-            self.original.weight.add_(delta.to(self.original.weight.dtype))
+            w = self.original.weight
+            w.add_(((self.lora_A.float() @ self.lora_B.float()).t() * self.scaling).to(w.dtype))
         return self.original
 
 
-def _children(model: nn.Module):
-    for name, module in model.named_modules():
-        for attr, child in list(module.named_children()):
-            yield name, module, attr, child
+def swap_linears(model: nn.Module, select: Callable[[str, nn.Module], bool],
+                 make: Callable[[nn.Module], nn.Module]) -> int:
+    """Replace every child ``c`` (attribute name ``attr``) with ``select(attr, c)`` by ``make(c)``; returns the count."""
+    swaps = [(parent, attr, child) for parent in model.modules() for attr, child in parent.named_children()
+             if select(attr, child)]
+    for parent, attr, child in swaps:
+        setattr(parent, attr, make(child))
+    return len(swaps)
 
 
-def apply_lora(model: nn.Module, rank: int = 16, alpha: float = 32.0, dropout: float = 0.0,
-               target_modules: Optional[Sequence[str]] = None) -> nn.Module:
-    targets = list(target_modules) if target_modules else DEFAULT_TARGET_MODULES
-    for p in model.parameters():
-        p.requires_grad = False
-    hit = 0
-    for _, parent, attr, child in _children(model):
-        if isinstance(child, nn.Linear) and any(t in attr for t in targets):
-            setattr(parent, attr, LoRALinear(child, rank, alpha, dropout))
-            hit += 1
-    if not hit:
+def attach_adapters(model: nn.Module, target_modules: Optional[Sequence[str]],
+                    make: Callable[[nn.Linear], nn.Module]) -> nn.Module:
+    """Freeze ``model`` and wrap every ``nn.Linear`` whose attribute name contains a target substring."""
+    targets = list(target_modules) if target_modules else list(DEFAULT_TARGET_MODULES)
+    model.requires_grad_(False)
+    hits = swap_linears(model, lambda attr, c: isinstance(c, nn.Linear) and any(t in attr for t in targets), make)
+    if not hits:
         raise ModelError(f"No linear layers matched target_modules={targets}")
     return model
 
 
+def apply_lora(model: nn.Module, rank: int = 16, alpha: float = 32.0, dropout: float = 0.0,
+               target_modules: Optional[Sequence[str]] = None) -> nn.Module:
+    return attach_adapters(model, target_modules, lambda lin: LoRALinear(lin, rank, alpha, dropout))
+
+
 def merge_lora(model: nn.Module) -> nn.Module:
-    for _, parent, attr, child in _children(model):
-        if isinstance(child, LoRALinear):
-            lin = child.merge()
-            lin.weight.requires_grad = True
-            if lin.bias is not None:
-                lin.bias.requires_grad = True
-            setattr(parent, attr, lin)
+    def unwrap(adapter: nn.Module) -> nn.Module:
+        return adapter.merge().requires_grad_(True)
+
+    swap_linears(model, lambda _attr, c: isinstance(c, LoRALinear), unwrap)
     return model
 
 
-def _is_adapter(m: nn.Module) -> bool:
-    return hasattr(m, "lora_A") and hasattr(m, "lora_B") and hasattr(m, "enabled")
+def _adapters(model: nn.Module) -> Dict[str, LowRankAdapter]:
+    return {n: m for n, m in model.named_modules() if isinstance(m, LowRankAdapter)}
 
 
 def set_lora_enabled(model: nn.Module, enabled: bool) -> None:
-    for m in model.modules():
-        if _is_adapter(m):
-            m.enabled = enabled
+    for m in _adapters(model).values():
+        m.enabled = enabled
 
 
 def lora_state_dict(model: nn.Module) -> Dict[str, Dict[str, object]]:
     return {n: {"lora_A": m.lora_A.detach().clone(), "lora_B": m.lora_B.detach().clone(), "rank": m.rank,
-                "alpha": m.alpha} for n, m in model.named_modules() if _is_adapter(m)}
+                "alpha": m.alpha} for n, m in _adapters(model).items()}
 
 
 def load_lora_state_dict(model: nn.Module, state: Dict[str, Dict[str, object]], strict: bool = True) -> int:
-    mods = {n: m for n, m in model.named_modules() if _is_adapter(m)}
-    n_loaded = 0
-    for name, entry in state.items():
-        if name not in mods:
-            if strict:
-                raise ModelError(f"LoRA state contains layer {name!r} that the model does not have")
-            continue
-        m = mods[name]
+    live = _adapters(model)
+    unknown = [n for n in state if n not in live]
+    if unknown and strict:
+        raise ModelError(f"LoRA state contains layer {unknown[0]!r} that the model does not have")
+    loaded = 0
+    for name in (n for n in state if n in live):
+        entry, m = state[name], live[name]
         if m.rank != entry["rank"]:
             raise ModelError(f"LoRA rank mismatch for {name}: model {m.rank} vs state {entry['rank']}")
         with torch.no_grad():
             m.lora_A.copy_(entry["lora_A"])
             m.lora_B.copy_(entry["lora_B"])
-        n_loaded += 1
-    return n_loaded
+        loaded += 1
+    return loaded
 
 
 def save_lora(model: nn.Module, path: str) -> int:
-    st = lora_state_dict(model)
-    torch.save(st, path)
-    return sum(int(s["lora_A"].numel() + s["lora_B"].numel()) for s in st.values())
+    state = lora_state_dict(model)
+    torch.save(state, path)
+    return sum(int(e["lora_A"].numel() + e["lora_B"].numel()) for e in state.values())
 
 
 def load_lora(model: nn.Module, path: str, device: Optional[str] = None) -> int:
@@ -135,6 +154,7 @@ def load_lora(model: nn.Module, path: str, device: Optional[str] = None) -> int:
 
 
 def trainable_parameter_report(model: nn.Module) -> Dict[str, float]:
-    total = sum(p.numel() for p in model.parameters())
-    train = sum(p.numel() for p in model.parameters() if p.requires_grad)
+    counts = [(p.numel(), p.requires_grad) for p in model.parameters()]
+    total = sum(n for n, _ in counts)
+    train = sum(n for n, g in counts if g)
     return {"total": total, "trainable": train, "fraction": train / max(total, 1)}

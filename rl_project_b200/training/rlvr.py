@@ -1,4 +1,11 @@
-"""RLVR: GRPO or DAPO driven by deterministic verifiers (``src/forgeline/training/rlvr.py``)."""
+"""RLVR: policy optimisation against deterministic verifiers (the capability of
+``src/forgeline/training/rlvr.py``).
+
+An RLVR run is GRPO or DAPO whose reward is a verifier's pass/fail score on each task's target
+(``answer``, or ``test_code`` for code tasks), optionally blended with a format check.  The pieces are
+looked up in two tables below rather than branched on; ``evaluate_pass_rate`` answers every evaluation
+task in one batched rollout call and scores the whole batch.
+"""
 
 from __future__ import annotations
 
@@ -14,6 +21,10 @@ from rl_project_b200.rollouts.verifiers import FormatVerifier, build_verifier
 from rl_project_b200.training.dapo import DAPOAlgorithm, DAPOConfig
 from rl_project_b200.training.grpo import GRPOAlgorithm, GRPOConfig
 
+# task type -> the task field its verifier checks the response against
+TARGET_FIELD: Dict[str, str] = {"math": "answer", "code": "test_code", "tagged_answer": "answer",
+                                "exact_match": "answer", "last_token_parity": "answer"}
+
 
 @dataclass
 class RLVRConfig:
@@ -28,48 +39,50 @@ class RLVRConfig:
     dapo: DAPOConfig = field(default_factory=DAPOConfig)
 
     def validate(self) -> None:
-        if self.optimizer not in ("dapo", "grpo"):
-            raise ConfigError("RLVR optimizer must be dapo|grpo")
-        if self.task_type not in ("math", "code", "tagged_answer", "exact_match", "last_token_parity"):
-            raise ConfigError("task_type must be math|code|tagged_answer|exact_match|last_token_parity")
+        if self.optimizer not in _ALGORITHMS:
+            raise ConfigError(f"RLVR optimizer must be {'|'.join(_ALGORITHMS)}")
+        if self.task_type not in TARGET_FIELD:
+            raise ConfigError(f"task_type must be {'|'.join(TARGET_FIELD)}")
 
 
 def build_verifiable_reward(cfg: RLVRConfig):
-    key = "test_code" if cfg.task_type == "code" else "answer"
-    correct = VerifierReward(build_verifier(cfg.task_type, **cfg.verifier_params), target_key=key)
+    """The verifier's score on the task target, or its weighted blend with the format check."""
+    correctness = VerifierReward(build_verifier(cfg.task_type, **cfg.verifier_params),
+                                 target_key=TARGET_FIELD[cfg.task_type])
     if not cfg.require_format:
-        return correct
-    fmt = VerifierReward(FormatVerifier(cfg.format_spec), target_key="format_spec")
-    return CompositeReward([(correct, cfg.correctness_weight), (fmt, cfg.format_weight)], name="rlvr")
+        return correctness
+    layout = VerifierReward(FormatVerifier(cfg.format_spec), target_key="format_spec")
+    return CompositeReward([(correctness, cfg.correctness_weight), (layout, cfg.format_weight)], name="rlvr")
+
+
+# optimizer name -> (algorithm class, the RLVRConfig field holding its config)
+_ALGORITHMS = {"dapo": (DAPOAlgorithm, "dapo"), "grpo": (GRPOAlgorithm, "grpo")}
 
 
 def build_rlvr_algorithm(policy, tasks: Sequence, cfg: RLVRConfig, rollout: Optional[RolloutConfig] = None):
     cfg.validate()
-    reward = build_verifiable_reward(cfg)
-    task_dicts = [t.to_dict() for t in tasks]
-    for d in task_dicts:
-        d.setdefault("format_spec", cfg.format_spec)
+    records = [{"format_spec": cfg.format_spec, **t.to_dict()} for t in tasks]
     prompts = [torch.tensor(policy.encode(t.prompt), dtype=torch.long) for t in tasks]
-    alg = (DAPOAlgorithm(policy, prompts, reward, cfg.dapo, rollout, tasks=task_dicts) if cfg.optimizer == "dapo"
-           else GRPOAlgorithm(policy, prompts, reward, cfg.grpo, rollout, tasks=task_dicts))
-    alg.name = "rlvr"
-    return alg
+    cls, sub = _ALGORITHMS[cfg.optimizer]
+    algorithm = cls(policy, prompts, build_verifiable_reward(cfg), getattr(cfg, sub), rollout, tasks=records)
+    algorithm.name = "rlvr"
+    return algorithm
 
 
 @torch.no_grad()
 def evaluate_pass_rate(policy, tasks: Sequence, reward, max_new_tokens: int = 64, temperature: float = 0.0,
                        limit: Optional[int] = None) -> Dict[str, float]:
+    """Pass rate, mean reward and malformed-answer rate of one sampled answer per task (all tasks in one batched
+    rollout).  An answer is malformed when the verifier could not extract a prediction or raised."""
+    chosen = list(tasks)[: limit or None]
+    if not chosen:
+        return {"pass_rate": 0.0, "reward": 0.0, "malformed_rate": 0.0, "n": 0}
     engine = RolloutEngine(policy, RolloutConfig(group_size=1, max_new_tokens=max_new_tokens, temperature=temperature,
                                                  record_old_logprobs=False))
-    n = passed = malformed = 0
-    total = 0.0
-    for task in list(tasks)[: limit or None]:
-        t = engine.rollout(torch.tensor(policy.encode(task.prompt)), task.to_dict())[0]
-        r = reward.score(t)
-        n += 1
-        total += r.value
-        passed += int(bool(r.passed))
-        if r.info.get("predicted", "x") is None or "error" in r.info:
-            malformed += 1
-    return {"pass_rate": passed / max(n, 1), "reward": total / max(n, 1), "malformed_rate": malformed / max(n, 1),
-            "n": n}
+    groups = engine.rollout_many([torch.tensor(policy.encode(t.prompt), dtype=torch.long) for t in chosen],
+                                 [t.to_dict() for t in chosen])
+    scores = [reward.score(grp[0]) for grp in groups]
+    n = len(scores)
+    malformed = sum(1 for s in scores if s.info.get("predicted", "x") is None or "error" in s.info)
+    return {"pass_rate": sum(bool(s.passed) for s in scores) / n, "reward": sum(s.value for s in scores) / n,
+            "malformed_rate": malformed / n, "n": n}

@@ -235,3 +235,39 @@ def test_agent_episodes_advance_in_lockstep_batches(char_tok):
     (segs0, obs0, final0), (segs1, obs1, final1) = out
     assert len(segs0) == 2 and "2" in obs0[0] and final0.endswith("</final_answer>")
     assert len(segs1) == 1 and obs1 == []
+
+
+def test_rlvr_pass_rate_scores_one_batched_answer_per_task(cspec, char_tok):
+    from rl_project_b200.training.rlvr import RLVRConfig, build_verifiable_reward, evaluate_pass_rate
+
+    pol = NativePolicy(TransformerLM(cspec), char_tok)
+    tasks = [VerifiableTask(prompt=f"What is {i}+1?", answer=str(i + 1)) for i in range(5)]
+    res = evaluate_pass_rate(pol, tasks, build_verifiable_reward(RLVRConfig(task_type="math")), max_new_tokens=4,
+                             limit=3)
+    assert res["n"] == 3 and 0.0 <= res["pass_rate"] <= 1.0 and 0.0 <= res["malformed_rate"] <= 1.0
+    assert evaluate_pass_rate(pol, [], build_verifiable_reward(RLVRConfig()))["n"] == 0
+
+
+def test_distillation_loss_value_and_gradient_match_autograd(monkeypatch):
+    """The chunked op with its analytic gradient equals the plain autograd formula (several row chunks)."""
+    import torch.nn.functional as F
+
+    from rl_project_b200.training import distill
+
+    monkeypatch.setattr(distill, "_CHUNK_ELEMS", 3 * 50)  # 3 rows per chunk
+    torch.manual_seed(0)
+    s = torch.randn(2, 5, 50, dtype=torch.float64, requires_grad=True)
+    t = torch.randn(2, 5, 50, dtype=torch.float64)
+    y = torch.randint(0, 50, (2, 5))
+    y[0, :2] = -1
+    T, a = 3.0, 0.6
+    got = distill.distillation_loss(s, t, y, T, a)
+    (g_got,) = torch.autograd.grad(2.0 * got, s)
+    s2 = s.detach().clone().requires_grad_(True)
+    kl = F.kl_div(F.log_softmax(s2.reshape(-1, 50) / T, -1), F.softmax(t.reshape(-1, 50) / T, -1),
+                  reduction="batchmean") * T ** 2
+    ref = a * kl + (1 - a) * F.cross_entropy(s2.reshape(-1, 50), y.reshape(-1), ignore_index=-1)
+    (g_ref,) = torch.autograd.grad(2.0 * ref, s2)
+    # the op works in fp32 whatever the input dtype
+    assert abs(float(got) - float(ref)) < 1e-5 * abs(float(ref))
+    assert torch.allclose(g_got, g_ref, atol=1e-7)
