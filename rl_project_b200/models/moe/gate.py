@@ -101,6 +101,20 @@ class ExpertGate(nn.Module):
         return w.type_as(x), idx
 
 
+def share_router_counts(modules, group) -> int:
+    """Make every aux-loss-free router in ``modules`` update its bias from the counts summed over ``group`` (the
+    data-parallel ranks that route different tokens through the same layers): replicas then keep identical
+    biases, and the step equals that of one process routing the whole global batch.  Returns the number of
+    routers attached."""
+    n = 0
+    for m in modules:
+        for sub in (m.modules() if m is not None else ()):
+            if isinstance(sub, ExpertGate):
+                sub.count_group = group
+                n += 1
+    return n
+
+
 class _FusedRoute(torch.autograd.Function):
     """Router kernel forward; backward recomputes the (small) score -> weight graph in PyTorch."""
 

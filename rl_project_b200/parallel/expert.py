@@ -166,10 +166,12 @@ class ExpertParallelStrategy:
         for blk in model.transformer.h:
             if isinstance(blk.ffn, MoELayer):
                 shard_experts(blk.ffn, self.ep_group, rt.rank() % ep, ep)
-                blk.ffn.gate.count_group = dist.group.WORLD
                 n += 1
         if n == 0:
             raise DistributedConfigError("expert_parallel needs a model with MoE layers")
+        from rl_project_b200.models.moe.gate import share_router_counts
+
+        share_router_counts([model], dist.group.WORLD)  # every rank routes its own tokens
         self.model = model
         from rl_project_b200.parallel.weight_sync import broadcast_parameters
 

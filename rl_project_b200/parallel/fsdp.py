@@ -149,6 +149,9 @@ class FSDPStrategy(_ProcessGroupStrategy):
         from rl_project_b200.parallel.weight_sync import broadcast_parameters
 
         broadcast_parameters([p.data for m in mods for p in m.parameters() if p.requires_grad], self.group)
+        from rl_project_b200.models.moe.gate import share_router_counts
+
+        share_router_counts(mods, self.group)  # MoE routers keep identical aux-free biases on every rank
         seen = set()
         for mi, m in enumerate(mods):
             blocks = list(m.transformer.h) if hasattr(m, "transformer") and hasattr(m.transformer, "h") else []

@@ -144,6 +144,9 @@ class MeshStrategy:
             self.runner = PipelineRunner(model, m.pp_rank, m.pp_size, m.prev_stage, m.next_stage)
         self.model = model
         if m.dp_size > 1:
+            from rl_project_b200.models.moe.gate import share_router_counts
+
+            share_router_counts([model], self._group("dp"))  # tensor-parallel peers already route alike
             src = m.dp_ranks()[0]
             with torch.no_grad():
                 for p in model.parameters():

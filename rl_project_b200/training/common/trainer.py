@@ -215,6 +215,9 @@ class Trainer:
             raise ConfigError("algorithm exposes no trainable parameters")
         if self._sync_grads:
             self._broadcast_parameters()
+            from rl_project_b200.models.moe.gate import share_router_counts
+
+            share_router_counts(getattr(self.alg, "modules", lambda: ())(), torch.distributed.group.WORLD)
         if self.cfg.compile_model:
             self._compile_modules()
         if strategy is not None and hasattr(strategy, "build_optimizer"):
