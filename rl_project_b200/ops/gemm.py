@@ -40,13 +40,15 @@ def _pairs(device_index: int) -> int:
     return _CLUSTERS[device_index]
 
 
-def nsub_for(M: int, N: int, epi: int, device_index: int = 0) -> int:
+def nsub_for(M: int, N: int, epi: int, device_index: int = 0, a_mn: int = 0) -> int:
     """Tile width of the 2-SM kernel for a product.  256 x 512 tiles (one A slice feeds two MMAs: a quarter
-    fewer operand bytes) unless the output is fp32, too narrow, or their last wave of CTA pairs would leave
-    clearly more of the GPU idle than 256 x 256 tiles (double-buffered accumulators) do."""
+    fewer operand bytes) unless the output is fp32, too narrow, A is read MN-major (the weight-gradient
+    layout, measured faster with 256 x 256 tiles and their double-buffered accumulators: 1.02x against 0.89x
+    of cuBLAS on the 1B model's 16384 x 2048 x 32768 weight gradient), or their last wave of CTA pairs would
+    leave clearly more of the GPU idle than 256 x 256 tiles do."""
     if _NSUB:
         return _NSUB
-    if epi != 0 or N <= 256:
+    if epi != 0 or N <= 256 or a_mn:
         return 1
     pairs = _pairs(device_index)
 
@@ -63,7 +65,7 @@ def _run(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha):
         native().gemm(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None)
     else:
         native().gemm2(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None, 0,
-                       nsub_for(M, N, epi, a.device.index or 0))
+                       nsub_for(M, N, epi, a.device.index or 0, a_mn))
 
 
 def _ok_ptr(t: torch.Tensor) -> bool:

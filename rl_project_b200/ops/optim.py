@@ -10,14 +10,16 @@ Adam as configured by ``src/forgeline/training/common/optim.py:11-30``.
 
 from __future__ import annotations
 
-import struct
 from typing import Dict, Iterable, List, Optional
 
+import numpy as np
 import torch
 
 from rl_project_b200.ops._ext import native
 
-_DESC = struct.Struct("<QQQQQqfi")  # must equal sizeof(AdamTensor) in csrc/adamw.cu
+# one AdamTensor of csrc/adamw.cu (packed, 56 bytes)
+_DESC = np.dtype([("master", "<u8"), ("p16", "<u8"), ("grad", "<u8"), ("m", "<u8"), ("v", "<u8"), ("n", "<i8"),
+                  ("wd", "<f4"), ("gb", "<i4")])
 
 
 class FusedAdamW(torch.optim.Optimizer):
@@ -38,6 +40,9 @@ class FusedAdamW(torch.optim.Optimizer):
         self._flat: Dict[str, torch.Tensor] = {}
         self._desc_key = None
         self._desc = None
+        self._host_desc = None
+        self._entry_param = self._entry_goff = self._entry_grads = None
+        self._grad_mask = None
         self._chunks = None
         self._nchunks = 0
         self._partial = None
@@ -67,55 +72,74 @@ class FusedAdamW(torch.optim.Optimizer):
             st["master"].copy_(p.detach().float())
             st["exp_avg"] = self._flat["exp_avg"][off:off + n].view_as(p)
             st["exp_avg_sq"] = self._flat["exp_avg_sq"][off:off + n].view_as(p)
-            st["step"] = torch.zeros((), dtype=torch.float32)
             off += n
+        # per-parameter step counts (a parameter without a gradient in a step is not stepped), kept as one
+        # array and written into the state only when it is serialised
+        self._param_index = {id(p): i for i, p in enumerate(ps)}
+        self._param_steps = np.zeros(len(ps), dtype=np.int64)
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
         self._partial = torch.empty(sms * 8, dtype=torch.float32, device=dev)
         self.norm_coef = torch.zeros(2, dtype=torch.float32, device=dev)
 
     def _build_desc(self) -> None:
+        """Device descriptors of every gradient-carrying tensor segment and the chunk list of the kernels.
+
+        The layout (which segments, their master / moment / bf16 pointers, sizes, decays, the chunk list)
+        only changes when the parameter set, a parameter's storage or a gradient dtype changes; it is then
+        rebuilt, the chunk list generated with numpy.  Gradient tensors are usually new every step
+        (``zero_grad(set_to_none=True)``): their pointers are patched into the host copy of the descriptors
+        and the ~50 bytes per segment re-uploaded, nothing else."""
+        ps = [p for g in self.param_groups for p in g["params"] if p.grad is not None]
+        layout = tuple((id(p), p.data_ptr(), p.grad.dtype, p.grad.is_contiguous()) for p in ps) + tuple(
+            a.data_ptr() for a in self._param16.values())
+        if layout != self._desc_key:
+            self._layout(ps)
+            self._desc_key = layout
+        gptr = np.fromiter((p.grad.data_ptr() for p in ps), dtype=np.uint64, count=len(ps))
+        grads = gptr[self._entry_param] + self._entry_goff
+        if self._entry_grads is None or not np.array_equal(grads, self._entry_grads):
+            self._host_desc["grad"] = grads
+            self._entry_grads = grads
+            self._desc = torch.from_numpy(self._host_desc.view(np.uint8)).to(ps[0].device, non_blocking=False)
+
+    def _layout(self, ps: List[torch.nn.Parameter]) -> None:
         C = native()
         chunk = C.adam_chunk_size()
-        assert C.adam_tensor_desc_bytes() == _DESC.size
-        ps, wds, raw, chunks = [], [], bytearray(), []
-        for g in self.param_groups:
-            for p in g["params"]:
-                if p.grad is None:
-                    continue
-                ps.append(p)
-                wds.append(float(g["weight_decay"]))
-        key = tuple((p.data_ptr(), p.grad.data_ptr(), p.grad.dtype) for p in ps) + tuple(
-            (a.data_ptr(),) for a in self._param16.values())
-        if key == self._desc_key:
-            return
-        entry = 0
-        for p, wd in zip(ps, wds):
-            st = self.state[p]
-            g = p.grad
+        assert C.adam_tensor_desc_bytes() == _DESC.itemsize
+        wd_of = {id(p): float(g["weight_decay"]) for g in self.param_groups for p in g["params"]}
+        rows, owner, goff = [], [], []
+        for k, p in enumerate(ps):
+            st, g = self.state[p], p.grad
             if not g.is_contiguous():
                 raise RuntimeError("FusedAdamW needs contiguous gradients")
             if p.dtype not in (torch.bfloat16, torch.float32):
                 raise RuntimeError(f"unsupported parameter dtype {p.dtype}")
             if p.dtype == torch.float32:
-                # fp32 parameters: the parameter itself is the master copy
-                st["master"] = p.data
+                st["master"] = p.data  # fp32 parameters: the parameter itself is the master copy
             alias = self._param16.get(p)
             p16 = alias if alias is not None else (p if p.dtype == torch.bfloat16 else None)
-            gb = 1 if g.dtype == torch.bfloat16 else 0
-            for (a, b, seg_wd) in self._segments.get(p, [(0, p.numel(), wd)]):
+            for (a, b, seg_wd) in self._segments.get(p, [(0, p.numel(), wd_of[id(p)])]):
                 if b <= a:
                     continue
-                raw += _DESC.pack(st["master"].data_ptr() + 4 * a, (p16.data_ptr() + 2 * a) if p16 is not None else 0,
-                                  g.data_ptr() + g.element_size() * a, st["exp_avg"].data_ptr() + 4 * a,
-                                  st["exp_avg_sq"].data_ptr() + 4 * a, b - a, float(seg_wd), gb)
-                for c in range((b - a + chunk - 1) // chunk):
-                    chunks.extend((entry, c))
-                entry += 1
+                rows.append((st["master"].data_ptr() + 4 * a, (p16.data_ptr() + 2 * a) if p16 is not None else 0, 0,
+                             st["exp_avg"].data_ptr() + 4 * a, st["exp_avg_sq"].data_ptr() + 4 * a, b - a,
+                             float(seg_wd), 1 if g.dtype == torch.bfloat16 else 0))
+                owner.append(k)
+                goff.append(g.element_size() * a)
+        self._host_desc = np.array(rows, dtype=_DESC)
+        self._entry_param = np.asarray(owner, dtype=np.int64)
+        self._entry_goff = np.asarray(goff, dtype=np.uint64)
+        self._entry_grads = None
+        # chunk list: (segment, chunk within segment) for every chunk of every segment
+        per = (self._host_desc["n"] + chunk - 1) // chunk
+        seg = np.repeat(np.arange(len(rows), dtype=np.int32), per)
+        first = np.repeat(np.cumsum(per) - per, per)
+        pairs = np.stack([seg, (np.arange(seg.size) - first).astype(np.int32)], 1)
         dev = ps[0].device
-        self._desc = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(dev)
-        self._chunks = torch.tensor(chunks, dtype=torch.int32).to(dev)
-        self._nchunks = len(chunks) // 2
-        self._desc_key = key
+        self._chunks = torch.from_numpy(np.ascontiguousarray(pairs)).reshape(-1).to(dev)
+        self._nchunks = int(seg.size)
+        self._grad_mask = np.zeros(len(self._param_index), dtype=bool)
+        self._grad_mask[[self._param_index[id(p)] for p in ps]] = True
 
     # ------------------------------------------------------------------ step
     @torch.no_grad()
@@ -161,10 +185,7 @@ class FusedAdamW(torch.optim.Optimizer):
         if len(lrs) != 1:
             raise RuntimeError("FusedAdamW expects one learning rate for all groups")
         b1, b2 = g0["betas"]
-        for g in self.param_groups:
-            for p in g["params"]:
-                if p.grad is not None:
-                    self.state[p]["step"] += 1
+        self._param_steps += self._grad_mask
         native().adam_step(self._desc, self._chunks, self._nchunks, self.norm_coef, float(g0["lr"]), float(b1),
                            float(b2), float(g0["eps"]), self._step, self.decoupled)
         if self._post_step is not None:
@@ -176,6 +197,8 @@ class FusedAdamW(torch.optim.Optimizer):
 
     # ------------------------------------------------------------------ (de)serialisation
     def state_dict(self):
+        for p, n in zip(self._params(), self._param_steps):
+            self.state[p]["step"] = torch.tensor(float(n))
         sd = super().state_dict()
         # detach views from the flat buffers so a checkpoint stores each tensor once
         for st in sd["state"].values():
@@ -197,7 +220,7 @@ class FusedAdamW(torch.optim.Optimizer):
                 elif k == "master":
                     st[k].copy_(p.detach().float())
             if "step" in src:
-                st["step"] = torch.as_tensor(src["step"], dtype=torch.float32).clone()
+                self._param_steps[i] = int(float(src["step"]))
         for g, sg in zip(self.param_groups, state_dict.get("param_groups", [])):
             for k, v in sg.items():
                 if k != "params":

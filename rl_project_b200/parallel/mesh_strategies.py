@@ -141,7 +141,8 @@ class MeshStrategy:
                 raise DistributedConfigError(f"pipeline parallelism needs an algorithm with pipeline_inputs "
                                              f"(pretrain, sft); got {trainer.alg.name}")
             partition_model(model, m.pp_rank, m.pp_size)
-            self.runner = PipelineRunner(model, m.pp_rank, m.pp_size, m.prev_stage, m.next_stage)
+            self.runner = PipelineRunner(model, m.pp_rank, m.pp_size, m.prev_stage, m.next_stage,
+                                         groups=m.groups)
         self.model = model
         if m.dp_size > 1:
             from rl_project_b200.models.moe.gate import share_router_counts

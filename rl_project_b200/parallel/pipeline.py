@@ -6,14 +6,25 @@ checkpoints of all stages tile the full model); the first stage keeps the
 embedding, the last the final norm and LM head (and, with tied embeddings, a
 copy of the embedding whose gradient is summed with the first stage's).
 
-``run_1f1b`` drives ``n_micro`` micro-batches through the pipeline: stage s
-runs ``min(P - s - 1, n_micro)`` warm-up forwards, then alternates one forward
-/ one backward, then drains the remaining backwards.  Activations go forward
-and activation gradients go backward as point-to-point messages (non-blocking
-sends, blocking receives, tagged by micro-batch), so every stage's parameters
-receive gradients -- unlike ``src/forgeline/distributed/pipeline_parallel.py``,
-whose scheduler ran the backward on the last stage only.  Messages use the
-compute dtype (bf16 on GPU).
+``PipelineRunner`` drives ``n_micro`` micro-batches through the pipeline with
+the 1F1B schedule: stage s runs ``min(P - s - 1, n_micro)`` warm-up forwards,
+then alternates one forward / one backward, then drains the remaining
+backwards.  Activations go forward and activation gradients go backward as
+point-to-point messages, so every stage's parameters receive gradients --
+unlike ``src/forgeline/distributed/pipeline_parallel.py``, whose scheduler ran
+the backward on the last stage only.  Messages use the compute dtype (bf16 on
+GPU).
+
+Overlap: given one process group per direction of each stage pair (the mesh
+builds them), the runner keeps ``lookahead`` receives posted in each
+direction -- the activations of the next forwards and the gradients of the
+next backwards -- so a transfer runs on the communicator's stream while the
+stage computes the micro-batch before it; waiting on a receive makes the
+compute stream wait, not the host.  Each directional group carries one
+sender's messages in the order the receiver consumes them, which is what lets
+receives be posted early (on a shared group, an early receive could be
+matched ahead of a send the peer is blocked on).  Without directional groups
+the runner posts each receive when it is needed, on the default group.
 """
 
 from __future__ import annotations
@@ -91,41 +102,74 @@ def schedule_1f1b(n_micro: int, stage: int, n_stages: int) -> List[Tuple[str, in
     return steps
 
 
+class _Inbox:
+    """Receives of one direction, posted up to ``depth`` messages ahead in the order they will be consumed."""
+
+    def __init__(self, src: Optional[int], group: Any, order: List[int], tag_of, depth: int):
+        self.src, self.group, self.order, self.tag_of, self.depth = src, group, order, tag_of, depth
+        self.posted: Dict[int, Tuple[torch.Tensor, Any]] = {}
+        self.next = 0  # index into `order` of the next receive to post
+
+    def _post(self, shape, dtype, device) -> None:
+        i = self.order[self.next]
+        self.next += 1
+        buf = torch.empty(shape, dtype=dtype, device=device)
+        self.posted[i] = (buf, dist.irecv(buf, src=self.src, tag=self.tag_of(i), group=self.group))
+
+    def take(self, i: int, shape, dtype, device) -> torch.Tensor:
+        while i not in self.posted:
+            self._post(shape, dtype, device)
+        buf, work = self.posted.pop(i)
+        # keep `depth` receives in flight behind this one (they land while this micro-batch computes)
+        while self.depth and self.next < len(self.order) and len(self.posted) < self.depth:
+            self._post(shape, dtype, device)
+        work.wait()  # NCCL: the compute stream waits for the transfer; gloo: the host waits
+        return buf
+
+
 class PipelineRunner:
     """Runs the 1F1B schedule of one stage for one optimiser step."""
 
     def __init__(self, model: nn.Module, stage: int, n_stages: int, prev_rank: Optional[int],
-                 next_rank: Optional[int], group: Any = None):
+                 next_rank: Optional[int], group: Any = None, groups: Optional[Dict[str, Any]] = None,
+                 lookahead: int = 2):
         self.model, self.stage, self.n_stages = model, stage, n_stages
         self.prev, self.next, self.group = prev_rank, next_rank, group
         self.first, self.last = stage == 0, stage == n_stages - 1
+        g = groups or {}
+        directional = all(g.get(k) is not None for k in
+                          ([] if self.first else ["pp_act_in", "pp_grad_out"]) +
+                          ([] if self.last else ["pp_act_out", "pp_grad_in"]))
+        self.groups = g if directional else {}
+        self.lookahead = lookahead if directional else 0
 
-    def _recv(self, shape, dtype, device, src: int, tag: int) -> torch.Tensor:
-        t = torch.empty(shape, dtype=dtype, device=device)
-        dist.recv(t, src=src, tag=tag)
-        return t
+    def _g(self, name: str):
+        return self.groups.get(name, self.group)
 
     def run(self, micro_inputs: Sequence[Tuple[torch.Tensor, torch.Tensor]], act_shape: Tuple[int, ...],
             dtype: torch.dtype, device: torch.device, scale: float) -> torch.Tensor:
         """``micro_inputs[i] = (idx, targets)``; returns the summed scaled loss (last stage) or 0."""
         n = len(micro_inputs)
+        steps = schedule_1f1b(n, self.stage, self.n_stages)
+        acts = None if self.first else _Inbox(self.prev, self._g("pp_act_in"), [i for k, i in steps if k == "F"],
+                                              lambda i: 2 * i, self.lookahead)
+        grads = None if self.last else _Inbox(self.next, self._g("pp_grad_in"), [i for k, i in steps if k == "B"],
+                                              lambda i: 2 * i + 1, self.lookahead)
         inputs: Dict[int, torch.Tensor] = {}
         outputs: Dict[int, torch.Tensor] = {}
         sends: List[Any] = []
         total = torch.zeros((), device=device, dtype=torch.float32)
-        for kind, i in schedule_1f1b(n, self.stage, self.n_stages):
+        for kind, i in steps:
             if kind == "F":
-                if self.first:
-                    x_in = micro_inputs[i][0]
-                else:
-                    x_in = self._recv(act_shape, dtype, device, self.prev, tag=2 * i).requires_grad_(True)
+                x_in = micro_inputs[i][0] if self.first else acts.take(i, act_shape, dtype, device).requires_grad_(True)
                 out = stage_forward(self.model, x_in, self.first)
                 if self.last:
                     loss = stage_loss(self.model, out, micro_inputs[i][1]) * scale
                     total += loss.detach().float()
                     outputs[i] = loss
                 else:
-                    sends.append(dist.isend(out.detach().contiguous(), dst=self.next, tag=2 * i))
+                    sends.append(dist.isend(out.detach().contiguous(), dst=self.next, tag=2 * i,
+                                            group=self._g("pp_act_out")))
                     outputs[i] = out
                 inputs[i] = x_in
             else:
@@ -133,11 +177,11 @@ class PipelineRunner:
                 if self.last:
                     out.backward()
                 else:
-                    grad = self._recv(out.shape, out.dtype, device, self.next, tag=2 * i + 1)
-                    out.backward(grad)
+                    out.backward(grads.take(i, out.shape, out.dtype, device))
                 x_in = inputs.pop(i)
                 if not self.first:
-                    sends.append(dist.isend(x_in.grad.contiguous(), dst=self.prev, tag=2 * i + 1))
+                    sends.append(dist.isend(x_in.grad.contiguous(), dst=self.prev, tag=2 * i + 1,
+                                            group=self._g("pp_grad_out")))
         for s in sends:
             s.wait()
         return total
@@ -185,7 +229,8 @@ class PipelineScheduler:
 
     def __init__(self, stage: PipelineStage, mesh: Any, n_micro: int = 4):
         self.stage, self.mesh, self.n_micro = stage, mesh, n_micro
-        self.runner = PipelineRunner(stage.model, mesh.pp_rank, mesh.pp_size, mesh.prev_stage, mesh.next_stage)
+        self.runner = PipelineRunner(stage.model, mesh.pp_rank, mesh.pp_size, mesh.prev_stage, mesh.next_stage,
+                                     groups=getattr(mesh, "groups", None))
 
     def run(self, inputs: torch.Tensor, targets: Optional[torch.Tensor] = None) -> torch.Tensor:
         if targets is None:

@@ -127,6 +127,18 @@ class ParallelMesh:
                 ranks = [self.rank_of(d, p, t) for p in range(self.pp_size)]
                 make("pp", ranks)
                 make("embed", sorted({ranks[0], ranks[-1]}))
+        # one two-rank group per direction of every adjacent stage pair: activations and activation gradients
+        # then travel on separate communicators, each a single in-order stream, so a stage can post its
+        # receives ahead of time without any ordering hazard against traffic in the other direction
+        for d in range(self.dp_size):
+            for t in range(self.tp_size):
+                chain = [self.rank_of(d, p, t) for p in range(self.pp_size)]
+                for a, b in zip(chain, chain[1:]):
+                    acts, grads = dist.new_group([a, b], **kw), dist.new_group([a, b], **kw)
+                    if self.rank == a:
+                        mine["pp_act_out"], mine["pp_grad_in"] = acts, grads
+                    if self.rank == b:
+                        mine["pp_act_in"], mine["pp_grad_out"] = acts, grads
         for p in range(self.pp_size):
             for t in range(self.tp_size):
                 make("dp", [self.rank_of(d, p, t) for d in range(self.dp_size)])
