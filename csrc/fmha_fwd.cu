@@ -465,11 +465,12 @@ struct PairLayout {
   static constexpr int DSUB = D / 64;
   static constexpr int KST = 2;
   static constexpr int VST = D == 64 ? 2 : 1;  // D = 128: one V stage keeps the CTA within shared memory
+  static constexpr int PST = D == 64 ? 2 : 1;  // P buffers per head (D = 64: P(j) written while P(j - 1) V runs)
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + 2 * DSUB * SUB_BYTES;
   static constexpr int V_OFF = K_OFF + KST * DSUB * SUB_BYTES;
-  static constexpr int P_OFF = V_OFF + VST * DSUB * SUB_BYTES;
-  static constexpr int BAR_OFF = P_OFF + 2 * 2 * SUB_BYTES;
+  static constexpr int P_OFF = V_OFF + VST * DSUB * SUB_BYTES;  // [PST][head][2 boxes]
+  static constexpr int BAR_OFF = P_OFF + PST * 2 * 2 * SUB_BYTES;
   static constexpr int BYTES = BAR_OFF + 512;
   static_assert(BYTES + 1024 <= 232448, "shared memory budget of one sm_100a CTA");
 };
@@ -479,7 +480,7 @@ __global__ void __launch_bounds__(PAIR_THREADS, 1) fmha_fwd_pair_kernel(const __
                                                                const __grid_constant__ CUtensorMap mk,
                                                                const __grid_constant__ CUtensorMap mv, Params p) {
   using L = PairLayout<D>;
-  constexpr int DSUB = L::DSUB, KST = L::KST, VST = L::VST;
+  constexpr int DSUB = L::DSUB, KST = L::KST, VST = L::VST, PST = L::PST;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sQ = smem + L::Q_OFF;
@@ -493,10 +494,12 @@ __global__ void __launch_bounds__(PAIR_THREADS, 1) fmha_fwd_pair_kernel(const __
   uint64_t* vfull = kempty + KST;
   uint64_t* vempty = vfull + VST;
   uint64_t* sfull = vempty + VST;  // [head]
-  uint64_t* sfree = sfull + 2;
+  uint64_t* sfree = sfull + 2;     // [head]
+  // [head][tile parity]: a barrier per tile parity cannot run two phases ahead of a waiter (a head finishing
+  // tiles j and j + 2 needs P(j) V in between)
   uint64_t* pfull = sfree + 2;
-  uint64_t* odone = pfull + 2;
-  uint64_t* drain = odone + 2;
+  uint64_t* odone = pfull + 4;
+  uint64_t* drain = odone + 4;
   uint32_t* tmem_slot = (uint32_t*)(drain + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
@@ -525,6 +528,8 @@ __global__ void __launch_bounds__(PAIR_THREADS, 1) fmha_fwd_pair_kernel(const __
     for (int i = 0; i < 2; ++i) {
       sm100::mbar_init(&sfull[i], 1);
       sm100::mbar_init(&sfree[i], 4);
+    }
+    for (int i = 0; i < 4; ++i) {
       sm100::mbar_init(&pfull[i], 4);
       sm100::mbar_init(&odone[i], 1);
     }
@@ -630,20 +635,20 @@ __global__ void __launch_bounds__(PAIR_THREADS, 1) fmha_fwd_pair_kernel(const __
           }
           const uint32_t va = sm100::smem_u32(sV + vb * DSUB * SUB_BYTES);
           for (int w = 0; w < 2 && ok; ++w) {
-            if (!wait(&pfull[w], i & 1)) {
+            if (!wait(&pfull[2 * w + (i & 1)], (i >> 1) & 1)) {
               fail(p.status, abort_flag, 6);
               ok = false;
               break;
             }
             sm100::tc_fence_after();
-            const uint32_t pa = sm100::smem_u32(sP + w * 2 * SUB_BYTES);
+            const uint32_t pa = sm100::smem_u32(sP + ((i % PST) * 2 + w) * 2 * SUB_BYTES);
 #pragma unroll
             for (int k = 0; k < BKV / 16; ++k) {
               const uint32_t poff = (uint32_t)(k >> 2) * SUB_BYTES + (uint32_t)(k & 3) * 32;
               sm100::mma_f16(tmem + 2 * BKV + w * D, sm100::desc_kmajor_sw128(pa + poff),
                              sm100::desc_mnmajor_sw128(va + k * 2048, SUB_BYTES), id_o, (i > 0 || k > 0) ? 1u : 0u);
             }
-            sm100::mma_commit(&odone[w]);
+            sm100::mma_commit(&odone[2 * w + (i & 1)]);
           }
           if (!ok) break;
           sm100::mma_commit(&vempty[vb]);
@@ -661,7 +666,8 @@ __global__ void __launch_bounds__(PAIR_THREADS, 1) fmha_fwd_pair_kernel(const __
     const int rq = q0 + row;
     const uint32_t lanes = tmem + ((uint32_t)(qq * 32) << 16);
     const uint32_t tS = lanes + w * BKV, tO = lanes + 2 * BKV + w * D;
-    uint8_t* myP = sP + w * 2 * SUB_BYTES;
+    // P V of tile i has completed (odone of head w, tile parity i & 1, phase i / 2)
+    auto pv_done = [&](int i) { return wait_warp(&odone[2 * w + (i & 1)], (i >> 1) & 1); };
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
@@ -710,15 +716,17 @@ __global__ void __launch_bounds__(PAIR_THREADS, 1) fmha_fwd_pair_kernel(const __
       const float m_new = fmaxf(m_used, m_tile);
       const bool need = m_new > m_used + RESCALE;  // also the first finite max
       const float alpha = !need ? 1.f : (m_used == -INFINITY ? 0.f : sm100::ex2_approx(m_used - m_new));
-      if (j >= 1) {
-        // P V of the previous tile has finished: its P buffer is free and O holds every earlier tile
-        if (!wait_warp(&odone[w], (j - 1) & 1)) {
+      // this tile's P buffer was last read by P V of tile j - PST; an O rescale needs every earlier P V done
+      const bool rescale = j >= 1 && __any_sync(0xffffffffu, need);
+      const int wait_tile = rescale ? j - 1 : j - PST;
+      if (wait_tile >= 0) {
+        if (!pv_done(wait_tile)) {
           fail(p.status, abort_flag, 10);
           ok = false;
           break;
         }
         sm100::tc_fence_after();
-        if (__any_sync(0xffffffffu, need)) {
+        if (rescale) {
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             uint32_t r[32];
@@ -736,6 +744,7 @@ __global__ void __launch_bounds__(PAIR_THREADS, 1) fmha_fwd_pair_kernel(const __
         l *= alpha;
       }
       // P = 2^(score - m_used) as bf16, 128-byte-swizzled K-major rows (see the single-head kernel)
+      uint8_t* myP = sP + ((j % PST) * 2 + w) * 2 * SUB_BYTES;
       float rs4[4] = {0.f, 0.f, 0.f, 0.f};  // one partial sum per 32-column chunk
       const float moff = m_used == -INFINITY ? 0.f : m_used;
 #pragma unroll
@@ -761,10 +770,10 @@ __global__ void __launch_bounds__(PAIR_THREADS, 1) fmha_fwd_pair_kernel(const __
       sm100::fence_async_shared();  // P (generic-proxy stores) visible to the tensor core
       sm100::tc_fence_before();     // and the O rescale ordered before the next P V
       __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(&pfull[w]);
+      if (lane == 0) sm100::mbar_arrive(&pfull[2 * w + (j & 1)]);
     }
     if (ok) {
-      if (wait_warp(&odone[w], (n - 1) & 1)) {
+      if (pv_done(n - 1)) {
         sm100::tc_fence_after();
         const float inv = l > 0.f ? 1.f / l : 0.f;
         __nv_bfloat16* dst = p.out + (((long long)b * p.T + rq) * p.Hq + h0 + w) * D;

@@ -1,18 +1,24 @@
-"""Policies over the native transformer (``PolicyModel`` protocol).
+"""Policies over the native transformer (the ``PolicyModel`` protocol; capabilities of
+``src/forgeline/models/policy.py:31-222``).
 
-``NativePolicy`` follows ``src/forgeline/models/policy.py:31-222``: LoRA /
-QLoRA injection, reference = adapters disabled or a frozen copy,
-per-token response log-probs, an optional value head, checkpoint dict
-``{model, adapter, value_head}``.  Log-probs go through the fused LM-head
-log-softmax kernel (ops/logprob.py), so no ``[B, T, V]`` fp32 tensor is
-built.  ``HFPolicy`` lives in models/hf_policy.py (optional dependency).
+``NativePolicy`` is organised around one scoring pass.  ``_score(prompt, response, wants)`` runs the trunk
+once over ``[prompt | response]`` and evaluates only the heads a caller asks for on its hidden states:
+``"logprobs"`` (per-response-token log-probs through the fused LM-head log-softmax kernel, no ``[B, T, V]``
+tensor), ``"entropy"`` (from the same kernel pass) and ``"value"`` (the value head on the last position).
+Every public scoring method (``logprobs``, ``logprobs_with_entropy``, ``values``, ``logprobs_and_values``)
+is a selection over it, so a PPO step that needs log-probs and values pays one forward.
+
+The frozen reference is either the live model with its adapters switched off (LoRA / QLoRA: no second copy
+of the weights) or a detached frozen copy; ``reference()`` swaps it in for the duration of a ``with`` block.
+Checkpoint dicts are ``{model, adapter, value_head}`` (the reference's keys); ``_PARTS`` lists how each part
+is saved and restored.
 """
 
 from __future__ import annotations
 
 import copy
 from contextlib import contextmanager
-from typing import Any, Dict, Iterator, List, Mapping, Optional
+from typing import Any, Callable, Dict, FrozenSet, Iterator, List, Mapping, Optional, Tuple
 
 import torch
 import torch.nn as nn
@@ -28,17 +34,25 @@ from rl_project_b200.ops.logprob import linear_logprobs, logprobs_from_logits
 
 
 class ValueHead(nn.Module):
+    """Scalar value from a hidden state: dropout, a half-width GELU layer, a linear read-out (parameter names
+    ``net.1`` / ``net.3`` are the checkpoint format)."""
+
     def __init__(self, hidden_size: int, dropout: float = 0.1):
         super().__init__()
         self.net = nn.Sequential(nn.Dropout(dropout), nn.Linear(hidden_size, hidden_size // 2), nn.GELU(),
                                  nn.Linear(hidden_size // 2, 1))
 
     def forward(self, hidden: torch.Tensor) -> torch.Tensor:
-        return self.net(hidden.to(self.net[1].weight.dtype)).squeeze(-1)
+        first = self.net[1]
+        return self.net(hidden.to(first.weight.dtype))[..., 0]
 
 
 def token_logprobs_from_logits(logits: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
     return logprobs_from_logits(logits, labels)
+
+
+# adapter method -> function that injects it into a model
+_ADAPTERS: Dict[str, Callable[..., nn.Module]] = {"lora": apply_lora, "qlora": apply_qlora}
 
 
 class NativePolicy(nn.Module):
@@ -48,18 +62,14 @@ class NativePolicy(nn.Module):
                  adapter: Optional[AdapterConfig] = None, reference_model: Optional[TransformerLM] = None,
                  value_head: bool = False):
         super().__init__()
-        self.model = model
-        self.tokenizer = tokenizer
-        self.pad_token_id = pad_token_id
+        self.model, self.tokenizer, self.pad_token_id = model, tokenizer, pad_token_id
         self.spec: ModelSpec = model.spec
         self.adapter = adapter or AdapterConfig()
-        self._has_adapter = self.adapter.method in ("lora", "qlora")
-        if self.adapter.method == "lora":
-            apply_lora(model, self.adapter.rank, self.adapter.alpha, self.adapter.dropout,
-                       self.adapter.target_modules or None)
-        elif self.adapter.method == "qlora":
-            apply_qlora(model, self.adapter.rank, self.adapter.alpha, self.adapter.dropout,
-                        self.adapter.target_modules or None)
+        inject = _ADAPTERS.get(self.adapter.method)
+        if inject is not None:
+            a = self.adapter
+            inject(model, a.rank, a.alpha, a.dropout, a.target_modules or None)
+        self._has_adapter = inject is not None
         self.reference_model = reference_model
         self.value_head: Optional[ValueHead] = ValueHead(self.spec.n_embd) if value_head else None
 
@@ -68,15 +78,13 @@ class NativePolicy(nn.Module):
         return cls(TransformerLM(spec), tokenizer, **kw)
 
     def with_frozen_reference(self) -> "NativePolicy":
-        if self._has_adapter:
-            return self
-        ref = copy.deepcopy(self.model).eval()
-        for p in ref.parameters():
-            p.requires_grad = False
-        self.reference_model = ref
+        """Keep a frozen copy of the current weights as the reference (adapter policies need none: the
+        reference is the model with its adapters off)."""
+        if not self._has_adapter:
+            self.reference_model = copy.deepcopy(self.model).eval().requires_grad_(False)
         return self
 
-    # protocol ------------------------------------------------------------
+    # ------------------------------------------------------------ protocol properties
     @property
     def device(self) -> torch.device:
         return next(self.model.parameters()).device
@@ -94,21 +102,22 @@ class NativePolicy(nn.Module):
         return self.spec.block_size
 
     def trainable_parameters(self) -> List[nn.Parameter]:
-        ps = [p for p in self.model.parameters() if p.requires_grad]
-        if self.value_head is not None:
-            ps += list(self.value_head.parameters())
-        return ps
+        head = list(self.value_head.parameters()) if self.value_head is not None else []
+        return [p for p in self.model.parameters() if p.requires_grad] + head
 
+    # ------------------------------------------------------------ generation
     @torch.no_grad()
     def generate(self, prompt_ids: torch.Tensor, settings: GenerationSettings) -> torch.Tensor:
+        """Sampled continuation tokens only (the prompt is not repeated)."""
         self.model.eval()
         prompt_ids = prompt_ids.to(self.device)
-        out = generate_tokens(self.model, prompt_ids, settings.max_new_tokens, temperature=settings.temperature,
-                              top_k=settings.top_k, top_p=settings.top_p, min_p=settings.min_p,
-                              repetition_penalty=settings.repetition_penalty, use_cache=settings.use_cache,
-                              stop_token_ids=settings.stop_token_ids)
+        s = settings
+        out = generate_tokens(self.model, prompt_ids, s.max_new_tokens, temperature=s.temperature, top_k=s.top_k,
+                              top_p=s.top_p, min_p=s.min_p, repetition_penalty=s.repetition_penalty,
+                              use_cache=s.use_cache, stop_token_ids=s.stop_token_ids)
         return out[:, prompt_ids.shape[1]:]
 
+    # ------------------------------------------------------------ whole-sequence scoring
     def token_logits(self, input_ids: torch.Tensor) -> torch.Tensor:
         return self.model.full_logits(input_ids.to(self.device))
 
@@ -124,95 +133,99 @@ class NativePolicy(nn.Module):
         return linear_cross_entropy(h.reshape(-1, h.shape[-1]), self.model.head_weight(),
                                     targets.to(self.device).reshape(-1))
 
-    def _full(self, prompt_ids: torch.Tensor, response_ids: torch.Tensor) -> torch.Tensor:
-        full = torch.cat([prompt_ids.to(self.device), response_ids.to(self.device)], dim=1)
+    # ------------------------------------------------------------ prompt / response scoring
+    def _joined(self, prompt_ids: torch.Tensor, response_ids: torch.Tensor) -> torch.Tensor:
+        dev = self.device
+        full = torch.cat([prompt_ids.to(dev), response_ids.to(dev)], dim=1)
         if full.shape[1] > self.spec.block_size:
             raise ModelError(f"prompt+response length {full.shape[1]} exceeds block_size {self.spec.block_size}")
         return full
 
-    def full_sequence_logits(self, prompt_ids: torch.Tensor, response_ids: torch.Tensor) -> torch.Tensor:
-        return self.model.full_logits(self._full(prompt_ids, response_ids))
-
-    def _response_lp(self, h: torch.Tensor, full: torch.Tensor, q_len: int, with_entropy: bool = False):
-        B, T, C = h.shape
-        hs = h[:, q_len - 1: T - 1, :].reshape(-1, C)
-        tg = full[:, q_len:].reshape(-1)
-        lp, extra = linear_logprobs(hs, self.model.head_weight(), tg, with_entropy)
-        R = T - q_len
-        return lp.view(B, R), (extra.view(B, R) if with_entropy else None)
+    def _score(self, prompt_ids: torch.Tensor, response_ids: torch.Tensor,
+               wants: FrozenSet[str]) -> Dict[str, torch.Tensor]:
+        full = self._joined(prompt_ids, response_ids)
+        h = self.model.forward_hidden(full)
+        out: Dict[str, torch.Tensor] = {}
+        if wants & {"logprobs", "entropy"}:
+            # position t predicts token t + 1: the response tokens are predicted from positions q - 1 .. T - 2
+            B, T, C = h.shape
+            q = prompt_ids.shape[1]
+            lp, ent = linear_logprobs(h[:, q - 1:T - 1].reshape(-1, C), self.model.head_weight(),
+                                      full[:, q:].reshape(-1), "entropy" in wants)
+            out["logprobs"] = lp.view(B, T - q)
+            if "entropy" in wants:
+                out["entropy"] = ent.view(B, T - q)
+        if "value" in wants:
+            if self.value_head is None:
+                raise ConfigError("values() requires value_head=True on the policy")
+            out["value"] = self.value_head(h[:, -1].float()).float()
+        return out
 
     def logprobs(self, prompt_ids: torch.Tensor, response_ids: torch.Tensor,
                  response_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
-        full = self._full(prompt_ids, response_ids)
-        h = self.model.forward_hidden(full)
-        lp, _ = self._response_lp(h, full, prompt_ids.shape[1])
-        if response_mask is not None:
-            lp = lp * response_mask.to(lp.device, lp.dtype)
-        return lp
+        lp = self._score(prompt_ids, response_ids, frozenset({"logprobs"}))["logprobs"]
+        return lp if response_mask is None else lp * response_mask.to(lp.device, lp.dtype)
 
     def logprobs_with_entropy(self, prompt_ids: torch.Tensor, response_ids: torch.Tensor):
-        full = self._full(prompt_ids, response_ids)
-        h = self.model.forward_hidden(full)
-        return self._response_lp(h, full, prompt_ids.shape[1], with_entropy=True)
+        r = self._score(prompt_ids, response_ids, frozenset({"logprobs", "entropy"}))
+        return r["logprobs"], r["entropy"]
 
     def values(self, prompt_ids: torch.Tensor, response_ids: torch.Tensor) -> torch.Tensor:
-        if self.value_head is None:
-            raise ConfigError("values() requires value_head=True on the policy")
-        h = self.model.forward_hidden(self._full(prompt_ids, response_ids))
-        return self.value_head(h[:, -1, :].float()).float()
+        return self._score(prompt_ids, response_ids, frozenset({"value"}))["value"]
 
     def logprobs_and_values(self, prompt_ids: torch.Tensor, response_ids: torch.Tensor):
-        full = self._full(prompt_ids, response_ids)
-        h = self.model.forward_hidden(full)
-        lp, _ = self._response_lp(h, full, prompt_ids.shape[1])
-        vals = self.value_head(h[:, -1, :].float()).float() if self.value_head is not None else None
-        return lp, vals
+        wants = frozenset({"logprobs", "value"} if self.value_head is not None else {"logprobs"})
+        r = self._score(prompt_ids, response_ids, wants)
+        return r["logprobs"], r.get("value")
 
+    # ------------------------------------------------------------ frozen reference
     @contextmanager
     def reference(self) -> Iterator["NativePolicy"]:
+        """Score with the reference policy inside the block: adapters off, or the frozen copy swapped in."""
         if self._has_adapter:
             set_lora_enabled(self.model, False)
             try:
                 yield self
             finally:
                 set_lora_enabled(self.model, True)
-        elif self.reference_model is not None:
-            live = self.model
-            self.model = self.reference_model
-            try:
-                yield self
-            finally:
-                self.model = live
-        else:
+            return
+        if self.reference_model is None:
             raise ConfigError("no reference policy: call with_frozen_reference() or use an adapter",
                               hint="KL-regularised algorithms need a frozen reference.")
+        live, self.model = self.model, self.reference_model
+        try:
+            yield self
+        finally:
+            self.model = live
 
-    # checkpoint ------------------------------------------------------------
-    def state_for_checkpoint(self) -> Dict[str, Any]:
-        st: Dict[str, Any] = {"model": self.model.state_dict()}
-        if self._has_adapter:
-            st["adapter"] = lora_state_dict(self.model)
-        if self.value_head is not None:
-            st["value_head"] = self.value_head.state_dict()
-        return st
-
-    def load_checkpoint_state(self, state: Mapping[str, Any]) -> None:
+    # ------------------------------------------------------------ checkpoint
+    def _parts(self) -> List[Tuple[str, Callable[[], Any], Callable[[Any], None]]]:
+        """(key, save, restore) of every part this policy carries."""
         from rl_project_b200.checkpoints.manager import load_model_state
 
-        if "model" in state:
-            load_model_state(self.model, state["model"], strict=False)
-        if "adapter" in state and self._has_adapter:
-            load_lora_state_dict(self.model, state["adapter"], strict=False)
-        if "value_head" in state and self.value_head is not None:
-            self.value_head.load_state_dict(state["value_head"])
+        parts = [("model", self.model.state_dict, lambda st: load_model_state(self.model, st, strict=False))]
+        if self._has_adapter:
+            parts.append(("adapter", lambda: lora_state_dict(self.model),
+                          lambda st: load_lora_state_dict(self.model, st, strict=False)))
+        if self.value_head is not None:
+            parts.append(("value_head", self.value_head.state_dict, self.value_head.load_state_dict))
+        return parts
 
+    def state_for_checkpoint(self) -> Dict[str, Any]:
+        return {key: save() for key, save, _ in self._parts()}
+
+    def load_checkpoint_state(self, state: Mapping[str, Any]) -> None:
+        for key, _, restore in self._parts():
+            if key in state:
+                restore(state[key])
+
+    # ------------------------------------------------------------ text
     def encode(self, text: str) -> List[int]:
         return self.tokenizer.encode(text)
 
     def decode(self, ids) -> str:
-        if isinstance(ids, torch.Tensor):
-            ids = ids.tolist()
-        return self.tokenizer.decode([int(t) for t in ids])
+        seq = ids.tolist() if isinstance(ids, torch.Tensor) else ids
+        return self.tokenizer.decode([int(t) for t in seq])
 
     def to(self, *args: Any, **kwargs: Any) -> "NativePolicy":  # type: ignore[override]
         super().to(*args, **kwargs)
@@ -221,10 +234,8 @@ class NativePolicy(nn.Module):
         return self
 
 
-
 def has_lora_modules(model: nn.Module) -> bool:
     """True when ``model`` carries LoRA / QLoRA adapter layers (src/forgeline/models/policy.py:421-422)."""
-    from rl_project_b200.models.adapters.lora import LoRALinear
-    from rl_project_b200.models.adapters.qlora import QLoRALinear
+    from rl_project_b200.models.adapters.lora import LowRankAdapter
 
-    return any(isinstance(m, (LoRALinear, QLoRALinear)) for m in model.modules())
+    return any(isinstance(m, LowRankAdapter) for m in model.modules())

@@ -48,6 +48,9 @@ def test_fmha_forward_matches_fp32(B, T, Hq, Hkv, D, causal):
     (2, 256, 4, 2, 64, True),
     (1, 300, 2, 1, 128, True),
     (1, 256, 2, 2, 64, False),
+    (1, 301, 4, 2, 64, True),      # T not a multiple of 4: the log-sum-exp rows are read element by element
+    (2, 640, 8, 2, 128, True),     # several query tiles and heads per key tile (d 128: dQ drained in-step)
+    (2, 640, 8, 2, 64, True),      # ... (d 64: dQ drained one step later, double-buffered tiles)
 ])
 def test_fmha_backward_matches_fp32_autograd(B, T, Hq, Hkv, D, causal):
     from rl_project_b200.ops.attention import attention_reference, fmha, fmha_check
