@@ -446,7 +446,7 @@ class InferenceEngine:
         """Split long contexts over several CTAs when the batch alone cannot fill the GPU."""
         if self.device.type != "cuda" or max_ctx <= 256:
             return 0
-        ctas = B * self.model.spec.n_kv_head
+        ctas = B * self.model.kv_layout()[1]
         if ctas >= self._sms:
             return 0
         splits = min((2 * self._sms + ctas - 1) // ctas, max_ctx // 128)

@@ -228,8 +228,10 @@ class TransformerLM(nn.Module):
         return all(type(b.attn) is CausalSelfAttention for b in self.transformer.h)
 
     def kv_layout(self) -> Tuple[int, int, int]:
-        """``(n_layer, n_kv_head, head_dim)`` of the KV cache."""
-        return self.spec.n_layer, self.spec.n_kv_head, self.spec.n_embd // self.spec.n_head
+        """``(n_layer, n_kv_head, head_dim)`` of this process's KV cache: the attention modules' own head
+        counts, which tensor parallelism divides by the group size."""
+        attn = self.transformer.h[0].attn
+        return self.spec.n_layer, attn.n_kv_head, attn.head_dim
 
     @torch.no_grad()
     def decode_paged(self, tokens: torch.Tensor, cache: Any, meta: Any) -> torch.Tensor:
