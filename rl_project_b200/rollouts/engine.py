@@ -42,6 +42,9 @@ class RolloutConfig:
     engine_max_batch: int = 256  # sequences decoding at once in the paged engine
     engine_kv_blocks: Optional[int] = None  # KV pool size in 16-token blocks (default: enough for max_batch)
     engine_decode_graphs: Optional[bool] = None  # replay decode steps from CUDA graphs (None: RLB_DECODE_GRAPHS)
+    # > 0 in a distributed run: the ranks form world / replica_tp tensor-parallel generation replicas of this
+    # many GPUs (rollouts/replicas.py) that share each step's prompts; 0: every rank generates its own
+    replica_tp: int = 0
 
 
 class RolloutEngine:

@@ -210,6 +210,8 @@ class Trainer:
         self.phase_events: Optional[List[Any]] = None
         if strategy is not None and hasattr(strategy, "prepare_training"):
             strategy.prepare_training(self)
+        if strategy is not None and hasattr(algorithm, "bind_strategy"):
+            algorithm.bind_strategy(strategy)
         self.params = [p for p in algorithm.parameters() if p.requires_grad]
         if not self.params:
             raise ConfigError("algorithm exposes no trainable parameters")

@@ -262,9 +262,11 @@ def build_algorithm(manifest: ExperimentManifest, ctx: RunContext) -> PostTraini
         if str(manifest.data.path) == "synthetic:random_prompts":
             from rl_project_b200.data.synthetic import random_prompts
 
+            # rollout replicas share one prompt pool (every rank draws the same prompts); otherwise per rank
+            shared = rollout is not None and rollout.replica_tp > 0
             prompts = random_prompts(int(extra.get("n_prompts", 1024)), manifest.model.vocab_size,
                                      int(extra.get("min_prompt", 128)), int(extra.get("max_prompt", 512)),
-                                     seed=manifest.data.seed + _rank())
+                                     seed=manifest.data.seed + (0 if shared else _rank()))
         elif tasks:
             prompts = [torch.tensor(policy.encode(t["prompt"]), dtype=torch.long) for t in tasks]
         else:

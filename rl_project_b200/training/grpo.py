@@ -95,6 +95,13 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
             rc.group_size = config.group_size
             self.rollouts = RolloutEngine(policy, rc)
         self._last_stats: Dict[str, float] = {}
+        self._strategy: Any = None
+        self._replica_set: Any = None
+        self._shared_rng = random.Random(config.seed)  # identical on every rank: the replicas' prompt choice
+
+    def bind_strategy(self, strategy: Any) -> None:
+        """The distributed strategy the Trainer runs (rollout replicas read the learner's sharded weights)."""
+        self._strategy = strategy
 
     def parameters(self) -> List[nn.Parameter]:
         return self.policy.trainable_parameters()
@@ -109,11 +116,14 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
     @torch.no_grad()
     def collect(self, step: int) -> List[GRPOGroup]:
         n = len(self.tasks if self.cfg.agent else self.prompts)
-        idx = [self.rng.randrange(n) for _ in range(self.cfg.prompts_per_step)]
         if self.cfg.agent:
+            idx = [self.rng.randrange(n) for _ in range(self.cfg.prompts_per_step)]
             # every episode of the step advances in one lock-step batch
             traj_groups = self.agent_engine.rollout_many([self.tasks[i] for i in idx], self.cfg.group_size)
+        elif self.rollouts.cfg.replica_tp > 0 and torch.distributed.is_initialized():
+            traj_groups = self._collect_replicated(step)
         else:
+            idx = [self.rng.randrange(n) for _ in range(self.cfg.prompts_per_step)]
             traj_groups = self.rollouts.rollout_many([self.prompts[i] for i in idx], [self.tasks[i] for i in idx])
         groups, skipped = [], 0
         for trajs in traj_groups:
@@ -135,6 +145,50 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
         }
         if self.cfg.agent:
             self._last_stats["tool_calls"] = float(sum(len(t.tool_results) for g in groups for t in g.trajectories))
+        return groups
+
+    @torch.no_grad()
+    def _collect_replicated(self, step: int) -> List[List[Trajectory]]:
+        """Every rank picks the same ``prompts_per_step`` prompts; each tensor-parallel replica generates its
+        block of them (after taking the learner's current weights) and each rank keeps its share of the
+        replica's groups, so the learner's per-rank batches need no exchange."""
+        from rl_project_b200.inference.requests import SamplingParams
+        from rl_project_b200.rollouts.engine import SEQ_ALIGN, _pad
+        from rl_project_b200.rollouts.replicas import RolloutReplicas
+
+        rc = self.rollouts.cfg
+        if self._replica_set is None:
+            dt = next(self.policy.model.parameters()).dtype
+            self._replica_set = RolloutReplicas(self.policy.spec, rc.replica_tp, self.policy.device,
+                                                dt if dt in (torch.bfloat16, torch.float16) else torch.float32,
+                                                max_batch=rc.engine_max_batch, max_blocks=rc.engine_kv_blocks)
+        rep = self._replica_set
+        if self._strategy is not None and getattr(self._strategy, "units", None):
+            rep.sync_from_fsdp(self._strategy)
+        else:
+            rep.sync_from_module(self.policy.model)
+        chosen = [self._shared_rng.randrange(len(self.prompts)) for _ in range(self.cfg.prompts_per_step)]
+        mine = rep.share(chosen)
+        prompts = [self.prompts[i][-rc.max_prompt_length:].tolist() for i in mine]
+        limit = rep.engine.max_seq_len
+        G = self.cfg.group_size
+        gens: List[List[List[int]]] = []
+        for p in prompts:  # one request group per prompt: max tokens depend on the prompt length
+            params = SamplingParams(max_tokens=max(1, min(rc.max_new_tokens, limit - len(p))),
+                                    temperature=rc.temperature, top_k=rc.top_k, top_p=rc.top_p,
+                                    stop_token_ids=[int(t) for t in rc.stop_token_ids])
+            gens.append(params)
+        outs = rep.generate_each(prompts, G, gens, seed=(self.cfg.seed * 1_000_003 + step) * 64 + rep.replica)
+        dev = self.policy.device
+        groups = []
+        for j in rep.learner_share(list(range(len(mine)))):
+            pid = torch.tensor(prompts[j], dtype=torch.long)
+            rows = outs[j]
+            responses = _pad(rows, dev, pid.numel(), SEQ_ALIGN)
+            batch = pid.unsqueeze(0).repeat(G, 1).to(dev)
+            old = self.rollouts._old_logprobs(batch, responses)  # one learner forward per group on every rank
+            groups.append(self.rollouts._to_trajs(pid, responses, old, self.tasks[mine[j]], "",
+                                                  lengths=[len(r) for r in rows]))
         return groups
 
     @torch.no_grad()
