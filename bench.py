@@ -50,8 +50,9 @@ def parse_args():
                     help="untimed steps after the timed region with per-phase CUDA events (0: none)")
     ap.add_argument("--workload", choices=["sft1b", "mesh8b", "moe", "grpo"], default="sft1b",
                     help="sft1b: the headline (dense 1B SFT). mesh8b: dense-8B pretrain on a TP x PP x DP "
-                         "mesh (1F1B). moe: MLA+MoE pretrain with expert parallelism. grpo: GRPO rollout+update "
-                         "on one GPU (see rl_project_b200.benchmarks.grpo).")
+                         "mesh (1F1B). moe: MLA+MoE pretrain with expert parallelism. grpo: GRPO rollout+update, "
+                         "FSDP learner + tensor-parallel rollout replicas on N GPUs (rl_project_b200.benchmarks.grpo; "
+                         "its flags pass through).")
     ap.add_argument("--tp", type=int, default=2)
     ap.add_argument("--pp", type=int, default=2)
     ap.add_argument("--micro", type=int, default=8)
@@ -70,7 +71,11 @@ def parse_args():
                     help="training / prefill attention: torch SDPA (cuDNN / flash) or this library's tcgen05 kernels")
     ap.add_argument("--decode-graphs", action="store_true",
                     help="grpo workload: replay the paged decode step from CUDA graphs")
-    return ap.parse_args()
+    args, extra = ap.parse_known_args()
+    args.extra = extra
+    if extra and args.workload != "grpo":
+        ap.error(f"unrecognised arguments: {' '.join(extra)}")
+    return args
 
 
 def apply_kernel_choices(args) -> dict:
@@ -459,8 +464,8 @@ def main():
     if args.workload == "grpo":
         from rl_project_b200.benchmarks import grpo
 
-        sys.argv = [sys.argv[0], "--steps", str(args.steps), "--warmup", str(args.warmup)]
-        grpo.main()
+        # the GRPO flags (--preset, --prompts, --group, --max-new, --rollout-tp, ...) pass through
+        grpo.run(["--steps", str(args.steps), "--warmup", str(args.warmup)] + list(args.extra))
         return
     run_ours(args, world, rank, local)
 
