@@ -451,10 +451,18 @@ def main():
         if rank == 0:
             print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
     if args.impl == "reference":
-        from baseline.harness import run_reference
+        from baseline.harness import run_reference, run_reference_workload
 
-        payload = run_reference(args, world, rank, local, time_device=time_device, time_wall=time_wall,
-                                clock_sampler=ClockSampler, metric=METRIC, model_name=MODEL_NAME)
+        if args.workload in ("mesh8b", "moe"):
+            payload = run_reference_workload(args, world, rank, local, time_device=time_device,
+                                             clock_sampler=ClockSampler, metric=METRIC)
+        elif args.workload == "grpo":
+            payload = {"impl": "reference", "unavailable": "GRPO reference arm not built: the reference runs GRPO "
+                       "only under DDP, whose 8B replica needs about 160 GB per GPU before activations (fp32 weights, "
+                       "gradients, AdamW state and the fp32 frozen copy), and the FSDP fallback loop is not written"}
+        else:
+            payload = run_reference(args, world, rank, local, time_device=time_device, time_wall=time_wall,
+                                    clock_sampler=ClockSampler, metric=METRIC, model_name=MODEL_NAME)
         emit(rank, payload)
         return
     apply_kernel_choices(args)
