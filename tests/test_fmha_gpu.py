@@ -1,17 +1,13 @@
-"""Own tcgen05 attention forward (csrc/fmha_fwd.cu) against an fp32 PyTorch reference of the same op.
-
-The kernel has not run on a B200 yet, so this module only runs when RLB_FMHA_TEST=1 is set; the
-default attention path (SDPA) does not use it.
+"""Own tcgen05 attention (csrc/fmha_fwd.cu, csrc/fmha_bwd.cu) against an fp32 PyTorch reference of the same
+op: forward output and log-sum-exp, backward dq / dk / dv through autograd, the paired-head forward (even
+GQA groups) and the one-head kernel (odd groups, MLA d_qk 192), causal / non-causal, sliding window, tanh
+soft-cap, ragged and odd sequence lengths.
 """
-
-import os
 
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("RLB_FMHA_TEST") != "1",
-                                 reason="own FMHA kernel not yet validated on a GPU (set RLB_FMHA_TEST=1)")]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("B,T,Hq,Hkv,D,causal", [
