@@ -426,7 +426,10 @@ def run_pretrain_workload(args, world, rank, local):
                "config": {"model": preset + (f" ({args.layers} layers)" if args.layers else ""), "global_batch": gb,
                           "seq_len": seq, "parallelism": layout, "micro_batches": micro,
                           "params_full_model": n_params_full, "workload": args.workload,
-                          "l2": "inputs larger than L2", "final_loss": trainer.history[-1].loss,
+                          "l2": "inputs larger than L2", "first_loss": trainer.history[0].loss,
+                          "final_loss": trainer.history[-1].loss,
+                          "loss_terms": ("next-token CE + MTP CE x mtp_loss_weight (about 2 ln V at init)"
+                                         if spec.n_predict_tokens > 1 else "next-token CE"),
                           "attention": args.attn, "gemm": args.gemm,
                           "tp_allreduce": (("fused tcgen05 GEMM epilogue over peer memory"
                                             if tp_fused_used() else "nccl") if args.workload == "mesh8b"
@@ -447,6 +450,11 @@ def _peak_tflops():
 def main():
     args = parse_args()
     world, rank, local = dist_env()
+    if os.environ.get("RLB_HANG_DUMP_S"):
+        # diagnostics: every thread's Python stack goes to stderr after this many seconds (the run goes on)
+        import faulthandler
+
+        faulthandler.dump_traceback_later(float(os.environ["RLB_HANG_DUMP_S"]), repeat=False)
     if world != args.gpus:
         if rank == 0:
             print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)

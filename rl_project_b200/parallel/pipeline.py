@@ -29,6 +29,7 @@ the runner posts each receive when it is needed, on the default group.
 
 from __future__ import annotations
 
+import os
 from typing import Any, Callable, Dict, List, Optional, Sequence, Tuple
 
 import torch
@@ -141,7 +142,8 @@ class PipelineRunner:
                           ([] if self.first else ["pp_act_in", "pp_grad_out"]) +
                           ([] if self.last else ["pp_act_out", "pp_grad_in"]))
         self.groups = g if directional else {}
-        self.lookahead = lookahead if directional else 0
+        la = os.environ.get("RLB_PP_LOOKAHEAD")  # diagnostics / A-B: receives posted ahead (0: when needed)
+        self.lookahead = (int(la) if la is not None else lookahead) if directional else 0
 
     def _g(self, name: str):
         return self.groups.get(name, self.group)
