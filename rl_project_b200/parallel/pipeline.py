@@ -103,6 +103,17 @@ def schedule_1f1b(n_micro: int, stage: int, n_stages: int) -> List[Tuple[str, in
     return steps
 
 
+_BATCHED = os.environ.get("RLB_PP_P2P", "plain") == "batched"
+
+
+def _p2p(op, tensor: torch.Tensor, peer: int, tag: int, group: Any):
+    """One point-to-point send / receive: plain ``isend`` / ``irecv``, or (``RLB_PP_P2P=batched``) a one-op
+    ``batch_isend_irecv`` group (NCCL group semantics)."""
+    if _BATCHED:
+        return dist.batch_isend_irecv([dist.P2POp(op, tensor, peer, group=group, tag=tag)])[0]
+    return op(tensor, peer, tag=tag, group=group)
+
+
 class _Inbox:
     """Receives of one direction, posted up to ``depth`` messages ahead in the order they will be consumed."""
 
@@ -115,7 +126,7 @@ class _Inbox:
         i = self.order[self.next]
         self.next += 1
         buf = torch.empty(shape, dtype=dtype, device=device)
-        self.posted[i] = (buf, dist.irecv(buf, src=self.src, tag=self.tag_of(i), group=self.group))
+        self.posted[i] = (buf, _p2p(dist.irecv, buf, self.src, self.tag_of(i), self.group))
 
     def take(self, i: int, shape, dtype, device) -> torch.Tensor:
         while i not in self.posted:
@@ -170,8 +181,7 @@ class PipelineRunner:
                     total += loss.detach().float()
                     outputs[i] = loss
                 else:
-                    sends.append(dist.isend(out.detach().contiguous(), dst=self.next, tag=2 * i,
-                                            group=self._g("pp_act_out")))
+                    sends.append(_p2p(dist.isend, out.detach().contiguous(), self.next, 2 * i, self._g("pp_act_out")))
                     outputs[i] = out
                 inputs[i] = x_in
             else:
@@ -182,8 +192,7 @@ class PipelineRunner:
                     out.backward(grads.take(i, out.shape, out.dtype, device))
                 x_in = inputs.pop(i)
                 if not self.first:
-                    sends.append(dist.isend(x_in.grad.contiguous(), dst=self.prev, tag=2 * i + 1,
-                                            group=self._g("pp_grad_out")))
+                    sends.append(_p2p(dist.isend, x_in.grad.contiguous(), self.prev, 2 * i + 1, self._g("pp_grad_out")))
         for s in sends:
             s.wait()
         return total
