@@ -1,11 +1,11 @@
 """``forgeline-b200`` command-line interface.
 
-The 13 commands and their flags mirror ``src/forgeline/cli/main.py:21-586`` so
-scripts written for the reference CLI run unchanged: presets, validate, data,
-train, generate, evaluate, serve, export, registry, rlaif, dashboard,
-allocation, synthesis-ppo.  Differences: ``train`` accepts every strategy the
-trainer implements (single, ddp, fsdp, zero2, tensor/pipeline/expert
-parallel, hybrid) and ``serve`` runs the paged-KV engine.
+The command names and flags are those of the reference CLI (``src/forgeline/cli/main.py:21-586``), so scripts
+written for it run unchanged: presets, validate, data, train, generate, evaluate, serve, export, registry,
+rlaif, dashboard, allocation, synthesis-ppo.  The parser is generated from one table (``_command_table``) and
+commands with sub-commands dispatch through handler tables.  Differences: ``train`` accepts every strategy
+the trainer implements (single, ddp, fsdp, zero2, tensor / pipeline / expert parallel, hybrid) and ``serve``
+runs the paged-KV engine.
 """
 
 from __future__ import annotations
@@ -14,7 +14,7 @@ import argparse
 import json
 import sys
 from pathlib import Path
-from typing import Any, List, Optional
+from typing import Any, Dict, List, Optional, Tuple
 
 from rl_project_b200 import __version__
 from rl_project_b200.core.errors import ForgelineError
@@ -55,32 +55,47 @@ def cmd_validate(args: argparse.Namespace) -> int:
     return 0
 
 
+def _data_prepare(args):
+    from rl_project_b200.data.preprocessing import prepare_text_corpus
+
+    return prepare_text_corpus(args.input, args.output, tokenizer=args.tokenizer, val_fraction=args.val_fraction)
+
+
+def _data_prepare_hf(args):
+    from rl_project_b200.data.preprocessing import prepare_hf_corpus
+
+    return prepare_hf_corpus(args.dataset, args.output, tokenizer_name=args.tokenizer, subset=args.subset,
+                             max_tokens=args.max_tokens, shard_size=args.shard_size)
+
+
+def _data_shard(args):
+    from rl_project_b200.data.pretraining import detect_token_dtype
+    from rl_project_b200.data.streaming import shard_token_file
+
+    paths = shard_token_file(args.input, args.output, args.n_shards, dtype=detect_token_dtype(Path(args.input).parent))
+    return [str(p) for p in paths]
+
+
+def _data_gsm8k(args):
+    from rl_project_b200.data.verifiable import build_gsm8k_tool_dataset
+
+    return {"written": build_gsm8k_tool_dataset(args.output, split=args.split, limit=args.limit)}
+
+
+def _data_validate(args):
+    from rl_project_b200.data.records import SCHEMAS, ReadReport, read_jsonl
+
+    report = ReadReport()
+    rows = read_jsonl(args.input, SCHEMAS[args.kind], on_error="skip", report=report)
+    return {"valid": len(rows), "skipped": report.skipped, "errors": report.errors[:20]}
+
+
+_DATA = {"prepare": _data_prepare, "prepare-hf": _data_prepare_hf, "shard": _data_shard, "gsm8k": _data_gsm8k,
+         "validate": _data_validate}
+
+
 def cmd_data(args: argparse.Namespace) -> int:
-    if args.data_cmd == "prepare":
-        from rl_project_b200.data.preprocessing import prepare_text_corpus
-
-        _print(prepare_text_corpus(args.input, args.output, tokenizer=args.tokenizer, val_fraction=args.val_fraction))
-    elif args.data_cmd == "prepare-hf":
-        from rl_project_b200.data.preprocessing import prepare_hf_corpus
-
-        _print(prepare_hf_corpus(args.dataset, args.output, tokenizer_name=args.tokenizer, subset=args.subset,
-                                 max_tokens=args.max_tokens, shard_size=args.shard_size))
-    elif args.data_cmd == "shard":
-        from rl_project_b200.data.pretraining import detect_token_dtype
-        from rl_project_b200.data.streaming import shard_token_file
-
-        dtype = detect_token_dtype(Path(args.input).parent)
-        _print([str(p) for p in shard_token_file(args.input, args.output, args.n_shards, dtype=dtype)])
-    elif args.data_cmd == "gsm8k":
-        from rl_project_b200.data.verifiable import build_gsm8k_tool_dataset
-
-        _print({"written": build_gsm8k_tool_dataset(args.output, split=args.split, limit=args.limit)})
-    elif args.data_cmd == "validate":
-        from rl_project_b200.data.records import SCHEMAS, ReadReport, read_jsonl
-
-        rep = ReadReport()
-        rows = read_jsonl(args.input, SCHEMAS[args.kind], on_error="skip", report=rep)
-        _print({"valid": len(rows), "skipped": rep.skipped, "errors": rep.errors[:20]})
+    _print(_DATA[args.data_cmd](args))
     return 0
 
 
@@ -289,47 +304,70 @@ def cmd_serve(args: argparse.Namespace) -> int:
 
 
 # ------------------------------------------------------------------ registry
+def _registry_list(reg, args):
+    return 0, [{"id": c.id, "key": c.key, "state": c.state.value, "algorithm": c.algorithm, "metrics": c.metrics,
+                "promotion": c.promotion_status} for c in reg.list()]
+
+
+def _registry_register(reg, args):
+    from rl_project_b200.deployment import ModelCandidate
+
+    metrics = json.loads(args.metrics) if args.metrics else {}
+    if args.metrics_file:
+        from rl_project_b200.evaluation.results import load_results, merge_metrics
+
+        metrics.update(merge_metrics(load_results(args.metrics_file)))
+    c = reg.register(ModelCandidate(name=args.name, version=args.version, algorithm=args.algorithm,
+                                    checkpoint=args.checkpoint, metrics=metrics, tags=args.tags or []))
+    return 0, {"registered": c.id, "key": c.key}
+
+
+def _registry_promote(reg, args):
+    """Move a candidate to ``--to``; a champion promotion with ``--gate`` must pass the gate against the incumbent
+    (exit 2 when it does not), and a candidate below challenger is staged through challenger first."""
+    from rl_project_b200.deployment import CandidateState, PromotionGate
+
+    c = reg.get(args.id)
+    target = CandidateState(args.to)
+    champion = target == CandidateState.CHAMPION
+    if champion and args.gate:
+        from rl_project_b200.core.config import load_config
+
+        incumbent = reg.champion(c.name)
+        report = PromotionGate.from_config(load_config(args.gate)).evaluate(
+            c.metrics, incumbent.metrics if incumbent else None)
+        c.promotion_status, c.promotion_report = ("passed" if report.passed else "rejected"), report.to_dict()
+        reg.update(c)
+        if not report.passed:
+            return 2, {"promoted": False, "report": report.to_dict()}
+    if champion and c.state not in (CandidateState.CHALLENGER, CandidateState.CHAMPION):
+        reg.transition(c.id, CandidateState.CHALLENGER, reason="staged before champion promotion")
+    reg.transition(c.id, target, reason=args.reason)
+    return 0, {"promoted": True, "id": c.id, "state": target.value}
+
+
+def _registry_rollback(reg, args):
+    from rl_project_b200.deployment import rollback
+
+    return 0, {"champion": rollback(reg, args.name, reason=args.reason).key}
+
+
+def _registry_disable(reg, args):
+    from rl_project_b200.deployment import disable_candidate
+
+    return 0, {"disabled": disable_candidate(reg, args.id, reason=args.reason).key}
+
+
+_REGISTRY = {"list": _registry_list, "register": _registry_register, "promote": _registry_promote,
+             "rollback": _registry_rollback, "disable": _registry_disable}
+
+
 def cmd_registry(args: argparse.Namespace) -> int:
-    from rl_project_b200.deployment import (CandidateRegistry, CandidateState, ModelCandidate, PromotionGate,
-                                            disable_candidate, rollback)
+    from rl_project_b200.deployment import CandidateRegistry
 
-    reg = CandidateRegistry(args.registry)
-    if args.registry_cmd == "list":
-        _print([{"id": c.id, "key": c.key, "state": c.state.value, "algorithm": c.algorithm, "metrics": c.metrics,
-                 "promotion": c.promotion_status} for c in reg.list()])
-    elif args.registry_cmd == "register":
-        metrics = json.loads(args.metrics) if args.metrics else {}
-        if args.metrics_file:
-            from rl_project_b200.evaluation.results import load_results, merge_metrics
-
-            metrics.update(merge_metrics(load_results(args.metrics_file)))
-        c = reg.register(ModelCandidate(name=args.name, version=args.version, algorithm=args.algorithm,
-                                        checkpoint=args.checkpoint, metrics=metrics, tags=args.tags or []))
-        _print({"registered": c.id, "key": c.key})
-    elif args.registry_cmd == "promote":
-        c = reg.get(args.id)
-        target = CandidateState(args.to)
-        if target == CandidateState.CHAMPION and args.gate:
-            from rl_project_b200.core.config import load_config
-
-            gate = PromotionGate.from_config(load_config(args.gate))
-            incumbent = reg.champion(c.name)
-            report = gate.evaluate(c.metrics, incumbent.metrics if incumbent else None)
-            c.promotion_status = "passed" if report.passed else "rejected"
-            c.promotion_report = report.to_dict()
-            reg.update(c)
-            if not report.passed:
-                _print({"promoted": False, "report": report.to_dict()})
-                return 2
-        if target == CandidateState.CHAMPION and c.state not in (CandidateState.CHALLENGER, CandidateState.CHAMPION):
-            reg.transition(c.id, CandidateState.CHALLENGER, reason="staged before champion promotion")
-        reg.transition(c.id, target, reason=args.reason)
-        _print({"promoted": True, "id": c.id, "state": target.value})
-    elif args.registry_cmd == "rollback":
-        _print({"champion": rollback(reg, args.name, reason=args.reason).key})
-    elif args.registry_cmd == "disable":
-        _print({"disabled": disable_candidate(reg, args.id, reason=args.reason).key})
-    return 0
+    code, out = _REGISTRY[args.registry_cmd](CandidateRegistry(args.registry), args)
+    _print(out)
+    return code
 
 
 # ------------------------------------------------------------------ rlaif / synthesis / dashboard / allocation
@@ -478,186 +516,142 @@ def cmd_allocation(args: argparse.Namespace) -> int:
 
 
 # ------------------------------------------------------------------ parser
-def _add(sub, name: str, fn, help_text: str = "", **kw):
-    p = sub.add_parser(name, help=help_text, **kw)
-    p.set_defaults(func=fn)
-    return p
+# The command line is data: every command is (help, handler, arguments), arguments are (flags, options), and a
+# command with sub-commands carries {"dest": ..., name: (help, arguments)}.  ``build_parser`` walks the table.
+
+
+def A(*flags: str, **options: Any):
+    return flags, options
+
+
+_POLICY_SOURCE = [A("--checkpoint", required=True),
+                  A("--data-dir", default=None, help="directory with meta.pkl when the checkpoint lacks it"),
+                  A("--device", default="auto")]
+
+_GENERATE = _POLICY_SOURCE + [
+    A("--prompt", default="\n"), A("--max-tokens", type=int, default=200), A("--temperature", type=float, default=0.8),
+    A("--top-k", type=int, default=50), A("--top-p", type=float, default=None), A("--min-p", type=float, default=None),
+    A("--repetition-penalty", type=float, default=1.0), A("--no-cache", action="store_true"),
+    A("--interactive", action="store_true"), A("--draft-checkpoint", default=None), A("--spec-k", type=int, default=5)]
+
+_EVALUATE = _POLICY_SOURCE + [
+    A("--suites", nargs="+", default=["gsm8k"]), A("--n-shot", type=int, default=0),
+    A("--max-tasks", type=int, default=0), A("--max-tokens", type=int, default=64),
+    A("--offline", action="store_true", help="use built-in sample tasks (no download)"),
+    A("--heldout-data", default=None), A("--output", default=None), A("--ray-workers", type=int, default=0),
+    A("--ray-address", default=None), A("--ray-cpus-per-worker", type=float, default=1.0),
+    A("--worker-backend", default="ray", choices=["ray", "threads"],
+      help="where --ray-workers run: Ray actors or in-process threads")]
+
+_SERVE = _POLICY_SOURCE + [
+    A("--host", default="127.0.0.1"), A("--port", type=int, default=8000), A("--model-name", default="forgeline-model"),
+    A("--max-batch", type=int, default=8), A("--max-seq-len", type=int, default=None),
+    A("--routing", default=None, help="routing policy JSON"), A("--metrics", default="none"),
+    A("--output-dir", default="runs/serve")]
+
+_RLAIF_COMMON = [A("--output", required=True), A("--n-prompts", type=int, default=10), A("--checkpoint", default=None),
+                 A("--data-dir", default=None), A("--device", default="auto"), A("--max-tokens", type=int, default=128)]
+
+_ALLOC_COMMON = [A("--env", default=None), A("--metrics", default="none"), A("--output-dir", default="runs/allocation")]
+
+
+def _command_table() -> Dict[str, Tuple[str, Any, Any]]:
+    return {
+        "presets": ("list model presets", cmd_presets,
+                    [A("--count-params", action="store_true"), A("--vocab-size", type=int, default=65536)]),
+        "validate": ("validate an experiment manifest without running it", cmd_validate,
+                     [A("manifest"), A("--world-size", type=int, default=None)]),
+        "data": ("dataset preparation and validation", cmd_data, {
+            "dest": "data_cmd",
+            "prepare": ("tokenize a text file into train.bin/val.bin", [
+                A("--input", required=True), A("--output", required=True),
+                A("--tokenizer", default="char", help="char | tiktoken[:enc] | hf:<name>"),
+                A("--val-fraction", type=float, default=0.1)]),
+            "prepare-hf": ("stream a HuggingFace dataset into shard files", [
+                A("--dataset", required=True), A("--subset", default=None), A("--tokenizer", default="Qwen/Qwen2.5-0.5B"),
+                A("--output", required=True), A("--max-tokens", type=int, default=100_000_000),
+                A("--shard-size", type=int, default=10_000_000)]),
+            "shard": ("split a .bin token file into shards", [
+                A("--input", required=True), A("--output", required=True), A("--n-shards", type=int, default=16)]),
+            "gsm8k": ("download GSM8K as verifiable tool-use tasks", [
+                A("--output", required=True), A("--split", default="train"), A("--limit", type=int, default=None)]),
+            "validate": ("validate a JSONL dataset against a schema", [
+                A("--input", required=True),
+                A("--kind", required=True, choices=["supervised", "preference", "verifiable", "process", "reward"])]),
+        }),
+        "train": ("run a training stage from a manifest", cmd_train, [
+            A("manifest"), A("--set", action="append", help="dotted override, e.g. trainer.max_steps=10"),
+            A("--max-steps", type=int, default=None), A("--output-dir", default=None), A("--resume", default=None),
+            A("--metrics", default="local", help="local | none | wandb | tensorboard")]),
+        "generate": ("", cmd_generate, _GENERATE),
+        "evaluate": ("", cmd_evaluate, _EVALUATE),
+        "serve": ("", cmd_serve, _SERVE),
+        "export": ("export a checkpoint to GGUF", cmd_export, [
+            A("--checkpoint", required=True), A("--output", required=True),
+            A("--quantize", default="none", choices=["none", "q8_0", "q4_0"]), A("--merge-adapters", action="store_true")]),
+        "registry": ("model candidate registry", cmd_registry, {
+            "dest": "registry_cmd", "parent": [A("--registry", default="registry/candidates.json")],
+            "list": ("", []),
+            "register": ("", [A("--name", required=True), A("--version", required=True), A("--algorithm", required=True),
+                              A("--checkpoint", required=True), A("--metrics", default=None, help="JSON object"),
+                              A("--metrics-file", default=None, help="evaluation results JSON"), A("--tags", nargs="*")]),
+            "promote": ("", [A("--id", required=True),
+                             A("--to", required=True, choices=["shadow", "challenger", "champion", "retired"]),
+                             A("--gate", default=None, help="promotion gate YAML"), A("--reason", default="")]),
+            "rollback": ("", [A("--name", required=True), A("--reason", default="manual rollback")]),
+            "disable": ("", [A("--id", required=True), A("--reason", default="disabled")]),
+        }),
+        "rlaif": ("AI-feedback data generation", cmd_rlaif, {
+            "dest": "rlaif_cmd",
+            "pairwise": ("", _RLAIF_COMMON + [A("--candidates", type=int, default=4)]),
+            "constitutional": ("", _RLAIF_COMMON + [A("--n-principles", type=int, default=2)]),
+        }),
+        "dashboard": ("local read-only dashboard", cmd_dashboard, [
+            A("--runs", nargs="+", default=["runs"]), A("--registry", default="registry/candidates.json"),
+            A("--benchmarks", default="benchmarks"), A("--host", default="127.0.0.1"), A("--port", type=int, default=8765),
+            A("--export", default=None, help="write a JSON snapshot instead of serving")]),
+        "allocation": ("budgeted sequential-allocation benchmark, OPE, A/B, shadow", cmd_allocation, {
+            "dest": "allocation_cmd",
+            "benchmark": ("", [A("--config", required=True), A("--output-dir", default=None)]),
+            "ope": ("", _ALLOC_COMMON + [A("--log", required=True), A("--target", required=True),
+                                        A("--max-weight", type=float, default=20.0), A("--bootstrap", type=int, default=500)]),
+            "ab": ("", _ALLOC_COMMON + [A("--incumbent", required=True), A("--challenger", required=True),
+                                       A("--episodes", type=int, default=400), A("--seed", type=int, default=0),
+                                       A("--challenger-percent", type=float, default=50.0),
+                                       A("--gate-metrics", default=None)]),
+            "shadow": ("", _ALLOC_COMMON + [A("--incumbent", required=True), A("--candidate", required=True),
+                                           A("--episodes", type=int, default=100), A("--seed", type=int, default=0)]),
+        }),
+        "synthesis-ppo": ("tabular actor-critic PPO on synthesis trajectories", cmd_synthesis, [
+            A("--data", required=True), A("--epochs", type=int, default=5), A("--batch-size", type=int, default=8),
+            A("--lr", type=float, default=1e-4), A("--output", default=None)]),
+    }
+
+
+def _add_arguments(parser: argparse.ArgumentParser, args) -> None:
+    for flags, options in args:
+        parser.add_argument(*flags, **options)
 
 
 def build_parser() -> argparse.ArgumentParser:
-    p = argparse.ArgumentParser(prog="forgeline-b200", description="Post-training, distributed training, evaluation, "
-                                "inference and model life cycle for language models on B200.")
-    p.add_argument("--version", action="version", version=f"forgeline-b200 {__version__}")
-    sub = p.add_subparsers(dest="command", required=True)
-
-    s = _add(sub, "presets", cmd_presets, "list model presets")
-    s.add_argument("--count-params", action="store_true")
-    s.add_argument("--vocab-size", type=int, default=65536)
-
-    s = _add(sub, "validate", cmd_validate, "validate an experiment manifest without running it")
-    s.add_argument("manifest")
-    s.add_argument("--world-size", type=int, default=None)
-
-    d = _add(sub, "data", cmd_data, "dataset preparation and validation")
-    ds = d.add_subparsers(dest="data_cmd", required=True)
-    x = ds.add_parser("prepare", help="tokenize a text file into train.bin/val.bin")
-    x.add_argument("--input", required=True)
-    x.add_argument("--output", required=True)
-    x.add_argument("--tokenizer", default="char", help="char | tiktoken[:enc] | hf:<name>")
-    x.add_argument("--val-fraction", type=float, default=0.1)
-    x = ds.add_parser("prepare-hf", help="stream a HuggingFace dataset into shard files")
-    x.add_argument("--dataset", required=True)
-    x.add_argument("--subset", default=None)
-    x.add_argument("--tokenizer", default="Qwen/Qwen2.5-0.5B")
-    x.add_argument("--output", required=True)
-    x.add_argument("--max-tokens", type=int, default=100_000_000)
-    x.add_argument("--shard-size", type=int, default=10_000_000)
-    x = ds.add_parser("shard", help="split a .bin token file into shards")
-    x.add_argument("--input", required=True)
-    x.add_argument("--output", required=True)
-    x.add_argument("--n-shards", type=int, default=16)
-    x = ds.add_parser("gsm8k", help="download GSM8K as verifiable tool-use tasks")
-    x.add_argument("--output", required=True)
-    x.add_argument("--split", default="train")
-    x.add_argument("--limit", type=int, default=None)
-    x = ds.add_parser("validate", help="validate a JSONL dataset against a schema")
-    x.add_argument("--input", required=True)
-    x.add_argument("--kind", required=True, choices=["supervised", "preference", "verifiable", "process", "reward"])
-
-    s = _add(sub, "train", cmd_train, "run a training stage from a manifest")
-    s.add_argument("manifest")
-    s.add_argument("--set", action="append", help="dotted override, e.g. trainer.max_steps=10")
-    s.add_argument("--max-steps", type=int, default=None)
-    s.add_argument("--output-dir", default=None)
-    s.add_argument("--resume", default=None)
-    s.add_argument("--metrics", default="local", help="local | none | wandb | tensorboard")
-
-    for name, fn in (("generate", cmd_generate), ("evaluate", cmd_evaluate), ("serve", cmd_serve)):
-        s = _add(sub, name, fn)
-        s.add_argument("--checkpoint", required=True)
-        s.add_argument("--data-dir", default=None, help="directory with meta.pkl when the checkpoint lacks it")
-        s.add_argument("--device", default="auto")
-        if name == "generate":
-            s.add_argument("--prompt", default="\n")
-            s.add_argument("--max-tokens", type=int, default=200)
-            s.add_argument("--temperature", type=float, default=0.8)
-            s.add_argument("--top-k", type=int, default=50)
-            s.add_argument("--top-p", type=float, default=None)
-            s.add_argument("--min-p", type=float, default=None)
-            s.add_argument("--repetition-penalty", type=float, default=1.0)
-            s.add_argument("--no-cache", action="store_true")
-            s.add_argument("--interactive", action="store_true")
-            s.add_argument("--draft-checkpoint", default=None)
-            s.add_argument("--spec-k", type=int, default=5)
-        elif name == "evaluate":
-            s.add_argument("--suites", nargs="+", default=["gsm8k"])
-            s.add_argument("--n-shot", type=int, default=0)
-            s.add_argument("--max-tasks", type=int, default=0)
-            s.add_argument("--max-tokens", type=int, default=64)
-            s.add_argument("--offline", action="store_true", help="use built-in sample tasks (no download)")
-            s.add_argument("--heldout-data", default=None)
-            s.add_argument("--output", default=None)
-            s.add_argument("--ray-workers", type=int, default=0)
-            s.add_argument("--ray-address", default=None)
-            s.add_argument("--ray-cpus-per-worker", type=float, default=1.0)
-            s.add_argument("--worker-backend", default="ray", choices=["ray", "threads"],
-                           help="where --ray-workers run: Ray actors or in-process threads")
+    root = argparse.ArgumentParser(prog="forgeline-b200", description="Post-training, distributed training, "
+                                   "evaluation, inference and model life cycle for language models on B200.")
+    root.add_argument("--version", action="version", version=f"forgeline-b200 {__version__}")
+    commands = root.add_subparsers(dest="command", required=True)
+    for name, (help_text, handler, body) in _command_table().items():
+        cmd = commands.add_parser(name, help=help_text)
+        cmd.set_defaults(func=handler)
+        if isinstance(body, dict):
+            _add_arguments(cmd, body.get("parent", []))
+            subs = cmd.add_subparsers(dest=body["dest"], required=True)
+            for sub_name, entry in body.items():
+                if sub_name in ("dest", "parent"):
+                    continue
+                sub_help, sub_args = entry
+                _add_arguments(subs.add_parser(sub_name, help=sub_help or None), sub_args)
         else:
-            s.add_argument("--host", default="127.0.0.1")
-            s.add_argument("--port", type=int, default=8000)
-            s.add_argument("--model-name", default="forgeline-model")
-            s.add_argument("--max-batch", type=int, default=8)
-            s.add_argument("--max-seq-len", type=int, default=None)
-            s.add_argument("--routing", default=None, help="routing policy JSON")
-            s.add_argument("--metrics", default="none")
-            s.add_argument("--output-dir", default="runs/serve")
-
-    s = _add(sub, "export", cmd_export, "export a checkpoint to GGUF")
-    s.add_argument("--checkpoint", required=True)
-    s.add_argument("--output", required=True)
-    s.add_argument("--quantize", default="none", choices=["none", "q8_0", "q4_0"])
-    s.add_argument("--merge-adapters", action="store_true")
-
-    r = _add(sub, "registry", cmd_registry, "model candidate registry")
-    r.add_argument("--registry", default="registry/candidates.json")
-    rs = r.add_subparsers(dest="registry_cmd", required=True)
-    rs.add_parser("list")
-    x = rs.add_parser("register")
-    for flag in ("--name", "--version", "--algorithm", "--checkpoint"):
-        x.add_argument(flag, required=True)
-    x.add_argument("--metrics", default=None, help="JSON object")
-    x.add_argument("--metrics-file", default=None, help="evaluation results JSON")
-    x.add_argument("--tags", nargs="*")
-    x = rs.add_parser("promote")
-    x.add_argument("--id", required=True)
-    x.add_argument("--to", required=True, choices=["shadow", "challenger", "champion", "retired"])
-    x.add_argument("--gate", default=None, help="promotion gate YAML")
-    x.add_argument("--reason", default="")
-    x = rs.add_parser("rollback")
-    x.add_argument("--name", required=True)
-    x.add_argument("--reason", default="manual rollback")
-    x = rs.add_parser("disable")
-    x.add_argument("--id", required=True)
-    x.add_argument("--reason", default="disabled")
-
-    a = _add(sub, "rlaif", cmd_rlaif, "AI-feedback data generation")
-    asub = a.add_subparsers(dest="rlaif_cmd", required=True)
-    for name in ("pairwise", "constitutional"):
-        x = asub.add_parser(name)
-        x.add_argument("--output", required=True)
-        x.add_argument("--n-prompts", type=int, default=10)
-        x.add_argument("--checkpoint", default=None)
-        x.add_argument("--data-dir", default=None)
-        x.add_argument("--device", default="auto")
-        x.add_argument("--max-tokens", type=int, default=128)
-        if name == "pairwise":
-            x.add_argument("--candidates", type=int, default=4)
-        else:
-            x.add_argument("--n-principles", type=int, default=2)
-
-    s = _add(sub, "dashboard", cmd_dashboard, "local read-only dashboard")
-    s.add_argument("--runs", nargs="+", default=["runs"])
-    s.add_argument("--registry", default="registry/candidates.json")
-    s.add_argument("--benchmarks", default="benchmarks")
-    s.add_argument("--host", default="127.0.0.1")
-    s.add_argument("--port", type=int, default=8765)
-    s.add_argument("--export", default=None, help="write a JSON snapshot instead of serving")
-
-    al = _add(sub, "allocation", cmd_allocation, "budgeted sequential-allocation benchmark, OPE, A/B, shadow")
-    als = al.add_subparsers(dest="allocation_cmd", required=True)
-    x = als.add_parser("benchmark")
-    x.add_argument("--config", required=True)
-    x.add_argument("--output-dir", default=None)
-    for name in ("ope", "ab", "shadow"):
-        x = als.add_parser(name)
-        x.add_argument("--env", default=None)
-        x.add_argument("--metrics", default="none")
-        x.add_argument("--output-dir", default="runs/allocation")
-        if name == "ope":
-            x.add_argument("--log", required=True)
-            x.add_argument("--target", required=True)
-            x.add_argument("--max-weight", type=float, default=20.0)
-            x.add_argument("--bootstrap", type=int, default=500)
-        elif name == "ab":
-            x.add_argument("--incumbent", required=True)
-            x.add_argument("--challenger", required=True)
-            x.add_argument("--episodes", type=int, default=400)
-            x.add_argument("--seed", type=int, default=0)
-            x.add_argument("--challenger-percent", type=float, default=50.0)
-            x.add_argument("--gate-metrics", default=None)
-        else:
-            x.add_argument("--incumbent", required=True)
-            x.add_argument("--candidate", required=True)
-            x.add_argument("--episodes", type=int, default=100)
-            x.add_argument("--seed", type=int, default=0)
-
-    s = _add(sub, "synthesis-ppo", cmd_synthesis, "tabular actor-critic PPO on synthesis trajectories")
-    s.add_argument("--data", required=True)
-    s.add_argument("--epochs", type=int, default=5)
-    s.add_argument("--batch-size", type=int, default=8)
-    s.add_argument("--lr", type=float, default=1e-4)
-    s.add_argument("--output", default=None)
-    return p
+            _add_arguments(cmd, body)
+    return root
 
 
 def main(argv: Optional[List[str]] = None) -> int:
