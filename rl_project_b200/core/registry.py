@@ -1,4 +1,10 @@
-"""Named factory registry (``src/forgeline/core/registry.py:12-50`` semantics)."""
+"""Named registries of factories (the contract of ``src/forgeline/core/registry.py:12-50``).
+
+A ``Registry`` maps names to objects of one kind (algorithms, verifiers, reward providers, ...).  ``register``
+works as a call (``reg.register("x", obj)``) or a decorator (``@reg.register("x")``); registering a name twice
+and looking up an unknown name are configuration errors that list what is registered.  Iteration yields the
+names in sorted order.
+"""
 
 from __future__ import annotations
 
@@ -14,19 +20,22 @@ class Registry(Generic[T]):
         self.kind = kind
         self._table: Dict[str, T] = {}
 
-    def register(self, name: str, item: Optional[T] = None):
-        def add(obj: T) -> T:
-            if name in self._table:
-                raise ConfigError(f"{self.kind} {name!r} is already registered")
-            self._table[name] = obj
-            return obj
+    def _insert(self, name: str, obj: T) -> T:
+        if name in self._table:
+            raise ConfigError(f"{self.kind} {name!r} is already registered")
+        self._table[name] = obj
+        return obj
 
-        return add(item) if item is not None else add
+    def register(self, name: str, item: Optional[T] = None):
+        if item is not None:
+            return self._insert(name, item)
+        return lambda obj: self._insert(name, obj)
 
     def get(self, name: str) -> T:
-        if name not in self._table:
+        found = self._table.get(name)
+        if found is None and name not in self._table:
             raise ConfigError(f"Unknown {self.kind} {name!r}. Registered: {self.names()}")
-        return self._table[name]
+        return found  # type: ignore[return-value]
 
     def names(self) -> list[str]:
         return sorted(self._table)
