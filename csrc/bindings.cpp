@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include "launchers.h"
+#include "tmap.h"
 
 namespace {
 
@@ -765,6 +766,7 @@ std::tuple<py::bytes, int64_t> peer_handle(const at::Tensor& buf) {
   }
   CUdeviceptr base = 0;
   size_t size = 0;
+  TORCH_CHECK(rlb_tmap::bind_thread_context(), "peer_handle: no CUDA context for this thread");
   TORCH_CHECK(address_range(&base, &size, (CUdeviceptr)buf.data_ptr()) == CUDA_SUCCESS,
               "peer_handle: cuMemGetAddressRange failed");
   const int64_t offset = (int64_t)((CUdeviceptr)buf.data_ptr() - base);

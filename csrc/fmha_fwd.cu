@@ -37,6 +37,7 @@
 #include <stdint.h>
 
 #include "sm100.cuh"
+#include "tmap.h"
 
 namespace fmha {
 
@@ -810,21 +811,8 @@ __global__ void __launch_bounds__(PAIR_THREADS, 1) fmha_fwd_pair_kernel(const __
 }
 
 // ------------------------------------------------------------------ host
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = (EncodeTiledFn)ptr;
-  }
-  return fn;
-}
+using rlb_tmap::EncodeTiledFn;
+using rlb_tmap::encode_fn;
 
 // [B][T][H * D] bf16 viewed as a 3-D map (columns, tokens, batch); box = 64 columns x 128 tokens x 1.
 // Rows past T read as zeros, so a tile never spills into the next sequence.

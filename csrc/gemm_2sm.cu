@@ -34,8 +34,10 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <stdio.h>
 
 #include "sm100.cuh"
+#include "tmap.h"
 
 namespace gemm2 {
 
@@ -486,21 +488,8 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
 }
 
 // ------------------------------------------------------------------ host
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = (EncodeTiledFn)ptr;
-  }
-  return fn;
-}
+using rlb_tmap::EncodeTiledFn;
+using rlb_tmap::encode_fn;
 
 // 2-D tensor map over a row-major matrix [rows][cols] (cols contiguous, leading dimension `ld` elements),
 // box {box_cols, box_rows}, 128-B swizzle (box_cols * element size == 128 B).
@@ -512,9 +501,13 @@ static bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int esize, const vo
   cuuint64_t strides[1] = {(cuuint64_t)(ld * esize)};
   cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  return enc(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  const CUresult r = enc(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    fprintf(stderr, "gemm2: tensor map rejected (CUresult %d): ptr %p rows %lld cols %lld ld %lld esize %d box %dx%d\n",
+            (int)r, ptr, rows, cols, ld, esize, box_cols, box_rows);
+  return r == CUDA_SUCCESS;
 }
 
 // Clusters of this kernel that can be resident at once on device `dev` (cached per instantiation and

@@ -25,6 +25,7 @@
 #include <stdint.h>
 
 #include "sm100.cuh"
+#include "tmap.h"
 
 namespace gemm {
 
@@ -498,21 +499,8 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ CU
 }
 
 // ------------------------------------------------------------------ host
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = (EncodeTiledFn)p;
-  }
-  return fn;
-}
+using rlb_tmap::EncodeTiledFn;
+using rlb_tmap::encode_fn;
 
 // 2-D bf16 tensor map over a row-major matrix [rows][cols] (cols contiguous), box {64 cols, box_rows}.
 static bool make_map(CUtensorMap* m, const void* ptr, long long rows, long long cols, long long ld, int box_rows) {

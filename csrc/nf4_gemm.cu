@@ -26,6 +26,7 @@
 #include <stdint.h>
 
 #include "sm100.cuh"
+#include "tmap.h"
 
 namespace nf4gemm {
 
@@ -252,21 +253,8 @@ __global__ void __launch_bounds__(THREADS, 1) nf4_gemm_kernel(const __grid_const
   }
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = (EncodeTiledFn)ptr;
-  }
-  return fn;
-}
+using rlb_tmap::EncodeTiledFn;
+using rlb_tmap::encode_fn;
 
 }  // namespace nf4gemm
 

@@ -60,24 +60,41 @@ def nsub_for(M: int, N: int, epi: int, device_index: int = 0, a_mn: int = 0) -> 
     return 2 if wave_fill(512) + 0.05 >= wave_fill(256) else 1
 
 
+def _describe(t: torch.Tensor) -> str:
+    return (f"{tuple(t.shape)} stride {tuple(t.stride())} {t.dtype} {t.device} ptr%16={t.data_ptr() % 16} "
+            f"contiguous={t.is_contiguous()}")
+
+
 def _run(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha):
-    if _KERNEL == "1sm":
-        native().gemm(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None)
-    else:
-        native().gemm2(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None, 0,
-                       nsub_for(M, N, epi, a.device.index or 0, a_mn))
+    try:
+        if _KERNEL == "1sm":
+            native().gemm(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None)
+        else:
+            native().gemm2(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None, 0,
+                           nsub_for(M, N, epi, a.device.index or 0, a_mn))
+    except RuntimeError as e:
+        raise RuntimeError(f"{e} [a_mn={a_mn} b_mn={b_mn} epi={epi} M={M} N={N} K={K} lda={lda} ldb={ldb} "
+                           f"ldc={ldc}; A {_describe(a)}; B {_describe(b)}; C {_describe(out)}; current device "
+                           f"{torch.cuda.current_device()}]") from e
 
 
 def _ok_ptr(t: torch.Tensor) -> bool:
     return t.data_ptr() % 16 == 0
 
 
+def _dense(t: torch.Tensor) -> torch.Tensor:
+    """``t`` as a contiguous tensor whose base is 16-byte aligned (the TMA descriptors need both); a contiguous
+    view at an odd storage offset -- e.g. a gradient slice handed over by autograd -- is copied."""
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
 def gemm_nt(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``a [M, K] @ b[N, K]^T`` in bf16 (fp32 accumulate)."""
     M, K = a.shape
     N = b.shape[0]
-    a = a.contiguous()
-    b = b.contiguous()
+    a = _dense(a)
+    b = _dense(b)
     if out is None:
         out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
     _run(a, b, out, 0, 0, 0, M, N, K, K, K, out.stride(0), alpha)
@@ -88,8 +105,8 @@ def gemm_nn(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0) -> torch.Tenso
     """``a [M, K] @ b [K, N]`` (b read MN-major, no transpose)."""
     M, K = a.shape
     N = b.shape[1]
-    a = a.contiguous()
-    b = b.contiguous()
+    a = _dense(a)
+    b = _dense(b)
     out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
     _run(a, b, out, 0, 1, 0, M, N, K, K, N, N, alpha)
     return out
@@ -100,8 +117,8 @@ def gemm_tn(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0, out: Optional[
     """``a [K, M]^T @ b [K, N]`` -> ``[M, N]`` (both read MN-major).  fp32 ``out`` + ``accumulate`` adds into it."""
     K, M = a.shape
     N = b.shape[1]
-    a = a.contiguous()
-    b = b.contiguous()
+    a = _dense(a)
+    b = _dense(b)
     if out is None:
         out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
         epi = 0
@@ -126,7 +143,7 @@ class _Linear(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         x2, w = ctx.saved_tensors
-        dy = dy.contiguous()
+        dy = _dense(dy)
         dx = gemm_nn(dy, w) if ctx.needs_input_grad[0] else None
         dw = gemm_tn(dy, x2) if ctx.needs_input_grad[1] else None
         return dx, dw

@@ -25,6 +25,12 @@ sender's messages in the order the receiver consumes them, which is what lets
 receives be posted early (on a shared group, an early receive could be
 matched ahead of a send the peer is blocked on).  Without directional groups
 the runner posts each receive when it is needed, on the default group.
+
+On NCCL the look-ahead defaults to 0 (each receive posted when it is consumed, still on its directional
+group): in eager-init mode NCCL treats every unbatched send / receive as a collective of its communicator,
+and with receives posted ahead a 2-stage 1F1B run deadlocked -- the first stage's host blocked posting a
+gradient receive while the last stage's compute stream waited on an activation receive queued behind the
+early ones.  ``RLB_PP_LOOKAHEAD`` overrides the depth; gloo keeps the default of 2.
 """
 
 from __future__ import annotations
@@ -114,6 +120,15 @@ def _p2p(op, tensor: torch.Tensor, peer: int, tag: int, group: Any):
     return op(tensor, peer, tag=tag, group=group)
 
 
+def _backend(group: Any) -> str:
+    if not dist.is_initialized():
+        return ""
+    try:
+        return str(dist.get_backend(group))
+    except (RuntimeError, ValueError):
+        return ""
+
+
 class _Inbox:
     """Receives of one direction, posted up to ``depth`` messages ahead in the order they will be consumed."""
 
@@ -154,7 +169,11 @@ class PipelineRunner:
                           ([] if self.last else ["pp_act_out", "pp_grad_in"]))
         self.groups = g if directional else {}
         la = os.environ.get("RLB_PP_LOOKAHEAD")  # diagnostics / A-B: receives posted ahead (0: when needed)
-        self.lookahead = (int(la) if la is not None else lookahead) if directional else 0
+        if la is not None:
+            lookahead = int(la)
+        elif _backend(group if group is not None else next(iter(self.groups.values()), None)) == "nccl":
+            lookahead = 0
+        self.lookahead = lookahead if directional else 0
 
     def _g(self, name: str):
         return self.groups.get(name, self.group)

@@ -93,3 +93,29 @@ def test_gemm2sm_agrees_with_one_sm_kernel(nsub):
         native().gemm2(a, b, o2, 0, 0, 0, M, N, K, K, K, N, 1.0, None, 0, nsub)
         torch.cuda.synchronize()
         assert _rel(o2, o1.float()) < 4e-3
+
+
+def test_tma_launchers_work_from_a_fresh_thread():
+    """A thread that has made no CUDA runtime call (like autograd's backward workers) can launch the TMA
+    kernels: the launchers bind the device's primary context before encoding tensor maps."""
+    import threading
+
+    from rl_project_b200.ops import gemm
+
+    a = torch.randn(512, 256, device="cuda").to(BF)
+    b = torch.randn(384, 256, device="cuda").to(BF)
+    ref = a.float() @ b.float().t()
+    out, err = {}, []
+
+    def work():
+        try:
+            out["y"] = gemm.gemm_nt(a, b)
+            torch.cuda.current_stream().synchronize()
+        except Exception as e:  # noqa: BLE001 - reported below
+            err.append(repr(e))
+
+    t = threading.Thread(target=work)
+    t.start()
+    t.join(120)
+    assert not err, err
+    assert _rel(out["y"], ref) < 8e-3
