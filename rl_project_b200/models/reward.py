@@ -1,11 +1,19 @@
-"""Reward models (``src/forgeline/models/reward.py`` contract): a native
-transformer backbone with a scalar head (last or mean pooling), the
-Bradley-Terry pairwise loss, and an optional HuggingFace encoder reward model."""
+"""Reward models (contract of ``src/forgeline/models/reward.py``: class names, constructor arguments, the
+``reward_head`` parameter name and the ``{model, pooling}`` checkpoint dict).
+
+``SequenceRewardModel`` pools the backbone's final hidden states with one weighted reduction: a ``[B, T]``
+pooling matrix (a one-hot at each row's last real token for ``last``, ``mask / length`` for ``mean``)
+contracted with ``h [B, T, C]``, followed by the bias-free scalar head -- the same code path with or
+without an attention mask (no mask = every position is real).
+
+``EncoderRewardModel`` is the text-level variant on a HuggingFace encoder (its CLS state through a small
+MLP head): ``regression`` (sigmoid output, MSE to scalar targets) or ``preference`` (raw score,
+Bradley-Terry on chosen / rejected texts).  Both fits run through one epoch loop over index batches.
+"""
 
 from __future__ import annotations
 
-import random
-from typing import Any, Dict, Mapping, Optional
+from typing import Any, Callable, Dict, Iterable, List, Mapping, Optional, Sequence
 
 import torch
 import torch.nn as nn
@@ -16,34 +24,33 @@ from rl_project_b200.core.errors import ConfigError, OptionalDependencyError
 from rl_project_b200.models.transformer.model import TransformerLM
 
 
+def pooling_weights(mask: torch.Tensor, pooling: str) -> torch.Tensor:
+    """``[B, T]`` weights that reduce hidden states to one vector per row."""
+    m = mask.float()
+    if pooling == "mean":
+        return m / m.sum(1, keepdim=True).clamp_min(1.0)
+    last = (m.sum(1).long() - 1).clamp_min(0)
+    return F.one_hot(last, m.shape[1]).float()
+
+
 class SequenceRewardModel(nn.Module):
     def __init__(self, spec: ModelSpec, backbone: Optional[TransformerLM] = None, pooling: str = "last"):
         super().__init__()
         if pooling not in ("last", "mean"):
             raise ValueError("pooling must be 'last' or 'mean'")
-        self.spec = spec
-        self.pooling = pooling
-        self.backbone = backbone or TransformerLM(spec)
+        self.spec, self.pooling = spec, pooling
+        self.backbone = backbone if backbone is not None else TransformerLM(spec)
         self.reward_head = nn.Linear(spec.n_embd, 1, bias=False)
 
     def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         h = self.backbone.forward_hidden(input_ids)
-        if self.pooling == "mean":
-            if attention_mask is None:
-                pooled = h.mean(1)
-            else:
-                m = attention_mask.unsqueeze(-1).to(h.dtype)
-                pooled = (h * m).sum(1) / m.sum(1).clamp(min=1.0)
-        elif attention_mask is None:
-            pooled = h[:, -1]
-        else:
-            last = attention_mask.long().sum(1).clamp(min=1) - 1
-            pooled = h[torch.arange(h.shape[0], device=h.device), last]
+        mask = attention_mask if attention_mask is not None else torch.ones(h.shape[:2], device=h.device)
+        w = pooling_weights(mask.to(h.device), self.pooling).to(h.dtype)
+        pooled = torch.bmm(w.unsqueeze(1), h).squeeze(1)
         return self.reward_head(pooled.to(self.reward_head.weight.dtype)).squeeze(-1)
 
     def freeze_backbone(self) -> None:
-        for p in self.backbone.parameters():
-            p.requires_grad = False
+        self.backbone.requires_grad_(False)
 
     def state_for_checkpoint(self) -> Dict[str, Any]:
         return {"model": self.state_dict(), "pooling": self.pooling}
@@ -53,16 +60,20 @@ class SequenceRewardModel(nn.Module):
 
 
 def bradley_terry_loss(chosen_scores: torch.Tensor, rejected_scores: torch.Tensor) -> torch.Tensor:
-    return -F.logsigmoid(chosen_scores.float() - rejected_scores.float()).mean()
+    """Mean ``-log sigmoid(chosen - rejected)`` (computed in fp32)."""
+    return F.softplus(rejected_scores.float() - chosen_scores.float()).mean()
 
 
 class EncoderRewardModel(nn.Module):
-    """Encoder (CLS) reward model on text, ``regression`` (sigmoid + MSE) or ``preference`` (Bradley-Terry)."""
+    """Encoder reward model on raw text; head: dropout, ``h -> h/2`` GELU layer, then a scalar read-out
+    (``regression`` adds dropout before it and a sigmoid after it)."""
+
+    _OBJECTIVES = ("regression", "preference")
 
     def __init__(self, backbone: str = "bert-base-uncased", objective: str = "regression", dropout: float = 0.1,
                  max_length: int = 128):
         super().__init__()
-        if objective not in ("regression", "preference"):
+        if objective not in self._OBJECTIVES:
             raise ConfigError("objective must be regression|preference")
         try:
             from transformers import AutoModel, AutoTokenizer
@@ -71,68 +82,65 @@ class EncoderRewardModel(nn.Module):
         self.objective, self.max_length = objective, max_length
         self.tokenizer = AutoTokenizer.from_pretrained(backbone)
         self.encoder = AutoModel.from_pretrained(backbone)
-        h = self.encoder.config.hidden_size
-        layers = [nn.Dropout(dropout), nn.Linear(h, h // 2), nn.GELU()]
-        layers += [nn.Dropout(dropout), nn.Linear(h // 2, 1), nn.Sigmoid()] if objective == "regression" \
-            else [nn.Linear(h // 2, 1)]
-        self.head = nn.Sequential(*layers)
+        self.head = self._head(self.encoder.config.hidden_size, dropout, objective == "regression")
         self.trained = False
 
-    def forward(self, texts) -> torch.Tensor:
-        enc = self.tokenizer(list(texts), return_tensors="pt", padding=True, truncation=True, max_length=self.max_length)
+    @staticmethod
+    def _head(h: int, dropout: float, bounded: bool) -> nn.Sequential:
+        readout = [nn.Dropout(dropout), nn.Linear(h // 2, 1), nn.Sigmoid()] if bounded else [nn.Linear(h // 2, 1)]
+        return nn.Sequential(nn.Dropout(dropout), nn.Linear(h, h // 2), nn.GELU(), *readout)
+
+    def forward(self, texts: Iterable[str]) -> torch.Tensor:
         dev = next(self.parameters()).device
-        out = self.encoder(input_ids=enc["input_ids"].to(dev), attention_mask=enc["attention_mask"].to(dev))
-        return self.head(out.last_hidden_state[:, 0]).squeeze(-1)
+        enc = self.tokenizer(list(texts), return_tensors="pt", padding=True, truncation=True,
+                             max_length=self.max_length).to(dev)
+        cls = self.encoder(input_ids=enc["input_ids"], attention_mask=enc["attention_mask"]).last_hidden_state[:, 0]
+        return self.head(cls).squeeze(-1)
 
     @torch.no_grad()
-    def score_texts(self, texts, probability: bool = True) -> torch.Tensor:
+    def score_texts(self, texts: Iterable[str], probability: bool = True) -> torch.Tensor:
         self.eval()
         s = self(texts)
-        return torch.sigmoid(s) if (probability and self.objective == "preference") else s
+        return s.sigmoid() if probability and self.objective == "preference" else s
 
-    def _fit(self, batches, loss_fn, epochs, opt, clip=None) -> list:
-        hist = []
+    def _epochs(self, n: int, batch_size: int, epochs: int, opt: torch.optim.Optimizer,
+                loss_of: Callable[[List[int]], torch.Tensor], order: Callable[[], List[int]],
+                clip: Optional[float] = None) -> List[float]:
+        """Mean loss per epoch; each epoch visits ``order()`` in ``batch_size`` slices."""
+        history = []
         self.train()
         for _ in range(epochs):
-            tot, n = 0.0, 0
-            for b in batches():
-                loss = loss_fn(b)
+            idx = order()
+            losses = []
+            for lo in range(0, n, batch_size):
+                loss = loss_of(idx[lo:lo + batch_size])
                 opt.zero_grad()
                 loss.backward()
                 if clip:
-                    torch.nn.utils.clip_grad_norm_(self.parameters(), clip)
+                    nn.utils.clip_grad_norm_(self.parameters(), clip)
                 opt.step()
-                tot += float(loss.detach())
-                n += 1
-            hist.append(tot / max(n, 1))
+                losses.append(float(loss.detach()))
+            history.append(sum(losses) / max(len(losses), 1))
         self.trained = True
-        return hist
+        return history
 
-    def fit_regression(self, texts, targets, epochs: int = 3, lr: float = 1e-4, batch_size: int = 16) -> list:
+    def fit_regression(self, texts: Sequence[str], targets: Iterable[float], epochs: int = 3, lr: float = 1e-4,
+                       batch_size: int = 16) -> List[float]:
         y = torch.tensor(list(targets), dtype=torch.float32)
-        opt = torch.optim.Adam(self.parameters(), lr=lr)
 
-        def batches():
-            for i in range(0, len(texts), batch_size):
-                yield i
+        def loss_of(idx):
+            pred = self([texts[i] for i in idx])
+            return F.mse_loss(pred, y[idx].to(pred.device))
 
-        def loss_fn(i):
-            p = self(texts[i:i + batch_size])
-            return F.mse_loss(p, y[i:i + batch_size].to(p.device))
+        return self._epochs(len(texts), batch_size, epochs, torch.optim.Adam(self.parameters(), lr=lr), loss_of,
+                            lambda: list(range(len(texts))))
 
-        return self._fit(batches, loss_fn, epochs, opt)
+    def fit_preference(self, pairs: Sequence[Sequence[str]], epochs: int = 3, lr: float = 2e-5, batch_size: int = 16,
+                       seed: int = 0) -> List[float]:
+        gen = torch.Generator().manual_seed(seed)
 
-    def fit_preference(self, pairs, epochs: int = 3, lr: float = 2e-5, batch_size: int = 16, seed: int = 0) -> list:
-        opt = torch.optim.AdamW(self.parameters(), lr=lr)
-        rng = random.Random(seed)
-
-        def batches():
-            order = list(range(len(pairs)))
-            rng.shuffle(order)
-            for i in range(0, len(order), batch_size):
-                yield order[i:i + batch_size]
-
-        def loss_fn(idx):
+        def loss_of(idx):
             return bradley_terry_loss(self([pairs[j][0] for j in idx]), self([pairs[j][1] for j in idx]))
 
-        return self._fit(batches, loss_fn, epochs, opt, clip=1.0)
+        return self._epochs(len(pairs), batch_size, epochs, torch.optim.AdamW(self.parameters(), lr=lr), loss_of,
+                            lambda: torch.randperm(len(pairs), generator=gen).tolist(), clip=1.0)
