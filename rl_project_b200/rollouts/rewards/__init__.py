@@ -1,13 +1,16 @@
-"""Reward providers: rules, verifier adapters, composites, process rewards, critics, learned models.
+"""Reward providers: rules, verifier adapters, composites, process rewards, critics and learned models.
 
-``build_reward_provider`` reads a manifest ``reward`` mapping
-(``src/forgeline/rollouts/rewards/__init__.py:16-56`` keys)."""
+``build_reward_provider`` turns a manifest ``reward`` mapping into a provider (the ``type`` values and keys
+of ``src/forgeline/rollouts/rewards/__init__.py``) through the ``_BUILDERS`` table: ``verifier``, ``rule``,
+``composite`` (members built recursively, each with its ``weight``), ``process``, ``tagged`` (tagged-answer
+verifier plus the tag-format bonus unless ``format_bonus`` is false), ``critic`` and ``synthesis_rule``.
+"""
 
-from typing import Any, Dict
+from typing import Any, Callable, Dict
 
 from rl_project_b200.core.errors import ConfigError
 from rl_project_b200.rollouts.rewards.composite import (CallableReward, CompositeReward, TagFormatReward,
-                                                        VerifierReward, score_trajectories)
+                                                        VerifierReward, batch_scores, score_trajectories)
 from rl_project_b200.rollouts.rewards.critic import CriticReward, heuristic_critic_score
 from rl_project_b200.rollouts.rewards.learned import BlendedReward, RewardModelProvider
 from rl_project_b200.rollouts.rewards.process import ProcessReward, compute_process_reward, parse_steps, score_step
@@ -18,30 +21,51 @@ RULE_REWARDS = {"length": LengthReward, "text_format": TextFormatReward, "repeti
                 "constant": ConstantReward}
 
 
-def build_reward_provider(config: Dict[str, Any]):
-    kind = config.get("type")
-    if kind == "verifier":
-        params = {k: v for k, v in config.items() if k not in ("type", "verifier", "target_key", "weight")}
-        return VerifierReward(build_verifier(config["verifier"], **params), target_key=config.get("target_key", "answer"),
-                              weight=float(config.get("weight", 1.0)))
-    if kind == "rule":
-        return RULE_REWARDS[config["name"]](**{k: v for k, v in config.items() if k not in ("type", "name", "weight")})
-    if kind == "composite":
-        provs = [(build_reward_provider({k: v for k, v in p.items() if k != "weight"}), float(p.get("weight", 1.0)))
-                 for p in config["providers"]]
-        return CompositeReward(provs, clip=tuple(config["clip"]) if config.get("clip") else None)
-    if kind == "process":
-        return ProcessReward(float(config.get("gamma", 0.9)), float(config.get("step_weight", 1.0)),
-                             config.get("target_key", "answer"), bool(config.get("execute_code", True)))
-    if kind == "tagged":
-        base = VerifierReward(build_verifier("tagged_answer"), target_key=config.get("target_key", "answer"))
-        if config.get("format_bonus", True):
-            return CompositeReward([(base, 1.0), (TagFormatReward(), 1.0)], name="tagged+format")
-        return base
-    if kind == "critic":
-        return CriticReward(mode=config.get("mode", "heuristic"))
-    if kind == "synthesis_rule":
-        from rl_project_b200.domains.synthesis.reward import SynthesisRuleReward
+def _without(cfg: Dict[str, Any], *keys: str) -> Dict[str, Any]:
+    return {k: v for k, v in cfg.items() if k not in keys}
 
-        return SynthesisRuleReward(decode_from_text=bool(config.get("decode_from_text", True)))
-    raise ConfigError(f"unknown reward type {kind!r}")
+
+def _verifier(cfg):
+    params = _without(cfg, "type", "verifier", "target_key", "weight")
+    return VerifierReward(build_verifier(cfg["verifier"], **params), target_key=cfg.get("target_key", "answer"),
+                          weight=float(cfg.get("weight", 1.0)))
+
+
+def _rule(cfg):
+    return RULE_REWARDS[cfg["name"]](**_without(cfg, "type", "name", "weight"))
+
+
+def _composite(cfg):
+    members = [(build_reward_provider(_without(m, "weight")), float(m.get("weight", 1.0))) for m in cfg["providers"]]
+    return CompositeReward(members, clip=tuple(cfg["clip"]) if cfg.get("clip") else None)
+
+
+def _process(cfg):
+    return ProcessReward(float(cfg.get("gamma", 0.9)), float(cfg.get("step_weight", 1.0)),
+                         cfg.get("target_key", "answer"), bool(cfg.get("execute_code", True)))
+
+
+def _tagged(cfg):
+    answer = VerifierReward(build_verifier("tagged_answer"), target_key=cfg.get("target_key", "answer"))
+    if not cfg.get("format_bonus", True):
+        return answer
+    return CompositeReward([(answer, 1.0), (TagFormatReward(), 1.0)], name="tagged+format")
+
+
+def _synthesis(cfg):
+    from rl_project_b200.domains.synthesis.reward import SynthesisRuleReward
+
+    return SynthesisRuleReward(decode_from_text=bool(cfg.get("decode_from_text", True)))
+
+
+_BUILDERS: Dict[str, Callable[[Dict[str, Any]], Any]] = {
+    "verifier": _verifier, "rule": _rule, "composite": _composite, "process": _process, "tagged": _tagged,
+    "critic": lambda cfg: CriticReward(mode=cfg.get("mode", "heuristic")), "synthesis_rule": _synthesis,
+}
+
+
+def build_reward_provider(config: Dict[str, Any]):
+    build = _BUILDERS.get(config.get("type"))
+    if build is None:
+        raise ConfigError(f"unknown reward type {config.get('type')!r}")
+    return build(config)

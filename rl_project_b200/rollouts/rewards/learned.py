@@ -1,4 +1,10 @@
-"""Rewards from learned models (``src/forgeline/rollouts/rewards/learned.py``)."""
+"""Rewards from learned models (the providers of ``src/forgeline/rollouts/rewards/learned.py``).
+
+``RewardModelProvider`` scores a whole batch with one forward of the sequence reward model: each
+trajectory's ``prompt + response`` ids (the last ``max_length`` of them) are right-padded into one
+``[B, T]`` tensor and the attention mask tells the model's pooling where each row ends.
+``BlendedReward`` mixes a rule score with a neural score and clips to [0, 1].
+"""
 
 from __future__ import annotations
 
@@ -17,17 +23,22 @@ class RewardModelProvider:
         self.max_length = max_length or model.spec.block_size
 
     @torch.no_grad()
+    def score_many(self, trajectories: List[Trajectory]) -> List[RewardResult]:
+        if not trajectories:
+            return []
+        dev = next(self.model.parameters()).device
+        rows = [torch.cat([t.prompt_ids, t.response_ids])[-self.max_length:] for t in trajectories]
+        width = max(r.numel() for r in rows)
+        ids = torch.zeros(len(rows), width, dtype=torch.long)
+        mask = torch.zeros(len(rows), width, dtype=torch.long)
+        for i, r in enumerate(rows):
+            ids[i, :r.numel()] = r
+            mask[i, :r.numel()] = 1
+        scores = self.model(ids.to(dev), mask.to(dev)).float().cpu().tolist()
+        return [RewardResult(v) for v in scores]
+
     def score(self, trajectory: Trajectory) -> RewardResult:
         return self.score_many([trajectory])[0]
-
-    @torch.no_grad()
-    def score_many(self, trajectories: List[Trajectory]) -> List[RewardResult]:
-        dev = next(self.model.parameters()).device
-        out = []
-        for t in trajectories:
-            ids = torch.cat([t.prompt_ids, t.response_ids])[None, -self.max_length:].to(dev)
-            out.append(RewardResult(float(self.model(ids).float().item())))
-        return out
 
 
 class BlendedReward:
@@ -39,8 +50,9 @@ class BlendedReward:
 
     def score(self, trajectory: Trajectory) -> RewardResult:
         rule = float(self.rule_fn(trajectory))
+        parts = {"rule": rule}
         if self.neural is None:
-            return RewardResult(rule, components={"rule": rule})
-        neural = float(self.neural(trajectory))
-        v = max(0.0, min(1.0, (1 - self.neural_weight) * rule + self.neural_weight * neural))
-        return RewardResult(v, components={"rule": rule, "neural": neural})
+            return RewardResult(rule, components=parts)
+        parts["neural"] = float(self.neural(trajectory))
+        mixed = (1.0 - self.neural_weight) * parts["rule"] + self.neural_weight * parts["neural"]
+        return RewardResult(min(1.0, max(0.0, mixed)), components=parts)

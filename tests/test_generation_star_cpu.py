@@ -166,6 +166,10 @@ def test_reward_model_provider_and_blend():
         ref = float(rm(torch.cat([t.prompt_ids, t.response_ids])[None, -16:]))
     assert r == pytest.approx(ref, rel=1e-5)  # the last max_length tokens are scored
     assert [x.value for x in prov.score_many([t, t])] == pytest.approx([r, r])
+    short = Trajectory(prompt_ids=torch.arange(3), response_ids=torch.arange(40, 45))
+    alone = prov.score(short).value
+    # one right-padded forward for a ragged batch scores every row as if it ran alone
+    assert [x.value for x in prov.score_many([t, short])] == pytest.approx([r, alone], rel=1e-4, abs=1e-5)
 
     blend = BlendedReward(lambda _: 0.5, lambda _: 1.0, neural_weight=0.6)
     res = blend.score(t)
