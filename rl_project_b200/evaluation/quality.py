@@ -1,6 +1,7 @@
 """Quality evaluators: held-out loss / perplexity, verifier pass rate, agent accuracy
-(``src/forgeline/evaluation/quality.py:16-89`` metrics).  The pass-rate suite
-decodes all tasks in one batched rollout instead of one generation per task."""
+(``src/forgeline/evaluation/quality.py:16-89`` metrics).  Every suite works on the whole task list at
+once: the pass-rate suite decodes all tasks in one batched rollout and scores them in one batch, the agent
+suite runs all episodes in lock-step, and the held-out loss is read back once for all batches."""
 
 from __future__ import annotations
 
@@ -54,12 +55,13 @@ class VerifierPassRateSuite:
         prompts = [torch.tensor(policy.encode(t.prompt), dtype=torch.long) for t in self.tasks]
         groups = engine.rollout_many(prompts, tasks=[t.to_dict() for t in self.tasks],
                                      prompt_texts=[t.prompt for t in self.tasks]) if self.tasks else []
+        from rl_project_b200.rollouts.rewards.composite import batch_scores
+
+        trajs = [g[0] for g in groups]
         per_item: List[Dict[str, Any]] = []
         passed = malformed = 0
         total = 0.0
-        for task, group in zip(self.tasks, groups):
-            traj = group[0]
-            r = self.reward.score(traj)
+        for task, traj, r in zip(self.tasks, trajs, batch_scores(self.reward, trajs)):  # one batched scoring
             ok = bool(r.passed)
             passed += ok
             malformed += ("error" in r.info) or (r.info.get("predicted", "x") is None)
@@ -87,11 +89,12 @@ class AgentAccuracySuite:
         from rl_project_b200.rollouts.verifiers import TaggedAnswerVerifier
 
         verifier = TaggedAnswerVerifier()
-        correct = used_tool = 0
-        for task in self.tasks:
-            _, _, output = self.engine.run_episode(build_agent_prompt(task.prompt), temperature=0.0)
-            correct += verifier.verify(output, task.answer).value >= 1.0
-            used_tool += "<tool_call>" in output
+        episodes = self.engine.run_episodes([build_agent_prompt(t.prompt) for t in self.tasks], temperature=0.0) \
+            if self.tasks else []  # every task's episode advanced in lock-step
+        outputs = [final for _, _, final in episodes]
+        scores = verifier.verify_many(outputs, [t.answer for t in self.tasks])
+        correct = sum(r.value >= 1.0 for r in scores)
+        used_tool = sum("<tool_call>" in o for o in outputs)
         n = max(len(self.tasks), 1)
         return EvaluationResult(self.name, {"accuracy": correct / n, "tool_use_rate": used_tool / n},
                                 n_samples=len(self.tasks))

@@ -1,8 +1,10 @@
-"""Regression rules: compare a candidate's metrics with a baseline's.
+"""Regression gates: a candidate's metrics against a baseline's (the rule / check / report types and the
+fail-closed semantics of ``src/forgeline/evaluation/regression.py``: a missing or non-finite metric on
+either side fails its check, and an empty rule list never passes).
 
-Fail-closed semantics of ``src/forgeline/evaluation/regression.py:11-65``: a
-missing or non-finite metric on either side fails its check, and an empty rule
-list never passes.
+A rule's direction is a sign: with ``s = +1`` for higher-is-better and ``-1`` for lower-is-better, a check
+passes when ``s * (candidate - baseline) >= -slack``, where the slack is ``max_regression`` (times
+``|baseline|`` for relative rules).
 """
 
 from __future__ import annotations
@@ -11,21 +13,25 @@ import math
 from dataclasses import dataclass, field
 from typing import List, Mapping, Optional
 
-DIRECTIONS = ("higher_is_better", "lower_is_better")
+_SIGN = {"higher_is_better": 1.0, "lower_is_better": -1.0}
+DIRECTIONS = tuple(_SIGN)
 
 
 @dataclass
 class RegressionRule:
     metric: str
     direction: str = "higher_is_better"
-    max_regression: float = 0.0  # allowed worsening (absolute, or a fraction of |baseline| if relative)
+    max_regression: float = 0.0  # allowed worsening: absolute, or a fraction of |baseline| when relative
     relative: bool = False
 
     def validate(self) -> None:
-        if self.direction not in DIRECTIONS:
+        if self.direction not in _SIGN:
             raise ValueError(f"direction must be one of {DIRECTIONS}")
         if self.max_regression < 0:
             raise ValueError("max_regression must be >= 0")
+
+    def slack(self, baseline: float) -> float:
+        return self.max_regression * (abs(baseline) if self.relative else 1.0)
 
 
 @dataclass
@@ -46,27 +52,25 @@ class RegressionReport:
         return [c for c in self.checks if not c.passed]
 
 
-def _finite(v) -> bool:
+def _usable(v) -> bool:
     return isinstance(v, (int, float)) and not isinstance(v, bool) and math.isfinite(float(v))
 
 
-def _check(rule: RegressionRule, c, b) -> RegressionCheck:
-    if not _finite(c):
-        return RegressionCheck(rule.metric, False, c, b, "candidate metric missing or non-finite")
-    if not _finite(b):
-        return RegressionCheck(rule.metric, False, c, b, "baseline metric missing or non-finite")
-    slack = rule.max_regression * (abs(b) if rule.relative else 1.0)
-    if rule.direction == "higher_is_better":
-        bound, ok, op = b - slack, c >= b - slack, ">="
-    else:
-        bound, ok, op = b + slack, c <= b + slack, "<="
-    verdict = "ok" if ok else "regressed"
-    return RegressionCheck(rule.metric, ok, c, b, f"{verdict}: need {op} {bound:.6g}, got {c:.6g}")
+def _check(rule: RegressionRule, cand, base) -> RegressionCheck:
+    for side, v in (("candidate", cand), ("baseline", base)):
+        if not _usable(v):
+            return RegressionCheck(rule.metric, False, cand, base, f"{side} metric missing or non-finite")
+    sign, slack = _SIGN[rule.direction], rule.slack(base)
+    ok = sign * (cand - base) >= -slack
+    limit = base - sign * slack
+    word = "ok" if ok else "regressed"
+    return RegressionCheck(rule.metric, ok, cand, base,
+                           f"{word}: need {'>=' if sign > 0 else '<='} {limit:.6g}, got {cand:.6g}")
 
 
 def evaluate_regression(candidate: Mapping[str, float], baseline: Mapping[str, float],
                         rules: List[RegressionRule]) -> RegressionReport:
-    for r in rules:
-        r.validate()
-    checks = [_check(r, candidate.get(r.metric), baseline.get(r.metric)) for r in rules]
-    return RegressionReport(passed=bool(rules) and all(c.passed for c in checks), checks=checks)
+    for rule in rules:
+        rule.validate()
+    checks = [_check(rule, candidate.get(rule.metric), baseline.get(rule.metric)) for rule in rules]
+    return RegressionReport(passed=bool(checks) and all(c.passed for c in checks), checks=checks)

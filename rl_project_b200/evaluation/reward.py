@@ -1,30 +1,39 @@
-"""Reward statistics over dataset records, policy trajectories and preference pairs
-(``src/forgeline/evaluation/reward.py:11-72`` metrics and keys)."""
+"""Reward evaluation suites (suite names, metric keys and the ``policy_dependent`` flag of
+``src/forgeline/evaluation/reward.py``): reward statistics over dataset records (a property of the data)
+or policy trajectories, and the preference win rate of a scorer.
+
+Statistics are computed on one float64 array: mean, population std, min, max, the improvement over a
+baseline in percent, and the percentage above each threshold.
+"""
 
 from __future__ import annotations
 
-import math
-from typing import Any, Callable, Dict, List, Sequence
+from typing import Any, Callable, Dict, Sequence
+
+import numpy as np
 
 from rl_project_b200.core.protocols import EvaluationResult, RewardProvider, Trajectory
 
 
 def reward_statistics(rewards: Sequence[float], baseline: float = 0.5,
                       thresholds: Sequence[float] = (0.6, 0.75)) -> Dict[str, float]:
-    if not rewards:
+    r = np.asarray(list(rewards), dtype=np.float64)
+    if r.size == 0:
         return {"mean": 0.0, "std": 0.0, "min": 0.0, "max": 0.0, "n": 0}
-    n = len(rewards)
-    mean = math.fsum(rewards) / n
-    out = {"mean": mean, "std": math.sqrt(math.fsum((r - mean) ** 2 for r in rewards) / n),
-           "min": min(rewards), "max": max(rewards), "n": float(n),
-           "improvement_vs_baseline_pct": (mean - baseline) / baseline * 100.0 if baseline else 0.0}
-    for t in thresholds:
-        out[f"pct_above_{t}"] = 100.0 * sum(r > t for r in rewards) / n
-    return out
+    mean = float(r.mean())
+    stats = {"mean": mean, "std": float(r.std()), "min": float(r.min()), "max": float(r.max()), "n": float(r.size),
+             "improvement_vs_baseline_pct": 100.0 * (mean - baseline) / baseline if baseline else 0.0}
+    stats.update({f"pct_above_{t}": 100.0 * float((r > t).mean()) for t in thresholds})
+    return stats
+
+
+def _result(name: str, rewards: Sequence[float], baseline: float, policy_dependent: bool) -> EvaluationResult:
+    return EvaluationResult(name, reward_statistics(rewards, baseline), n_samples=len(rewards),
+                            details={"policy_dependent": policy_dependent})
 
 
 class RecordRewardSuite:
-    """Scores dataset records with a scorer: measures the data, not a policy (``policy_dependent`` False)."""
+    """Scores dataset records: measures the data, not a policy."""
 
     name = "record_reward"
 
@@ -33,9 +42,7 @@ class RecordRewardSuite:
         self.records, self.score_fn, self.baseline = list(records), score_fn, baseline
 
     def run(self, target: Any = None, **kwargs: Any) -> EvaluationResult:
-        rewards = [float(self.score_fn(r)) for r in self.records]
-        return EvaluationResult(self.name, reward_statistics(rewards, self.baseline), n_samples=len(rewards),
-                                details={"policy_dependent": False})
+        return _result(self.name, [float(self.score_fn(r)) for r in self.records], self.baseline, False)
 
 
 class TrajectoryRewardSuite:
@@ -45,15 +52,14 @@ class TrajectoryRewardSuite:
         self.reward, self.baseline = reward, baseline
 
     def run(self, trajectories: Sequence[Trajectory], **kwargs: Any) -> EvaluationResult:
-        score_many = getattr(self.reward, "score_many", None)
-        results = score_many(list(trajectories)) if score_many else [self.reward.score(t) for t in trajectories]
-        rewards = [float(r.value) for r in results]
-        return EvaluationResult(self.name, reward_statistics(rewards, self.baseline), n_samples=len(rewards),
-                                details={"policy_dependent": True})
+        from rl_project_b200.rollouts.rewards.composite import batch_scores
+
+        values = [float(r.value) for r in batch_scores(self.reward, list(trajectories))]
+        return _result(self.name, values, self.baseline, True)
 
 
 class PreferenceWinRateSuite:
-    """Fraction of pairs whose ``chosen`` scores above ``rejected``, and the mean margin."""
+    """Fraction of pairs whose ``chosen`` side the scorer ranks above ``rejected``, and the mean margin."""
 
     name = "preference_win_rate"
 
@@ -61,8 +67,8 @@ class PreferenceWinRateSuite:
         self.pairs, self.score_fn = list(pairs), score_fn
 
     def run(self, target: Any = None, **kwargs: Any) -> EvaluationResult:
-        margins: List[float] = [float(self.score_fn(p["prompt"], p["chosen"]) - self.score_fn(p["prompt"], p["rejected"]))
-                                for p in self.pairs]
+        margin = np.asarray([float(self.score_fn(p["prompt"], p["chosen"])) - float(self.score_fn(p["prompt"], p["rejected"]))
+                             for p in self.pairs], dtype=np.float64)
         n = max(len(self.pairs), 1)
-        return EvaluationResult(self.name, {"win_rate": sum(m > 0 for m in margins) / n,
-                                            "mean_margin": math.fsum(margins) / n}, n_samples=len(self.pairs))
+        return EvaluationResult(self.name, {"win_rate": float((margin > 0).sum()) / n,
+                                            "mean_margin": float(margin.sum()) / n}, n_samples=len(self.pairs))
