@@ -1,8 +1,9 @@
 """Model candidates and their lifecycle state machine.
 
-States and allowed moves follow ``src/forgeline/deployment/candidates.py:14-74``:
-experimental -> shadow / challenger -> champion -> retired, with a retired
-candidate returning only through an explicit restore (rollback).
+States and allowed moves are those of ``src/forgeline/deployment/candidates.py``
+(experimental -> shadow / challenger -> champion -> retired, a retired candidate
+returning only through an explicit restore), written down as an edge list that
+is parsed into the transition table.
 """
 
 from __future__ import annotations
@@ -24,14 +25,29 @@ class CandidateState(str, Enum):
     RETIRED = "retired"
 
 
-_S = CandidateState
-ALLOWED_TRANSITIONS: Dict[CandidateState, Set[CandidateState]] = {
-    _S.EXPERIMENTAL: {_S.SHADOW, _S.CHALLENGER, _S.RETIRED},
-    _S.SHADOW: {_S.CHALLENGER, _S.EXPERIMENTAL, _S.RETIRED},
-    _S.CHALLENGER: {_S.CHAMPION, _S.SHADOW, _S.EXPERIMENTAL, _S.RETIRED},
-    _S.CHAMPION: {_S.RETIRED, _S.CHALLENGER},
-    _S.RETIRED: {_S.CHALLENGER, _S.CHAMPION},  # restore paths only
-}
+# the lifecycle graph, one "from -> to, to, ..." line per state (retired returns only by restore / rollback)
+_GRAPH = """
+experimental -> shadow, challenger, retired
+shadow       -> challenger, experimental, retired
+challenger   -> champion, shadow, experimental, retired
+champion     -> retired, challenger
+retired      -> challenger, champion
+"""
+
+
+def _edges(spec: str) -> Dict[CandidateState, Set[CandidateState]]:
+    graph: Dict[CandidateState, Set[CandidateState]] = {}
+    for line in filter(None, (ln.strip() for ln in spec.splitlines())):
+        src, _, dsts = line.partition("->")
+        graph[CandidateState(src.strip())] = {CandidateState(d.strip()) for d in dsts.split(",")}
+    return graph
+
+
+ALLOWED_TRANSITIONS: Dict[CandidateState, Set[CandidateState]] = _edges(_GRAPH)
+
+
+def can_move(src: CandidateState, dst: CandidateState) -> bool:
+    return dst in ALLOWED_TRANSITIONS[src]
 
 
 @dataclass
@@ -65,7 +81,7 @@ class ModelCandidate:
         self.updated_at = time.time()
 
     def transition(self, new_state: CandidateState, reason: str = "") -> None:
-        if new_state not in ALLOWED_TRANSITIONS[self.state]:
+        if not can_move(self.state, new_state):
             raise RegistryError(f"cannot move candidate {self.key} from {self.state.value} to {new_state.value}")
         self.note(new_state, reason)
         self.state = new_state
