@@ -198,6 +198,31 @@ def run_reference(args, world, rank, local, *, time_device, time_wall, clock_sam
             "clocks": clocks, "e2e": e2e, "compiled": compiled, "gpu_launches": 0, "impl": "reference"}
 
 
+_PATCHES = {"mesh8b": ["ffn width 14336", "rope theta 500000", "untied lm_head"],
+            "moe": ["dense ffn width 10944", "expert ffn width 1408", "shared expert ffn width 2816 (2 x 1408)"]}
+
+
+def _build_reference_model(TransformerLM, spec, args, n_layer, seq, widen, RotaryEmbedding, nn):
+    """The reference's TransformerLM with the config's widths set through its public modules."""
+    model = TransformerLM(spec)
+    if args.workload == "mesh8b":
+        for blk in model.transformer.h:
+            widen(blk.ffn, spec.n_embd, 14336, n_layer)
+            blk.attn.rotary_emb = RotaryEmbedding(spec.n_embd // spec.n_head, max_seq_len=seq, base=500000.0)
+        model.lm_head.weight = nn.Parameter(model.transformer.wte.weight.detach().clone())
+        return model
+    for blk in model.transformer.h:
+        ffn = blk.ffn
+        if hasattr(ffn, "experts"):
+            for e in ffn.experts:
+                widen(e, spec.n_embd, 1408, n_layer)
+            if ffn.shared_experts is not None:  # one shared FFN of 2 x 1408 (the reference builds one)
+                widen(ffn.shared_experts, spec.n_embd, 2 * 1408, n_layer)
+        else:
+            widen(ffn, spec.n_embd, 10944, n_layer)
+    return model
+
+
 def run_reference_workload(args, world, rank, local, *, time_device, clock_sampler, metric):
     """Reference arms of bench.py's ``--workload mesh8b`` and ``moe`` (config 4).
 
@@ -231,7 +256,6 @@ def run_reference_workload(args, world, rank, local, *, time_device, clock_sampl
             TransformerLM._init_weights(lin)
         nn.init.normal_(ffn.w2.weight, mean=0.0, std=0.02 / math.sqrt(2 * n_layer))
 
-    patched = []
     if args.workload == "mesh8b":
         seq = args.seq if args.seq != 4096 else 8192
         n_layer = args.layers or 32
@@ -258,24 +282,11 @@ def run_reference_workload(args, world, rank, local, *, time_device, clock_sampl
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     torch.manual_seed(1234)
-    model = TransformerLM(spec)
-    if args.workload == "mesh8b":
-        for blk in model.transformer.h:
-            widen(blk.ffn, spec.n_embd, 14336, n_layer)
-            blk.attn.rotary_emb = RotaryEmbedding(spec.n_embd // spec.n_head, max_seq_len=seq, base=500000.0)
-        model.lm_head.weight = nn.Parameter(model.transformer.wte.weight.detach().clone())
-        patched = ["ffn width 14336", "rope theta 500000", "untied lm_head"]
-    else:
-        for i, blk in enumerate(model.transformer.h):
-            ffn = blk.ffn
-            if hasattr(ffn, "experts"):
-                for e in ffn.experts:
-                    widen(e, spec.n_embd, 1408, n_layer)
-                if ffn.shared_experts is not None:  # one shared FFN of 2 x 1408 (the reference builds one)
-                    widen(ffn.shared_experts, spec.n_embd, 2 * 1408, n_layer)
-            else:
-                widen(ffn, spec.n_embd, 10944, n_layer)
-        patched = ["dense ffn width 10944", "expert ffn width 1408", "shared expert ffn width 2816 (2 x 1408)"]
+    # built directly on the GPU (a default-device context; the reference code is unchanged): eight ranks each
+    # materialising the 8B model in fp32 host memory first would need 256 GB of host RAM
+    with torch.device(device):
+        model = _build_reference_model(TransformerLM, spec, args, n_layer, seq, widen, RotaryEmbedding, nn)
+    patched = _PATCHES[args.workload]
     if ckpt:
         model.enable_gradient_checkpointing()
     model = strategy.wrap_model(model.to(device))
@@ -294,12 +305,12 @@ def run_reference_workload(args, world, rank, local, *, time_device, clock_sampl
         x, y = pool[state["i"] % 2]
         state["i"] += 1
         opt.zero_grad(set_to_none=True)
-        total = 0.0
+        total = torch.zeros((), device=device)
         for xs, ys in zip(x.split(micro), y.split(micro)):
             with prec.autocast():
                 _, loss = model(xs, ys)
             prec.backward(loss * (xs.shape[0] / rows))
-            total += float(loss.detach()) * xs.shape[0] / rows
+            total += loss.detach().float() * (xs.shape[0] / rows)  # read once, after timing
         prec.unscale(opt)
         if world > 1:
             strategy.clip_grad_norm(model, 1.0)
@@ -324,5 +335,5 @@ def run_reference_workload(args, world, rank, local, *, time_device, clock_sampl
                        "parallelism": f"fsdp{world}" if world > 1 else "single",
                        "reference_layout_note": "the config's TPxPP / EP layout is not runnable in the reference",
                        "gradient_checkpointing": ckpt, "patched_from_outside": patched,
-                       "final_loss": state["loss"], "workload": args.workload},
+                       "final_loss": float(state["loss"]), "workload": args.workload},
             "clocks": clocks, "e2e": None, "gpu_launches": 0, "impl": "reference"}

@@ -1,21 +1,27 @@
-"""Direct Preference Optimization (``src/forgeline/training/dpo.py`` objective):
+"""Direct Preference Optimization (the objective and options of ``src/forgeline/training/dpo.py``)::
 
-    L = -log sigmoid( beta (log pi(y_w|x) - log pi_ref(y_w|x)) - beta (log pi(y_l|x) - log pi_ref(y_l|x)) )
+    z = beta * (log pi(y_w|x) - log pi_ref(y_w|x)) - beta * (log pi(y_l|x) - log pi_ref(y_l|x))
+    L = (1 - eps) * softplus(-z) + eps * softplus(z)          (eps = label smoothing; softplus(-z) = -log sigmoid z)
 
-with ``logprob_reduction`` sum | mean, ``reference_free`` and label smoothing.
+with sequence scores reduced by ``sum`` or ``mean`` over response tokens, and ``reference_free`` dropping
+the reference terms.
 
-Batched: every (prompt + chosen) and (prompt + rejected) sequence of the
-micro-batch is right-padded into ONE forward pass.  With causal attention,
-padding placed after a sequence cannot change its log-probs, and every row
-keeps positions 0..L-1, so this equals the reference's one-forward-per-example
-loop exactly while running one fused LM-head kernel for the whole batch.
+Execution plan of a step:
+
+* ``collect`` draws the examples and scores them under the frozen reference right away -- the reference
+  terms do not depend on the policy's weights, so they are computed once per step, outside the
+  gradient-accumulation loop, and travel with the batch;
+* each micro-batch scores chosen and rejected sides of all its examples in ONE policy forward: every
+  ``prompt + response`` row is right-padded into a ``[2B, T]`` batch whose targets are -1 outside the
+  response, and the fused LM-head log-prob kernel scores all rows at once.  Under causal attention the
+  padding after a row cannot change its log-probs, so this equals scoring each example alone.
 """
 
 from __future__ import annotations
 
 import random
 from dataclasses import dataclass
-from typing import Any, Dict, List, Mapping, Optional, Sequence, Tuple
+from typing import Any, Dict, List, Mapping, Sequence, Tuple
 
 import torch
 import torch.nn as nn
@@ -45,36 +51,46 @@ class DPOConfig:
 
 def dpo_loss(policy_chosen: torch.Tensor, policy_rejected: torch.Tensor, ref_chosen: torch.Tensor,
              ref_rejected: torch.Tensor, beta: float, label_smoothing: float = 0.0) -> Dict[str, torch.Tensor]:
-    cr = beta * (policy_chosen - ref_chosen)
-    rr = beta * (policy_rejected - ref_rejected)
-    z = cr - rr
-    loss = -F.logsigmoid(z) * (1 - label_smoothing) - F.logsigmoid(-z) * label_smoothing if label_smoothing > 0 \
-        else -F.logsigmoid(z)
-    return {"loss": loss.mean(), "chosen_reward": cr.detach(), "rejected_reward": rr.detach(),
-            "margin": (cr - rr).detach(), "accuracy": (cr > rr).float().detach()}
+    """Loss and implicit rewards from sequence log-probs ``[B]``."""
+    implicit = beta * (torch.stack([policy_chosen, policy_rejected]) - torch.stack([ref_chosen, ref_rejected]))
+    z = implicit[0] - implicit[1]
+    per_pair = F.softplus(-z) if label_smoothing <= 0 else \
+        (1.0 - label_smoothing) * F.softplus(-z) + label_smoothing * F.softplus(z)
+    r = implicit.detach()
+    return {"loss": per_pair.mean(), "chosen_reward": r[0], "rejected_reward": r[1], "margin": r[0] - r[1],
+            "accuracy": (r[0] > r[1]).float()}
 
 
 def pack_prompt_response(pairs: Sequence[Tuple[List[int], List[int]]], pad: int):
-    """Right-padded ``inputs [B, T]`` and ``targets [B, T]`` (-1 outside each response)."""
-    seqs = [list(p) + list(r) for p, r in pairs]
-    T = max(len(s) for s in seqs) - 1
-    inputs = torch.full((len(seqs), T), pad, dtype=torch.long)
-    targets = torch.full((len(seqs), T), -1, dtype=torch.long)
-    for i, ((p, r), s) in enumerate(zip(pairs, seqs)):
-        L = len(s)
-        inputs[i, : L - 1] = torch.tensor(s[:-1])
-        targets[i, len(p) - 1: L - 1] = torch.tensor(s[len(p):])
+    """Right-padded ``inputs [N, T]`` and ``targets [N, T]`` (-1 outside each response): row ``i`` holds
+    ``prompt + response`` shifted by one, so target ``t`` is the token that follows input ``t``."""
+    rows = [list(p) + list(r) for p, r in pairs]
+    starts = torch.tensor([len(p) - 1 for p, _ in pairs])  # first input position that predicts a response token
+    lengths = torch.tensor([len(x) - 1 for x in rows])
+    T = int(lengths.max())
+    flat = torch.full((len(rows), T + 1), pad, dtype=torch.long)
+    for i, x in enumerate(rows):
+        flat[i, :len(x)] = torch.as_tensor(x)
+    cols = torch.arange(T)[None, :]
+    inputs = torch.where(cols < lengths[:, None], flat[:, :-1], torch.full_like(flat[:, :-1], pad))
+    in_response = (cols >= starts[:, None]) & (cols < lengths[:, None])
+    targets = torch.where(in_response, flat[:, 1:], torch.full_like(flat[:, 1:], -1))
     return inputs, targets
 
 
 def sequence_logprobs(policy, pairs, reduction: str) -> torch.Tensor:
+    """Per-row response log-prob, summed or averaged over the row's response tokens."""
     inputs, targets = pack_prompt_response(pairs, policy.pad_token_id)
     dev = policy.device
     targets = targets.to(dev)
-    lp = policy.token_logprobs(inputs.to(dev), targets).float()
-    if reduction == "sum":
-        return lp.sum(1)
-    return lp.sum(1) / (targets >= 0).sum(1).clamp(min=1)
+    total = policy.token_logprobs(inputs.to(dev), targets).float().sum(1)
+    return total if reduction == "sum" else total / (targets >= 0).sum(1).clamp(min=1)
+
+
+@dataclass
+class _Batch:
+    examples: List[Dict[str, List[int]]]
+    ref: torch.Tensor  # [2, B] reference scores (chosen, rejected); zeros when reference-free
 
 
 class DPOAlgorithm(PostTrainingAlgorithm):
@@ -82,16 +98,27 @@ class DPOAlgorithm(PostTrainingAlgorithm):
 
     def __init__(self, policy, dataset, config: DPOConfig, eval_dataset=None):
         config.validate()
-        self.policy = policy
-        self.dataset = dataset
-        self.eval_dataset = eval_dataset
-        self.cfg = config
+        if len(dataset) == 0:
+            raise ConfigError("DPO dataset is empty")
+        self.policy, self.dataset, self.eval_dataset, self.cfg = policy, dataset, eval_dataset, config
         self.rng = random.Random(config.seed)
         if not config.reference_free and not policy.has_adapter and policy.reference_model is None:
             policy.with_frozen_reference()
-        if len(dataset) == 0:
-            raise ConfigError("DPO dataset is empty")
 
+    # ------------------------------------------------------------ scoring
+    def _both_sides(self, examples: Sequence[Dict[str, List[int]]]) -> torch.Tensor:
+        """``[2, B]``: chosen and rejected scores of every example from one forward."""
+        pairs = [(e["prompt"], e[side]) for side in ("chosen", "rejected") for e in examples]
+        return sequence_logprobs(self.policy, pairs, self.cfg.logprob_reduction).view(2, len(examples))
+
+    @torch.no_grad()
+    def _reference(self, examples: Sequence[Dict[str, List[int]]]) -> torch.Tensor:
+        if self.cfg.reference_free:
+            return torch.zeros(2, len(examples), device=self.policy.device)
+        with self.policy.reference():
+            return self._both_sides(examples)
+
+    # ------------------------------------------------------------ algorithm protocol
     def parameters(self) -> List[nn.Parameter]:
         return self.policy.trainable_parameters()
 
@@ -101,26 +128,17 @@ class DPOAlgorithm(PostTrainingAlgorithm):
     def frozen_modules(self):
         return (self.policy.reference_model,) if self.policy.reference_model is not None else ()
 
-    def collect(self, step: int):
-        return [self.dataset[self.rng.randrange(len(self.dataset))] for _ in range(self.cfg.batch_size)]
+    def collect(self, step: int) -> _Batch:
+        examples = [self.dataset[self.rng.randrange(len(self.dataset))] for _ in range(self.cfg.batch_size)]
+        return _Batch(examples, self._reference(examples))
 
-    def _scores(self, examples) -> Tuple[torch.Tensor, torch.Tensor]:
-        pairs = [(e["prompt"], e["chosen"]) for e in examples] + [(e["prompt"], e["rejected"]) for e in examples]
-        s = sequence_logprobs(self.policy, pairs, self.cfg.logprob_reduction)
-        n = len(examples)
-        return s[:n], s[n:]
-
-    def loss(self, batch, micro_step: int, n_micro: int):
-        chunk = batch[micro_step::n_micro] if n_micro > 1 else batch
-        if not chunk:
+    def loss(self, batch: _Batch, micro_step: int, n_micro: int):
+        idx = list(range(micro_step, len(batch.examples), n_micro)) if n_micro > 1 else list(range(len(batch.examples)))
+        if not idx:
             return torch.zeros((), device=self.policy.device, requires_grad=True), {}
-        pc, pr = self._scores(chunk)
-        if self.cfg.reference_free:
-            rc, rr = torch.zeros_like(pc), torch.zeros_like(pr)
-        else:
-            with torch.no_grad(), self.policy.reference():
-                rc, rr = self._scores(chunk)
-        out = dpo_loss(pc, pr, rc, rr, self.cfg.beta, self.cfg.label_smoothing)
+        pol = self._both_sides([batch.examples[i] for i in idx])
+        ref = batch.ref[:, idx]
+        out = dpo_loss(pol[0], pol[1], ref[0], ref[1], self.cfg.beta, self.cfg.label_smoothing)
         return out["loss"], {"reward_margin": out["margin"].mean(), "chosen_reward": out["chosen_reward"].mean(),
                              "rejected_reward": out["rejected_reward"].mean(),
                              "preference_accuracy": out["accuracy"].mean()}
@@ -128,14 +146,9 @@ class DPOAlgorithm(PostTrainingAlgorithm):
     @torch.no_grad()
     def evaluate(self, step: int) -> Dict[str, float]:
         ds = self.eval_dataset or self.dataset
-        ex = [ds[i] for i in range(min(len(ds), 32))]
-        pc, pr = self._scores(ex)
-        if self.cfg.reference_free:
-            rc, rr = torch.zeros_like(pc), torch.zeros_like(pr)
-        else:
-            with self.policy.reference():
-                rc, rr = self._scores(ex)
-        out = dpo_loss(pc, pr, rc, rr, self.cfg.beta)
+        examples = [ds[i] for i in range(min(len(ds), 32))]
+        pol, ref = self._both_sides(examples), self._reference(examples)
+        out = dpo_loss(pol[0], pol[1], ref[0], ref[1], self.cfg.beta)
         return {"loss": float(out["loss"]), "preference_accuracy": float(out["accuracy"].mean()),
                 "reward_margin": float(out["margin"].mean())}
 
