@@ -281,6 +281,70 @@ def bench_attention(cases=((8, 4096, 32, 8, 64), (2, 8192, 32, 8, 128))):
                           "cudnn_bwd_ms": round(tbr, 4), "cudnn_bwd_tflops": round(fl_b / tbr / 1e9, 1)}), flush=True)
 
 
+def bench_nf4(cases=((4096, 4096, 4096), (4096, 14336, 4096), (4096, 4096, 14336))):
+    """QLoRA base layer: the NF4 weight expanded inside the tcgen05 main loop (csrc/nf4_gemm.cu) against the
+    unfused path (dequantise to bf16 with csrc/nf4.cu, then cuBLAS), forward ``x W^T`` and input gradient
+    ``dy W``; bytes moved by the weight: 0.5 B + 1/16 B absmax per element fused, 2 B written + read unfused."""
+    from rl_project_b200.models.quantization.nf4 import NF4_TABLE, dequantize_nf4, quantize_nf4
+    from rl_project_b200.ops._ext import native
+
+    peak_tf, _ = _peaks()
+    for M, N, K in cases:
+        w = torch.randn(N, K, device="cuda") * 0.02
+        packed, absmax, shape = quantize_nf4(w)
+        packed, absmax, table = packed.cuda(), absmax.float().cuda(), NF4_TABLE.cuda()
+        st = torch.zeros(1, dtype=torch.int32, device="cuda")
+        x = torch.randn(M, K, device="cuda").bfloat16()
+        dy = torch.randn(M, N, device="cuda").bfloat16()
+        fl = 2.0 * M * N * K
+        for mode, a in ((0, x), (1, dy)):
+            fused = time_ms(lambda: native().nf4_gemm(a, packed, absmax, table, mode, N, K, st))
+
+            def unfused():
+                wd = dequantize_nf4(packed, absmax, shape, torch.bfloat16)
+                return a @ (wd.t() if mode == 0 else wd)
+
+            ref = time_ms(unfused)
+            print(json.dumps({"kernel": "nf4_gemm", "mode": ["x W^T", "dy W"][mode], "M": M, "N": N, "K": K,
+                              "ms": round(fused, 4), "tflops": round(fl / fused / 1e9, 1),
+                              "frac_of_measured_bf16": round(fl / fused / 1e9 / peak_tf, 3),
+                              "dequant_plus_cublas_ms": round(ref, 4), "speedup": round(ref / fused, 2),
+                              "status": int(st.item())}), flush=True)
+
+
+def bench_decode_graphs(batch: int = 64, prompt: int = 256, new: int = 128):
+    """Paged-KV decode of the dense 1B model: eager steps against steps replayed from CUDA graphs (greedy,
+    same requests); generated tokens per second of the whole ``generate_batch`` call."""
+    import time
+
+    from rl_project_b200.core.config import model_spec_from_preset
+    from rl_project_b200.inference.engine import InferenceEngine
+    from rl_project_b200.inference.requests import SamplingParams
+    from rl_project_b200.models.transformer.model import TransformerLM
+
+    spec = model_spec_from_preset("bl_dense_1b", block_size=prompt + new + 16)
+    torch.manual_seed(0)
+    with torch.device("cuda"):
+        model = TransformerLM(spec).to(torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, spec.vocab_size, (prompt,), generator=g).tolist() for _ in range(batch)]
+    params = SamplingParams(max_tokens=new, temperature=0.0, top_k=None)
+    out = {}
+    for graphs in (False, True):
+        eng = InferenceEngine(model, max_batch=batch, decode_graphs=graphs)
+        eng.generate_batch(prompts[:4], SamplingParams(max_tokens=8, temperature=0.0, top_k=None))  # warm-up
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        reqs = eng.generate_batch(prompts, params)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        out[graphs] = (sum(len(r.generated_tokens) for r in reqs) / dt, [r.generated_tokens for r in reqs])
+    print(json.dumps({"kernel": "paged_decode_engine", "batch": batch, "prompt": prompt, "new_tokens": new,
+                      "eager_tokens_per_s": round(out[False][0], 1), "graphs_tokens_per_s": round(out[True][0], 1),
+                      "speedup": round(out[True][0] / out[False][0], 2),
+                      "same_tokens": out[True][1] == out[False][1]}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--which", default="gemm,mem,adam,paged,sample")
@@ -304,6 +368,10 @@ def main():
         bench_grouped()
     if "attn" in which:
         bench_attention()
+    if "nf4" in which:
+        bench_nf4()
+    if "decode" in which:
+        bench_decode_graphs()
     if "attn1" in which:  # one small case (profiling)
         bench_attention(((2, 2048, 32, 8, 64),))
 

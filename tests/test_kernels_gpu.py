@@ -266,8 +266,6 @@ def test_tcgen05_linear_autograd():
     _close(w.grad, wr.grad, 2e-2)
 
 
-@pytest.mark.skipif(__import__("os").environ.get("RLB_NF4_TEST") != "1",
-                    reason="NF4 main-loop GEMM not yet validated on a GPU (set RLB_NF4_TEST=1)")
 @pytest.mark.parametrize("M,N,K", [(256, 512, 256), (300, 520, 192), (64, 256, 1024)])
 def test_nf4_gemm_matches_dequantised_matmul(M, N, K):
     from rl_project_b200.models.quantization.nf4 import NF4_TABLE, dequantize_nf4, quantize_nf4
