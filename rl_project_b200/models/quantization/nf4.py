@@ -6,8 +6,8 @@ al., 2023), the same data the reference ships.  On CUDA, ``NF4Linear``
 dequantises in the sm_100a kernel csrc/nf4.cu straight to bf16 in one pass
 (the reference dequantises through fp32 index tensors on every forward); with
 ``RLB_NF4_GEMM=1`` the forward and input gradient instead run csrc/nf4_gemm.cu,
-which expands the weight tile by tile inside the tcgen05 GEMM (written, not yet
-run on a GPU).
+which expands the weight tile by tile inside the tcgen05 GEMM (tested on B200
+against an fp32 matmul of the dequantised weight).
 """
 
 from __future__ import annotations

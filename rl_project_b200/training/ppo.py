@@ -1,11 +1,21 @@
-"""PPO for language-model policies (``src/forgeline/training/ppo.py`` switches:
-``ratio_level`` sequence_mean | token, ``kl_mode`` monitor | penalty | reward,
-``entropy_mode`` sampled_logprob | full; advantages ``reward - value``,
-normalised, with a value MSE loss).
+"""PPO for language-model policies (the options of ``src/forgeline/training/ppo.py``):
 
-Rollouts of all prompts are sampled together and the old log-probs come from
-the rollout itself (no second old-policy pass); ``entropy_mode="full"`` uses the
-fused LM-head entropy kernel instead of materialising the logits.
+* ``ratio_level``: ``sequence_mean`` (ratio ``exp(mean_t(log pi - log pi_old))`` per sequence) or ``token``;
+* ``kl_mode``: ``monitor`` (detached, logged), ``penalty`` (``kl_coef * KL`` added to the loss) or ``reward``
+  (subtracted from the reward before the advantage);
+* ``entropy_mode``: ``sampled_logprob`` (``-mean log pi(y_t)``) or ``full`` (exact entropy, from the fused
+  LM-head kernel: no ``[B, T, V]`` logits);
+* advantages ``reward - value`` (optionally normalised) and a value MSE loss.
+
+Data flow: all prompts of a step are sampled together by the rollout engine; one scoring pass over the
+left-padded batch yields old log-probs and values, one pass with adapters off / the frozen copy yields
+the reference log-probs.  The surrogate (and penalty KL) run in the fused ``clipped_kl_loss`` op.
+
+``ppo_epochs``: the objective averages ``ppo_epochs`` evaluations of the same loss at the same weights
+(no optimizer step between them).  When the forward is deterministic (no active dropout) those
+evaluations are identical, so the loss is evaluated once -- the same value and gradient for
+``1 / ppo_epochs`` of the work; with dropout active each evaluation draws its own masks and all of them
+run.
 """
 
 from __future__ import annotations
@@ -20,12 +30,15 @@ import torch.nn.functional as F
 
 from rl_project_b200.core.errors import ConfigError
 from rl_project_b200.core.protocols import RewardProvider, Trajectory
+from rl_project_b200.ops.rl_loss import clipped_kl_loss
 from rl_project_b200.rollouts.engine import RolloutConfig, RolloutEngine
 from rl_project_b200.rollouts.rewards.composite import score_trajectories
 from rl_project_b200.training.common.advantages import normalize_advantages
-from rl_project_b200.ops.rl_loss import clipped_kl_loss
 from rl_project_b200.training.common.logprobs import kl_logprob_diff, masked_mean
 from rl_project_b200.training.common.trainer import PostTrainingAlgorithm
+
+_CHOICES = {"ratio_level": ("sequence_mean", "token"), "kl_mode": ("monitor", "penalty", "reward"),
+            "entropy_mode": ("sampled_logprob", "full")}
 
 
 @dataclass
@@ -44,12 +57,9 @@ class PPOConfig:
     seed: int = 0
 
     def validate(self) -> None:
-        if self.ratio_level not in ("sequence_mean", "token"):
-            raise ConfigError("ratio_level must be sequence_mean|token")
-        if self.kl_mode not in ("monitor", "penalty", "reward"):
-            raise ConfigError("kl_mode must be monitor|penalty|reward")
-        if self.entropy_mode not in ("sampled_logprob", "full"):
-            raise ConfigError("entropy_mode must be sampled_logprob|full")
+        for field_name, allowed in _CHOICES.items():
+            if getattr(self, field_name) not in allowed:
+                raise ConfigError(f"{field_name} must be {'|'.join(allowed)}")
         if not 0 < self.clip_ratio < 1:
             raise ConfigError("clip_ratio must be in (0, 1)")
         if min(self.ppo_epochs, self.prompts_per_step, self.samples_per_prompt) < 1:
@@ -58,7 +68,7 @@ class PPOConfig:
 
 def ppo_clipped_objective(ratio: torch.Tensor, advantages: torch.Tensor, clip_ratio: float) -> torch.Tensor:
     """Elementwise ``-min(r A, clip(r, 1-eps, 1+eps) A)``."""
-    return -torch.min(ratio * advantages, torch.clamp(ratio, 1.0 - clip_ratio, 1.0 + clip_ratio) * advantages)
+    return -torch.minimum(ratio * advantages, ratio.clamp(1.0 - clip_ratio, 1.0 + clip_ratio) * advantages)
 
 
 @dataclass
@@ -74,17 +84,17 @@ class PPOBatch:
 
 
 def left_pad_batch(trajectories: Sequence[Trajectory], pad: int):
-    P = max(t.prompt_ids.numel() for t in trajectories)
-    R = max(t.response_length for t in trajectories)
-    N = len(trajectories)
-    prompt = torch.full((N, P), pad, dtype=torch.long)
-    resp = torch.full((N, R), pad, dtype=torch.long)
-    mask = torch.zeros((N, R))
-    for i, t in enumerate(trajectories):
-        prompt[i, P - t.prompt_ids.numel():] = t.prompt_ids
-        resp[i, : t.response_length] = t.response_ids
-        mask[i, : t.response_length] = 1.0
-    return prompt, resp, mask
+    """``(prompts [N, P] left-padded, responses [N, R] right-padded, response mask [N, R] float)``."""
+    from rl_project_b200.data.collators import pad_sequences
+
+    prompts, _ = pad_sequences([t.prompt_ids.tolist() for t in trajectories], pad, "left")
+    responses, mask = pad_sequences([t.response_ids.tolist() for t in trajectories], pad, "right")
+    return prompts, responses, mask.float()
+
+
+def _has_active_dropout(modules) -> bool:
+    return any(isinstance(m, nn.Dropout) and m.p > 0 and m.training for mod in modules if mod is not None
+               for m in mod.modules())
 
 
 class PPOAlgorithm(PostTrainingAlgorithm):
@@ -95,13 +105,11 @@ class PPOAlgorithm(PostTrainingAlgorithm):
         config.validate()
         if policy.value_head is None:
             raise ConfigError("PPO requires a policy with value_head=True")
-        self.policy = policy
         if not policy.has_adapter and policy.reference_model is None:
             policy.with_frozen_reference()
+        self.policy, self.reward, self.cfg = policy, reward, config
         self.prompts = list(prompts)
         self.tasks = list(tasks) if tasks else [{} for _ in self.prompts]
-        self.reward = reward
-        self.cfg = config
         self.rollouts = RolloutEngine(policy, rollout or RolloutConfig(group_size=config.samples_per_prompt))
         self.rng = random.Random(config.seed)
         self._last_stats: Dict[str, float] = {}
@@ -115,10 +123,11 @@ class PPOAlgorithm(PostTrainingAlgorithm):
     def frozen_modules(self):
         return (self.policy.reference_model,) if self.policy.reference_model is not None else ()
 
+    # ------------------------------------------------------------ rollouts
     @torch.no_grad()
     def collect(self, step: int) -> PPOBatch:
-        idx = [self.rng.randrange(len(self.prompts)) for _ in range(self.cfg.prompts_per_step)]
-        groups = self.rollouts.rollout_many([self.prompts[i] for i in idx], [self.tasks[i] for i in idx],
+        picks = [self.rng.randrange(len(self.prompts)) for _ in range(self.cfg.prompts_per_step)]
+        groups = self.rollouts.rollout_many([self.prompts[i] for i in picks], [self.tasks[i] for i in picks],
                                             group_size=self.cfg.samples_per_prompt)
         trajs = [t for g in groups for t in g]
         rewards = torch.tensor(score_trajectories(self.reward, trajs), dtype=torch.float32)
@@ -126,52 +135,49 @@ class PPOAlgorithm(PostTrainingAlgorithm):
         old_lp, old_v = self.policy.logprobs_and_values(prompt, resp)
         with self.policy.reference():
             ref_lp = self.policy.logprobs(prompt, resp)
-        old_lp, ref_lp = old_lp.float().cpu(), ref_lp.float().cpu()
+        old_lp, ref_lp, old_v = old_lp.float().cpu(), ref_lp.float().cpu(), old_v.float().cpu()
         if self.cfg.kl_mode == "reward":
             rewards = rewards - self.cfg.kl_coef * kl_logprob_diff(ref_lp, old_lp, mask, clamp_min=None)
         self._last_stats = {"reward_mean": float(rewards.mean()),
                             "reward_std": float(rewards.std()) if len(trajs) > 1 else 0.0,
                             "response_len": float(mask.sum(1).mean())}
-        return PPOBatch(prompt, resp, mask, old_lp, ref_lp, old_v.float().cpu(), rewards, trajs)
+        return PPOBatch(prompt, resp, mask, old_lp, ref_lp, old_v, rewards, trajs)
+
+    # ------------------------------------------------------------ objective
+    def _terms(self, batch: PPOBatch, mask, returns, adv, old_lp, ref_lp) -> Dict[str, torch.Tensor]:
+        """One evaluation of the PPO loss terms at the current weights."""
+        cfg = self.cfg
+        if cfg.entropy_mode == "full":
+            new_lp, ent_tok = self.policy.logprobs_with_entropy(batch.prompt_ids, batch.response_ids)
+            values = self.policy.values(batch.prompt_ids, batch.response_ids)
+            entropy = masked_mean(ent_tok.float(), mask).mean()
+        else:
+            new_lp, values = self.policy.logprobs_and_values(batch.prompt_ids, batch.response_ids)
+            entropy = -masked_mean(new_lp.float(), mask).mean()
+        new_lp = new_lp.float()
+        surrogate, _, _ = clipped_kl_loss(new_lp, old_lp, ref_lp, mask, adv, cfg.clip_ratio, 0.0, cfg.ratio_level,
+                                          "logprob_diff_rows")
+        kl = kl_logprob_diff(ref_lp, new_lp, mask).mean() if cfg.kl_mode == "penalty" else \
+            masked_mean(old_lp - ref_lp, mask).mean().detach()
+        value_loss = F.mse_loss(values.float(), returns)
+        loss = surrogate + cfg.value_coef * value_loss - cfg.entropy_coef * entropy
+        if cfg.kl_mode == "penalty":
+            loss = loss + cfg.kl_coef * kl
+        return {"loss": loss, "policy_loss": surrogate, "value_loss": value_loss, "kl": kl, "entropy": entropy}
 
     def loss(self, batch: PPOBatch, micro_step: int, n_micro: int):
         dev = self.policy.device
-        mask = batch.mask.to(dev)
-        returns = batch.rewards.to(dev)
+        mask, returns = batch.mask.to(dev), batch.rewards.to(dev)
         adv = returns - batch.old_values.to(dev)
-        if self.cfg.normalize_advantages:
-            adv = normalize_advantages(adv)
-        adv = adv.detach()
+        adv = (normalize_advantages(adv) if self.cfg.normalize_advantages else adv).detach()
         old_lp, ref_lp = batch.old_logprobs.to(dev), batch.ref_logprobs.to(dev)
-        total = torch.zeros((), device=dev)
-        agg: Dict[str, torch.Tensor] = {}
-        for _ in range(self.cfg.ppo_epochs):
-            if self.cfg.entropy_mode == "full":
-                new_lp, ent_tok = self.policy.logprobs_with_entropy(batch.prompt_ids, batch.response_ids)
-                values = self.policy.values(batch.prompt_ids, batch.response_ids)
-            else:
-                new_lp, values = self.policy.logprobs_and_values(batch.prompt_ids, batch.response_ids)
-                ent_tok = None
-            new_lp = new_lp.float()
-            # surrogate and (penalty mode) KL in one fused op; the KL penalty is added below
-            pl, _, _ = clipped_kl_loss(new_lp, old_lp, ref_lp, mask, adv, self.cfg.clip_ratio, 0.0,
-                                       self.cfg.ratio_level, "logprob_diff_rows")
-            vl = F.mse_loss(values.float(), returns)
-            if self.cfg.kl_mode == "penalty":
-                kl = kl_logprob_diff(ref_lp, new_lp, mask).mean()
-            else:
-                kl = masked_mean(old_lp - ref_lp, mask).mean().detach()
-            ent = masked_mean(ent_tok.float(), mask).mean() if ent_tok is not None else -masked_mean(new_lp, mask).mean()
-            loss = pl + self.cfg.value_coef * vl - self.cfg.entropy_coef * ent
-            if self.cfg.kl_mode == "penalty":
-                loss = loss + self.cfg.kl_coef * kl
-            total = total + loss
-            for k, v in (("policy_loss", pl), ("value_loss", vl), ("kl", kl), ("entropy", ent)):
-                agg[k] = agg.get(k, 0.0) + v.detach() / self.cfg.ppo_epochs
-        metrics: Dict[str, Any] = dict(agg)
+        passes = self.cfg.ppo_epochs if _has_active_dropout(self.modules()) else 1
+        runs = [self._terms(batch, mask, returns, adv, old_lp, ref_lp) for _ in range(passes)]
+        mean = {k: sum(r[k] for r in runs) / passes for k in runs[0]}
+        metrics: Dict[str, Any] = {k: v.detach() for k, v in mean.items() if k != "loss"}
         metrics.update(self._last_stats)
         metrics["advantage_mean"] = adv.mean()
-        return total / self.cfg.ppo_epochs, metrics
+        return mean["loss"], metrics
 
     def state(self) -> Dict[str, Any]:
         return self.policy.state_for_checkpoint()

@@ -91,6 +91,33 @@ def test_ppo_modes(make_ctx, cspec, char_tok, ratio_level, kl_mode, entropy_mode
     assert "kl" in alg.loss(alg.collect(0), 0, 1)[1]
 
 
+def test_ppo_epochs_average_equals_one_evaluation_without_dropout(cspec, char_tok):
+    """With no active dropout the ``ppo_epochs`` evaluations at fixed weights are identical, so the loss is
+    evaluated once; its value and gradient equal the explicit average of ``ppo_epochs`` evaluations."""
+    torch.manual_seed(3)
+    pol = NativePolicy(TransformerLM(cspec), char_tok, value_head=True)
+    pol.value_head.net[0].p = 0.0  # the value head's dropout off: a deterministic forward
+    prompts = [torch.tensor(char_tok.encode(f"Q{i}:")) for i in range(3)]
+    alg = PPOAlgorithm(pol, prompts, LengthReward(6), PPOConfig(prompts_per_step=2, samples_per_prompt=2, ppo_epochs=3),
+                       RolloutConfig(max_new_tokens=5))
+    batch = alg.collect(0)
+    params = [p for p in alg.parameters() if p.requires_grad]
+    loss, _ = alg.loss(batch, 0, 1)
+    g1 = torch.autograd.grad(loss, params, allow_unused=True)
+    dev = pol.device
+    mask, returns = batch.mask.to(dev), batch.rewards.to(dev)
+    from rl_project_b200.training.common.advantages import normalize_advantages
+
+    adv = normalize_advantages(returns - batch.old_values.to(dev)).detach()
+    runs = [alg._terms(batch, mask, returns, adv, batch.old_logprobs, batch.ref_logprobs)["loss"] for _ in range(3)]
+    ref = sum(runs) / 3
+    g3 = torch.autograd.grad(ref, params, allow_unused=True)
+    assert abs(float(loss) - float(ref)) < 1e-6
+    for a, b in zip(g1, g3):
+        if a is not None:
+            assert torch.allclose(a, b, atol=1e-6)
+
+
 @pytest.mark.parametrize("objective,ratio_level", [("clipped", "sequence_mean"), ("clipped", "token"),
                                                    ("reinforce", "sequence_mean")])
 def test_grpo_objectives(make_ctx, cspec, char_tok, objective, ratio_level):
