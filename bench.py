@@ -65,8 +65,9 @@ def parse_args():
                     help="CTAs of each fused reduce-scatter that overlaps backward")
     ap.add_argument("--fused-multicast", choices=["off", "on", "symm"], default="off",
                     help="fused reduce-scatter transport: CUDA IPC peer loads (off) or NVLink multicast (on)")
-    ap.add_argument("--gemm", choices=["tcgen05", "cublas"], default="tcgen05",
-                    help="dense linear layers and LM head: this library's 2-SM tcgen05 GEMM or cuBLAS")
+    ap.add_argument("--gemm", choices=["tcgen05", "cublas", "tuned"], default="tcgen05",
+                    help="dense linear layers and LM head: this library's 2-SM tcgen05 GEMM, cuBLAS, or per shape "
+                         "the fastest of the two (timed on the first call of each shape)")
     ap.add_argument("--attn", choices=["sdpa", "tcgen05"], default="sdpa",
                     help="training / prefill attention: torch SDPA (cuDNN / flash) or this library's tcgen05 kernels")
     ap.add_argument("--decode-graphs", action="store_true",
@@ -87,6 +88,21 @@ def apply_kernel_choices(args) -> dict:
     if args.decode_graphs:
         os.environ["RLB_DECODE_GRAPHS"] = "1"
     return {"attention": args.attn, "gemm": args.gemm, "decode_graphs": bool(args.decode_graphs)}
+
+
+def gemm_choice_summary() -> dict:
+    """In ``--gemm tuned`` mode: how many product shapes went to each kernel."""
+    from rl_project_b200.ops import gemm
+
+    picks = gemm.tuned_choices()
+    if not picks:
+        return {}
+    counts: dict = {}
+    for (a_mn, b_mn, _, M, N, K, _), choice in picks.items():
+        layout = {(0, 0): "fwd", (0, 1): "dgrad", (1, 1): "wgrad"}.get((a_mn, b_mn), "other")
+        counts.setdefault(layout, {}).setdefault(choice, 0)
+        counts[layout][choice] += 1
+    return {"gemm_tuned_picks": counts}
 
 
 # --------------------------------------------------------------------------- clocks
@@ -314,7 +330,7 @@ def run_ours(args, world, rank, local):
                    "model_tflops_per_gpu": flops_tok * args.seq * args.batch_per_gpu / (ms / 1e3) / 1e12,
                    "mfu_vs_measured_bf16": (flops_tok * args.seq * args.batch_per_gpu / (ms / 1e3) / 1e12 / peak)
                    if peak else None,
-                   "attention": args.attn, "gemm": args.gemm,
+                   "attention": args.attn, "gemm": args.gemm, **gemm_choice_summary(),
                    "final_loss": last.loss, "first_loss": trainer.history[0].loss,
                    "final_grad_norm": last.metrics.get("grad_norm"),
                    "grad_reduce": ("fused peer-memory reduce-scatter" + (" (NVLink multicast)"

@@ -314,7 +314,8 @@ def bench_nf4(cases=((4096, 4096, 4096), (4096, 14336, 4096), (4096, 4096, 14336
 
 def bench_decode_graphs(batch: int = 64, prompt: int = 256, new: int = 128):
     """Paged-KV decode of the dense 1B model: eager steps against steps replayed from CUDA graphs (greedy,
-    same requests); generated tokens per second of the whole ``generate_batch`` call."""
+    same requests); generated tokens per second of a whole ``generate_batch`` call, after one untimed call of
+    the same batch (graph capture happens there)."""
     import time
 
     from rl_project_b200.core.config import model_spec_from_preset
@@ -332,7 +333,7 @@ def bench_decode_graphs(batch: int = 64, prompt: int = 256, new: int = 128):
     out = {}
     for graphs in (False, True):
         eng = InferenceEngine(model, max_batch=batch, decode_graphs=graphs)
-        eng.generate_batch(prompts[:4], SamplingParams(max_tokens=8, temperature=0.0, top_k=None))  # warm-up
+        eng.generate_batch(prompts, params)  # warm-up: the same batch, so every (batch, width) bucket is captured
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         reqs = eng.generate_batch(prompts, params)
@@ -342,7 +343,10 @@ def bench_decode_graphs(batch: int = 64, prompt: int = 256, new: int = 128):
     print(json.dumps({"kernel": "paged_decode_engine", "batch": batch, "prompt": prompt, "new_tokens": new,
                       "eager_tokens_per_s": round(out[False][0], 1), "graphs_tokens_per_s": round(out[True][0], 1),
                       "speedup": round(out[True][0] / out[False][0], 2),
-                      "same_tokens": out[True][1] == out[False][1]}), flush=True)
+                      # greedy tokens of a random-init model sit on near-ties; a different attention split can
+                      # flip one, after which a row diverges -- so report the share of rows that agree fully
+                      "rows_identical": sum(a == b for a, b in zip(out[True][1], out[False][1])) / batch}),
+          flush=True)
 
 
 def main():

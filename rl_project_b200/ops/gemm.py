@@ -8,8 +8,11 @@ without transposing anything:
 * weight grad  ``dW = dy^T x``   A = dy read MN-major,      B = x read MN-major
 
 ``RLB_GEMM`` selects the implementation of the model's plain linear layers:
-``tcgen05`` (this library's kernels), ``cublas`` (torch.matmul) or ``auto``
-(tcgen05 once the numerics self-check on the first call passed).
+``tcgen05`` (this library's kernels), ``cublas`` (torch.matmul), ``auto``
+(tcgen05 once the numerics self-check on the first call passed) or ``tuned``
+(per product shape, the fastest of the 2-SM kernel with 256 x 256 tiles, with
+256 x 512 tiles, and cuBLAS -- timed once with CUDA events on the first call of
+that shape; accumulating and graph-captured calls keep the per-shape default).
 ``RLB_GEMM_KERNEL`` picks the kernel: ``2sm`` (default; CTA pairs issuing
 ``tcgen05.mma.cta_group::2`` on 256 x 256 tiles, TMA-store epilogue) or
 ``1sm`` (one CTA per 128 x 256 tile, register-to-global epilogue; the base of
@@ -65,10 +68,73 @@ def _describe(t: torch.Tensor) -> str:
             f"contiguous={t.is_contiguous()}")
 
 
+# ---------------------------------------------------------------- per-shape kernel choice ("tuned" mode)
+# (a_mn, b_mn, epi, M, N, K, device) -> "own1" | "own2" | "cublas": the fastest of the 2-SM kernel with
+# 256 x 256 tiles, with 256 x 512 tiles, and cuBLAS, timed with CUDA events on the first call of a shape
+_TUNED: dict = {}
+_TUNE_REPS = 3
+
+
+def _launch(choice: str, a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha) -> None:
+    if choice == "cublas":  # only offered for bf16 outputs, alpha 1 and a dense output
+        lhs = a.t() if a_mn else a
+        rhs = b if b_mn else b.t()
+        torch.matmul(lhs, rhs, out=out)
+        return
+    native().gemm2(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None, 0, 2 if choice == "own2" else 1)
+
+
+def _candidates(epi: int, alpha: float, N: int, ldc: int):
+    cands = ["own1"]
+    if epi == 0 and N > 256:
+        cands.append("own2")
+    if epi == 0 and alpha == 1.0 and ldc == N:
+        cands.append("cublas")
+    return cands
+
+
+def _choose(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha) -> str:
+    key = (a_mn, b_mn, epi, M, N, K, a.device.index)
+    got = _TUNED.get(key)
+    if got is not None:
+        return got
+    default = "own2" if nsub_for(M, N, epi, a.device.index or 0, a_mn) == 2 else "own1"
+    cands = _candidates(epi, alpha, N, ldc)
+    if len(cands) == 1 or torch.cuda.is_current_stream_capturing() or epi != 0:
+        return default  # accumulating outputs are never re-run; graphs cannot be timed
+    times = {}
+    for c in cands:
+        _launch(c, a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha)  # warm-up (and correct output)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(_TUNE_REPS):
+            _launch(c, a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha)
+        t1.record()
+        t1.synchronize()
+        times[c] = t0.elapsed_time(t1)
+    best = min(times, key=times.get)
+    _TUNED[key] = best
+    _launch(best, a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha)
+    return best
+
+
+def tuned_choices() -> dict:
+    """The kernel picked for every shape seen so far in ``tuned`` mode."""
+    return dict(_TUNED)
+
+
 def _run(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha):
     try:
         if _KERNEL == "1sm":
             native().gemm(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None)
+        elif _MODE == "tuned":
+            key = (a_mn, b_mn, epi, M, N, K, a.device.index)
+            if key in _TUNED:
+                _launch(_TUNED[key], a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha)
+            else:
+                choice = _choose(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha)
+                if key not in _TUNED:  # not timed (graph capture, accumulation): the per-shape default
+                    _launch(choice, a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha)
         else:
             native().gemm2(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None, 0,
                            nsub_for(M, N, epi, a.device.index or 0, a_mn))
@@ -162,7 +228,7 @@ def _self_check(device: torch.device) -> bool:
 
 
 def enabled() -> bool:
-    return available() and _MODE in ("tcgen05", "auto")
+    return available() and _MODE in ("tcgen05", "auto", "tuned")
 
 
 def supported(a: torch.Tensor, b: torch.Tensor) -> bool:
@@ -170,7 +236,7 @@ def supported(a: torch.Tensor, b: torch.Tensor) -> bool:
         return False
     if not _shape_ok(a, b):
         return False
-    return _MODE == "tcgen05" or _self_check(a.device)
+    return _MODE in ("tcgen05", "tuned") or _self_check(a.device)
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
