@@ -285,6 +285,9 @@ class InferenceEngine:
                 done = self._decode_graph(seqs)
             except Exception as exc:  # noqa: BLE001
                 torch.cuda.current_stream(self.device).synchronize()
+                import traceback
+
+                log.error("decode_graph_step_failed", error=repr(exc), where=traceback.format_exc(limit=6))
                 for s in seqs:
                     self._fail(s, exc)
                 return 0

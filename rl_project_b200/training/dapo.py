@@ -25,8 +25,8 @@ from rl_project_b200.core.protocols import RewardProvider, Trajectory
 from rl_project_b200.rollouts.engine import RolloutConfig, RolloutEngine
 from rl_project_b200.rollouts.rewards.composite import batch_scores, score_trajectories
 from rl_project_b200.training.common.advantages import group_relative_advantages
+from rl_project_b200.training.common.logprobs import packed_response_logprobs
 from rl_project_b200.training.common.trainer import PostTrainingAlgorithm
-from rl_project_b200.training.dpo import pack_prompt_response
 
 
 @dataclass
@@ -111,20 +111,8 @@ class DAPOAlgorithm(PostTrainingAlgorithm):
     def frozen_modules(self):
         return (self.policy.reference_model,) if self.policy.reference_model is not None else ()
 
-    # ------------------------------------------------------------ packed scoring
-    def _score(self, trajs: Sequence[Trajectory], width: int, entropy: bool = False
-               ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
-        """Response-aligned ``[N, width]`` log-probs (and entropies) of the current ``policy.model`` from one
-        packed forward over every trajectory."""
-        pairs = [(t.prompt_ids.tolist(), t.response_ids.tolist()) for t in trajs]
-        inputs, targets = pack_prompt_response(pairs, self.policy.pad_token_id)
-        dev = self.policy.device
-        out = self.policy.model.token_logprobs(inputs.to(dev), targets.to(dev), with_entropy=entropy)
-        lp, ent = out if entropy else (out, None)
-        starts = torch.tensor([len(p) - 1 for p, _ in pairs], device=dev)
-        cols = (starts[:, None] + torch.arange(width, device=dev)[None, :]).clamp(max=lp.shape[1] - 1)
-        take = lambda x: x.float().gather(1, cols)  # noqa: E731
-        return take(lp), (take(ent) if ent is not None else None)
+    def _score(self, trajs: Sequence[Trajectory], width: int, entropy: bool = False):
+        return packed_response_logprobs(self.policy, trajs, width, entropy)
 
     # ------------------------------------------------------------ collection
     def _shape_rewards(self, trajs: Sequence[Trajectory], rewards: torch.Tensor) -> torch.Tensor:

@@ -28,6 +28,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from rl_project_b200.core.errors import ConfigError
+from rl_project_b200.training.common.logprobs import pack_prompt_response  # noqa: F401 - re-exported
 from rl_project_b200.training.common.trainer import PostTrainingAlgorithm
 
 
@@ -59,23 +60,6 @@ def dpo_loss(policy_chosen: torch.Tensor, policy_rejected: torch.Tensor, ref_cho
     r = implicit.detach()
     return {"loss": per_pair.mean(), "chosen_reward": r[0], "rejected_reward": r[1], "margin": r[0] - r[1],
             "accuracy": (r[0] > r[1]).float()}
-
-
-def pack_prompt_response(pairs: Sequence[Tuple[List[int], List[int]]], pad: int):
-    """Right-padded ``inputs [N, T]`` and ``targets [N, T]`` (-1 outside each response): row ``i`` holds
-    ``prompt + response`` shifted by one, so target ``t`` is the token that follows input ``t``."""
-    rows = [list(p) + list(r) for p, r in pairs]
-    starts = torch.tensor([len(p) - 1 for p, _ in pairs])  # first input position that predicts a response token
-    lengths = torch.tensor([len(x) - 1 for x in rows])
-    T = int(lengths.max())
-    flat = torch.full((len(rows), T + 1), pad, dtype=torch.long)
-    for i, x in enumerate(rows):
-        flat[i, :len(x)] = torch.as_tensor(x)
-    cols = torch.arange(T)[None, :]
-    inputs = torch.where(cols < lengths[:, None], flat[:, :-1], torch.full_like(flat[:, :-1], pad))
-    in_response = (cols >= starts[:, None]) & (cols < lengths[:, None])
-    targets = torch.where(in_response, flat[:, 1:], torch.full_like(flat[:, 1:], -1))
-    return inputs, targets
 
 
 def sequence_logprobs(policy, pairs, reduction: str) -> torch.Tensor:

@@ -29,7 +29,8 @@ from rl_project_b200.rollouts.engine import RolloutConfig, RolloutEngine, stack_
 from rl_project_b200.rollouts.rewards.composite import score_trajectories
 from rl_project_b200.training.common.advantages import group_relative_advantages
 from rl_project_b200.ops.rl_loss import clipped_kl_loss
-from rl_project_b200.training.common.logprobs import kl_k3, kl_logprob_diff, masked_mean, masked_sum
+from rl_project_b200.training.common.logprobs import (kl_k3, kl_logprob_diff, masked_mean, masked_sum,
+                                                      packed_response_logprobs)
 from rl_project_b200.training.common.trainer import PostTrainingAlgorithm
 from rl_project_b200.training.ppo import ppo_clipped_objective
 
@@ -214,33 +215,54 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
 
     # ---------------------------------------------------------------- objective
     def loss(self, groups: List[GRPOGroup], micro_step: int, n_micro: int):
-        chunk = groups[micro_step::n_micro] if n_micro > 1 else groups
+        chunk = [g for g in (groups[micro_step::n_micro] if n_micro > 1 else groups) if not g.skipped]
+        if not chunk:
+            zero = sum(p.sum() for p in self.parameters()) * 0.0
+            return zero, {**self._last_stats, "policy_loss": 0.0, "kl": 0.0}
         dev = self.policy.device
+        news = [None] * len(chunk) if self.cfg.agent else self._packed_new(chunk)
         total = torch.zeros((), device=dev)
-        used, kl_acc, pl_acc = 0, torch.zeros((), device=dev), torch.zeros((), device=dev)
-        for grp in chunk:
-            if grp.skipped:
-                continue
+        kl_acc = torch.zeros((), device=dev)
+        pl_acc = torch.zeros((), device=dev)
+        for grp, new in zip(chunk, news):
             adv = grp.advantages.to(dev)
             if self.cfg.objective == "reinforce":
-                loss, kl = self._reinforce_loss(grp, adv), torch.zeros((), device=dev)
+                loss, kl = self._reinforce_loss(grp, adv, new), torch.zeros((), device=dev)
             else:
-                loss, kl = self._clipped_loss(grp, adv)
+                loss, kl = self._clipped_loss(grp, adv, new)
             total = total + loss
             pl_acc = pl_acc + loss.detach()
             kl_acc = kl_acc + kl.detach()
-            used += 1
-        if used == 0:
-            zero = sum(p.sum() for p in self.parameters()) * 0.0
-            return zero, {**self._last_stats, "policy_loss": 0.0, "kl": 0.0}
-        return total / used, {**self._last_stats, "policy_loss": pl_acc / used, "kl": kl_acc / used}
+        n = len(chunk)
+        return total / n, {**self._last_stats, "policy_loss": pl_acc / n, "kl": kl_acc / n}
+
+    def _widths(self, grp: GRPOGroup) -> int:
+        return grp.old_logprobs.shape[1] if grp.old_logprobs is not None else \
+            max(t.response_length for t in grp.trajectories)
+
+    def _packed_new(self, chunk: Sequence[GRPOGroup]) -> List[torch.Tensor]:
+        """Every group's per-token log-probs ``[G, R_g]`` from ONE packed forward over all trajectories of the
+        micro-batch (rows of different prompt lengths right-padded; exact under causal attention)."""
+        trajs = [t for g in chunk for t in g.trajectories]
+        widths = [self._widths(g) for g in chunk]
+        lp, _ = packed_response_logprobs(self.policy, trajs, max(widths))
+        out, row = [], 0
+        for g, w in zip(chunk, widths):
+            out.append(lp[row:row + len(g.trajectories), :w])
+            row += len(g.trajectories)
+        return out
+
+    @staticmethod
+    def _mask(grp: GRPOGroup, width: int, dev) -> torch.Tensor:
+        lengths = torch.tensor([t.response_length for t in grp.trajectories], device=dev)
+        return (torch.arange(width, device=dev)[None, :] < lengths[:, None]).float()
 
     def _kl(self, ref, new, mask):
         if self.cfg.kl_estimator == "k3":
             return kl_k3(ref, new, mask).mean()
         return kl_logprob_diff(ref, new, mask, clamp_min=None).mean().clamp(min=0)
 
-    def _clipped_loss(self, grp: GRPOGroup, adv: torch.Tensor):
+    def _clipped_loss(self, grp: GRPOGroup, adv: torch.Tensor, new: Optional[torch.Tensor]):
         dev = self.policy.device
         if self.cfg.agent:
             new = self.agent_engine.trajectories_logprob(grp.trajectories).float()
@@ -248,21 +270,18 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
             pl = ppo_clipped_objective(torch.exp(new - old), adv, self.cfg.clip_ratio).mean()
             kl = (ref - new).clamp(min=0).mean()
             return pl + self.cfg.kl_coef * kl, kl
-        prompt, resp, mask = stack_group(grp.trajectories, self.policy.pad_token_id)
-        mask = mask.to(dev)
-        new = self.policy.logprobs(prompt, resp).float() * mask
+        mask = self._mask(grp, new.shape[1], dev)
         old, ref = grp.old_logprobs.to(dev), grp.ref_logprobs.to(dev)
         # surrogate + KL (and their gradient) in one fused op; same formulas as _kl / ppo_clipped_objective
-        loss, _, kl = clipped_kl_loss(new, old, ref, mask, adv, self.cfg.clip_ratio, self.cfg.kl_coef,
+        loss, _, kl = clipped_kl_loss(new * mask, old, ref, mask, adv, self.cfg.clip_ratio, self.cfg.kl_coef,
                                       self.cfg.ratio_level, "k3" if self.cfg.kl_estimator == "k3" else "logprob_diff")
         return loss, kl
 
-    def _reinforce_loss(self, grp: GRPOGroup, adv: torch.Tensor) -> torch.Tensor:
+    def _reinforce_loss(self, grp: GRPOGroup, adv: torch.Tensor, new: Optional[torch.Tensor]) -> torch.Tensor:
         if self.cfg.agent:
             lp = self.agent_engine.trajectories_logprob(grp.trajectories).float()
             return (-adv * lp).sum()
-        prompt, resp, mask = stack_group(grp.trajectories, self.policy.pad_token_id)
-        seq_lp = masked_sum(self.policy.logprobs(prompt, resp).float(), mask.to(self.policy.device))
+        seq_lp = masked_sum(new, self._mask(grp, new.shape[1], self.policy.device))
         return (-adv * seq_lp).sum()
 
     # ---------------------------------------------------------------- evaluation

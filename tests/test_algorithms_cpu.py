@@ -193,6 +193,35 @@ def test_dapo_skips_zero_variance_groups(make_ctx, cspec, char_tok):
     assert ok(Trainer(make_ctx("dapo"), alg2).fit())
 
 
+def test_dapo_packed_loss_equals_group_by_group(cspec, char_tok):
+    """The packed forward over every trajectory of a micro-batch (prompts of different lengths) gives the
+    loss of scoring each group alone with its own [G, P] prompt batch."""
+    from rl_project_b200.rollouts.engine import stack_group
+    from rl_project_b200.training.dapo import dapo_token_objective
+
+    torch.manual_seed(7)
+    pol = NativePolicy(TransformerLM(cspec), char_tok)
+    prompts = [torch.tensor(char_tok.encode("Q:")), torch.tensor(char_tok.encode("Longer Q?"))]
+    cfg = DAPOConfig(group_size=3, prompts_per_step=2, dynamic_sampling=False, kl_coef=0.1, entropy_coef=0.01)
+    alg = DAPOAlgorithm(pol, prompts, LengthReward(3), cfg, RolloutConfig(max_new_tokens=6, temperature=1.3))
+    groups = alg.collect(0)
+    loss, _ = alg.loss(groups, 0, 1)
+    pg = kl = ent = 0.0
+    ntok = 0.0
+    for g in groups:
+        prompt, resp, _ = stack_group(g.trajectories, pol.pad_token_id)
+        new, e = pol.logprobs_with_entropy(prompt, resp)
+        R = g.mask.shape[1]
+        new, e = new[:, :R].float() * g.mask, e[:, :R].float()
+        per = dapo_token_objective(torch.exp(new - g.old_logprobs) * g.mask, g.advantages[:, None], 0.2, 0.28)
+        pg += float((per * g.mask).sum())
+        kl += float(((new - g.ref_logprobs) * g.mask).sum())
+        ent += float((e * g.mask).sum())
+        ntok += float(g.mask.sum())
+    ref = (pg + 0.1 * kl - 0.01 * ent) / ntok
+    assert abs(float(loss) - ref) < 1e-4, (float(loss), ref)
+
+
 def test_rlvr_both_optimizers(make_ctx, cspec, char_tok):
     pol = NativePolicy(TransformerLM(cspec), char_tok)
     tasks = [VerifiableTask(prompt=f"What is {i}+1?", answer=str(i + 1)) for i in range(4)]
