@@ -40,19 +40,21 @@ RLB_DEVICE long long head_offset(const RopeArgs& a, int b, int t, int head, int 
 }
 
 // One thread = 8 consecutive dims of the first half of one (token, head) and
-// their 8 partners in the second half.
-template <bool INVERSE>
+// their 8 partners in the second half.  IT is the index type: 32-bit whenever the
+// whole index space (plus one grid stride) fits, so the per-chunk div / mod that
+// locate (token, head, chunk) are 32-bit operations; the cos / sin values of the 8
+// dims are two 16-byte loads each (the table rows are 16-byte aligned: D/2 % 4 == 0).
+template <bool INVERSE, typename IT>
 __global__ void rope_qkv_kernel(RopeArgs a) {
   const int half = a.D >> 1;
   const int chunks = half >> 3;
   const int heads = a.Hq + 2 * a.Hkv;
-  const long long total = (long long)a.B * a.T * heads * chunks;
-  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
+  const IT total = (IT)a.B * a.T * heads * chunks;
+  for (IT idx = (IT)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (IT)gridDim.x * blockDim.x) {
     const int c = (int)(idx % chunks);
-    const long long r = idx / chunks;
+    const IT r = idx / chunks;
     const int head = (int)(r % heads);
-    const long long tok = r / heads;
+    const IT tok = r / heads;
     const int t = (int)(tok % a.T), b = (int)(tok / a.T);
     const int i0 = c * 8;
     // where this head lives on the split side
@@ -64,7 +66,7 @@ __global__ void rope_qkv_kernel(RopeArgs a) {
     else if (head < a.Hq + a.Hkv) { H = a.Hkv; hl = head - a.Hq; }
     else { H = a.Hkv; hl = head - a.Hq - a.Hkv; rotate = false; }
     const long long split_off = head_offset(a, b, t, hl, H);
-    const long long fused_off = tok * a.row_stride + (long long)head * a.D;
+    const long long fused_off = (long long)tok * a.row_stride + (long long)head * a.D;
     if (!INVERSE) {
       sptr = a.src + fused_off;
       dptr = (head < a.Hq ? a.q_dst : (head < a.Hq + a.Hkv ? a.k_dst : a.v_dst)) + split_off;
@@ -79,17 +81,19 @@ __global__ void rope_qkv_kernel(RopeArgs a) {
       rotate = false;
     }
     if (rotate) {
-      const float* ct = a.cos_t + (long long)pos * half + i0;
-      const float* st = a.sin_t + (long long)pos * half + i0;
+      const float4* ct = reinterpret_cast<const float4*>(a.cos_t + (long long)pos * half + i0);
+      const float4* st = reinterpret_cast<const float4*>(a.sin_t + (long long)pos * half + i0);
+      const float4 c4[2] = {__ldg(ct), __ldg(ct + 1)}, s4[2] = {__ldg(st), __ldg(st + 1)};
+      const float* cs = reinterpret_cast<const float*>(c4);
+      const float* sn = reinterpret_cast<const float*>(s4);
       float xl[8], xh[8], ol[8], oh[8];
       unpack8(lo, xl);
       unpack8(hi, xh);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const float cs = ct[k];
-        const float sn = INVERSE ? -st[k] : st[k];
-        ol[k] = xl[k] * cs - xh[k] * sn;
-        oh[k] = xh[k] * cs + xl[k] * sn;
+        const float sk = INVERSE ? -sn[k] : sn[k];
+        ol[k] = xl[k] * cs[k] - xh[k] * sk;
+        oh[k] = xh[k] * cs[k] + xl[k] * sk;
       }
       lo = pack8(ol);
       hi = pack8(oh);
@@ -97,6 +101,22 @@ __global__ void rope_qkv_kernel(RopeArgs a) {
     stg8(dptr + i0, lo);
     stg8(dptr + i0 + half, hi);
   }
+}
+
+static int grid_for(long long work, int sms) {
+  long long g = (work + 255) / 256;
+  long long cap = (long long)sms * 16;
+  return (int)(g < 1 ? 1 : (g < cap ? g : cap));
+}
+
+// 32-bit indices when the index space and one grid stride fit in an int
+template <bool INVERSE>
+static void launch_rope_qkv(const RopeArgs& a, long long work, int sms, cudaStream_t s) {
+  const int grid = grid_for(work, sms);
+  if (work + (long long)grid * 256 < 2147483647LL)
+    rope_qkv_kernel<INVERSE, int><<<grid, 256, 0, s>>>(a);
+  else
+    rope_qkv_kernel<INVERSE, long long><<<grid, 256, 0, s>>>(a);
 }
 
 // In-place rotation of x[b, t, h, 0:D] addressed with explicit strides.
@@ -130,12 +150,6 @@ __global__ void rope_inplace_kernel(__nv_bfloat16* x, int B, int T, int H, int D
 
 using namespace rlb;
 
-static int grid_for(long long work, int sms) {
-  long long g = (work + 255) / 256;
-  long long cap = (long long)sms * 16;
-  return (int)(g < 1 ? 1 : (g < cap ? g : cap));
-}
-
 cudaError_t rlb_rope_qkv_fwd(const void* qkv, long long row_stride, void* q, void* k, void* v, const float* cos_t,
                              const float* sin_t, const int* positions, int B, int T, int Hq, int Hkv, int D,
                              int pos_offset, int heads_major, int table_rows, int* status, int sms, cudaStream_t s) {
@@ -153,7 +167,7 @@ cudaError_t rlb_rope_qkv_fwd(const void* qkv, long long row_stride, void* q, voi
   a.table_rows = table_rows;
   a.status = status;
   const long long work = (long long)B * T * (Hq + 2 * Hkv) * (D / 16);
-  rope_qkv_kernel<false><<<grid_for(work, sms), 256, 0, s>>>(a);
+  launch_rope_qkv<false>(a, work, sms, s);
   return cudaGetLastError();
 }
 
@@ -175,7 +189,7 @@ cudaError_t rlb_rope_qkv_bwd(const void* dq, const void* dk, const void* dv, voi
   a.table_rows = table_rows;
   a.status = status;
   const long long work = (long long)B * T * (Hq + 2 * Hkv) * (D / 16);
-  rope_qkv_kernel<true><<<grid_for(work, sms), 256, 0, s>>>(a);
+  launch_rope_qkv<true>(a, work, sms, s);
   return cudaGetLastError();
 }
 

@@ -2,8 +2,9 @@
 
 ``linear`` (every linear layer, with its backward) and ``matmul_nt`` /
 ``matmul_nn`` / ``matmul_tn`` (the LM head's products) run this library's
-tcgen05 GEMM (csrc/gemm_2sm.cu) on sm_100a; ``RLB_GEMM=cublas`` routes them
-to cuBLAS instead (the library baseline, no fused epilogue).
+tcgen05 GEMM (csrc/gemm_2sm.cu) on sm_100a when ``RLB_GEMM=tcgen05``; by default
+(``RLB_GEMM=cublas``) they are plain cuBLAS products, which measured faster in the full
+training step.
 """
 
 from __future__ import annotations

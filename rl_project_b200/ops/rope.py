@@ -19,7 +19,7 @@ from rl_project_b200.ops._ext import native
 
 def rope_inv_freq(dim: int, theta: float = 10000.0, scaling_type: str = "none", factor: float = 1.0,
                   max_seq_len: int = 8192) -> torch.Tensor:
-    exps = torch.arange(0, dim, 2, dtype=torch.float64) / dim
+    exps = torch.arange(0, dim, 2, dtype=torch.float64, device="cpu") / dim  # host, whatever the default device
     if scaling_type == "yarn" and factor != 1.0:
         base = theta * factor ** (dim / (dim - 2))
         inv = base ** (-exps)
@@ -46,8 +46,10 @@ class RopeTable:
         self._build(max(max_seq_len, 1))
 
     def _build(self, rows: int) -> None:
-        t = torch.arange(rows, dtype=torch.float64)
-        ang = torch.outer(t, self.inv_freq.double())
+        # built on the host (a model constructed under a CUDA default device would otherwise put these on the
+        # GPU at construction and on the host when the table grows later), copied to each device on use
+        t = torch.arange(rows, dtype=torch.float64, device="cpu")
+        ang = torch.outer(t, self.inv_freq.double().cpu())
         self._cos = ang.cos().float()
         self._sin = ang.sin().float()
         self._rows = rows

@@ -113,3 +113,15 @@ def test_fmha_wrapper_shapes_and_layout():
     with pytest.raises(KernelError):  # 3 query heads do not group over 2 key/value heads
         fmha_forward(torch.zeros(1, 3, 4, 64, dtype=torch.bfloat16), torch.zeros(1, 2, 4, 64, dtype=torch.bfloat16),
                      torch.zeros(1, 2, 4, 64, dtype=torch.bfloat16))
+
+
+def test_rope_table_stays_on_the_host_under_a_default_device():
+    """Tables built while a non-CPU default device is active (a model constructed under ``torch.device``)
+    are host tensors, so growing them later cannot mix devices."""
+    from rl_project_b200.ops.rope import RopeTable
+
+    with torch.device("meta"):
+        table = RopeTable(64, max_seq_len=16)
+    assert table.inv_freq.device.type == "cpu" and table._cos.device.type == "cpu"
+    cos, sin = table.tables(64, torch.device("cpu"))  # grows the table outside the context
+    assert cos.shape == (64, 32) and torch.isfinite(sin).all()
