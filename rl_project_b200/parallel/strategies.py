@@ -147,40 +147,30 @@ class DeepSpeedStrategy(_ProcessGroupStrategy):
         return self.initialize(model)
 
 
+# strategy name -> (module, class, constructor keywords); the heavier strategies import on first use
+_LAZY = {
+    "fsdp": ("rl_project_b200.parallel.fsdp", "FSDPStrategy", {}),
+    "zero2": ("rl_project_b200.parallel.fsdp", "FSDPStrategy", {"reshard_params": False, "name": "zero2"}),
+    "tensor_parallel": ("rl_project_b200.parallel.mesh_strategies", "MeshStrategy", {"name": "tensor_parallel"}),
+    "pipeline_parallel": ("rl_project_b200.parallel.mesh_strategies", "MeshStrategy", {"name": "pipeline_parallel"}),
+    "hybrid": ("rl_project_b200.parallel.mesh_strategies", "MeshStrategy", {"name": "hybrid"}),
+    "expert_parallel": ("rl_project_b200.parallel.expert", "ExpertParallelStrategy", {}),
+}
+
+
 def _lazy(name: str):
+    module, cls, kw = _LAZY[name]
+
     def make(cfg: DistributedConfig):
-        if name == "fsdp":
-            from rl_project_b200.parallel.fsdp import FSDPStrategy
+        import importlib
 
-            return FSDPStrategy(cfg)
-        if name == "zero2":
-            from rl_project_b200.parallel.fsdp import FSDPStrategy
-
-            return FSDPStrategy(cfg, reshard_params=False, name="zero2")
-        if name in ("tensor_parallel", "pipeline_parallel", "hybrid"):
-            from rl_project_b200.parallel.mesh_strategies import MeshStrategy
-
-            return MeshStrategy(cfg, name)
-        if name == "expert_parallel":
-            from rl_project_b200.parallel.expert import ExpertParallelStrategy
-
-            return ExpertParallelStrategy(cfg)
-        raise DistributedConfigError(f"unknown strategy {name!r}")
+        return getattr(importlib.import_module(module), cls)(cfg, **kw)
 
     return make
 
 
-STRATEGIES = {
-    "single": SingleProcessStrategy,
-    "ddp": DDPStrategy,
-    "deepspeed": DeepSpeedStrategy,
-    "fsdp": _lazy("fsdp"),
-    "zero2": _lazy("zero2"),
-    "tensor_parallel": _lazy("tensor_parallel"),
-    "pipeline_parallel": _lazy("pipeline_parallel"),
-    "hybrid": _lazy("hybrid"),
-    "expert_parallel": _lazy("expert_parallel"),
-}
+STRATEGIES = {"single": SingleProcessStrategy, "ddp": DDPStrategy, "deepspeed": DeepSpeedStrategy,
+              **{name: _lazy(name) for name in _LAZY}}
 
 
 def build_strategy(cfg: DistributedConfig):
