@@ -53,21 +53,34 @@ class RoutingPolicy:
         return bool(name) and name not in self.disabled
 
     def route(self, request_id: str, requested: Optional[str] = None) -> RoutingDecision:
+        """First rule that decides wins: an explicitly requested pinned backend, a pin of this request id, then
+        the hash split between challenger and champion; the shadow copy is decided independently."""
         self.validate()
+        for rule in (self._explicit, self._pinned):
+            decision = rule(request_id, requested)
+            if decision is not None:
+                return decision
+        bucket = stable_bucket(request_id, self.salt)
+        to_challenger = self._live(self.challenger) and bucket < self.challenger_percent * 100
+        primary = self.challenger if to_challenger else self.champion
+        reason = f"challenger ({self.challenger_percent}%)" if to_challenger else "champion"
+        return RoutingDecision(primary=primary, shadow=self._shadow_for(request_id, primary), bucket=bucket,  # type: ignore[arg-type]
+                               reason=reason)
+
+    def _explicit(self, request_id: str, requested: Optional[str]) -> Optional[RoutingDecision]:
         if requested and requested in self.pinned.values() and self._live(requested):
             return RoutingDecision(primary=requested, bucket=-1, reason="explicit model request")
+        return None
+
+    def _pinned(self, request_id: str, requested: Optional[str]) -> Optional[RoutingDecision]:
         pin = self.pinned.get(request_id)
-        if self._live(pin):
-            return RoutingDecision(primary=pin, bucket=-1, reason="pinned")  # type: ignore[arg-type]
-        bucket = stable_bucket(request_id, self.salt)
-        primary, reason = self.champion, "champion"
-        if self._live(self.challenger) and bucket < self.challenger_percent * 100:
-            primary, reason = self.challenger, f"challenger ({self.challenger_percent}%)"  # type: ignore[assignment]
-        shadow = None
+        return RoutingDecision(primary=pin, bucket=-1, reason="pinned") if self._live(pin) else None  # type: ignore[arg-type]
+
+    def _shadow_for(self, request_id: str, primary: Optional[str]) -> Optional[str]:
         if self._live(self.shadow) and self.shadow != primary and \
                 in_percentage(request_id, self.salt + ":shadow", self.shadow_percent):
-            shadow = self.shadow
-        return RoutingDecision(primary=primary, shadow=shadow, bucket=bucket, reason=reason)
+            return self.shadow
+        return None
 
     def as_route_fn(self) -> Callable[[str, Optional[str]], str]:
         return lambda request_id, requested: self.route(request_id, requested).primary

@@ -1,9 +1,8 @@
 """Orchestration settings, importable without Ray.
 
-``RayConfig`` keeps the reference's manifest keys
-(``src/forgeline/orchestration/config.py:14-67``); ``validate_orchestration``
-checks an ``orchestration`` mapping without importing Ray
-(``src/forgeline/orchestration/__init__.py:27-39``).
+``RayConfig`` carries the manifest keys of ``src/forgeline/orchestration/config.py`` and is validated
+against the ``_RULES`` table; ``validate_orchestration`` checks an ``orchestration`` mapping without
+importing Ray (the check of ``src/forgeline/orchestration/__init__.py``).
 """
 
 from __future__ import annotations
@@ -39,18 +38,9 @@ class RayConfig:
     backend: str = "ray"  # "ray" actors, or "threads": in-process workers (single node, tests)
 
     def validate(self) -> None:
-        if self.backend not in ("ray", "threads"):
-            raise ConfigError("orchestration.backend must be 'ray' or 'threads'")
-        if self.address is not None and (self.num_cpus is not None or self.num_gpus is not None):
-            raise ConfigError("orchestration.num_cpus/num_gpus apply only when Ray is started locally (address unset)")
-        if min(self.rollout_workers, self.reward_workers) < 0:
-            raise ConfigError("orchestration worker counts must be >= 0")
-        if min(self.cpus_per_worker, self.gpus_per_worker) < 0:
-            raise ConfigError("orchestration per-worker resources must be >= 0")
-        if self.placement_strategy is not None and self.placement_strategy not in PLACEMENT_STRATEGIES:
-            raise ConfigError(f"placement_strategy must be one of {PLACEMENT_STRATEGIES}")
-        if self.max_restarts < -1 or self.max_call_retries < 0:
-            raise ConfigError("max_restarts must be >= -1 and max_call_retries >= 0")
+        for broken, message in _RULES:
+            if broken(self):
+                raise ConfigError(message)
 
     @classmethod
     def from_dict(cls, data: Mapping[str, Any]) -> "RayConfig":
@@ -64,6 +54,19 @@ class RayConfig:
 
     def to_dict(self) -> Dict[str, Any]:
         return dataclasses.asdict(self)
+
+
+# (condition that makes a config invalid, message), checked in order
+_RULES = (
+    (lambda c: c.backend not in ("ray", "threads"), "orchestration.backend must be 'ray' or 'threads'"),
+    (lambda c: c.address is not None and (c.num_cpus is not None or c.num_gpus is not None),
+     "orchestration.num_cpus/num_gpus apply only when Ray is started locally (address unset)"),
+    (lambda c: min(c.rollout_workers, c.reward_workers) < 0, "orchestration worker counts must be >= 0"),
+    (lambda c: min(c.cpus_per_worker, c.gpus_per_worker) < 0, "orchestration per-worker resources must be >= 0"),
+    (lambda c: c.placement_strategy is not None and c.placement_strategy not in PLACEMENT_STRATEGIES,
+     f"placement_strategy must be one of {PLACEMENT_STRATEGIES}"),
+    (lambda c: c.max_restarts < -1 or c.max_call_retries < 0, "max_restarts must be >= -1 and max_call_retries >= 0"),
+)
 
 
 def ray_available() -> bool:

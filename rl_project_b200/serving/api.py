@@ -28,6 +28,9 @@ log = get_logger("forgeline.serving")
 
 Response = Tuple[int, Union[Dict[str, Any], Iterator[str]]]
 
+# exception type -> (HTTP status, error code); first match wins (BackendUnavailableError is a ServingError)
+_ERRORS = ((BackendUnavailableError, (503, "backend_unavailable")), (ServingError, (400, "invalid_request_error")))
+
 
 def _percentile(sorted_vals, q: float) -> float:
     if not sorted_vals:
@@ -62,15 +65,11 @@ class Router:
             return 404, error_response(f"no route for {method} {path}", "not_found", 404)
         try:
             return fn()
-        except BackendUnavailableError as exc:
+        except Exception as exc:  # noqa: BLE001 - every failure becomes a JSON error response
+            status, code = next((sc for kind, sc in _ERRORS if isinstance(exc, kind)), (500, "server_error"))
             self._error(exc)
-            return 503, error_response(str(getattr(exc, "message", exc)), "backend_unavailable", 503)
-        except ServingError as exc:
-            self._error(exc)
-            return 400, error_response(str(getattr(exc, "message", exc)), "invalid_request_error", 400)
-        except Exception as exc:  # noqa: BLE001
-            self._error(exc)
-            return 500, error_response(f"{type(exc).__name__}: {exc}", "server_error", 500)
+            msg = str(getattr(exc, "message", exc)) if status != 500 else f"{type(exc).__name__}: {exc}"
+            return status, error_response(msg, code, status)
 
     def _error(self, exc: BaseException) -> None:
         with self._lock:
