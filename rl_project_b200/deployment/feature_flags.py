@@ -45,16 +45,15 @@ class FeatureFlag:
             raise ConfigError(f"flag {self.name!r}: percentage must be in [0, 100]")
 
     def is_on(self, key: Optional[str] = None) -> bool:
+        """Disabled flags are off; a key on the deny / allow list is off / on; otherwise the percentage
+        decides (all, none, or the key's stable bucket -- a flag below 100 % is off for anonymous calls)."""
         if not self.enabled:
             return False
-        if key is not None and key in self.deny:
-            return False
-        if key is not None and key in self.allow:
-            return True
-        if self.percentage >= 100.0:
-            return True
-        if self.percentage <= 0.0 or key is None:
-            return False
+        listed = None if key is None else (False if key in self.deny else (True if key in self.allow else None))
+        if listed is not None:
+            return listed
+        if self.percentage >= 100.0 or self.percentage <= 0.0 or key is None:
+            return self.percentage >= 100.0
         return in_percentage(key, self.salt or self.name, self.percentage)
 
     def to_dict(self) -> Dict[str, Any]:

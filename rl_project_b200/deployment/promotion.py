@@ -101,25 +101,22 @@ class PromotionGate:
             return GateCheck(rule.metric, False, None if c is None else float("nan"), b,
                              "candidate metric missing or non-finite")
         c = float(c)
-        problems: List[str] = []
-        if rule.min is not None and c < rule.min:
-            problems.append(f"{c:.6g} < min {rule.min:.6g}")
-        if rule.max is not None and c > rule.max:
-            problems.append(f"{c:.6g} > max {rule.max:.6g}")
+        # (active, violated, message) of every absolute bound
+        bounds = [(rule.min is not None, lambda: c < rule.min, lambda: f"{c:.6g} < min {rule.min:.6g}"),
+                  (rule.max is not None, lambda: c > rule.max, lambda: f"{c:.6g} > max {rule.max:.6g}")]
+        problems = [msg() for active, bad, msg in bounds if active and bad()]
         note = ""
         if rule.needs_baseline:
             if baseline is None and self.when_no_baseline == "skip_relative":
-                note = " (relative rule skipped: no incumbent)"
-                b = None
-            elif not _finite(b):
+                return GateCheck(rule.metric, not problems, c, None,
+                                 ("; ".join(problems) or "ok") + " (relative rule skipped: no incumbent)")
+            if not _finite(b):
                 return GateCheck(rule.metric, False, c, b, "baseline metric missing or non-finite")
-            else:
-                b = float(b)
-                scale = abs(b) if rule.relative else 1.0
-                if rule.min_delta is not None and c < b + rule.min_delta * scale:
-                    problems.append(f"{c:.6g} < baseline {b:.6g} + {rule.min_delta * scale:.6g}")
-                if rule.max_increase is not None and c > b + rule.max_increase * scale:
-                    problems.append(f"{c:.6g} > baseline {b:.6g} + {rule.max_increase * scale:.6g}")
+            b = float(b)
+            scale = abs(b) if rule.relative else 1.0
+            relative = [(rule.min_delta, lambda d: c < b + d, lambda d: f"{c:.6g} < baseline {b:.6g} + {d:.6g}"),
+                        (rule.max_increase, lambda d: c > b + d, lambda d: f"{c:.6g} > baseline {b:.6g} + {d:.6g}")]
+            problems += [msg(v * scale) for v, bad, msg in relative if v is not None and bad(v * scale)]
         return GateCheck(rule.metric, not problems, c, b, ("; ".join(problems) or "ok") + note)
 
     def evaluate(self, candidate: Mapping[str, float],
