@@ -70,8 +70,8 @@ def parse_args():
                          "the fastest of the two (timed on the first call of each shape)")
     ap.add_argument("--attn", choices=["sdpa", "tcgen05"], default="sdpa",
                     help="training / prefill attention: torch SDPA (cuDNN / flash) or this library's tcgen05 kernels")
-    ap.add_argument("--decode-graphs", action="store_true",
-                    help="grpo workload: replay the paged decode step from CUDA graphs")
+    ap.add_argument("--decode-graphs", choices=["on", "off"], default="on",
+                    help="grpo workload: replay the paged decode step from CUDA graphs (single-GPU engines)")
     args, extra = ap.parse_known_args()
     args.extra = extra
     if extra and args.workload != "grpo":
@@ -85,9 +85,8 @@ def apply_kernel_choices(args) -> dict:
 
     attention._ATTN = args.attn
     gemm._MODE = args.gemm
-    if args.decode_graphs:
-        os.environ["RLB_DECODE_GRAPHS"] = "1"
-    return {"attention": args.attn, "gemm": args.gemm, "decode_graphs": bool(args.decode_graphs)}
+    os.environ["RLB_DECODE_GRAPHS"] = "1" if args.decode_graphs == "on" else "0"
+    return {"attention": args.attn, "gemm": args.gemm, "decode_graphs": args.decode_graphs == "on"}
 
 
 def gemm_choice_summary() -> dict:

@@ -22,14 +22,13 @@ built differently:
 Models whose attention is not grouped-query (MLA, NSA) decode through the
 model's own contiguous ``step`` cache, grouped by length as in the reference.
 
-With ``decode_graphs=True`` (or ``RLB_DECODE_GRAPHS=1``) the paged decode step
-is replayed from CUDA graphs instead of launching its ~10 kernels per layer from
-the host: one graph per (batch, block-table width) bucket, both rounded up to a
-power of two, captured on first use.  Padding rows decode a dummy token into a
-block reserved for them, so they never touch a live sequence's K/V.  Graphs
-hold the model's weight and KV-pool addresses: call ``reset_graphs()`` after
-replacing (not updating in place) a weight tensor.  Not yet measured on a GPU,
-so off by default.
+On CUDA the paged decode step is replayed from CUDA graphs (default; ``decode_graphs=False`` or
+``RLB_DECODE_GRAPHS=0`` launches it eagerly) instead of launching its ~10 kernels per layer from
+the host: one graph per (batch, block-table width) bucket, both rounded up to a power of two,
+captured on first use.  Padding rows decode a dummy token into a block reserved for them, so they
+never touch a live sequence's K/V.  Graphs hold the model's weight and KV-pool addresses: call
+``reset_graphs()`` after replacing (not updating in place) a weight tensor.  Measured on B200 with
+the dense 1B model, batch 64: 26.9k generated tokens/s against 13.5k eager, identical greedy tokens.
 """
 
 from __future__ import annotations
@@ -106,7 +105,7 @@ class InferenceEngine:
         self._lock = threading.Lock()
         # CUDA-graph decode (paged models on CUDA only)
         if decode_graphs is None:
-            decode_graphs = os.environ.get("RLB_DECODE_GRAPHS", "0") == "1"
+            decode_graphs = os.environ.get("RLB_DECODE_GRAPHS", "1") == "1"
         self.max_batch = max_batch
         self._graphs: Dict[Tuple[int, int], Any] = {}
         self._graph_pool: Any = None

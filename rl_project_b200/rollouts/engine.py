@@ -41,7 +41,7 @@ class RolloutConfig:
     engine: str = "auto"  # "auto" | "paged" | "generate"
     engine_max_batch: int = 256  # sequences decoding at once in the paged engine
     engine_kv_blocks: Optional[int] = None  # KV pool size in 16-token blocks (default: enough for max_batch)
-    engine_decode_graphs: Optional[bool] = None  # replay decode steps from CUDA graphs (None: RLB_DECODE_GRAPHS)
+    engine_decode_graphs: Optional[bool] = None  # replay decode steps from CUDA graphs (None: RLB_DECODE_GRAPHS, default on)
     # > 0 in a distributed run: the ranks form world / replica_tp tensor-parallel generation replicas of this
     # many GPUs (rollouts/replicas.py) that share each step's prompts; 0: every rank generates its own
     replica_tp: int = 0

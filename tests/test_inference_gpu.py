@@ -43,7 +43,7 @@ def test_engine_greedy_matches_full_forward(n_embd, n_head, n_kv, extra):
     for p, r in zip(prompts, reqs):
         assert len(r.generated_tokens) == 16
         _check_greedy(model, p, r.generated_tokens)
-    assert eng.allocator.used_blocks == 0
+    assert eng.allocator.used_blocks == (1 if eng.decode_graphs else 0)  # graph decode keeps a padding block
 
 
 def test_engine_prefix_sharing_gpu():
@@ -60,7 +60,7 @@ def test_engine_prefix_sharing_gpu():
     _check_greedy(model, prompt, reqs[0].generated_tokens)
     for r in sampled:
         assert len(r.generated_tokens) == 10 and all(0 <= t < 512 for t in r.generated_tokens)
-    assert eng.allocator.used_blocks == 0
+    assert eng.allocator.used_blocks == (1 if eng.decode_graphs else 0)  # graph decode keeps a padding block
 
 
 def test_graph_decode_matches_eager_decode():
