@@ -64,62 +64,87 @@ class RLAIFConfig:
 
 
 def _gen(policy, prompt: str, temperature: float, max_new: int, top_p=None) -> str:
-    ids = torch.tensor(policy.encode(prompt), dtype=torch.long)[None]
-    with torch.no_grad():
-        out = policy.generate(ids.to(policy.device), GenerationSettings(max_new_tokens=max_new, temperature=temperature,
-                                                                        top_p=top_p))
-    return policy.decode(out[0])
+    return _gen_many(policy, [prompt], temperature, max_new, top_p)[0]
+
+
+def _gen_many(policy, prompts: Sequence[str], temperature: float, max_new: int, top_p=None) -> List[str]:
+    """Decoded continuations of every prompt: prompts of equal token length share one batched ``generate``
+    call."""
+    encoded = [policy.encode(p) or [0] for p in prompts]
+    by_len: Dict[int, List[int]] = {}
+    for i, ids in enumerate(encoded):
+        by_len.setdefault(len(ids), []).append(i)
+    out: List[Optional[str]] = [None] * len(prompts)
+    settings = GenerationSettings(max_new_tokens=max_new, temperature=temperature, top_p=top_p)
+    for rows in by_len.values():
+        batch = torch.tensor([encoded[i] for i in rows], dtype=torch.long, device=policy.device)
+        with torch.no_grad():
+            gen = policy.generate(batch, settings)
+        for i, g in zip(rows, gen):
+            out[i] = policy.decode(g)
+    return out  # type: ignore[return-value]
+
+
+_SOLVE = "Solve step by step, showing every calculation, and end with the numeric answer.\n{prompt}\n"
 
 
 class RLAIFTrainer:
+    """Rounds of: K candidates per task (one batched generation per task), the policy judging every candidate
+    (judge prompts batched by length), and one reference-free DPO step over all pairs whose judged scores
+    differ by at least ``pair_gap`` (every pair's chosen and rejected sides scored in one packed forward)."""
+
     def __init__(self, policy, tasks: Sequence[VerifiableTask], cfg: RLAIFConfig, output_dir: str | Path,
                  judge_fn: Optional[Callable[[str, str], float]] = None):
         self.policy, self.cfg = policy, cfg
         self.tasks = list(tasks)[: cfg.num_problems]
         self.out = Path(output_dir)
         self.out.mkdir(parents=True, exist_ok=True)
-        self.judge_fn = judge_fn or self._self_judge
+        self.judge_fn = judge_fn
         self.optimizer = torch.optim.AdamW(policy.trainable_parameters(), lr=cfg.learning_rate)
         self.history: List[Dict] = []
         self.rng = random.Random(cfg.seed)
 
     def _self_judge(self, problem: str, response: str) -> float:
-        return parse_judge_score(_gen(self.policy, JUDGE_TEMPLATE.format(problem=problem, response=response[:800]), 0.0,
-                                      self.cfg.judge_max_tokens))
+        return self._judge_many([(problem, response)])[0]
+
+    def _judge_many(self, items: Sequence[Tuple[str, str]]) -> List[float]:
+        if self.judge_fn is not None:
+            return [float(self.judge_fn(p, r)) for p, r in items]
+        prompts = [JUDGE_TEMPLATE.format(problem=p, response=r[:800]) for p, r in items]
+        return [parse_judge_score(t) for t in _gen_many(self.policy, prompts, 0.0, self.cfg.judge_max_tokens)]
 
     def collect_pairs(self) -> List[PreferenceRecord]:
+        K = self.cfg.candidates_per_prompt
+        prompts = [_SOLVE.format(prompt=t.prompt) for t in self.tasks]
+        cands = [_gen_many(self.policy, [p] * K, self.cfg.temperature, self.cfg.max_new_tokens) for p in prompts]
+        scores = self._judge_many([(t.prompt, c) for t, cs in zip(self.tasks, cands) for c in cs])
+        gap = self.cfg.pair_gap / 10.0
         pairs = []
-        for task in self.tasks:
-            prompt = f"Solve step by step, showing every calculation, and end with the numeric answer.\n{task.prompt}\n"
-            cands = [_gen(self.policy, prompt, self.cfg.temperature, self.cfg.max_new_tokens)
-                     for _ in range(self.cfg.candidates_per_prompt)]
-            scores = [self.judge_fn(task.prompt, c) for c in cands]
-            for i, ci in enumerate(cands):
-                for j, cj in enumerate(cands):
-                    if i != j and ci != cj and scores[i] - scores[j] >= self.cfg.pair_gap / 10.0:
-                        pairs.append(PreferenceRecord(prompt, ci, cj, {"score_gap": round(scores[i] - scores[j], 3)}))
+        for n, (prompt, cs) in enumerate(zip(prompts, cands)):
+            sc = scores[n * K:(n + 1) * K]
+            pairs += [PreferenceRecord(prompt, cs[i], cs[j], {"score_gap": round(sc[i] - sc[j], 3)})
+                      for i in range(K) for j in range(K) if i != j and cs[i] != cs[j] and sc[i] - sc[j] >= gap]
         log.info("rlaif_pairs", pairs=len(pairs), problems=len(self.tasks))
         return pairs
 
-    def _dpo_step(self, pairs: List[PreferenceRecord]) -> float:
-        from rl_project_b200.training.dpo import dpo_loss
-
+    def _fit(self, q: List[int], r: List[int]) -> Tuple[List[int], List[int]]:
+        """Keep prompt + response within the model's block: the response is cut to half a block first."""
         block = getattr(getattr(self.policy, "spec", None), "block_size", None)
+        if block is not None and len(q) + len(r) > block:
+            r = r[:max(1, block // 2)]
+            q = q[-(block - len(r)):]
+        return q, r
 
-        def fit(q, r):
-            if block is not None and len(q) + len(r) > block:
-                r = r[: max(1, block // 2)]
-                q = q[-(block - len(r)):]
-            return torch.tensor(q)[None], torch.tensor(r)[None]
+    def _dpo_step(self, pairs: List[PreferenceRecord]) -> float:
+        from rl_project_b200.training.dpo import dpo_loss, sequence_logprobs
 
-        total = torch.zeros((), device=self.policy.device)
-        for p in pairs:
-            q = self.policy.encode(p.prompt) or [0]
-            lc = self.policy.logprobs(*fit(q, self.policy.encode(p.chosen) or [0])).float().sum()
-            lr = self.policy.logprobs(*fit(q, self.policy.encode(p.rejected) or [0])).float().sum()
-            z = torch.zeros(1, device=lc.device)
-            total = total + dpo_loss(lc[None], lr[None], z, z, self.cfg.dpo_beta)["loss"]
-        loss = total / max(len(pairs), 1)
+        rows = []
+        for side in ("chosen", "rejected"):
+            for p in pairs:
+                rows.append(self._fit(self.policy.encode(p.prompt) or [0], self.policy.encode(getattr(p, side)) or [0]))
+        seq = sequence_logprobs(self.policy, rows, "sum").view(2, len(pairs))  # one packed forward
+        zero = torch.zeros_like(seq[0])
+        loss = dpo_loss(seq[0], seq[1], zero, zero, self.cfg.dpo_beta)["loss"]  # reference-free
         loss.backward()
         torch.nn.utils.clip_grad_norm_(self.policy.trainable_parameters(), 1.0)
         self.optimizer.step()

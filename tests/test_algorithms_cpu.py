@@ -327,3 +327,24 @@ def test_distillation_loss_value_and_gradient_match_autograd(monkeypatch):
     # the op works in fp32 whatever the input dtype
     assert abs(float(got) - float(ref)) < 1e-5 * abs(float(ref))
     assert torch.allclose(g_got, g_ref, atol=1e-7)
+
+
+def test_rlaif_trainer_round_with_batched_generation_and_packed_dpo(cspec, char_tok, tmp_path):
+    """One RLAIF round: K candidates per task from one batched generation, judged (a content-hash judge and
+    the policy's own judge), pairs past the score gap, one reference-free DPO step over all pairs."""
+    from rl_project_b200.training.rlaif import RLAIFConfig, RLAIFTrainer
+
+    torch.manual_seed(11)
+    pol = NativePolicy(TransformerLM(cspec), char_tok)
+    tasks = [VerifiableTask(prompt=f"What is {i}+2?", answer=str(i + 2)) for i in range(2)]
+    cfg = RLAIFConfig(num_rounds=1, candidates_per_prompt=3, pair_gap=0.5, max_new_tokens=8, temperature=1.5,
+                      judge_max_tokens=4, num_problems=2)
+    w0 = [p.detach().clone() for p in pol.trainable_parameters()]
+    res = RLAIFTrainer(pol, tasks, cfg, tmp_path, judge_fn=lambda q, r: (sum(map(ord, r)) % 11) / 10.0).run()
+    h = res["history"][0]
+    assert h["pairs"] > 0 and math.isfinite(h["dpo_loss"])
+    assert any(not torch.equal(a, b) for a, b in zip(w0, pol.trainable_parameters()))
+    # the policy as its own judge: scores parsed from its replies (fallback 0.5 for unparsable text)
+    own = RLAIFTrainer(pol, tasks, cfg, tmp_path / "own")
+    scores = own._judge_many([("1+1?", "2"), ("2+2?", "4")])
+    assert len(scores) == 2 and all(0.0 <= s <= 1.0 for s in scores)
