@@ -13,9 +13,11 @@ synthetic sources used by the benchmark configurations:
 
 from __future__ import annotations
 
+from dataclasses import dataclass
+
 import dataclasses
 from pathlib import Path
-from typing import Any, Dict, List, Optional
+from typing import Any, Dict, List, Optional, Tuple
 
 import torch
 
@@ -147,159 +149,211 @@ def _rank() -> int:
     return data_parallel_rank()
 
 
+@dataclass
+class _Job:
+    """What every algorithm builder reads: the manifest, the run context, the algorithm parameters (the
+    ``rollout`` block taken out and parsed) and the data section's extra keys."""
+
+    manifest: ExperimentManifest
+    ctx: RunContext
+    params: Dict[str, Any]
+    rollout: Optional[RolloutConfig]
+    extra: Dict[str, Any]
+
+
+def _build_pretrain(j: _Job) -> PostTrainingAlgorithm:
+    from rl_project_b200.training.pretrain import PretrainAlgorithm, PretrainConfig
+
+    m, ctx = j.manifest, j.ctx
+    cfg = _kw({"batch_size": m.trainer.batch_size, "eval_batches": m.trainer.eval_batches, **j.params}, PretrainConfig)
+    if _synthetic(m):
+        from rl_project_b200.data.synthetic import SyntheticPretrainSource
+
+        model = build_model(m, ctx)
+        src = SyntheticPretrainSource(m.model.vocab_size, m.model.block_size, cfg.batch_size, seed=m.data.seed,
+                                      rank=_rank())
+        return PretrainAlgorithm(model, src, cfg, None, device=ctx.device)
+    root = Path(m.data.path)
+    tok_meta = load_tokenizer_metadata(m.data.path) if (root / "meta.pkl").exists() else None
+    if tok_meta:
+        m.model.vocab_size = int(tok_meta["vocab_size"])
+    model = build_model(m, ctx)
+    train = MemmapCorpus(m.data.path, "train", m.model.block_size)
+    val = MemmapCorpus(m.data.path, "val", m.model.block_size) if (root / "val.bin").exists() else None
+    return PretrainAlgorithm(model, train, cfg, val, device=ctx.device, tokenizer_meta=tok_meta)
+
+
+def _build_distill(j: _Job) -> PostTrainingAlgorithm:
+    from rl_project_b200.training.distill import DistillationAlgorithm, DistillConfig
+
+    m, p = j.manifest, j.params
+    tpath = p.pop("teacher_checkpoint", None)
+    if not tpath:
+        raise ConfigError("distill needs algorithm_params.teacher_checkpoint")
+    teacher, _, _ = load_model_from_checkpoint(tpath, j.ctx.device)
+    m.model.vocab_size = teacher.spec.vocab_size
+    student = build_model(m, j.ctx)
+    corpus = MemmapCorpus(m.data.path, "train", m.model.block_size)
+    return DistillationAlgorithm(student, teacher, corpus, _kw({"batch_size": m.trainer.batch_size, **p}, DistillConfig),
+                                 device=j.ctx.device)
+
+
+def _sft_records(j: _Job):
+    """(train, val) SFT records of the data section: the addition tasks, synthesis trajectories or JSONL."""
+    m, extra = j.manifest, j.extra
+    if str(m.data.path) == "synthetic:addition":
+        from rl_project_b200.data.synthetic import addition_tasks
+
+        recs = [SFTRecord(t["prompt"], t["response"]) for t in
+                addition_tasks(int(extra.get("n_tasks", 512)), seed=m.data.seed)]
+        return deterministic_split(recs, m.data.val_fraction, m.data.seed)
+    if m.data.kind == "trajectories":
+        from rl_project_b200.domains.synthesis import build_sft_records, filter_high_reward
+        from rl_project_b200.domains.synthesis.tabular_ppo import load_trajectories
+
+        rows = filter_high_reward(load_trajectories(m.data.path), float(extra.get("reward_threshold", 0.8)))
+        return build_sft_records(rows), []
+    recs = read_jsonl(m.data.path, SFTRecord, on_error=extra.get("on_error", "raise"))
+    return deterministic_split(recs, m.data.val_fraction, m.data.seed)
+
+
+def _build_sft(j: _Job) -> PostTrainingAlgorithm:
+    from rl_project_b200.training.sft import SFTAlgorithm, SFTConfig
+
+    m = j.manifest
+    policy = build_policy(m, j.ctx)
+    cfg = _kw({"batch_size": m.trainer.batch_size, "max_length": m.data.max_length, **j.params}, SFTConfig)
+    if str(m.data.path) == "synthetic":
+        from rl_project_b200.data.synthetic import SyntheticSFTSource
+
+        src = SyntheticSFTSource(m.model.vocab_size, m.model.block_size, cfg.batch_size,
+                                 prompt_fraction=float(j.extra.get("prompt_fraction", 0.25)), seed=m.data.seed,
+                                 rank=_rank())
+        return SFTAlgorithm(policy, src, cfg)
+    train, val = _sft_records(j)
+    ds = lambda recs: SupervisedDataset(recs, policy.tokenizer, cfg.max_length)  # noqa: E731
+    return SFTAlgorithm(policy, ds(train), cfg, ds(val) if val else None)
+
+
+def _preference_records(j: _Job):
+    m, extra = j.manifest, j.extra
+    if m.data.kind == "trajectories":
+        from rl_project_b200.domains.synthesis import build_preference_pairs
+        from rl_project_b200.domains.synthesis.preferences import pairs_to_records
+
+        rows, _ = _trajectory_split(m)
+        return pairs_to_records(build_preference_pairs(rows, int(extra.get("pairs_per_molecule", 20)),
+                                                       seed=m.data.seed)), []
+    recs = read_jsonl(m.data.path, PreferenceRecord, on_error=extra.get("on_error", "raise"))
+    return deterministic_split(recs, m.data.val_fraction, m.data.seed)
+
+
+def _build_preference(j: _Job) -> PostTrainingAlgorithm:
+    """DPO (a policy) or reward-model training (a sequence reward model) on preference pairs."""
+    m, p = j.manifest, j.params
+    train, val = _preference_records(j)
+    mp = j.extra.get("max_prompt_length", 384)
+    mr = j.extra.get("max_response_length", m.data.max_length)
+    if m.algorithm == "dpo":
+        from rl_project_b200.training.dpo import DPOAlgorithm, DPOConfig
+
+        policy = build_policy(m, j.ctx)
+        ds = lambda recs: PreferenceDataset(recs, policy.tokenizer, mp, mr)  # noqa: E731
+        return DPOAlgorithm(policy, ds(train), _kw({"batch_size": m.trainer.batch_size, **p}, DPOConfig),
+                            ds(val) if val else None)
+    from rl_project_b200.training.reward_model import RewardModelAlgorithm, RewardModelConfig
+
+    tok = build_tokenizer(m)
+    m.model.vocab_size = tok.vocab_size
+    rm = SequenceRewardModel(m.model, pooling=p.pop("pooling", "last")).to(j.ctx.device)
+    if m.checkpoint_path:
+        rm.backbone = load_model_from_checkpoint(m.checkpoint_path, j.ctx.device)[0]
+    ds = lambda recs: PreferenceDataset(recs, tok, mp, mr)  # noqa: E731
+    return RewardModelAlgorithm(rm, ds(train), _kw({"batch_size": m.trainer.batch_size, **p}, RewardModelConfig),
+                                ds(val) if val else None, tokenizer_meta=tok.metadata())
+
+
+def _rl_prompts(j: _Job, policy) -> Tuple[List[torch.Tensor], Optional[List[Dict[str, Any]]]]:
+    """Prompt token tensors (and their task dicts, when the data has answers) for the online algorithms."""
+    m, extra = j.manifest, j.extra
+    tasks: Optional[List[Dict[str, Any]]] = None
+    random_prompts_source = str(m.data.path) == "synthetic:random_prompts"
+    if m.data.kind == "trajectories":
+        from rl_project_b200.domains.synthesis import build_synthesis_prompt
+
+        rows, _ = _trajectory_split(m)
+        tasks = [dict(t, prompt=build_synthesis_prompt(t)) for t in rows]
+    elif m.data.kind == "verifiable" and not random_prompts_source:
+        tasks = [t.to_dict() for t in _tasks(m)]
+    if random_prompts_source:
+        from rl_project_b200.data.synthetic import random_prompts
+
+        # rollout replicas share one prompt pool (every rank draws the same prompts); otherwise per rank
+        shared = j.rollout is not None and j.rollout.replica_tp > 0
+        prompts = random_prompts(int(extra.get("n_prompts", 1024)), m.model.vocab_size, int(extra.get("min_prompt", 128)),
+                                 int(extra.get("max_prompt", 512)), seed=m.data.seed + (0 if shared else _rank()))
+    elif tasks:
+        prompts = [torch.tensor(policy.encode(t["prompt"]), dtype=torch.long) for t in tasks]
+    else:
+        src = m.data.path if Path(m.data.path).is_file() else None
+        prompts = [torch.tensor(ids, dtype=torch.long) for ids in load_prompts(src, policy.tokenizer, m.data.max_length)]
+    return prompts, tasks
+
+
+def _build_online(j: _Job) -> PostTrainingAlgorithm:
+    """PPO, GRPO (single-turn or agent) and DAPO."""
+    m, p, alg = j.manifest, j.params, j.manifest.algorithm
+    reward_cfg = m.reward or {"type": "rule", "name": "length", "target_length": 32}
+    reward = build_reward_provider(reward_cfg)
+    policy = build_policy(m, j.ctx, value_head=(alg == "ppo"))
+    prompts, tasks = _rl_prompts(j, policy)
+    if alg == "ppo":
+        from rl_project_b200.training.ppo import PPOAlgorithm, PPOConfig
+
+        built = PPOAlgorithm(policy, prompts, reward, _kw(p, PPOConfig), j.rollout, tasks=tasks)
+    elif alg == "grpo":
+        from rl_project_b200.training.grpo import GRPOAlgorithm, GRPOConfig
+
+        cfg = _kw(p, GRPOConfig)
+        built = (GRPOAlgorithm(policy, tasks or [], reward, cfg) if cfg.agent
+                 else GRPOAlgorithm(policy, prompts, reward, cfg, j.rollout, tasks=tasks))
+    else:
+        from rl_project_b200.training.dapo import DAPOAlgorithm, DAPOConfig
+
+        built = DAPOAlgorithm(policy, prompts, reward, _kw(p, DAPOConfig), j.rollout, tasks=tasks)
+    return _attach_orchestration(built, m, reward_cfg)
+
+
+def _build_allocation(j: _Job) -> PostTrainingAlgorithm:
+    from rl_project_b200.domains.allocation.ppo import build_allocation_ppo
+
+    return build_allocation_ppo(j.params, j.ctx.device)
+
+
+def _build_rlvr(j: _Job) -> PostTrainingAlgorithm:
+    from rl_project_b200.training.dapo import DAPOConfig
+    from rl_project_b200.training.grpo import GRPOConfig
+    from rl_project_b200.training.rlvr import RLVRConfig, build_rlvr_algorithm
+
+    p = j.params
+    policy = build_policy(j.manifest, j.ctx)
+    grpo = _kw(p.pop("grpo", {}) or {}, GRPOConfig)
+    dapo = _kw(p.pop("dapo", {}) or {}, DAPOConfig)
+    return build_rlvr_algorithm(policy, _tasks(j.manifest), _kw({**p, "grpo": grpo, "dapo": dapo}, RLVRConfig),
+                                j.rollout)
+
+
+_BUILDERS = {"pretrain": _build_pretrain, "distill": _build_distill, "sft": _build_sft, "dpo": _build_preference,
+             "reward_model": _build_preference, "ppo": _build_online, "grpo": _build_online, "dapo": _build_online,
+             "allocation_ppo": _build_allocation, "rlvr": _build_rlvr}
+
+
 def build_algorithm(manifest: ExperimentManifest, ctx: RunContext) -> PostTrainingAlgorithm:
-    alg = manifest.algorithm
-    p = dict(manifest.algorithm_params)
-    rp = p.pop("rollout", {}) or {}
-    rollout = _kw(rp, RolloutConfig) if rp else None
-    extra = manifest.data.extra
-    if alg == "pretrain":
-        from rl_project_b200.training.pretrain import PretrainAlgorithm, PretrainConfig
-
-        cfg = _kw({"batch_size": manifest.trainer.batch_size, "eval_batches": manifest.trainer.eval_batches, **p},
-                  PretrainConfig)
-        if _synthetic(manifest):
-            from rl_project_b200.data.synthetic import SyntheticPretrainSource
-
-            model = build_model(manifest, ctx)
-            src = SyntheticPretrainSource(manifest.model.vocab_size, manifest.model.block_size, cfg.batch_size,
-                                          seed=manifest.data.seed, rank=_rank())
-            return PretrainAlgorithm(model, src, cfg, None, device=ctx.device)
-        meta_file = Path(manifest.data.path) / "meta.pkl"
-        tok_meta = load_tokenizer_metadata(manifest.data.path) if meta_file.exists() else None
-        if tok_meta:
-            manifest.model.vocab_size = int(tok_meta["vocab_size"])
-        model = build_model(manifest, ctx)
-        train = MemmapCorpus(manifest.data.path, "train", manifest.model.block_size)
-        val = (MemmapCorpus(manifest.data.path, "val", manifest.model.block_size)
-               if (Path(manifest.data.path) / "val.bin").exists() else None)
-        return PretrainAlgorithm(model, train, cfg, val, device=ctx.device, tokenizer_meta=tok_meta)
-    if alg == "distill":
-        from rl_project_b200.training.distill import DistillationAlgorithm, DistillConfig
-
-        tpath = p.pop("teacher_checkpoint", None)
-        if not tpath:
-            raise ConfigError("distill needs algorithm_params.teacher_checkpoint")
-        teacher, _, _ = load_model_from_checkpoint(tpath, ctx.device)
-        manifest.model.vocab_size = teacher.spec.vocab_size
-        student = build_model(manifest, ctx)
-        corpus = MemmapCorpus(manifest.data.path, "train", manifest.model.block_size)
-        return DistillationAlgorithm(student, teacher, corpus, _kw({"batch_size": manifest.trainer.batch_size, **p},
-                                                                   DistillConfig), device=ctx.device)
-    if alg == "sft":
-        from rl_project_b200.training.sft import SFTAlgorithm, SFTConfig
-
-        policy = build_policy(manifest, ctx)
-        cfg = _kw({"batch_size": manifest.trainer.batch_size, "max_length": manifest.data.max_length, **p}, SFTConfig)
-        if str(manifest.data.path) == "synthetic":
-            from rl_project_b200.data.synthetic import SyntheticSFTSource
-
-            src = SyntheticSFTSource(manifest.model.vocab_size, manifest.model.block_size, cfg.batch_size,
-                                     prompt_fraction=float(extra.get("prompt_fraction", 0.25)),
-                                     seed=manifest.data.seed, rank=_rank())
-            return SFTAlgorithm(policy, src, cfg)
-        if str(manifest.data.path) == "synthetic:addition":
-            from rl_project_b200.data.synthetic import addition_tasks
-
-            recs = [SFTRecord(t["prompt"], t["response"]) for t in
-                    addition_tasks(int(extra.get("n_tasks", 512)), seed=manifest.data.seed)]
-            train, val = deterministic_split(recs, manifest.data.val_fraction, manifest.data.seed)
-        elif manifest.data.kind == "trajectories":
-            from rl_project_b200.domains.synthesis import build_sft_records, filter_high_reward
-            from rl_project_b200.domains.synthesis.tabular_ppo import load_trajectories
-
-            train = build_sft_records(filter_high_reward(load_trajectories(manifest.data.path),
-                                                         float(extra.get("reward_threshold", 0.8))))
-            val = []
-        else:
-            recs = read_jsonl(manifest.data.path, SFTRecord, on_error=extra.get("on_error", "raise"))
-            train, val = deterministic_split(recs, manifest.data.val_fraction, manifest.data.seed)
-        return SFTAlgorithm(policy, SupervisedDataset(train, policy.tokenizer, cfg.max_length), cfg,
-                            SupervisedDataset(val, policy.tokenizer, cfg.max_length) if val else None)
-    if alg in ("dpo", "reward_model"):
-        if manifest.data.kind == "trajectories":
-            from rl_project_b200.domains.synthesis import build_preference_pairs
-            from rl_project_b200.domains.synthesis.preferences import pairs_to_records
-
-            rows, _ = _trajectory_split(manifest)
-            train = pairs_to_records(build_preference_pairs(rows, int(extra.get("pairs_per_molecule", 20)),
-                                                            seed=manifest.data.seed))
-            val = []
-        else:
-            recs = read_jsonl(manifest.data.path, PreferenceRecord, on_error=extra.get("on_error", "raise"))
-            train, val = deterministic_split(recs, manifest.data.val_fraction, manifest.data.seed)
-        mp = extra.get("max_prompt_length", 384)
-        mr = extra.get("max_response_length", manifest.data.max_length)
-        if alg == "dpo":
-            from rl_project_b200.training.dpo import DPOAlgorithm, DPOConfig
-
-            policy = build_policy(manifest, ctx)
-            return DPOAlgorithm(policy, PreferenceDataset(train, policy.tokenizer, mp, mr),
-                                _kw({"batch_size": manifest.trainer.batch_size, **p}, DPOConfig),
-                                PreferenceDataset(val, policy.tokenizer, mp, mr) if val else None)
-        from rl_project_b200.training.reward_model import RewardModelAlgorithm, RewardModelConfig
-
-        tok = build_tokenizer(manifest)
-        manifest.model.vocab_size = tok.vocab_size
-        rm = SequenceRewardModel(manifest.model, pooling=p.pop("pooling", "last")).to(ctx.device)
-        if manifest.checkpoint_path:
-            rm.backbone = load_model_from_checkpoint(manifest.checkpoint_path, ctx.device)[0]
-        return RewardModelAlgorithm(rm, PreferenceDataset(train, tok, mp, mr),
-                                    _kw({"batch_size": manifest.trainer.batch_size, **p}, RewardModelConfig),
-                                    PreferenceDataset(val, tok, mp, mr) if val else None, tokenizer_meta=tok.metadata())
-    if alg in ("ppo", "grpo", "dapo"):
-        reward_cfg = manifest.reward or {"type": "rule", "name": "length", "target_length": 32}
-        reward = build_reward_provider(reward_cfg)
-        policy = build_policy(manifest, ctx, value_head=(alg == "ppo"))
-        tasks: Optional[List[Dict[str, Any]]] = None
-        if manifest.data.kind == "trajectories":
-            from rl_project_b200.domains.synthesis import build_synthesis_prompt
-
-            rows, _ = _trajectory_split(manifest)
-            tasks = [dict(t, prompt=build_synthesis_prompt(t)) for t in rows]
-        elif manifest.data.kind == "verifiable" and str(manifest.data.path) != "synthetic:random_prompts":
-            tasks = [t.to_dict() for t in _tasks(manifest)]
-        if str(manifest.data.path) == "synthetic:random_prompts":
-            from rl_project_b200.data.synthetic import random_prompts
-
-            # rollout replicas share one prompt pool (every rank draws the same prompts); otherwise per rank
-            shared = rollout is not None and rollout.replica_tp > 0
-            prompts = random_prompts(int(extra.get("n_prompts", 1024)), manifest.model.vocab_size,
-                                     int(extra.get("min_prompt", 128)), int(extra.get("max_prompt", 512)),
-                                     seed=manifest.data.seed + (0 if shared else _rank()))
-        elif tasks:
-            prompts = [torch.tensor(policy.encode(t["prompt"]), dtype=torch.long) for t in tasks]
-        else:
-            src = manifest.data.path if Path(manifest.data.path).is_file() else None
-            prompts = [torch.tensor(ids, dtype=torch.long)
-                       for ids in load_prompts(src, policy.tokenizer, manifest.data.max_length)]
-        if alg == "ppo":
-            from rl_project_b200.training.ppo import PPOAlgorithm, PPOConfig
-
-            built = PPOAlgorithm(policy, prompts, reward, _kw(p, PPOConfig), rollout, tasks=tasks)
-        elif alg == "grpo":
-            from rl_project_b200.training.grpo import GRPOAlgorithm, GRPOConfig
-
-            cfg = _kw(p, GRPOConfig)
-            built = (GRPOAlgorithm(policy, tasks or [], reward, cfg) if cfg.agent
-                     else GRPOAlgorithm(policy, prompts, reward, cfg, rollout, tasks=tasks))
-        else:
-            from rl_project_b200.training.dapo import DAPOAlgorithm, DAPOConfig
-
-            built = DAPOAlgorithm(policy, prompts, reward, _kw(p, DAPOConfig), rollout, tasks=tasks)
-        return _attach_orchestration(built, manifest, reward_cfg)
-    if alg == "allocation_ppo":
-        from rl_project_b200.domains.allocation.ppo import build_allocation_ppo
-
-        return build_allocation_ppo(p, ctx.device)
-    if alg == "rlvr":
-        from rl_project_b200.training.dapo import DAPOConfig
-        from rl_project_b200.training.grpo import GRPOConfig
-        from rl_project_b200.training.rlvr import RLVRConfig, build_rlvr_algorithm
-
-        policy = build_policy(manifest, ctx)
-        grpo = _kw(p.pop("grpo", {}) or {}, GRPOConfig)
-        dapo = _kw(p.pop("dapo", {}) or {}, DAPOConfig)
-        return build_rlvr_algorithm(policy, _tasks(manifest), _kw({**p, "grpo": grpo, "dapo": dapo}, RLVRConfig), rollout)
-    raise ConfigError(f"algorithm {alg!r} is not run through the step trainer; use the dedicated CLI command",
-                      hint="rlaif/constitutional/star/hill_climb/tabular_ppo have their own commands.")
+    build = _BUILDERS.get(manifest.algorithm)
+    if build is None:
+        raise ConfigError(f"algorithm {manifest.algorithm!r} is not run through the step trainer; use the dedicated "
+                          "CLI command",
+                          hint="rlaif/constitutional/star/hill_climb/tabular_ppo have their own commands.")
+    params = dict(manifest.algorithm_params)
+    rp = params.pop("rollout", {}) or {}
+    return build(_Job(manifest, ctx, params, _kw(rp, RolloutConfig) if rp else None, manifest.data.extra))
