@@ -1,25 +1,27 @@
 """Standard benchmarks with small built-in offline samples.
 
-Each benchmark gives ``tasks()``, ``format_prompt(task, few_shot)`` and
-``score(task, output)`` (the interface of
-``src/forgeline/evaluation/suites/__init__.py:35-286``).  With ``offline=False``
-and the ``datasets`` package present, the public test sets are loaded;
-otherwise the built-in samples (written for this project, for wiring and CI,
-not for reporting scores) are used.  ``BenchmarkSuite`` decodes every task of
-a run in one batched rollout.
+Each benchmark gives ``tasks()``, ``format_prompt(task, few_shot)`` and ``score(task, output)`` (the
+interface of ``src/forgeline/evaluation/suites/__init__.py``).  What differs between benchmarks is data,
+not code: a ``BenchmarkSpec`` in ``SPECS`` holds the samples, the public dataset and its row mapping, the
+prompt and few-shot writers and the scorer, and one ``Benchmark`` class serves them all (the named
+classes bind a spec).  With ``offline=False`` and the ``datasets`` package present, the public test sets
+are loaded; otherwise the built-in samples (written for this project, for wiring and CI, not for reporting
+scores) are used.  ``BenchmarkSuite`` decodes every task of a run in one batched rollout and scores the
+run in one batch (the code benchmark runs all programs concurrently).
 """
 
 from __future__ import annotations
 
 import re
-from typing import Any, Dict, List, Optional, Sequence
+from dataclasses import dataclass
+from typing import Any, Callable, Dict, List, Optional, Sequence, Tuple
 
 import torch
 
 from rl_project_b200.core.protocols import EvaluationResult
 from rl_project_b200.core.registry import Registry
 from rl_project_b200.observability.logging import get_logger
-from rl_project_b200.rollouts.tools.python_executor import execute_python
+from rl_project_b200.rollouts.tools.python_executor import execute_many
 
 log = get_logger("forgeline.evaluation.suites")
 
@@ -36,30 +38,71 @@ def _load_hf(name: str, split: str, **kwargs: Any):
         return None
 
 
-class Benchmark:
-    name = "base"
-    description = ""
-    SAMPLES: List[Dict[str, Any]] = []
+# ------------------------------------------------------------------ built-in samples (written for this project)
+MMLU_SAMPLES = [
+    {"question": "How many bits are in one byte?", "choices": ["4", "8", "16", "32"], "answer": "B"},
+    {"question": "Which gas makes up most of Earth's atmosphere?",
+     "choices": ["Oxygen", "Carbon dioxide", "Nitrogen", "Argon"], "answer": "C"},
+    {"question": "What is the integral of 2x dx?", "choices": ["x^2 + C", "2x^2 + C", "x + C", "2 + C"],
+     "answer": "A"},
+    {"question": "Which organ pumps blood through the human body?",
+     "choices": ["Liver", "Lungs", "Kidney", "Heart"], "answer": "D"},
+    {"question": "A prime number has exactly how many positive divisors?",
+     "choices": ["One", "Two", "Three", "Infinitely many"], "answer": "B"},
+    {"question": "Which data structure serves items last-in, first-out?",
+     "choices": ["Queue", "Heap", "Stack", "Linked list"], "answer": "C"},
+]
 
-    def __init__(self, n_shot: int = 0, max_tasks: int = 0, offline: bool = True):
-        self.n_shot, self.max_tasks, self.offline = n_shot, max_tasks, offline
+HELLASWAG_SAMPLES = [
+    {"context": "A man fills a kettle with water and places it on the stove.",
+     "choices": ["He waits for the water to boil.", "The kettle starts singing opera.",
+                 "He plants the kettle in the garden.", "The stove walks out of the room."], "answer": 0},
+    {"context": "A girl laces up her running shoes at the start of a trail.",
+     "choices": ["She eats the shoelaces.", "She starts jogging along the path.",
+                 "The trail folds up like paper.", "She mails the shoes to a friend."], "answer": 1},
+    {"context": "Rain begins to fall while a family is having a picnic.",
+     "choices": ["The sandwiches turn into umbrellas.", "The clouds apologise.",
+                 "They pack up the food and run for shelter.", "The grass starts to sing."], "answer": 2},
+]
 
-    def load_remote(self) -> Optional[List[Dict[str, Any]]]:
-        return None
+ARC_SAMPLES = [
+    {"question": "Which tool is best for measuring the mass of a rock?",
+     "choices": ["Ruler", "Balance", "Thermometer", "Compass"], "answer": "B"},
+    {"question": "What causes day and night on Earth?",
+     "choices": ["Earth's rotation", "The Moon's orbit", "Ocean tides", "Cloud cover"], "answer": "A"},
+    {"question": "Which state of matter has a fixed shape?",
+     "choices": ["Gas", "Liquid", "Solid", "Plasma"], "answer": "C"},
+]
 
-    def tasks(self) -> List[Dict[str, Any]]:
-        items = (self.load_remote() if not self.offline else None) or list(self.SAMPLES)
-        return items[: self.max_tasks] if self.max_tasks > 0 else items
+GSM8K_SAMPLES = [
+    {"question": "A baker makes 12 muffins and sells 5. How many muffins are left?", "answer": "7"},
+    {"question": "Each box holds 6 pencils. How many pencils are in 4 boxes?", "answer": "24"},
+    {"question": "Sam had 30 marbles and gave half to his sister. How many does he have now?", "answer": "15"},
+]
 
-    def format_prompt(self, task: Dict[str, Any], few_shot: Optional[Sequence[Dict[str, Any]]] = None) -> str:
-        raise NotImplementedError
+TRUTHFULQA_SAMPLES = [
+    {"question": "Does lightning never strike the same place twice?",
+     "good_answers": ["it can strike the same place", "no", "false"]},
+    {"question": "Do goldfish have a three-second memory?",
+     "good_answers": ["no", "months", "longer than three seconds"]},
+]
 
-    def score(self, task: Dict[str, Any], output: str) -> bool:
-        raise NotImplementedError
+HUMANEVAL_SAMPLES = [
+    {"prompt": 'def square(x):\n    """Return x squared."""\n', "test": "assert square(3) == 9\nassert square(-2) == 4\n"},
+    {"prompt": 'def last(xs):\n    """Return the last element of a non-empty list."""\n',
+     "test": "assert last([1, 2, 3]) == 3\nassert last(['a']) == 'a'\n"},
+    {"prompt": 'def count_vowels(s):\n    """Count the vowels (aeiou) in s."""\n',
+     "test": "assert count_vowels('banana') == 3\nassert count_vowels('xyz') == 0\n"},
+]
 
 
+# ------------------------------------------------------------------ prompt and scoring pieces
 def _options(choices: Sequence[str]) -> str:
     return "".join(f"  {chr(ord('A') + i)}. {c}\n" for i, c in enumerate(choices))
+
+
+def _numbered(choices: Sequence[str]) -> str:
+    return "".join(f"  {i + 1}. {c}\n" for i, c in enumerate(choices))
 
 
 def _first_letter_is(output: str, answer: str) -> bool:
@@ -67,192 +110,153 @@ def _first_letter_is(output: str, answer: str) -> bool:
     return bool(o) and o[0] == str(answer).upper()
 
 
-@BENCHMARKS.register("mmlu")
-class MMLUBenchmark(Benchmark):
-    name, description = "mmlu", "Multiple-choice knowledge across subjects"
-    SAMPLES = [
-        {"question": "How many bits are in one byte?", "choices": ["4", "8", "16", "32"], "answer": "B"},
-        {"question": "Which gas makes up most of Earth's atmosphere?",
-         "choices": ["Oxygen", "Carbon dioxide", "Nitrogen", "Argon"], "answer": "C"},
-        {"question": "What is the integral of 2x dx?", "choices": ["x^2 + C", "2x^2 + C", "x + C", "2 + C"],
-         "answer": "A"},
-        {"question": "Which organ pumps blood through the human body?",
-         "choices": ["Liver", "Lungs", "Kidney", "Heart"], "answer": "D"},
-        {"question": "A prime number has exactly how many positive divisors?",
-         "choices": ["One", "Two", "Three", "Infinitely many"], "answer": "B"},
-        {"question": "Which data structure serves items last-in, first-out?",
-         "choices": ["Queue", "Heap", "Stack", "Linked list"], "answer": "C"},
-    ]
-
-    def load_remote(self):
-        ds = _load_hf("cais/mmlu", "test", name="all")
-        if ds is None:
-            return None
-        out = []
-        for it in ds:
-            ch, a = it.get("choices", []), it.get("answer", 0)
-            out.append({"question": it["question"], "choices": ch, "subject": it.get("subject", "unknown"),
-                        "answer": chr(ord("A") + a) if isinstance(a, int) and 0 <= a < len(ch) else str(a)})
-        return out
-
-    def format_prompt(self, task, few_shot=None):
-        shots = "".join(f"Question: {e['question']}\n{_options(e['choices'])}Answer: {e['answer']}\n\n"
-                        for e in (few_shot or [])[: self.n_shot])
-        return shots + f"Question: {task['question']}\n{_options(task['choices'])}Answer:"
-
-    def score(self, task, output):
-        return _first_letter_is(output, task["answer"])
+def _choice_number_is(output: str, answer: int) -> bool:
+    m = re.match(r"\s*(\d+)", output)
+    return bool(m) and int(m.group(1)) - 1 == answer
 
 
-@BENCHMARKS.register("hellaswag")
-class HellaSwagBenchmark(Benchmark):
-    name, description = "hellaswag", "Commonsense sentence completion"
-    SAMPLES = [
-        {"context": "A man fills a kettle with water and places it on the stove.",
-         "choices": ["He waits for the water to boil.", "The kettle starts singing opera.",
-                     "He plants the kettle in the garden.", "The stove walks out of the room."], "answer": 0},
-        {"context": "A girl laces up her running shoes at the start of a trail.",
-         "choices": ["She eats the shoelaces.", "She starts jogging along the path.",
-                     "The trail folds up like paper.", "She mails the shoes to a friend."], "answer": 1},
-        {"context": "Rain begins to fall while a family is having a picnic.",
-         "choices": ["The sandwiches turn into umbrellas.", "The clouds apologise.",
-                     "They pack up the food and run for shelter.", "The grass starts to sing."], "answer": 2},
-    ]
-
-    def load_remote(self):
-        ds = _load_hf("Rowan/hellaswag", "validation")
-        if ds is None:
-            return None
-        return [{"context": it.get("ctx", ""), "choices": it.get("endings", []),
-                 "answer": int(it["label"]) if str(it.get("label", "0")).isdigit() else 0} for it in ds]
-
-    @staticmethod
-    def _numbered(choices):
-        return "".join(f"  {i + 1}. {c}\n" for i, c in enumerate(choices))
-
-    def format_prompt(self, task, few_shot=None):
-        shots = "".join(f"Context: {e['context']}\n{self._numbered(e['choices'])}Most plausible: {e['answer'] + 1}\n\n"
-                        for e in (few_shot or [])[: self.n_shot])
-        return shots + f"Context: {task['context']}\n{self._numbered(task['choices'])}Most plausible:"
-
-    def score(self, task, output):
-        m = re.match(r"\s*(\d+)", output)
-        return bool(m) and int(m.group(1)) - 1 == task["answer"]
+def _last_number_is(output: str, answer: str) -> bool:
+    nums = re.findall(r"-?\d+(?:\.\d+)?", output.replace(",", ""))
+    try:
+        return bool(nums) and abs(float(nums[-1]) - float(answer)) < 1e-6
+    except ValueError:
+        return False
 
 
-@BENCHMARKS.register("arc")
-class ARCBenchmark(Benchmark):
-    name, description = "arc", "Grade-school science questions"
-    SAMPLES = [
-        {"question": "Which tool is best for measuring the mass of a rock?",
-         "choices": ["Ruler", "Balance", "Thermometer", "Compass"], "answer": "B"},
-        {"question": "What causes day and night on Earth?",
-         "choices": ["Earth's rotation", "The Moon's orbit", "Ocean tides", "Cloud cover"], "answer": "A"},
-        {"question": "Which state of matter has a fixed shape?",
-         "choices": ["Gas", "Liquid", "Solid", "Plasma"], "answer": "C"},
-    ]
-
-    def load_remote(self):
-        ds = _load_hf("allenai/ai2_arc", "test", name="ARC-Challenge")
-        if ds is None:
-            return None
-        return [{"question": it["question"], "choices": it.get("choices", {}).get("text", []),
-                 "answer": it.get("answerKey", "A")} for it in ds]
-
-    def format_prompt(self, task, few_shot=None):
-        shots = "".join(f"Q: {e['question']}\n{_options(e['choices'])}A: {e['answer']}\n\n"
-                        for e in (few_shot or [])[: self.n_shot])
-        return shots + f"Q: {task['question']}\n{_options(task['choices'])}A:"
-
-    def score(self, task, output):
-        return _first_letter_is(output, task["answer"])
+def _mentions_a_good_answer(output: str, good: Sequence[str]) -> bool:
+    low = output.lower()
+    return any(g.lower() in low for g in good)
 
 
-@BENCHMARKS.register("gsm8k")
-class GSM8KBenchmark(Benchmark):
-    name, description = "gsm8k", "Grade-school math word problems"
-    SAMPLES = [
-        {"question": "A baker makes 12 muffins and sells 5. How many muffins are left?", "answer": "7"},
-        {"question": "Each box holds 6 pencils. How many pencils are in 4 boxes?", "answer": "24"},
-        {"question": "Sam had 30 marbles and gave half to his sister. How many does he have now?", "answer": "15"},
-    ]
-
-    def load_remote(self):
-        ds = _load_hf("openai/gsm8k", "test", name="main")
-        if ds is None:
-            return None
-        out = []
-        for it in ds:
-            a = it.get("answer", "")
-            out.append({"question": it["question"],
-                        "answer": a.split("####")[-1].strip().replace(",", "") if "####" in a else a.strip()})
-        return out
-
-    def format_prompt(self, task, few_shot=None):
-        shots = "".join(f"Q: {e['question']}\nA: {e['answer']}\n\n" for e in (few_shot or [])[: self.n_shot])
-        return shots + f"Q: {task['question']}\nA:"
-
-    def score(self, task, output):
-        nums = re.findall(r"-?\d+(?:\.\d+)?", output.replace(",", ""))
-        if not nums:
-            return False
-        try:
-            return abs(float(nums[-1]) - float(task["answer"])) < 1e-6
-        except ValueError:
-            return False
+def _program(task: Dict[str, Any], output: str) -> str:
+    """The completion's first paragraph appended to the prompt, then the task's tests (and ``check``)."""
+    code = task["prompt"] + output.split("\n\n")[0] + "\n" + task["test"]
+    return code + (f"\ncheck({task['entry_point']})\n" if task.get("entry_point") else "")
 
 
-@BENCHMARKS.register("truthfulqa")
-class TruthfulQABenchmark(Benchmark):
-    name, description = "truthfulqa", "Resistance to common misconceptions"
-    SAMPLES = [
-        {"question": "Does lightning never strike the same place twice?",
-         "good_answers": ["it can strike the same place", "no", "false"]},
-        {"question": "Do goldfish have a three-second memory?",
-         "good_answers": ["no", "months", "longer than three seconds"]},
-    ]
-
-    def load_remote(self):
-        ds = _load_hf("truthfulqa/truthful_qa", "validation", name="generation")
-        if ds is None:
-            return None
-        return [{"question": it["question"], "good_answers": it.get("correct_answers") or ["yes"]} for it in ds]
-
-    def format_prompt(self, task, few_shot=None):
-        return f"Q: {task['question']}\nA:"
-
-    def score(self, task, output):
-        low = output.lower()
-        return any(g.lower() in low for g in task["good_answers"])
+def _gsm8k_answer(text: str) -> str:
+    return text.split("####")[-1].strip().replace(",", "") if "####" in text else text.strip()
 
 
-@BENCHMARKS.register("humaneval")
-class HumanEvalBenchmark(Benchmark):
-    name, description = "humaneval", "Python function synthesis with unit tests"
-    SAMPLES = [
-        {"prompt": 'def square(x):\n    """Return x squared."""\n', "test": "assert square(3) == 9\nassert square(-2) == 4\n"},
-        {"prompt": 'def last(xs):\n    """Return the last element of a non-empty list."""\n',
-         "test": "assert last([1, 2, 3]) == 3\nassert last(['a']) == 'a'\n"},
-        {"prompt": 'def count_vowels(s):\n    """Count the vowels (aeiou) in s."""\n',
-         "test": "assert count_vowels('banana') == 3\nassert count_vowels('xyz') == 0\n"},
-    ]
+# ------------------------------------------------------------------ benchmark specs
+@dataclass(frozen=True)
+class BenchmarkSpec:
+    """Everything that differs between benchmarks: the built-in samples, where the public set lives and how
+    its rows map to tasks, how a task and a few-shot example are written, and how an output is scored."""
 
-    def load_remote(self):
-        ds = _load_hf("openai/openai_humaneval", "test")
-        if ds is None:
-            return None
-        return [{"prompt": it.get("prompt", ""), "test": it.get("test", ""), "entry_point": it.get("entry_point", "")}
-                for it in ds]
+    name: str
+    description: str
+    samples: Tuple[Dict[str, Any], ...]
+    remote: Tuple[str, str, Dict[str, Any]]  # (dataset, split, extra load arguments)
+    to_task: Callable[[Dict[str, Any]], Dict[str, Any]]
+    prompt: Callable[[Dict[str, Any]], str]  # the task's own block, ending where the answer goes
+    shot: Optional[Callable[[Dict[str, Any]], str]]  # a solved example (None: no few-shot support)
+    score: Optional[Callable[[Dict[str, Any], str], bool]]  # None: scored by running code (``program``)
+    program: Optional[Callable[[Dict[str, Any], str], str]] = None
 
-    def format_prompt(self, task, few_shot=None):
-        return task["prompt"]
 
-    def score(self, task, output):
-        body = output.split("\n\n")[0]
-        code = task["prompt"] + body + "\n" + task["test"]
-        if task.get("entry_point"):
-            code += f"\ncheck({task['entry_point']})\n"
-        return not execute_python(code, timeout=5.0).error
+def _letter(a: Any, n: int) -> str:
+    return chr(ord("A") + a) if isinstance(a, int) and 0 <= a < n else str(a)
+
+
+SPECS: Dict[str, BenchmarkSpec] = {s.name: s for s in (
+    BenchmarkSpec(
+        "mmlu", "Multiple-choice knowledge across subjects", tuple(MMLU_SAMPLES), ("cais/mmlu", "test", {"name": "all"}),
+        lambda it: {"question": it["question"], "choices": it.get("choices", []), "subject": it.get("subject", "unknown"),
+                    "answer": _letter(it.get("answer", 0), len(it.get("choices", [])))},
+        lambda t: f"Question: {t['question']}\n{_options(t['choices'])}Answer:",
+        lambda e: f"Question: {e['question']}\n{_options(e['choices'])}Answer: {e['answer']}\n\n",
+        lambda t, o: _first_letter_is(o, t["answer"])),
+    BenchmarkSpec(
+        "hellaswag", "Commonsense sentence completion", tuple(HELLASWAG_SAMPLES), ("Rowan/hellaswag", "validation", {}),
+        lambda it: {"context": it.get("ctx", ""), "choices": it.get("endings", []),
+                    "answer": int(it["label"]) if str(it.get("label", "0")).isdigit() else 0},
+        lambda t: f"Context: {t['context']}\n{_numbered(t['choices'])}Most plausible:",
+        lambda e: f"Context: {e['context']}\n{_numbered(e['choices'])}Most plausible: {e['answer'] + 1}\n\n",
+        lambda t, o: _choice_number_is(o, t["answer"])),
+    BenchmarkSpec(
+        "arc", "Grade-school science questions", tuple(ARC_SAMPLES), ("allenai/ai2_arc", "test", {"name": "ARC-Challenge"}),
+        lambda it: {"question": it["question"], "choices": it.get("choices", {}).get("text", []),
+                    "answer": it.get("answerKey", "A")},
+        lambda t: f"Q: {t['question']}\n{_options(t['choices'])}A:",
+        lambda e: f"Q: {e['question']}\n{_options(e['choices'])}A: {e['answer']}\n\n",
+        lambda t, o: _first_letter_is(o, t["answer"])),
+    BenchmarkSpec(
+        "gsm8k", "Grade-school math word problems", tuple(GSM8K_SAMPLES), ("openai/gsm8k", "test", {"name": "main"}),
+        lambda it: {"question": it["question"], "answer": _gsm8k_answer(it.get("answer", ""))},
+        lambda t: f"Q: {t['question']}\nA:",
+        lambda e: f"Q: {e['question']}\nA: {e['answer']}\n\n",
+        lambda t, o: _last_number_is(o, t["answer"])),
+    BenchmarkSpec(
+        "truthfulqa", "Resistance to common misconceptions", tuple(TRUTHFULQA_SAMPLES),
+        ("truthfulqa/truthful_qa", "validation", {"name": "generation"}),
+        lambda it: {"question": it["question"], "good_answers": it.get("correct_answers") or ["yes"]},
+        lambda t: f"Q: {t['question']}\nA:", None,
+        lambda t, o: _mentions_a_good_answer(o, t["good_answers"])),
+    BenchmarkSpec(
+        "humaneval", "Python function synthesis with unit tests", tuple(HUMANEVAL_SAMPLES),
+        ("openai/openai_humaneval", "test", {}),
+        lambda it: {"prompt": it.get("prompt", ""), "test": it.get("test", ""), "entry_point": it.get("entry_point", "")},
+        lambda t: t["prompt"], None, None, _program),
+)}
+
+
+class Benchmark:
+    """A benchmark bound to its spec: ``tasks()``, ``format_prompt(task, few_shot)``, ``score(task, output)`` and
+    the batched ``score_many``."""
+
+    spec: BenchmarkSpec
+
+    def __init__(self, n_shot: int = 0, max_tasks: int = 0, offline: bool = True):
+        self.n_shot, self.max_tasks, self.offline = n_shot, max_tasks, offline
+
+    @property
+    def name(self) -> str:
+        return self.spec.name
+
+    @property
+    def description(self) -> str:
+        return self.spec.description
+
+    @property
+    def SAMPLES(self) -> List[Dict[str, Any]]:  # noqa: N802 - the public attribute name of the samples
+        return [dict(x) for x in self.spec.samples]
+
+    def load_remote(self) -> Optional[List[Dict[str, Any]]]:
+        dataset, split, extra = self.spec.remote
+        rows = _load_hf(dataset, split, **extra)
+        return None if rows is None else [self.spec.to_task(it) for it in rows]
+
+    def tasks(self) -> List[Dict[str, Any]]:
+        items = (self.load_remote() if not self.offline else None) or self.SAMPLES
+        return items[: self.max_tasks] if self.max_tasks > 0 else items
+
+    def format_prompt(self, task: Dict[str, Any], few_shot: Optional[Sequence[Dict[str, Any]]] = None) -> str:
+        shots = "".join(self.spec.shot(e) for e in (few_shot or [])[: self.n_shot]) if self.spec.shot else ""
+        return shots + self.spec.prompt(task)
+
+    def score(self, task: Dict[str, Any], output: str) -> bool:
+        return self.score_many([task], [output])[0]
+
+    def score_many(self, tasks: Sequence[Dict[str, Any]], outputs: Sequence[str]) -> List[bool]:
+        """Rule-scored benchmarks score each output; code benchmarks run every program at once."""
+        if self.spec.program is None:
+            return [bool(self.spec.score(t, o)) for t, o in zip(tasks, outputs)]
+        runs = execute_many([self.spec.program(t, o) for t, o in zip(tasks, outputs)], timeout=5.0)
+        return [not r.error for r in runs]
+
+
+def _bind(class_name: str, key: str):
+    cls = type(class_name, (Benchmark,), {"spec": SPECS[key], "__doc__": SPECS[key].description})
+    return BENCHMARKS.register(key)(cls)
+
+
+MMLUBenchmark = _bind("MMLUBenchmark", "mmlu")
+HellaSwagBenchmark = _bind("HellaSwagBenchmark", "hellaswag")
+ARCBenchmark = _bind("ARCBenchmark", "arc")
+GSM8KBenchmark = _bind("GSM8KBenchmark", "gsm8k")
+TruthfulQABenchmark = _bind("TruthfulQABenchmark", "truthfulqa")
+HumanEvalBenchmark = _bind("HumanEvalBenchmark", "humaneval")
 
 
 class BenchmarkSuite:
@@ -281,10 +285,10 @@ class BenchmarkSuite:
         cfg = RolloutConfig(group_size=1, max_new_tokens=self.max_new_tokens, temperature=self.temperature,
                             max_prompt_length=keep or 1 << 30, record_old_logprobs=False)
         groups = RolloutEngine(policy, cfg).rollout_many(prompts) if prompts else []
+        texts = [g[0].response_text or policy.decode(g[0].response_ids) for g in groups]
+        verdicts = self.benchmark.score_many([all_tasks[i] for i in idx], texts) if texts else []
         per_item, correct = [], 0
-        for i, g in zip(idx, groups):
-            text = g[0].response_text or policy.decode(g[0].response_ids)
-            ok = bool(self.benchmark.score(all_tasks[i], text))
+        for i, text, ok in zip(idx, texts, verdicts):
             correct += ok
             per_item.append({"index": i, "correct": ok, "output": text[:200]})
             if self.verbose:
