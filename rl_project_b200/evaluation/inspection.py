@@ -11,16 +11,25 @@ import torch
 
 
 def weight_statistics(model: torch.nn.Module, bins: int = 20) -> List[Dict[str, Any]]:
-    stats = []
-    for name, p in model.named_parameters():
+    """Per parameter: shape, size, mean, std, min, max, mean |w|, L2 norm and a ``bins``-bucket histogram.
+    The scalar statistics of every parameter are computed on its device and fetched in one transfer; the
+    histograms are built on the host."""
+    named = list(model.named_parameters())
+    if not named:
+        return []
+    rows = []
+    for _, p in named:
         d = p.detach().float()
-        lo, hi = float(d.min()), float(d.max())
-        counts = torch.histc(d.flatten().cpu(), bins=bins, min=lo, max=hi if hi > lo else lo + 1e-12)
-        stats.append({"name": name, "shape": list(p.shape), "numel": p.numel(), "mean": float(d.mean()),
-                      "std": float(d.std()) if d.numel() > 1 else 0.0, "min": lo, "max": hi,
-                      "abs_mean": float(d.abs().mean()), "norm": float(d.norm()),
-                      "histogram": {"counts": counts.tolist(),
-                                    "edges": [lo + i * (hi - lo) / bins for i in range(bins + 1)]}})
+        std = d.std() if d.numel() > 1 else torch.zeros((), device=d.device)
+        rows.append(torch.stack([d.mean(), std, d.min(), d.max(), d.abs().mean(), d.norm()]))
+    same_device = len({r.device for r in rows}) == 1
+    table = (torch.stack(rows).cpu() if same_device else torch.stack([r.cpu() for r in rows])).tolist()
+    stats = []
+    for (name, p), (mean, std, lo, hi, abs_mean, norm) in zip(named, table):
+        counts = torch.histc(p.detach().float().flatten().cpu(), bins=bins, min=lo, max=hi if hi > lo else lo + 1e-12)
+        stats.append({"name": name, "shape": list(p.shape), "numel": p.numel(), "mean": mean, "std": std, "min": lo,
+                      "max": hi, "abs_mean": abs_mean, "norm": norm,
+                      "histogram": {"counts": counts.tolist(), "edges": [lo + i * (hi - lo) / bins for i in range(bins + 1)]}})
     return stats
 
 
