@@ -65,7 +65,7 @@ def parse_args():
                     help="CTAs of each fused reduce-scatter that overlaps backward")
     ap.add_argument("--fused-multicast", choices=["off", "on", "symm"], default="off",
                     help="fused reduce-scatter transport: CUDA IPC peer loads (off) or NVLink multicast (on)")
-    ap.add_argument("--gemm", choices=["tcgen05", "cublas", "tuned"], default="cublas",
+    ap.add_argument("--gemm", choices=["tcgen05", "cublas", "tuned", "hybrid"], default="cublas",
                     help="dense linear layers and LM head: this library's 2-SM tcgen05 GEMM, cuBLAS, or per shape "
                          "the fastest of the two (timed on the first call of each shape)")
     ap.add_argument("--attn", choices=["sdpa", "tcgen05"], default="sdpa",

@@ -12,7 +12,8 @@ without transposing anything:
 (tcgen05 once the numerics self-check on the first call passed) or ``tuned``
 (per product shape, the fastest of the 2-SM kernel with 256 x 256 tiles, with
 256 x 512 tiles, and cuBLAS -- timed once with CUDA events on the first call of
-that shape; accumulating and graph-captured calls keep the per-shape default).
+that shape; accumulating and graph-captured calls keep the per-shape default) or
+``hybrid`` (forward products on the 2-SM kernel, gradient products on cuBLAS).
 ``RLB_GEMM_KERNEL`` picks the kernel: ``2sm`` (default; CTA pairs issuing
 ``tcgen05.mma.cta_group::2`` on 256 x 256 tiles, TMA-store epilogue) or
 ``1sm`` (one CTA per 128 x 256 tile, register-to-global epilogue; the base of
@@ -212,6 +213,8 @@ class _Linear(torch.autograd.Function):
     def backward(ctx, dy):
         x2, w = ctx.saved_tensors
         dy = _dense(dy)
+        if not backward_own():  # "hybrid": the gradient products go to cuBLAS
+            return (dy @ w if ctx.needs_input_grad[0] else None, dy.t() @ x2 if ctx.needs_input_grad[1] else None)
         dx = gemm_nn(dy, w) if ctx.needs_input_grad[0] else None
         dw = gemm_tn(dy, x2) if ctx.needs_input_grad[1] else None
         return dx, dw
@@ -230,7 +233,13 @@ def _self_check(device: torch.device) -> bool:
 
 
 def enabled() -> bool:
-    return available() and _MODE in ("tcgen05", "auto", "tuned")
+    return available() and _MODE in ("tcgen05", "auto", "tuned", "hybrid")
+
+
+def backward_own() -> bool:
+    """Whether the input- and weight-gradient products of the own linear layers run the own kernel too
+    (every enabled mode except ``hybrid``, which keeps the forward on it and sends the gradients to cuBLAS)."""
+    return enabled() and _MODE != "hybrid"
 
 
 def supported(a: torch.Tensor, b: torch.Tensor) -> bool:
@@ -238,7 +247,7 @@ def supported(a: torch.Tensor, b: torch.Tensor) -> bool:
         return False
     if not _shape_ok(a, b):
         return False
-    return _MODE in ("tcgen05", "tuned") or _self_check(a.device)
+    return _MODE in ("tcgen05", "tuned", "hybrid") or _self_check(a.device)
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:

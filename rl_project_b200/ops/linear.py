@@ -32,9 +32,15 @@ def matmul_nt(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return a @ b.t()
 
 
+def _own_grad(a: torch.Tensor, b: torch.Tensor) -> bool:
+    from rl_project_b200.ops import gemm
+
+    return _own(a, b) and gemm.backward_own()
+
+
 def matmul_nn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """``a [M, K] @ b [K, N]`` (b read as stored)."""
-    if _own(a, b):
+    """``a [M, K] @ b [K, N]`` (b read as stored; a gradient product of the LM head)."""
+    if _own_grad(a, b):
         from rl_project_b200.ops import gemm
 
         return gemm.gemm_nn(a, b)
@@ -42,8 +48,8 @@ def matmul_nn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
 
 
 def matmul_tn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """``a [K, M]^T @ b [K, N]`` (both read as stored)."""
-    if _own(a, b):
+    """``a [K, M]^T @ b [K, N]`` (both read as stored; a gradient product of the LM head)."""
+    if _own_grad(a, b):
         from rl_project_b200.ops import gemm
 
         return gemm.gemm_tn(a, b)
