@@ -121,13 +121,15 @@ def test_tma_launchers_work_from_a_fresh_thread():
     assert _rel(out["y"], ref) < 8e-3
 
 
-def test_tuned_mode_linear_matches_fp32():
-    """``tuned`` mode (per-shape choice among the 2-SM kernel's tile shapes and cuBLAS) gives the fp32 product
-    in every layout of a linear layer, and records a choice for each shape it timed."""
+@pytest.mark.parametrize("mode", ["tuned", "hybrid"])
+def test_tuned_and_hybrid_modes_linear_match_fp32(mode):
+    """``tuned`` (per-shape choice among the 2-SM kernel's tile shapes and cuBLAS) and ``hybrid`` (own forward,
+    cuBLAS gradients) give the fp32 product in every layout of a linear layer; ``tuned`` records a choice for
+    each shape it timed."""
     from rl_project_b200.ops import gemm
 
     old = gemm._MODE
-    gemm._MODE = "tuned"
+    gemm._MODE = mode
     try:
         x = torch.randn(1024, 512, device="cuda").to(BF).requires_grad_()
         w = (0.05 * torch.randn(1536, 512, device="cuda")).to(BF).requires_grad_()
@@ -140,8 +142,9 @@ def test_tuned_mode_linear_matches_fp32():
         yr = xr @ wr.t()
         yr.backward(gy.float())
         assert _rel(y, yr) < 8e-3 and _rel(x.grad, xr.grad) < 1e-2 and _rel(w.grad, wr.grad) < 1e-2
-        picks = gemm.tuned_choices()
-        assert {(k[0], k[1]) for k in picks} >= {(0, 0), (0, 1), (1, 1)}
-        assert set(picks.values()) <= {"own1", "own2", "cublas"}
+        if mode == "tuned":
+            picks = gemm.tuned_choices()
+            assert {(k[0], k[1]) for k in picks} >= {(0, 0), (0, 1), (1, 1)}
+            assert set(picks.values()) <= {"own1", "own2", "cublas"}
     finally:
         gemm._MODE = old
