@@ -125,3 +125,36 @@ def test_rope_table_stays_on_the_host_under_a_default_device():
     assert table.inv_freq.device.type == "cpu" and table._cos.device.type == "cpu"
     cos, sin = table.tables(64, torch.device("cpu"))  # grows the table outside the context
     assert cos.shape == (64, 32) and torch.isfinite(sin).all()
+
+
+def test_nsa_shared_score_fine_branches_equal_per_branch_oracle():
+    """The fused selected + window branches equal computing each branch on its own (gathered top-k values,
+    separate window scores), combined with the same gates."""
+    import torch.nn.functional as F
+
+    from rl_project_b200.models.attention.sparse import NativeSparseAttention
+
+    torch.manual_seed(0)
+    spec = model_spec_from_preset("tiny", vocab_size=40, block_size=32, use_nsa=True, nsa_block_size=4,
+                                  nsa_top_k=3, nsa_window_size=5)
+    attn = NativeSparseAttention(spec).eval()
+    x = torch.randn(2, 11, spec.n_embd)
+    got, _ = attn(x)
+    B, T, C = x.shape
+    H, D = attn.n_head, attn.head_dim
+    heads = lambda t: t.view(B, T, H, D).transpose(1, 2)  # noqa: E731
+    q, k, v = heads(attn.q_proj(x)), heads(attn.k_proj(x)), heads(attn.v_proj(x))
+    from rl_project_b200.ops.rope import apply_rope
+
+    q, k = apply_rope(q, attn.rope), apply_rope(k, attn.rope)
+    s = (q @ k.transpose(-2, -1)) * attn.scale
+    causal = torch.triu(torch.ones(T, T, dtype=torch.bool), 1)
+    top_s, top_i = s.masked_fill(causal, float("-inf")).topk(3, dim=-1)
+    vs = torch.gather(v.unsqueeze(2).expand(-1, -1, T, -1, -1), 3, top_i.unsqueeze(-1).expand(-1, -1, -1, -1, D))
+    sel = (torch.softmax(top_s, -1).unsqueeze(-2) @ vs).squeeze(-2)
+    qp, kp = torch.arange(T)[:, None], torch.arange(T)[None, :]
+    win = torch.softmax(s.masked_fill(~((kp <= qp) & (qp - kp < 5)), float("-inf")), -1) @ v
+    g = F.softmax(attn.gate(x).view(B, T, 3, H), dim=2).permute(0, 3, 1, 2)
+    y = g[..., 0:1] * attn._compressed(q, k, v) + g[..., 1:2] * sel + g[..., 2:3] * win
+    ref = attn.c_proj(y.transpose(1, 2).reshape(B, T, C))
+    assert torch.allclose(got, ref, atol=1e-5), (got - ref).abs().max()
