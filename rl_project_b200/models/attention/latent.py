@@ -2,9 +2,10 @@
 
 Low-rank KV (``wkv_a -> [c_kv | k_rope]``, ``kv_norm``, ``wkv_b``), optional
 q-LoRA (``wq_a``/``q_norm``/``wq_b``), decoupled RoPE on ``qk_rope_head_dim``.
-Cache ``(c_kv [B, T, r], k_rope [B, 1, T, d_r])``.  Training/prefill use the
-decompressed ("naive") path; single-token eval decode uses the absorbed path
-that attends in the latent space.
+Cache ``(c_kv [B, T, r], k_rope [B, 1, T, d_r])``.  Training / prefill use the
+decompressed ("naive") path (cuDNN SDPA, or the own d_qk 192 / d_v 128 forward
+kernel for inference prefill); single-token eval decode uses the absorbed path:
+multi-query attention over one shared ``r + d_r``-wide key in the latent space.
 """
 
 from __future__ import annotations
@@ -72,21 +73,23 @@ class MultiHeadLatentAttention(nn.Module):
                                    q_offset=k.shape[2] - T)
 
     def _absorbed(self, q_nope, q_rope, kv_latent, k_rope, T):
-        total = kv_latent.shape[1]
+        """Attention in the latent space, as multi-query attention over ONE shared key of width
+        ``kv_lora_rank + qk_rope_head_dim``: each head's no-RoPE query is mapped into the latent space by its
+        slice of ``wkv_b`` and concatenated with its RoPE query, the cached ``[latent | k_rope]`` rows are the
+        keys, the latent rows the values, and ``wkv_b``'s value slice maps the result back per head."""
+        S = kv_latent.shape[1]
         w = self.wkv_b.weight.view(self.n_heads, self.qk_nope_head_dim + self.v_head_dim, self.kv_lora_rank)
-        w_k, w_v = w[:, : self.qk_nope_head_dim], w[:, self.qk_nope_head_dim:]
-        q_abs = torch.einsum("bthn,hnl->bhtl", q_nope, w_k)
-        lat = kv_latent.unsqueeze(1)
-        scores = (q_abs @ lat.transpose(-2, -1) + q_rope @ k_rope.transpose(-2, -1)) * self.softmax_scale
+        w_k, w_v = w.split([self.qk_nope_head_dim, self.v_head_dim], dim=1)
+        q_cat = torch.cat([torch.einsum("bthn,hnl->bhtl", q_nope, w_k), q_rope], dim=-1)  # [B, H, T, r + d_r]
+        k_cat = torch.cat([kv_latent, k_rope[:, 0]], dim=-1).unsqueeze(1)  # [B, 1, S, r + d_r]
+        scores = (q_cat @ k_cat.transpose(-2, -1)) * self.softmax_scale
         if self.attn_logit_cap > 0:
             scores = torch.tanh(scores / self.attn_logit_cap) * self.attn_logit_cap
         if T > 1:
-            qpos = torch.arange(total - T, total, device=scores.device)[:, None]
-            kpos = torch.arange(total, device=scores.device)[None, :]
-            scores = scores.masked_fill(kpos > qpos, float("-inf"))
+            future = torch.arange(S, device=scores.device)[None, :] > torch.arange(S - T, S, device=scores.device)[:, None]
+            scores = scores.masked_fill(future, float("-inf"))
         p = scores.float().softmax(-1).type_as(q_nope)
-        out_lat = p @ lat
-        return torch.einsum("bhtl,hvl->bhtv", out_lat, w_v)
+        return torch.einsum("bhtl,hvl->bhtv", p @ kv_latent.unsqueeze(1), w_v)
 
     def forward(self, x: torch.Tensor, past_kv: Optional[LatentCache] = None, positions=None):
         B, T, _ = x.shape
