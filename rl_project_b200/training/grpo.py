@@ -287,18 +287,20 @@ class GRPOAlgorithm(PostTrainingAlgorithm):
     # ---------------------------------------------------------------- evaluation
     @torch.no_grad()
     def evaluate(self, step: int) -> Dict[str, float]:
+        """Greedy (agent) or sampled single completions of the first 8 prompts, decoded and scored as one batch."""
         n = min(8, len(self.tasks if self.cfg.agent else self.prompts))
-        passed = total = 0
-        rsum = 0.0
-        for i in range(n):
-            trajs = (self.agent_engine.rollout(self.tasks[i], 1, temperature=0.0) if self.cfg.agent
-                     else self.rollouts.rollout(self.prompts[i], self.tasks[i], group_size=1))
-            for t in trajs:
-                r = self.reward.score(t)
-                rsum += r.value
-                passed += int(bool(r.passed))
-                total += 1
-        return {"reward": rsum / max(total, 1), "pass_rate": passed / max(total, 1)}
+        if n == 0:
+            return {"reward": 0.0, "pass_rate": 0.0}
+        if self.cfg.agent:
+            groups = self.agent_engine.rollout_many(self.tasks[:n], 1, temperature=0.0)
+        else:
+            groups = self.rollouts.rollout_many(self.prompts[:n], self.tasks[:n], group_size=1)
+        trajs = [t for g in groups for t in g]
+        from rl_project_b200.rollouts.rewards.composite import batch_scores
+
+        results = batch_scores(self.reward, trajs)
+        return {"reward": sum(r.value for r in results) / max(len(results), 1),
+                "pass_rate": sum(bool(r.passed) for r in results) / max(len(results), 1)}
 
     def state(self) -> Dict[str, Any]:
         return self.policy.state_for_checkpoint()
