@@ -23,7 +23,7 @@ import numpy as np
 import torch
 
 from rl_project_b200.core.errors import ConfigError
-from rl_project_b200.domains.allocation.env import ACTION_NAMES, AllocationEnvConfig
+from rl_project_b200.domains.allocation.env import ACTION_NAMES, AllocationEnvConfig, strict_config
 from rl_project_b200.domains.allocation.experiment import ABConfig, run_ab_experiment, shadow_evaluate
 from rl_project_b200.domains.allocation.ope import OPEConfig, OPEError, evaluate_target_policy
 from rl_project_b200.domains.allocation.oracle import oracle_values
@@ -59,10 +59,7 @@ class BenchmarkConfig:
 
     @classmethod
     def from_dict(cls, d: Dict[str, Any]) -> "BenchmarkConfig":
-        unknown = set(d) - {f.name for f in dataclasses.fields(cls)}
-        if unknown:
-            raise ConfigError(f"unknown benchmark keys: {sorted(unknown)}")
-        return cls(**d)
+        return strict_config(cls, d, "benchmark")
 
 
 def train_policy(kind: str, env_cfg: AllocationEnvConfig, bcfg: BenchmarkConfig, seed: int, out_dir: Path,

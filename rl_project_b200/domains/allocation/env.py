@@ -23,7 +23,7 @@ from __future__ import annotations
 import dataclasses
 import math
 from dataclasses import dataclass
-from typing import Any, Dict, List, Optional, Sequence, Tuple
+from typing import Any, Callable, Dict, List, Mapping, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -35,6 +35,20 @@ OBS_DIM = 14
 OBS_NAMES: Tuple[str, ...] = ("remaining_frac", "elapsed_frac", "remaining_steps_frac", "value_rel", "cost_rel",
                               "quality", "season", "pacing_error", "cum_value_norm", "last_multiplier",
                               "last_reward_rel", "last_spend_rel", "recent_value_rel", "recent_cost_rel")
+
+
+def strict_config(cls, data: Mapping[str, Any], what: str, coerce: Optional[Dict[str, Callable]] = None):
+    """Build the dataclass ``cls`` from ``data``: unknown keys are a ``ConfigError`` naming ``what``, values
+    of the keys in ``coerce`` go through their converter, and the result's ``validate()`` (if any) runs."""
+    names = {f.name for f in dataclasses.fields(cls)}
+    unknown = sorted(set(data) - names)
+    if unknown:
+        raise ConfigError(f"unknown {what} keys: {unknown}")
+    conv = coerce or {}
+    obj = cls(**{k: (conv[k](v) if k in conv else v) for k, v in data.items()})
+    if hasattr(obj, "validate"):
+        obj.validate()
+    return obj
 
 
 def response_gain(u):
@@ -80,15 +94,8 @@ class AllocationEnvConfig:
 
     @classmethod
     def from_dict(cls, data: Dict[str, Any]) -> "AllocationEnvConfig":
-        unknown = set(data) - {f.name for f in dataclasses.fields(cls)}
-        if unknown:
-            raise ConfigError(f"unknown allocation env keys: {sorted(unknown)}")
-        d = dict(data)
-        if "multipliers" in d:
-            d["multipliers"] = tuple(float(m) for m in d["multipliers"])
-        cfg = cls(**d)
-        cfg.validate()
-        return cfg
+        return strict_config(cls, data, "allocation env",
+                             coerce={"multipliers": lambda ms: tuple(float(m) for m in ms)})
 
     def to_dict(self) -> Dict[str, Any]:
         d = dataclasses.asdict(self)

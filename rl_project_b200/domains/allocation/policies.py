@@ -23,7 +23,8 @@ import torch
 import torch.nn as nn
 
 from rl_project_b200.core.errors import ConfigError
-from rl_project_b200.domains.allocation.env import OBS_DIM, AllocationEnvConfig, StepArrays, StepContext  # noqa: F401
+from rl_project_b200.domains.allocation.env import (OBS_DIM, AllocationEnvConfig, StepArrays,  # noqa: F401
+                                                     StepContext, strict_config)
 
 
 def one_hot(actions: np.ndarray, n: int) -> np.ndarray:
@@ -123,12 +124,7 @@ class PolicyNetConfig:
 
     @classmethod
     def from_dict(cls, d: Dict[str, Any]) -> "PolicyNetConfig":
-        unknown = set(d) - {f.name for f in dataclasses.fields(cls)}
-        if unknown:
-            raise ConfigError(f"unknown policy keys: {sorted(unknown)}")
-        c = cls(**d)
-        c.validate()
-        return c
+        return strict_config(cls, d, "policy")
 
     def to_dict(self) -> Dict[str, Any]:
         return dataclasses.asdict(self)

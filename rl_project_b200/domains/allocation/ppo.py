@@ -1,21 +1,23 @@
 """PPO for allocation policies, run by the framework's ``Trainer`` (algorithm ``allocation_ppo``).
 
-``collect`` rolls out ``episodes_per_rollout`` episodes in one vectorised
-environment (a fresh rollout every ``ppo_epochs`` optimiser steps, reshuffled
-minibatches in between); advantages are per-episode GAE (gamma = 1 by default:
-undiscounted finite horizon), computed for all episodes at once.  The loss is
-the clipped surrogate + value MSE - entropy bonus.  ``evaluate`` runs the
-stochastic policy on a held-out seed family; ``primary`` = -value so the
-trainer keeps the best checkpoint.  The checkpoint ``model_spec`` has
-``family: allocation_policy`` plus the env and network configs, from which
-``load_allocation_policy`` rebuilds the policy (the spec layout follows
-``src/forgeline/domains/allocation/ppo.py:190-217``).
+Design: a rollout writes straight into a :class:`Trajectory`, a set of ``[T, n, ...]`` tensors on the
+algorithm's device, so the network's outputs never leave the device during collection except for the
+sampled actions the CPU environment needs.  Advantages are computed for all episodes and all steps at
+once as one matrix product with the GAE discount operator (an upper-triangular ``[T, T]`` matrix of
+``(gamma * lambda) ** (s - t)``), instead of a backward recursion.  A rollout is reused for
+``ppo_epochs`` optimiser steps with a fresh permutation each step; micro-batches are strided slices of
+that permutation.
+
+Interfaces kept as the reference defines them (``src/forgeline/domains/allocation/ppo.py``): the
+``AllocationPPOConfig`` field names and defaults, the algorithm name, ``build_allocation_ppo`` taking
+``{env: {...}, policy: {...}, <config fields>}``, and the checkpoint ``model_spec``
+``{family: allocation_policy, policy, env}`` that ``load_allocation_policy`` reads back
+(``src/forgeline/domains/allocation/ppo.py:190-217``).
 """
 
 from __future__ import annotations
 
-import dataclasses
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import Any, Dict, List, Mapping, Optional
 
 import numpy as np
@@ -24,12 +26,15 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from rl_project_b200.core.errors import ConfigError
-from rl_project_b200.domains.allocation.env import OBS_DIM, AllocationEnvConfig, VectorEnv
+from rl_project_b200.domains.allocation.env import OBS_DIM, AllocationEnvConfig, VectorEnv, strict_config
 from rl_project_b200.domains.allocation.policies import (NeuralPolicy, PolicyNetConfig, build_actor_critic,
                                                          history_feature_dim)
 from rl_project_b200.domains.allocation.rollout import aggregate_metrics, run_episodes, seeds_for
 from rl_project_b200.training.common.trainer import PostTrainingAlgorithm
 from rl_project_b200.training.ppo import ppo_clipped_objective
+
+_EVAL_KEYS = ("value", "value_std", "utilization", "pacing_error", "early_exhaustion", "violations",
+              "final_pressure")
 
 
 @dataclass
@@ -47,34 +52,66 @@ class AllocationPPOConfig:
     seed: int = 0
 
     def validate(self) -> None:
-        if min(self.episodes_per_rollout, self.ppo_epochs, self.eval_episodes) < 1:
-            raise ConfigError("episodes_per_rollout, ppo_epochs and eval_episodes must be >= 1")
-        if not (0 < self.clip_ratio < 1 and 0 < self.gamma <= 1 and 0 <= self.gae_lambda <= 1):
-            raise ConfigError("clip_ratio in (0,1), gamma in (0,1], gae_lambda in [0,1] required")
+        rules = (
+            (min(self.episodes_per_rollout, self.ppo_epochs, self.eval_episodes) >= 1,
+             "episodes_per_rollout, ppo_epochs and eval_episodes must be >= 1"),
+            (0 < self.clip_ratio < 1 and 0 < self.gamma <= 1 and 0 <= self.gae_lambda <= 1,
+             "clip_ratio in (0,1), gamma in (0,1], gae_lambda in [0,1] required"),
+        )
+        for ok, msg in rules:
+            if not ok:
+                raise ConfigError(msg)
 
     @classmethod
     def from_dict(cls, d: Dict[str, Any]) -> "AllocationPPOConfig":
-        unknown = set(d) - {f.name for f in dataclasses.fields(cls)}
-        if unknown:
-            raise ConfigError(f"unknown AllocationPPOConfig keys: {sorted(unknown)}")
-        c = cls(**d)
-        c.validate()
-        return c
+        return strict_config(cls, d, "AllocationPPOConfig")
 
 
-def batched_gae(rewards: np.ndarray, values: np.ndarray, gamma: float, lam: float):
-    """GAE over ``[T, n]`` rewards and ``[T+1, n]`` values (terminal value 0): (advantages, returns)."""
-    T = rewards.shape[0]
-    adv = np.zeros_like(rewards)
-    run = np.zeros(rewards.shape[1], dtype=rewards.dtype)
-    for t in range(T - 1, -1, -1):
-        run = rewards[t] + gamma * values[t + 1] - values[t] + gamma * lam * run
-        adv[t] = run
-    return adv, adv + values[:T]
+def gae_operator(T: int, gamma: float, lam: float, device=None, dtype=torch.float32) -> torch.Tensor:
+    """``D[t, s] = (gamma * lam) ** (s - t)`` for ``s >= t`` (else 0): advantages = ``D @ deltas``."""
+    steps = torch.arange(T, device=device, dtype=dtype)
+    lag = steps[None, :] - steps[:, None]
+    return torch.where(lag >= 0, (gamma * lam) ** lag.clamp(min=0), torch.zeros((), device=device, dtype=dtype))
+
+
+def batched_gae(rewards, values, gamma: float, lam: float):
+    """GAE over ``[T, n]`` rewards and ``[T+1, n]`` values (terminal value 0) for every episode at once:
+    returns (advantages ``[T, n]``, returns ``[T, n]``).  Accepts numpy arrays or tensors."""
+    as_np = isinstance(rewards, np.ndarray)
+    r = torch.as_tensor(rewards, dtype=torch.float64)
+    v = torch.as_tensor(values, dtype=torch.float64, device=r.device)
+    deltas = r + gamma * v[1:] - v[:-1]
+    adv = gae_operator(r.shape[0], gamma, lam, r.device, torch.float64) @ deltas
+    ret = adv + v[:-1]
+    if as_np:
+        return adv.numpy().astype(rewards.dtype), ret.numpy().astype(rewards.dtype)
+    return adv.to(rewards.dtype), ret.to(rewards.dtype)
+
+
+@dataclass
+class Trajectory:
+    """One rollout of ``n`` episodes over ``T`` steps, stored step-major on the device."""
+
+    obs: torch.Tensor                     # [T, n, OBS_DIM]
+    actions: torch.Tensor                 # [T, n] int64
+    logp: torch.Tensor                    # [T, n]
+    values: torch.Tensor                  # [T + 1, n]; the last row stays 0 (terminal)
+    rewards: torch.Tensor                 # [T, n]
+    hist: Optional[torch.Tensor] = None   # [T, n, W, D] for sequence policies
+    lengths: Optional[torch.Tensor] = None
+
+    @classmethod
+    def empty(cls, T: int, n: int, device, window: int = 0, hist_dim: int = 0) -> "Trajectory":
+        z = lambda *s, dt=torch.float32: torch.zeros(*s, device=device, dtype=dt)  # noqa: E731
+        seq = window > 0
+        return cls(z(T, n, OBS_DIM), z(T, n, dt=torch.int64), z(T, n), z(T + 1, n), z(T, n),
+                   z(T, n, window, hist_dim) if seq else None, z(T, n, dt=torch.int64) if seq else None)
 
 
 @dataclass
 class RolloutBatch:
+    """Flattened ``[T * n]`` training view of a :class:`Trajectory` with its advantages."""
+
     obs: torch.Tensor
     hist: Optional[torch.Tensor]
     lengths: Optional[torch.Tensor]
@@ -83,7 +120,10 @@ class RolloutBatch:
     advantages: torch.Tensor
     returns: torch.Tensor
     perm: torch.Tensor
-    stats: Dict[str, float]
+    stats: Dict[str, float] = field(default_factory=dict)
+
+    def features(self, idx: torch.Tensor):
+        return self.obs[idx] if self.hist is None else (self.obs[idx], self.hist[idx], self.lengths[idx])
 
 
 class AllocationPPOAlgorithm(PostTrainingAlgorithm):
@@ -91,17 +131,18 @@ class AllocationPPOAlgorithm(PostTrainingAlgorithm):
 
     def __init__(self, env_cfg: AllocationEnvConfig, net_cfg: PolicyNetConfig, config: AllocationPPOConfig,
                  device: torch.device | str = "cpu"):
-        env_cfg.validate()
-        net_cfg.validate()
-        config.validate()
+        for c in (env_cfg, net_cfg, config):
+            c.validate()
         self.env_cfg, self.net_cfg, self.cfg = env_cfg, net_cfg, config
         self.device = torch.device(device)
         self.net = build_actor_critic(env_cfg.n_actions, net_cfg).to(self.device)
         self.policy = NeuralPolicy(self.net, env_cfg, self.device)
         self.rng = np.random.default_rng(config.seed)
+        self._gae = gae_operator(env_cfg.horizon, config.gamma, config.gae_lambda, self.device)
         self._batch: Optional[RolloutBatch] = None
         self._episodes_seen = 0
 
+    # ------------------------------------------------------------------ trainer protocol
     def parameters(self) -> List[nn.Parameter]:
         return [p for p in self.net.parameters() if p.requires_grad]
 
@@ -109,82 +150,39 @@ class AllocationPPOAlgorithm(PostTrainingAlgorithm):
         return (self.net,)
 
     def collect(self, step: int) -> RolloutBatch:
-        if self._batch is None or step % self.cfg.ppo_epochs == 0:
-            self._batch = self._rollout()
-        S = self._batch.actions.shape[0]
-        self._batch.perm = torch.as_tensor(self.rng.permutation(S), device=self.device)
+        fresh = self._batch is None or step % self.cfg.ppo_epochs == 0
+        if fresh:
+            self._batch = self._to_batch(*self._roll())
+        self._batch.perm = torch.as_tensor(self.rng.permutation(self._batch.actions.numel()), device=self.device)
         return self._batch
 
-    @torch.no_grad()
-    def _rollout(self) -> RolloutBatch:
-        cfg, env_cfg = self.cfg, self.env_cfg
-        n, T = cfg.episodes_per_rollout, env_cfg.horizon
-        seeds = [int(s) for s in self.rng.integers(0, 2 ** 31 - 1, size=n)]
-        self._episodes_seen += n
-        venv = VectorEnv(env_cfg, n)
-        obs = venv.reset(seeds)
-        self.policy.start(n)
-        seq = self.policy.is_sequence
-        W, D = self.net_cfg.window, history_feature_dim(env_cfg.n_actions)
-        obs_buf = np.zeros((T, n, OBS_DIM), np.float32)
-        hist_buf = np.zeros((T, n, W, D), np.float32) if seq else None
-        len_buf = np.zeros((T, n), np.int64)
-        act_buf = np.zeros((T, n), np.int64)
-        logp_buf = np.zeros((T, n), np.float32)
-        val_buf = np.zeros((T + 1, n), np.float32)
-        rew_buf = np.zeros((T, n), np.float32)
-        clipped = 0
-        for t in range(T):
-            if seq:
-                self.policy.hist.set_obs(obs)
-                hist_buf[t], len_buf[t] = self.policy.hist.buf, self.policy.hist.lengths
-            logits, value = self.policy.evaluate(obs)
-            dist = torch.distributions.Categorical(logits=logits)
-            a = dist.sample()
-            obs_buf[t], act_buf[t] = obs, a.cpu().numpy()
-            logp_buf[t], val_buf[t] = dist.log_prob(a).cpu().numpy(), value.cpu().numpy()
-            obs, rewards, _, infos = venv.step(act_buf[t])
-            rew_buf[t] = rewards
-            clipped += sum(i.clipped for i in infos)
-            self.policy.observe(act_buf[t], rewards, np.array([i.spend for i in infos]),
-                                np.array([i.remaining_after for i in infos]))
-        adv, ret = batched_gae(rew_buf, val_buf, cfg.gamma, cfg.gae_lambda)
-        flat = lambda x: torch.as_tensor(x.reshape(T * n, *x.shape[2:]), device=self.device)  # noqa: E731
-        advantages = flat(adv)
-        if cfg.normalize_advantages and advantages.numel() > 1:
-            advantages = (advantages - advantages.mean()) / (advantages.std() + 1e-8)
-        ep_values = rew_buf.sum(0)
-        stats = {"reward_mean": float(ep_values.mean()), "reward_std": float(ep_values.std()),
-                 "clipped_per_episode": clipped / n, "episodes_seen": float(self._episodes_seen),
-                 "utilization": float((venv.cum_spend / env_cfg.budget).mean())}
-        return RolloutBatch(flat(obs_buf), flat(hist_buf) if seq else None, flat(len_buf) if seq else None,
-                            flat(act_buf), flat(logp_buf), advantages, flat(ret), torch.arange(T * n), stats)
-
     def loss(self, batch: RolloutBatch, micro_step: int, n_micro: int):
-        idx = batch.perm[micro_step::n_micro] if n_micro > 1 else batch.perm
-        feats = batch.obs[idx] if batch.hist is None else (batch.obs[idx], batch.hist[idx], batch.lengths[idx])
-        logits, values = self.net(feats)
+        idx = batch.perm[micro_step::n_micro]
+        logits, values = self.net(batch.features(idx))
         logp_all = F.log_softmax(logits, -1)
         logp = logp_all.gather(1, batch.actions[idx, None]).squeeze(1)
-        ratio = torch.exp(logp - batch.old_logp[idx])
-        pg = ppo_clipped_objective(ratio, batch.advantages[idx], self.cfg.clip_ratio).mean()
-        v_loss = F.mse_loss(values, batch.returns[idx])
-        entropy = -(logp_all.exp() * logp_all).sum(-1).mean()
-        loss = pg + self.cfg.value_coef * v_loss - self.cfg.entropy_coef * entropy
+        log_ratio = logp - batch.old_logp[idx]
+        ratio = log_ratio.exp()
+        terms = {
+            "policy_loss": ppo_clipped_objective(ratio, batch.advantages[idx], self.cfg.clip_ratio).mean(),
+            "value_loss": F.mse_loss(values, batch.returns[idx]),
+            "entropy": -(logp_all.exp() * logp_all).sum(-1).mean(),
+        }
+        loss = terms["policy_loss"] + self.cfg.value_coef * terms["value_loss"] - self.cfg.entropy_coef * terms["entropy"]
         with torch.no_grad():
-            metrics = {**batch.stats, "policy_loss": float(pg), "value_loss": float(v_loss), "entropy": float(entropy),
-                       "approx_kl": float((batch.old_logp[idx] - logp).mean()),
-                       "clip_fraction": float(((ratio - 1).abs() > self.cfg.clip_ratio).float().mean())}
+            extra = torch.stack([(-log_ratio).mean(), ((ratio - 1).abs() > self.cfg.clip_ratio).float().mean()])
+            vals = torch.stack([t.detach() for t in terms.values()] + list(extra)).tolist()  # one host read
+        metrics = dict(batch.stats)
+        metrics.update(zip(list(terms) + ["approx_kl", "clip_fraction"], vals))
         return loss, metrics
 
     @torch.no_grad()
     def evaluate(self, step: int) -> Dict[str, float]:
-        eps = run_episodes(self.policy, self.env_cfg, seeds_for(self.cfg.eval_seed, self.cfg.eval_episodes),
-                           rng_seed=self.cfg.eval_seed)
-        m = aggregate_metrics(eps, self.env_cfg)
-        out = {k: m[k] for k in ("value", "value_std", "utilization", "pacing_error", "early_exhaustion",
-                                 "violations", "final_pressure")}
-        out["primary"] = -m["value"]
+        seeds = seeds_for(self.cfg.eval_seed, self.cfg.eval_episodes)
+        m = aggregate_metrics(run_episodes(self.policy, self.env_cfg, seeds, rng_seed=self.cfg.eval_seed),
+                              self.env_cfg)
+        out = {k: m[k] for k in _EVAL_KEYS}
+        out["primary"] = -m["value"]  # the trainer keeps the lowest primary
         return out
 
     def state(self) -> Dict[str, Any]:
@@ -199,16 +197,62 @@ class AllocationPPOAlgorithm(PostTrainingAlgorithm):
     def tokenizer_meta(self):
         return None
 
+    # ------------------------------------------------------------------ rollout
+    @torch.no_grad()
+    def _roll(self):
+        n, T = self.cfg.episodes_per_rollout, self.env_cfg.horizon
+        seq = self.policy.is_sequence
+        traj = Trajectory.empty(T, n, self.device, self.net_cfg.window if seq else 0,
+                                history_feature_dim(self.env_cfg.n_actions))
+        venv = VectorEnv(self.env_cfg, n)
+        obs = venv.reset([int(s) for s in self.rng.integers(0, 2 ** 31 - 1, size=n)])
+        self._episodes_seen += n
+        self.policy.start(n)
+        clipped = 0
+        for t in range(T):
+            if seq:
+                self.policy.hist.set_obs(obs)
+                traj.hist[t].copy_(torch.from_numpy(self.policy.hist.buf))
+                traj.lengths[t].copy_(torch.from_numpy(self.policy.hist.lengths))
+            traj.obs[t].copy_(torch.from_numpy(np.asarray(obs, dtype=np.float32)))
+            logits, value = self.policy.evaluate(obs)
+            logp_all = F.log_softmax(logits.float(), -1)
+            a = torch.multinomial(logp_all.exp(), 1).squeeze(1)
+            traj.actions[t], traj.logp[t], traj.values[t] = a, logp_all.gather(1, a[:, None]).squeeze(1), value
+            a_host = a.cpu().numpy()
+            obs, rewards, _, infos = venv.step(a_host)
+            traj.rewards[t].copy_(torch.from_numpy(np.asarray(rewards, dtype=np.float32)))
+            clipped += sum(i.clipped for i in infos)
+            self.policy.observe(a_host, rewards, np.array([i.spend for i in infos]),
+                                np.array([i.remaining_after for i in infos]))
+        ep_value = traj.rewards.sum(0)
+        stats = {"reward_mean": float(ep_value.mean()), "reward_std": float(ep_value.double().std(unbiased=False)),
+                 "clipped_per_episode": clipped / n, "episodes_seen": float(self._episodes_seen),
+                 "utilization": float((venv.cum_spend / self.env_cfg.budget).mean())}
+        return traj, stats
+
+    def _to_batch(self, traj: Trajectory, stats: Dict[str, float]) -> RolloutBatch:
+        deltas = traj.rewards + self.cfg.gamma * traj.values[1:] - traj.values[:-1]
+        adv = self._gae @ deltas
+        ret = adv + traj.values[:-1]
+        flat = lambda x: None if x is None else x.reshape(-1, *x.shape[2:])  # noqa: E731
+        adv = flat(adv)
+        if self.cfg.normalize_advantages and adv.numel() > 1:
+            adv = (adv - adv.mean()) / (adv.std() + 1e-8)
+        return RolloutBatch(flat(traj.obs), flat(traj.hist), flat(traj.lengths), flat(traj.actions),
+                            flat(traj.logp), adv, flat(ret), torch.arange(adv.numel(), device=self.device), stats)
+
 
 def build_allocation_ppo(params: Dict[str, Any], device: torch.device | str = "cpu") -> AllocationPPOAlgorithm:
     """From ``algorithm_params`` ``{env: {...}, policy: {...}, <AllocationPPOConfig fields>}``."""
-    p = dict(params)
-    env_cfg = AllocationEnvConfig.from_dict(p.pop("env", {}) or {})
-    net_cfg = PolicyNetConfig.from_dict(p.pop("policy", {}) or {})
-    return AllocationPPOAlgorithm(env_cfg, net_cfg, AllocationPPOConfig.from_dict(p), device)
+    rest = {k: v for k, v in params.items() if k not in ("env", "policy")}
+    return AllocationPPOAlgorithm(AllocationEnvConfig.from_dict(params.get("env") or {}),
+                                  PolicyNetConfig.from_dict(params.get("policy") or {}),
+                                  AllocationPPOConfig.from_dict(rest), device)
 
 
 def load_allocation_policy(checkpoint: str, device: torch.device | str = "cpu") -> NeuralPolicy:
+    """Rebuild the trained policy from a checkpoint directory written by the trainer."""
     from rl_project_b200.checkpoints.manager import CheckpointManager
 
     state = CheckpointManager.load(checkpoint, map_location="cpu")
@@ -219,5 +263,4 @@ def load_allocation_policy(checkpoint: str, device: torch.device | str = "cpu") 
     env_cfg = AllocationEnvConfig.from_dict(spec["env"])
     net = build_actor_critic(env_cfg.n_actions, PolicyNetConfig.from_dict(spec["policy"]))
     net.load_state_dict(state.model_state["model"])
-    net.eval()
-    return NeuralPolicy(net, env_cfg, device)
+    return NeuralPolicy(net.eval(), env_cfg, device)
