@@ -65,9 +65,11 @@ def parse_args():
                     help="CTAs of each fused reduce-scatter that overlaps backward")
     ap.add_argument("--fused-multicast", choices=["off", "on", "symm"], default="off",
                     help="fused reduce-scatter transport: CUDA IPC peer loads (off) or NVLink multicast (on)")
-    ap.add_argument("--gemm", choices=["tcgen05", "cublas", "tuned", "hybrid"], default="cublas",
-                    help="dense linear layers and LM head: this library's 2-SM tcgen05 GEMM, cuBLAS, or per shape "
-                         "the fastest of the two (timed on the first call of each shape)")
+    ap.add_argument("--gemm", choices=["tcgen05", "cublas", "tuned", "hybrid", "fwd_dgrad"], default="hybrid",
+                    help="dense linear layers and LM head: hybrid (default: own 2-SM tcgen05 GEMM for the forward "
+                         "products, SwiGLU fused into the FFN projection's epilogue, cuBLAS for the gradient products), "
+                         "tcgen05 (own kernel for all), fwd_dgrad (own forward and input gradients), cublas, or tuned "
+                         "(per shape the fastest, timed on the first call of each shape)")
     ap.add_argument("--attn", choices=["sdpa", "tcgen05"], default="sdpa",
                     help="training / prefill attention: torch SDPA (cuDNN / flash) or this library's tcgen05 kernels")
     ap.add_argument("--decode-graphs", choices=["on", "off"], default="on",

@@ -417,10 +417,11 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t a_m
 }
 
 // The same product on the 2-SM kernel (256 x 256 nsub tiles per CTA pair, TMA-store epilogue); max_ctas > 0
-// caps its persistent grid (0: as many CTA pairs as fit on the device).
-void gemm2(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t a_mn, int64_t b_mn, int64_t epi,
-           int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, double alpha,
-           const c10::optional<at::Tensor>& status, int64_t max_ctas, int64_t nsub) {
+// caps its persistent grid (0: as many CTA pairs as fit on the device).  gemm2x adds the K-split count (> 1
+// only into an fp32 output it reduce-adds to, epi 2) and the raster group height (0: default).
+void gemm2x(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t a_mn, int64_t b_mn, int64_t epi,
+            int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, double alpha,
+            const c10::optional<at::Tensor>& status, int64_t max_ctas, int64_t nsub, int64_t splits, int64_t group_m) {
   check_bf16(A, "A");
   check_bf16(B, "B");
   check_dev(B, A, "B");
@@ -432,8 +433,37 @@ void gemm2(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t a_
   const c10::cuda::CUDAGuard g(A.device());
   CHECK_OK(rlb_gemm2sm((int)a_mn, (int)b_mn, (int)epi, (int)nsub, (int)M, (int)N, (int)K, A.data_ptr(), lda, B.data_ptr(), ldb,
                        out.data_ptr(), ldc, (float)alpha, status.has_value() ? status->data_ptr<int>() : nullptr,
-                       (int)max_ctas, cur_stream()),
+                       (int)max_ctas, cur_stream(), (int)splits, (int)group_m),
            "gemm2");
+}
+
+void gemm2(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t a_mn, int64_t b_mn, int64_t epi,
+           int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, double alpha,
+           const c10::optional<at::Tensor>& status, int64_t max_ctas, int64_t nsub) {
+  gemm2x(A, B, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, status, max_ctas, nsub, 1, 0);
+}
+
+// x [M][K] times w13 = [W1; W3] ([2H][K]) with the SwiGLU activation fused into the epilogue: writes the
+// projection h13 [M][2H] and the activation act [M][H].
+void gemm2_swiglu(const at::Tensor& X, const at::Tensor& W13, at::Tensor& h13, at::Tensor& act, int64_t group_m) {
+  check_bf16(X, "x");
+  check_bf16(W13, "w13");
+  check_bf16(h13, "h13");
+  check_bf16(act, "act");
+  check_dev(W13, X, "w13");
+  check_dev(h13, X, "h13");
+  check_dev(act, X, "act");
+  TORCH_CHECK(X.dim() == 2 && W13.dim() == 2 && X.size(1) == W13.size(1) && W13.size(0) % 2 == 0,
+              "gemm2_swiglu: x [M, K] and w13 [2H, K] expected");
+  const int64_t M = X.size(0), K = X.size(1), H = W13.size(0) / 2;
+  TORCH_CHECK(X.stride(1) == 1 && W13.stride(1) == 1 && h13.stride(1) == 1 && act.is_contiguous(),
+              "gemm2_swiglu: rows must be contiguous");
+  TORCH_CHECK(h13.size(0) == M && h13.size(1) == 2 * H && act.size(0) == M && act.size(1) == H,
+              "gemm2_swiglu: output shapes");
+  const c10::cuda::CUDAGuard g(X.device());
+  CHECK_OK(rlb_gemm2sm_swiglu((int)M, (int)H, (int)K, X.data_ptr(), X.stride(0), W13.data_ptr(), W13.stride(0),
+                              h13.data_ptr(), h13.stride(0), act.data_ptr(), nullptr, 0, cur_stream(), (int)group_m),
+           "gemm2_swiglu");
 }
 
 // Grouped GEMM (mixture-of-experts): see rlb_gemm_grouped for the two modes.
@@ -849,6 +879,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nf4_gemm", &nf4_gemm);
   m.def("gemm", &gemm);
   m.def("gemm2", &gemm2);
+  m.def("gemm2x", &gemm2x);
+  m.def("gemm2_swiglu", &gemm2_swiglu);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("fmha_fwd", &fmha_fwd);

@@ -68,21 +68,29 @@ struct Cfg {
   static_assert(ACCS * BN <= TMEM_COLS, "accumulators fit in TMEM");
 };
 
-enum Epi : int { kStoreBF16 = 0, kStoreF32 = 1, kAccumF32 = 2 };
+// kSwiGLU: forward of a gated FFN's fused [gate | up] projection (B = [W1; W3], N = the hidden width H).  A
+// tile holds the gate and up columns of the same 256 hidden units (its two 256-column sub-tiles read W1 rows
+// h.. and W3 rows H + h..); the epilogue stores both into h13 (kept for the backward) and silu(gate) * up,
+// computed from their bf16 values as the standalone activation kernel does, into the activation output.
+enum Epi : int { kStoreBF16 = 0, kStoreF32 = 1, kAccumF32 = 2, kSwiGLU = 3 };
+
+__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
 
 struct Params {
   int M, N, K;
+  int splits;   // K ranges per tile (> 1 only with kAccumF32: each range reduce-adds its partial product)
+  int group_m;  // M tiles per raster group (consecutive work units walk M inside a group, then N)
   float alpha;
   int* status;
   float* c32;     // kAccumF32: C itself, for the ragged edge chunks the threads accumulate directly
   long long ldc;
 };
 
-__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m, int& n) {
-  const int per_group = GROUP_M * num_n;
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group_m, int& m, int& n) {
+  const int per_group = group_m * num_n;
   const int g = t / per_group;
-  const int first_m = g * GROUP_M;
-  const int gsize = min(num_m - first_m, GROUP_M);
+  const int first_m = g * group_m;
+  const int gsize = min(num_m - first_m, group_m);
   const int r = t % per_group;
   m = first_m + r % gsize;
   n = r / gsize;
@@ -114,6 +122,8 @@ template <int A_MN, int B_MN, int EPI, int NSUB>
 __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __grid_constant__ CUtensorMap tma_a,
                                                                         const __grid_constant__ CUtensorMap tma_b,
                                                                         const __grid_constant__ CUtensorMap tma_c,
+                                                                        const __grid_constant__ CUtensorMap tma_c2,
+                                                                        const __grid_constant__ CUtensorMap tma_c3,
                                                                         Params p) {
   using C = Cfg<NSUB>;
   constexpr int BN = C::BN, STAGES = C::STAGES, ACCS = C::ACCS;
@@ -133,9 +143,19 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
 
   const uint32_t rank = sm100::cluster_ctarank();  // 0: the CTA that issues the pair MMAs
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
+  static_assert(EPI != kSwiGLU || (NSUB == 2 && A_MN == 0 && B_MN == 0), "SwiGLU epilogue: forward, 256 x 512");
+  constexpr int TN = EPI == kSwiGLU ? SUBN : BN;  // output columns (hidden units for kSwiGLU) per tile
+  const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + TN - 1) / TN;
   const int num_tiles = num_m * num_n;
   const int nk = (p.K + BK - 1) / BK;
+  // work unit u: tile u % num_tiles, K blocks [kb_lo, kb_hi) of split u / num_tiles (split-major, so the
+  // units in flight together share their K range and its operand slices in L2)
+  const int num_units = num_tiles * p.splits;
+  auto k_range = [&](int u, int& lo, int& hi) {
+    const int sp = u / num_tiles;
+    lo = (int)((long long)sp * nk / p.splits);
+    hi = (int)((long long)(sp + 1) * nk / p.splits);
+  };
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
   const Ctl ctl{abort_flag, sm100::mapa(sm100::smem_u32((const void*)abort_flag), rank ^ 1u), p.status};
 
@@ -154,6 +174,10 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
     sm100::prefetch_tensormap(&tma_a);
     sm100::prefetch_tensormap(&tma_b);
     sm100::prefetch_tensormap(&tma_c);
+    if (EPI == kSwiGLU) {
+      sm100::prefetch_tensormap(&tma_c2);
+      sm100::prefetch_tensormap(&tma_c3);
+    }
   }
   if (warp == 1) {
     sm100::tmem_alloc_pair(tmem_slot, TMEM_COLS);
@@ -170,13 +194,14 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
       int stage = 0;
       uint32_t phase = 0;
       const uint32_t full0 = sm100::mapa(sm100::smem_u32(full), 0);
-      for (int t = cluster; t < num_tiles && !*abort_flag; t += nclusters) {
-        int tm, tn;
-        tile_coords(t, num_m, num_n, tm, tn);
+      for (int u = cluster; u < num_units && !*abort_flag; u += nclusters) {
+        int tm, tn, kb_lo, kb_hi;
+        tile_coords(u % num_tiles, num_m, num_n, p.group_m, tm, tn);
+        k_range(u, kb_lo, kb_hi);
         const int m0 = tm * BM + (int)rank * HM;  // this CTA's rows of A
-        const int nb = tn * BN + (int)rank * HN;  // ... and of B in the first sub-tile
+        const int nb = tn * TN + (int)rank * HN;  // ... and of B in the first sub-tile
         bool dead = false;
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!wait(&empty[stage], phase ^ 1)) {
             fail(ctl, 1);
             dead = true;
@@ -201,7 +226,7 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
 #pragma unroll
           for (int j = 0; j < NSUB; ++j) {
             uint8_t* bj = b + j * B_SUB_BYTES;
-            const int n0 = nb + j * SUBN;
+            const int n0 = nb + j * (EPI == kSwiGLU ? p.N : SUBN);  // kSwiGLU: sub-tile 1 reads W3's rows
             if (B_MN) {
 #pragma unroll
               for (int h = 0; h < HN / 64; ++h) sm100::tma_load_2d_pair(bj + h * (BK * 128), &tma_b, fb, n0 + 64 * h, k0);
@@ -223,7 +248,7 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
       constexpr uint32_t idesc = sm100::idesc_bf16_f32(BM, SUBN, A_MN, B_MN);
       const uint32_t empty0 = sm100::mapa(sm100::smem_u32(empty), 0), empty1 = sm100::mapa(sm100::smem_u32(empty), 1);
       const uint32_t tfull0 = sm100::mapa(sm100::smem_u32(tfull), 0), tfull1 = sm100::mapa(sm100::smem_u32(tfull), 1);
-      // MMAs of one 64-deep K slice (stage `st`, K block `kb`) into accumulator sub-tile j
+      // MMAs of one 64-deep K slice (stage `st`, K block `kb` counted from the unit's first) into sub-tile j
       auto issue = [&](uint32_t d, int st, int kb, int j) {
         const uint32_t a = sm100::smem_u32(sA + st * A_BYTES);
         const uint32_t bj = sm100::smem_u32(sB + st * C::B_BYTES) + j * B_SUB_BYTES;
@@ -247,7 +272,9 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int t = cluster; t < num_tiles && !*abort_flag; t += nclusters) {
+      for (int u = cluster; u < num_units && !*abort_flag; u += nclusters) {
+        int kb_lo, kb_hi;
+        k_range(u, kb_lo, kb_hi);
         // NSUB == 2: one accumulator of two sub-tiles whose columns the epilogue hands back one after the
         // other (tempty[0], tempty[1]).  The sub-tile 0 MMAs of this tile start as soon as sub-tile 0 is
         // free; K slices whose sub-tile 1 MMAs must wait stay pending (their stages unreleased), at most a
@@ -264,19 +291,19 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
         auto catch_up = [&]() {
           for (int i = 0; i < pend; ++i) {
             const int st = (pend_st + i) % STAGES;
-            issue(d, st, pend_kb + i, 1);
+            issue(d, st, pend_kb + i - kb_lo, 1);
             release(st);
           }
           pend = 0;
         };
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!wait(&full[stage], phase)) {
             fail(ctl, 3);
             dead = true;
             break;
           }
           sm100::tc_fence_after();
-          issue(d, stage, kb, 0);
+          issue(d, stage, kb - kb_lo, 0);
           if constexpr (NSUB == 2) {
             if (!sub1_free) {
               bool now_free = sm100::mbar_test_wait(&tempty[1], acc_phase ^ 1);
@@ -301,7 +328,7 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
               ++pend;
             } else {
               catch_up();
-              issue(d, stage, kb, 1);
+              issue(d, stage, kb - kb_lo, 1);
               release(stage);
             }
           } else {
@@ -345,10 +372,10 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
     int acc = 0;
     uint32_t acc_phase = 0;
     int ebuf = 0;
-    for (int t = cluster; t < num_tiles; t += nclusters) {
+    for (int u = cluster; u < num_units; u += nclusters) {
       if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
       int tm, tn;
-      tile_coords(t, num_m, num_n, tm, tn);
+      tile_coords(u % num_tiles, num_m, num_n, p.group_m, tm, tn);
       const int row0 = tm * BM + (int)rank * HM + q * 32;  // first C row of this warp's 32 rows
       if (!__all_sync(0xffffffffu, wait(&tfull[acc], acc_phase))) {
         if (lane == 0) fail(ctl, 4);
@@ -356,7 +383,7 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
       }
       sm100::tc_fence_after();
       const uint32_t lanes = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-      if constexpr (EPI == kStoreBF16 && NSUB == 2) {
+      if constexpr ((EPI == kStoreBF16 || EPI == kSwiGLU) && NSUB == 2) {
         // read this warp's 128 columns of sub-tile 0, hand sub-tile 0 back (the next tile's first MMAs may
         // start), then its 128 columns of sub-tile 1 and hand those back; all kept as packed bf16 in registers
         uint32_t pk[2][64];
@@ -376,25 +403,39 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
           __syncwarp();
           if (lane == 0) sm100::mbar_arrive_cluster(tempty0 + (uint32_t)sb * 8u);
         }
+        // kSwiGLU: out 0 / 1 are the gate / up halves of h13 (maps c, c2), out 2 the activation (map c3)
+        constexpr int NOUT = EPI == kSwiGLU ? 3 : 2;
 #pragma unroll
-        for (int sb = 0; sb < 2; ++sb) {
+        for (int o = 0; o < NOUT; ++o) {
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            const int col0 = tn * BN + sb * SUBN + half * 128 + c * 64;
+            const int col0 = (EPI == kSwiGLU ? tn * SUBN : tn * BN + o * SUBN) + half * 128 + c * 64;
             uint8_t* tile = stage_tiles;
             if (lane == 0) sm100::bulk_wait_read<0>();  // the staging tile's previous store has read it
             __syncwarp();
             // row `lane`: 8 chunks of 16 B; chunk j stored at j ^ (row % 8) (the TMA 128-B swizzle)
             uint8_t* rowp = tile + lane * 128;
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) =
-                  make_uint4(pk[sb][c * 32 + 4 * j], pk[sb][c * 32 + 4 * j + 1], pk[sb][c * 32 + 4 * j + 2],
-                             pk[sb][c * 32 + 4 * j + 3]);
+            for (int j = 0; j < 8; ++j) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int i = c * 32 + 4 * j + e;
+                if (o < 2) {
+                  w[e] = pk[o][i];
+                } else {  // silu(gate) * up from the bf16 pair values (bf16 -> fp32 is a 16-bit shift), rounded once
+                  const uint32_t g2 = pk[0][i], u2 = pk[1][i];
+                  w[e] = pack_bf16(silu(__uint_as_float(g2 << 16)) * __uint_as_float(u2 << 16),
+                                   silu(__uint_as_float(g2 & 0xffff0000u)) * __uint_as_float(u2 & 0xffff0000u));
+                }
+              }
+              *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
             sm100::fence_async_shared();  // generic-proxy writes visible to the TMA engine
             __syncwarp();
             if (lane == 0 && row0 < p.M && col0 < p.N) {
-              sm100::tma_store_2d(&tma_c, tile, col0, row0);  // clipped at M and N by the tensor map
+              const CUtensorMap* map = o == 0 ? &tma_c : (o == 1 ? &tma_c2 : &tma_c3);
+              sm100::tma_store_2d(EPI == kSwiGLU ? map : &tma_c, tile, col0, row0);  // clipped at M and N
               sm100::bulk_commit();
             }
           }
@@ -428,12 +469,13 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
           if (EPI == kAccumF32 && (row0 + 32 > p.M || col0 + 32 > p.N)) {
             // A reduce-add box that runs past C's edge lost updates on B200 (tested: columns past the inner
             // extent), so a clipped chunk is accumulated by the threads: row `lane`, its columns below N.
+            // Atomically: with split K, other units add their partial sums to the same elements.
             const int row = row0 + lane;
             if (row < p.M) {
               float* dst = p.c32 + (long long)row * p.ldc + col0;
 #pragma unroll
               for (int e = 0; e < 32; ++e)
-                if (col0 + e < p.N) dst[e] += __uint_as_float(r[e]) * p.alpha;
+                if (col0 + e < p.N) atomicAdd(dst + e, __uint_as_float(r[e]) * p.alpha);
             }
             continue;
           }
@@ -540,15 +582,26 @@ static int max_clusters(int dev) {
 
 template <int A_MN, int B_MN, int EPI, int NSUB>
 static cudaError_t launch(const void* A, long long lda, const void* B, long long ldb, void* Cp, long long ldc,
-                          const Params& p, int max_ctas, cudaStream_t s) {
+                          const Params& p, int max_ctas, cudaStream_t s, void* act = nullptr) {
   using C = Cfg<NSUB>;
   CUtensorMap ma, mb, mc;
   const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   // K-major operand: [rows][K], box 64 k x 128 rows.  MN-major: [K][rows], box 64 rows x 64 k.
   const bool ok_a = A_MN ? make_map(&ma, bf, 2, A, p.K, p.M, lda, 64, BK) : make_map(&ma, bf, 2, A, p.M, p.K, lda, 64, HM);
-  const bool ok_b = B_MN ? make_map(&mb, bf, 2, B, p.K, p.N, ldb, 64, BK) : make_map(&mb, bf, 2, B, p.N, p.K, ldb, 64, HN);
-  const bool ok_c = EPI == kStoreBF16 ? make_map(&mc, bf, 2, Cp, p.M, p.N, ldc, 64, 32)
-                                      : make_map(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Cp, p.M, p.N, ldc, 32, 32);
+  const long long b_rows = EPI == kSwiGLU ? 2LL * p.N : p.N;  // kSwiGLU: B = [W1; W3]
+  const bool ok_b = B_MN ? make_map(&mb, bf, 2, B, p.K, p.N, ldb, 64, BK) : make_map(&mb, bf, 2, B, b_rows, p.K, ldb, 64, HN);
+  CUtensorMap mc2, mc3;
+  bool ok_c;
+  if (EPI == kSwiGLU) {  // gate / up halves of h13 [M][2H] (row pitch ldc) and the activation [M][H]
+    ok_c = make_map(&mc, bf, 2, Cp, p.M, p.N, ldc, 64, 32) &&
+           make_map(&mc2, bf, 2, (const __nv_bfloat16*)Cp + p.N, p.M, p.N, ldc, 64, 32) &&
+           make_map(&mc3, bf, 2, act, p.M, p.N, p.N, 64, 32);
+  } else {
+    ok_c = EPI == kStoreBF16 ? make_map(&mc, bf, 2, Cp, p.M, p.N, ldc, 64, 32)
+                             : make_map(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Cp, p.M, p.N, ldc, 32, 32);
+    mc2 = mc;
+    mc3 = mc;
+  }
   if (!ok_a || !ok_b || !ok_c) return cudaErrorInvalidResourceHandle;  // tensor-map encoding rejected an operand
   auto kern = gemm2sm_kernel<A_MN, B_MN, EPI, NSUB>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
@@ -559,8 +612,9 @@ static cudaError_t launch(const void* A, long long lda, const void* B, long long
   int clusters = max_clusters<A_MN, B_MN, EPI, NSUB>(dev);
   if (clusters <= 0) return cudaErrorNotSupported;
   if (max_ctas > 0 && clusters > max_ctas / 2) clusters = max_ctas / 2 > 0 ? max_ctas / 2 : 1;
-  const int tiles = ((p.M + BM - 1) / BM) * ((p.N + C::BN - 1) / C::BN);
-  if (clusters > tiles) clusters = tiles;
+  const int tile_n = EPI == kSwiGLU ? SUBN : C::BN;
+  const int units = ((p.M + BM - 1) / BM) * ((p.N + tile_n - 1) / tile_n) * p.splits;
+  if (clusters > units) clusters = units;
   (void)cudaGetLastError();  // drop a stale, non-sticky error left by unrelated calls on this thread
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -574,7 +628,7 @@ static cudaError_t launch(const void* A, long long lda, const void* B, long long
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, p);
+  e = cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, mc2, mc3, p);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
@@ -585,11 +639,18 @@ static cudaError_t launch(const void* A, long long lda, const void* B, long long
 // epi: 0 = store bf16, 1 = store fp32, 2 = accumulate into fp32.  nsub: 1 = 256 x 256 tiles (double-buffered
 // accumulators), 2 = 256 x 512 tiles (one A slice per two MMAs).  Leading dimensions must be multiples of 8
 // elements (C: 16 bytes), base pointers 16-byte aligned.  max_ctas > 0 caps the grid (CTAs, even).
+// splits > 1 divides each tile's K blocks into that many ranges, each its own work unit that reduce-adds its
+// partial product into C (epi 2 only; C must hold the starting value, e.g. zeros): for products with few
+// output tiles and a long K (weight gradients of narrow layers), where whole tiles would leave most of the
+// last wave of CTA pairs idle.  group_m: M tiles per raster group (0: the default of 8).
 cudaError_t rlb_gemm2sm(int a_mn, int b_mn, int epi, int nsub, int M, int N, int K, const void* A, long long lda,
                         const void* B, long long ldb, void* C, long long ldc, float alpha, int* status, int max_ctas,
-                        cudaStream_t s) {
+                        cudaStream_t s, int splits, int group_m) {
   using namespace gemm2;
   if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+  const int nk = (K + BK - 1) / BK;
+  if (splits < 1 || splits > nk || (splits > 1 && epi != kAccumF32)) return cudaErrorInvalidValue;
+  if (group_m < 1) group_m = GROUP_M;
   if ((lda % 8) || (ldb % 8) || ((ldc * (epi == kStoreBF16 ? 2 : 4)) % 16)) return cudaErrorInvalidPitchValue;
   if ((((uintptr_t)A) | ((uintptr_t)B) | ((uintptr_t)C)) & 15) return cudaErrorInvalidDevicePointer;
   if (nsub != 1 && nsub != 2) return cudaErrorInvalidValue;
@@ -597,6 +658,8 @@ cudaError_t rlb_gemm2sm(int a_mn, int b_mn, int epi, int nsub, int M, int N, int
   p.M = M;
   p.N = N;
   p.K = K;
+  p.splits = splits;
+  p.group_m = group_m;
   p.alpha = alpha;
   p.status = status;
   p.c32 = (float*)C;
@@ -614,4 +677,28 @@ cudaError_t rlb_gemm2sm(int a_mn, int b_mn, int epi, int nsub, int M, int N, int
   RLB_GEMM2_CASE(0, 0, 2)
 #undef RLB_GEMM2_CASE
   return cudaErrorNotSupported;
+}
+
+// Forward of a gated FFN's fused projection on the 2-SM kernel with the SwiGLU activation in the epilogue:
+// h13 = x [M][K] * w13^T (w13 = [W1; W3], [2H][K], K contiguous) stored [M][2H] (row pitch ldh), and
+// act = silu(h13[:, :H]) * h13[:, H:] stored [M][H].  H, K, ldx, ldw and ldh multiples of 8; pointers
+// 16-byte aligned.  group_m as for rlb_gemm2sm.
+cudaError_t rlb_gemm2sm_swiglu(int M, int H, int K, const void* X, long long ldx, const void* W13, long long ldw,
+                               void* H13, long long ldh, void* act, int* status, int max_ctas, cudaStream_t s,
+                               int group_m) {
+  using namespace gemm2;
+  if (M <= 0 || H <= 0 || K <= 0) return cudaSuccess;
+  if ((H % 8) || (ldx % 8) || (ldw % 8) || (ldh % 8) || ldh < 2LL * H) return cudaErrorInvalidPitchValue;
+  if ((((uintptr_t)X) | ((uintptr_t)W13) | ((uintptr_t)H13) | ((uintptr_t)act)) & 15) return cudaErrorInvalidDevicePointer;
+  Params p{};
+  p.M = M;
+  p.N = H;
+  p.K = K;
+  p.splits = 1;
+  p.group_m = group_m < 1 ? GROUP_M : group_m;
+  p.alpha = 1.f;
+  p.status = status;
+  p.c32 = nullptr;
+  p.ldc = ldh;
+  return launch<0, 0, kSwiGLU, 2>(X, ldx, W13, ldw, H13, ldh, p, max_ctas, s, act);
 }

@@ -53,10 +53,17 @@ cudaError_t rlb_gemm(int a_mn, int b_mn, int epi, int M, int N, int K, const voi
                      long long ldb, void* C, long long ldc, float alpha, int* status, int sms, cudaStream_t s);
 
 // 2-SM variant (CTA pairs, 256 x 256 nsub tiles, nsub 1 or 2): same operands and epilogues; max_ctas > 0
-// caps the grid.
+// caps the grid; splits > 1 (epi 2 only) splits each tile's K into ranges that reduce-add into C; group_m is
+// the raster group height in M tiles (0: default).
 cudaError_t rlb_gemm2sm(int a_mn, int b_mn, int epi, int nsub, int M, int N, int K, const void* A, long long lda,
                         const void* B, long long ldb, void* C, long long ldc, float alpha, int* status, int max_ctas,
-                        cudaStream_t s);
+                        cudaStream_t s, int splits = 1, int group_m = 0);
+
+// Gated-FFN forward on the 2-SM kernel: h13 = x w13^T ([M][2H], pitch ldh) and act = silu(gate) * up ([M][H])
+// from one GEMM whose epilogue applies the activation.
+cudaError_t rlb_gemm2sm_swiglu(int M, int H, int K, const void* X, long long ldx, const void* W13, long long ldw,
+                               void* H13, long long ldh, void* act, int* status, int max_ctas, cudaStream_t s,
+                               int group_m);
 
 cudaError_t rlb_gemm_grouped(int mode, int b_mn, int epi, int M, int N, int K, const void* A, long long lda,
                              const void* B, long long ldb, void* C, long long ldc, float alpha, int groups,

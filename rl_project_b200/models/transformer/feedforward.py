@@ -2,7 +2,8 @@
 
 ``SwiGLUFeedForward`` keeps the reference's ``w1``/``w2``/``w3`` parameters
 (checkpoint keys) but runs ``w1`` and ``w3`` as ONE GEMM over the
-concatenated weight, followed by the fused SwiGLU kernel.  The hidden width
+concatenated weight, followed by the fused SwiGLU kernel -- or, with the own GEMM enabled, as one GEMM
+whose epilogue applies the activation.  The hidden width
 is ``hidden_dim`` (``ModelSpec.d_ff``) or the reference's derived width.
 """
 
@@ -14,6 +15,7 @@ import torch
 import torch.nn as nn
 
 from rl_project_b200.core.config import ModelSpec
+from rl_project_b200.ops import gemm
 from rl_project_b200.ops.activation import gelu_tanh, swiglu
 from rl_project_b200.ops.linear import linear
 
@@ -42,8 +44,11 @@ class SwiGLUFeedForward(nn.Module):
             from rl_project_b200.parallel.tensor_parallel import column_parallel_in, copy_to_tp, row_parallel_out
         if self._fusable():
             w13 = torch.cat([self.w1.weight, self.w3.weight], dim=0)
-            h13 = column_parallel_in(x, w13, None, self.tp_group) if self.tp_group is not None else linear(x, w13)
-            a = swiglu(h13)
+            if self.tp_group is None and x.is_cuda and gemm.swiglu_fusable(x.reshape(-1, x.shape[-1]), w13):
+                a = gemm.linear_swiglu(x, w13)  # activation in the GEMM epilogue
+            else:
+                h13 = column_parallel_in(x, w13, None, self.tp_group) if self.tp_group is not None else linear(x, w13)
+                a = swiglu(h13)
         else:  # adapters wrap w1/w3: run them as modules
             if self.tp_group is not None:
                 x = copy_to_tp(x, self.tp_group)

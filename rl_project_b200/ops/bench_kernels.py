@@ -1,6 +1,7 @@
 """Kernel micro-benchmarks (CUDA-event timing after warm-up, L2 flushed between timed calls).
 
     python -m rl_project_b200.ops.bench_kernels [--which gemm,mem,adam,paged]
+    python -m rl_project_b200.ops.bench_kernels --which gemm_sustained,swiglu   (power-capped GEMM comparison)
 
 Prints one JSON line per case with the achieved TFLOP/s or GB/s and the
 fraction of the measured peaks in MEASURED_PEAKS.json ("of measured").
@@ -349,6 +350,92 @@ def bench_decode_graphs(batch: int = 64, prompt: int = 256, new: int = 128):
           flush=True)
 
 
+def _sustained(fn, seconds: float):
+    """Mean ms per call over a back-to-back loop of ``seconds`` (the GPU settles under its power cap), with the
+    median SM clock (MHz) and power (W) that ``nvidia-smi`` sampled during the last three quarters of it."""
+    import subprocess
+    import time
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    smi = subprocess.Popen(["nvidia-smi", "--query-gpu=clocks.sm,power.draw", "--format=csv,noheader,nounits",
+                            "-lms", "100", "-i", str(torch.cuda.current_device())], stdout=subprocess.PIPE, text=True)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n, t0 = 0, time.time()
+    a.record()
+    while time.time() - t0 < seconds:
+        for _ in range(4):
+            fn()
+        n += 4
+        torch.cuda.synchronize()
+    b.record()
+    torch.cuda.synchronize()
+    smi.terminate()
+    rows = [ln.split(",") for ln in smi.communicate()[0].strip().splitlines() if ln.strip()]
+    rows = rows[len(rows) // 4:]
+    med = lambda xs: sorted(xs)[len(xs) // 2] if xs else 0.0  # noqa: E731
+    return a.elapsed_time(b) / n, med([float(r[0]) for r in rows]), med([float(r[1]) for r in rows])
+
+
+# every dense product of one dense-1B training step (8 x 4096 tokens): forward x W^T, input gradient dy W,
+# weight gradient dy^T x, for q|k|v, o, w1|w3, w2 and the LM head
+_T1B = 32768
+GEMM_1B_STEP = ([(_T1B, n, k, "nt") for n, k in ((3072, 2048), (2048, 2048), (16384, 2048), (2048, 8192), (128256, 2048))]
+                + [(_T1B, n, k, "nn") for n, k in ((2048, 3072), (2048, 2048), (2048, 16384), (8192, 2048), (2048, 128256))]
+                + [(m, n, _T1B, "tn") for m, n in ((3072, 2048), (2048, 2048), (16384, 2048), (2048, 8192), (128256, 2048))])
+
+
+def bench_gemm_sustained(shapes=GEMM_1B_STEP, seconds: float = 2.0):
+    """Own 2-SM GEMM (the layers' tile / raster / K-split choices) against cuBLAS, each run back to back for
+    ``seconds`` so both settle under the 1 kW power cap as they do inside a training step: a kernel that
+    needs more energy per FLOP shows it as a lower sustained clock."""
+    from rl_project_b200.ops import gemm
+
+    for (M, N, K, kind) in shapes:
+        g = torch.Generator(device="cuda").manual_seed(0)
+        if kind == "nt":
+            a = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+            b = torch.randn(N, K, device="cuda", generator=g).to(torch.bfloat16)
+            ours, ref = (lambda: gemm.gemm_nt(a, b)), (lambda: a @ b.t())
+        elif kind == "nn":
+            a = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+            b = torch.randn(K, N, device="cuda", generator=g).to(torch.bfloat16)
+            ours, ref = (lambda: gemm.gemm_nn(a, b)), (lambda: a @ b)
+        else:
+            a = torch.randn(K, M, device="cuda", generator=g).to(torch.bfloat16)
+            b = torch.randn(K, N, device="cuda", generator=g).to(torch.bfloat16)
+            ours, ref = (lambda: gemm.gemm_tn(a, b)), (lambda: a.t() @ b)
+        fl = 2.0 * M * N * K
+        (t_o, c_o, p_o), (t_r, c_r, p_r) = _sustained(ours, seconds), _sustained(ref, seconds)
+        print(json.dumps({"kernel": "gemm2sm_sustained", "layout": kind, "M": M, "N": N, "K": K,
+                          "ms": round(t_o, 4), "tflops": round(fl / t_o / 1e9, 1), "sm_mhz": c_o, "power_w": p_o,
+                          "cublas_ms": round(t_r, 4), "cublas_tflops": round(fl / t_r / 1e9, 1), "cublas_sm_mhz": c_r,
+                          "cublas_power_w": p_r, "speedup_vs_cublas": round(t_r / t_o, 3)}), flush=True)
+        del a, b
+        torch.cuda.empty_cache()
+
+
+def bench_swiglu_gemm(M: int = 32768, H: int = 8192, K: int = 2048):
+    """Gated-FFN projection with the SwiGLU activation in the GEMM epilogue against the same GEMM followed by the
+    standalone activation kernel (L2 flushed between timed calls)."""
+    from rl_project_b200.ops import gemm
+    from rl_project_b200.ops._ext import native
+
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    w13 = (torch.randn(2 * H, K, device="cuda") / K ** 0.5).to(torch.bfloat16)
+    h13 = gemm.gemm_nt(x, w13)
+    t_f = time_ms(lambda: gemm.gemm_nt_swiglu(x, w13))
+    t_g = time_ms(lambda: gemm.gemm_nt(x, w13))
+    t_a = time_ms(lambda: native().swiglu_fwd(h13))
+    fl = 2.0 * M * 2 * H * K
+    peak_tf, _ = _peaks()
+    print(json.dumps({"kernel": "gemm2sm_swiglu", "M": M, "H": H, "K": K, "fused_ms": round(t_f, 4),
+                      "fused_tflops": round(fl / t_f / 1e9, 1), "frac_of_measured_bf16": round(fl / t_f / 1e9 / peak_tf, 3),
+                      "gemm_ms": round(t_g, 4), "activation_ms": round(t_a, 4),
+                      "speedup_vs_unfused": round((t_g + t_a) / t_f, 3)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--which", default="gemm,mem,adam,paged,sample")
@@ -376,6 +463,12 @@ def main():
         bench_nf4()
     if "decode" in which:
         bench_decode_graphs()
+    if "gemm_sustained" in which:
+        bench_gemm_sustained()
+    if "swiglu" in which:
+        bench_swiglu_gemm()
+    if "swiglu_small" in which:  # profiling case
+        bench_swiglu_gemm(M=4096)
     if "attn1" in which:  # one small case (profiling)
         bench_attention(((2, 2048, 32, 8, 64),))
 

@@ -8,12 +8,15 @@ without transposing anything:
 * weight grad  ``dW = dy^T x``   A = dy read MN-major,      B = x read MN-major
 
 ``RLB_GEMM`` selects the implementation of the model's plain linear layers:
-``cublas`` (torch.matmul; the default), ``tcgen05`` (this library's kernels), ``auto``
+``cublas`` (torch.matmul), ``tcgen05`` (this library's kernels), ``auto``
 (tcgen05 once the numerics self-check on the first call passed) or ``tuned``
 (per product shape, the fastest of the 2-SM kernel with 256 x 256 tiles, with
 256 x 512 tiles, and cuBLAS -- timed once with CUDA events on the first call of
 that shape; accumulating and graph-captured calls keep the per-shape default) or
-``hybrid`` (forward products on the 2-SM kernel, gradient products on cuBLAS).
+``hybrid`` (the default: forward products on the 2-SM kernel -- the gated FFN's projection with the
+SwiGLU activation in its epilogue -- and gradient products on cuBLAS) or ``fwd_dgrad`` (forward and
+input-gradient products on the 2-SM kernel, weight gradients on cuBLAS).  Products too small to give every
+CTA pair a tile (decode steps, short prefills) go to cuBLAS in every mode (``fills_gpu``).
 ``RLB_GEMM_KERNEL`` picks the kernel: ``2sm`` (default; CTA pairs issuing
 ``tcgen05.mma.cta_group::2`` on 256 x 256 tiles, TMA-store epilogue) or
 ``1sm`` (one CTA per 128 x 256 tile, register-to-global epilogue; the base of
@@ -29,11 +32,15 @@ import torch
 
 from rl_project_b200.ops._ext import available, native
 
-# plain dense layers default to cuBLAS: in the full 1B training step on B200 it measured 257-259 ms against
-# 272-275 ms with the own kernel (per-shape benches are within a few percent either way; see the GEMM notes)
-_MODE = os.environ.get("RLB_GEMM", "cublas")
+# default "hybrid": in the full 1B training step on B200 (alternating runs on one box) the own forward products
+# with the fused SwiGLU epilogue and cuBLAS gradients measured 259.9-263.0 ms against 261.4-262.6 ms for all-cuBLAS;
+# own input- and weight-gradient products still cost 1.5-4 % in the step under the power cap
+_MODE = os.environ.get("RLB_GEMM", "hybrid")
 _KERNEL = os.environ.get("RLB_GEMM_KERNEL", "2sm")
 _NSUB = int(os.environ.get("RLB_GEMM_NSUB", "0"))  # 0: per shape; 1: 256 x 256 tiles; 2: 256 x 512 tiles
+_GROUP_M = int(os.environ.get("RLB_GEMM_GROUP_M", "0"))  # raster group height in M tiles (0: kernel default)
+_SPLITK = os.environ.get("RLB_GEMM_SPLITK", "auto")  # "auto" | "off" | a fixed split count
+_MIN_TILES = int(os.environ.get("RLB_GEMM_MIN_TILES", "-1"))  # layers' own-kernel threshold (-1: one per CTA pair)
 _checked: dict = {}
 
 
@@ -48,14 +55,17 @@ def _pairs(device_index: int) -> int:
 
 def nsub_for(M: int, N: int, epi: int, device_index: int = 0, a_mn: int = 0) -> int:
     """Tile width of the 2-SM kernel for a product.  256 x 512 tiles (one A slice feeds two MMAs: a quarter
-    fewer operand bytes) unless the output is fp32, too narrow, A is read MN-major (the weight-gradient
-    layout, measured faster with 256 x 256 tiles and their double-buffered accumulators: 1.02x against 0.89x
-    of cuBLAS on the 1B model's 16384 x 2048 x 32768 weight gradient), or their last wave of CTA pairs would
-    leave clearly more of the GPU idle than 256 x 256 tiles do."""
+    fewer operand bytes per FLOP, which under the 1 kW power cap is a higher sustained clock) unless the output
+    is fp32 or too narrow.  Weight gradients (A read MN-major, long K) always take them: their wave
+    quantisation is evened out by splitting K (``k_splits``); sustained on B200 this measured 0.92-1.00x of
+    cuBLAS against 0.75-0.94x with 256 x 256 tiles on the 1B model's weight gradients.  For the other
+    layouts, 256 x 256 tiles when the last wave of 256 x 512 tiles would leave clearly more of the GPU idle."""
     if _NSUB:
         return _NSUB
-    if epi != 0 or N <= 256 or a_mn:
+    if epi != 0 or N <= 256:
         return 1
+    if a_mn:
+        return 2
     pairs = _pairs(device_index)
 
     def wave_fill(bn: int) -> float:
@@ -64,6 +74,43 @@ def nsub_for(M: int, N: int, epi: int, device_index: int = 0, a_mn: int = 0) -> 
         return tiles / (waves * pairs)
 
     return 2 if wave_fill(512) + 0.05 >= wave_fill(256) else 1
+
+
+def group_for(N: int, a_mn: int) -> int:
+    """Raster group height (M tiles walked before moving to the next N tile).  Wide outputs (N >= 8192: the
+    w1|w3 and LM-head forward, the w2 input gradient) walk 32 M tiles, so each B tile is read by all the CTA
+    pairs that need it while it is in L2 instead of being re-read from HBM for every group of 8; measured
+    under the power cap on B200 this lifted the LM-head forward from 0.96x to 1.00x of cuBLAS (and its SM
+    clock from 1267 to 1305 MHz).  Narrower outputs and weight gradients keep groups of 8."""
+    if _GROUP_M:
+        return _GROUP_M
+    return 32 if (N >= 8192 and not a_mn) else 8
+
+
+# per-unit cost of a K-split work unit beyond its MMAs (pipeline fill, accumulator drain), in 64-deep K slices
+_UNIT_OVERHEAD = 4.0
+
+
+def k_splits(M: int, N: int, K: int, nsub: int, device_index: int = 0) -> int:
+    """K ranges per output tile for a weight-gradient product (bf16 output): more than one when the tiles
+    alone would leave much of the last wave of CTA pairs idle and K is long enough to divide -- e.g. the
+    1B model's q|k|v weight gradient (3072 x 2048 over K = 32768: 96 tiles for 74 CTA pairs, two waves at
+    65 % occupancy) runs as three ranges of 170 K slices (288 units, 3.9 waves).  The model counts a unit as
+    its K slices plus a fixed overhead, and a split must save 6 % of it to pay for the fp32 partial sums'
+    zero fill and the final bf16 conversion."""
+    if _SPLITK == "off":
+        return 1
+    nk = -(-K // 64)
+    if _SPLITK != "auto":
+        return max(1, min(int(_SPLITK), nk))
+    pairs = _pairs(device_index)
+    tiles = -(-M // 256) * -(-N // (256 * nsub))
+
+    def cost(sp: int) -> float:
+        return -(-tiles * sp // pairs) * (nk / sp + _UNIT_OVERHEAD)
+
+    best = min((sp for sp in range(1, 9) if sp == 1 or nk // sp >= 16), key=cost)
+    return best if cost(best) < 0.94 * cost(1) else 1
 
 
 def _describe(t: torch.Tensor) -> str:
@@ -84,7 +131,8 @@ def _launch(choice: str, a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alp
         rhs = b if b_mn else b.t()
         torch.matmul(lhs, rhs, out=out)
         return
-    native().gemm2(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None, 0, 2 if choice == "own2" else 1)
+    native().gemm2x(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None, 0, 2 if choice == "own2" else 1,
+                    1, group_for(N, a_mn))
 
 
 def _candidates(epi: int, alpha: float, N: int, ldc: int):
@@ -139,8 +187,16 @@ def _run(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha):
                 if key not in _TUNED:  # not timed (graph capture, accumulation): the per-shape default
                     _launch(choice, a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha)
         else:
-            native().gemm2(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None, 0,
-                           nsub_for(M, N, epi, a.device.index or 0, a_mn))
+            nsub = nsub_for(M, N, epi, a.device.index or 0, a_mn)
+            splits = k_splits(M, N, K, nsub, a.device.index or 0) if (a_mn and epi == 0) else 1
+            if splits > 1:  # partial products reduce-added into fp32, then rounded once to bf16
+                acc = torch.zeros(M, N, dtype=torch.float32, device=a.device)
+                native().gemm2x(a, b, acc, a_mn, b_mn, 2, M, N, K, lda, ldb, N, alpha, None, 0, nsub, splits,
+                                group_for(N, a_mn))
+                out.copy_(acc)
+            else:
+                native().gemm2x(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None, 0, nsub, 1,
+                                group_for(N, a_mn))
     except RuntimeError as e:
         raise RuntimeError(f"{e} [a_mn={a_mn} b_mn={b_mn} epi={epi} M={M} N={N} K={K} lda={lda} ldb={ldb} "
                            f"ldc={ldc}; A {_describe(a)}; B {_describe(b)}; C {_describe(out)}; current device "
@@ -213,11 +269,59 @@ class _Linear(torch.autograd.Function):
     def backward(ctx, dy):
         x2, w = ctx.saved_tensors
         dy = _dense(dy)
-        if not backward_own():  # "hybrid": the gradient products go to cuBLAS
-            return (dy @ w if ctx.needs_input_grad[0] else None, dy.t() @ x2 if ctx.needs_input_grad[1] else None)
-        dx = gemm_nn(dy, w) if ctx.needs_input_grad[0] else None
-        dw = gemm_tn(dy, x2) if ctx.needs_input_grad[1] else None
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm_nn(dy, w) if dgrad_own() else dy @ w
+        if ctx.needs_input_grad[1]:
+            dw = gemm_tn(dy, x2) if wgrad_own() else dy.t() @ x2
         return dx, dw
+
+
+def gemm_nt_swiglu(x2: torch.Tensor, w13: torch.Tensor):
+    """``h13 = x2 w13^T`` for ``w13 = [W1; W3]`` and ``act = silu(h13[:, :H]) * h13[:, H:]`` from one GEMM whose
+    epilogue applies the activation (256 x 512 tiles pairing the gate and up columns of 256 hidden units)."""
+    x2, w13 = _dense(x2), _dense(w13)
+    M, H = x2.shape[0], w13.shape[0] // 2
+    h13 = torch.empty(M, 2 * H, dtype=torch.bfloat16, device=x2.device)
+    act = torch.empty(M, H, dtype=torch.bfloat16, device=x2.device)
+    native().gemm2_swiglu(x2, w13, h13, act, group_for(2 * H, 0))
+    return h13, act
+
+
+class _LinearSwiGLU(torch.autograd.Function):
+    """Gated FFN input projection + activation: forward in one GEMM (activation in its epilogue); backward
+    through the activation kernel and the linear layer's two gradient products."""
+
+    @staticmethod
+    def forward(ctx, x2, w13):
+        h13, act = gemm_nt_swiglu(x2, w13)
+        ctx.save_for_backward(x2, w13, h13)
+        return act
+
+    @staticmethod
+    def backward(ctx, da):
+        x2, w13, h13 = ctx.saved_tensors
+        dh13 = native().swiglu_bwd(h13, _dense(da))
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm_nn(dh13, w13) if dgrad_own() else dh13 @ w13
+        if ctx.needs_input_grad[1]:
+            dw = gemm_tn(dh13, x2) if wgrad_own() else dh13.t() @ x2
+        return dx, dw
+
+
+def swiglu_fusable(x2: torch.Tensor, w13: torch.Tensor) -> bool:
+    return (enabled() and _MODE != "tuned" and x2.dtype == torch.bfloat16 and w13.dtype == torch.bfloat16
+            and x2.dim() == 2 and x2.shape[0] > 0 and (w13.shape[0] // 2) % 8 == 0 and w13.shape[0] % 2 == 0
+            and x2.shape[1] % 8 == 0 and _ok_ptr(x2) and _ok_ptr(w13)
+            and fills_gpu(x2.shape[0], w13.shape[0] // 2, 256, x2.device.index or 0))
+
+
+def linear_swiglu(x: torch.Tensor, w13: torch.Tensor) -> torch.Tensor:
+    """``silu(x W1^T) * (x W3^T)`` for ``w13 = [W1; W3]``; the activation is fused into the GEMM epilogue."""
+    shape = x.shape
+    act = _LinearSwiGLU.apply(x.reshape(-1, shape[-1]), w13)
+    return act.view(*shape[:-1], w13.shape[0] // 2)
 
 
 def _self_check(device: torch.device) -> bool:
@@ -233,21 +337,40 @@ def _self_check(device: torch.device) -> bool:
 
 
 def enabled() -> bool:
-    return available() and _MODE in ("tcgen05", "auto", "tuned", "hybrid")
+    return available() and _MODE in ("tcgen05", "auto", "tuned", "hybrid", "fwd_dgrad")
+
+
+def dgrad_own() -> bool:
+    """Whether input-gradient products (``dy W``) run the own kernel: every enabled mode except ``hybrid``."""
+    return enabled() and _MODE != "hybrid"
+
+
+def wgrad_own() -> bool:
+    """Whether weight-gradient products (``dy^T x``) run the own kernel: not under ``hybrid`` (all gradient
+    products on cuBLAS) nor ``fwd_dgrad`` (forward and input gradients on the own kernel, weight gradients --
+    the MN-major x MN-major layout where it is furthest behind cuBLAS under the power cap -- on cuBLAS)."""
+    return enabled() and _MODE not in ("hybrid", "fwd_dgrad")
 
 
 def backward_own() -> bool:
-    """Whether the input- and weight-gradient products of the own linear layers run the own kernel too
-    (every enabled mode except ``hybrid``, which keeps the forward on it and sends the gradients to cuBLAS)."""
-    return enabled() and _MODE != "hybrid"
+    """Whether every gradient product runs the own kernel."""
+    return dgrad_own() and wgrad_own()
+
+
+def fills_gpu(M: int, N: int, tile_n: int, device_index: int = 0) -> bool:
+    """Whether a product has at least one 256 x ``tile_n`` output tile per CTA pair (``RLB_GEMM_MIN_TILES``
+    overrides the count).  Smaller products -- decode steps, short prefills -- would leave most of the GPU
+    idle on the persistent 2-SM kernel, so the layers send them to cuBLAS."""
+    need = _MIN_TILES if _MIN_TILES >= 0 else _pairs(device_index)
+    return -(-M // 256) * -(-N // tile_n) >= need
 
 
 def supported(a: torch.Tensor, b: torch.Tensor) -> bool:
     if not enabled() or a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16 or a.dim() != 2:
         return False
-    if not _shape_ok(a, b):
+    if not _shape_ok(a, b) or not fills_gpu(a.shape[0], b.shape[0], 512, a.device.index or 0):
         return False
-    return _MODE in ("tcgen05", "tuned", "hybrid") or _self_check(a.device)
+    return _MODE in ("tcgen05", "tuned", "hybrid", "fwd_dgrad") or _self_check(a.device)
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -2,9 +2,9 @@
 
 ``linear`` (every linear layer, with its backward) and ``matmul_nt`` /
 ``matmul_nn`` / ``matmul_tn`` (the LM head's products) run this library's
-tcgen05 GEMM (csrc/gemm_2sm.cu) on sm_100a when ``RLB_GEMM=tcgen05``; by default
-(``RLB_GEMM=cublas``) they are plain cuBLAS products, which measured faster in the full
-training step.
+tcgen05 GEMM (csrc/gemm_2sm.cu) on sm_100a as ``RLB_GEMM`` selects: by default
+(``hybrid``) the forward products run the own kernel and the gradient products
+cuBLAS; ``tcgen05`` runs all of them on the own kernel, ``cublas`` none.
 """
 
 from __future__ import annotations
@@ -32,15 +32,11 @@ def matmul_nt(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return a @ b.t()
 
 
-def _own_grad(a: torch.Tensor, b: torch.Tensor) -> bool:
+def matmul_nn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """``a [M, K] @ b [K, N]`` (b read as stored; the LM head's input gradient)."""
     from rl_project_b200.ops import gemm
 
-    return _own(a, b) and gemm.backward_own()
-
-
-def matmul_nn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """``a [M, K] @ b [K, N]`` (b read as stored; a gradient product of the LM head)."""
-    if _own_grad(a, b):
+    if _own(a, b) and gemm.dgrad_own():
         from rl_project_b200.ops import gemm
 
         return gemm.gemm_nn(a, b)
@@ -48,8 +44,10 @@ def matmul_nn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
 
 
 def matmul_tn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """``a [K, M]^T @ b [K, N]`` (both read as stored; a gradient product of the LM head)."""
-    if _own_grad(a, b):
+    """``a [K, M]^T @ b [K, N]`` (both read as stored; the LM head's weight gradient)."""
+    from rl_project_b200.ops import gemm
+
+    if _own(a, b) and gemm.wgrad_own():
         from rl_project_b200.ops import gemm
 
         return gemm.gemm_tn(a, b)
