@@ -445,7 +445,8 @@ void gemm2(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t a_
 
 // x [M][K] times w13 = [W1; W3] ([2H][K]) with the SwiGLU activation fused into the epilogue: writes the
 // projection h13 [M][2H] and the activation act [M][H].
-void gemm2_swiglu(const at::Tensor& X, const at::Tensor& W13, at::Tensor& h13, at::Tensor& act, int64_t group_m) {
+void gemm2_swiglu(const at::Tensor& X, const at::Tensor& W13, at::Tensor& h13, at::Tensor& act, int64_t group_m,
+                  int64_t max_ctas) {
   check_bf16(X, "x");
   check_bf16(W13, "w13");
   check_bf16(h13, "h13");
@@ -462,7 +463,8 @@ void gemm2_swiglu(const at::Tensor& X, const at::Tensor& W13, at::Tensor& h13, a
               "gemm2_swiglu: output shapes");
   const c10::cuda::CUDAGuard g(X.device());
   CHECK_OK(rlb_gemm2sm_swiglu((int)M, (int)H, (int)K, X.data_ptr(), X.stride(0), W13.data_ptr(), W13.stride(0),
-                              h13.data_ptr(), h13.stride(0), act.data_ptr(), nullptr, 0, cur_stream(), (int)group_m),
+                              h13.data_ptr(), h13.stride(0), act.data_ptr(), nullptr, (int)max_ctas, cur_stream(),
+                              (int)group_m),
            "gemm2_swiglu");
 }
 

@@ -41,6 +41,7 @@ _NSUB = int(os.environ.get("RLB_GEMM_NSUB", "0"))  # 0: per shape; 1: 256 x 256 
 _GROUP_M = int(os.environ.get("RLB_GEMM_GROUP_M", "0"))  # raster group height in M tiles (0: kernel default)
 _SPLITK = os.environ.get("RLB_GEMM_SPLITK", "auto")  # "auto" | "off" | a fixed split count
 _MIN_TILES = int(os.environ.get("RLB_GEMM_MIN_TILES", "-1"))  # layers' own-kernel threshold (-1: one per CTA pair)
+_MAX_CTAS = int(os.environ.get("RLB_GEMM_MAX_CTAS", "0"))  # cap on the persistent grid (0: every SM)
 _checked: dict = {}
 
 
@@ -131,7 +132,7 @@ def _launch(choice: str, a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alp
         rhs = b if b_mn else b.t()
         torch.matmul(lhs, rhs, out=out)
         return
-    native().gemm2x(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None, 0, 2 if choice == "own2" else 1,
+    native().gemm2x(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None, _MAX_CTAS, 2 if choice == "own2" else 1,
                     1, group_for(N, a_mn))
 
 
@@ -191,11 +192,11 @@ def _run(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha):
             splits = k_splits(M, N, K, nsub, a.device.index or 0) if (a_mn and epi == 0) else 1
             if splits > 1:  # partial products reduce-added into fp32, then rounded once to bf16
                 acc = torch.zeros(M, N, dtype=torch.float32, device=a.device)
-                native().gemm2x(a, b, acc, a_mn, b_mn, 2, M, N, K, lda, ldb, N, alpha, None, 0, nsub, splits,
+                native().gemm2x(a, b, acc, a_mn, b_mn, 2, M, N, K, lda, ldb, N, alpha, None, _MAX_CTAS, nsub, splits,
                                 group_for(N, a_mn))
                 out.copy_(acc)
             else:
-                native().gemm2x(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None, 0, nsub, 1,
+                native().gemm2x(a, b, out, a_mn, b_mn, epi, M, N, K, lda, ldb, ldc, alpha, None, _MAX_CTAS, nsub, 1,
                                 group_for(N, a_mn))
     except RuntimeError as e:
         raise RuntimeError(f"{e} [a_mn={a_mn} b_mn={b_mn} epi={epi} M={M} N={N} K={K} lda={lda} ldb={ldb} "
@@ -284,7 +285,7 @@ def gemm_nt_swiglu(x2: torch.Tensor, w13: torch.Tensor):
     M, H = x2.shape[0], w13.shape[0] // 2
     h13 = torch.empty(M, 2 * H, dtype=torch.bfloat16, device=x2.device)
     act = torch.empty(M, H, dtype=torch.bfloat16, device=x2.device)
-    native().gemm2_swiglu(x2, w13, h13, act, group_for(2 * H, 0))
+    native().gemm2_swiglu(x2, w13, h13, act, group_for(2 * H, 0), _MAX_CTAS)
     return h13, act
 
 
