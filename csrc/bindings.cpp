@@ -297,6 +297,36 @@ std::vector<at::Tensor> logprob_fwd(const at::Tensor& logits, const c10::optiona
   return {lse, lp};
 }
 
+// lse / lp (/ entropy) of each row from the LM-head GEMM's per-chunk statistics (gemm2_lse).
+std::vector<at::Tensor> logprob_combine(const at::Tensor& stats, const at::Tensor& logits,
+                                        const c10::optional<at::Tensor>& targets, bool with_entropy,
+                                        const c10::optional<at::Tensor>& status) {
+  check_bf16(logits, "logits");
+  check_dev(stats, logits, "stats");
+  check_dev(targets, logits, "targets");
+  check_dev(status, logits, "status");
+  TORCH_CHECK(stats.scalar_type() == at::kFloat && stats.dim() == 3 && stats.size(2) == 4 && stats.is_contiguous() &&
+              stats.size(0) == logits.size(0), "stats must be fp32 [rows, chunks, 4]");
+  const c10::cuda::CUDAGuard g(logits.device());
+  const long long rows = logits.size(0);
+  auto fopt = logits.options().dtype(at::kFloat);
+  auto lse = at::empty({rows}, fopt);
+  auto lp = at::empty({rows}, fopt);
+  at::Tensor ent = with_entropy ? at::empty({rows}, fopt) : at::Tensor();
+  const long long* tg = nullptr;
+  if (targets.has_value()) {
+    TORCH_CHECK(targets->scalar_type() == at::kLong && targets->is_contiguous(), "targets must be contiguous int64");
+    tg = lptr(*targets);
+  }
+  CHECK_OK(rlb_logprob_combine(stats.data_ptr(), (int)stats.size(1), logits.data_ptr(), logits.stride(0), rows,
+                               (int)logits.size(1), tg, lse.data_ptr<float>(), lp.data_ptr<float>(),
+                               with_entropy ? ent.data_ptr<float>() : nullptr,
+                               status.has_value() ? status->data_ptr<int>() : nullptr, cur_stream()),
+           "logprob_combine");
+  if (with_entropy) return {lse, lp, ent};
+  return {lse, lp};
+}
+
 void logprob_bwd_(at::Tensor& logits, const c10::optional<at::Tensor>& targets, const at::Tensor& lse,
                   const c10::optional<at::Tensor>& g_lp, const c10::optional<at::Tensor>& ent,
                   const c10::optional<at::Tensor>& g_ent, double scale) {
@@ -466,6 +496,29 @@ void gemm2_swiglu(const at::Tensor& X, const at::Tensor& W13, at::Tensor& h13, a
                               h13.data_ptr(), h13.stride(0), act.data_ptr(), nullptr, (int)max_ctas, cur_stream(),
                               (int)group_m),
            "gemm2_swiglu");
+}
+
+// LM-head forward with the row statistics in the epilogue: logits [M][N] bf16 and stats [M][2 * ceil(N / 512)][4]
+// fp32 (max, sum exp, sum exp * x, unused).
+void gemm2_lse(const at::Tensor& A, const at::Tensor& B, at::Tensor& logits, at::Tensor& stats, int64_t group_m,
+               int64_t max_ctas) {
+  check_bf16(A, "h");
+  check_bf16(B, "W");
+  check_bf16(logits, "logits");
+  check_dev(B, A, "W");
+  check_dev(logits, A, "logits");
+  check_dev(stats, A, "stats");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1) && A.stride(1) == 1 && B.stride(1) == 1,
+              "gemm2_lse: h [M, K] and W [N, K] with contiguous rows expected");
+  const int64_t M = A.size(0), N = B.size(0), K = A.size(1);
+  TORCH_CHECK(logits.size(0) == M && logits.size(1) == N && logits.stride(1) == 1, "gemm2_lse: logits shape");
+  TORCH_CHECK(stats.scalar_type() == at::kFloat && stats.is_contiguous() && stats.numel() == M * 2 * ((N + 511) / 512) * 4,
+              "gemm2_lse: stats must be fp32 [M, 2 * ceil(N / 512), 4]");
+  const c10::cuda::CUDAGuard g(A.device());
+  CHECK_OK(rlb_gemm2sm_lse((int)M, (int)N, (int)K, A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0),
+                           logits.data_ptr(), logits.stride(0), stats.data_ptr(), nullptr, (int)max_ctas, cur_stream(),
+                           (int)group_m),
+           "gemm2_lse");
 }
 
 // Grouped GEMM (mixture-of-experts): see rlb_gemm_grouped for the two modes.
@@ -883,6 +936,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm2", &gemm2);
   m.def("gemm2x", &gemm2x);
   m.def("gemm2_swiglu", &gemm2_swiglu);
+  m.def("gemm2_lse", &gemm2_lse);
+  m.def("logprob_combine", &logprob_combine);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("fmha_fwd", &fmha_fwd);

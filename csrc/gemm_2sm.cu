@@ -72,7 +72,11 @@ struct Cfg {
 // tile holds the gate and up columns of the same 256 hidden units (its two 256-column sub-tiles read W1 rows
 // h.. and W3 rows H + h..); the epilogue stores both into h13 (kept for the backward) and silu(gate) * up,
 // computed from their bf16 values as the standalone activation kernel does, into the activation output.
-enum Epi : int { kStoreBF16 = 0, kStoreF32 = 1, kAccumF32 = 2, kSwiGLU = 3 };
+// kLogitsLSE: LM-head forward.  Stores the bf16 logits as kStoreBF16 does and, per row and per 256-column
+// half tile, the running statistics of its bf16 values -- max m, sum exp(x - m) and sum exp(x - m) * x -- into
+// `lse_stats` ([M][2 * tiles_n] float4), from which one small pass gets each row's log-sum-exp, target
+// log-prob and entropy without reading the logits again.
+enum Epi : int { kStoreBF16 = 0, kStoreF32 = 1, kAccumF32 = 2, kSwiGLU = 3, kLogitsLSE = 4 };
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
 
@@ -84,6 +88,7 @@ struct Params {
   int* status;
   float* c32;     // kAccumF32: C itself, for the ragged edge chunks the threads accumulate directly
   long long ldc;
+  float4* lse_stats;  // kLogitsLSE: [M][2 * ceil(N / 512)] per-half-tile row statistics
 };
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group_m, int& m, int& n) {
@@ -144,6 +149,7 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
   const uint32_t rank = sm100::cluster_ctarank();  // 0: the CTA that issues the pair MMAs
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   static_assert(EPI != kSwiGLU || (NSUB == 2 && A_MN == 0 && B_MN == 0), "SwiGLU epilogue: forward, 256 x 512");
+  static_assert(EPI != kLogitsLSE || (NSUB == 2 && A_MN == 0 && B_MN == 0), "LSE epilogue: forward, 256 x 512");
   constexpr int TN = EPI == kSwiGLU ? SUBN : BN;  // output columns (hidden units for kSwiGLU) per tile
   const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + TN - 1) / TN;
   const int num_tiles = num_m * num_n;
@@ -383,7 +389,7 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
       }
       sm100::tc_fence_after();
       const uint32_t lanes = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-      if constexpr ((EPI == kStoreBF16 || EPI == kSwiGLU) && NSUB == 2) {
+      if constexpr ((EPI == kStoreBF16 || EPI == kSwiGLU || EPI == kLogitsLSE) && NSUB == 2) {
         // read this warp's 128 columns of sub-tile 0, hand sub-tile 0 back (the next tile's first MMAs may
         // start), then its 128 columns of sub-tile 1 and hand those back; all kept as packed bf16 in registers
         uint32_t pk[2][64];
@@ -402,6 +408,43 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
           sm100::tc_fence_before();
           __syncwarp();
           if (lane == 0) sm100::mbar_arrive_cluster(tempty0 + (uint32_t)sb * 8u);
+        }
+        if constexpr (EPI == kLogitsLSE) {
+          // statistics of this row's 256 columns of the tile (128 per sub-tile), from the stored bf16 values:
+          // one pass, folding 16 values at a time into the running max / sums with one rescale per group
+          float m = -INFINITY, se = 0.f, te = 0.f;
+#pragma unroll
+          for (int sb = 0; sb < 2; ++sb) {
+#pragma unroll
+            for (int g8 = 0; g8 < 8; ++g8) {
+              const int col = tn * BN + sb * SUBN + half * 128 + g8 * 16;  // first column of the group
+              float x[16];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const uint32_t w = pk[sb][g8 * 8 + e];
+                x[2 * e] = col + 2 * e < p.N ? __uint_as_float(w << 16) : -INFINITY;
+                x[2 * e + 1] = col + 2 * e + 1 < p.N ? __uint_as_float(w & 0xffff0000u) : -INFINITY;
+              }
+              float gm = x[0];
+#pragma unroll
+              for (int e = 1; e < 16; ++e) gm = fmaxf(gm, x[e]);
+              if (gm != -INFINITY) {
+                const float mn = fmaxf(m, gm);
+                const float f = __expf(m - mn);  // 0 while m is -inf
+                se *= f;
+                te *= f;
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                  const float ex = __expf(x[e] - mn);  // 0 for masked columns
+                  se += ex;
+                  te += x[e] == -INFINITY ? 0.f : ex * x[e];
+                }
+                m = mn;
+              }
+            }
+          }
+          const int row = row0 + lane;
+          if (row < p.M) p.lse_stats[(long long)row * (2 * num_n) + 2 * tn + half] = make_float4(m, se, te, 0.f);
         }
         // kSwiGLU: out 0 / 1 are the gate / up halves of h13 (maps c, c2), out 2 the activation (map c3)
         constexpr int NOUT = EPI == kSwiGLU ? 3 : 2;
@@ -597,7 +640,7 @@ static cudaError_t launch(const void* A, long long lda, const void* B, long long
            make_map(&mc2, bf, 2, (const __nv_bfloat16*)Cp + p.N, p.M, p.N, ldc, 64, 32) &&
            make_map(&mc3, bf, 2, act, p.M, p.N, p.N, 64, 32);
   } else {
-    ok_c = EPI == kStoreBF16 ? make_map(&mc, bf, 2, Cp, p.M, p.N, ldc, 64, 32)
+    ok_c = (EPI == kStoreBF16 || EPI == kLogitsLSE) ? make_map(&mc, bf, 2, Cp, p.M, p.N, ldc, 64, 32)
                              : make_map(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Cp, p.M, p.N, ldc, 32, 32);
     mc2 = mc;
     mc3 = mc;
@@ -701,4 +744,28 @@ cudaError_t rlb_gemm2sm_swiglu(int M, int H, int K, const void* X, long long ldx
   p.c32 = nullptr;
   p.ldc = ldh;
   return launch<0, 0, kSwiGLU, 2>(X, ldx, W13, ldw, H13, ldh, p, max_ctas, s, act);
+}
+
+// LM-head forward on the 2-SM kernel: logits = h [M][K] * W^T (W [N][K]) stored bf16 (row pitch ldc), plus
+// per row and per 256-column half tile the statistics (max, sum exp(x - max), sum exp(x - max) * x) of the
+// stored bf16 values in stats [M][2 * ceil(N / 512)] (float4, fourth lane unused).
+cudaError_t rlb_gemm2sm_lse(int M, int N, int K, const void* A, long long lda, const void* B, long long ldb,
+                            void* C, long long ldc, void* stats, int* status, int max_ctas, cudaStream_t s,
+                            int group_m) {
+  using namespace gemm2;
+  if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+  if ((lda % 8) || (ldb % 8) || (ldc % 8)) return cudaErrorInvalidPitchValue;
+  if ((((uintptr_t)A) | ((uintptr_t)B) | ((uintptr_t)C) | ((uintptr_t)stats)) & 15) return cudaErrorInvalidDevicePointer;
+  Params p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.splits = 1;
+  p.group_m = group_m < 1 ? GROUP_M : group_m;
+  p.alpha = 1.f;
+  p.status = status;
+  p.c32 = nullptr;
+  p.ldc = ldc;
+  p.lse_stats = (float4*)stats;
+  return launch<0, 0, kLogitsLSE, 2>(A, lda, B, ldb, C, ldc, p, max_ctas, s);
 }

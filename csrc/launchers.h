@@ -65,6 +65,14 @@ cudaError_t rlb_gemm2sm_swiglu(int M, int H, int K, const void* X, long long ldx
                                void* H13, long long ldh, void* act, int* status, int max_ctas, cudaStream_t s,
                                int group_m);
 
+// LM-head forward with per-row statistics of each 256-column half tile in the epilogue (see gemm_2sm.cu).
+cudaError_t rlb_gemm2sm_lse(int M, int N, int K, const void* A, long long lda, const void* B, long long ldb,
+                            void* C, long long ldc, void* stats, int* status, int max_ctas, cudaStream_t s,
+                            int group_m);
+// Row log-sum-exp / target log-prob / entropy from those statistics (logprob.cu).
+cudaError_t rlb_logprob_combine(const void* stats, int chunks, const void* logits, long long ld, long long rows, int V,
+                                const long long* tgt, float* lse, float* lp, float* ent, int* status, cudaStream_t s);
+
 cudaError_t rlb_gemm_grouped(int mode, int b_mn, int epi, int M, int N, int K, const void* A, long long lda,
                              const void* B, long long ldb, void* C, long long ldc, float alpha, int groups,
                              const int* tile_group, const int* k_begin, const int* k_len, long long k_total,

@@ -96,6 +96,43 @@ __global__ void __launch_bounds__(THREADS) logprob_fwd_kernel(
   }
 }
 
+// Log-sum-exp, target log-prob and entropy of each row from per-chunk statistics {max, sum exp(x - max),
+// sum exp(x - max) * x} that the LM-head GEMM's epilogue wrote ([rows][chunks] float4): one warp per row
+// merges its chunks (the online merge above), then reads the target's bf16 logit.  Same outputs as
+// logprob_fwd_kernel, without a pass over the logits.
+__global__ void logprob_combine_kernel(const float4* __restrict__ stats, int chunks, const __nv_bfloat16* __restrict__ logits,
+                                       long long ld, int V, long long rows, const long long* __restrict__ tgt,
+                                       float* __restrict__ lse_out, float* __restrict__ lp_out,
+                                       float* __restrict__ ent_out, int* status) {
+  const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  OnlineStats st{-INFINITY, 0.f, 0.f};
+  const float4* row = stats + r * chunks;
+  for (int i = lane; i < chunks; i += 32) {
+    const float4 c = row[i];
+    st = online_merge(st, OnlineStats{c.x, c.y, c.z});
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    OnlineStats other{__shfl_xor_sync(0xffffffffu, st.m, o), __shfl_xor_sync(0xffffffffu, st.s, o),
+                      __shfl_xor_sync(0xffffffffu, st.t, o)};
+    st = online_merge(st, other);
+  }
+  if (lane == 0) {
+    const float lse = st.m + logf(st.s);
+    lse_out[r] = lse;
+    const long long tg = tgt ? tgt[r] : -1;
+    float lp = 0.f;
+    if (tg >= 0) {
+      if (tg < V) lp = __bfloat162float(logits[r * ld + tg]) - lse;
+      else report(status, kBadIndex);
+    }
+    if (lp_out) lp_out[r] = lp;
+    if (ent_out) ent_out[r] = lse - st.t / st.s;
+  }
+}
+
 template <int THREADS>
 __global__ void __launch_bounds__(THREADS) logprob_bwd_kernel(
     __nv_bfloat16* __restrict__ logits, long long ld, int V, const long long* __restrict__ tgt,
@@ -148,6 +185,15 @@ cudaError_t rlb_logprob_fwd(const void* logits, long long ld, long long rows, in
   if (rows == 0) return cudaSuccess;
   logprob_fwd_kernel<512><<<(unsigned)rows, 512, 0, s>>>((const __nv_bfloat16*)logits, ld, V, tgt, lse, lp, ent,
                                                          status);
+  return cudaGetLastError();
+}
+
+cudaError_t rlb_logprob_combine(const void* stats, int chunks, const void* logits, long long ld, long long rows, int V,
+                                const long long* tgt, float* lse, float* lp, float* ent, int* status, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  const int warps = 8;
+  logprob_combine_kernel<<<(unsigned)((rows + warps - 1) / warps), 32 * warps, 0, s>>>(
+      (const float4*)stats, chunks, (const __nv_bfloat16*)logits, ld, V, rows, tgt, lse, lp, ent, status);
   return cudaGetLastError();
 }
 

@@ -436,6 +436,30 @@ def bench_swiglu_gemm(M: int = 32768, H: int = 8192, K: int = 2048):
                       "speedup_vs_unfused": round((t_g + t_a) / t_f, 3)}), flush=True)
 
 
+def bench_lse_gemm(M: int = 32768, V: int = 128256, K: int = 2048):
+    """LM-head forward with the row statistics in the GEMM epilogue + the merge pass, against the same GEMM
+    followed by the standalone log-softmax pass over the bf16 logits (L2 flushed between timed calls)."""
+    from rl_project_b200.ops import gemm
+    from rl_project_b200.ops._ext import native
+
+    h = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(V, K, device="cuda") / K ** 0.5).to(torch.bfloat16)
+    tgt = torch.randint(0, V, (M,), device="cuda")
+    logits, stats = gemm.gemm_nt_lse(h, w)
+
+    def fused():
+        lg, st = gemm.gemm_nt_lse(h, w)
+        native().logprob_combine(st, lg, tgt, False, None)
+
+    t_f = time_ms(fused, iters=5)
+    t_g = time_ms(lambda: gemm.gemm_nt(h, w), iters=5)
+    t_p = time_ms(lambda: native().logprob_fwd(logits, tgt, False, None), iters=5)
+    t_c = time_ms(lambda: native().logprob_combine(stats, logits, tgt, False, None), iters=5)
+    print(json.dumps({"kernel": "gemm2sm_lse", "M": M, "V": V, "K": K, "fused_ms": round(t_f, 4),
+                      "combine_ms": round(t_c, 4), "gemm_ms": round(t_g, 4), "logprob_pass_ms": round(t_p, 4),
+                      "speedup_vs_unfused": round((t_g + t_p) / t_f, 3)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--which", default="gemm,mem,adam,paged,sample")
@@ -467,6 +491,8 @@ def main():
         bench_gemm_sustained()
     if "swiglu" in which:
         bench_swiglu_gemm()
+    if "lse" in which:
+        bench_lse_gemm()
     if "swiglu_small" in which:  # profiling case
         bench_swiglu_gemm(M=4096)
     if "attn1" in which:  # one small case (profiling)

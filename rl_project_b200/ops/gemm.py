@@ -325,6 +325,23 @@ def linear_swiglu(x: torch.Tensor, w13: torch.Tensor) -> torch.Tensor:
     return act.view(*shape[:-1], w13.shape[0] // 2)
 
 
+def lse_fusable(h: torch.Tensor, w: torch.Tensor) -> bool:
+    """Whether the LM-head forward ``h W^T`` takes the GEMM whose epilogue also writes the rows' log-sum-exp
+    statistics (the own kernel handles the forward in the current mode and the product fills the GPU)."""
+    return supported(h, w) and w.shape[0] >= 512
+
+
+def gemm_nt_lse(h: torch.Tensor, w: torch.Tensor):
+    """``logits = h w^T`` (bf16) plus, per row and per 256-column half tile, ``(max, sum exp(x - max),
+    sum exp(x - max) x)`` of the stored bf16 logits: ``stats [M, 2 * ceil(N / 512), 4]`` fp32."""
+    h, w = _dense(h), _dense(w)
+    M, N = h.shape[0], w.shape[0]
+    logits = torch.empty(M, N, dtype=torch.bfloat16, device=h.device)
+    stats = torch.empty(M, 2 * (-(-N // 512)), 4, dtype=torch.float32, device=h.device)
+    native().gemm2_lse(h, w, logits, stats, group_for(N, 0), _MAX_CTAS)
+    return logits, stats
+
+
 def _self_check(device: torch.device) -> bool:
     key = (device.type, device.index)
     if key not in _checked:

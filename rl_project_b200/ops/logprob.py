@@ -2,8 +2,11 @@
 
 ``linear_logprobs(h, W, targets)`` returns per-token ``log p(target)`` (and
 optionally the entropy) without ever building an fp32 ``[N, V]`` tensor:
-logits exist only in bf16, the kernel makes ONE pass over each row for the
-forward (online log-sum-exp), and the backward rewrites the same buffer in
+logits exist only in bf16; when the own GEMM runs the LM-head forward its
+epilogue also writes each row's online log-sum-exp statistics per 256-column
+chunk, so a small merge pass gives the outputs without re-reading the logits
+(otherwise the kernel makes ONE pass over each row for the forward), and the
+backward rewrites the same buffer in
 place with ``g * (onehot - softmax)`` before the two GEMMs that produce
 ``dh`` and ``dW``.  When ``N * V`` bf16 logits exceed the keep budget, rows
 are processed in chunks and recomputed in backward.
@@ -44,9 +47,17 @@ class _LinearLogprob(torch.autograd.Function):
         keep = N * V * 2 <= KEEP_BUDGET_BYTES
         step = N if keep else max(1, min(N, CHUNK_ROWS))
         lse_parts, lp_parts, ent_parts, kept = [], [], [], []
+        from rl_project_b200.ops import gemm
+
         for s in range(0, N, step):
-            logits = _gemm_nt(h[s:s + step], W)
-            outs = native().logprob_fwd(logits, targets[s:s + step], with_entropy, None)
+            hs = h[s:s + step]
+            if hs.is_cuda and gemm.lse_fusable(hs, W):
+                # the GEMM's epilogue writes per-chunk row statistics: no second pass over the logits
+                logits, stats = gemm.gemm_nt_lse(hs, W)
+                outs = native().logprob_combine(stats, logits, targets[s:s + step], with_entropy, None)
+            else:
+                logits = _gemm_nt(hs, W)
+                outs = native().logprob_fwd(logits, targets[s:s + step], with_entropy, None)
             lse_parts.append(outs[0])
             lp_parts.append(outs[1])
             if with_entropy:

@@ -235,3 +235,50 @@ def test_linear_swiglu_gradients_match_fp32():
         assert _rel(a, ar) < 1.5e-2 and _rel(x.grad, xr.grad) < 2e-2 and _rel(w13.grad, wr.grad) < 2e-2
     finally:
         gemm._MODE, gemm._MIN_TILES = old, old_min
+
+
+@pytest.mark.parametrize("M,N,K", [(600, 1000, 256), (4096, 32000, 512), (2048, 128256, 2048)])
+def test_lse_epilogue_matches_logprob_pass(M, N, K):
+    """LM-head forward whose epilogue writes per-chunk row statistics: the merged log-sum-exp, target log-prob
+    and entropy equal the standalone pass over the same bf16 logits (ragged last tile included)."""
+    from rl_project_b200.ops import gemm
+    from rl_project_b200.ops._ext import native
+
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    h = torch.randn(M, K, device="cuda", generator=g).to(BF)
+    w = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5 * 3).to(BF)
+    tgt = torch.randint(0, N, (M,), device="cuda", generator=g)
+    tgt[::7] = -1
+    logits, stats = gemm.gemm_nt_lse(h, w)
+    lse, lp, ent = native().logprob_combine(stats, logits, tgt, True, None)
+    rlse, rlp, rent = native().logprob_fwd(logits, tgt, True, None)
+    torch.cuda.synchronize()
+    assert _rel(logits, h.float() @ w.float().t()) < 8e-3
+    assert torch.allclose(lse, rlse, rtol=1e-5, atol=1e-4)
+    assert torch.allclose(lp, rlp, rtol=1e-5, atol=1e-4)
+    assert torch.allclose(ent, rent, rtol=1e-4, atol=1e-3)
+
+
+def test_linear_logprobs_with_lse_epilogue_matches_fp32():
+    """The fused-loss entry point takes the statistics epilogue when the own GEMM runs the LM head; log-probs
+    and both gradients match an fp32 log-softmax."""
+    from rl_project_b200.ops import gemm
+    from rl_project_b200.ops.logprob import linear_logprobs, linear_logprobs_reference
+
+    old, old_min = gemm._MODE, gemm._MIN_TILES
+    gemm._MODE, gemm._MIN_TILES = "hybrid", 0
+    try:
+        M, V, K = 1024, 8192, 512
+        h = torch.randn(M, K, device="cuda").to(BF).requires_grad_()
+        w = (torch.randn(V, K, device="cuda") / K ** 0.5).to(BF).requires_grad_()
+        tgt = torch.randint(0, V, (M,), device="cuda")
+        assert gemm.lse_fusable(h.detach(), w.detach())
+        lp, ent = linear_logprobs(h, w, tgt, with_entropy=True)
+        (lp.sum() + 0.1 * ent.sum()).backward()
+        hr, wr = h.detach().float().requires_grad_(), w.detach().float().requires_grad_()
+        rlp, rent = linear_logprobs_reference(hr, wr, tgt, with_entropy=True)
+        (rlp.sum() + 0.1 * rent.sum()).backward()
+        assert (lp - rlp).abs().max().item() < 0.1 and _rel(ent, rent) < 1e-2
+        assert _rel(h.grad, hr.grad) < 3e-2 and _rel(w.grad, wr.grad) < 3e-2
+    finally:
+        gemm._MODE, gemm._MIN_TILES = old, old_min
