@@ -228,21 +228,39 @@ __global__ void __launch_bounds__(MAXT) rmsnorm_bwd_wide(const __nv_bfloat16* __
   unpack8(ldg8(w + c), wf);
 #pragma unroll
   for (int k = 0; k < 8; ++k) acc[k] = 0.f;
-  for (long long row0 = (long long)blockIdx.x * kRows; row0 < rows; row0 += (long long)gridDim.x * kRows) {
+  const long long stride = (long long)gridDim.x * kRows;
+  // raw operands of the rows in flight: the next rows' loads are issued before this iteration's reduction
+  bf16x8 nh[kRows], ng[kRows], nr[kRows];
+  float nrs[kRows];
+  auto issue = [&](long long r0) {
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      const long long row = r0 + r;
+      if (row < rows) {
+        nrs[r] = rstd[row];
+        nh[r] = ldg8(h + row * dim + c);
+        ng[r] = ldg8(dy + row * dim + c);
+        if (dres != nullptr) nr[r] = ldg8(dres + row * dim + c);
+      }
+    }
+  };
+  long long row0 = (long long)blockIdx.x * kRows;
+  issue(row0);
+  for (; row0 < rows; row0 += stride) {
     float xh[kRows][8], g[kRows][8], dot[kRows], rs[kRows];
     bf16x8 rres[kRows];
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
-      const long long row = row0 + r;
       dot[r] = 0.f;
       rs[r] = 0.f;
-      if (row < rows) {
-        rs[r] = rstd[row];
-        unpack8(ldg8(h + row * dim + c), xh[r]);
-        unpack8(ldg8(dy + row * dim + c), g[r]);
-        if (dres != nullptr) rres[r] = ldg8(dres + row * dim + c);  // issued with the others: one round trip
+      if (row0 + r < rows) {
+        rs[r] = nrs[r];
+        unpack8(nh[r], xh[r]);
+        unpack8(ng[r], g[r]);
+        rres[r] = nr[r];
       }
     }
+    if (row0 + stride < rows) issue(row0 + stride);
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
       if (row0 + r < rows) {
