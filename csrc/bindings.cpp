@@ -521,6 +521,37 @@ void gemm2_lse(const at::Tensor& A, const at::Tensor& B, at::Tensor& logits, at:
            "gemm2_lse");
 }
 
+// q, k, v ([B, T, H, D], token-major) = rope(split(x w^T)) for x [B*T, K] and w = [W_q; W_k; W_v] from one GEMM
+// whose epilogue rotates q and k; positions [B*T] int32 (optional; else t + pos_offset).
+std::vector<at::Tensor> gemm2_rope_qkv(const at::Tensor& X, const at::Tensor& W, const at::Tensor& cos_t,
+                                       const at::Tensor& sin_t, const c10::optional<at::Tensor>& positions, int64_t B,
+                                       int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int64_t pos_offset,
+                                       int64_t group_m, int64_t max_ctas) {
+  check_bf16(X, "x");
+  check_bf16(W, "w");
+  check_dev(W, X, "w");
+  check_dev(cos_t, X, "cos");
+  check_dev(sin_t, X, "sin");
+  check_dev(positions, X, "positions");
+  TORCH_CHECK(X.dim() == 2 && W.dim() == 2 && X.size(1) == W.size(1) && X.stride(1) == 1 && W.stride(1) == 1 &&
+              X.size(0) == B * T && W.size(0) == (Hq + 2 * Hkv) * D, "gemm2_rope_qkv: operand shapes");
+  TORCH_CHECK(cos_t.scalar_type() == at::kFloat && sin_t.scalar_type() == at::kFloat && cos_t.is_contiguous() &&
+              sin_t.is_contiguous() && cos_t.size(1) == D / 2, "gemm2_rope_qkv: cos / sin tables [rows, D/2] fp32");
+  if (positions.has_value())
+    TORCH_CHECK(positions->scalar_type() == at::kInt && positions->is_contiguous() && positions->numel() == B * T,
+                "gemm2_rope_qkv: positions int32 [B*T]");
+  const c10::cuda::CUDAGuard g(X.device());
+  auto opts = X.options();
+  auto q = at::empty({B, T, Hq, D}, opts), k = at::empty({B, T, Hkv, D}, opts), v = at::empty({B, T, Hkv, D}, opts);
+  CHECK_OK(rlb_gemm2sm_rope_qkv((int)(B * T), (int)Hq, (int)Hkv, (int)D, (int)X.size(1), X.data_ptr(), X.stride(0),
+                                W.data_ptr(), W.stride(0), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
+                                positions.has_value() ? positions->data_ptr<int>() : nullptr, (int)T, (int)pos_offset,
+                                (int)cos_t.size(0), bounds_word(X.device()), (int)max_ctas, cur_stream(), (int)group_m),
+           "gemm2_rope_qkv");
+  return {q, k, v};
+}
+
 // Grouped GEMM (mixture-of-experts): see rlb_gemm_grouped for the two modes.
 void gemm_grouped(int64_t mode, int64_t b_mn, int64_t epi, const at::Tensor& A, const at::Tensor& B, at::Tensor& out,
                   int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, double alpha,
@@ -937,6 +968,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm2x", &gemm2x);
   m.def("gemm2_swiglu", &gemm2_swiglu);
   m.def("gemm2_lse", &gemm2_lse);
+  m.def("gemm2_rope_qkv", &gemm2_rope_qkv);
   m.def("logprob_combine", &logprob_combine);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_allreduce", &gemm_allreduce);

@@ -76,7 +76,12 @@ struct Cfg {
 // half tile, the running statistics of its bf16 values -- max m, sum exp(x - m) and sum exp(x - m) * x -- into
 // `lse_stats` ([M][2 * tiles_n] float4), from which one small pass gets each row's log-sum-exp, target
 // log-prob and entropy without reading the logits again.
-enum Epi : int { kStoreBF16 = 0, kStoreF32 = 1, kAccumF32 = 2, kSwiGLU = 3, kLogitsLSE = 4 };
+// kRope64 / kRope128: attention input projection x [W_q; W_k; W_v]^T with rotary embedding applied in the
+// epilogue (head dim 64 / 128, rotate-half pairs (i, i + D/2) of each q and k head by pos * inv_freq[i], from the
+// bf16 values as the standalone RoPE kernel does) and the q / k / v column ranges stored into three token-major
+// tensors (maps c, c2, c3).  A position outside the cos / sin table is reported in `rope_err` and that row
+// is left unrotated.
+enum Epi : int { kStoreBF16 = 0, kStoreF32 = 1, kAccumF32 = 2, kSwiGLU = 3, kLogitsLSE = 4, kRope64 = 5, kRope128 = 6 };
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
 
@@ -89,6 +94,12 @@ struct Params {
   float* c32;     // kAccumF32: C itself, for the ragged edge chunks the threads accumulate directly
   long long ldc;
   float4* lse_stats;  // kLogitsLSE: [M][2 * ceil(N / 512)] per-half-tile row statistics
+  // kRope64 / kRope128
+  const float* rope_cos;  // [table_rows][D / 2]
+  const float* rope_sin;
+  const int* rope_pos;    // [M] positions, or null: (row % seq_T) + pos_offset
+  int seq_T, pos_offset, table_rows, q_cols, kv_cols;
+  int* rope_err;
 };
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group_m, int& m, int& n) {
@@ -150,6 +161,8 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   static_assert(EPI != kSwiGLU || (NSUB == 2 && A_MN == 0 && B_MN == 0), "SwiGLU epilogue: forward, 256 x 512");
   static_assert(EPI != kLogitsLSE || (NSUB == 2 && A_MN == 0 && B_MN == 0), "LSE epilogue: forward, 256 x 512");
+  constexpr bool ROPE = EPI == kRope64 || EPI == kRope128;
+  static_assert(!ROPE || (NSUB == 2 && A_MN == 0 && B_MN == 0), "RoPE epilogue: forward, 256 x 512");
   constexpr int TN = EPI == kSwiGLU ? SUBN : BN;  // output columns (hidden units for kSwiGLU) per tile
   const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + TN - 1) / TN;
   const int num_tiles = num_m * num_n;
@@ -180,7 +193,7 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
     sm100::prefetch_tensormap(&tma_a);
     sm100::prefetch_tensormap(&tma_b);
     sm100::prefetch_tensormap(&tma_c);
-    if (EPI == kSwiGLU) {
+    if (EPI == kSwiGLU || EPI == kRope64 || EPI == kRope128) {
       sm100::prefetch_tensormap(&tma_c2);
       sm100::prefetch_tensormap(&tma_c3);
     }
@@ -389,7 +402,7 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
       }
       sm100::tc_fence_after();
       const uint32_t lanes = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-      if constexpr ((EPI == kStoreBF16 || EPI == kSwiGLU || EPI == kLogitsLSE) && NSUB == 2) {
+      if constexpr ((EPI == kStoreBF16 || EPI == kSwiGLU || EPI == kLogitsLSE || ROPE) && NSUB == 2) {
         // read this warp's 128 columns of sub-tile 0, hand sub-tile 0 back (the next tile's first MMAs may
         // start), then its 128 columns of sub-tile 1 and hand those back; all kept as packed bf16 in registers
         uint32_t pk[2][64];
@@ -446,6 +459,39 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
           const int row = row0 + lane;
           if (row < p.M) p.lse_stats[(long long)row * (2 * num_n) + 2 * tn + half] = make_float4(m, se, te, 0.f);
         }
+        if constexpr (ROPE) {
+          constexpr int D = EPI == kRope64 ? 64 : 128;
+          constexpr int QW = D / 4;  // packed words (column pairs) in half a head
+          const int row = row0 + lane;
+          int pos = -1;
+          if (row < p.M) {
+            pos = p.rope_pos ? p.rope_pos[row] : row % p.seq_T + p.pos_offset;
+            if (pos < 0 || pos >= p.table_rows) {
+              if (p.rope_err) atomicCAS(p.rope_err, 0, 2);  // index error word: bad index
+              pos = -1;
+            }
+          }
+#pragma unroll
+          for (int sb = 0; sb < 2; ++sb) {
+            const int cb = tn * BN + sb * SUBN + half * 128;  // first column of this thread's 128 (whole heads)
+            if (pos >= 0 && cb < p.q_cols + p.kv_cols) {    // q and k heads rotate, v passes through
+              const float2* cs = reinterpret_cast<const float2*>(p.rope_cos + (long long)pos * (D / 2));
+              const float2* sn = reinterpret_cast<const float2*>(p.rope_sin + (long long)pos * (D / 2));
+#pragma unroll
+              for (int hh = 0; hh < 128 / D; ++hh) {
+#pragma unroll
+                for (int i = 0; i < QW; ++i) {
+                  const int w1 = hh * (D / 2) + i, w2 = w1 + QW;  // columns (2i, 2i+1) and their partners + D/2
+                  const float2 c2 = __ldg(cs + i), s2 = __ldg(sn + i);
+                  const float a0 = __uint_as_float(pk[sb][w1] << 16), a1 = __uint_as_float(pk[sb][w1] & 0xffff0000u);
+                  const float b0 = __uint_as_float(pk[sb][w2] << 16), b1 = __uint_as_float(pk[sb][w2] & 0xffff0000u);
+                  pk[sb][w1] = pack_bf16(a0 * c2.x - b0 * s2.x, a1 * c2.y - b1 * s2.y);
+                  pk[sb][w2] = pack_bf16(b0 * c2.x + a0 * s2.x, b1 * c2.y + a1 * s2.y);
+                }
+              }
+            }
+          }
+        }
         // kSwiGLU: out 0 / 1 are the gate / up halves of h13 (maps c, c2), out 2 the activation (map c3)
         constexpr int NOUT = EPI == kSwiGLU ? 3 : 2;
 #pragma unroll
@@ -478,7 +524,18 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
             __syncwarp();
             if (lane == 0 && row0 < p.M && col0 < p.N) {
               const CUtensorMap* map = o == 0 ? &tma_c : (o == 1 ? &tma_c2 : &tma_c3);
-              sm100::tma_store_2d(EPI == kSwiGLU ? map : &tma_c, tile, col0, row0);  // clipped at M and N
+              int col = col0;
+              if (ROPE) {  // q | k | v column ranges go to their own tensors
+                map = &tma_c;
+                if (col0 >= p.q_cols + p.kv_cols) {
+                  map = &tma_c3;
+                  col = col0 - p.q_cols - p.kv_cols;
+                } else if (col0 >= p.q_cols) {
+                  map = &tma_c2;
+                  col = col0 - p.q_cols;
+                }
+              }
+              sm100::tma_store_2d((EPI == kSwiGLU || ROPE) ? map : &tma_c, tile, col, row0);  // clipped at M and N
               sm100::bulk_commit();
             }
           }
@@ -635,7 +692,12 @@ static cudaError_t launch(const void* A, long long lda, const void* B, long long
   const bool ok_b = B_MN ? make_map(&mb, bf, 2, B, p.K, p.N, ldb, 64, BK) : make_map(&mb, bf, 2, B, b_rows, p.K, ldb, 64, HN);
   CUtensorMap mc2, mc3;
   bool ok_c;
-  if (EPI == kSwiGLU) {  // gate / up halves of h13 [M][2H] (row pitch ldc) and the activation [M][H]
+  if (EPI == kRope64 || EPI == kRope128) {  // q [M][q_cols], k and v [M][kv_cols]; `act` holds {k, v}
+    void* const* kv = static_cast<void* const*>(act);
+    ok_c = make_map(&mc, bf, 2, Cp, p.M, p.q_cols, p.q_cols, 64, 32) &&
+           make_map(&mc2, bf, 2, kv[0], p.M, p.kv_cols, p.kv_cols, 64, 32) &&
+           make_map(&mc3, bf, 2, kv[1], p.M, p.kv_cols, p.kv_cols, 64, 32);
+  } else if (EPI == kSwiGLU) {  // gate / up halves of h13 [M][2H] (row pitch ldc) and the activation [M][H]
     ok_c = make_map(&mc, bf, 2, Cp, p.M, p.N, ldc, 64, 32) &&
            make_map(&mc2, bf, 2, (const __nv_bfloat16*)Cp + p.N, p.M, p.N, ldc, 64, 32) &&
            make_map(&mc3, bf, 2, act, p.M, p.N, p.N, 64, 32);
@@ -768,4 +830,39 @@ cudaError_t rlb_gemm2sm_lse(int M, int N, int K, const void* A, long long lda, c
   p.ldc = ldc;
   p.lse_stats = (float4*)stats;
   return launch<0, 0, kLogitsLSE, 2>(A, lda, B, ldb, C, ldc, p, max_ctas, s);
+}
+
+// Attention input projection with rotary embedding in the epilogue: x [M][K] times w = [W_q; W_k; W_v]
+// ([(Hq + 2 Hkv) D][K]); q [M][Hq D], k and v [M][Hkv D] (token-major, i.e. [B, T, H, D]) with q and k rotated by
+// the cos / sin tables [table_rows][D / 2] at position positions[row] (or row % seq_T + pos_offset).  D is 64 or
+// 128; Hq D and Hkv D multiples of 128.
+cudaError_t rlb_gemm2sm_rope_qkv(int M, int Hq, int Hkv, int D, int K, const void* X, long long ldx, const void* W,
+                                 long long ldw, void* q, void* k, void* v, const float* cos_t, const float* sin_t,
+                                 const int* positions, int seq_T, int pos_offset, int table_rows, int* err,
+                                 int max_ctas, cudaStream_t s, int group_m) {
+  using namespace gemm2;
+  if (M <= 0 || K <= 0) return cudaSuccess;
+  if ((D != 64 && D != 128) || ((Hq * D) % 128) || ((Hkv * D) % 128) || seq_T <= 0) return cudaErrorInvalidValue;
+  if ((ldx % 8) || (ldw % 8)) return cudaErrorInvalidPitchValue;
+  if ((((uintptr_t)X) | ((uintptr_t)W) | ((uintptr_t)q) | ((uintptr_t)k) | ((uintptr_t)v)) & 15)
+    return cudaErrorInvalidDevicePointer;
+  Params p{};
+  p.M = M;
+  p.N = (Hq + 2 * Hkv) * D;
+  p.K = K;
+  p.splits = 1;
+  p.group_m = group_m < 1 ? GROUP_M : group_m;
+  p.alpha = 1.f;
+  p.rope_cos = cos_t;
+  p.rope_sin = sin_t;
+  p.rope_pos = positions;
+  p.seq_T = seq_T;
+  p.pos_offset = pos_offset;
+  p.table_rows = table_rows;
+  p.q_cols = Hq * D;
+  p.kv_cols = Hkv * D;
+  p.rope_err = err;
+  void* kv[2] = {k, v};
+  return D == 64 ? launch<0, 0, kRope64, 2>(X, ldx, W, ldw, q, p.q_cols, p, max_ctas, s, kv)
+                 : launch<0, 0, kRope128, 2>(X, ldx, W, ldw, q, p.q_cols, p, max_ctas, s, kv);
 }

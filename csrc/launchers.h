@@ -73,6 +73,12 @@ cudaError_t rlb_gemm2sm_lse(int M, int N, int K, const void* A, long long lda, c
 cudaError_t rlb_logprob_combine(const void* stats, int chunks, const void* logits, long long ld, long long rows, int V,
                                 const long long* tgt, float* lse, float* lp, float* ent, int* status, cudaStream_t s);
 
+// Attention input projection with RoPE and the q / k / v split in the epilogue (see gemm_2sm.cu).
+cudaError_t rlb_gemm2sm_rope_qkv(int M, int Hq, int Hkv, int D, int K, const void* X, long long ldx, const void* W,
+                                 long long ldw, void* q, void* k, void* v, const float* cos_t, const float* sin_t,
+                                 const int* positions, int seq_T, int pos_offset, int table_rows, int* err,
+                                 int max_ctas, cudaStream_t s, int group_m);
+
 cudaError_t rlb_gemm_grouped(int mode, int b_mn, int epi, int M, int N, int K, const void* A, long long lda,
                              const void* B, long long ldb, void* C, long long ldc, float alpha, int groups,
                              const int* tile_group, const int* k_begin, const int* k_len, long long k_total,

@@ -17,6 +17,7 @@ import torch
 import torch.nn as nn
 
 from rl_project_b200.core.config import ModelSpec
+from rl_project_b200.ops import gemm
 from rl_project_b200.ops.attention import attention_reference, causal_attention
 from rl_project_b200.ops.linear import linear
 from rl_project_b200.ops.paged_attention import paged_decode, paged_write
@@ -99,14 +100,30 @@ class CausalSelfAttention(nn.Module):
             y = self.c_proj(y)
         return self.resid_dropout(y)
 
+    def _rope_qkv_fused(self, x: torch.Tensor, offset: int, positions: Optional[torch.Tensor]):
+        """q, k, v from one GEMM whose epilogue applies RoPE and splits the heads, when the own GEMM runs the
+        forward projections; None otherwise."""
+        mods = (self.q_proj, self.k_proj, self.v_proj)
+        if not (self.use_rope and self.tp_group is None and x.is_cuda and x.dtype == torch.bfloat16
+                and positions is None and all(type(m) is nn.Linear and m.bias is None for m in mods)):
+            return None
+        w = torch.cat([m.weight for m in mods], 0)
+        if not gemm.rope_qkv_fusable(x.reshape(-1, x.shape[-1]), w, self.n_head, self.n_kv_head, self.head_dim):
+            return None
+        cos, sin = self.rope.tables(offset + x.shape[1], x.device)
+        return gemm.linear_rope_qkv(x, w, cos, sin, None, self.n_head, self.n_kv_head, self.head_dim, offset)
+
     def forward(self, x: torch.Tensor, past_kv: Optional[KVCache] = None, positions: Optional[torch.Tensor] = None):
         B, T, C = x.shape
-        qkv = self._qkv(x)
         offset = past_kv[0].shape[2] if past_kv is not None else 0
         # q/k/v come out token-major [B, T, H, D]; attention reads them through [B, H, T, D]
         # views so its output is already in the [B, T, H*D] layout the output projection wants
-        q, k, v = rope_split_qkv(qkv, self.rope, self.n_head, self.n_kv_head, self.head_dim, offset=offset,
-                                 positions=positions, rotate=self.use_rope, heads_major=False)
+        fused = self._rope_qkv_fused(x, offset, positions)
+        if fused is not None:
+            q, k, v = fused
+        else:
+            q, k, v = rope_split_qkv(self._qkv(x), self.rope, self.n_head, self.n_kv_head, self.head_dim,
+                                     offset=offset, positions=positions, rotate=self.use_rope, heads_major=False)
         q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
         if past_kv is not None:
             k = torch.cat([past_kv[0], k], dim=2)

@@ -460,6 +460,25 @@ def bench_lse_gemm(M: int = 32768, V: int = 128256, K: int = 2048):
                       "speedup_vs_unfused": round((t_g + t_p) / t_f, 3)}), flush=True)
 
 
+def bench_rope_qkv_gemm(B: int = 8, T: int = 4096, C: int = 2048, Hq: int = 32, Hkv: int = 8, D: int = 64):
+    """Attention input projection with RoPE and the head split in the GEMM epilogue against the GEMM followed
+    by the standalone RoPE + split kernel (L2 flushed between timed calls)."""
+    from rl_project_b200.ops import gemm
+    from rl_project_b200.ops._ext import native
+    from rl_project_b200.ops.rope import RopeTable
+
+    x = torch.randn(B * T, C, device="cuda").to(torch.bfloat16)
+    w = (torch.randn((Hq + 2 * Hkv) * D, C, device="cuda") / C ** 0.5).to(torch.bfloat16)
+    cos, sin = RopeTable(D, 500000.0, max_seq_len=T).tables(T, x.device)
+    qkv = gemm.gemm_nt(x, w)
+    t_f = time_ms(lambda: native().gemm2_rope_qkv(x, w, cos, sin, None, B, T, Hq, Hkv, D, 0, 8, 0))
+    t_g = time_ms(lambda: gemm.gemm_nt(x, w))
+    t_r = time_ms(lambda: native().rope_qkv_fwd(qkv, cos, sin, None, B, T, Hq, Hkv, D, 0, False))
+    print(json.dumps({"kernel": "gemm2sm_rope_qkv", "M": B * T, "N": (Hq + 2 * Hkv) * D, "K": C,
+                      "fused_ms": round(t_f, 4), "gemm_ms": round(t_g, 4), "rope_ms": round(t_r, 4),
+                      "speedup_vs_unfused": round((t_g + t_r) / t_f, 3)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--which", default="gemm,mem,adam,paged,sample")
@@ -493,6 +512,8 @@ def main():
         bench_swiglu_gemm()
     if "lse" in which:
         bench_lse_gemm()
+    if "rope" in which:
+        bench_rope_qkv_gemm()
     if "swiglu_small" in which:  # profiling case
         bench_swiglu_gemm(M=4096)
     if "attn1" in which:  # one small case (profiling)

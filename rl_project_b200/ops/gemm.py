@@ -342,6 +342,52 @@ def gemm_nt_lse(h: torch.Tensor, w: torch.Tensor):
     return logits, stats
 
 
+def rope_qkv_fusable(x2: torch.Tensor, w: torch.Tensor, n_head: int, n_kv_head: int, head_dim: int) -> bool:
+    """Whether the attention input projection can run as one GEMM with RoPE and the q / k / v split in its
+    epilogue (own kernel on the forward, head dim 64 or 128, whole 128-column blocks per q / k / v range)."""
+    return (head_dim in (64, 128) and (n_head * head_dim) % 128 == 0 and (n_kv_head * head_dim) % 128 == 0
+            and supported(x2, w))
+
+
+class _LinearRopeQKV(torch.autograd.Function):
+    """q, k, v = rope(split(x w^T)): forward in one GEMM; backward through the RoPE kernel's inverse rotation
+    (which re-interleaves dq | dk | dv) and the linear layer's two gradient products."""
+
+    @staticmethod
+    def forward(ctx, x2, w, cos, sin, positions, B, T, Hq, Hkv, D, offset):
+        x2, w = _dense(x2), _dense(w)
+        q, k, v = native().gemm2_rope_qkv(x2, w, cos, sin, positions, B, T, Hq, Hkv, D, offset, group_for(w.shape[0], 0),
+                                          _MAX_CTAS)
+        ctx.save_for_backward(x2, w, cos, sin, positions if positions is not None else torch.empty(0))
+        ctx.args = (B, T, Hq, Hkv, D, offset, positions is not None)
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        x2, w, cos, sin, pos = ctx.saved_tensors
+        B, T, Hq, Hkv, D, offset, has_pos = ctx.args
+        dq = torch.zeros((B, T, Hq, D), dtype=x2.dtype, device=x2.device) if dq is None else dq.contiguous()
+        dk = torch.zeros((B, T, Hkv, D), dtype=x2.dtype, device=x2.device) if dk is None else dk.contiguous()
+        dv = torch.zeros((B, T, Hkv, D), dtype=x2.dtype, device=x2.device) if dv is None else dv.contiguous()
+        dy = native().rope_qkv_bwd(dq, dk, dv, cos, sin, pos if has_pos else None, B, T, Hq, Hkv, D, offset,
+                                   False).view(B * T, -1)
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm_nn(dy, w) if dgrad_own() else dy @ w
+        if ctx.needs_input_grad[1]:
+            dw = gemm_tn(dy, x2) if wgrad_own() else dy.t() @ x2
+        return dx, dw, None, None, None, None, None, None, None, None, None
+
+
+def linear_rope_qkv(x: torch.Tensor, w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                    positions: Optional[torch.Tensor], n_head: int, n_kv_head: int, head_dim: int, offset: int = 0):
+    """``x [B, T, C]`` -> token-major ``q [B, T, Hq, D]``, ``k``, ``v [B, T, Hkv, D]`` with RoPE applied to q and
+    k inside the projection GEMM's epilogue (cos / sin tables ``[rows, D/2]`` fp32 on the device)."""
+    B, T, C = x.shape
+    pos = positions.to(torch.int32).reshape(-1).contiguous() if positions is not None else None
+    return _LinearRopeQKV.apply(x.reshape(B * T, C), w, cos, sin, pos, B, T, n_head, n_kv_head, head_dim, offset)
+
+
 def _self_check(device: torch.device) -> bool:
     key = (device.type, device.index)
     if key not in _checked:

@@ -282,3 +282,37 @@ def test_linear_logprobs_with_lse_epilogue_matches_fp32():
         assert _rel(h.grad, hr.grad) < 3e-2 and _rel(w.grad, wr.grad) < 3e-2
     finally:
         gemm._MODE, gemm._MIN_TILES = old, old_min
+
+
+@pytest.mark.parametrize("Hq,Hkv,D", [(32, 8, 64), (16, 4, 128)])
+def test_rope_qkv_epilogue_matches_unfused(Hq, Hkv, D):
+    """One GEMM with RoPE and the q / k / v split in its epilogue against the projection followed by the RoPE
+    kernel: forward outputs and the gradients of x and w."""
+    from rl_project_b200.ops import gemm
+    from rl_project_b200.ops.rope import RopeTable, rope_split_qkv
+
+    old, old_min = gemm._MODE, gemm._MIN_TILES
+    gemm._MODE, gemm._MIN_TILES = "hybrid", 0
+    try:
+        B, T, C = 2, 1024, 1024
+        g = torch.Generator(device="cuda").manual_seed(D)
+        x = torch.randn(B, T, C, device="cuda", generator=g).to(BF).requires_grad_()
+        w = (torch.randn((Hq + 2 * Hkv) * D, C, device="cuda", generator=g) / C ** 0.5).to(BF).requires_grad_()
+        table = RopeTable(D, 500000.0, max_seq_len=T)
+        cos, sin = table.tables(T + 3, x.device)
+        assert gemm.rope_qkv_fusable(x.detach().reshape(-1, C), w.detach(), Hq, Hkv, D)
+        q, k, v = gemm.linear_rope_qkv(x, w, cos, sin, None, Hq, Hkv, D, offset=3)
+        gq, gk, gv = (torch.randn_like(t) for t in (q, k, v))
+        (q.float() * gq).sum().add_((k.float() * gk).sum()).add_((v.float() * gv).sum()).backward()
+        dx, dw = x.grad.clone(), w.grad.clone()
+        x.grad = w.grad = None
+        qkv = (x.reshape(-1, C) @ w.t()).view(B, T, -1)
+        rq, rk, rv = rope_split_qkv(qkv, table, Hq, Hkv, D, offset=3, heads_major=False)
+        (rq.float() * gq).sum().add_((rk.float() * gk).sum()).add_((rv.float() * gv).sum()).backward()
+        torch.cuda.synchronize()
+        for got, ref in ((q, rq), (k, rk), (v, rv)):
+            assert got.shape == ref.shape
+            assert _rel(got, ref.float()) < 1e-2
+        assert _rel(dx, x.grad.float()) < 1e-2 and _rel(dw, w.grad.float()) < 1e-2
+    finally:
+        gemm._MODE, gemm._MIN_TILES = old, old_min
