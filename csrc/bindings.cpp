@@ -552,6 +552,29 @@ std::vector<at::Tensor> gemm2_rope_qkv(const at::Tensor& X, const at::Tensor& W,
   return {q, k, v};
 }
 
+// dh13 [M][2H] = SwiGLU backward of (dy [M][K] W2) against h13 [M][2H], W2 = the down projection's weight
+// [K][H]: one GEMM whose epilogue applies the activation's backward (dh itself is never stored).
+void gemm2_dgrad_swiglu(const at::Tensor& dY, const at::Tensor& W2, const at::Tensor& h13, at::Tensor& dh13,
+                        int64_t group_m, int64_t max_ctas) {
+  check_bf16(dY, "dy");
+  check_bf16(W2, "w2");
+  check_bf16(h13, "h13");
+  check_bf16(dh13, "dh13");
+  check_dev(W2, dY, "w2");
+  check_dev(h13, dY, "h13");
+  check_dev(dh13, dY, "dh13");
+  TORCH_CHECK(dY.dim() == 2 && W2.dim() == 2 && dY.size(1) == W2.size(0) && dY.stride(1) == 1 && W2.stride(1) == 1,
+              "gemm2_dgrad_swiglu: dy [M, K] and w2 [K, H] with contiguous rows expected");
+  const int64_t M = dY.size(0), K = dY.size(1), H = W2.size(1);
+  TORCH_CHECK(h13.size(0) == M && h13.size(1) == 2 * H && h13.stride(1) == 1 && dh13.size(0) == M &&
+              dh13.size(1) == 2 * H && dh13.stride(1) == 1, "gemm2_dgrad_swiglu: h13 / dh13 must be [M, 2H]");
+  const c10::cuda::CUDAGuard g(dY.device());
+  CHECK_OK(rlb_gemm2sm_dgrad_swiglu((int)M, (int)H, (int)K, dY.data_ptr(), dY.stride(0), W2.data_ptr(), W2.stride(0),
+                                    h13.data_ptr(), h13.stride(0), dh13.data_ptr(), dh13.stride(0), (int)max_ctas,
+                                    cur_stream(), (int)group_m),
+           "gemm2_dgrad_swiglu");
+}
+
 // Grouped GEMM (mixture-of-experts): see rlb_gemm_grouped for the two modes.
 void gemm_grouped(int64_t mode, int64_t b_mn, int64_t epi, const at::Tensor& A, const at::Tensor& B, at::Tensor& out,
                   int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, double alpha,
@@ -969,6 +992,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm2_swiglu", &gemm2_swiglu);
   m.def("gemm2_lse", &gemm2_lse);
   m.def("gemm2_rope_qkv", &gemm2_rope_qkv);
+  m.def("gemm2_dgrad_swiglu", &gemm2_dgrad_swiglu);
   m.def("logprob_combine", &logprob_combine);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_allreduce", &gemm_allreduce);

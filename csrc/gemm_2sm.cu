@@ -81,7 +81,12 @@ struct Cfg {
 // bf16 values as the standalone RoPE kernel does) and the q / k / v column ranges stored into three token-major
 // tensors (maps c, c2, c3).  A position outside the cos / sin table is reported in `rope_err` and that row
 // is left unrotated.
-enum Epi : int { kStoreBF16 = 0, kStoreF32 = 1, kAccumF32 = 2, kSwiGLU = 3, kLogitsLSE = 4, kRope64 = 5, kRope128 = 6 };
+// kSwiGLUBwd: input gradient of a gated FFN's down projection, dh = dy W2 (A = dy K-major, B = W2 [K][H] read
+// MN-major), rounded to bf16 as a stored dh would be, and in the epilogue the SwiGLU backward against the
+// forward's h13 [M][2H]: d gate = dh * up * s * (1 + gate * (1 - s)), d up = dh * gate * s (s = sigmoid(gate)),
+// stored into dh13's two halves (maps c, c2).  dh itself is never written.
+enum Epi : int { kStoreBF16 = 0, kStoreF32 = 1, kAccumF32 = 2, kSwiGLU = 3, kLogitsLSE = 4, kRope64 = 5, kRope128 = 6,
+                 kSwiGLUBwd = 7 };
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
 
@@ -100,6 +105,8 @@ struct Params {
   const int* rope_pos;    // [M] positions, or null: (row % seq_T) + pos_offset
   int seq_T, pos_offset, table_rows, q_cols, kv_cols;
   int* rope_err;
+  const __nv_bfloat16* h13;  // kSwiGLUBwd: the forward's [gate | up] projection, row pitch ldh
+  long long ldh;
 };
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group_m, int& m, int& n) {
@@ -163,6 +170,7 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
   static_assert(EPI != kLogitsLSE || (NSUB == 2 && A_MN == 0 && B_MN == 0), "LSE epilogue: forward, 256 x 512");
   constexpr bool ROPE = EPI == kRope64 || EPI == kRope128;
   static_assert(!ROPE || (NSUB == 2 && A_MN == 0 && B_MN == 0), "RoPE epilogue: forward, 256 x 512");
+  static_assert(EPI != kSwiGLUBwd || (NSUB == 2 && A_MN == 0 && B_MN == 1), "SwiGLU backward: dy W, 256 x 512");
   constexpr int TN = EPI == kSwiGLU ? SUBN : BN;  // output columns (hidden units for kSwiGLU) per tile
   const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + TN - 1) / TN;
   const int num_tiles = num_m * num_n;
@@ -193,7 +201,7 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
     sm100::prefetch_tensormap(&tma_a);
     sm100::prefetch_tensormap(&tma_b);
     sm100::prefetch_tensormap(&tma_c);
-    if (EPI == kSwiGLU || EPI == kRope64 || EPI == kRope128) {
+    if (EPI == kSwiGLU || EPI == kRope64 || EPI == kRope128 || EPI == kSwiGLUBwd) {
       sm100::prefetch_tensormap(&tma_c2);
       sm100::prefetch_tensormap(&tma_c3);
     }
@@ -402,7 +410,8 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
       }
       sm100::tc_fence_after();
       const uint32_t lanes = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-      if constexpr ((EPI == kStoreBF16 || EPI == kSwiGLU || EPI == kLogitsLSE || ROPE) && NSUB == 2) {
+      if constexpr ((EPI == kStoreBF16 || EPI == kSwiGLU || EPI == kLogitsLSE || ROPE || EPI == kSwiGLUBwd) &&
+                    NSUB == 2) {
         // read this warp's 128 columns of sub-tile 0, hand sub-tile 0 back (the next tile's first MMAs may
         // start), then its 128 columns of sub-tile 1 and hand those back; all kept as packed bf16 in registers
         uint32_t pk[2][64];
@@ -492,6 +501,59 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
             }
           }
         }
+        if constexpr (EPI == kSwiGLUBwd) {
+          // pk holds dh; gate and up of this thread's row come from h13, 8 columns (16 B) at a time
+          const int row = row0 + lane;
+          const bool row_ok = row < p.M;
+          const __nv_bfloat16* hrow = p.h13 + (long long)(row_ok ? row : 0) * p.ldh;
+          // (sub-tile, chunk) outermost so each chunk's dh registers die after its two stores
+#pragma unroll
+          for (int sb = 0; sb < 2; ++sb) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              const int col0 = tn * BN + sb * SUBN + half * 128 + c * 64;
+#pragma unroll
+              for (int o = 0; o < 2; ++o) {  // 0: d gate -> dh13[:, :H] (map c); 1: d up -> dh13[:, H:] (map c2)
+                uint8_t* tile = stage_tiles;
+                if (lane == 0) sm100::bulk_wait_read<0>();  // the staging tile's previous store has read it
+                __syncwarp();
+                uint8_t* rowp = tile + lane * 128;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  uint4 gv = make_uint4(0u, 0u, 0u, 0u), uv = make_uint4(0u, 0u, 0u, 0u);
+                  if (row_ok && col0 + 8 * j < p.N) {
+                    gv = __ldg(reinterpret_cast<const uint4*>(hrow + col0 + 8 * j));
+                    if (o == 0) uv = __ldg(reinterpret_cast<const uint4*>(hrow + p.N + col0 + 8 * j));
+                  }
+                  uint32_t w[4];
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const uint32_t gw = e == 0 ? gv.x : (e == 1 ? gv.y : (e == 2 ? gv.z : gv.w));
+                    const uint32_t uw = e == 0 ? uv.x : (e == 1 ? uv.y : (e == 2 ? uv.z : uv.w));
+                    const uint32_t dw = pk[sb][c * 32 + 4 * j + e];
+                    float r2[2];
+#pragma unroll
+                    for (int l = 0; l < 2; ++l) {
+                      const float g = __uint_as_float(l ? (gw & 0xffff0000u) : (gw << 16));
+                      const float u = __uint_as_float(l ? (uw & 0xffff0000u) : (uw << 16));
+                      const float d = __uint_as_float(l ? (dw & 0xffff0000u) : (dw << 16));
+                      const float sg = 1.f / (1.f + __expf(-g));
+                      r2[l] = o == 0 ? d * u * sg * (1.f + g * (1.f - sg)) : d * g * sg;
+                    }
+                    w[e] = pack_bf16(r2[0], r2[1]);
+                  }
+                  *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+                sm100::fence_async_shared();
+                __syncwarp();
+                if (lane == 0 && row0 < p.M && col0 < p.N) {
+                  sm100::tma_store_2d(o == 0 ? &tma_c : &tma_c2, tile, col0, row0);  // clipped at M and H
+                  sm100::bulk_commit();
+                }
+              }
+            }
+          }
+        } else {
         // kSwiGLU: out 0 / 1 are the gate / up halves of h13 (maps c, c2), out 2 the activation (map c3)
         constexpr int NOUT = EPI == kSwiGLU ? 3 : 2;
 #pragma unroll
@@ -540,6 +602,7 @@ __global__ void __launch_bounds__(Cfg<NSUB>::THREADS, 1) gemm2sm_kernel(const __
             }
           }
         }
+        }  // kSwiGLUBwd / other stores
       } else {
         // chunk by chunk through the staging tile (64 bf16 or 32 fp32 columns per 128-B row), the accumulator
         // released after the last read (double-buffered accumulators hide this, or fp32 output).  Warp ew
@@ -692,7 +755,11 @@ static cudaError_t launch(const void* A, long long lda, const void* B, long long
   const bool ok_b = B_MN ? make_map(&mb, bf, 2, B, p.K, p.N, ldb, 64, BK) : make_map(&mb, bf, 2, B, b_rows, p.K, ldb, 64, HN);
   CUtensorMap mc2, mc3;
   bool ok_c;
-  if (EPI == kRope64 || EPI == kRope128) {  // q [M][q_cols], k and v [M][kv_cols]; `act` holds {k, v}
+  if (EPI == kSwiGLUBwd) {  // the two halves of dh13 [M][2H] (row pitch ldc)
+    ok_c = make_map(&mc, bf, 2, Cp, p.M, p.N, ldc, 64, 32) &&
+           make_map(&mc2, bf, 2, (const __nv_bfloat16*)Cp + p.N, p.M, p.N, ldc, 64, 32);
+    mc3 = mc;
+  } else if (EPI == kRope64 || EPI == kRope128) {  // q [M][q_cols], k and v [M][kv_cols]; `act` holds {k, v}
     void* const* kv = static_cast<void* const*>(act);
     ok_c = make_map(&mc, bf, 2, Cp, p.M, p.q_cols, p.q_cols, 64, 32) &&
            make_map(&mc2, bf, 2, kv[0], p.M, p.kv_cols, p.kv_cols, 64, 32) &&
@@ -865,4 +932,27 @@ cudaError_t rlb_gemm2sm_rope_qkv(int M, int Hq, int Hkv, int D, int K, const voi
   void* kv[2] = {k, v};
   return D == 64 ? launch<0, 0, kRope64, 2>(X, ldx, W, ldw, q, p.q_cols, p, max_ctas, s, kv)
                  : launch<0, 0, kRope128, 2>(X, ldx, W, ldw, q, p.q_cols, p, max_ctas, s, kv);
+}
+
+// Gated-FFN down projection's input gradient with the SwiGLU backward in the epilogue: dh = dy [M][K] W2 (W2
+// stored [K][H], H contiguous), then dh13 [M][2H] = (d gate, d up) against h13 [M][2H] (row pitches ldh, ldd).
+cudaError_t rlb_gemm2sm_dgrad_swiglu(int M, int H, int K, const void* dY, long long ldy, const void* W2, long long ldw,
+                                     const void* h13, long long ldh, void* dh13, long long ldd, int max_ctas,
+                                     cudaStream_t s, int group_m) {
+  using namespace gemm2;
+  if (M <= 0 || H <= 0 || K <= 0) return cudaSuccess;
+  if ((H % 8) || (ldy % 8) || (ldw % 8) || (ldh % 8) || (ldd % 8) || ldh < 2LL * H || ldd < 2LL * H)
+    return cudaErrorInvalidPitchValue;
+  if ((((uintptr_t)dY) | ((uintptr_t)W2) | ((uintptr_t)h13) | ((uintptr_t)dh13)) & 15) return cudaErrorInvalidDevicePointer;
+  Params p{};
+  p.M = M;
+  p.N = H;
+  p.K = K;
+  p.splits = 1;
+  p.group_m = group_m < 1 ? GROUP_M : group_m;
+  p.alpha = 1.f;
+  p.ldc = ldd;
+  p.h13 = (const __nv_bfloat16*)h13;
+  p.ldh = ldh;
+  return launch<0, 1, kSwiGLUBwd, 2>(dY, ldy, W2, ldw, dh13, ldd, p, max_ctas, s);
 }

@@ -79,6 +79,11 @@ cudaError_t rlb_gemm2sm_rope_qkv(int M, int Hq, int Hkv, int D, int K, const voi
                                  const int* positions, int seq_T, int pos_offset, int table_rows, int* err,
                                  int max_ctas, cudaStream_t s, int group_m);
 
+// Gated-FFN down projection's input gradient with the SwiGLU backward in the epilogue (see gemm_2sm.cu).
+cudaError_t rlb_gemm2sm_dgrad_swiglu(int M, int H, int K, const void* dY, long long ldy, const void* W2, long long ldw,
+                                     const void* h13, long long ldh, void* dh13, long long ldd, int max_ctas,
+                                     cudaStream_t s, int group_m);
+
 cudaError_t rlb_gemm_grouped(int mode, int b_mn, int epi, int M, int N, int K, const void* A, long long lda,
                              const void* B, long long ldb, void* C, long long ldc, float alpha, int groups,
                              const int* tile_group, const int* k_begin, const int* k_len, long long k_total,

@@ -45,6 +45,9 @@ class SwiGLUFeedForward(nn.Module):
         if self._fusable():
             w13 = torch.cat([self.w1.weight, self.w3.weight], dim=0)
             if self.tp_group is None and x.is_cuda and gemm.swiglu_fusable(x.reshape(-1, x.shape[-1]), w13):
+                if type(self.w2) is nn.Linear and self.w2.bias is None:
+                    # forward activation and its backward both in GEMM epilogues
+                    return self.dropout(gemm.swiglu_ffn(x, w13, self.w2.weight))
                 a = gemm.linear_swiglu(x, w13)  # activation in the GEMM epilogue
             else:
                 h13 = column_parallel_in(x, w13, None, self.tp_group) if self.tp_group is not None else linear(x, w13)

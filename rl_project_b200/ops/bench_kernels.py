@@ -479,6 +479,25 @@ def bench_rope_qkv_gemm(B: int = 8, T: int = 4096, C: int = 2048, Hq: int = 32, 
                       "speedup_vs_unfused": round((t_g + t_r) / t_f, 3)}), flush=True)
 
 
+def bench_dgrad_swiglu_gemm(M: int = 32768, H: int = 8192, K: int = 2048):
+    """Down projection's input gradient with the SwiGLU backward in the GEMM epilogue against the input-gradient
+    GEMM followed by the standalone activation backward (L2 flushed between timed calls)."""
+    from rl_project_b200.ops import gemm
+    from rl_project_b200.ops._ext import native
+
+    dy = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    w2 = (torch.randn(K, H, device="cuda") / H ** 0.5).to(torch.bfloat16)
+    h13 = torch.randn(M, 2 * H, device="cuda").to(torch.bfloat16)
+    da = gemm.gemm_nn(dy, w2)
+    t_f = time_ms(lambda: gemm.gemm_dgrad_swiglu(dy, w2, h13))
+    t_g = time_ms(lambda: gemm.gemm_nn(dy, w2))
+    t_c = time_ms(lambda: dy @ w2)
+    t_a = time_ms(lambda: native().swiglu_bwd(h13, da))
+    print(json.dumps({"kernel": "gemm2sm_dgrad_swiglu", "M": M, "H": H, "K": K, "fused_ms": round(t_f, 4),
+                      "gemm_ms": round(t_g, 4), "cublas_ms": round(t_c, 4), "activation_bwd_ms": round(t_a, 4),
+                      "speedup_vs_cublas_unfused": round((t_c + t_a) / t_f, 3)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--which", default="gemm,mem,adam,paged,sample")
@@ -514,6 +533,8 @@ def main():
         bench_lse_gemm()
     if "rope" in which:
         bench_rope_qkv_gemm()
+    if "swiglu_bwd" in which:
+        bench_dgrad_swiglu_gemm()
     if "swiglu_small" in which:  # profiling case
         bench_swiglu_gemm(M=4096)
     if "attn1" in which:  # one small case (profiling)

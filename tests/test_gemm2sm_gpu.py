@@ -316,3 +316,46 @@ def test_rope_qkv_epilogue_matches_unfused(Hq, Hkv, D):
         assert _rel(dx, x.grad.float()) < 1e-2 and _rel(dw, w.grad.float()) < 1e-2
     finally:
         gemm._MODE, gemm._MIN_TILES = old, old_min
+
+
+@pytest.mark.parametrize("M,H,K", [(1000, 1408, 512), (4096, 2816, 2048)])
+def test_dgrad_swiglu_epilogue_matches_unfused(M, H, K):
+    """The down projection's input gradient with the SwiGLU backward in the epilogue equals dy W2 rounded to
+    bf16 followed by the standalone activation backward."""
+    from rl_project_b200.ops import gemm
+    from rl_project_b200.ops._ext import native
+
+    g = torch.Generator(device="cuda").manual_seed(M + H)
+    dy = torch.randn(M, K, device="cuda", generator=g).to(BF)
+    w2 = (torch.randn(K, H, device="cuda", generator=g) / H ** 0.5).to(BF)
+    h13 = torch.randn(M, 2 * H, device="cuda", generator=g).to(BF)
+    got = gemm.gemm_dgrad_swiglu(dy, w2, h13)
+    ref = native().swiglu_bwd(h13, (dy.float() @ w2.float()).to(BF))
+    torch.cuda.synchronize()
+    assert _rel(got, ref.float()) < 1e-2
+
+
+@pytest.mark.parametrize("fused_bwd", [False, True])
+def test_swiglu_ffn_matches_fp32(fused_bwd):
+    """Whole gated FFN on the fused epilogues (with and without the activation backward in the down projection's
+    input-gradient GEMM): output and the gradients of x, [W1; W3] and W2 against fp32."""
+    from rl_project_b200.ops import gemm
+
+    old, old_min, old_bwd = gemm._MODE, gemm._MIN_TILES, gemm._SWIGLU_BWD
+    gemm._MODE, gemm._MIN_TILES, gemm._SWIGLU_BWD = "hybrid", 0, fused_bwd
+    try:
+        M, C, H = 2048, 768, 2048
+        x = torch.randn(M, C, device="cuda").to(BF).requires_grad_()
+        w13 = (torch.randn(2 * H, C, device="cuda") / C ** 0.5).to(BF).requires_grad_()
+        w2 = (torch.randn(C, H, device="cuda") / H ** 0.5).to(BF).requires_grad_()
+        out = gemm.swiglu_ffn(x, w13, w2)
+        gout = torch.randn_like(out)
+        out.backward(gout)
+        xr, w13r, w2r = (t.detach().float().requires_grad_() for t in (x, w13, w2))
+        hr = xr @ w13r.t()
+        outr = (torch.nn.functional.silu(hr[:, :H]) * hr[:, H:]) @ w2r.t()
+        outr.backward(gout.float())
+        assert _rel(out, outr) < 2e-2
+        assert _rel(x.grad, xr.grad) < 3e-2 and _rel(w13.grad, w13r.grad) < 3e-2 and _rel(w2.grad, w2r.grad) < 3e-2
+    finally:
+        gemm._MODE, gemm._MIN_TILES, gemm._SWIGLU_BWD = old, old_min, old_bwd
