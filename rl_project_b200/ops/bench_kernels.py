@@ -531,6 +531,8 @@ def main():
         bench_swiglu_gemm()
     if "lse" in which:
         bench_lse_gemm()
+    if "lse_small" in which:  # profiling case
+        bench_lse_gemm(M=4096, V=32768)
     if "rope" in which:
         bench_rope_qkv_gemm()
     if "swiglu_bwd" in which:
