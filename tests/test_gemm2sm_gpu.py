@@ -265,8 +265,8 @@ def test_linear_logprobs_with_lse_epilogue_matches_fp32():
     from rl_project_b200.ops import gemm
     from rl_project_b200.ops.logprob import linear_logprobs, linear_logprobs_reference
 
-    old, old_min = gemm._MODE, gemm._MIN_TILES
-    gemm._MODE, gemm._MIN_TILES = "hybrid", 0
+    old, old_min, old_rows = gemm._MODE, gemm._MIN_TILES, gemm._LSE_MIN_ROWS
+    gemm._MODE, gemm._MIN_TILES, gemm._LSE_MIN_ROWS = "hybrid", 0, 0
     try:
         M, V, K = 1024, 8192, 512
         h = torch.randn(M, K, device="cuda").to(BF).requires_grad_()
@@ -281,7 +281,7 @@ def test_linear_logprobs_with_lse_epilogue_matches_fp32():
         assert (lp - rlp).abs().max().item() < 0.1 and _rel(ent, rent) < 1e-2
         assert _rel(h.grad, hr.grad) < 3e-2 and _rel(w.grad, wr.grad) < 3e-2
     finally:
-        gemm._MODE, gemm._MIN_TILES = old, old_min
+        gemm._MODE, gemm._MIN_TILES, gemm._LSE_MIN_ROWS = old, old_min, old_rows
 
 
 @pytest.mark.parametrize("Hq,Hkv,D", [(32, 8, 64), (16, 4, 128)])
