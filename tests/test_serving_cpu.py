@@ -98,3 +98,24 @@ def test_http_server_end_to_end(engine_backend):
         assert ei.value.code == 400
     finally:
         server.stop()
+
+
+def test_http_server_keeps_json_connections_alive():
+    """Two JSON requests over one HTTP/1.1 connection; an unknown route is a 404 and the server stops cleanly."""
+    import http.client
+
+    server = ServingServer(Router({"echo": EchoBackend()}, default_model="echo"), port=0)
+    server.start()
+    try:
+        conn = http.client.HTTPConnection("127.0.0.1", server.port, timeout=30)
+        for _ in range(2):
+            conn.request("GET", "/v1/models")
+            resp = conn.getresponse()
+            assert resp.status == 200 and json.loads(resp.read())["data"][0]["id"] == "echo"
+        conn.request("GET", "/nope")
+        resp = conn.getresponse()
+        assert resp.status == 404
+        resp.read()
+        conn.close()
+    finally:
+        server.stop()
