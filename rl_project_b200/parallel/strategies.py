@@ -19,14 +19,49 @@ from rl_project_b200.core.errors import DistributedConfigError, OptionalDependen
 from rl_project_b200.parallel import runtime as rt
 
 
+class _OneProcess:
+    """Topology of a run without a process group: a single rank."""
+
+    @staticmethod
+    def rank() -> int:
+        return 0
+
+    @staticmethod
+    def size() -> int:
+        return 1
+
+    @staticmethod
+    def sync() -> None:
+        return None
+
+    @staticmethod
+    def leave() -> None:
+        return None
+
+
+class _DefaultGroup:
+    """Topology of torch.distributed's default process group, read live (answers like one rank until the
+    group exists)."""
+
+    rank = staticmethod(rt.rank)
+    size = staticmethod(rt.world_size)
+    sync = staticmethod(rt.barrier)
+    leave = staticmethod(rt.destroy_process_group)
+
+
 class SingleProcessStrategy:
+    """Base of every strategy: rank queries go to its topology object (one process here, the default
+    process group for the distributed strategies); subclasses add ``setup`` and the model wrapper."""
+
     name = "single"
+    topology = _OneProcess
 
     def __init__(self, cfg: Optional[DistributedConfig] = None):
         self.cfg = cfg or DistributedConfig()
+        self.monitor = None
 
     def setup(self) -> None:
-        pass
+        return None
 
     def wrap_model(self, model: nn.Module) -> nn.Module:
         return model
@@ -34,31 +69,43 @@ class SingleProcessStrategy:
     def unwrap_model(self, model: nn.Module) -> nn.Module:
         return model
 
-    def is_main_process(self) -> bool:
-        return True
+    def rank(self) -> int:
+        return self.topology.rank()
 
     def world_size(self) -> int:
-        return 1
+        return self.topology.size()
 
-    def rank(self) -> int:
-        return 0
+    def is_main_process(self) -> bool:
+        return self.rank() == 0
 
     def barrier(self) -> None:
-        pass
+        self.topology.sync()
+
+    def check_health(self) -> None:
+        """Raise DistributedTimeoutError if a peer rank stopped beating (called between steps)."""
+        if self.monitor is not None:
+            self.monitor.check()
 
     def teardown(self) -> None:
-        pass
+        if self.monitor is not None:
+            self.monitor.stop("teardown")
+            self.monitor = None
+        self.topology.leave()
 
 
 class _ProcessGroupStrategy(SingleProcessStrategy):
+    """Joins (or creates, when not launched and a one-process group is allowed) the default process group and
+    starts the store heartbeat when the config asks for one."""
+
+    topology = _DefaultGroup
+
     def __init__(self, cfg: DistributedConfig, allow_single_process: bool = True):
         super().__init__(cfg)
         self.allow_single_process = allow_single_process
         self.info: Optional[rt.DistributedInfo] = None
 
     def setup(self) -> None:
-        env = rt.read_launcher_env()
-        if not env.launched and not self.allow_single_process:
+        if not (rt.read_launcher_env().launched or self.allow_single_process):
             raise DistributedConfigError(f"{self.name} strategy requires a torchrun launch (RANK/WORLD_SIZE not set)")
         self.info = rt.init_process_group(self.cfg.backend, timeout_s=self.cfg.timeout_s)
         self.start_health_monitor()
@@ -66,32 +113,9 @@ class _ProcessGroupStrategy(SingleProcessStrategy):
     def start_health_monitor(self) -> None:
         from rl_project_b200.parallel.health import monitor_for_process_group
 
-        iv = float(getattr(self.cfg, "heartbeat_interval_s", 0.0) or 0.0)
-        self.monitor = monitor_for_process_group(iv, float(getattr(self.cfg, "heartbeat_timeout_s", 60.0))) \
-            if iv > 0 else None
-
-    def check_health(self) -> None:
-        """Raise DistributedTimeoutError if a peer rank stopped beating (called between steps)."""
-        if getattr(self, "monitor", None) is not None:
-            self.monitor.check()
-
-    def is_main_process(self) -> bool:
-        return rt.is_main_process()
-
-    def world_size(self) -> int:
-        return rt.world_size()
-
-    def rank(self) -> int:
-        return rt.rank()
-
-    def barrier(self) -> None:
-        rt.barrier()
-
-    def teardown(self) -> None:
-        if getattr(self, "monitor", None) is not None:
-            self.monitor.stop("teardown")
-            self.monitor = None
-        rt.destroy_process_group()
+        every = float(getattr(self.cfg, "heartbeat_interval_s", 0.0) or 0.0)
+        limit = float(getattr(self.cfg, "heartbeat_timeout_s", 60.0))
+        self.monitor = monitor_for_process_group(every, limit) if every > 0 else None
 
     def unwrap_model(self, model: nn.Module) -> nn.Module:
         return getattr(model, "module", model)
