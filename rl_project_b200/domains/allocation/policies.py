@@ -191,33 +191,49 @@ def build_actor_critic(n_actions: int, config: PolicyNetConfig) -> ActorCritic:
 
 
 class HistoryBuffer:
-    """Per-episode window of history rows, kept oldest-first with valid rows at the front."""
+    """Per-episode window of realised steps kept as a ring: ``push`` writes each episode's new row into its next
+    slot (no shifting of the window); ``ordered`` returns the rows oldest-first with the valid ones at the front
+    and zeros after, the layout the GRU packs."""
 
     def __init__(self, n: int, window: int, n_actions: int, env_cfg: AllocationEnvConfig):
         self.n, self.window, self.n_actions, self.cfg = n, window, n_actions, env_cfg
         self.dim = history_feature_dim(n_actions)
-        self.buf = np.zeros((n, window, self.dim), dtype=np.float32)
-        self.lengths = np.zeros(n, dtype=np.int64)
+        self.ring = np.zeros((n, window, self.dim), dtype=np.float32)
+        self.count = np.zeros(n, dtype=np.int64)  # rows pushed so far per episode
+        self._norm = np.array([env_cfg.value_mean, env_cfg.cost_mean, env_cfg.budget], dtype=np.float64)
         self._obs: Optional[np.ndarray] = None
+
+    @property
+    def lengths(self) -> np.ndarray:
+        return np.minimum(self.count, self.window)
 
     def set_obs(self, obs: np.ndarray) -> None:
         self._obs = np.asarray(obs, dtype=np.float32)
 
     def push(self, actions, rewards, spends, remaining) -> None:
+        """Row = (observation before the step, one-hot action, reward / v_mean, spend / c_mean, remaining / B)."""
+        ep = np.arange(self.n)
         row = np.zeros((self.n, self.dim), dtype=np.float32)
         row[:, :OBS_DIM] = self._obs
-        row[np.arange(self.n), OBS_DIM + np.asarray(actions, dtype=np.int64)] = 1.0
-        row[:, -3] = np.asarray(rewards) / self.cfg.value_mean
-        row[:, -2] = np.asarray(spends) / self.cfg.cost_mean
-        row[:, -1] = np.asarray(remaining) / self.cfg.budget
-        full = self.lengths >= self.window
-        self.buf[full] = np.roll(self.buf[full], -1, axis=1)  # drop the oldest row of full windows
-        pos = np.minimum(self.lengths, self.window - 1)
-        self.buf[np.arange(self.n), pos] = row
-        self.lengths = np.minimum(self.lengths + 1, self.window)
+        row[ep, OBS_DIM + np.asarray(actions, dtype=np.int64)] = 1.0
+        row[:, -3:] = np.stack([np.asarray(rewards), np.asarray(spends), np.asarray(remaining)], 1) / self._norm
+        self.ring[ep, self.count % self.window] = row
+        self.count += 1
+
+    def ordered(self) -> Tuple[np.ndarray, np.ndarray]:
+        L = self.lengths
+        slots = (self.count - L)[:, None] + np.arange(self.window)[None, :]  # oldest kept row first
+        out = np.take_along_axis(self.ring, (slots % self.window)[:, :, None], axis=1)
+        out[np.arange(self.window)[None, :] >= L[:, None]] = 0.0
+        return out, L
+
+    @property
+    def buf(self) -> np.ndarray:
+        return self.ordered()[0]
 
     def tensors(self, device) -> Tuple[torch.Tensor, torch.Tensor]:
-        return torch.as_tensor(self.buf, device=device), torch.as_tensor(self.lengths, device=device)
+        rows, L = self.ordered()
+        return torch.as_tensor(rows, device=device), torch.as_tensor(L, device=device)
 
 
 class NeuralPolicy(Policy):

@@ -212,8 +212,9 @@ class AllocationPPOAlgorithm(PostTrainingAlgorithm):
         for t in range(T):
             if seq:
                 self.policy.hist.set_obs(obs)
-                traj.hist[t].copy_(torch.from_numpy(self.policy.hist.buf))
-                traj.lengths[t].copy_(torch.from_numpy(self.policy.hist.lengths))
+                rows, lengths = self.policy.hist.ordered()
+                traj.hist[t].copy_(torch.from_numpy(rows))
+                traj.lengths[t].copy_(torch.from_numpy(lengths))
             traj.obs[t].copy_(torch.from_numpy(np.asarray(obs, dtype=np.float32)))
             logits, value = self.policy.evaluate(obs)
             logp_all = F.log_softmax(logits.float(), -1)
