@@ -12,14 +12,14 @@ from __future__ import annotations
 import json
 import threading
 from collections import OrderedDict
-from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
 from importlib import resources
 from pathlib import Path
-from typing import Any, Optional, Tuple
+from typing import Any, Dict, Optional, Tuple
 from urllib.parse import parse_qs, urlparse
 
 from rl_project_b200.dashboard import data
 from rl_project_b200.dashboard.data import DashboardSources
+from rl_project_b200.serving.http import AsyncHTTPServer
 
 JSON = "application/json"
 
@@ -89,45 +89,34 @@ class DashboardApp:
         return 404, JSON, {"error": f"no route {route}"}
 
 
-def make_handler(app: DashboardApp):
-    class Handler(BaseHTTPRequestHandler):
-        server_version = "forgeline-b200-dashboard/0.1"
-
-        def do_GET(self) -> None:  # noqa: N802
-            status, ctype, payload = app.handle(self.path)
-            body = payload.encode() if isinstance(payload, str) else json.dumps(payload, default=str).encode()
-            self.send_response(status)
-            self.send_header("Content-Type", ctype)
-            self.send_header("Content-Length", str(len(body)))
-            self.send_header("Cache-Control", "no-store")
-            self.end_headers()
-            self.wfile.write(body)
-
-        def log_message(self, format: str, *args: Any) -> None:  # noqa: A002
-            pass
-
-    return Handler
-
-
 class DashboardServer:
+    """The dashboard's read-only views over the shared asyncio HTTP core (GET only; file-system reads run in
+    its thread pool)."""
+
     def __init__(self, app: DashboardApp, host: str = "127.0.0.1", port: int = 8765):
-        self.httpd = ThreadingHTTPServer((host, port), make_handler(app))
-        self.httpd.daemon_threads = True
-        self.host, self.port = host, int(self.httpd.server_address[1])
-        self._thread: Optional[threading.Thread] = None
+        self.app = app
+        self._http = AsyncHTTPServer(self._serve, host, port, workers=4, server_name="forgeline-b200-dashboard/0.1",
+                                     on_bad_request=lambda status, msg: json.dumps({"error": msg}).encode(),
+                                     extra_headers={"Cache-Control": "no-store"})
+        self.host, self.port = host, self._http.port
+
+    def _serve(self, method: str, target: str, headers: Dict[str, str], body: bytes):
+        if method != "GET":
+            return 404, "application/json", json.dumps({"error": f"no route for {method}"}).encode()
+        status, ctype, payload = self.app.handle(target)
+        data = payload.encode() if isinstance(payload, str) else json.dumps(payload, default=str).encode()
+        return status, ctype, data
 
     @property
     def url(self) -> str:
         return f"http://{self.host}:{self.port}"
 
     def start(self) -> "DashboardServer":
-        self._thread = threading.Thread(target=self.httpd.serve_forever, daemon=True, name="forgeline-dashboard")
-        self._thread.start()
+        self._http.start("forgeline-dashboard")
         return self
 
     def serve_forever(self) -> None:
-        self.httpd.serve_forever()
+        self._http.serve_forever()
 
     def stop(self) -> None:
-        self.httpd.shutdown()
-        self.httpd.server_close()
+        self._http.stop()
