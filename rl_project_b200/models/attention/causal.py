@@ -107,6 +107,10 @@ class CausalSelfAttention(nn.Module):
         if not (self.use_rope and self.tp_group is None and x.is_cuda and x.dtype == torch.bfloat16
                 and positions is None and all(type(m) is nn.Linear and m.bias is None for m in mods)):
             return None
+        rows = x.shape[0] * x.shape[1]
+        if not (gemm.enabled() and gemm.fills_gpu(rows, sum(m.weight.shape[0] for m in mods), 512,
+                                                   x.device.index or 0)):
+            return None  # decided before concatenating the weights
         w = torch.cat([m.weight for m in mods], 0)
         if not gemm.rope_qkv_fusable(x.reshape(-1, x.shape[-1]), w, self.n_head, self.n_kv_head, self.head_dim):
             return None
