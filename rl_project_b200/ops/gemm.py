@@ -13,12 +13,13 @@ without transposing anything:
 (per product shape, the fastest of the 2-SM kernel with 256 x 256 tiles, with
 256 x 512 tiles, and cuBLAS -- timed once with CUDA events on the first call of
 that shape; accumulating and graph-captured calls keep the per-shape default) or
-``hybrid`` (the default: forward products on the 2-SM kernel -- the gated FFN's projection with the
-SwiGLU activation in its epilogue -- and gradient products on cuBLAS) or ``fwd_dgrad`` (forward and
-input-gradient products on the 2-SM kernel, weight gradients on cuBLAS).  Products too small to give every
-CTA pair a tile (decode steps, short prefills) go to cuBLAS in every mode (``fills_gpu``).
+``hybrid`` (the default: forward products on the 2-SM kernel, with fused epilogues where one applies --
+the gated FFN's projection with the SwiGLU activation, the attention projection with RoPE and the q / k / v
+split, the LM head with per-row log-sum-exp statistics -- and gradient products on cuBLAS) or ``fwd_dgrad``
+(forward and input-gradient products on the 2-SM kernel, weight gradients on cuBLAS).  Products too small to
+give every CTA pair a tile (decode steps, short prefills) go to cuBLAS in every mode (``fills_gpu``).
 ``RLB_GEMM_KERNEL`` picks the kernel: ``2sm`` (default; CTA pairs issuing
-``tcgen05.mma.cta_group::2`` on 256 x 256 tiles, TMA-store epilogue) or
+``tcgen05.mma.cta_group::2`` on 256 x 256 or 256 x 512 tiles, TMA-store epilogue) or
 ``1sm`` (one CTA per 128 x 256 tile, register-to-global epilogue; the base of
 the grouped and all-reduce variants).
 """
@@ -33,7 +34,7 @@ import torch
 from rl_project_b200.ops._ext import available, native
 
 # default "hybrid": in the full 1B training step on B200 (alternating runs on one box) the own forward products
-# with the fused SwiGLU epilogue and cuBLAS gradients measured 259.9-263.0 ms against 261.4-262.6 ms for all-cuBLAS;
+# with the fused epilogues and cuBLAS gradients measured 256.5-257.0 ms against 257.9-258.8 ms for all-cuBLAS;
 # own input- and weight-gradient products still cost 1.5-4 % in the step under the power cap
 _MODE = os.environ.get("RLB_GEMM", "hybrid")
 _KERNEL = os.environ.get("RLB_GEMM_KERNEL", "2sm")
