@@ -119,3 +119,47 @@ def test_http_server_keeps_json_connections_alive():
         conn.close()
     finally:
         server.stop()
+
+
+def test_http_core_streams_pieces_and_reports_a_failing_producer():
+    """The shared asyncio core: a streamed body arrives piece by piece and a producer that fails mid-stream
+    ends with an error event; sized bodies keep the connection open; an oversized body is refused."""
+    import http.client
+
+    from rl_project_b200.serving.http import MAX_BODY_BYTES, AsyncHTTPServer
+
+    def pieces(fail):
+        yield "data: 1\n\n"
+        yield "data: 2\n\n"
+        if fail:
+            raise RuntimeError("backend lost")
+
+    def app(method, target, headers, body):
+        if target.startswith("/stream"):
+            return 200, "text/event-stream", pieces("fail" in target)
+        return 200, "application/json", json.dumps({"echo": body.decode(), "target": target}).encode()
+
+    srv = AsyncHTTPServer(app, port=0, on_bad_request=lambda s, m: json.dumps({"error": m}).encode())
+    srv.start()
+    try:
+        conn = http.client.HTTPConnection("127.0.0.1", srv.port, timeout=30)
+        conn.request("POST", "/x?y=1", body=b"abc")
+        resp = conn.getresponse()
+        assert resp.status == 200 and json.loads(resp.read()) == {"echo": "abc", "target": "/x?y=1"}
+        conn.request("GET", "/stream")
+        assert conn.getresponse().read().decode() == "data: 1\n\ndata: 2\n\n"
+        conn.close()
+        conn = http.client.HTTPConnection("127.0.0.1", srv.port, timeout=30)
+        conn.request("GET", "/stream-fail")
+        text = conn.getresponse().read().decode()
+        assert text.startswith("data: 1\n\ndata: 2\n\n") and "backend lost" in text
+        conn.close()
+        conn = http.client.HTTPConnection("127.0.0.1", srv.port, timeout=30)
+        conn.putrequest("POST", "/big")
+        conn.putheader("Content-Length", str(MAX_BODY_BYTES + 1))
+        conn.endheaders()
+        resp = conn.getresponse()
+        assert resp.status == 413 and "too large" in json.loads(resp.read())["error"]
+        conn.close()
+    finally:
+        srv.stop()
