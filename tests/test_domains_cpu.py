@@ -158,3 +158,34 @@ def test_allocation_benchmark_and_cli(tmp_path):
     assert rc in (0, 1, 3)  # a deterministic target on an eps log is valid (warnings allowed)
     assert main(["allocation", "shadow", "--env", str(env_yaml), "--incumbent", "dual", "--candidate", ckpt,
                  "--episodes", "5"]) == 0
+
+
+def test_gae_operator_equals_backward_recursion():
+    """GAE as one product with the discount operator equals the usual backward recursion."""
+    from rl_project_b200.domains.allocation.ppo import batched_gae
+
+    rng = np.random.default_rng(3)
+    T, n, gamma, lam = 9, 4, 0.97, 0.9
+    r = rng.random((T, n)).astype(np.float32)
+    v = rng.random((T + 1, n)).astype(np.float32)
+    v[-1] = 0.0
+    adv_ref = np.zeros_like(r)
+    run = np.zeros(n, np.float32)
+    for t in range(T - 1, -1, -1):
+        run = r[t] + gamma * v[t + 1] - v[t] + gamma * lam * run
+        adv_ref[t] = run
+    adv, ret = batched_gae(r, v, gamma, lam)
+    assert np.allclose(adv, adv_ref, atol=1e-5) and np.allclose(ret, adv_ref + v[:T], atol=1e-5)
+
+
+def test_allocation_configs_reject_unknown_keys():
+    from rl_project_b200.core.errors import ConfigError
+    from rl_project_b200.domains.allocation.env import AllocationEnvConfig
+    from rl_project_b200.domains.allocation.ppo import AllocationPPOConfig
+
+    with pytest.raises(ConfigError, match="unknown AllocationPPOConfig keys"):
+        AllocationPPOConfig.from_dict({"ppo_epochs": 2, "bogus": 1})
+    with pytest.raises(ConfigError, match="unknown allocation env keys"):
+        AllocationEnvConfig.from_dict({"nope": 1})
+    cfg = AllocationEnvConfig.from_dict({"multipliers": [0, 1, 2]})
+    assert cfg.multipliers == (0.0, 1.0, 2.0) and cfg.n_actions == 3
